@@ -1,0 +1,67 @@
+"""Block-scaled FP8 (e4m3) quantization, the checkpoint format of BASELINE config 3.
+
+Weights: one fp32 scale per 128x128 block, stored HF-style as ``<name>_scale_inv`` [ceil(N/128),
+ceil(K/128)] so that ``w_fp32 ~= w_fp8 * scale_inv`` (the DeepSeek/Qwen FP8 checkpoint layout).
+Activations: one fp32 scale per token per 128 channels, computed at run time by the fused norm /
+SwiGLU kernels; this module holds the torch definition those kernels are tested against.
+
+The scale is amax / 448 (448 = largest finite e4m3 value), as in the reference's per-token quant
+(docker/opt/v5/fusedq/silu_quant.cuh:28-79 computes scale = amax/448 per token); a zero block gets
+scale 1 so that it quantizes to exact zeros.
+"""
+from __future__ import annotations
+
+from typing import Tuple
+
+import torch
+
+FP8_MAX = 448.0
+FP8_DTYPE = torch.float8_e4m3fn
+BLOCK = 128
+
+
+def quant_weight_block(w: torch.Tensor, block: int = BLOCK) -> Tuple[torch.Tensor, torch.Tensor]:
+    """fp32/bf16 [N, K] -> (fp8 [N, K], fp32 scale_inv [ceil(N/b), ceil(K/b)])."""
+    n, k = w.shape
+    nb, kb = (n + block - 1) // block, (k + block - 1) // block
+    wp = torch.zeros(nb * block, kb * block, dtype=torch.float32, device=w.device)
+    wp[:n, :k] = w.float()
+    blocks = wp.view(nb, block, kb, block)
+    amax = blocks.abs().amax(dim=(1, 3))
+    scale = torch.where(amax > 0, amax / FP8_MAX, torch.ones_like(amax))
+    q = (blocks / scale[:, None, :, None]).clamp(-FP8_MAX, FP8_MAX).to(FP8_DTYPE)
+    return q.view(nb * block, kb * block)[:n, :k].contiguous(), scale
+
+
+def quant_act_block(x: torch.Tensor, block: int = BLOCK) -> Tuple[torch.Tensor, torch.Tensor]:
+    """[M, K] -> (fp8 [M, K], fp32 scales [K/128, M]) — the scale tensor is stored k-block major
+    (M contiguous) so that a GEMM tile reads one contiguous run of M scales per K block."""
+    m, k = x.shape
+    assert k % block == 0, "activation width must be a multiple of 128"
+    xb = x.float().view(m, k // block, block)
+    amax = xb.abs().amax(-1)
+    scale = torch.where(amax > 0, amax / FP8_MAX, torch.ones_like(amax))
+    q = (xb / scale[..., None]).clamp(-FP8_MAX, FP8_MAX).to(FP8_DTYPE).view(m, k)
+    return q, scale.t().contiguous()
+
+
+def dequant_act_block(q: torch.Tensor, s: torch.Tensor, block: int = BLOCK) -> torch.Tensor:
+    m, k = q.shape
+    return (q.float().view(m, k // block, block) * s.t()[..., None]).view(m, k)
+
+
+def gemm_fp8_block_ref(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
+                       block: int = BLOCK) -> torch.Tensor:
+    """fp32 oracle of the block-scaled GEMM: out[m, n] = sum_kb xs[kb, m] * ws[n/128, kb] *
+    sum_{k in kb} xq[m, k] * wq[n, k]. Returns fp32 [M, N]."""
+    m, k = xq.shape
+    n = wq.shape[0]
+    kb = k // block
+    out = torch.zeros(m, n, dtype=torch.float32, device=xq.device)
+    xf, wf = xq.float(), wq.float()
+    wsn = ws.float().repeat_interleave(block, 0)[:n]  # [N, KB]
+    for b in range(kb):
+        sl = slice(b * block, (b + 1) * block)
+        part = xf[:, sl] @ wf[:, sl].t()
+        out += part * xs[b].float()[:, None] * wsn[:, b][None, :]
+    return out
