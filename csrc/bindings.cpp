@@ -1,0 +1,37 @@
+// Python bindings of the sm_100a kernels (module phung5_b200._C).
+#include <torch/extension.h>
+
+namespace phx {
+void gemm_fp8_block(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor out,
+                    torch::Tensor status, int64_t bn, int64_t max_ctas);
+void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tensor status, int64_t bn,
+               int64_t max_ctas);
+void add_rmsnorm_quant(torch::Tensor h, c10::optional<torch::Tensor> delta, torch::Tensor w, double eps,
+                       c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> qs,
+                       c10::optional<torch::Tensor> out);
+void silu_mul_quant(torch::Tensor gu, c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> qs,
+                    c10::optional<torch::Tensor> out);
+void act_quant(torch::Tensor x, torch::Tensor q, torch::Tensor qs);
+void rope_kv_write(torch::Tensor qkv, torch::Tensor pos, c10::optional<torch::Tensor> slots, torch::Tensor cos_sin,
+                   torch::Tensor q_out, c10::optional<torch::Tensor> k_cache, c10::optional<torch::Tensor> v_cache,
+                   int64_t Hq, int64_t Hkv, int64_t D, int64_t page_size);
+void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor pages,
+                     torch::Tensor page_indptr, torch::Tensor prefix_len, torch::Tensor q_start,
+                     c10::optional<torch::Tensor> tree, torch::Tensor items, torch::Tensor tile_item,
+                     torch::Tensor tile_row0, int64_t num_tiles, bool causal, double softmax_scale,
+                     c10::optional<torch::Tensor> o_in, c10::optional<torch::Tensor> lse_in,
+                     c10::optional<torch::Tensor> o_part, c10::optional<torch::Tensor> lse_part,
+                     c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> out_q,
+                     c10::optional<torch::Tensor> out_qs);
+}  // namespace phx
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "phung5_b200 sm_100a kernels";
+  m.def("gemm_fp8_block", &phx::gemm_fp8_block);
+  m.def("gemm_bf16", &phx::gemm_bf16);
+  m.def("add_rmsnorm_quant", &phx::add_rmsnorm_quant);
+  m.def("silu_mul_quant", &phx::silu_mul_quant);
+  m.def("act_quant", &phx::act_quant);
+  m.def("rope_kv_write", &phx::rope_kv_write);
+  m.def("paged_attention", &phx::paged_attention);
+}

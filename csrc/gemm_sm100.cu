@@ -1,0 +1,325 @@
+// tcgen05 / TMEM / TMA GEMMs for sm_100a.
+//
+//   gemm_fp8_block: out[M,N] (bf16) = sum_kb xs[kb,m] * ws[n/128,kb] * (xq[m, kb*128:+128] . wq[n, kb*128:+128])
+//     xq fp8 e4m3 [M,K] row-major, xs fp32 [K/128, M], wq fp8 [N,K] row-major, ws fp32 [ceil(N/128), K/128].
+//     This is the block-scaled FP8 linear of DeepSeek/Qwen-style FP8 checkpoints (128x128 weight blocks,
+//     1x128 activation blocks). The reference runs its FP8 linears through a CUTLASS sm90 wgmma tile table
+//     (docker/opt/v5/wq/kopt_wq_gemm.cuh:47-221, per-token x per-channel scales); this kernel is the
+//     Blackwell design for the block-scaled format.
+//   gemm_bf16: out[M,N] (bf16) = x[M,K] . w[N,K]^T, fp32 accumulate (lm_head, bf16 models).
+//
+// Design (one persistent CTA per SM, 320 threads):
+//   warp 0      TMA producer: 128-byte-wide K slices of A (128 rows) and B (BN rows) into a STAGES-deep
+//               ring of SWIZZLE_128B tiles, one mbarrier (full/empty) pair per stage.
+//   warp 1      allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=BN, K=32 fp8 or 16 bf16 per
+//               instruction, 4 per stage) into one of two TMEM accumulators and commits to mbarriers.
+//   warps 2-9   epilogue. fp8: every 128-wide K block lands in a fresh TMEM accumulator; the epilogue
+//               reads it with tcgen05.ld and adds it, scaled by xs[kb,row]*ws[nblk,kb], into fp32
+//               registers (exact fp32 scale application per K block), while the MMA fills the other
+//               accumulator with the next K block. bf16: the MMA accumulates the whole K range in TMEM
+//               and the epilogue drains it once per tile, overlapped with the next tile's MMAs.
+//   Tiles are walked M-fastest so CTAs running together share weight (B) columns in L2.
+//   No TMA multicast and no clusters: every CTA loads its own tiles.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "tmap.h"
+
+namespace phx {
+
+constexpr int kBM = 128;
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + kEpiWarps * 32;  // producer warp, MMA warp, 8 epilogue warps
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  uint8_t a[STAGES][kBM * 128];
+  uint8_t b[STAGES][BN * 128];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int BN>
+constexpr int gemm_stages() {
+  return BN == 256 ? 4 : 6;
+}
+
+template <int BN, bool FP8>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      __nv_bfloat16* __restrict__ out, int M, int N, int K, int ldc, const float* __restrict__ sa,
+                      const float* __restrict__ sb, int* status) {
+  constexpr int STAGES = gemm_stages<BN>();
+  constexpr int BKE = FP8 ? 128 : 64;  // K elements per 128-byte stage row
+  constexpr uint32_t IDESC = idesc_make(kBM, BN, FP8 ? 0 : 1);
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr int CPT = BN / 2;  // columns per epilogue thread
+  using Smem = GemmSmem<BN, STAGES>;
+
+  extern __shared__ uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023));
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int m_tiles = (M + kBM - 1) / kBM;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int ksteps = K / BKE;          // smem stages per tile
+  const int kblocks = K / 128;         // scale blocks (fp8)
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.tfull[i], 1);
+      mbar_init(&s.tempty[i], kEpiWarps);
+    }
+    mbar_init(&s.done, 1);
+    s.abort = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s.tmem_base;
+  volatile int* abort = &s.abort;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x) {
+        const int m_blk = t % m_tiles, n_blk = t / m_tiles;
+        for (int ks = 0; ks < ksteps; ++ks) {
+          if (!mbar_wait(&s.empty[stage], phase ^ 1, status, kErrTimeoutProducer, abort)) break;
+          mbar_arrive_expect_tx(&s.full[stage], (kBM + BN) * 128);
+          tma_load_2d(&tmA, &s.full[stage], s.a[stage], ks * BKE, m_blk * kBM);
+          tma_load_2d(&tmB, &s.full[stage], s.b[stage], ks * BKE, n_blk * BN);
+          ++issued;
+          if (++stage == STAGES) stage = 0, phase ^= 1;
+        }
+      }
+      // drain: the copies of the last (up to STAGES) armed stages have landed before exit (bounded)
+      volatile int never = 0;
+      for (int i = 0; i < STAGES && i < issued; ++i) {
+        if (--stage < 0) stage = STAGES - 1, phase ^= 1;
+        mbar_wait(&s.full[stage], phase, nullptr, 0, &never);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int tb = 0;
+      uint32_t tphase = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x) {
+        for (int ks = 0; ks < ksteps; ++ks) {
+          const bool new_acc = FP8 || ks == 0;
+          const bool end_acc = FP8 || ks == ksteps - 1;
+          if (new_acc) {
+            if (!mbar_wait(&s.tempty[tb], tphase ^ 1, status, kErrTimeoutMma, abort)) goto mma_done;
+            tc_fence_after();
+          }
+          if (!mbar_wait(&s.full[stage], phase, status, kErrTimeoutMma, abort)) goto mma_done;
+          tc_fence_after();
+          {
+            const uint64_t da = sdesc_sw128(smem_u32(s.a[stage]));
+            const uint64_t db = sdesc_sw128(smem_u32(s.b[stage]));
+            const uint32_t dtm = tmem_base + tb * BN;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t acc = new_acc ? (k > 0) : 1u;
+              if (FP8)
+                umma_f8(dtm, da + 2 * k, db + 2 * k, IDESC, acc);
+              else
+                umma_f16(dtm, da + 2 * k, db + 2 * k, IDESC, acc);
+            }
+            umma_commit(&s.empty[stage]);
+            if (end_acc) umma_commit(&s.tfull[tb]);
+          }
+          if (++stage == STAGES) stage = 0, phase ^= 1;
+          if (end_acc)
+            if (++tb == 2) tb = 0, tphase ^= 1;
+        }
+      }
+    mma_done:
+      // all issued MMAs complete before teardown
+      umma_commit(&s.done);
+      volatile int never = 0;
+      mbar_wait(&s.done, 0, nullptr, 0, &never);
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int ew = warp - 2;
+    const int sub = warp & 3;     // TMEM lane quarter this warp may access
+    const int half = ew >> 2;     // column half of the tile
+    int tb = 0;
+    uint32_t tphase = 0;
+    float acc[CPT];
+    const int epi_blocks = FP8 ? kblocks : 1;
+    for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x) {
+      const int m_blk = t % m_tiles, n_blk = t / m_tiles;
+      const int row = m_blk * kBM + sub * 32 + lane;
+      const int col0 = n_blk * BN + half * CPT;
+      const bool col_ok = col0 < N;
+      const int srow = row < M ? row : M - 1;
+      for (int kb = 0; kb < epi_blocks; ++kb) {
+        const bool ok = mbar_wait(&s.tfull[tb], tphase, status, kErrTimeoutEpilogue, abort);
+        if (!__all_sync(0xffffffffu, ok)) goto epi_done;
+        tc_fence_after();
+        float scale = 1.0f;
+        if (FP8) scale = sa[(size_t)kb * M + srow] * (col_ok ? sb[(size_t)(col0 >> 7) * kblocks + kb] : 0.0f);
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + tb * BN + half * CPT;
+#pragma unroll
+        for (int c = 0; c < CPT / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld16(taddr + c * 16, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float v = __uint_as_float(r[j]);
+            if (FP8)
+              acc[c * 16 + j] = kb == 0 ? v * scale : fmaf(v, scale, acc[c * 16 + j]);
+            else
+              acc[c * 16 + j] = v;
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.tempty[tb]);
+        if (++tb == 2) tb = 0, tphase ^= 1;
+      }
+      if (row < M && col_ok) {
+        __nv_bfloat16* dst = out + (size_t)row * ldc + col0;
+        const bool full_cols = col0 + CPT <= N;
+#pragma unroll
+        for (int c = 0; c < CPT / 8; ++c) {
+          if (!full_cols && col0 + 8 * c >= N) break;
+          uint4 v;
+          v.x = pack_bf16x2(acc[8 * c + 0], acc[8 * c + 1]);
+          v.y = pack_bf16x2(acc[8 * c + 2], acc[8 * c + 3]);
+          v.z = pack_bf16x2(acc[8 * c + 4], acc[8 * c + 5]);
+          v.w = pack_bf16x2(acc[8 * c + 6], acc[8 * c + 7]);
+          *reinterpret_cast<uint4*>(dst + 8 * c) = v;
+        }
+      }
+    }
+  epi_done:;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ------------------------------------------------------------------------------------------------
+// host
+// ------------------------------------------------------------------------------------------------
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, bool FP8>
+void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, const float* sa,
+                 const float* sb, int* status, cudaStream_t stream, int max_ctas) {
+  const int M = a.size(0), K = a.size(1), N = b.size(0);
+  const CUtensorMapDataType dt = FP8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int esz = FP8 ? 1 : 2;
+  const uint32_t box_inner = 128 / esz;
+  CUtensorMap ta = make_tmap_2d(a.data_ptr(), dt, K, M, (uint64_t)a.stride(0) * esz, box_inner, kBM,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tb = make_tmap_2d(b.data_ptr(), dt, K, N, (uint64_t)b.stride(0) * esz, box_inner, BN,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+  constexpr int STAGES = gemm_stages<BN>();
+  const size_t smem = sizeof(GemmSmem<BN, STAGES>) + 1024;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    attr_set = true;
+  }
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
+  gemm_sm100_kernel<BN, FP8><<<grid, kGemmThreads, smem, stream>>>(ta, tb, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                                                                    M, N, K, (int)out.stride(0), sa, sb, status);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+static int pick_bn(int M, int N) {
+  // BN=256 halves the A-operand shared-memory traffic per FLOP; use 128 when 256 leaves SMs idle
+  // or N is not a multiple of 256.
+  if (N % 256 != 0) return 128;
+  const long tiles256 = (long)((M + 127) / 128) * (N / 256);
+  if (tiles256 < num_sms() && (long)((M + 127) / 128) * (N / 128) <= 2L * num_sms()) return 128;
+  return 256;
+}
+
+void gemm_fp8_block(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor out,
+                    torch::Tensor status, int64_t bn, int64_t max_ctas) {
+  TORCH_CHECK(xq.is_cuda() && wq.is_cuda() && out.is_cuda());
+  TORCH_CHECK(xq.scalar_type() == at::kFloat8_e4m3fn && wq.scalar_type() == at::kFloat8_e4m3fn);
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16);
+  TORCH_CHECK(xs.scalar_type() == at::kFloat && ws.scalar_type() == at::kFloat);
+  const int M = xq.size(0), K = xq.size(1), N = wq.size(0);
+  TORCH_CHECK(wq.size(1) == K && K % 128 == 0 && N % 8 == 0, "gemm_fp8_block: K % 128 and N % 8 must be 0");
+  TORCH_CHECK(xq.stride(1) == 1 && wq.stride(1) == 1 && out.stride(1) == 1);
+  TORCH_CHECK(xs.is_contiguous() && xs.size(0) == K / 128 && xs.size(1) == M, "xs must be [K/128, M]");
+  TORCH_CHECK(ws.is_contiguous() && ws.size(0) == (N + 127) / 128 && ws.size(1) == K / 128,
+              "ws must be [ceil(N/128), K/128]");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N);
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(xq.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int b = bn > 0 ? (int)bn : pick_bn(M, N);
+  if (b == 256)
+    launch_gemm<256, true>(xq, wq, out, xs.data_ptr<float>(), ws.data_ptr<float>(), status.data_ptr<int>(), stream,
+                           (int)max_ctas);
+  else
+    launch_gemm<128, true>(xq, wq, out, xs.data_ptr<float>(), ws.data_ptr<float>(), status.data_ptr<int>(), stream,
+                           (int)max_ctas);
+}
+
+void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tensor status, int64_t bn,
+               int64_t max_ctas) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+              out.scalar_type() == at::kBFloat16);
+  const int M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && K % 64 == 0 && N % 8 == 0, "gemm_bf16: K % 64 and N % 8 must be 0");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1);
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N);
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int b = bn > 0 ? (int)bn : pick_bn(M, N);
+  if (b == 256)
+    launch_gemm<256, false>(x, w, out, nullptr, nullptr, status.data_ptr<int>(), stream, (int)max_ctas);
+  else
+    launch_gemm<128, false>(x, w, out, nullptr, nullptr, status.data_ptr<int>(), stream, (int)max_ctas);
+}
+
+}  // namespace phx

@@ -1,0 +1,222 @@
+"""Python entry points of the sm_100a kernels.
+
+Every op runs its native kernel when given CUDA tensors; if the extension is missing on a CUDA
+tensor the op raises (there is no silent eager fallback on the GPU). CPU tensors run the plain-torch
+definition of the op, which is also the oracle the GPU tests compare against and what the CPU test
+suite exercises (engine logic, multi-rank gloo runs).
+
+Kernel status: kernels with bounded waits write a nonzero code into a per-device int32 status word
+instead of hanging; `check_status()` raises if any kernel reported a timeout.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from ..weights.quant import FP8_DTYPE, dequant_act_block, gemm_fp8_block_ref, quant_act_block
+
+try:  # the in-tree extension (python setup.py build_ext --inplace)
+    from .. import _C  # type: ignore
+    _C_ERR: Optional[BaseException] = None
+except ImportError as e:  # pragma: no cover - depends on the build
+    _C = None
+    _C_ERR = e
+
+_STATUS = {}
+
+STATUS_CODES = {1: "timeout in TMA producer", 2: "timeout in MMA issuer", 3: "timeout in epilogue",
+                4: "timeout waiting for a peer rank", 5: "bad arguments"}
+
+
+def ext():
+    if _C is None:
+        raise RuntimeError(f"phung5_b200._C is not built (python setup.py build_ext --inplace): {_C_ERR}")
+    return _C
+
+
+def native_available() -> bool:
+    return _C is not None
+
+
+def status_tensor(device) -> torch.Tensor:
+    device = torch.device(device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _STATUS.get(idx)
+    if t is None:
+        t = torch.zeros(4, dtype=torch.int32, device=f"cuda:{idx}")
+        _STATUS[idx] = t
+    return t
+
+
+def check_status(device=None) -> None:
+    """Raise if a kernel on `device` recorded an error; clears the status word."""
+    if not torch.cuda.is_available():
+        return
+    devs = [torch.device(device)] if device is not None else [torch.device("cuda", i) for i in _STATUS]
+    for d in devs:
+        t = status_tensor(d)
+        v = int(t[0].item())
+        if v:
+            t.zero_()
+            raise RuntimeError(f"kernel status on {d}: {STATUS_CODES.get(v, v)}")
+
+
+# ------------------------------------------------------------------------------------------------
+# GEMMs
+# ------------------------------------------------------------------------------------------------
+
+def gemm_fp8_block(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
+                   out: Optional[torch.Tensor] = None, bn: int = 0, max_ctas: int = 0) -> torch.Tensor:
+    """Block-scaled FP8 linear: xq [M,K] e4m3, xs [K/128, M] fp32, wq [N,K] e4m3, ws [N/128, K/128]
+    fp32 -> bf16 [M, N]."""
+    m, n = xq.shape[0], wq.shape[0]
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=xq.device)
+    if xq.is_cuda:
+        ext().gemm_fp8_block(xq, xs, wq, ws, out, status_tensor(xq.device), bn, max_ctas)
+    else:
+        out.copy_(gemm_fp8_block_ref(xq, xs, wq, ws).to(out.dtype))
+    return out
+
+
+def gemm_bf16(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None, bn: int = 0,
+              max_ctas: int = 0) -> torch.Tensor:
+    """x [M,K] bf16 @ w [N,K]^T -> bf16 [M,N] (fp32 accumulate)."""
+    if out is None:
+        out = torch.empty(x.shape[0], w.shape[0], dtype=torch.bfloat16, device=x.device)
+    if x.is_cuda:
+        ext().gemm_bf16(x, w, out, status_tensor(x.device), bn, max_ctas)
+    else:
+        out.copy_((x.float() @ w.float().t()).to(out.dtype))
+    return out
+
+
+# ------------------------------------------------------------------------------------------------
+# norms / activations / quant
+# ------------------------------------------------------------------------------------------------
+
+def add_rmsnorm_quant(h: torch.Tensor, delta: Optional[torch.Tensor], w: torch.Tensor, eps: float,
+                      quant: bool = True, out_bf16: bool = False):
+    """In place h <- bf16(h + delta) (if delta), y = rmsnorm(h) * w. Returns (q, qs, y_bf16) with q/qs the
+    block-scaled fp8 of y (or None) and y_bf16 (or None)."""
+    m, hd = h.shape
+    q = qs = y = None
+    if quant:
+        q = torch.empty(m, hd, dtype=FP8_DTYPE, device=h.device)
+        qs = torch.empty(hd // 128, m, dtype=torch.float32, device=h.device)
+    if out_bf16:
+        y = torch.empty(m, hd, dtype=torch.bfloat16, device=h.device)
+    if h.is_cuda:
+        ext().add_rmsnorm_quant(h, delta, w, eps, q, qs, y)
+        return q, qs, y
+    if delta is not None:
+        h.copy_((h.float() + delta.float()).to(h.dtype))
+    hf = h.float()
+    yf = hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+    if quant:
+        q_, s_ = quant_act_block(yf)
+        q.copy_(q_)
+        qs.copy_(s_)
+    if out_bf16:
+        y.copy_(yf.to(torch.bfloat16))
+    return q, qs, y
+
+
+def silu_mul_quant(gu: torch.Tensor, quant: bool = True, out_bf16: bool = False):
+    """gu [M, 2F] = [gate | up] -> a = bf16(silu(gate) * up) as block-scaled fp8 (q, qs) and/or bf16."""
+    m, f2 = gu.shape
+    f = f2 // 2
+    q = qs = y = None
+    if quant:
+        q = torch.empty(m, f, dtype=FP8_DTYPE, device=gu.device)
+        qs = torch.empty(f // 128, m, dtype=torch.float32, device=gu.device)
+    if out_bf16:
+        y = torch.empty(m, f, dtype=torch.bfloat16, device=gu.device)
+    if gu.is_cuda:
+        ext().silu_mul_quant(gu, q, qs, y)
+        return q, qs, y
+    g, u = gu[:, :f].float(), gu[:, f:].float()
+    a = (torch.nn.functional.silu(g) * u).to(torch.bfloat16)
+    if quant:
+        q_, s_ = quant_act_block(a.float())
+        q.copy_(q_)
+        qs.copy_(s_)
+    if out_bf16:
+        y.copy_(a)
+    return q, qs, y
+
+
+def act_quant(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    m, k = x.shape
+    if x.is_cuda:
+        q = torch.empty(m, k, dtype=FP8_DTYPE, device=x.device)
+        qs = torch.empty(k // 128, m, dtype=torch.float32, device=x.device)
+        ext().act_quant(x, q, qs)
+        return q, qs
+    return quant_act_block(x.float())
+
+
+# ------------------------------------------------------------------------------------------------
+# RoPE + paged KV
+# ------------------------------------------------------------------------------------------------
+
+def rope_table(max_pos: int, head_dim: int, theta: float, device) -> torch.Tensor:
+    """[max_pos, head_dim/2, 2] fp32 (cos, sin), computed in float64 (rotate-half convention)."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
+    return torch.stack([ang.cos(), ang.sin()], -1).float().to(device)
+
+
+def rope_kv_write(qkv: torch.Tensor, pos: torch.Tensor, slots: Optional[torch.Tensor], cos_sin: torch.Tensor,
+                  k_cache: Optional[torch.Tensor], v_cache: Optional[torch.Tensor], hq: int, hkv: int, d: int,
+                  q_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """qkv [M, (hq+2hkv)*d] -> roped q [M, hq, d]; roped k and v written at `slots` (page*page_size+off)
+    of the paged cache [pages, hkv, page_size, d]."""
+    m = qkv.shape[0]
+    if q_out is None:
+        q_out = torch.empty(m, hq, d, dtype=qkv.dtype, device=qkv.device)
+    page_size = k_cache.shape[2] if k_cache is not None else 1
+    if qkv.is_cuda:
+        ext().rope_kv_write(qkv, pos, slots, cos_sin, q_out, k_cache, v_cache, hq, hkv, d, page_size)
+        return q_out
+    cs = cos_sin[pos.long()]  # [M, d/2, 2]
+    cos, sin = cs[..., 0][:, None, :], cs[..., 1][:, None, :]
+
+    def rot(x, sel=None):
+        x = x.float()
+        c, s = (cos, sin) if sel is None else (cos[sel], sin[sel])
+        x1, x2 = x[..., : d // 2], x[..., d // 2:]
+        return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], -1)
+
+    q = qkv[:, : hq * d].view(m, hq, d)
+    k = qkv[:, hq * d: (hq + hkv) * d].view(m, hkv, d)
+    v = qkv[:, (hq + hkv) * d:].view(m, hkv, d)
+    q_out.copy_(rot(q).to(q_out.dtype))
+    if k_cache is not None and slots is not None:
+        ok = slots >= 0
+        sl = slots[ok].long()
+        pg, off = sl // page_size, sl % page_size
+        k_cache[pg, :, off, :] = rot(k[ok], ok).to(k_cache.dtype)
+        v_cache[pg, :, off, :] = v[ok].to(v_cache.dtype)
+    return q_out
+
+
+# ------------------------------------------------------------------------------------------------
+# attention
+# ------------------------------------------------------------------------------------------------
+
+def paged_attention(q, k_cache, v_cache, meta, softmax_scale: float, o_in=None, lse_in=None, o_part=None,
+                    lse_part=None, out=None, out_q=None, out_qs=None, items=None, tiles=None):
+    """Run one attention pass described by `meta` (an AttnMeta from engine/attn_meta.py) and a work list
+    (`items`, `tiles` = (tile_item, tile_row0, num_tiles)); see csrc/attention.cu for the semantics."""
+    if q.is_cuda:
+        ti, tr, nt = tiles
+        ext().paged_attention(q, k_cache, v_cache, meta.pages, meta.page_indptr, meta.prefix_len, meta.q_start,
+                              meta.tree, items, ti, tr, nt, meta.causal, softmax_scale, o_in, lse_in, o_part,
+                              lse_part, out, out_q, out_qs)
+        return
+    from ..engine.attn_meta import attention_reference
+    attention_reference(q, k_cache, v_cache, meta, softmax_scale, items, o_in, lse_in, o_part, lse_part, out,
+                        out_q, out_qs)

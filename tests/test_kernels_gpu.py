@@ -1,0 +1,210 @@
+"""Numerics of the sm_100a kernels against plain-PyTorch fp32 references of the same ops."""
+import math
+
+import pytest
+import torch
+
+from phung5_b200 import ops
+from phung5_b200.engine.attn_meta import build_items, cascade_groups, make_meta, pack_work
+from phung5_b200.weights.quant import FP8_DTYPE, dequant_act_block, gemm_fp8_block_ref, quant_act_block, quant_weight_block
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / b.norm().clamp(min=1e-12)).item()
+
+
+@pytest.fixture(autouse=True)
+def _status():
+    yield
+    ops.check_status()
+
+
+@pytest.mark.parametrize("m,n,k,bn", [(128, 256, 256, 0), (200, 384, 512, 0), (1000, 1280, 1024, 256),
+                                      (64, 128, 128, 128), (513, 1024, 2048, 128), (4096, 2048, 1024, 0),
+                                      (96, 4000, 512, 0), (33, 200, 256, 256)])
+def test_gemm_fp8_block(m, n, k, bn):
+    g = torch.Generator(device=DEV).manual_seed(m + n + k)
+    x = torch.randn(m, k, device=DEV, generator=g)
+    w = torch.randn(n, k, device=DEV, generator=g) * 0.05
+    xq, xs = quant_act_block(x)
+    wq, ws = quant_weight_block(w)
+    out = ops.gemm_fp8_block(xq, xs, wq, ws, bn=bn)
+    torch.cuda.synchronize()
+    ref = gemm_fp8_block_ref(xq, xs, wq, ws)
+    assert _rel(out, ref) < 5e-3
+    assert (out.float() - ref).abs().max().item() <= 0.02 * ref.abs().max().item()
+
+
+def test_gemm_fp8_block_persistent_small_grid():
+    # few CTAs -> every CTA walks many tiles through both TMEM accumulators
+    m, n, k = 512, 1024, 1024
+    x = torch.randn(m, k, device=DEV)
+    w = torch.randn(n, k, device=DEV) * 0.05
+    xq, xs = quant_act_block(x)
+    wq, ws = quant_weight_block(w)
+    out = ops.gemm_fp8_block(xq, xs, wq, ws, bn=256, max_ctas=3)
+    ref = gemm_fp8_block_ref(xq, xs, wq, ws)
+    assert _rel(out, ref) < 5e-3
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (300, 640, 1024), (2048, 4096, 4096), (77, 128256, 512),
+                                   (50, 4000, 4096), (130, 200, 128)])
+def test_gemm_bf16(m, n, k):
+    x = torch.randn(m, k, device=DEV).bfloat16()
+    w = (torch.randn(n, k, device=DEV) * 0.05).bfloat16()
+    out = ops.gemm_bf16(x, w)
+    ref = x.float() @ w.float().t()
+    assert _rel(out, ref) < 5e-3
+
+
+def _deq_close(q, s, ref, tol=1.0 / 15):
+    deq = dequant_act_block(q.float().to(FP8_DTYPE) if q.dtype != FP8_DTYPE else q, s)
+    m, k = ref.shape
+    blk_amax = ref.abs().view(m, k // 128, 128).amax(-1, keepdim=True).clamp(min=1e-6)
+    err = ((deq - ref).abs().view(m, k // 128, 128) / blk_amax).max().item()
+    assert err <= tol, err
+
+
+@pytest.mark.parametrize("m,h", [(1, 256), (7, 1024), (333, 8192), (64, 4096), (5, 1152)])
+def test_add_rmsnorm_quant(m, h):
+    hx = torch.randn(m, h, device=DEV).bfloat16()
+    dx = torch.randn(m, h, device=DEV).bfloat16()
+    w = (1 + 0.1 * torch.randn(h, device=DEV)).bfloat16()
+    h_cpu, d_cpu, w_cpu = hx.cpu().clone(), dx.cpu(), w.cpu()
+    quant = h % 128 == 0
+    q, qs, y = ops.add_rmsnorm_quant(hx, dx, w, 1e-5, quant=quant, out_bf16=True)
+    _, _, yr = ops.add_rmsnorm_quant(h_cpu, d_cpu, w_cpu, 1e-5, quant=False, out_bf16=True)
+    assert torch.equal(hx.cpu(), h_cpu)  # residual add is exact bf16 round of the fp32 sum
+    assert _rel(y.cpu(), yr) < 1e-2
+    hf = h_cpu.float()
+    yref = hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-5) * w_cpu.float()
+    if quant:
+        _deq_close(q.cpu(), qs.cpu(), yref)
+
+
+@pytest.mark.parametrize("m,f", [(1, 128), (37, 3584), (256, 14336)])
+def test_silu_mul_quant(m, f):
+    gu = torch.randn(m, 2 * f, device=DEV).bfloat16()
+    q, qs, y = ops.silu_mul_quant(gu, quant=True, out_bf16=True)
+    g, u = gu[:, :f].float().cpu(), gu[:, f:].float().cpu()
+    a = (torch.nn.functional.silu(g) * u).bfloat16()
+    assert _rel(y.cpu(), a) < 1e-2
+    _deq_close(q.cpu(), qs.cpu(), a.float())
+
+
+def test_act_quant():
+    x = torch.randn(99, 1024, device=DEV).bfloat16()
+    q, qs = ops.act_quant(x)
+    _deq_close(q.cpu(), qs.cpu(), x.float().cpu())
+
+
+def test_rope_kv_write():
+    hq, hkv, d, ps, npages = 8, 2, 128, 64, 10
+    m = 37
+    qkv = torch.randn(m, (hq + 2 * hkv) * d, device=DEV).bfloat16()
+    pos = torch.randint(0, 4000, (m,), device=DEV, dtype=torch.int32)
+    slots = torch.randperm(npages * ps, device=DEV)[:m].to(torch.int64)
+    slots[3] = -1
+    cs = ops.rope_table(4096, d, 5e5, DEV)
+    kc = torch.zeros(npages, hkv, ps, d, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    qo = ops.rope_kv_write(qkv, pos, slots, cs, kc, vc, hq, hkv, d)
+    kc2, vc2 = kc.cpu().zero_(), vc.cpu().zero_()
+    qo2 = ops.rope_kv_write(qkv.cpu(), pos.cpu(), slots.cpu(), cs.cpu(), kc2, vc2, hq, hkv, d)
+    assert _rel(qo.cpu(), qo2) < 1e-2
+    assert _rel(kc.cpu(), kc2) < 1e-2
+    assert torch.equal(vc.cpu(), vc2)
+
+
+def _paged_case(seed, q_lens, prefix, hq=8, hkv=2, shared_pages=0, tree=False):
+    """Random paged KV for R requests; the first `shared_pages` pages are shared by all requests."""
+    g = torch.Generator().manual_seed(seed)
+    d, ps = 128, 64
+    r = len(q_lens)
+    kv_len = [p + n for p, n in zip(prefix, q_lens)]
+    need = [(k + ps - 1) // ps for k in kv_len]
+    npages = shared_pages + sum(n - shared_pages for n in need) + 1
+    perm = torch.randperm(npages, generator=g).tolist()
+    shared = perm[:shared_pages]
+    nxt = shared_pages
+    page_lists = []
+    for n in need:
+        own = perm[nxt: nxt + n - shared_pages]
+        nxt += n - shared_pages
+        page_lists.append(shared + own)
+    kc = torch.randn(npages, hkv, ps, d, generator=g).bfloat16()
+    vc = torch.randn(npages, hkv, ps, d, generator=g).bfloat16()
+    t = sum(q_lens)
+    q = torch.randn(t, hq, d, generator=g).bfloat16()
+    tree_bits = None
+    if tree:
+        bits = []
+        for n in q_lens:
+            par = [-1] + [int(torch.randint(0, i, (1,), generator=g)) for i in range(1, n)]
+            for i in range(n):
+                b, j = 0, i
+                while j >= 0:
+                    b |= 1 << j
+                    j = par[j]
+                bits.append(b - (1 << 64) if b >= (1 << 63) else b)
+        tree_bits = torch.tensor(bits, dtype=torch.int64)
+    meta = make_meta(page_lists, prefix, q_lens, tree_bits, causal=not tree, device="cpu")
+    return q, kc, vc, meta
+
+
+def _to(meta, dev):
+    import dataclasses
+    return dataclasses.replace(meta, pages=meta.pages.to(dev), page_indptr=meta.page_indptr.to(dev),
+                               prefix_len=meta.prefix_len.to(dev), kv_len=meta.kv_len.to(dev),
+                               q_start=meta.q_start.to(dev), tree=None if meta.tree is None else meta.tree.to(dev))
+
+
+@pytest.mark.parametrize("case", ["prefill", "decode", "tree", "cascade_tree"])
+def test_paged_attention(case):
+    hq, hkv = 8, 2
+    if case == "prefill":
+        q, kc, vc, meta = _paged_case(1, [100, 7, 64], [0, 130, 64])
+    elif case == "decode":
+        q, kc, vc, meta = _paged_case(2, [1, 1, 1, 1], [1, 500, 64, 4000])
+    elif case == "tree":
+        q, kc, vc, meta = _paged_case(3, [64, 17], [300, 1024], tree=True)
+    else:
+        q, kc, vc, meta = _paged_case(4, [64, 64, 9], [640, 700, 520], tree=True, shared_pages=8)
+    scale = 1 / math.sqrt(128)
+    t = q.shape[0]
+    groups = cascade_groups(meta, 64) if case == "cascade_tree" else None
+    if case == "cascade_tree":
+        assert groups and groups[0][2] == 8 * 64
+    p1, p2 = build_items(meta, hq // hkv, groups)
+    # reference
+    out_ref = torch.zeros(t, hq * 128)
+    oq_ref = torch.zeros(t, hq * 128, dtype=FP8_DTYPE)
+    os_ref = torch.zeros(hq, t)
+    o_part = torch.zeros(t, hq, 128)
+    lse_part = torch.full((t, hq), float("-inf"))
+    if p1:
+        ops.paged_attention(q, kc, vc, meta, scale, o_part=o_part, lse_part=lse_part, items=p1)
+    ops.paged_attention(q, kc, vc, meta, scale, o_in=o_part if p1 else None, lse_in=lse_part if p1 else None,
+                        out=out_ref, out_q=oq_ref, out_qs=os_ref, items=p2)
+    # gpu
+    gm = _to(meta, DEV)
+    qg, kg, vg = q.to(DEV), kc.to(DEV), vc.to(DEV)
+    out = torch.zeros(t, hq * 128, device=DEV, dtype=torch.bfloat16)
+    oq = torch.zeros(t, hq * 128, device=DEV, dtype=FP8_DTYPE)
+    osc = torch.zeros(hq, t, device=DEV)
+    op = torch.zeros(t, hq, 128, device=DEV, dtype=torch.bfloat16)
+    lp = torch.full((t, hq), float("-inf"), device=DEV)
+    if p1:
+        it, tl = pack_work(p1, hq // hkv, DEV)
+        ops.paged_attention(qg, kg, vg, gm, scale, o_part=op, lse_part=lp, items=it, tiles=tl)
+    it, tl = pack_work(p2, hq // hkv, DEV)
+    ops.paged_attention(qg, kg, vg, gm, scale, o_in=op if p1 else None, lse_in=lp if p1 else None, out=out,
+                        out_q=oq, out_qs=osc, items=it, tiles=tl)
+    torch.cuda.synchronize()
+    assert _rel(out.cpu(), out_ref) < 1e-2
+    deq = (oq.cpu().float().view(t, hq, 128) * osc.cpu().t()[..., None]).view(t, hq * 128)
+    assert _rel(deq, out_ref) < 4e-2

@@ -1,0 +1,62 @@
+"""CPU checks of the op definitions (the oracles the GPU kernels are tested against)."""
+import math
+
+import torch
+
+from phung5_b200 import ops
+from phung5_b200.engine.attn_meta import build_items, cascade_groups
+from phung5_b200.weights.quant import gemm_fp8_block_ref, quant_act_block, quant_weight_block
+from tests.test_kernels_gpu import _paged_case
+
+
+def _run(q, kc, vc, meta, groups):
+    hq, hkv = q.shape[1], kc.shape[1]
+    t = q.shape[0]
+    p1, p2 = build_items(meta, hq // hkv, groups)
+    out = torch.zeros(t, hq * 128)
+    op = torch.zeros(t, hq, 128)
+    lp = torch.full((t, hq), float("-inf"))
+    if p1:
+        ops.paged_attention(q, kc, vc, meta, 1 / math.sqrt(128), o_part=op, lse_part=lp, items=p1)
+    ops.paged_attention(q, kc, vc, meta, 1 / math.sqrt(128), o_in=op if p1 else None, lse_in=lp if p1 else None,
+                        out=out, items=p2)
+    return out
+
+
+def test_cascade_equals_single_pass():
+    q, kc, vc, meta = _paged_case(4, [64, 64, 9], [640, 700, 520], tree=True, shared_pages=8)
+    groups = cascade_groups(meta, 64)
+    assert groups == [(0, 2, 512)]
+    a = _run(q, kc, vc, meta, None)
+    b = _run(q, kc, vc, meta, groups)
+    assert (a - b).abs().max() < 1e-4
+
+
+def test_tree_mask_matches_dense_reference():
+    # a token whose mask is only itself + root sees the committed prefix, the root and itself
+    from phung5_b200.models.reference import attention
+    q, kc, vc, meta = _paged_case(3, [64, 17], [300, 1024], tree=True)
+    out = _run(q, kc, vc, meta, None)
+    r = 1
+    q0, n, plen = meta.h_q_start[r], 17, meta.h_prefix_len[r]
+    pages = meta.h_pages[meta.h_page_indptr[r]:meta.h_page_indptr[r + 1]]
+    keys = torch.arange(plen + n)
+    k = kc[torch.tensor(pages)[keys // 64], :, keys % 64].float()
+    v = vc[torch.tensor(pages)[keys // 64], :, keys % 64].float()
+    bits = meta.tree[q0:q0 + n]
+    mask = torch.ones(n, plen + n, dtype=torch.bool)
+    for i in range(n):
+        for j in range(n):
+            mask[i, plen + j] = bool((int(bits[i]) >> j) & 1)
+    ref = attention(q[q0:q0 + n].float(), k, v, mask, 1 / math.sqrt(128)).reshape(n, -1)
+    assert (out[q0:q0 + n] - ref).abs().max() < 1e-4
+
+
+def test_gemm_fp8_ref_close_to_dense():
+    x = torch.randn(64, 512)
+    w = torch.randn(256, 512) * 0.05
+    xq, xs = quant_act_block(x)
+    wq, ws = quant_weight_block(w)
+    out = ops.gemm_fp8_block(xq, xs, wq, ws)
+    dense = x @ w.t()
+    assert ((out.float() - dense).norm() / dense.norm()) < 0.08
