@@ -1,0 +1,236 @@
+"""Headline benchmark: output tokens/s (and p50 TPOT) of Llama-3-70B-shaped block-scaled FP8
+speculative decoding with tensor parallelism over the GPUs of one node.
+
+Workload: 64 requests sharing one 4096-token random prefix plus 512-token unique
+random suffixes; an EAGLE-style one-layer draft head builds a 64-node top-k=8 tree (depth 6) per
+request per step; the target verifies the tree with cascade attention over the shared prefix;
+256 output tokens per request. Weights are random-init (no checkpoints offline), token ids are
+synthetic, and the accepted length per request per step is drawn from a seeded Geometric(p=0.3)
+capped at 6 (random weights never agree with their drafter; every step still computes the full
+draft, verify, target sampling and accept walk).
+
+A "step" is one speculative step of the whole batch. W warm-up steps, then exactly K timed steps
+between barriers + device synchronisation, timed with CUDA events on the launching stream; the
+per-rank time is reduced with MAX. Inputs are larger than L2 (70 GB of weights per step at TP1).
+Then K more steps are timed end to end through the public engine API (host scheduling, pinned H2D
+of step inputs, D2H of step results).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "output tok/s at Llama-3-70B FP8 TP8 spec decode, max over ranks; p50 TPOT"
+
+
+def reference_arm(args):
+    """The reference (huypg-zenai/phung5) is an application around external SGLang/vLLM engines: it has no
+    setup.py/pyproject (pip refuses to install it) and its inference engines are downloaded at container
+    start, so its own serving path cannot run offline here."""
+    line = {"impl": "reference",
+            "unavailable": "reference is not installable (no setup.py/pyproject.toml) and its SGLang/vLLM "
+                           "engines are fetched from the network at start; no offline build of its serving path",
+            "metric": METRIC, "n_gpus": args.gpus}
+    print(json.dumps(line))
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.rows.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="llama3-70b-fp8")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--prefix", type=int, default=4096)
+    ap.add_argument("--suffix", type=int, default=512)
+    ap.add_argument("--out-tokens", type=int, default=256)
+    ap.add_argument("--tree-nodes", type=int, default=64)
+    ap.add_argument("--topk", type=int, default=8)
+    ap.add_argument("--depth", type=int, default=6)
+    ap.add_argument("--comm", default="nccl", choices=["nccl", "fused"])
+    ap.add_argument("--no-cascade", action="store_true")
+    ap.add_argument("--layers", type=int, default=0, help="override layer count (smoke runs only; not a bench value)")
+    args = ap.parse_args()
+
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+
+    from phung5_b200 import ops
+    from phung5_b200.config import CacheConfig, DraftConfig, EngineConfig, ParallelConfig, SpecConfig, preset
+    from phung5_b200.engine.engine import LLMEngine
+    from phung5_b200.engine.oracle import SamplingParams
+    from phung5_b200.parallel.comm import NcclCommunicator, init_distributed
+
+    rank, world, local = init_distributed()
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    comm = NcclCommunicator() if world > 1 else None
+    if world > 1 and args.comm == "fused":
+        from phung5_b200.parallel.fused import FusedCommunicator
+        comm = FusedCommunicator()
+
+    mc = preset(args.model)
+    if args.layers:
+        mc.num_layers = args.layers
+    spec = SpecConfig(mode="tree", tree_nodes=args.tree_nodes, topk=args.topk, depth=args.depth,
+                      accept="geometric", accept_p=0.3, accept_cap=6, accept_seed=0)
+    per_req_pages = (args.prefix + args.suffix + args.out_tokens + 2 * args.tree_nodes + 128) // 64 + 2
+    num_pages = args.batch * per_req_pages + 64
+    ecfg = EngineConfig(model=mc, spec=spec, draft=DraftConfig(kind="eagle"),
+                        parallel=ParallelConfig(tp=world, comm=args.comm),
+                        cache=CacheConfig(page_size=64, num_pages=num_pages, enable_cascade=not args.no_cascade),
+                        max_prefill_tokens=8192, seed=0)
+    t0 = time.time()
+    eng = LLMEngine(ecfg, device=dev, comm=comm, max_context=args.prefix + args.suffix + args.out_tokens + 512)
+    torch.cuda.synchronize()
+    t_init = time.time() - t0
+
+    g = torch.Generator().manual_seed(1234)
+    prefix = torch.randint(0, mc.vocab, (args.prefix,), generator=g).tolist()
+    prompts = [prefix + torch.randint(0, mc.vocab, (args.suffix,), generator=g).tolist() for _ in range(args.batch)]
+    sp = SamplingParams(temperature=0.0, max_new_tokens=args.out_tokens)
+    for p in prompts:
+        eng.add_request(p, sp)
+    t0 = time.time()
+    while eng.waiting:
+        eng.step()
+    torch.cuda.synchronize()
+    t_prefill = time.time() - t0
+
+    def barrier():
+        if comm is not None:
+            comm.barrier()
+
+    for _ in range(args.warmup):
+        eng.step()
+    ops.check_status(dev)
+
+    # ---- device-timed region ----
+    n_before = eng.stats["tokens_out"]
+    per_req_before = {r.rid: len(r.out) for r in eng.running}
+    l0 = ops.launches()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    phys = int(vis.split(",")[local]) if vis else local
+    with ClockSampler(phys) as clk:
+        ev0.record()
+        for _ in range(args.steps):
+            eng.step()
+        ev1.record()
+        torch.cuda.synchronize()
+    barrier()
+    launches = ops.launches() - l0
+    ms = ev0.elapsed_time(ev1)
+    ms = comm.max_float(ms) if comm is not None else ms
+    tokens = eng.stats["tokens_out"] - n_before
+    live = [r for r in eng.running]
+    tpot = [ms / max(1, len(r.out) - per_req_before.get(r.rid, 0)) for r in live if r.rid in per_req_before]
+    ops.check_status(dev)
+
+    # ---- end-to-end region through the public API ----
+    h2d0, d2h0 = eng.stats["h2d_bytes"], eng.stats["d2h_bytes"]
+    e2e_tokens = 0
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for o in eng.step():
+            e2e_tokens += len(o.new_tokens)
+    e2e_s = time.perf_counter() - t0
+    e2e_s = comm.max_float(e2e_s) if comm is not None else e2e_s
+    h2d = (eng.stats["h2d_bytes"] - h2d0) / args.steps
+    d2h = (eng.stats["d2h_bytes"] - d2h0) / args.steps
+
+    value = tokens / (ms / 1e3)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp8_block+bf16",
+            "data": "synthetic token ids, random-init weights, geometric(p=0.3, cap 6) synthetic acceptance",
+            "config": {"model": mc.name + (f"-{mc.num_layers}L" if args.layers else ""), "global_batch": args.batch,
+                       "seq_len": args.prefix + args.suffix, "shared_prefix": args.prefix, "suffix": args.suffix,
+                       "out_tokens": args.out_tokens, "tree_nodes": args.tree_nodes, "topk": args.topk,
+                       "depth": args.depth, "parallelism": f"tp{world}", "comm": args.comm if world > 1 else "none",
+                       "cascade": not args.no_cascade, "l2": "inputs larger than L2 (weights stream every step)"},
+            "p50_tpot_ms": round(statistics.median(tpot), 3) if tpot else None,
+            "tokens_per_step": round(tokens / args.steps, 2),
+            "e2e": {"value": round(e2e_tokens / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "init_s": round(t_init, 1), "prefill_s": round(t_prefill, 1),
+        }
+        print(json.dumps(line))
+    if comm is not None:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,564 @@
+"""The serving engine: continuous batching over a paged KV pool with speculative decoding.
+
+Public API (the call a user makes):
+    eng = LLMEngine(EngineConfig(...), device="cuda")
+    rid = eng.add_request(prompt_ids, SamplingParams(...))
+    outs = eng.step()            # one scheduling step: prefill chunk(s) and/or one speculative step
+    tokens = eng.generate(prompts, params)
+
+One speculative step for the R running requests (all on device, one host round trip at the end):
+  1. draft catch-up: the drafter consumes every token committed since its last step plus the root
+     (pending token) — for EAGLE paired with the target's hidden state at the previous position;
+  2. tree expansion: `depth` rounds; each round runs the drafter on the K frontier nodes of every
+     request (tree-masked over the draft scratch KV), takes the top-K children of each by draft
+     log-probability, and keeps the K best children (cumulative score) as the next frontier;
+  3. the N-1 best candidates (ancestor-closed) become the verify tree, node 0 = root;
+  4. verify: one target forward over R*N nodes with ancestor masks; cascade attention shares the
+     prefix pages common to several requests;
+  5. accept: greedy match, seeded target-only tree sampling, or the synthetic geometric length;
+  6. commit: accepted nodes' KV rows and hidden states move to their final slots; one D2H copy of
+     (accepted count, tokens, bonus) per step feeds the host scheduler.
+The reference performs the same step inside SGLang's DFlash worker with chain drafts.
+"""
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from .. import ops
+from ..config import EngineConfig, ModelConfig, preset
+from ..models.llama import Communicator, ForwardBatch, LlamaModel, ModelWeights, random_packed_weights
+from .attn_meta import build_items, cascade_groups, make_meta, pack_work
+from .kv_pool import KVPool
+from .oracle import SamplingParams
+from .sampling import geometric_accept_len, sample_from, seeded_coins, target_probs
+
+
+@dataclass
+class Request:
+    rid: int
+    tokens: List[int]
+    prompt_len: int
+    params: SamplingParams
+    pages: List[int] = field(default_factory=list)
+    committed: int = 0        # tokens whose target KV is written
+    prefilled: int = 0        # prompt tokens processed so far
+    root: Optional[int] = None
+    dlen: int = 0             # positions with draft KV written
+    out: List[int] = field(default_factory=list)
+    finished: bool = False
+    steps: int = 0
+    accepted: List[int] = field(default_factory=list)
+    t_arrive: float = 0.0
+    t_first: float = 0.0
+    t_done: float = 0.0
+
+
+@dataclass
+class StepOutput:
+    rid: int
+    new_tokens: List[int]
+    finished: bool
+
+
+class _VocabOps:
+    """Top-k / log-softmax / argmax over vocab-sharded logits. Single rank: local ops."""
+
+    def __init__(self, comm: Communicator, vocab_start: int):
+        self.comm = comm
+        self.v0 = vocab_start
+
+    def topk_logprobs(self, logits: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        lf = logits.float()
+        lse = torch.logsumexp(lf, -1, keepdim=True)
+        v, i = torch.topk(lf, k, dim=-1)
+        if self.comm.size == 1:
+            return v - lse, i
+        return self.comm.topk_logprobs_merge(v, i + self.v0, lse, k)
+
+    def argmax(self, logits: torch.Tensor) -> torch.Tensor:
+        if self.comm.size == 1:
+            return logits.argmax(-1)
+        v, i = torch.max(logits.float(), -1)
+        return self.comm.argmax_merge(v, i + self.v0)
+
+    def full(self, logits: torch.Tensor) -> torch.Tensor:
+        return logits if self.comm.size == 1 else self.comm.all_gather_vocab(logits)
+
+
+class LLMEngine:
+    def __init__(self, cfg: EngineConfig, device="cuda", target: Optional[ModelWeights] = None,
+                 drafter=None, comm: Optional[Communicator] = None, num_pages: Optional[int] = None,
+                 max_context: int = 16384, dtype: torch.dtype = torch.bfloat16):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.comm = comm or Communicator()
+        self.dtype = dtype
+        mc = cfg.model
+        tp = self.comm.size
+        if target is None:
+            target = random_packed_weights(mc, self.device, seed=cfg.seed, tp_rank=self.comm.rank, tp_size=tp)
+        self.tw = target
+        self.ps = cfg.cache.page_size
+        hkv = mc.num_kv_heads // tp
+        spec = cfg.spec
+        self.K = spec.topk if spec.mode == "tree" else 1
+        self.D = spec.depth if spec.mode == "tree" else spec.num_draft
+        self.N = spec.tree_nodes if spec.mode == "tree" else spec.num_draft + 1
+        self.spec_on = spec.enabled
+        self.eagle = cfg.draft.kind == "eagle"
+        draft_layers = 0
+        if self.spec_on:
+            draft_layers = 1 if self.eagle else (drafter.cfg.num_layers if drafter is not None else cfg.draft.num_layers)
+        if num_pages is None:
+            num_pages = cfg.cache.num_pages or self._pages_from_memory(mc, hkv, draft_layers)
+        self.pool = KVPool(mc.num_layers, num_pages, hkv, self.ps, mc.head_dim, self.device,
+                           draft_layers=draft_layers, hidden=mc.hidden if (self.spec_on and self.eagle) else 0,
+                           dtype=dtype)
+        self.cos_sin = ops.rope_table(max_context + 2 * self.ps, mc.head_dim, mc.rope_theta, self.device)
+        self.max_context = max_context
+        self.target = LlamaModel(target, self.pool.k, self.pool.v, self.cos_sin, self.comm)
+        self.drafter = None
+        if self.spec_on:
+            if self.eagle:
+                from ..models.eagle import EagleHead, random_eagle
+                ew = drafter if drafter is not None else random_eagle(mc, self.device, seed=cfg.seed + 1,
+                                                                      tp_rank=self.comm.rank, tp_size=tp)
+                self.drafter = EagleHead(ew, target, self.pool.dk, self.pool.dv, self.cos_sin, self.comm)
+            else:
+                dw = drafter
+                if dw is None:
+                    dcfg = preset("tiny-draft") if mc.name == "tiny" else ModelConfig(**{**mc.to_dict(), "num_layers": cfg.draft.num_layers})
+                    dw = random_packed_weights(dcfg, self.device, seed=cfg.seed + 1, tp_rank=self.comm.rank, tp_size=tp)
+                self.drafter = LlamaModel(dw, self.pool.dk, self.pool.dv, self.cos_sin, self.comm)
+        self.vocab = _VocabOps(self.comm, target.vocab_start)
+        self.dvocab = _VocabOps(self.comm, self.drafter.w.vocab_start if (self.drafter is not None and not self.eagle)
+                                else target.vocab_start)
+        self.reqs: Dict[int, Request] = {}
+        self.waiting: List[Request] = []
+        self.running: List[Request] = []
+        self._next_rid = 0
+        self.stats = {"steps": 0, "spec_steps": 0, "tokens_out": 0, "accepted": 0, "prefill_tokens": 0,
+                      "h2d_bytes": 0, "d2h_bytes": 0}
+        self.use_cascade = cfg.cache.enable_cascade
+
+    # ------------------------------------------------------------------------------------------
+    def _pages_from_memory(self, mc: ModelConfig, hkv: int, draft_layers: int) -> int:
+        per = KVPool.bytes_per_page(mc.num_layers, hkv, self.ps, mc.head_dim, draft_layers,
+                                    mc.hidden if self.eagle else 0)
+        if self.device.type == "cuda":
+            free, _ = torch.cuda.mem_get_info(self.device)
+            budget = free * self.cfg.cache.mem_fraction - 8 * 1024 ** 3
+            return max(64, int(budget // per))
+        return 512
+
+    # ------------------------------------------------------------------------------------------
+    def add_request(self, prompt: Sequence[int], params: Optional[SamplingParams] = None) -> int:
+        rid = self._next_rid
+        self._next_rid += 1
+        r = Request(rid=rid, tokens=list(prompt), prompt_len=len(prompt), params=params or SamplingParams(),
+                    t_arrive=time.perf_counter())
+        self.reqs[rid] = r
+        self.waiting.append(r)
+        return rid
+
+    def has_work(self) -> bool:
+        return bool(self.waiting) or any(not r.finished for r in self.running)
+
+    def generate(self, prompts: Sequence[Sequence[int]], params: Optional[SamplingParams] = None) -> List[List[int]]:
+        rids = [self.add_request(p, params) for p in prompts]
+        while self.has_work():
+            self.step()
+        return [self.reqs[r].out for r in rids]
+
+    def step(self) -> List[StepOutput]:
+        outs: List[StepOutput] = []
+        if self.waiting:
+            outs += self._prefill()
+        live = [r for r in self.running if not r.finished and r.root is not None]
+        if live:
+            if self.spec_on:
+                outs += self._spec_step(live)
+            else:
+                outs += self._decode_step(live)
+        self.running = [r for r in self.running if not r.finished]
+        self.stats["steps"] += 1
+        return outs
+
+    # ------------------------------------------------------------------------------------------
+    def _slot(self, r: Request, pos: int) -> int:
+        return r.pages[pos // self.ps] * self.ps + pos % self.ps
+
+    def _ensure_pages(self, r: Request, upto: int) -> None:
+        need = (upto + self.ps - 1) // self.ps - len(r.pages)
+        if need > 0:
+            r.pages += self.pool.prefix.alloc_pages(need)
+
+    def _h2d(self, data, dtype) -> torch.Tensor:
+        t = torch.tensor(data, dtype=dtype)
+        if self.device.type == "cuda":
+            t = t.pin_memory()
+            self.stats["h2d_bytes"] += t.numel() * t.element_size()
+            return t.to(self.device, non_blocking=True)
+        return t
+
+    def _finish(self, r: Request) -> None:
+        r.finished = True
+        r.t_done = time.perf_counter()
+        n_full = min(r.committed, len(r.tokens)) // self.ps
+        self.pool.prefix.insert(r.tokens, r.pages, n_full)
+        self.pool.prefix.release(r.pages)
+        r.pages = []
+
+    def _emit(self, r: Request, new: List[int]) -> StepOutput:
+        room = r.params.max_new_tokens - len(r.out)
+        new = new[:room]
+        r.out += new
+        self.stats["tokens_out"] += len(new)
+        done = len(r.out) >= r.params.max_new_tokens or r.committed + self.N + 2 * self.ps >= self.max_context
+        if done:
+            self._finish(r)
+        return StepOutput(r.rid, new, done)
+
+    def _first_token(self, logits: torch.Tensor, reqs: List[Request]) -> List[int]:
+        full = self.vocab.full(logits)
+        temp = torch.tensor([r.params.temperature for r in reqs])
+        if float(temp.max()) <= 0:
+            return full.argmax(-1).tolist()
+        probs = target_probs(full.float().cpu(), temp, torch.tensor([r.params.top_k for r in reqs]),
+                             torch.tensor([r.params.top_p for r in reqs]))
+        coins = seeded_coins(torch.tensor([r.params.seed for r in reqs]),
+                             torch.tensor([r.prompt_len - 1 for r in reqs]), 1)[:, 0]
+        toks = sample_from(probs, coins)
+        return [int(t) if r.params.temperature > 0 else int(a) for t, a, r in
+                zip(toks, full.argmax(-1).cpu(), reqs)]
+
+    # ------------------------------------------------------------------------------------------
+    # prefill
+    # ------------------------------------------------------------------------------------------
+    def _prefill(self) -> List[StepOutput]:
+        budget = self.cfg.max_prefill_tokens
+        batch: List[Tuple[Request, int, int]] = []  # (req, start, end)
+        local_keys: Dict[int, int] = {}
+        while self.waiting and budget > 0:
+            r = self.waiting[0]
+            if r.prefilled == 0 and not r.pages:
+                # prefix cache (and pages being written by requests earlier in this pass)
+                n_match = (r.prompt_len - 1) // self.ps
+                keys = self.pool.prefix.chain_keys(r.tokens, self.ps, n_match)
+                pages = self.pool.prefix.match(r.tokens, (r.prompt_len - 1))
+                for k in keys[len(pages):]:
+                    p = local_keys.get(k)
+                    if p is None:
+                        break
+                    pages.append(p)
+                    self.pool.alloc.incref([p])
+                r.pages = pages
+                r.prefilled = len(pages) * self.ps
+                r.committed = r.prefilled
+                r.dlen = r.prefilled
+            start = r.prefilled
+            end = min(r.prompt_len, start + budget)
+            self._ensure_pages(r, end)
+            for i, k in enumerate(self.pool.prefix.chain_keys(r.tokens, self.ps, end // self.ps)):
+                local_keys.setdefault(k, r.pages[i])
+            batch.append((r, start, end))
+            budget -= end - start
+            r.prefilled = end
+            if end == r.prompt_len:
+                self.waiting.pop(0)
+            else:
+                break
+        toks, pos, slots, last_rows = [], [], [], []
+        for r, s, e in batch:
+            toks += r.tokens[s:e]
+            pos += list(range(s, e))
+            slots += [self._slot(r, p) for p in range(s, e)]
+            last_rows.append(len(toks) - 1)
+        meta = make_meta([r.pages for r, _, _ in batch], [s for _, s, _ in batch], [e - s for _, s, e in batch],
+                         None, True, self.device)
+        g = self.target.hq // self.target.hkv
+        _, p2 = build_items(meta, g)
+        fb = ForwardBatch(tokens=self._h2d(toks, torch.int64), positions=self._h2d(pos, torch.int32),
+                          slots=self._h2d(slots, torch.int64), meta=meta, work2=pack_work(p2, g, self.device),
+                          logits_rows=self._h2d(last_rows, torch.int64))
+        logits, h = self.target.forward(fb, want_hidden=True)
+        if self.pool.hidden is not None:
+            self.pool.hidden[fb.slots] = h
+        self.stats["prefill_tokens"] += len(toks)
+        outs = []
+        done = [(i, r) for i, (r, s, e) in enumerate(batch) if e == r.prompt_len]
+        for r, s, e in batch:
+            r.committed = e
+        if done:
+            firsts = self._first_token(logits[[i for i, _ in done]], [r for _, r in done])
+            for (i, r), t in zip(done, firsts):
+                r.root = t
+                r.tokens.append(t)
+                r.t_first = time.perf_counter()
+                self.running.append(r)
+                outs.append(self._emit(r, [t]))
+        return outs
+
+    # ------------------------------------------------------------------------------------------
+    # plain decode (speculation off)
+    # ------------------------------------------------------------------------------------------
+    def _decode_step(self, reqs: List[Request]) -> List[StepOutput]:
+        for r in reqs:
+            self._ensure_pages(r, r.committed + 1)
+        meta = make_meta([r.pages for r in reqs], [r.committed for r in reqs], [1] * len(reqs), None, True,
+                         self.device)
+        g = self.target.hq // self.target.hkv
+        _, p2 = build_items(meta, g)
+        fb = ForwardBatch(tokens=self._h2d([r.root for r in reqs], torch.int64),
+                          positions=self._h2d([r.committed for r in reqs], torch.int32),
+                          slots=self._h2d([self._slot(r, r.committed) for r in reqs], torch.int64), meta=meta,
+                          work2=pack_work(p2, g, self.device))
+        logits, _ = self.target.forward(fb)
+        nxt = self._first_token(logits, reqs) if any(r.params.temperature > 0 for r in reqs) else \
+            self.vocab.argmax(logits).tolist()
+        outs = []
+        for r, t in zip(reqs, nxt):
+            r.committed += 1
+            r.root = t
+            r.tokens.append(t)
+            outs.append(self._emit(r, [t]))
+        return outs
+
+    # ------------------------------------------------------------------------------------------
+    # speculative step
+    # ------------------------------------------------------------------------------------------
+    def _draft_forward(self, fb: ForwardBatch, hidden_in: Optional[torch.Tensor]):
+        if self.eagle:
+            return self.drafter.forward(fb, hidden_in)
+        logits, _ = self.drafter.forward(fb)
+        return logits, None
+
+    def _groups(self, meta):
+        if not self.use_cascade:
+            return None
+        gr = cascade_groups(meta, self.ps)
+        return gr or None
+
+    def _work(self, meta, groups):
+        g = self.target.hq // self.target.hkv
+        p1, p2 = build_items(meta, g, groups)
+        return (pack_work(p1, g, self.device) if p1 else None), pack_work(p2, g, self.device)
+
+    def _spec_step(self, reqs: List[Request]) -> List[StepOutput]:
+        dev = self.device
+        R, K, D, N = len(reqs), self.K, self.D, self.N
+        scratch = 1 + (D - 1) * K
+        for r in reqs:
+            self._ensure_pages(r, r.committed + max(N, scratch) + 1)
+        maxp = max(len(r.pages) for r in reqs)
+        pt = self._h2d([r.pages + [0] * (maxp - len(r.pages)) for r in reqs], torch.int64)  # [R, maxp]
+        c_h = [r.committed for r in reqs]
+        c = self._h2d(c_h, torch.int64)
+        ridx = torch.arange(R, device=dev)
+
+        def slots_of(pos):  # pos [R, n] (device) -> slots
+            return pt.gather(1, pos // self.ps) * self.ps + pos % self.ps
+
+        # ---- 1. draft catch-up: positions [dlen, committed] (root at `committed`) ----
+        cu_tok, cu_pos, cu_slot, cu_hslot, last = [], [], [], [], []
+        for r in reqs:
+            for p in range(r.dlen, r.committed + 1):
+                cu_tok.append(r.tokens[p])
+                cu_pos.append(p)
+                cu_slot.append(self._slot(r, p))
+                cu_hslot.append(self._slot(r, p - 1) if p > 0 else 0)
+            last.append(len(cu_tok) - 1)
+        meta = make_meta([r.pages for r in reqs], [r.dlen for r in reqs], [r.committed + 1 - r.dlen for r in reqs],
+                         None, True, dev)
+        w1, w2 = self._work(meta, self._groups(meta))
+        fb = ForwardBatch(tokens=self._h2d(cu_tok, torch.int64), positions=self._h2d(cu_pos, torch.int32),
+                          slots=self._h2d(cu_slot, torch.int64), meta=meta, work1=w1, work2=w2,
+                          logits_rows=self._h2d(last, torch.int64))
+        hid_in = self.pool.hidden[self._h2d(cu_hslot, torch.int64)] if self.eagle else None
+        logits, feat = self._draft_forward(fb, hid_in)
+        for r in reqs:
+            r.dlen = r.committed + 1
+        root_feat = feat[fb.logits_rows] if feat is not None else None
+
+        # ---- 2. tree expansion ----
+        lp, ti = self.dvocab.topk_logprobs(logits, K)          # [R, K]
+        pool_tok, pool_score = [ti], [lp]
+        pool_par = [torch.full((R, K), -1, dtype=torch.int64, device=dev)]
+        pool_depth = [torch.ones(R, K, dtype=torch.int64, device=dev)]
+        front_idx = torch.arange(K, device=dev).expand(R, K)        # pool indices of the frontier
+        front_tok, front_score = ti, lp
+        front_bits_parent = torch.zeros(R, K, dtype=torch.int64, device=dev)
+        front_feat = root_feat[:, None, :].expand(R, K, -1) if root_feat is not None else None
+        n_pool = K
+        for d in range(1, D):
+            j = torch.arange(K, device=dev)
+            sidx = (d - 1) * K + j                                   # scratch entry of each frontier node
+            bits = front_bits_parent | (torch.ones_like(front_bits_parent) << sidx[None, :])
+            pos = (c[:, None] + d).expand(R, K)
+            sl = slots_of(c[:, None] + 1 + sidx[None, :])
+            dmeta = make_meta([r.pages for r in reqs], [r.committed + 1 for r in reqs], [K] * R, None, False, dev)
+            dmeta.tree = bits.reshape(-1)
+            dmeta.h_prefix_len = [ch + 1 for ch in c_h]
+            dmeta.h_kv_len = [ch + 1 + d * K for ch in c_h]
+            dmeta.kv_len = dmeta.prefix_len + d * K
+            # draft scratch holds d*K entries after this round; keys [prefix, prefix + d*K)
+            dw1, dw2 = self._work(dmeta, self._groups(dmeta))
+            fb = ForwardBatch(tokens=front_tok.reshape(-1), positions=pos.reshape(-1).to(torch.int32),
+                              slots=sl.reshape(-1), meta=dmeta, work1=dw1, work2=dw2)
+            lg, fe = self._draft_forward(fb, front_feat.reshape(R * K, -1) if front_feat is not None else None)
+            clp, cti = self.dvocab.topk_logprobs(lg, K)              # [R*K, K]
+            cscore = (front_score.reshape(-1, 1) + clp).reshape(R, K * K)
+            ctok = cti.reshape(R, K * K)
+            cpar = front_idx.reshape(R, K, 1).expand(R, K, K).reshape(R, K * K)
+            pool_tok.append(ctok)
+            pool_score.append(cscore)
+            pool_par.append(cpar)
+            pool_depth.append(torch.full((R, K * K), d + 1, dtype=torch.int64, device=dev))
+            base = n_pool
+            n_pool += K * K
+            # next frontier: K best children
+            fs, fi = torch.topk(cscore, K, dim=-1)
+            front_idx = base + fi
+            front_tok = ctok.gather(1, fi)
+            front_score = fs
+            prow = fi // K                                          # which frontier row produced it
+            front_bits_parent = bits.gather(1, prow)
+            if fe is not None:
+                fe = fe.reshape(R, K, -1)
+                front_feat = fe.gather(1, prow[..., None].expand(R, K, fe.shape[-1]))
+        P_tok = torch.cat(pool_tok, 1)
+        P_score = torch.cat(pool_score, 1)
+        P_par = torch.cat(pool_par, 1)
+        P_depth = torch.cat(pool_depth, 1)
+
+        # ---- 3. select the verify tree ----
+        nsel = N - 1
+        adj = P_score - 1e-4 * P_depth.float()
+        _, sel = torch.topk(adj, nsel, dim=-1)
+        key = P_depth.gather(1, sel).float() * 1e4 - adj.gather(1, sel)
+        order = torch.argsort(key, dim=-1)
+        sel = sel.gather(1, order)                                    # pool idx of nodes 1..N-1
+        node_of = torch.zeros(R, n_pool, dtype=torch.int64, device=dev)
+        node_of.scatter_(1, sel, torch.arange(1, N, device=dev).expand(R, nsel))
+        par_pool = P_par.gather(1, sel)
+        parent = torch.cat([torch.full((R, 1), -1, device=dev, dtype=torch.int64),
+                            torch.where(par_pool < 0, torch.zeros_like(par_pool),
+                                        node_of.gather(1, par_pool.clamp(min=0)))], 1)      # [R, N]
+        depth = torch.cat([torch.zeros(R, 1, dtype=torch.int64, device=dev), P_depth.gather(1, sel)], 1)
+        roots = self._h2d([r.root for r in reqs], torch.int64)
+        tokens = torch.cat([roots[:, None], P_tok.gather(1, sel)], 1)
+        nb = torch.ones(R, N, dtype=torch.int64, device=dev) << torch.arange(N, device=dev)[None, :]
+        tbits = nb.clone()
+        for dd in range(1, D + 1):
+            pb = tbits.gather(1, parent.clamp(min=0))
+            tbits = torch.where(depth == dd, pb | nb, tbits)
+
+        # ---- 4. verify ----
+        vpos = c[:, None] + depth
+        vslot = slots_of(c[:, None] + torch.arange(N, device=dev)[None, :])
+        vmeta = make_meta([r.pages for r in reqs], c_h, [N] * R, None, False, dev)
+        vmeta.tree = tbits.reshape(-1)
+        vw1, vw2 = self._work(vmeta, self._groups(vmeta))
+        fb = ForwardBatch(tokens=tokens.reshape(-1), positions=vpos.reshape(-1).to(torch.int32),
+                          slots=vslot.reshape(-1), meta=vmeta, work1=vw1, work2=vw2)
+        vlogits, vh = self.target.forward(fb, want_hidden=self.eagle)
+        if self.pool.hidden is not None:
+            self.pool.hidden[fb.slots] = vh
+
+        # ---- 5. accept ----
+        acc_nodes, bonus = self._accept(reqs, vlogits.reshape(R, N, -1), tokens, parent, depth, c)
+
+        # ---- 6. commit ----
+        valid = acc_nodes >= 0
+        jj = torch.arange(D, device=dev)[None, :].expand(R, D)
+        src = slots_of(c[:, None] + acc_nodes.clamp(min=0))
+        dst = slots_of(c[:, None] + 1 + jj)
+        self.pool.move_slots(src[valid], dst[valid])
+        acc_tok = torch.where(valid, tokens.gather(1, acc_nodes.clamp(min=0)), torch.full_like(acc_nodes, -1))
+        packed = torch.cat([valid.sum(1, keepdim=True), acc_tok, bonus[:, None]], 1).cpu()
+        self.stats["d2h_bytes"] += packed.numel() * packed.element_size()
+        outs = []
+        for i, r in enumerate(reqs):
+            n = int(packed[i, 0])
+            new = [int(x) for x in packed[i, 1:1 + n]] + [int(packed[i, -1])]
+            r.tokens += new
+            r.committed += 1 + n
+            r.root = new[-1]
+            r.steps += 1
+            r.accepted.append(n)
+            self.stats["accepted"] += n
+            outs.append(self._emit(r, new))
+        self.stats["spec_steps"] += 1
+        return outs
+
+    def _accept(self, reqs, logits, tokens, parent, depth, c):
+        """Returns (accepted node ids [R, D] (-1 = none), bonus tokens [R])."""
+        dev = self.device
+        R, N, D = len(reqs), self.N, self.D
+        greedy_all = all(r.params.temperature <= 0 for r in reqs)
+        cur = torch.zeros(R, dtype=torch.int64, device=dev)
+        alive = torch.ones(R, dtype=torch.bool, device=dev)
+        acc = torch.full((R, D), -1, dtype=torch.int64, device=dev)
+        nidx = torch.arange(N, device=dev)[None, :]
+        spec = self.cfg.spec
+        if spec.accept == "geometric":
+            steps = torch.tensor([r.steps for r in reqs])
+            rid = torch.tensor([r.rid for r in reqs])
+            ngeo = geometric_accept_len(spec.accept_seed, steps, rid, spec.accept_p, spec.accept_cap).to(dev)
+        if greedy_all or spec.accept == "geometric":
+            tgt = self.vocab.argmax(logits.reshape(R * N, -1)).reshape(R, N)
+            for d in range(1, D + 1):
+                kids = parent == cur[:, None]
+                if spec.accept == "geometric":
+                    match = kids & (d <= ngeo)[:, None]
+                else:
+                    match = kids & (tokens == tgt.gather(1, cur[:, None]))
+                match &= alive[:, None]
+                has = match.any(1)
+                first = torch.where(match, nidx.expand(R, N), torch.full_like(tokens, N)).min(1).values
+                acc[:, d - 1] = torch.where(has, first, torch.full_like(first, -1))
+                cur = torch.where(has, first, cur)
+                alive &= has
+            return acc, tgt.gather(1, cur[:, None])[:, 0]
+        # seeded target-only tree sampling (per-request temperature / top-k / top-p)
+        temp = torch.tensor([r.params.temperature for r in reqs], device=dev)
+        topk = torch.tensor([r.params.top_k for r in reqs], device=dev)
+        topp = torch.tensor([r.params.top_p for r in reqs], device=dev)
+        coins = seeded_coins(torch.tensor([r.params.seed for r in reqs]), c.cpu(), D + 2).to(dev)
+        rows = torch.arange(R, device=dev)
+        bonus = torch.zeros(R, dtype=torch.int64, device=dev)
+        done = torch.zeros(R, dtype=torch.bool, device=dev)
+        for d in range(1, D + 2):
+            lg = self.vocab.full(logits[rows, cur])
+            p = target_probs(lg, temp, topk, topp)                        # [R, V]
+            kids = (parent == cur[:, None]) & ~done[:, None] & (d <= D)
+            kp = torch.where(kids, p.gather(1, tokens.clamp(min=0)), torch.zeros_like(p[:, :N]))
+            cum = torch.cumsum(kp, 1)
+            u = coins[:, d - 1]
+            hit = kids & (u[:, None] < cum)
+            has = hit.any(1) & ~done
+            first = torch.where(hit, nidx.expand(R, N), torch.full_like(tokens, N)).min(1).values
+            # rows that stop here draw the bonus from p minus the children's tokens
+            stop = ~has & ~done
+            if stop.any():
+                hitcnt = torch.zeros(p.shape, dtype=torch.int32, device=dev).scatter_add_(
+                    1, tokens.clamp(min=0), kids.to(torch.int32))
+                q = p.masked_fill(hitcnt > 0, 0.0)
+                empty = q.sum(1) <= 0
+                q = torch.where(empty[:, None], p, q)
+                samp = sample_from(q, coins[:, D + 1])
+                greedy_rows = temp <= 0
+                samp = torch.where(greedy_rows, p.argmax(1), samp)
+                bonus = torch.where(stop, samp, bonus)
+            if d <= D:
+                acc[:, d - 1] = torch.where(has, first, torch.full_like(first, -1))
+                cur = torch.where(has, first, cur)
+            done |= stop
+            if bool(done.all()):
+                break
+        return acc, bonus

@@ -1,0 +1,307 @@
+"""Engine model for Llama-family decoders (dense SwiGLU; Mixtral MoE in models/mixtral.py).
+
+Weights are packed for the kernels: q/k/v fused into one column-parallel projection, gate/up fused
+into one [2F, H] projection (gate rows, then up rows), o/down row-parallel. Under tensor parallelism
+rank r keeps heads [r*Hq/tp, (r+1)*Hq/tp) (and the matching KV heads) and FFN columns
+[r*F/tp, (r+1)*F/tp); o_proj and down_proj produce partial sums that the communicator reduces.
+
+Per layer (fp8_block):
+  (xq, xs) = add_rmsnorm_quant(h, delta, w_in)       h <- h + delta (previous MLP output, reduced)
+  qkv      = gemm_fp8_block(xq, xs, Wqkv)            tcgen05
+  q        = rope_kv_write(qkv, pos, slots)          k/v -> paged cache
+  (aq, as) = paged_attention(q, ...)                 fp8 output, one scale per (token, head)
+  o        = gemm_fp8_block(aq, as, Wo)  -> reduce
+  (xq, xs) = add_rmsnorm_quant(h, o, w_post)
+  gu       = gemm_fp8_block(xq, xs, Wgu)
+  (aq, as) = silu_mul_quant(gu)
+  delta    = gemm_fp8_block(aq, as, Wd)  -> reduce
+bf16 models run the same sequence with bf16 activations and gemm_bf16.
+The reference runs these layers inside SGLang with its FP8 GEMM table and fused SiLU+quant patches
+(docker/opt/v5/wq/kopt_wq.py:92-116, docker/opt/v5/fusedq/fusedq.py:289-329).
+"""
+from __future__ import annotations
+
+import math
+import zlib
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Tuple
+
+import torch
+
+from .. import ops
+from ..config import ModelConfig
+from ..weights.quant import FP8_DTYPE, quant_weight_block
+
+
+@dataclass
+class Linear:
+    """A packed linear layer: bf16 weight [N, K], or fp8 e4m3 [N, K] + fp32 block scales [ceil(N/128), K/128]."""
+
+    w: torch.Tensor
+    ws: Optional[torch.Tensor] = None
+
+    @property
+    def fp8(self) -> bool:
+        return self.ws is not None
+
+    @property
+    def out_features(self) -> int:
+        return self.w.shape[0]
+
+    def __call__(self, x, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.fp8:
+            xq, xs = x
+            return ops.gemm_fp8_block(xq, xs, self.w, self.ws, out=out)
+        return ops.gemm_bf16(x, self.w, out=out)
+
+
+@dataclass
+class LayerWeights:
+    in_norm: torch.Tensor
+    post_norm: torch.Tensor
+    qkv: Linear
+    o: Linear
+    gu: Optional[Linear] = None       # dense MLP
+    down: Optional[Linear] = None
+    moe: Optional[object] = None      # MoE block (models/mixtral.py)
+
+
+@dataclass
+class ModelWeights:
+    cfg: ModelConfig
+    embed: torch.Tensor               # [V, H] bf16 (full vocab on every rank)
+    layers: List[LayerWeights]
+    final_norm: torch.Tensor
+    lm_head: torch.Tensor             # [V_local, H] bf16 (vocab-sharded under TP)
+    vocab_start: int = 0
+    tp_rank: int = 0
+    tp_size: int = 1
+
+    @property
+    def fp8(self) -> bool:
+        return self.layers[0].qkv.fp8
+
+
+def _shard_rows(t: torch.Tensor, rank: int, size: int) -> torch.Tensor:
+    n = t.shape[0] // size
+    return t[rank * n: (rank + 1) * n]
+
+
+def _shard_cols(t: torch.Tensor, rank: int, size: int) -> torch.Tensor:
+    n = t.shape[1] // size
+    return t[:, rank * n: (rank + 1) * n]
+
+
+def _pack_linear(parts: List[Tuple[torch.Tensor, Optional[torch.Tensor]]], device, fp8: bool,
+                 dtype: torch.dtype = torch.bfloat16) -> Linear:
+    """Concatenate row blocks of (weight, scale_inv) pairs; requantize when the checkpoint is not fp8 but
+    the model runs fp8. Row blocks must be multiples of 128 rows for fp8 scale alignment."""
+    ws_list, ss_list = [], []
+    for w, s in parts:
+        if fp8:
+            if s is None:
+                q, s = quant_weight_block(w.to(device).float())
+                ws_list.append(q)
+                ss_list.append(s)
+            else:
+                ws_list.append(w.to(device))
+                ss_list.append(s.to(device).float())
+        else:
+            if s is not None:
+                from .reference import dequant_block_fp8
+                w = dequant_block_fp8(w, s)
+            ws_list.append(w.to(device=device, dtype=dtype))
+    w = torch.cat(ws_list, 0).contiguous()
+    return Linear(w, torch.cat(ss_list, 0).contiguous() if fp8 else None)
+
+
+def _get(wd: Dict[str, torch.Tensor], name: str):
+    return wd[name], wd.get(name + "_scale_inv")
+
+
+def _row_shard_pair(pair, rank, size):
+    w, s = pair
+    w = _shard_rows(w, rank, size)
+    if s is not None:
+        s = _shard_rows(s, rank, size)
+    return w, s
+
+
+def _col_shard_pair(pair, rank, size):
+    w, s = pair
+    w = _shard_cols(w, rank, size)
+    if s is not None:
+        s = _shard_cols(s, rank, size)
+    return w, s
+
+
+def pack_weights(cfg: ModelConfig, wd: Dict[str, torch.Tensor], device, tp_rank: int = 0, tp_size: int = 1,
+                 prefix: str = "model.", dtype: torch.dtype = torch.bfloat16) -> ModelWeights:
+    """HF-named (optionally fp8 block-scaled) weights -> packed, TP-sharded device weights."""
+    fp8 = cfg.quant == "fp8_block"
+    assert cfg.num_heads % tp_size == 0 and cfg.num_kv_heads % tp_size == 0 and cfg.ffn % tp_size == 0
+    layers = []
+    if cfg.quant != "fp8_block":
+        fp8 = False
+    for i in range(cfg.num_layers):
+        p = f"{prefix}layers.{i}."
+        qkv = _pack_linear([_row_shard_pair(_get(wd, p + f"self_attn.{n}.weight"), tp_rank, tp_size)
+                            for n in ("q_proj", "k_proj", "v_proj")], device, fp8, dtype)
+        o = _pack_linear([_col_shard_pair(_get(wd, p + "self_attn.o_proj.weight"), tp_rank, tp_size)], device, fp8, dtype)
+        lw = LayerWeights(in_norm=wd[p + "input_layernorm.weight"].to(device, dtype),
+                          post_norm=wd[p + "post_attention_layernorm.weight"].to(device, dtype),
+                          qkv=qkv, o=o)
+        if cfg.is_moe:
+            from .mixtral import pack_moe
+            lw.moe = pack_moe(cfg, wd, p, device, tp_rank, tp_size)
+        else:
+            lw.gu = _pack_linear([_row_shard_pair(_get(wd, p + f"mlp.{n}.weight"), tp_rank, tp_size)
+                                  for n in ("gate_proj", "up_proj")], device, fp8, dtype)
+            lw.down = _pack_linear([_col_shard_pair(_get(wd, p + "mlp.down_proj.weight"), tp_rank, tp_size)],
+                                   device, fp8, dtype)
+        layers.append(lw)
+    embed = wd[f"{prefix}embed_tokens.weight"].to(device, dtype)
+    head = embed if cfg.tie_embeddings else wd["lm_head.weight"]
+    vl = cfg.vocab // tp_size
+    return ModelWeights(cfg=cfg, embed=embed, layers=layers,
+                        final_norm=wd[f"{prefix}norm.weight"].to(device, dtype),
+                        lm_head=head[tp_rank * vl:(tp_rank + 1) * vl].to(device, dtype).contiguous(),
+                        vocab_start=tp_rank * vl, tp_rank=tp_rank, tp_size=tp_size)
+
+
+def random_packed_weights(cfg: ModelConfig, device, seed: int = 0, tp_rank: int = 0, tp_size: int = 1,
+                          std: float = 0.02) -> ModelWeights:
+    """Random-init packed weights generated directly on the device, shard by shard (no host copy of
+    the full model: 70B fp8 is generated in seconds). Each rank draws its own shard from a seed
+    derived from (seed, layer, tensor, rank)."""
+    fp8 = cfg.quant == "fp8_block"
+    h, hd = cfg.hidden, cfg.head_dim
+    hq, hkv, f = cfg.num_heads // tp_size, cfg.num_kv_heads // tp_size, cfg.ffn // tp_size
+    gen = torch.Generator(device=device)
+
+    def rnd(n, k, tag):
+        gen.manual_seed(zlib.crc32(repr((seed, tag, tp_rank)).encode()) & 0x7FFFFFFF)
+        w = torch.randn(n, k, device=device, generator=gen, dtype=torch.bfloat16) * std
+        if fp8:
+            q, s = quant_weight_block(w.float())
+            del w
+            return Linear(q, s)
+        return Linear(w)
+
+    layers = []
+    for i in range(cfg.num_layers):
+        lw = LayerWeights(in_norm=torch.ones(h, device=device, dtype=torch.bfloat16),
+                          post_norm=torch.ones(h, device=device, dtype=torch.bfloat16),
+                          qkv=rnd((hq + 2 * hkv) * hd, h, (i, "qkv")), o=rnd(h, hq * hd, (i, "o")))
+        if cfg.is_moe:
+            from .mixtral import random_moe
+            lw.moe = random_moe(cfg, device, seed, i, tp_rank, tp_size, std)
+        else:
+            lw.gu = rnd(2 * f, h, (i, "gu"))
+            lw.down = rnd(h, f, (i, "down"))
+        layers.append(lw)
+        torch.cuda.empty_cache() if torch.device(device).type == "cuda" else None
+    gen.manual_seed(seed * 7 + 1)
+    embed = torch.randn(cfg.vocab, h, device=device, generator=gen, dtype=torch.bfloat16) * std
+    vl = cfg.vocab // tp_size
+    gen.manual_seed(seed * 7 + 2 + tp_rank)
+    head = torch.randn(vl, h, device=device, generator=gen, dtype=torch.bfloat16) * std
+    return ModelWeights(cfg=cfg, embed=embed, layers=layers, final_norm=torch.ones(h, device=device, dtype=torch.bfloat16),
+                        lm_head=head, vocab_start=tp_rank * vl, tp_rank=tp_rank, tp_size=tp_size)
+
+
+# ------------------------------------------------------------------------------------------------
+# forward
+# ------------------------------------------------------------------------------------------------
+
+@dataclass
+class ForwardBatch:
+    """Per-forward inputs (device tensors) plus the attention work lists."""
+
+    tokens: torch.Tensor          # int64 [T]
+    positions: torch.Tensor       # int32 [T]
+    slots: torch.Tensor           # int64 [T] cache slot (page * page_size + offset)
+    meta: object                  # AttnMeta
+    work1: Optional[tuple] = None  # cascade pass-1 (items, tiles) or None
+    work2: tuple = None            # main pass (items, tiles)
+    logits_rows: Optional[torch.Tensor] = None  # rows whose logits are needed (None = all)
+
+
+class Communicator:
+    """Tensor-parallel reduction hook; the single-GPU communicator is the identity."""
+
+    size = 1
+    rank = 0
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        return x
+
+    def all_gather_vocab(self, x: torch.Tensor) -> torch.Tensor:
+        return x
+
+
+class LlamaModel:
+    """Runs a packed Llama-family model over a paged KV cache."""
+
+    def __init__(self, w: ModelWeights, kv_k: torch.Tensor, kv_v: torch.Tensor, cos_sin: torch.Tensor,
+                 comm: Optional[Communicator] = None):
+        self.w = w
+        self.cfg = w.cfg
+        self.kv_k = kv_k  # [L, P, Hkv_local, page, D]
+        self.kv_v = kv_v
+        self.cos_sin = cos_sin
+        self.comm = comm or Communicator()
+        self.hq = self.cfg.num_heads // w.tp_size
+        self.hkv = self.cfg.num_kv_heads // w.tp_size
+        self.scale = 1.0 / math.sqrt(self.cfg.head_dim)
+
+    def attention(self, li: int, q: torch.Tensor, fb: ForwardBatch, fp8_out: bool):
+        t = q.shape[0]
+        dt = q.dtype
+        d = self.cfg.head_dim
+        kc, vc = self.kv_k[li], self.kv_v[li]
+        o_part = lse_part = None
+        if fb.work1 is not None:
+            o_part = torch.empty(t, self.hq, d, dtype=dt, device=q.device)
+            lse_part = torch.full((t, self.hq), float("-inf"), dtype=torch.float32, device=q.device)
+            it, tl = fb.work1
+            ops.paged_attention(q, kc, vc, fb.meta, self.scale, o_part=o_part, lse_part=lse_part, items=it, tiles=tl)
+        it, tl = fb.work2
+        if fp8_out:
+            oq = torch.empty(t, self.hq * d, dtype=FP8_DTYPE, device=q.device)
+            os_ = torch.empty(self.hq, t, dtype=torch.float32, device=q.device)
+            ops.paged_attention(q, kc, vc, fb.meta, self.scale, o_in=o_part, lse_in=lse_part, out_q=oq, out_qs=os_,
+                                items=it, tiles=tl)
+            return (oq, os_)
+        out = torch.empty(t, self.hq * d, dtype=dt, device=q.device)
+        ops.paged_attention(q, kc, vc, fb.meta, self.scale, o_in=o_part, lse_in=lse_part, out=out, items=it,
+                            tiles=tl)
+        return out
+
+    def layer(self, li: int, h: torch.Tensor, delta: Optional[torch.Tensor], fb: ForwardBatch) -> torch.Tensor:
+        lw = self.w.layers[li]
+        cfg = self.cfg
+        fp8 = lw.qkv.fp8
+        xq, xs, xb = ops.add_rmsnorm_quant(h, delta, lw.in_norm, cfg.rms_eps, quant=fp8, out_bf16=not fp8)
+        qkv = lw.qkv((xq, xs) if fp8 else xb)
+        q = ops.rope_kv_write(qkv, fb.positions, fb.slots, self.cos_sin, self.kv_k[li], self.kv_v[li], self.hq,
+                              self.hkv, cfg.head_dim)
+        a = self.attention(li, q, fb, fp8)
+        o = self.comm.all_reduce(lw.o(a))
+        xq, xs, xb = ops.add_rmsnorm_quant(h, o, lw.post_norm, cfg.rms_eps, quant=fp8, out_bf16=not fp8)
+        if lw.moe is not None:
+            return self.comm.all_reduce(lw.moe((xq, xs) if fp8 else xb, xb))
+        gu = lw.gu((xq, xs) if fp8 else xb)
+        aq, as_, ab = ops.silu_mul_quant(gu, quant=fp8, out_bf16=not fp8)
+        return self.comm.all_reduce(lw.down((aq, as_) if fp8 else ab))
+
+    def forward(self, fb: ForwardBatch, want_hidden: bool = False):
+        """Returns (logits [rows, V_local] bf16, final residual h [T, H] bf16 (pre-norm) if want_hidden)."""
+        h = self.w.embed[fb.tokens]
+        delta = None
+        for li in range(self.cfg.num_layers):
+            delta = self.layer(li, h, delta, fb)
+        _, _, y = ops.add_rmsnorm_quant(h, delta, self.w.final_norm, self.cfg.rms_eps, quant=False, out_bf16=True)
+        rows = y if fb.logits_rows is None else y[fb.logits_rows]
+        logits = ops.gemm_bf16(rows, self.w.lm_head)
+        return logits, (h if want_hidden else None)

@@ -30,7 +30,16 @@ STATUS_CODES = {1: "timeout in TMA producer", 2: "timeout in MMA issuer", 3: "ti
                 4: "timeout waiting for a peer rank", 5: "bad arguments"}
 
 
+_LAUNCHES = [0]
+
+
+def launches() -> int:
+    """Number of native kernel launches issued through this module so far (all devices)."""
+    return _LAUNCHES[0]
+
+
 def ext():
+    _LAUNCHES[0] += 1
     if _C is None:
         raise RuntimeError(f"phung5_b200._C is not built (python setup.py build_ext --inplace): {_C_ERR}")
     return _C
@@ -85,7 +94,7 @@ def gemm_bf16(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = No
               max_ctas: int = 0) -> torch.Tensor:
     """x [M,K] bf16 @ w [N,K]^T -> bf16 [M,N] (fp32 accumulate)."""
     if out is None:
-        out = torch.empty(x.shape[0], w.shape[0], dtype=torch.bfloat16, device=x.device)
+        out = torch.empty(x.shape[0], w.shape[0], dtype=torch.bfloat16 if x.is_cuda else x.dtype, device=x.device)
     if x.is_cuda:
         ext().gemm_bf16(x, w, out, status_tensor(x.device), bn, max_ctas)
     else:
@@ -107,7 +116,7 @@ def add_rmsnorm_quant(h: torch.Tensor, delta: Optional[torch.Tensor], w: torch.T
         q = torch.empty(m, hd, dtype=FP8_DTYPE, device=h.device)
         qs = torch.empty(hd // 128, m, dtype=torch.float32, device=h.device)
     if out_bf16:
-        y = torch.empty(m, hd, dtype=torch.bfloat16, device=h.device)
+        y = torch.empty(m, hd, dtype=torch.bfloat16 if h.is_cuda else h.dtype, device=h.device)
     if h.is_cuda:
         ext().add_rmsnorm_quant(h, delta, w, eps, q, qs, y)
         return q, qs, y
@@ -120,7 +129,7 @@ def add_rmsnorm_quant(h: torch.Tensor, delta: Optional[torch.Tensor], w: torch.T
         q.copy_(q_)
         qs.copy_(s_)
     if out_bf16:
-        y.copy_(yf.to(torch.bfloat16))
+        y.copy_(yf)
     return q, qs, y
 
 
@@ -133,12 +142,14 @@ def silu_mul_quant(gu: torch.Tensor, quant: bool = True, out_bf16: bool = False)
         q = torch.empty(m, f, dtype=FP8_DTYPE, device=gu.device)
         qs = torch.empty(f // 128, m, dtype=torch.float32, device=gu.device)
     if out_bf16:
-        y = torch.empty(m, f, dtype=torch.bfloat16, device=gu.device)
+        y = torch.empty(m, f, dtype=torch.bfloat16 if gu.is_cuda else gu.dtype, device=gu.device)
     if gu.is_cuda:
         ext().silu_mul_quant(gu, q, qs, y)
         return q, qs, y
     g, u = gu[:, :f].float(), gu[:, f:].float()
-    a = (torch.nn.functional.silu(g) * u).to(torch.bfloat16)
+    a = (torch.nn.functional.silu(g) * u)
+    if gu.dtype == torch.bfloat16:
+        a = a.to(torch.bfloat16)
     if quant:
         q_, s_ = quant_act_block(a.float())
         q.copy_(q_)
