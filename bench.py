@@ -136,8 +136,10 @@ def main():
         mc.num_layers = args.layers
     spec = SpecConfig(mode="tree", tree_nodes=args.tree_nodes, topk=args.topk, depth=args.depth,
                       accept="geometric", accept_p=0.3, accept_cap=6, accept_seed=0)
-    per_req_pages = (args.prefix + args.suffix + args.out_tokens + 2 * args.tree_nodes + 128) // 64 + 2
-    num_pages = args.batch * per_req_pages + 64
+    # the shared prefix pages are held once (prefix cache); each request adds its suffix, outputs and
+    # speculation scratch
+    per_req_pages = (args.suffix + args.out_tokens + 2 * args.tree_nodes + 128) // 64 + 3
+    num_pages = args.prefix // 64 + args.batch * per_req_pages + 64
     ecfg = EngineConfig(model=mc, spec=spec, draft=DraftConfig(kind="eagle"),
                         parallel=ParallelConfig(tp=world, comm=args.comm),
                         cache=CacheConfig(page_size=64, num_pages=num_pages, enable_cascade=not args.no_cascade),
@@ -176,12 +178,17 @@ def main():
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     phys = int(vis.split(",")[local]) if vis else local
+    profile = os.environ.get("PHX_PROFILE_TIMED") == "1"   # ncu --profile-from-start off captures only this
     with ClockSampler(phys) as clk:
+        if profile:
+            torch.cuda.profiler.start()
         ev0.record()
         for _ in range(args.steps):
             eng.step()
         ev1.record()
         torch.cuda.synchronize()
+        if profile:
+            torch.cuda.profiler.stop()
     barrier()
     launches = ops.launches() - l0
     ms = ev0.elapsed_time(ev1)

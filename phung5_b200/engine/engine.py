@@ -385,6 +385,7 @@ class LLMEngine:
             r.dlen = r.committed + 1
         root_feat = feat[fb.logits_rows] if feat is not None else None
 
+        synth = self.cfg.spec.accept == "geometric" and K > 1
         # ---- 2. tree expansion ----
         lp, ti = self.dvocab.topk_logprobs(logits, K)          # [R, K]
         pool_tok, pool_score = [ti], [lp]
@@ -421,8 +422,14 @@ class LLMEngine:
             pool_depth.append(torch.full((R, K * K), d + 1, dtype=torch.int64, device=dev))
             base = n_pool
             n_pool += K * K
-            # next frontier: K best children
-            fs, fi = torch.topk(cscore, K, dim=-1)
+            # next frontier: K best children. Synthetic acceptance keeps the spine (frontier row 0 is the
+            # spine node; column 0 is its best child) so the drawn accept length is realizable.
+            sel_score = cscore
+            if synth:
+                sel_score = cscore.clone()
+                sel_score[:, 0] = float("inf")
+            _, fi = torch.topk(sel_score, K, dim=-1)
+            fs = cscore.gather(1, fi)
             front_idx = base + fi
             front_tok = ctok.gather(1, fi)
             front_score = fs
@@ -439,6 +446,10 @@ class LLMEngine:
         # ---- 3. select the verify tree ----
         nsel = N - 1
         adj = P_score - 1e-4 * P_depth.float()
+        if synth:
+            # spine nodes (best child of the spine at every depth) are pool entries 0, K, K+K*K, ...
+            spine = torch.tensor([0] + [K + (d - 1) * K * K for d in range(1, D)], device=dev)
+            adj = adj.index_fill(1, spine, 0.0) + torch.zeros_like(adj).index_fill(1, spine, 1e6)
         _, sel = torch.topk(adj, nsel, dim=-1)
         key = P_depth.gather(1, sel).float() * 1e4 - adj.gather(1, sel)
         order = torch.argsort(key, dim=-1)
