@@ -27,6 +27,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "attention_params.h"
 #include "common.cuh"
 
 namespace phx {
@@ -36,28 +37,7 @@ constexpr int kAttRows = 64;
 constexpr int kAttKeys = 64;
 constexpr float kLog2e = 1.4426950408889634f;
 
-struct AttnParams {
-  const __nv_bfloat16* q;   // [T, Hq, D]
-  const __nv_bfloat16* kc;  // [P, Hkv, 64, D]
-  const __nv_bfloat16* vc;
-  const int* pages;
-  const int* page_indptr;
-  const int* prefix_len;    // [R]
-  const int* q_start;       // [R]
-  const uint64_t* tree;     // [T] or null
-  const int* items;         // [W, 6]
-  const int* tile_item;     // [tiles]
-  const int* tile_row0;     // [tiles]
-  const __nv_bfloat16* o_in;  // seed partial [T, Hq, D] or null
-  const float* lse_in;        // [T, Hq]
-  __nv_bfloat16* o_part;      // partial out [T, Hq, D] or null
-  float* lse_part;
-  __nv_bfloat16* out;         // final bf16 [T, Hq*D] or null
-  uint8_t* out_q;             // final fp8 [T, Hq*D] or null
-  float* out_qs;              // [Hq, T]
-  int T, Hq, Hkv, causal, num_tiles;
-  float scale_log2;
-};
+
 
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {  // byte offset in a [rows][256B] tile
   return row * 256 + ((chunk ^ (row & 7)) << 4);
@@ -382,6 +362,14 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
   dim3 grid((unsigned)num_tiles, Hkv);
   paged_attention_kernel<<<grid, 128, smem, stream>>>(p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Launch on raw pointers (used by entry points that manage their own buffers).
+void launch_paged_attention_raw(const AttnParams& p, int num_tiles, cudaStream_t stream) {
+  const int smem = 5 * 64 * 256;
+  cudaFuncSetAttribute(paged_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  dim3 grid((unsigned)num_tiles, p.Hkv);
+  paged_attention_kernel<<<grid, 128, smem, stream>>>(p);
 }
 
 }  // namespace phx
