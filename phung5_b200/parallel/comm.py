@@ -51,9 +51,11 @@ class NcclCommunicator(Communicator):
         return x
 
     def _gather(self, x: torch.Tensor) -> torch.Tensor:
-        out = torch.empty((self.size,) + tuple(x.shape), dtype=x.dtype, device=x.device)
-        dist.all_gather_into_tensor(out, x.contiguous(), group=self.group)
-        return out
+        """[...] -> [world, ...] (gathered as one flat concatenation, the form every backend accepts)."""
+        x = x.contiguous()
+        flat = torch.empty((self.size * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(flat, x, group=self.group)
+        return flat.view((self.size,) + tuple(x.shape))
 
     def all_gather_vocab(self, x: torch.Tensor) -> torch.Tensor:
         g = self._gather(x)                       # [tp, rows, V/tp]
