@@ -23,6 +23,14 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
                      c10::optional<torch::Tensor> o_part, c10::optional<torch::Tensor> lse_part,
                      c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> out_q,
                      c10::optional<torch::Tensor> out_qs);
+void paged_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor pages,
+                        torch::Tensor page_indptr, torch::Tensor prefix_len, torch::Tensor q_start,
+                        c10::optional<torch::Tensor> tree, torch::Tensor items, torch::Tensor tile_item,
+                        torch::Tensor tile_row0, int64_t num_tiles, bool causal, double softmax_scale,
+                        c10::optional<torch::Tensor> o_in, c10::optional<torch::Tensor> lse_in,
+                        c10::optional<torch::Tensor> o_part, c10::optional<torch::Tensor> lse_part,
+                        c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> out_q,
+                        c10::optional<torch::Tensor> out_qs, torch::Tensor status);
 }  // namespace phx
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -34,4 +42,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("act_quant", &phx::act_quant);
   m.def("rope_kv_write", &phx::rope_kv_write);
   m.def("paged_attention", &phx::paged_attention);
+  m.def("paged_attention_tc", &phx::paged_attention_tc);
 }

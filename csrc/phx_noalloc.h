@@ -12,7 +12,8 @@
 //   * The partial buffer holds at most PHX_NOALLOC_MAX_ROWS (token, query-head) rows: T * Hq must not
 //     exceed it (32768 rows = 8 MiB of bf16 partials + 128 KiB of fp32 LSE). Every GPU that loads the
 //     library holds this array until the process exits. Larger calls return PHX_NOALLOC_ERR_TOO_LARGE.
-//   * head_dim must be 128 and the KV page size 64 (the kernel's tile shape).
+//   * head_dim must be 128 and the KV page size 64 (the kernel's tile shape); the work lists must be
+//     built with 64 query rows per tile (tile_row0 multiples of 64).
 //   * Runs on the current device and on `stream`, which must belong to it. The first call on a device
 //     looks up the device address of the array (cudaGetSymbolAddress); make that first call before any
 //     stream capture. Later calls only launch kernels.

@@ -124,7 +124,10 @@ def build_items(meta: AttnMeta, group_size: int, groups: Optional[List[Tuple[int
     return p1, p2
 
 
-def tiles_for(items: List[List[int]], group_size: int, rows: int = ROWS_PER_TILE):
+def tiles_for(items: List[List[int]], group_size: int, rows: Optional[int] = None):
+    if rows is None:
+        from .. import ops
+        rows = ops.attn_rows()
     ti, tr = [], []
     for i, it in enumerate(items):
         nrows = it[1] * group_size
@@ -134,8 +137,8 @@ def tiles_for(items: List[List[int]], group_size: int, rows: int = ROWS_PER_TILE
     return ti, tr
 
 
-def pack_work(items: List[List[int]], group_size: int, device, pad_tiles: int = 0):
-    ti, tr = tiles_for(items, group_size)
+def pack_work(items: List[List[int]], group_size: int, device, pad_tiles: int = 0, rows: Optional[int] = None):
+    ti, tr = tiles_for(items, group_size, rows)
     n = len(ti)
     if pad_tiles > n:
         ti = ti + [-1] * (pad_tiles - n)

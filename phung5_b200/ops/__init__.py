@@ -218,15 +218,30 @@ def rope_kv_write(qkv: torch.Tensor, pos: torch.Tensor, slots: Optional[torch.Te
 # attention
 # ------------------------------------------------------------------------------------------------
 
+ATTN_IMPL = {"impl": "tc"}   # "tc" = tcgen05 kernel (128-row tiles), "mma" = mma.sync kernel (64-row tiles)
+
+
+def attn_rows(impl: Optional[str] = None) -> int:
+    """Query rows per work tile for the selected attention kernel."""
+    return 128 if (impl or ATTN_IMPL["impl"]) == "tc" else 64
+
+
 def paged_attention(q, k_cache, v_cache, meta, softmax_scale: float, o_in=None, lse_in=None, o_part=None,
-                    lse_part=None, out=None, out_q=None, out_qs=None, items=None, tiles=None):
+                    lse_part=None, out=None, out_q=None, out_qs=None, items=None, tiles=None, impl=None):
     """Run one attention pass described by `meta` (an AttnMeta from engine/attn_meta.py) and a work list
-    (`items`, `tiles` = (tile_item, tile_row0, num_tiles)); see csrc/attention.cu for the semantics."""
+    (`items`, `tiles` = (tile_item, tile_row0, num_tiles) built with attn_rows(impl) rows per tile); see
+    csrc/attention.cu for the semantics. impl: "tc" (tcgen05, default) or "mma" (mma.sync)."""
     if q.is_cuda:
         ti, tr, nt = tiles
-        ext().paged_attention(q, k_cache, v_cache, meta.pages, meta.page_indptr, meta.prefix_len, meta.q_start,
-                              meta.tree, items, ti, tr, nt, meta.causal, softmax_scale, o_in, lse_in, o_part,
-                              lse_part, out, out_q, out_qs)
+        impl = impl or ATTN_IMPL["impl"]
+        if impl == "tc":
+            ext().paged_attention_tc(q, k_cache, v_cache, meta.pages, meta.page_indptr, meta.prefix_len,
+                                     meta.q_start, meta.tree, items, ti, tr, nt, meta.causal, softmax_scale, o_in,
+                                     lse_in, o_part, lse_part, out, out_q, out_qs, status_tensor(q.device))
+        else:
+            ext().paged_attention(q, k_cache, v_cache, meta.pages, meta.page_indptr, meta.prefix_len, meta.q_start,
+                                  meta.tree, items, ti, tr, nt, meta.causal, softmax_scale, o_in, lse_in, o_part,
+                                  lse_part, out, out_q, out_qs)
         return
     from ..engine.attn_meta import attention_reference
     attention_reference(q, k_cache, v_cache, meta, softmax_scale, items, o_in, lse_in, o_part, lse_part, out,

@@ -163,8 +163,9 @@ def _to(meta, dev):
                                q_start=meta.q_start.to(dev), tree=None if meta.tree is None else meta.tree.to(dev))
 
 
-@pytest.mark.parametrize("case", ["prefill", "decode", "tree", "cascade_tree"])
-def test_paged_attention(case):
+@pytest.mark.parametrize("impl", ["tc", "mma"])
+@pytest.mark.parametrize("case", ["prefill", "decode", "tree", "cascade_tree", "long_prefix", "gqa1"])
+def test_paged_attention(case, impl):
     hq, hkv = 8, 2
     if case == "prefill":
         q, kc, vc, meta = _paged_case(1, [100, 7, 64], [0, 130, 64])
@@ -172,13 +173,21 @@ def test_paged_attention(case):
         q, kc, vc, meta = _paged_case(2, [1, 1, 1, 1], [1, 500, 64, 4000])
     elif case == "tree":
         q, kc, vc, meta = _paged_case(3, [64, 17], [300, 1024], tree=True)
-    else:
+    elif case == "cascade_tree":
         q, kc, vc, meta = _paged_case(4, [64, 64, 9], [640, 700, 520], tree=True, shared_pages=8)
+    elif case == "long_prefix":
+        q, kc, vc, meta = _paged_case(5, [64, 64, 64, 64], [4096 + 520, 4096 + 512, 4096 + 700, 4096 + 300],
+                                      tree=True, shared_pages=64)
+    else:
+        q, kc, vc, meta = _paged_case(7, [33, 5], [200, 64], hq=4, hkv=4)
+        hq, hkv = 4, 4
     scale = 1 / math.sqrt(128)
     t = q.shape[0]
     groups = cascade_groups(meta, 64) if case == "cascade_tree" else None
     if case == "cascade_tree":
         assert groups and groups[0][2] == 8 * 64
+    if case == "long_prefix":
+        groups = cascade_groups(meta, 64)
     p1, p2 = build_items(meta, hq // hkv, groups)
     # reference
     out_ref = torch.zeros(t, hq * 128)
@@ -198,12 +207,13 @@ def test_paged_attention(case):
     osc = torch.zeros(hq, t, device=DEV)
     op = torch.zeros(t, hq, 128, device=DEV, dtype=torch.bfloat16)
     lp = torch.full((t, hq), float("-inf"), device=DEV)
+    rows = ops.attn_rows(impl)
     if p1:
-        it, tl = pack_work(p1, hq // hkv, DEV)
-        ops.paged_attention(qg, kg, vg, gm, scale, o_part=op, lse_part=lp, items=it, tiles=tl)
-    it, tl = pack_work(p2, hq // hkv, DEV)
+        it, tl = pack_work(p1, hq // hkv, DEV, rows=rows)
+        ops.paged_attention(qg, kg, vg, gm, scale, o_part=op, lse_part=lp, items=it, tiles=tl, impl=impl)
+    it, tl = pack_work(p2, hq // hkv, DEV, rows=rows)
     ops.paged_attention(qg, kg, vg, gm, scale, o_in=op if p1 else None, lse_in=lp if p1 else None, out=out,
-                        out_q=oq, out_qs=osc, items=it, tiles=tl)
+                        out_q=oq, out_qs=osc, items=it, tiles=tl, impl=impl)
     torch.cuda.synchronize()
     assert _rel(out.cpu(), out_ref) < 1e-2
     deq = (oq.cpu().float().view(t, hq, 128) * osc.cpu().t()[..., None]).view(t, hq * 128)

@@ -62,8 +62,8 @@ def _noalloc(lib, q, kc, vc, meta, gm, scale, p1, p2):
     from phung5_b200.weights.quant import FP8_DTYPE
     t, hq, hkv = q.shape[0], q.shape[1], kc.shape[1]
     g = hq // hkv
-    w1 = pack_work(p1, g, DEV) if p1 else None
-    it2, (ti2, tr2, n2) = pack_work(p2, g, DEV)
+    w1 = pack_work(p1, g, DEV, rows=64) if p1 else None      # the entry point's kernel tiles 64 rows
+    it2, (ti2, tr2, n2) = pack_work(p2, g, DEV, rows=64)
     out = torch.zeros(t, hq * 128, device=DEV, dtype=torch.bfloat16)
     oq = torch.zeros(t, hq * 128, device=DEV, dtype=FP8_DTYPE)
     osc = torch.zeros(hq, t, device=DEV)
