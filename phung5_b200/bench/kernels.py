@@ -1,0 +1,164 @@
+"""Per-kernel microbenchmarks with roofline fractions.
+
+    python -m phung5_b200.bench.kernels [--kernel NAME ...] [--iters 10]
+
+Each case is timed with CUDA events on the current stream after 3 warm-up launches, flushing L2
+(a 512 MB write) before every timed launch, and reported as achieved TFLOP/s or GB/s and as the fraction
+of the measured peaks in MEASURED_PEAKS.json (copy bandwidth, cuBLAS bf16 burst); fp8 tensor work is
+compared against twice the measured bf16 rate (the dense fp8:bf16 ratio of the part).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+from .. import ops
+from ..engine.attn_meta import build_items, cascade_groups, make_meta, pack_work
+from ..weights.quant import FP8_DTYPE
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+_FLUSH = {}
+
+
+def flush_l2(dev):
+    buf = _FLUSH.get(dev)
+    if buf is None:
+        buf = _FLUSH[dev] = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    buf.fill_(1)
+
+
+def time_it(fn, iters=10, warmup=3, dev="cuda"):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        flush_l2(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def case_gemm_fp8(m, n, k, bn=0):
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    xq, xs = ops.act_quant(x)
+    wq = (torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.05).to(FP8_DTYPE)
+    ws = torch.rand((n + 127) // 128, k // 128, device="cuda") * 0.01
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    fn = lambda: ops.gemm_fp8_block(xq, xs, wq, ws, out=out, bn=bn)
+    return fn, 2.0 * m * n * k, "fp8"
+
+
+def case_gemm_bf16(m, n, k):
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.05
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    return (lambda: ops.gemm_bf16(x, w, out=out)), 2.0 * m * n * k, "bf16"
+
+
+def _verify_case(reqs=64, nodes=64, prefix=4096, suffix=600, hq=64, hkv=8):
+    """The verify attention of the headline workload: `reqs` requests sharing `prefix` keys, each with
+    `suffix` private committed keys and a `nodes`-node tree."""
+    ps = 64
+    shared = prefix // ps
+    own = (suffix + nodes + ps - 1) // ps + 1
+    npages = shared + reqs * own + 1
+    kc = torch.randn(npages, hkv, ps, 128, device="cuda", dtype=torch.bfloat16)
+    vc = torch.randn_like(kc)
+    page_lists, nxt = [], shared
+    for _ in range(reqs):
+        page_lists.append(list(range(shared)) + list(range(nxt, nxt + own)))
+        nxt += own
+    par = [-1] + [(i - 1) // 8 if i > 8 else 0 for i in range(1, nodes)]
+    bits = []
+    for i in range(nodes):
+        b, j = 0, i
+        while j >= 0:
+            b |= 1 << j
+            j = par[j]
+        bits.append(b - (1 << 64) if b >= (1 << 63) else b)
+    tree = torch.tensor(bits * reqs, dtype=torch.int64)
+    meta = make_meta(page_lists, [prefix + suffix] * reqs, [nodes] * reqs, tree, False, "cuda")
+    q = torch.randn(reqs * nodes, hq, 128, device="cuda", dtype=torch.bfloat16)
+    return q, kc, vc, meta
+
+
+def case_attention(which, impl):
+    q, kc, vc, meta = _verify_case()
+    t, hq = q.shape[0], q.shape[1]
+    g = hq // kc.shape[1]
+    groups = cascade_groups(meta, 64)
+    p1, p2 = build_items(meta, g, groups)
+    rows = ops.attn_rows(impl)
+    scale = 1 / math.sqrt(128)
+    op = torch.empty(t, hq, 128, device="cuda", dtype=torch.bfloat16)
+    lp = torch.full((t, hq), float("-inf"), device="cuda")
+    oq = torch.empty(t, hq * 128, device="cuda", dtype=FP8_DTYPE)
+    osc = torch.empty(hq, t, device="cuda")
+    if which == "prefix":
+        it, tl = pack_work(p1, g, "cuda", rows=rows)
+        fn = lambda: ops.paged_attention(q, kc, vc, meta, scale, o_part=op, lse_part=lp, items=it, tiles=tl, impl=impl)
+        flops = 4.0 * t * hq * 4096 * 128
+    else:
+        it, tl = pack_work(p2, g, "cuda", rows=rows)
+        fn = lambda: ops.paged_attention(q, kc, vc, meta, scale, o_in=op, lse_in=lp, out_q=oq, out_qs=osc, items=it,
+                                         tiles=tl, impl=impl)
+        keys = sum(k - 4096 for k in meta.h_kv_len) / len(meta.h_kv_len)
+        flops = 4.0 * t * hq * keys * 128  # includes masked tree keys
+    return fn, flops, "bf16"
+
+
+CASES = {
+    "gemm_fp8_qkv": lambda: case_gemm_fp8(4096, 10240, 8192),
+    "gemm_fp8_o": lambda: case_gemm_fp8(4096, 8192, 8192),
+    "gemm_fp8_gate_up": lambda: case_gemm_fp8(4096, 57344, 8192),
+    "gemm_fp8_down": lambda: case_gemm_fp8(4096, 8192, 28672),
+    "gemm_fp8_gate_up_tp8": lambda: case_gemm_fp8(4096, 7168, 8192),
+    "gemm_fp8_draft_m512": lambda: case_gemm_fp8(512, 57344, 8192),
+    "gemm_bf16_lm_head": lambda: case_gemm_bf16(4096, 128256, 8192),
+    "attn_prefix_tc": lambda: case_attention("prefix", "tc"),
+    "attn_prefix_mma": lambda: case_attention("prefix", "mma"),
+    "attn_suffix_tc": lambda: case_attention("suffix", "tc"),
+    "attn_suffix_mma": lambda: case_attention("suffix", "mma"),
+}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", nargs="*", default=list(CASES))
+    ap.add_argument("--iters", type=int, default=10)
+    args = ap.parse_args()
+    pk = peaks()
+    for name in args.kernel:
+        fn, flops, kind = CASES[name]()
+        ms = time_it(fn, args.iters)
+        ops.check_status()
+        tf = flops / ms / 1e9
+        denom = pk["bf16_tflops"] * (2 if kind == "fp8" else 1)
+        print(json.dumps({"kernel": name, "ms": round(ms, 4), "tflops": round(tf, 1),
+                          "frac_of_" + pk["src"]: round(tf / denom, 3),
+                          "denominator_tflops": denom, "kind": kind}))
+        torch.cuda.empty_cache()
+
+
+if __name__ == "__main__":
+    main()
