@@ -40,8 +40,8 @@ struct GemmSmem {
   uint8_t b[STAGES][BN * 128];
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
+  uint64_t tfull[512 / BN];
+  uint64_t tempty[512 / BN];
   uint64_t done;
   uint32_t tmem_base;
   int abort;
@@ -60,7 +60,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr int STAGES = gemm_stages<BN>();
   constexpr int BKE = FP8 ? 128 : 64;  // K elements per 128-byte stage row
   constexpr uint32_t IDESC = idesc_make(kBM, BN, FP8 ? 0 : 1);
-  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr int NBUF = 512 / BN;        // TMEM accumulators (all 512 columns)
+  constexpr uint32_t TMEM_COLS = 512;
   constexpr int CPT = BN / 2;  // columns per epilogue thread
   using Smem = GemmSmem<BN, STAGES>;
 
@@ -80,7 +81,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NBUF; ++i) {
       mbar_init(&s.tfull[i], 1);
       mbar_init(&s.tempty[i], kEpiWarps);
     }
@@ -158,7 +159,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           if (++stage == STAGES) stage = 0, phase ^= 1;
           if (end_acc)
-            if (++tb == 2) tb = 0, tphase ^= 1;
+            if (++tb == NBUF) tb = 0, tphase ^= 1;
         }
       }
     mma_done:
@@ -174,39 +175,57 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int half = ew >> 2;     // column half of the tile
     int tb = 0;
     uint32_t tphase = 0;
-    float acc[CPT];
+    float2 acc[CPT / 2];          // packed pairs: the promotion uses the f32x2 FMA (half the issue slots)
     const int epi_blocks = FP8 ? kblocks : 1;
-    for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x) {
+    // the scales of the next (tile, k block) are loaded one step ahead, so their latency overlaps the
+    // current block's TMEM drain
+    int t = blockIdx.x;
+    float sa_next = 0.f, sb_next = 0.f;
+    auto load_scales = [&](int tt, int kb) {
+      if (!FP8 || tt >= num_tiles) return;
+      const int mb = tt % m_tiles, nb = tt / m_tiles;
+      const int rr = mb * kBM + sub * 32 + lane;
+      const int c0 = nb * BN + half * CPT;
+      sa_next = sa[(size_t)kb * M + (rr < M ? rr : M - 1)];
+      sb_next = c0 < N ? sb[(size_t)(c0 >> 7) * kblocks + kb] : 0.f;
+    };
+    load_scales(t, 0);
+    for (; t < num_tiles && !*abort; t += gridDim.x) {
       const int m_blk = t % m_tiles, n_blk = t / m_tiles;
       const int row = m_blk * kBM + sub * 32 + lane;
       const int col0 = n_blk * BN + half * CPT;
       const bool col_ok = col0 < N;
-      const int srow = row < M ? row : M - 1;
       for (int kb = 0; kb < epi_blocks; ++kb) {
+        const float scale = FP8 ? sa_next * sb_next : 1.f;
+        if (kb + 1 < epi_blocks) load_scales(t, kb + 1);
+        else load_scales(t + gridDim.x, 0);
         const bool ok = mbar_wait(&s.tfull[tb], tphase, status, kErrTimeoutEpilogue, abort);
         if (!__all_sync(0xffffffffu, ok)) goto epi_done;
         tc_fence_after();
-        float scale = 1.0f;
-        if (FP8) scale = sa[(size_t)kb * M + srow] * (col_ok ? sb[(size_t)(col0 >> 7) * kblocks + kb] : 0.0f);
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + tb * BN + half * CPT;
+        constexpr int BATCH = CPT >= 128 ? 16 : CPT;   // columns per tcgen05.wait::ld (register budget)
+        const float2 s2 = make_float2(scale, scale);
 #pragma unroll
-        for (int c = 0; c < CPT / 16; ++c) {
-          uint32_t r[16];
-          tmem_ld16(taddr + c * 16, r);
+        for (int c0 = 0; c0 < CPT; c0 += BATCH) {
+          uint32_t r[BATCH];
+#pragma unroll
+          for (int q = 0; q < BATCH / 16; ++q)
+            tmem_ld16(taddr + c0 + q * 16, *reinterpret_cast<uint32_t(*)[16]>(r + q * 16));
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float v = __uint_as_float(r[j]);
+          for (int j = 0; j < BATCH / 2; ++j) {
+            const float2 v = make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+            float2& a = acc[(c0 >> 1) + j];
             if (FP8)
-              acc[c * 16 + j] = kb == 0 ? v * scale : fmaf(v, scale, acc[c * 16 + j]);
+              a = kb == 0 ? __fmul2_rn(v, s2) : __ffma2_rn(v, s2, a);
             else
-              acc[c * 16 + j] = v;
+              a = v;
           }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.tempty[tb]);
-        if (++tb == 2) tb = 0, tphase ^= 1;
+        if (++tb == NBUF) tb = 0, tphase ^= 1;
       }
       if (row < M && col_ok) {
         __nv_bfloat16* dst = out + (size_t)row * ldc + col0;
@@ -215,10 +234,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int c = 0; c < CPT / 8; ++c) {
           if (!full_cols && col0 + 8 * c >= N) break;
           uint4 v;
-          v.x = pack_bf16x2(acc[8 * c + 0], acc[8 * c + 1]);
-          v.y = pack_bf16x2(acc[8 * c + 2], acc[8 * c + 3]);
-          v.z = pack_bf16x2(acc[8 * c + 4], acc[8 * c + 5]);
-          v.w = pack_bf16x2(acc[8 * c + 6], acc[8 * c + 7]);
+          v.x = pack_bf16x2(acc[4 * c + 0].x, acc[4 * c + 0].y);
+          v.y = pack_bf16x2(acc[4 * c + 1].x, acc[4 * c + 1].y);
+          v.z = pack_bf16x2(acc[4 * c + 2].x, acc[4 * c + 2].y);
+          v.w = pack_bf16x2(acc[4 * c + 3].x, acc[4 * c + 3].y);
           *reinterpret_cast<uint4*>(dst + 8 * c) = v;
         }
       }

@@ -131,6 +131,7 @@ CASES = {
     "gemm_fp8_qkv": lambda: case_gemm_fp8(4096, 10240, 8192),
     "gemm_fp8_o": lambda: case_gemm_fp8(4096, 8192, 8192),
     "gemm_fp8_gate_up": lambda: case_gemm_fp8(4096, 57344, 8192),
+    "gemm_fp8_gate_up_bn128": lambda: case_gemm_fp8(4096, 57344, 8192, bn=128),
     "gemm_fp8_down": lambda: case_gemm_fp8(4096, 8192, 28672),
     "gemm_fp8_gate_up_tp8": lambda: case_gemm_fp8(4096, 7168, 8192),
     "gemm_fp8_draft_m512": lambda: case_gemm_fp8(512, 57344, 8192),

@@ -218,7 +218,7 @@ def rope_kv_write(qkv: torch.Tensor, pos: torch.Tensor, slots: Optional[torch.Te
 # attention
 # ------------------------------------------------------------------------------------------------
 
-ATTN_IMPL = {"impl": "tc"}   # "tc" = tcgen05 kernel (128-row tiles), "mma" = mma.sync kernel (64-row tiles)
+ATTN_IMPL = {"impl": "mma"}  # "tc" = tcgen05 kernel (128-row tiles), "mma" = mma.sync kernel (64-row tiles)
 
 
 def attn_rows(impl: Optional[str] = None) -> int:
