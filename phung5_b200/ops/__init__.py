@@ -218,12 +218,12 @@ def rope_kv_write(qkv: torch.Tensor, pos: torch.Tensor, slots: Optional[torch.Te
 # attention
 # ------------------------------------------------------------------------------------------------
 
-ATTN_IMPL = {"impl": "mma"}  # "tc" = tcgen05 kernel (128-row tiles), "mma" = mma.sync kernel (64-row tiles)
+ATTN_IMPL = {"impl": "tc"}   # "tc" = tcgen05 kernel (256-row tiles), "mma" = mma.sync kernel (64-row tiles)
 
 
 def attn_rows(impl: Optional[str] = None) -> int:
     """Query rows per work tile for the selected attention kernel."""
-    return 128 if (impl or ATTN_IMPL["impl"]) == "tc" else 64
+    return 256 if (impl or ATTN_IMPL["impl"]) == "tc" else 64
 
 
 def paged_attention(q, k_cache, v_cache, meta, softmax_scale: float, o_in=None, lse_in=None, o_part=None,
