@@ -31,6 +31,8 @@ void paged_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_
                         c10::optional<torch::Tensor> o_part, c10::optional<torch::Tensor> lse_part,
                         c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> out_q,
                         c10::optional<torch::Tensor> out_qs, torch::Tensor status);
+void topk_logprobs(torch::Tensor logits, int64_t k, double temperature, torch::Tensor lp, torch::Tensor idx,
+                   c10::optional<torch::Tensor> lse, int64_t vocab_offset);
 }  // namespace phx
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -43,4 +45,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_kv_write", &phx::rope_kv_write);
   m.def("paged_attention", &phx::paged_attention);
   m.def("paged_attention_tc", &phx::paged_attention_tc);
+  m.def("topk_logprobs", &phx::topk_logprobs);
 }

@@ -73,18 +73,18 @@ class _VocabOps:
         self.v0 = vocab_start
 
     def topk_logprobs(self, logits: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
-        lf = logits.float()
-        lse = torch.logsumexp(lf, -1, keepdim=True)
-        v, i = torch.topk(lf, k, dim=-1)
+        """Top-k of log-softmax over the full vocab: the fused kernel on this rank's shard, then (TP) a
+        merge of every shard's k candidates and log-sum-exp."""
+        lp, i, lse = ops.topk_logprobs(logits, k, vocab_offset=self.v0)
         if self.comm.size == 1:
-            return v - lse, i
-        return self.comm.topk_logprobs_merge(v, i + self.v0, lse, k)
+            return lp, i
+        return self.comm.topk_logprobs_merge(lp + lse[:, None], i, lse[:, None], k)
 
     def argmax(self, logits: torch.Tensor) -> torch.Tensor:
+        lp, i, lse = ops.topk_logprobs(logits, 1, vocab_offset=self.v0)
         if self.comm.size == 1:
-            return logits.argmax(-1)
-        v, i = torch.max(logits.float(), -1)
-        return self.comm.argmax_merge(v, i + self.v0)
+            return i[:, 0]
+        return self.comm.argmax_merge(lp[:, 0] + lse, i[:, 0])
 
     def full(self, logits: torch.Tensor) -> torch.Tensor:
         return logits if self.comm.size == 1 else self.comm.all_gather_vocab(logits)
@@ -165,6 +165,76 @@ class LLMEngine:
         self.reqs[rid] = r
         self.waiting.append(r)
         return rid
+
+    # ------------------------------------------------------------------------------------------
+    # sleep / wake: weights to pinned host memory and back, KV pool released and rebuilt (the
+    # reference's burst swap relies on SGLang release/resume_memory_occupation and vLLM /sleep, /wake_up,
+    # docker/opt/sgl/lb_proxy.py:13-25)
+    # ------------------------------------------------------------------------------------------
+    @property
+    def sleeping(self) -> bool:
+        return getattr(self, "_host_copies", None) is not None
+
+    def _weight_tensors(self):
+        seen, out = set(), []
+
+        def walk(o):
+            if isinstance(o, torch.Tensor):
+                if id(o) not in seen:
+                    seen.add(id(o))
+                    out.append(o)
+            elif isinstance(o, (list, tuple)):
+                for x in o:
+                    walk(x)
+            elif hasattr(o, "__dataclass_fields__"):
+                for f in o.__dataclass_fields__:
+                    walk(getattr(o, f))
+        walk(self.tw)
+        if self.drafter is not None:
+            walk(self.drafter.ew if self.eagle else self.drafter.w)
+        return out
+
+    def sleep(self) -> None:
+        """Offload every weight to pinned host memory and drop the KV pool (requests must be finished)."""
+        if self.sleeping:
+            return
+        if self.has_work():
+            raise RuntimeError("sleep() with requests in flight")
+        copies = []
+        for t in self._weight_tensors():
+            h = torch.empty(t.shape, dtype=t.dtype, device="cpu", pin_memory=self.device.type == "cuda")
+            h.copy_(t, non_blocking=True)
+            copies.append((t, h))
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        for t, h in copies:
+            t.data = torch.empty(0, dtype=t.dtype, device=t.device)
+        self._host_copies = copies
+        self._pool_shape = (self.pool.k.shape, self.pool.dk.shape if self.pool.dk is not None else None,
+                            None if self.pool.hidden is None else self.pool.hidden.shape)
+        for name in ("k", "v", "dk", "dv", "hidden"):
+            t = getattr(self.pool, name)
+            if t is not None:
+                t.data = torch.empty(0, dtype=t.dtype, device=t.device)
+        self.pool.prefix = type(self.pool.prefix)(self.pool.alloc, self.ps)   # cached pages are gone
+        self.pool.alloc = type(self.pool.alloc)(self.pool.num_pages, reserved=1)
+        self.pool.prefix.alloc = self.pool.alloc
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
+
+    def wake_up(self) -> None:
+        if not self.sleeping:
+            return
+        for t, h in self._host_copies:
+            t.data = h.to(self.device, non_blocking=True)
+        kshape, dshape, hshape = self._pool_shape
+        for name, shape in (("k", kshape), ("v", kshape), ("dk", dshape), ("dv", dshape), ("hidden", hshape)):
+            t = getattr(self.pool, name)
+            if t is not None and shape is not None:
+                t.data = torch.zeros(shape, dtype=t.dtype, device=self.device)
+        self._host_copies = None
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
 
     def has_work(self) -> bool:
         return bool(self.waiting) or any(not r.finished for r in self.running)

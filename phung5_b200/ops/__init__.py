@@ -103,6 +103,28 @@ def gemm_bf16(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = No
 
 
 # ------------------------------------------------------------------------------------------------
+# sampling
+# ------------------------------------------------------------------------------------------------
+
+def topk_logprobs(logits: torch.Tensor, k: int, temperature: float = 1.0, vocab_offset: int = 0):
+    """Fused top-k of log-softmax(logits / T) per row: returns (logprobs [R, k] fp32, indices [R, k] int64
+    (+ vocab_offset), logsumexp [R] fp32). On a vocab shard the results are shard-local (the lse of the
+    shard), which a tensor-parallel merge combines."""
+    r = logits.shape[0]
+    if logits.is_cuda:
+        lp = torch.empty(r, k, dtype=torch.float32, device=logits.device)
+        idx = torch.empty(r, k, dtype=torch.int64, device=logits.device)
+        lse = torch.empty(r, dtype=torch.float32, device=logits.device)
+        ext().topk_logprobs(logits.contiguous() if logits.stride(-1) != 1 else logits, k, temperature, lp, idx, lse,
+                            vocab_offset)
+        return lp, idx, lse
+    x = logits.float() / temperature
+    lse = torch.logsumexp(x, -1)
+    v, i = torch.topk(x, k, dim=-1)
+    return v - lse[:, None], i + vocab_offset, lse
+
+
+# ------------------------------------------------------------------------------------------------
 # norms / activations / quant
 # ------------------------------------------------------------------------------------------------
 

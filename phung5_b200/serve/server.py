@@ -1,0 +1,261 @@
+"""OpenAI-compatible HTTP server over `LLMEngine`.
+
+The engine runs on one background thread (every `step()` is one scheduling step: prefill and/or one
+speculative step for all running requests); HTTP handlers submit requests through a queue and await
+per-request streams. Endpoints mirror what the reference's clients use of SGLang/vLLM
+(pipeline_service/llm/session.py:150-270, docker/opt/sgl/lb_proxy.py:13-25):
+
+  GET  /health                      200 while serving, 503 while asleep or after an engine error
+  GET  /v1/models
+  POST /v1/completions              prompt: str | [int]; max_tokens, temperature, top_p, top_k, seed, stream
+  POST /v1/chat/completions         messages (chat template of the tokenizer); same sampling fields
+  GET  /get_load                    {"num_running", "num_waiting"}
+  GET  /metrics                     Prometheus text (tokens, accept length, step latency, TPOT)
+  POST /sleep, /wake_up             weights to host memory and back (vLLM names)
+  POST /release_memory_occupation, /resume_memory_occupation   (SGLang names, same actions)
+
+    python -m phung5_b200.serve.server --model llama3-8b --port 8001 [--spec tree] [--device cuda]
+"""
+from __future__ import annotations
+
+import argparse
+import asyncio
+import json
+import queue
+import threading
+import time
+import traceback
+import uuid
+from dataclasses import dataclass, field
+from typing import AsyncIterator, Dict, List, Optional
+
+from fastapi import FastAPI, Request
+from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+
+from ..engine.oracle import SamplingParams
+from .metrics import EngineMetrics
+
+
+@dataclass
+class _Pending:
+    prompt: List[int]
+    params: SamplingParams
+    out: "asyncio.Queue"
+    loop: asyncio.AbstractEventLoop
+    rid: int = -1
+
+
+class AsyncEngine:
+    """Drives an LLMEngine from a background thread; thread-safe submission, asyncio streams out."""
+
+    def __init__(self, engine, metrics: Optional[EngineMetrics] = None):
+        self.engine = engine
+        self.metrics = metrics or EngineMetrics()
+        self._submit: "queue.Queue[_Pending]" = queue.Queue()
+        self._control: "queue.Queue" = queue.Queue()
+        self._streams: Dict[int, _Pending] = {}
+        self._wake = threading.Event()
+        self._stop = False
+        self.error: Optional[str] = None
+        self._thread = threading.Thread(target=self._run, name="phx-engine", daemon=True)
+        self._thread.start()
+
+    # -- engine thread --------------------------------------------------------------------------
+    def _run(self):
+        eng = self.engine
+        while not self._stop:
+            try:
+                while True:
+                    try:
+                        op, fut, loop = self._control.get_nowait()
+                    except queue.Empty:
+                        break
+                    try:
+                        getattr(eng, op)()
+                        loop.call_soon_threadsafe(fut.set_result, True)
+                    except Exception as e:  # pragma: no cover - surfaced to the caller
+                        loop.call_soon_threadsafe(fut.set_exception, e)
+                while True:
+                    try:
+                        p = self._submit.get_nowait()
+                    except queue.Empty:
+                        break
+                    p.rid = eng.add_request(p.prompt, p.params)
+                    self._streams[p.rid] = p
+                if not eng.has_work():
+                    self._wake.wait(0.05)
+                    self._wake.clear()
+                    continue
+                t0 = time.perf_counter()
+                outs = eng.step()
+                dt = time.perf_counter() - t0
+                self.metrics.observe_step(dt, outs, eng)
+                for o in outs:
+                    p = self._streams.get(o.rid)
+                    if p is None:
+                        continue
+                    p.loop.call_soon_threadsafe(p.out.put_nowait, o)
+                    if o.finished:
+                        del self._streams[o.rid]
+            except Exception:  # keep serving health; report the error
+                self.error = traceback.format_exc()
+                for p in list(self._streams.values()):
+                    p.loop.call_soon_threadsafe(p.out.put_nowait, None)
+                self._streams.clear()
+                time.sleep(0.1)
+
+    # -- asyncio side ---------------------------------------------------------------------------
+    async def generate(self, prompt: List[int], params: SamplingParams) -> AsyncIterator:
+        loop = asyncio.get_running_loop()
+        q: asyncio.Queue = asyncio.Queue()
+        self._submit.put(_Pending(prompt, params, q, loop))
+        self._wake.set()
+        while True:
+            o = await q.get()
+            if o is None:
+                raise RuntimeError(self.error or "engine error")
+            yield o
+            if o.finished:
+                return
+
+    async def control(self, op: str):
+        loop = asyncio.get_running_loop()
+        fut = loop.create_future()
+        self._control.put((op, fut, loop))
+        self._wake.set()
+        return await fut
+
+    def load(self) -> Dict[str, int]:
+        return {"num_running": len(self.engine.running), "num_waiting": len(self.engine.waiting) + self._submit.qsize()}
+
+    def shutdown(self):
+        self._stop = True
+        self._wake.set()
+        self._thread.join(timeout=5)
+
+
+def _sampling(body: dict, default_max: int = 256) -> SamplingParams:
+    return SamplingParams(temperature=float(body.get("temperature", 0.0) or 0.0),
+                          top_k=int(body.get("top_k", 0) or 0), top_p=float(body.get("top_p", 1.0) or 1.0),
+                          seed=int(body.get("seed", 42) if body.get("seed") is not None else 42),
+                          max_new_tokens=int(body.get("max_tokens", body.get("max_completion_tokens", default_max))
+                                             or default_max))
+
+
+def build_app(aeng: AsyncEngine, tokenizer, model_name: str = "phung5_b200"):
+    app = FastAPI(title="phung5_b200")
+
+    @app.get("/health")
+    async def health():
+        if aeng.error or aeng.engine.sleeping:
+            return JSONResponse({"status": "unavailable", "error": aeng.error, "sleeping": aeng.engine.sleeping},
+                                status_code=503)
+        return {"status": "ok"}
+
+    @app.get("/v1/models")
+    async def models():
+        return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "phung5_b200"}]}
+
+    @app.get("/get_load")
+    async def get_load():
+        return aeng.load()
+
+    @app.get("/metrics")
+    async def metrics():
+        return PlainTextResponse(aeng.metrics.render(), media_type="text/plain; version=0.0.4")
+
+    async def _control(op):
+        await aeng.control(op)
+        return {"ok": True, "sleeping": aeng.engine.sleeping}
+
+    @app.post("/sleep")
+    async def sleep():
+        return await _control("sleep")
+
+    @app.post("/wake_up")
+    async def wake_up():
+        return await _control("wake_up")
+
+    @app.post("/release_memory_occupation")
+    async def release():
+        return await _control("sleep")
+
+    @app.post("/resume_memory_occupation")
+    async def resume():
+        return await _control("wake_up")
+
+    async def _complete(ids: List[int], body: dict, chat: bool):
+        sp = _sampling(body)
+        rid = f"{'chatcmpl' if chat else 'cmpl'}-{uuid.uuid4().hex[:16]}"
+        created = int(time.time())
+        if body.get("stream"):
+            async def events():
+                n = 0
+                async for o in aeng.generate(ids, sp):
+                    n += len(o.new_tokens)
+                    text = tokenizer.decode(o.new_tokens)
+                    if chat:
+                        chunk = {"id": rid, "object": "chat.completion.chunk", "created": created, "model": model_name,
+                                 "choices": [{"index": 0, "delta": {"content": text},
+                                              "finish_reason": "length" if o.finished else None}]}
+                    else:
+                        chunk = {"id": rid, "object": "text_completion", "created": created, "model": model_name,
+                                 "choices": [{"index": 0, "text": text, "token_ids": o.new_tokens,
+                                              "finish_reason": "length" if o.finished else None}]}
+                    yield f"data: {json.dumps(chunk)}\n\n"
+                yield "data: [DONE]\n\n"
+            return StreamingResponse(events(), media_type="text/event-stream")
+        toks: List[int] = []
+        async for o in aeng.generate(ids, sp):
+            toks += o.new_tokens
+        text = tokenizer.decode(toks)
+        usage = {"prompt_tokens": len(ids), "completion_tokens": len(toks), "total_tokens": len(ids) + len(toks)}
+        if chat:
+            return {"id": rid, "object": "chat.completion", "created": created, "model": model_name,
+                    "choices": [{"index": 0, "message": {"role": "assistant", "content": text},
+                                 "finish_reason": "length"}], "usage": usage}
+        return {"id": rid, "object": "text_completion", "created": created, "model": model_name,
+                "choices": [{"index": 0, "text": text, "token_ids": toks, "finish_reason": "length"}], "usage": usage}
+
+    @app.post("/v1/completions")
+    async def completions(req: Request):
+        body = await req.json()
+        prompt = body.get("prompt", "")
+        ids = list(prompt) if isinstance(prompt, list) else tokenizer.encode(prompt)
+        if not ids:
+            return JSONResponse({"error": "empty prompt"}, status_code=400)
+        return await _complete(ids, body, chat=False)
+
+    @app.post("/v1/chat/completions")
+    async def chat(req: Request):
+        body = await req.json()
+        ids = tokenizer.encode(tokenizer.apply_chat_template(body.get("messages", [])))
+        return await _complete(ids, body, chat=True)
+
+    return app
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="small-bf16")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8001)
+    ap.add_argument("--device", default="cuda")
+    ap.add_argument("--spec", default="tree", choices=["off", "chain", "tree"])
+    ap.add_argument("--tokenizer", default=None)
+    ap.add_argument("--num-pages", type=int, default=0)
+    args = ap.parse_args(argv)
+    import uvicorn
+    from ..config import CacheConfig, DraftConfig, EngineConfig, SpecConfig, preset
+    from ..engine.engine import LLMEngine
+    spec = SpecConfig(enabled=args.spec != "off", mode=args.spec if args.spec != "off" else "chain")
+    cfg = EngineConfig(model=preset(args.model), spec=spec, draft=DraftConfig(kind="eagle"),
+                       cache=CacheConfig(num_pages=args.num_pages))
+    eng = LLMEngine(cfg, device=args.device)
+    aeng = AsyncEngine(eng)
+    uvicorn.run(build_app(aeng, __import__("phung5_b200.serve.tokenizer", fromlist=["load_tokenizer"]).load_tokenizer(
+        args.tokenizer), args.model), host=args.host, port=args.port, log_level="warning")
+
+
+if __name__ == "__main__":
+    main()

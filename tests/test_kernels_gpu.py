@@ -218,3 +218,21 @@ def test_paged_attention(case, impl):
     assert _rel(out.cpu(), out_ref) < 1e-2
     deq = (oq.cpu().float().view(t, hq, 128) * osc.cpu().t()[..., None]).view(t, hq * 128)
     assert _rel(deq, out_ref) < 4e-2
+
+
+@pytest.mark.parametrize("r,v,k,t", [(512, 128256, 8, 1.0), (4096, 16032, 1, 1.0), (7, 32000, 16, 0.7),
+                                     (3, 1000, 4, 1.0), (64, 4001, 8, 1.3)])
+def test_topk_logprobs(r, v, k, t):
+    g = torch.Generator(device=DEV).manual_seed(r + v)
+    x = (torch.randn(r, v, device=DEV, generator=g) * 2).bfloat16()
+    if v == 4001:
+        x = x[:, :4000]          # non-16-byte-aligned row stride
+    lp, idx, lse = ops.topk_logprobs(x, k, temperature=t)
+    xf = x.float() / t
+    ref_lse = torch.logsumexp(xf, -1)
+    rv, ri = torch.topk(xf, k, dim=-1)
+    assert torch.allclose(lse, ref_lse, atol=1e-3, rtol=1e-5)
+    assert torch.allclose(lp, rv - ref_lse[:, None], atol=1e-3)
+    # indices agree up to exact ties in bf16
+    got = xf.gather(1, idx)
+    assert torch.equal(got, rv)
