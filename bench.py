@@ -107,6 +107,8 @@ def main():
     ap.add_argument("--tree-nodes", type=int, default=64)
     ap.add_argument("--topk", type=int, default=8)
     ap.add_argument("--depth", type=int, default=6)
+    ap.add_argument("--mode", default="tree", choices=["tree", "chain"])
+    ap.add_argument("--num-draft", type=int, default=4)
     ap.add_argument("--comm", default="nccl", choices=["nccl", "fused"])
     ap.add_argument("--no-cascade", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override layer count (smoke runs only; not a bench value)")
@@ -134,8 +136,8 @@ def main():
     mc = preset(args.model)
     if args.layers:
         mc.num_layers = args.layers
-    spec = SpecConfig(mode="tree", tree_nodes=args.tree_nodes, topk=args.topk, depth=args.depth,
-                      accept="geometric", accept_p=0.3, accept_cap=6, accept_seed=0)
+    spec = SpecConfig(mode=args.mode, tree_nodes=args.tree_nodes, topk=args.topk, depth=args.depth,
+                      num_draft=args.num_draft, accept="geometric", accept_p=0.3, accept_cap=6, accept_seed=0)
     # the shared prefix pages are held once (prefix cache); each request adds its suffix, outputs and
     # speculation scratch
     per_req_pages = (args.suffix + args.out_tokens + 2 * args.tree_nodes + 128) // 64 + 3
@@ -221,8 +223,9 @@ def main():
             "data": "synthetic token ids, random-init weights, geometric(p=0.3, cap 6) synthetic acceptance",
             "config": {"model": mc.name + (f"-{mc.num_layers}L" if args.layers else ""), "global_batch": args.batch,
                        "seq_len": args.prefix + args.suffix, "shared_prefix": args.prefix, "suffix": args.suffix,
-                       "out_tokens": args.out_tokens, "tree_nodes": args.tree_nodes, "topk": args.topk,
-                       "depth": args.depth, "parallelism": f"tp{world}", "comm": args.comm if world > 1 else "none",
+                       "out_tokens": args.out_tokens, "spec": args.mode,
+                       "tree_nodes": args.tree_nodes if args.mode == "tree" else args.num_draft + 1,
+                       "topk": args.topk, "depth": args.depth if args.mode == "tree" else args.num_draft, "parallelism": f"tp{world}", "comm": args.comm if world > 1 else "none",
                        "cascade": not args.no_cascade, "l2": "inputs larger than L2 (weights stream every step)"},
             "p50_tpot_ms": round(statistics.median(tpot), 3) if tpot else None,
             "tokens_per_step": round(tokens / args.steps, 2),

@@ -33,12 +33,18 @@ void paged_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_
                         c10::optional<torch::Tensor> out_qs, torch::Tensor status);
 void topk_logprobs(torch::Tensor logits, int64_t k, double temperature, torch::Tensor lp, torch::Tensor idx,
                    c10::optional<torch::Tensor> lse, int64_t vocab_offset);
+void gemm_fp8_grouped(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor offsets,
+                      torch::Tensor out, torch::Tensor status);
+void gemm_bf16_grouped(torch::Tensor x, torch::Tensor w, torch::Tensor offsets, torch::Tensor out,
+                       torch::Tensor status);
 }  // namespace phx
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "phung5_b200 sm_100a kernels";
   m.def("gemm_fp8_block", &phx::gemm_fp8_block);
   m.def("gemm_bf16", &phx::gemm_bf16);
+  m.def("gemm_fp8_grouped", &phx::gemm_fp8_grouped);
+  m.def("gemm_bf16_grouped", &phx::gemm_bf16_grouped);
   m.def("add_rmsnorm_quant", &phx::add_rmsnorm_quant);
   m.def("silu_mul_quant", &phx::silu_mul_quant);
   m.def("act_quant", &phx::act_quant);

@@ -52,11 +52,56 @@ constexpr int gemm_stages() {
   return BN == 256 ? 4 : 6;
 }
 
+// Output tile t -> rows [m0, m_end) of A / out, rows [b0, b0 + BN) of B, output columns [n0, n0 + BN),
+// weight-scale row base. Plain GEMM: tiles walk M fastest. Grouped GEMM (grp_off != null, MoE experts):
+// A rows are sorted by group, group e owns rows [grp_off[e], grp_off[e+1]) and B rows [e*N, (e+1)*N);
+// tiles are enumerated group by group (M fastest inside a group) from the device-side offsets, so the
+// tile list needs no host round trip; tiles past the last group are invalid.
+struct TileInfo {
+  int m0, m_end, b0, n0, sb_base;
+  bool valid;
+};
+
+template <int BN>
+__device__ __forceinline__ TileInfo tile_info(int t, int M, int N, int m_tiles, int n_tiles, const int* grp_off,
+                                              int groups) {
+  TileInfo ti;
+  if (!grp_off) {
+    const int m_blk = t % m_tiles, n_blk = t / m_tiles;
+    ti.m0 = m_blk * kBM;
+    ti.m_end = M;
+    ti.n0 = n_blk * BN;
+    ti.b0 = ti.n0;
+    ti.sb_base = 0;
+    ti.valid = t < m_tiles * n_tiles;
+    return ti;
+  }
+  ti.valid = false;
+  for (int e = 0; e < groups; ++e) {
+    const int lo = grp_off[e], hi = grp_off[e + 1];
+    const int mt = (hi - lo + kBM - 1) / kBM;
+    const int tiles = mt * n_tiles;
+    if (t < tiles) {
+      const int n_blk = t / mt, m_blk = t % mt;
+      ti.m0 = lo + m_blk * kBM;
+      ti.m_end = hi;
+      ti.n0 = n_blk * BN;
+      ti.b0 = e * N + ti.n0;
+      ti.sb_base = e * ((N + 127) / 128);
+      ti.valid = true;
+      return ti;
+    }
+    t -= tiles;
+  }
+  return ti;
+}
+
 template <int BN, bool FP8>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       __nv_bfloat16* __restrict__ out, int M, int N, int K, int ldc, const float* __restrict__ sa,
-                      const float* __restrict__ sb, int* status) {
+                      const float* __restrict__ sb, int* status, const int* __restrict__ grp_off, int groups,
+                      int max_tiles) {
   constexpr int STAGES = gemm_stages<BN>();
   constexpr int BKE = FP8 ? 128 : 64;  // K elements per 128-byte stage row
   constexpr uint32_t IDESC = idesc_make(kBM, BN, FP8 ? 0 : 1);
@@ -72,7 +117,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int lane = lane_id();
   const int m_tiles = (M + kBM - 1) / kBM;
   const int n_tiles = (N + BN - 1) / BN;
-  const int num_tiles = m_tiles * n_tiles;
+  const int num_tiles = grp_off ? max_tiles : m_tiles * n_tiles;
   const int ksteps = K / BKE;          // smem stages per tile
   const int kblocks = K / 128;         // scale blocks (fp8)
 
@@ -108,12 +153,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x) {
-        const int m_blk = t % m_tiles, n_blk = t / m_tiles;
+        const TileInfo ti = tile_info<BN>(t, M, N, m_tiles, n_tiles, grp_off, groups);
+        if (!ti.valid) break;
         for (int ks = 0; ks < ksteps; ++ks) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1, status, kErrTimeoutProducer, abort)) break;
           mbar_arrive_expect_tx(&s.full[stage], (kBM + BN) * 128);
-          tma_load_2d(&tmA, &s.full[stage], s.a[stage], ks * BKE, m_blk * kBM);
-          tma_load_2d(&tmB, &s.full[stage], s.b[stage], ks * BKE, n_blk * BN);
+          tma_load_2d(&tmA, &s.full[stage], s.a[stage], ks * BKE, ti.m0);
+          tma_load_2d(&tmB, &s.full[stage], s.b[stage], ks * BKE, ti.b0);
           ++issued;
           if (++stage == STAGES) stage = 0, phase ^= 1;
         }
@@ -133,6 +179,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int tb = 0;
       uint32_t tphase = 0;
       for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x) {
+        if (grp_off && !tile_info<BN>(t, M, N, m_tiles, n_tiles, grp_off, groups).valid) break;
         for (int ks = 0; ks < ksteps; ++ks) {
           const bool new_acc = FP8 || ks == 0;
           const bool end_acc = FP8 || ks == ksteps - 1;
@@ -183,17 +230,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     float sa_next = 0.f, sb_next = 0.f;
     auto load_scales = [&](int tt, int kb) {
       if (!FP8 || tt >= num_tiles) return;
-      const int mb = tt % m_tiles, nb = tt / m_tiles;
-      const int rr = mb * kBM + sub * 32 + lane;
-      const int c0 = nb * BN + half * CPT;
+      const TileInfo ti = tile_info<BN>(tt, M, N, m_tiles, n_tiles, grp_off, groups);
+      if (!ti.valid) return;
+      const int rr = ti.m0 + sub * 32 + lane;
+      const int c0 = ti.n0 + half * CPT;
       sa_next = sa[(size_t)kb * M + (rr < M ? rr : M - 1)];
-      sb_next = c0 < N ? sb[(size_t)(c0 >> 7) * kblocks + kb] : 0.f;
+      sb_next = c0 < N ? sb[(size_t)(ti.sb_base + (c0 >> 7)) * kblocks + kb] : 0.f;
     };
     load_scales(t, 0);
     for (; t < num_tiles && !*abort; t += gridDim.x) {
-      const int m_blk = t % m_tiles, n_blk = t / m_tiles;
-      const int row = m_blk * kBM + sub * 32 + lane;
-      const int col0 = n_blk * BN + half * CPT;
+      const TileInfo ti = tile_info<BN>(t, M, N, m_tiles, n_tiles, grp_off, groups);
+      if (!ti.valid) break;
+      const int row = ti.m0 + sub * 32 + lane;
+      const int col0 = ti.n0 + half * CPT;
       const bool col_ok = col0 < N;
       for (int kb = 0; kb < epi_blocks; ++kb) {
         const float scale = FP8 ? sa_next * sb_next : 1.f;
@@ -227,7 +276,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) mbar_arrive(&s.tempty[tb]);
         if (++tb == NBUF) tb = 0, tphase ^= 1;
       }
-      if (row < M && col_ok) {
+      if (row < ti.m_end && row < M && col_ok) {
         __nv_bfloat16* dst = out + (size_t)row * ldc + col0;
         const bool full_cols = col0 + CPT <= N;
 #pragma unroll
@@ -266,14 +315,16 @@ int num_sms() {
 
 template <int BN, bool FP8>
 void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, const float* sa,
-                 const float* sb, int* status, cudaStream_t stream, int max_ctas) {
-  const int M = a.size(0), K = a.size(1), N = b.size(0);
+                 const float* sb, int* status, cudaStream_t stream, int max_ctas, const int* grp_off = nullptr,
+                 int groups = 0) {
+  const int M = a.size(0), K = a.size(1);
+  const int N = grp_off ? (int)out.size(1) : (int)b.size(0);   // grouped: b holds groups * N rows
   const CUtensorMapDataType dt = FP8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int esz = FP8 ? 1 : 2;
   const uint32_t box_inner = 128 / esz;
   CUtensorMap ta = make_tmap_2d(a.data_ptr(), dt, K, M, (uint64_t)a.stride(0) * esz, box_inner, kBM,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tb = make_tmap_2d(b.data_ptr(), dt, K, N, (uint64_t)b.stride(0) * esz, box_inner, BN,
+  CUtensorMap tb = make_tmap_2d(b.data_ptr(), dt, K, b.size(0), (uint64_t)b.stride(0) * esz, box_inner, BN,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   constexpr int STAGES = gemm_stages<BN>();
   const size_t smem = sizeof(GemmSmem<BN, STAGES>) + 1024;
@@ -282,10 +333,13 @@ void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& 
     cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr_set = true;
   }
-  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  // grouped: at most M/128 + groups row tiles in total (one partial tile per group)
+  const int m_tiles_bound = grp_off ? (M + kBM - 1) / kBM + groups : (M + kBM - 1) / kBM;
+  const int tiles = m_tiles_bound * ((N + BN - 1) / BN);
   int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
-  gemm_sm100_kernel<BN, FP8><<<grid, kGemmThreads, smem, stream>>>(ta, tb, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-                                                                    M, N, K, (int)out.stride(0), sa, sb, status);
+  gemm_sm100_kernel<BN, FP8><<<grid, kGemmThreads, smem, stream>>>(
+      ta, tb, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), M, N, K, (int)out.stride(0), sa, sb, status, grp_off,
+      groups, tiles);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -321,6 +375,36 @@ void gemm_fp8_block(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch:
   else
     launch_gemm<128, true>(xq, wq, out, xs.data_ptr<float>(), ws.data_ptr<float>(), status.data_ptr<int>(), stream,
                            (int)max_ctas);
+}
+
+// Grouped block-scaled FP8 GEMM (MoE experts): xq [Mtot, K] rows sorted by group, group e = rows
+// [offsets[e], offsets[e+1]) (device int32 [G+1]); wq [G*N, K]; ws [G*ceil(N/128), K/128]; out [Mtot, N].
+void gemm_fp8_grouped(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor offsets,
+                      torch::Tensor out, torch::Tensor status) {
+  TORCH_CHECK(xq.scalar_type() == at::kFloat8_e4m3fn && wq.scalar_type() == at::kFloat8_e4m3fn);
+  TORCH_CHECK(offsets.scalar_type() == at::kInt && offsets.is_cuda() && offsets.dim() == 1);
+  const int M = xq.size(0), K = xq.size(1), N = out.size(1), G = offsets.size(0) - 1;
+  TORCH_CHECK(G >= 1 && wq.size(0) == (int64_t)G * N && wq.size(1) == K && K % 128 == 0 && N % 8 == 0);
+  TORCH_CHECK(ws.size(0) == (int64_t)G * ((N + 127) / 128) && ws.size(1) == K / 128);
+  TORCH_CHECK(xs.size(0) == K / 128 && xs.size(1) == M && out.size(0) == M);
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(xq.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  launch_gemm<256, true>(xq, wq, out, xs.data_ptr<float>(), ws.data_ptr<float>(), status.data_ptr<int>(), stream, 0,
+                         offsets.data_ptr<int>(), G);
+}
+
+// Grouped bf16 GEMM (bf16 MoE experts); same layout as gemm_fp8_grouped without scales.
+void gemm_bf16_grouped(torch::Tensor x, torch::Tensor w, torch::Tensor offsets, torch::Tensor out,
+                       torch::Tensor status) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16);
+  TORCH_CHECK(offsets.scalar_type() == at::kInt && offsets.is_cuda() && offsets.dim() == 1);
+  const int M = x.size(0), K = x.size(1), N = out.size(1), G = offsets.size(0) - 1;
+  TORCH_CHECK(G >= 1 && w.size(0) == (int64_t)G * N && w.size(1) == K && K % 64 == 0 && N % 8 == 0);
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  launch_gemm<256, false>(x, w, out, nullptr, nullptr, status.data_ptr<int>(), stream, 0, offsets.data_ptr<int>(), G);
 }
 
 void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tensor status, int64_t bn,

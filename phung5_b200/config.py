@@ -166,6 +166,8 @@ PRESETS: Dict[str, ModelConfig] = {
                         ffn=688, vocab=4096, rope_theta=1e4, rms_eps=1e-5),
     "tiny-draft": ModelConfig(name="tiny-draft", num_layers=1, hidden=256, num_heads=4, num_kv_heads=4,
                               head_dim=64, ffn=688, vocab=4096, rope_theta=1e4, rms_eps=1e-5),
+    "tiny-moe": ModelConfig(name="tiny-moe", arch="mixtral", num_layers=2, hidden=256, num_heads=4, num_kv_heads=4,
+                            head_dim=64, ffn=256, vocab=4096, rope_theta=1e4, num_experts=4, experts_per_token=2),
     "llama3-8b": ModelConfig(name="llama3-8b", num_layers=32, hidden=4096, num_heads=32, num_kv_heads=8,
                              head_dim=128, ffn=14336, vocab=128256, rope_theta=5e5, rms_eps=1e-5),
     "llama3-70b": ModelConfig(name="llama3-70b", num_layers=80, hidden=8192, num_heads=64, num_kv_heads=8,

@@ -153,7 +153,7 @@ def pack_weights(cfg: ModelConfig, wd: Dict[str, torch.Tensor], device, tp_rank:
                           qkv=qkv, o=o)
         if cfg.is_moe:
             from .mixtral import pack_moe
-            lw.moe = pack_moe(cfg, wd, p, device, tp_rank, tp_size)
+            lw.moe = pack_moe(cfg, wd, p, device, tp_rank, tp_size, dtype)
         else:
             lw.gu = _pack_linear([_row_shard_pair(_get(wd, p + f"mlp.{n}.weight"), tp_rank, tp_size)
                                   for n in ("gate_proj", "up_proj")], device, fp8, dtype)
@@ -288,7 +288,8 @@ class LlamaModel:
                               self.hkv, cfg.head_dim)
         a = self.attention(li, q, fb, fp8)
         o = self.comm.all_reduce(lw.o(a))
-        xq, xs, xb = ops.add_rmsnorm_quant(h, o, lw.post_norm, cfg.rms_eps, quant=fp8, out_bf16=not fp8)
+        xq, xs, xb = ops.add_rmsnorm_quant(h, o, lw.post_norm, cfg.rms_eps, quant=fp8,
+                                           out_bf16=(not fp8) or lw.moe is not None)
         if lw.moe is not None:
             return self.comm.all_reduce(lw.moe((xq, xs) if fp8 else xb, xb))
         gu = lw.gu((xq, xs) if fp8 else xb)

@@ -1,0 +1,156 @@
+"""Mixtral-style sparse MoE block on the grouped tcgen05 GEMMs.
+
+Routing: router logits = x @ W_gate^T (replicated [E, H]); each token takes its top-k experts, weights =
+softmax over the selected logits (Mixtral's rule, also the oracle's in models/reference.py).
+
+Expert parallelism: rank r of `ep` ranks owns experts [r*E/ep, (r+1)*E/ep) with full FFN width. Every
+rank holds every token (attention is tensor-parallel and its output is all-reduced), so dispatch is a
+local selection: the (token, slot) assignments of local experts are sorted by expert on the device
+(stable argsort, counts -> offsets, no host round trip), the fp8 activations are gathered in that
+order, gate/up and down run as grouped GEMMs over the per-expert row segments, and the combine
+scatters weight * expert output back per token. Each rank's output holds only its experts'
+contributions; the layer's all-reduce (the same collective as tensor-parallel MLPs) completes it.
+Rows beyond the local assignment count are never written by the grouped GEMMs; the combine selects
+(not multiplies) them away, so uninitialised rows cannot leak NaN.
+
+The reference serves no MoE model (EP row); this follows BASELINE config 4.
+"""
+from __future__ import annotations
+
+import zlib
+from dataclasses import dataclass
+from typing import Dict, Optional
+
+import torch
+
+from .. import ops
+from ..config import ModelConfig
+from ..weights.quant import quant_weight_block
+
+
+@dataclass
+class MoEBlock:
+    gate: torch.Tensor          # [E, H] router weight (bf16 / fp32), replicated
+    w13: torch.Tensor           # [E_local * 2F, H]: per expert gate rows then up rows
+    w13_s: Optional[torch.Tensor]
+    w2: torch.Tensor            # [E_local * H, F]
+    w2_s: Optional[torch.Tensor]
+    num_experts: int
+    top_k: int
+    e_lo: int
+    e_local: int
+    ffn: int
+    hidden: int
+
+    @property
+    def fp8(self) -> bool:
+        return self.w13_s is not None
+
+    def route(self, xb: torch.Tensor):
+        """-> (expert ids [T, k] int64, weights [T, k] fp32)."""
+        if xb.is_cuda and xb.dtype == torch.bfloat16 and self.gate.dtype == torch.bfloat16:
+            logits = ops.gemm_bf16(xb, self.gate)
+        else:
+            logits = xb.float() @ self.gate.float().t()
+        v, i = torch.topk(logits.float(), self.top_k, dim=-1)
+        return i, torch.softmax(v, dim=-1)
+
+    def __call__(self, x_act, xb: torch.Tensor) -> torch.Tensor:
+        t = xb.shape[0]
+        k, el = self.top_k, self.e_local
+        ids, w = self.route(xb)
+        flat = ids.reshape(-1) - self.e_lo                         # local expert of each assignment
+        local = (flat >= 0) & (flat < el)
+        key = torch.where(local, flat, torch.full_like(flat, el))  # non-local assignments sort last
+        order = torch.argsort(key, stable=True)                    # permuted position -> assignment
+        counts = torch.bincount(key, minlength=el + 1)[:el]
+        offsets = torch.zeros(el + 1, dtype=torch.int32, device=xb.device)
+        offsets[1:] = torch.cumsum(counts, 0).to(torch.int32)
+        tok = order // k                                          # token of each permuted row
+        if self.fp8:
+            xq, xs = x_act
+            xp = (xq[tok], xs[:, tok].contiguous())
+        else:
+            xp = x_act[tok]
+        gu = ops.gemm_grouped(xp, self.w13, self.w13_s, offsets, 2 * self.ffn)
+        aq, as_, ab = ops.silu_mul_quant(gu, quant=self.fp8, out_bf16=not self.fp8)
+        y = ops.gemm_grouped((aq, as_) if self.fp8 else ab, self.w2, self.w2_s, offsets, self.hidden)
+        # combine: position of every assignment in the permuted order
+        pos = torch.empty_like(order)
+        pos[order] = torch.arange(order.numel(), device=xb.device)
+        pos = pos.view(t, k)
+        valid = local.view(t, k)
+        g = y[pos.clamp(min=0)]                                    # [T, k, H]
+        contrib = torch.where(valid[..., None], g.float() * w[..., None], torch.zeros((), device=xb.device))
+        return contrib.sum(1).to(xb.dtype)
+
+
+def _expert_range(cfg: ModelConfig, rank: int, size: int):
+    if cfg.num_experts % size:
+        raise ValueError(f"{cfg.num_experts} experts do not split over {size} expert-parallel ranks")
+    el = cfg.num_experts // size
+    return rank * el, el
+
+
+def pack_moe(cfg: ModelConfig, wd: Dict[str, torch.Tensor], prefix: str, device, rank: int = 0, size: int = 1,
+             dtype: torch.dtype = torch.bfloat16) -> MoEBlock:
+    """HF Mixtral names: block_sparse_moe.gate.weight, block_sparse_moe.experts.{e}.w1/w3/w2.weight (+ _scale_inv)."""
+    fp8 = cfg.quant == "fp8_block"
+    e_lo, el = _expert_range(cfg, rank, size)
+    p = prefix + "block_sparse_moe."
+    w13, s13, w2, s2 = [], [], [], []
+
+    def get(name, want_fp8):
+        w, s = wd[name], wd.get(name + "_scale_inv")
+        if want_fp8:
+            if s is None:
+                return quant_weight_block(w.to(device).float())
+            return w.to(device), s.to(device).float()
+        if s is not None:
+            from .reference import dequant_block_fp8
+            w = dequant_block_fp8(w, s)
+        return w.to(device, dtype), None
+
+    for e in range(e_lo, e_lo + el):
+        ep = p + f"experts.{e}."
+        for nm in ("w1", "w3"):
+            w, s = get(ep + nm + ".weight", fp8)
+            w13.append(w)
+            s13.append(s)
+        w, s = get(ep + "w2.weight", fp8)
+        w2.append(w)
+        s2.append(s)
+    return MoEBlock(gate=wd[p + "gate.weight"].to(device, dtype), w13=torch.cat(w13).contiguous(),
+                    w13_s=torch.cat(s13).contiguous() if fp8 else None, w2=torch.cat(w2).contiguous(),
+                    w2_s=torch.cat(s2).contiguous() if fp8 else None, num_experts=cfg.num_experts,
+                    top_k=cfg.experts_per_token, e_lo=e_lo, e_local=el, ffn=cfg.ffn, hidden=cfg.hidden)
+
+
+def random_moe(cfg: ModelConfig, device, seed: int, layer: int, rank: int = 0, size: int = 1,
+               std: float = 0.02) -> MoEBlock:
+    fp8 = cfg.quant == "fp8_block"
+    e_lo, el = _expert_range(cfg, rank, size)
+    gen = torch.Generator(device=device)
+
+    def rnd(n, k, tag):
+        gen.manual_seed(zlib.crc32(repr((seed, layer, tag)).encode()) & 0x7FFFFFFF)
+        w = torch.randn(n, k, device=device, generator=gen, dtype=torch.bfloat16) * std
+        if fp8:
+            return quant_weight_block(w.float())
+        return w, None
+
+    w13, s13, w2, s2 = [], [], [], []
+    for e in range(e_lo, e_lo + el):
+        for nm in ("w1", "w3"):
+            w, s = rnd(cfg.ffn, cfg.hidden, (e, nm))
+            w13.append(w)
+            s13.append(s)
+        w, s = rnd(cfg.hidden, cfg.ffn, (e, "w2"))
+        w2.append(w)
+        s2.append(s)
+    gen.manual_seed(zlib.crc32(repr((seed, layer, "gate")).encode()) & 0x7FFFFFFF)
+    gate = torch.randn(cfg.num_experts, cfg.hidden, device=device, generator=gen, dtype=torch.bfloat16) * std
+    return MoEBlock(gate=gate, w13=torch.cat(w13).contiguous(),
+                    w13_s=torch.cat(s13).contiguous() if fp8 else None, w2=torch.cat(w2).contiguous(),
+                    w2_s=torch.cat(s2).contiguous() if fp8 else None, num_experts=cfg.num_experts,
+                    top_k=cfg.experts_per_token, e_lo=e_lo, e_local=el, ffn=cfg.ffn, hidden=cfg.hidden)

@@ -102,6 +102,36 @@ def gemm_bf16(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = No
     return out
 
 
+def gemm_grouped(x, w: torch.Tensor, ws: Optional[torch.Tensor], offsets: torch.Tensor, n: int,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Grouped linear for MoE experts. x = (xq, xs) block-scaled fp8 or a bf16 tensor, rows sorted by group;
+    group e owns rows [offsets[e], offsets[e+1]) (int32 device tensor, no host sync) and weight rows
+    [e*n, (e+1)*n) of w (ws: fp8 block scales [G*ceil(n/128), K/128]). Rows past offsets[-1] are not
+    written."""
+    xq = x[0] if isinstance(x, tuple) else x
+    m = xq.shape[0]
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.bfloat16 if xq.is_cuda else (torch.float32 if ws is not None else xq.dtype),
+                          device=xq.device)
+    if xq.is_cuda:
+        if ws is not None:
+            ext().gemm_fp8_grouped(x[0], x[1], w, ws, offsets, out, status_tensor(xq.device))
+        else:
+            ext().gemm_bf16_grouped(x, w, offsets, out, status_tensor(xq.device))
+        return out
+    off = offsets.tolist()
+    nb = (n + 127) // 128
+    for e in range(len(off) - 1):
+        a, b = off[e], off[e + 1]
+        if b <= a:
+            continue
+        if ws is not None:
+            out[a:b] = gemm_fp8_block_ref(x[0][a:b], x[1][:, a:b], w[e * n:(e + 1) * n], ws[e * nb:(e + 1) * nb]).to(out.dtype)
+        else:
+            out[a:b] = (x[a:b].float() @ w[e * n:(e + 1) * n].float().t()).to(out.dtype)
+    return out
+
+
 # ------------------------------------------------------------------------------------------------
 # sampling
 # ------------------------------------------------------------------------------------------------

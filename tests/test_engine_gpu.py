@@ -19,7 +19,7 @@ def _prompts(b, n, vocab, seed=0, shared=0):
     return [pre + torch.randint(0, vocab, (n - shared,), generator=g).tolist() for _ in range(b)]
 
 
-@pytest.mark.parametrize("name,tol", [("small-bf16", 0.03), ("small-fp8", 0.12)])
+@pytest.mark.parametrize("name,tol", [("small-bf16", 0.03), ("small-fp8", 0.12), ("small-moe-fp8", 0.15)])
 def test_engine_prefill_logits_close_to_oracle(name, tol):
     from phung5_b200.engine.attn_meta import build_items, make_meta, pack_work
     from phung5_b200.models.llama import ForwardBatch
@@ -39,7 +39,13 @@ def test_engine_prefill_logits_close_to_oracle(name, tol):
     logits, _ = eng.target.forward(fb)
     ops.check_status()
     rl, _ = ref.forward(torch.tensor(prompt), torch.arange(200), ref.new_cache())
-    err = ((logits.float().cpu() - rl).norm(dim=-1) / rl.norm(dim=-1)).max().item()
+    rows = (logits.float().cpu() - rl).norm(dim=-1) / rl.norm(dim=-1)
+    if cfg.is_moe:
+        # a near-tied router logit can route a token to another expert under bf16 vs fp32 routing:
+        # judge the bulk of the rows, not the worst one
+        err = rows.quantile(0.9).item()
+    else:
+        err = rows.max().item()
     assert err < tol, err
     # argmax agreement per position (a single greedy trajectory is fragile: near-tied random logits)
     agree = (logits.float().cpu().argmax(-1) == rl.argmax(-1)).float().mean().item()

@@ -236,3 +236,37 @@ def test_topk_logprobs(r, v, k, t):
     # indices agree up to exact ties in bf16
     got = xf.gather(1, idx)
     assert torch.equal(got, rv)
+
+
+@pytest.mark.parametrize("sizes,n,k", [([100, 0, 300, 7, 256], 512, 1024), ([513], 384, 256), ([0, 0, 64], 256, 512),
+                                       ([40] * 8, 3072, 1024)])
+def test_gemm_grouped(sizes, n, k):
+    g = len(sizes)
+    m = sum(sizes) + 50                       # tail rows past the last group are never written
+    x = torch.randn(m, k, device=DEV)
+    xq, xs = quant_act_block(x)
+    ws_list, s_list = [], []
+    for e in range(g):
+        q_, s_ = quant_weight_block(torch.randn(n, k, device=DEV) * 0.05)
+        ws_list.append(q_)
+        s_list.append(s_)
+    wq, ws = torch.cat(ws_list), torch.cat(s_list)
+    off = torch.tensor([0] + list(torch.tensor(sizes).cumsum(0)), dtype=torch.int32, device=DEV)
+    out = torch.full((m, n), 7.0, device=DEV, dtype=torch.bfloat16)
+    ops.gemm_grouped((xq, xs), wq, ws, off, n, out=out)
+    torch.cuda.synchronize()
+    o = off.tolist()
+    for e in range(g):
+        a, b = o[e], o[e + 1]
+        if b > a:
+            ref = gemm_fp8_block_ref(xq[a:b], xs[:, a:b], ws_list[e], s_list[e])
+            assert _rel(out[a:b], ref) < 5e-3
+    assert (out[o[-1]:].float() == 7.0).all()
+    # bf16 grouped
+    xb = x.bfloat16()
+    wb = torch.cat([w_.float() * 0 + torch.randn_like(w_.float()) * 0.05 for w_ in ws_list]).bfloat16()
+    outb = ops.gemm_grouped(xb, wb, None, off, n)
+    for e in range(g):
+        a, b = o[e], o[e + 1]
+        if b > a:
+            assert _rel(outb[a:b], xb[a:b].float() @ wb[e * n:(e + 1) * n].float().t()) < 5e-3
