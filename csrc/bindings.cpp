@@ -37,6 +37,8 @@ void gemm_fp8_grouped(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torc
                       torch::Tensor out, torch::Tensor status);
 void gemm_bf16_grouped(torch::Tensor x, torch::Tensor w, torch::Tensor offsets, torch::Tensor out,
                        torch::Tensor status);
+void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M, int64_t H, double eps, int64_t epoch,
+                torch::Tensor w, bool out_bf16, torch::Tensor status, std::vector<int64_t> offsets, int64_t s_ld);
 }  // namespace phx
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -52,4 +54,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_attention", &phx::paged_attention);
   m.def("paged_attention_tc", &phx::paged_attention_tc);
   m.def("topk_logprobs", &phx::topk_logprobs);
+  m.def("tp_ar_norm", &phx::tp_ar_norm);
 }

@@ -1,0 +1,240 @@
+// Fused tensor-parallel reduction + residual add + RMSNorm + block-FP8 quantization over NVLink peer memory.
+//
+// After a row-parallel projection (o_proj, down_proj) every rank holds a bf16 partial sum [M, H] in its
+// symmetric workspace. One launch of tp_ar_norm_kernel replaces "NCCL all-reduce, then add+RMSNorm+quant":
+//   1. start barrier: each rank publishes `epoch` into slot [0][rank] of every peer's flag array
+//      (st.release.sys) and waits until all peers' flags in its own array reach `epoch` (ld.acquire.sys);
+//   2. rank r owns rows [r*ceil(M/W), ...): for each row, a CTA loads the W peers' partial rows (P2P loads,
+//      16 bytes per thread per peer in flight), sums in fp32, rounds the sum to bf16 (as a bf16 all-reduce
+//      result), adds the residual, RMSNorm (block reduction), and quantizes to e4m3 with one fp32 scale per
+//      128 channels — or emits the normalized row in bf16 (final norm, bf16 models);
+//   3. pushes the new residual row, the fp8 row and its scales (or the bf16 row) into EVERY rank's
+//      workspace with P2P stores (a reduce-scatter + all-gather, fused with the normalization);
+//   4. end barrier: the last CTA to finish (device atomic counter) publishes slot [1][rank] to all peers
+//      and waits for theirs, so no rank's next GEMM overwrites a partial a peer is still reading, and
+//      every rank's outputs are complete when the kernel retires.
+// Every spin is bounded by a %globaltimer deadline; on expiry the kernel records kErrTimeoutPeer and
+// skips its work instead of hanging.
+// The reference has no tensor parallelism (configuration.yaml: tensor_parallel_size 1 everywhere); this is
+// the fused "GEMM -> reduce-scatter -> +residual -> RMSNorm -> FP8 quant -> all-gather" path of the
+// B200 design (the all-gather pushes the quantized rows the next GEMM consumes).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace phx {
+
+struct TpArgs {
+  const uint64_t* peer_base;  // [W] base address of every rank's workspace (device array)
+  int rank, world, M, H;
+  float eps;
+  uint32_t epoch;
+  const __nv_bfloat16* w;     // norm weight [H], local
+  int out_bf16;               // 0: fp8 q + scales, 1: bf16 y
+  int* status;
+  // byte offsets inside the workspace
+  uint64_t off_partial, off_h, off_y, off_q, off_s, off_flags, off_counter;
+  int s_ld;                   // row stride (elements) of the scale matrix [H/128, s_ld]
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// wait until flags[slot0 + i] >= epoch for i < W (threads 0..W-1 each poll one); false on timeout
+__device__ __forceinline__ bool wait_flags(const uint32_t* flags, int W, uint32_t epoch, int* status) {
+  __shared__ int fail;
+  if (threadIdx.x == 0) fail = 0;
+  __syncthreads();
+  if (threadIdx.x < W) {
+    const uint64_t t0 = globaltimer();
+    while ((int32_t)(ld_acquire_sys(flags + threadIdx.x) - epoch) < 0) {
+      if (globaltimer() - t0 > PHX_WAIT_TIMEOUT_NS) {
+        atomicCAS(status, 0, kErrTimeoutPeer);
+        fail = 1;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  return fail == 0;
+}
+
+template <int MAXC>
+__global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
+  __shared__ float red[32];
+  __shared__ int is_last;
+  const int W = a.world;
+  auto base = [&](int p) { return reinterpret_cast<uint8_t*>(a.peer_base[p]); };
+  uint8_t* mine = base(a.rank);
+  uint32_t* my_flags = reinterpret_cast<uint32_t*>(mine + a.off_flags);
+
+  // ---- 1. start barrier ----
+  if (blockIdx.x == 0 && threadIdx.x < W) {
+    __threadfence_system();
+    st_release_sys(reinterpret_cast<uint32_t*>(base(threadIdx.x) + a.off_flags) + a.rank, a.epoch);
+  }
+  const bool ok = wait_flags(my_flags, W, a.epoch, a.status);
+
+  // ---- 2./3. reduce my rows, normalize, push to every rank ----
+  const int H = a.H, nch = H / 8;
+  const int rows_per = (a.M + W - 1) / W;
+  const int r0 = a.rank * rows_per, r1 = min(a.M, r0 + rows_per);
+  for (int row = r0 + blockIdx.x; ok && row < r1; row += gridDim.x) {
+    float x[MAXC][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < nch) {
+        float acc[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+        const size_t off = ((size_t)row * H + c * 8) * 2;
+        for (int p = 0; p < W; ++p) {
+          const uint4 v = *reinterpret_cast<const uint4*>(base(p) + a.off_partial + off);
+          const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = unpack_bf16x2(vw[e]);
+            acc[2 * e] += f.x;
+            acc[2 * e + 1] += f.y;
+          }
+        }
+        const uint4 hv = *reinterpret_cast<const uint4*>(mine + a.off_h + off);
+        const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+        uint32_t nh[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          // all-reduce result rounded to bf16, then the bf16 residual add (the unfused path's rounding)
+          const float2 o = unpack_bf16x2(pack_bf16x2(acc[2 * e], acc[2 * e + 1]));
+          const float2 h = unpack_bf16x2(hw[e]);
+          nh[e] = pack_bf16x2(h.x + o.x, h.y + o.y);
+          const float2 r = unpack_bf16x2(nh[e]);
+          x[i][2 * e] = r.x;
+          x[i][2 * e + 1] = r.y;
+          ss += r.x * r.x + r.y * r.y;
+        }
+        const uint4 out = make_uint4(nh[0], nh[1], nh[2], nh[3]);
+        for (int p = 0; p < W; ++p) *reinterpret_cast<uint4*>(base(p) + a.off_h + off) = out;
+      }
+    }
+    // RMSNorm statistics
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+    __syncthreads();
+    const float inv = rsqrtf(tot / (float)H + a.eps);
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      const bool valid = c < nch;
+      float y[8];
+      if (valid) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(a.w + c * 8);
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_bf16x2(ww[e]);
+          y[2 * e] = x[i][2 * e] * inv * f.x;
+          y[2 * e + 1] = x[i][2 * e + 1] * inv * f.y;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = 0.f;
+      }
+      if (a.out_bf16) {
+        if (valid) {
+          const uint4 out = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
+                                       pack_bf16x2(y[6], y[7]));
+          const size_t off = ((size_t)row * H + c * 8) * 2;
+          for (int p = 0; p < W; ++p) *reinterpret_cast<uint4*>(base(p) + a.off_y + off) = out;
+        }
+      } else if (__any_sync(0xffffffffu, valid)) {
+        float amax = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(y[e]));
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        if (valid) {
+          const float sc = amax > 0.f ? amax / kFp8Max : 1.f;
+          const uint2 q = make_uint2(pack_fp8x4(y[0] / sc, y[1] / sc, y[2] / sc, y[3] / sc),
+                                     pack_fp8x4(y[4] / sc, y[5] / sc, y[6] / sc, y[7] / sc));
+          const size_t qoff = (size_t)row * H + c * 8;
+          const size_t soff = ((size_t)(c >> 4) * a.s_ld + row) * 4;
+          for (int p = 0; p < W; ++p) {
+            *reinterpret_cast<uint2*>(base(p) + a.off_q + qoff) = q;
+            if ((c & 15) == 0) *reinterpret_cast<float*>(base(p) + a.off_s + soff) = sc;
+          }
+        }
+      }
+    }
+  }
+
+  // ---- 4. end barrier (last CTA of this rank) ----
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    unsigned int* cnt = reinterpret_cast<unsigned int*>(mine + a.off_counter);
+    const unsigned int old = atomicAdd(cnt, 1u);
+    is_last = old == gridDim.x - 1;
+    if (is_last) *cnt = 0;  // the next launch starts after this one retires
+  }
+  __syncthreads();
+  if (is_last) {
+    if (threadIdx.x < W) {
+      __threadfence_system();
+      st_release_sys(reinterpret_cast<uint32_t*>(base(threadIdx.x) + a.off_flags) + W + a.rank, a.epoch);
+    }
+    wait_flags(my_flags + W, W, a.epoch, a.status);
+  }
+}
+
+void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M, int64_t H, double eps, int64_t epoch,
+                torch::Tensor w, bool out_bf16, torch::Tensor status, std::vector<int64_t> offsets, int64_t s_ld) {
+  TORCH_CHECK(peer_base.is_cuda() && peer_base.scalar_type() == at::kLong && peer_base.numel() == world);
+  TORCH_CHECK(H % 128 == 0 && world >= 1 && world <= 32 && offsets.size() == 7);
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(w.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  TpArgs a;
+  a.peer_base = reinterpret_cast<const uint64_t*>(peer_base.data_ptr<int64_t>());
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.M = (int)M;
+  a.H = (int)H;
+  a.eps = (float)eps;
+  a.epoch = (uint32_t)epoch;
+  a.w = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  a.out_bf16 = out_bf16 ? 1 : 0;
+  a.status = status.data_ptr<int>();
+  a.off_partial = offsets[0];
+  a.off_h = offsets[1];
+  a.off_y = offsets[2];
+  a.off_q = offsets[3];
+  a.off_s = offsets[4];
+  a.off_flags = offsets[5];
+  a.off_counter = offsets[6];
+  a.s_ld = (int)s_ld;
+  const int rows_per = (int)((M + world - 1) / world);
+  const int grid = std::max(1, std::min(rows_per, 148 * 4));
+  const int maxc = (int)((H / 8 + 255) / 256);
+  if (maxc <= 1) tp_ar_norm_kernel<1><<<grid, 256, 0, stream>>>(a);
+  else if (maxc <= 2) tp_ar_norm_kernel<2><<<grid, 256, 0, stream>>>(a);
+  else if (maxc <= 4) tp_ar_norm_kernel<4><<<grid, 256, 0, stream>>>(a);
+  else if (maxc <= 8) tp_ar_norm_kernel<8><<<grid, 256, 0, stream>>>(a);
+  else TORCH_CHECK(false, "hidden size too large");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace phx

@@ -296,8 +296,46 @@ class LlamaModel:
         aq, as_, ab = ops.silu_mul_quant(gu, quant=fp8, out_bf16=not fp8)
         return self.comm.all_reduce(lw.down((aq, as_) if fp8 else ab))
 
+    def forward_fused(self, fb: ForwardBatch, want_hidden: bool = False):
+        """Tensor-parallel forward on a fused communicator (parallel/fused.py): the residual stream lives in
+        the communicator's symmetric workspace, o_proj / down_proj write their partial sums into it, and one
+        `ar_norm` kernel per reduction does reduce-scatter + residual add + RMSNorm + quant + all-gather."""
+        comm, cfg = self.comm, self.cfg
+        m = fb.tokens.shape[0]
+        h = comm.h(m)
+        h.copy_(self.w.embed[fb.tokens])
+        fp8 = self.w.layers[0].qkv.fp8
+        xq, xs, xb = ops.add_rmsnorm_quant(h, None, self.w.layers[0].in_norm, cfg.rms_eps, quant=fp8, out_bf16=not fp8)
+        x = (xq, xs) if fp8 else xb
+        n = cfg.num_layers
+        for li in range(n):
+            lw = self.w.layers[li]
+            qkv = lw.qkv(x)
+            q = ops.rope_kv_write(qkv, fb.positions, fb.slots, self.cos_sin, self.kv_k[li], self.kv_v[li], self.hq,
+                                  self.hkv, cfg.head_dim)
+            a = self.attention(li, q, fb, fp8)
+            lw.o(a, out=comm.partial(m))
+            if lw.moe is not None:
+                yb = comm.ar_norm(m, lw.post_norm, cfg.rms_eps, out_bf16=True)
+                comm.partial(m).copy_(lw.moe(ops.act_quant(yb) if fp8 else yb, yb))
+            else:
+                x = comm.ar_norm(m, lw.post_norm, cfg.rms_eps, out_bf16=not fp8)
+                gu = lw.gu(x)
+                aq, as_, ab = ops.silu_mul_quant(gu, quant=fp8, out_bf16=not fp8)
+                lw.down((aq, as_) if fp8 else ab, out=comm.partial(m))
+            last = li == n - 1
+            wnext = self.w.final_norm if last else self.w.layers[li + 1].in_norm
+            x = comm.ar_norm(m, wnext, cfg.rms_eps, out_bf16=last or not fp8)
+        rows = x if fb.logits_rows is None else x[fb.logits_rows]
+        logits = ops.gemm_bf16(rows, self.w.lm_head)
+        return logits, (h if want_hidden else None)
+
     def forward(self, fb: ForwardBatch, want_hidden: bool = False):
         """Returns (logits [rows, V_local] bf16, final residual h [T, H] bf16 (pre-norm) if want_hidden)."""
+        comm = self.comm
+        if (getattr(comm, "fused", False) and 0 < fb.tokens.shape[0] <= comm.max_tokens
+                and comm.hidden == self.cfg.hidden):
+            return self.forward_fused(fb, want_hidden)
         h = self.w.embed[fb.tokens]
         delta = None
         for li in range(self.cfg.num_layers):

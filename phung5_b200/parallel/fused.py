@@ -1,0 +1,109 @@
+"""Fused tensor-parallel communicator: in-kernel NVLink reductions instead of NCCL collectives.
+
+Every rank allocates one symmetric workspace (torch.distributed._symmetric_memory: cuMem allocations
+mapped into every peer, exchanged at rendezvous) holding, for up to `max_tokens` rows:
+    partial [M, H] bf16   output of the row-parallel projection (o_proj / down_proj) of this rank
+    h       [M, H] bf16   residual stream (identical on every rank)
+    y       [M, H] bf16   normalized rows (final norm / bf16 models)
+    q       [M, H] e4m3   normalized rows, block-scaled fp8 (input of the next GEMM)
+    s       [H/128, Mmax] fp32 scales of q
+    flags   [2, W] u32    barrier flags (epochs)
+`ar_norm(M, w)` runs csrc/tp_fused.cu: reduce-scatter of the partials with P2P loads, + residual,
+RMSNorm, fp8 quant, all-gather of the results with P2P stores, in one kernel. The engine's model uses
+it when the communicator reports `fused = True` (models/llama.py, forward_fused); the EAGLE head and
+anything larger than the workspace keep the NCCL path of the base class.
+
+`FusedEmulator` gives the same interface on CPU ranks (gloo all-reduce + the op definitions) so the
+fused forward's plumbing is tested without GPUs.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from .comm import NcclCommunicator
+
+
+class _Workspace:
+    def __init__(self, max_tokens: int, hidden: int, device, world: int, alloc):
+        self.mmax, self.h = max_tokens, hidden
+        mh = max_tokens * hidden
+        off, o = {}, 0
+        for name, nbytes in (("partial", 2 * mh), ("h", 2 * mh), ("y", 2 * mh), ("q", mh),
+                             ("s", 4 * (hidden // 128) * max_tokens), ("flags", 4 * 2 * world), ("counter", 16)):
+            off[name] = o
+            o += (nbytes + 255) // 256 * 256
+        self.off = off
+        self.buf = alloc(o)
+
+    def view(self, name, dtype, shape):
+        n = 1
+        for d in shape:
+            n *= d
+        esz = torch.tensor([], dtype=dtype).element_size()
+        return self.buf[self.off[name]: self.off[name] + n * esz].view(dtype).view(*shape)
+
+
+class FusedCommunicator(NcclCommunicator):
+    fused = True
+
+    def __init__(self, max_tokens: int = 8192, hidden: int = 8192, group=None):
+        super().__init__(group)
+        import torch.distributed._symmetric_memory as symm
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
+        self.ws = _Workspace(max_tokens, hidden, dev, self.size,
+                             lambda n: symm.empty(n, dtype=torch.uint8, device=dev))
+        grp = self.group or dist.group.WORLD
+        self.handle = symm.rendezvous(self.ws.buf, grp.group_name)
+        self.peer_base = torch.tensor(list(self.handle.buffer_ptrs), dtype=torch.int64, device=dev)
+        self.ws.view("flags", torch.int32, (2 * self.size,)).zero_()
+        self.ws.view("counter", torch.int32, (4,)).zero_()
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)
+        self.epoch = 0
+        self.max_tokens = max_tokens
+        self.hidden = hidden
+
+    def partial(self, m: int) -> torch.Tensor:
+        return self.ws.view("partial", torch.bfloat16, (m, self.hidden))
+
+    def h(self, m: int) -> torch.Tensor:
+        return self.ws.view("h", torch.bfloat16, (m, self.hidden))
+
+    def ar_norm(self, m: int, w: torch.Tensor, eps: float, out_bf16: bool = False):
+        """h += sum over ranks of partial; returns the normalized rows: (q, s) fp8 or y bf16."""
+        self.epoch += 1
+        off = [self.ws.off[k] for k in ("partial", "h", "y", "q", "s", "flags", "counter")]
+        ops.ext().tp_ar_norm(self.peer_base, self.rank, self.size, m, self.hidden, eps, self.epoch, w, out_bf16,
+                             ops.status_tensor(self.device), off, m)
+        if out_bf16:
+            return self.ws.view("y", torch.bfloat16, (m, self.hidden))
+        q = self.ws.view("q", torch.float8_e4m3fn, (m, self.hidden))
+        s = self.ws.view("s", torch.float32, (self.hidden // 128, m))
+        return q, s
+
+
+class FusedEmulator(NcclCommunicator):
+    """CPU stand-in with FusedCommunicator's interface: all-reduce + the op definitions."""
+
+    fused = True
+
+    def __init__(self, max_tokens: int = 8192, hidden: int = 256, group=None, dtype=torch.float32):
+        super().__init__(group)
+        self.max_tokens, self.hidden = max_tokens, hidden
+        self._partial = torch.zeros(max_tokens, hidden, dtype=dtype)
+        self._h = torch.zeros(max_tokens, hidden, dtype=dtype)
+
+    def partial(self, m):
+        return self._partial[:m]
+
+    def h(self, m):
+        return self._h[:m]
+
+    def ar_norm(self, m, w, eps, out_bf16=False):
+        p = self._partial[:m].clone()
+        self.all_reduce(p)
+        q, s, y = ops.add_rmsnorm_quant(self._h[:m], p, w, eps, quant=not out_bf16, out_bf16=out_bf16)
+        return y if out_bf16 else (q, s)

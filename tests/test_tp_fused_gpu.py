@@ -1,0 +1,95 @@
+"""The fused NVLink all-reduce + RMSNorm + FP8 quant kernel (csrc/tp_fused.cu) on 2 GPUs: the fused
+forward equals the NCCL forward, and a peer that never arrives makes the bounded wait report
+kErrTimeoutPeer through the status word instead of hanging (NVLS is not used by this kernel)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from phung5_b200 import ops
+        from phung5_b200.config import preset
+        from phung5_b200.engine.attn_meta import build_items, make_meta, pack_work
+        from phung5_b200.models.llama import ForwardBatch, LlamaModel, random_packed_weights
+        from phung5_b200.parallel.comm import NcclCommunicator
+        from phung5_b200.parallel.fused import FusedCommunicator
+        cfg = preset("small-fp8")
+        dev = torch.device("cuda", rank)
+        w = random_packed_weights(cfg, dev, seed=0, tp_rank=rank, tp_size=world)
+        hkv = cfg.num_kv_heads // world
+        cs = ops.rope_table(2048, cfg.head_dim, cfg.rope_theta, dev)
+        fused = FusedCommunicator(max_tokens=1024, hidden=cfg.hidden)
+        res = {}
+        for name, comm in (("nccl", NcclCommunicator()), ("fused", fused)):
+            kk = torch.zeros(cfg.num_layers, 16, hkv, 64, 128, device=dev, dtype=torch.bfloat16)
+            vv = torch.zeros_like(kk)
+            model = LlamaModel(w, kk, vv, cs, comm)
+            n = 300
+            g = torch.Generator().manual_seed(5)
+            toks = torch.randint(0, cfg.vocab, (n,), generator=g).to(dev)
+            pages = list(range(1, 6))
+            meta = make_meta([pages], [0], [n], None, True, dev)
+            gg = model.hq // model.hkv
+            _, p2 = build_items(meta, gg)
+            slots = torch.tensor([pages[i // 64] * 64 + i % 64 for i in range(n)], device=dev)
+            fb = ForwardBatch(tokens=toks, positions=torch.arange(n, device=dev, dtype=torch.int32), slots=slots,
+                              meta=meta, work2=pack_work(p2, gg, dev))
+            for _ in range(2):      # twice: epochs advance, barriers reused
+                logits, h = model.forward(fb, want_hidden=True)
+            torch.cuda.synchronize()
+            ops.check_status(dev)
+            res[name] = (logits.float().cpu(), h.float().cpu().clone())
+        rel = ((res["fused"][0] - res["nccl"][0]).norm() / res["nccl"][0].norm()).item()
+        relh = ((res["fused"][1] - res["nccl"][1]).norm() / res["nccl"][1].norm()).item()
+        # timeout: only rank 0 launches the kernel; rank 1's flag never arrives
+        dist.barrier()
+        status = None
+        if rank == 0:
+            fused.ar_norm(8, w.layers[0].post_norm, cfg.rms_eps)
+            torch.cuda.synchronize()
+            status = int(ops.status_tensor(dev)[0].item())
+            ops.status_tensor(dev).zero_()
+        dist.barrier()
+        q.put((rank, rel, relh, status))
+    finally:
+        import torch.distributed as dist2
+        dist2.destroy_process_group()
+
+
+def test_fused_tp2_equals_nccl_and_times_out_cleanly():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in procs])
+    for p in procs:
+        p.join(timeout=60)
+    assert all(p.exitcode == 0 for p in procs)
+    for rank, rel, relh, status in res:
+        assert rel < 2e-2, rel
+        assert relh < 2e-2, relh
+    assert res[0][3] == 4     # kErrTimeoutPeer
