@@ -39,6 +39,17 @@ void gemm_bf16_grouped(torch::Tensor x, torch::Tensor w, torch::Tensor offsets, 
                        torch::Tensor status);
 void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M, int64_t H, double eps, int64_t epoch,
                 torch::Tensor w, bool out_bf16, torch::Tensor status, std::vector<int64_t> offsets, int64_t s_ld);
+void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+                   torch::Tensor state, torch::Tensor tok_start, torch::Tensor slot, double scale, torch::Tensor out,
+                   bool write_state, c10::optional<torch::Tensor> st_k, c10::optional<torch::Tensor> st_v,
+                   c10::optional<torch::Tensor> st_g);
+void gdn_fold(torch::Tensor state, torch::Tensor tok_start, torch::Tensor slot, torch::Tensor n_accept,
+              torch::Tensor st_k, torch::Tensor st_v, torch::Tensor st_g);
+void gdn_gates(torch::Tensor a, torch::Tensor b, torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor g,
+               torch::Tensor beta);
+void causal_conv1d(torch::Tensor x, torch::Tensor window, torch::Tensor w, c10::optional<torch::Tensor> bias,
+                   torch::Tensor tok_start, torch::Tensor slot, c10::optional<torch::Tensor> n_commit, torch::Tensor y);
+void gated_rmsnorm(torch::Tensor o, torch::Tensor z, torch::Tensor w, double eps, torch::Tensor y);
 }  // namespace phx
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -55,4 +66,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_attention_tc", &phx::paged_attention_tc);
   m.def("topk_logprobs", &phx::topk_logprobs);
   m.def("tp_ar_norm", &phx::tp_ar_norm);
+  m.def("gdn_recurrent", &phx::gdn_recurrent);
+  m.def("gdn_fold", &phx::gdn_fold);
+  m.def("gdn_gates", &phx::gdn_gates);
+  m.def("causal_conv1d", &phx::causal_conv1d);
+  m.def("gated_rmsnorm", &phx::gated_rmsnorm);
 }

@@ -270,3 +270,32 @@ def test_gemm_grouped(sizes, n, k):
         a, b = o[e], o[e + 1]
         if b > a:
             assert _rel(outb[a:b], xb[a:b].float() @ wb[e * n:(e + 1) * n].float().t()) < 5e-3
+
+
+def test_gdn_kernels_match_definitions():
+    from phung5_b200.models.gdn import random_gdn_layer
+    torch.manual_seed(0)
+    layer_c = random_gdn_layer(512, 2, 4, "cpu", seed=3, dtype=torch.float32)
+    layer_g = random_gdn_layer(512, 2, 4, DEV, seed=3, dtype=torch.bfloat16)
+    lens = [5, 1, 9]
+    ts = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+    slot = torch.tensor([2, 0, 1], dtype=torch.int32)
+    x = torch.randn(sum(lens), 512)
+    win = torch.randn(3, 3, layer_c.conv_channels) * 0.1
+    st = torch.randn(3, 4, 128, 128) * 0.01
+    wg, sg = win.to(DEV, torch.bfloat16), st.to(DEV)
+    wc, sc = win.to(torch.bfloat16).float(), st.clone()
+    xb = x.to(DEV, torch.bfloat16)
+    y_g = layer_g.forward(xb, ts.to(DEV), slot.to(DEV), wg, sg, mode="verify")
+    y_c = layer_c.forward(xb.float().cpu(), ts, slot, wc, sc, mode="verify")
+    assert _rel(y_g.float().cpu(), y_c) < 3e-2
+    n = torch.tensor([3, 1, 0], dtype=torch.int32)
+    layer_g.commit(n.to(DEV), wg, sg)
+    layer_c.commit(n, wc, sc)
+    torch.cuda.synchronize()
+    assert _rel(sg.cpu(), sc) < 2e-2
+    assert _rel(wg.float().cpu(), wc) < 1e-2
+    # prefill mode (state written in the kernel)
+    y2 = layer_g.forward(xb, ts.to(DEV), slot.to(DEV), wg, sg, mode="prefill")
+    y2c = layer_c.forward(xb.float().cpu(), ts, slot, wc, sc, mode="prefill")
+    assert _rel(y2.float().cpu(), y2c) < 3e-2 and _rel(sg.cpu(), sc) < 3e-2
