@@ -39,6 +39,24 @@ def _worker(rank, world, port, q):
         hkv = cfg.num_kv_heads // world
         cs = ops.rope_table(2048, cfg.head_dim, cfg.rope_theta, dev)
         fused = FusedCommunicator(max_tokens=1024, hidden=cfg.hidden)
+        # kernel-level check: seeded partials of every rank -> ar_norm vs a local torch reference
+        m, hd = 77, cfg.hidden
+        parts = [torch.randn(m, hd, generator=torch.Generator().manual_seed(100 + r)).bfloat16() for r in range(world)]
+        h0 = torch.randn(m, hd, generator=torch.Generator().manual_seed(7)).bfloat16()
+        wn = (1 + 0.1 * torch.randn(hd, generator=torch.Generator().manual_seed(8))).bfloat16()
+        fused.partial(m).copy_(parts[rank])
+        fused.h(m).copy_(h0)
+        torch.cuda.synchronize()
+        qf, sf = fused.ar_norm(m, wn.to(dev), cfg.rms_eps)
+        torch.cuda.synchronize()
+        tot = sum(p.float() for p in parts).bfloat16()
+        h_ref = (h0.float() + tot.float()).bfloat16()
+        hf = h_ref.float()
+        y_ref = hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + cfg.rms_eps) * wn.float()
+        deq = qf.float().cpu().view(m, hd // 128, 128) * sf.cpu().t()[..., None]
+        h_exact = torch.equal(fused.h(m).cpu(), h_ref)
+        y_err = ((deq.view(m, hd) - y_ref).abs().view(m, hd // 128, 128).amax(-1)
+                 / y_ref.abs().view(m, hd // 128, 128).amax(-1)).max().item()
         res = {}
         for name, comm in (("nccl", NcclCommunicator()), ("fused", fused)):
             kk = torch.zeros(cfg.num_layers, 16, hkv, 64, 128, device=dev, dtype=torch.bfloat16)
@@ -70,7 +88,7 @@ def _worker(rank, world, port, q):
             status = int(ops.status_tensor(dev)[0].item())
             ops.status_tensor(dev).zero_()
         dist.barrier()
-        q.put((rank, rel, relh, status))
+        q.put((rank, rel, relh, status, h_exact, y_err))
     finally:
         import torch.distributed as dist2
         dist2.destroy_process_group()
@@ -89,7 +107,10 @@ def test_fused_tp2_equals_nccl_and_times_out_cleanly():
     for p in procs:
         p.join(timeout=60)
     assert all(p.exitcode == 0 for p in procs)
-    for rank, rel, relh, status in res:
-        assert rel < 2e-2, rel
-        assert relh < 2e-2, relh
+    for rank, rel, relh, status, h_exact, y_err in res:
+        assert h_exact                          # reduce + residual add is the bf16 definition exactly
+        assert y_err <= 1.0 / 15, y_err         # fp8 rows within one e4m3 step of the definition
+        # whole 2-layer fp8 model: every activation is re-quantized, so tiny order differences compound
+        assert rel < 5e-2, rel
+        assert relh < 5e-2, relh
     assert res[0][3] == 4     # kErrTimeoutPeer
