@@ -201,7 +201,8 @@ def main():
     ops.check_status(dev)
 
     # ---- end-to-end region through the public API ----
-    h2d0, d2h0 = eng.stats["h2d_bytes"], eng.stats["d2h_bytes"]
+    from phung5_b200.engine.attn_meta import UPLOADED_BYTES
+    h2d0, d2h0 = eng.stats["h2d_bytes"] + UPLOADED_BYTES[0], eng.stats["d2h_bytes"]
     e2e_tokens = 0
     barrier()
     torch.cuda.synchronize()
@@ -211,7 +212,7 @@ def main():
             e2e_tokens += len(o.new_tokens)
     e2e_s = time.perf_counter() - t0
     e2e_s = comm.max_float(e2e_s) if comm is not None else e2e_s
-    h2d = (eng.stats["h2d_bytes"] - h2d0) / args.steps
+    h2d = (eng.stats["h2d_bytes"] + UPLOADED_BYTES[0] - h2d0) / args.steps
     d2h = (eng.stats["d2h_bytes"] - d2h0) / args.steps
 
     value = tokens / (ms / 1e3)
@@ -235,6 +236,9 @@ def main():
             "clocks": clk.summary(),
             "init_s": round(t_init, 1), "prefill_s": round(t_prefill, 1),
         }
+        if eng.host_times:
+            n = 2 * args.steps + args.warmup
+            line["host_ms_per_step"] = {k: round(1e3 * v / n, 2) for k, v in eng.host_times.items()}
         print(json.dumps(line))
     if comm is not None:
         import torch.distributed as dist

@@ -23,6 +23,20 @@ import torch
 ROWS_PER_TILE = 64
 
 
+UPLOADED_BYTES = [0]   # host->device bytes moved by upload() (reported per step by the benchmark)
+
+
+def upload(data, dtype, device) -> torch.Tensor:
+    """Host list / tensor -> device tensor without a stream synchronisation: CUDA destinations go through
+    pinned memory with a non-blocking copy (a pageable copy would wait for all queued GPU work)."""
+    t = data if isinstance(data, torch.Tensor) else torch.tensor(data, dtype=dtype)
+    t = t.to(dtype)
+    if torch.device(device).type == "cuda":
+        UPLOADED_BYTES[0] += t.numel() * t.element_size()
+        return t.pin_memory().to(device, non_blocking=True)
+    return t.to(device)
+
+
 @dataclass
 class AttnMeta:
     pages: torch.Tensor          # int32 [sum pages]
@@ -59,11 +73,11 @@ def make_meta(page_lists: Sequence[Sequence[int]], prefix_len: Sequence[int], q_
     for n in q_lens:
         qs.append(qs[-1] + n)
     kv = [p + n for p, n in zip(prefix_len, q_lens)]
-    i32 = dict(dtype=torch.int32, device=device)
+    i32 = torch.int32
     return AttnMeta(
-        pages=torch.tensor(flat if flat else [0], **i32), page_indptr=torch.tensor(indptr, **i32),
-        prefix_len=torch.tensor(list(prefix_len), **i32), kv_len=torch.tensor(kv, **i32),
-        q_start=torch.tensor(qs, **i32), tree=None if tree is None else tree.to(device=device, dtype=torch.int64),
+        pages=upload(flat if flat else [0], i32, device), page_indptr=upload(indptr, i32, device),
+        prefix_len=upload(list(prefix_len), i32, device), kv_len=upload(kv, i32, device),
+        q_start=upload(qs, i32, device), tree=None if tree is None else upload(tree, torch.int64, device),
         causal=causal, h_page_indptr=indptr, h_pages=flat, h_prefix_len=list(prefix_len), h_kv_len=kv,
         h_q_start=qs)
 
@@ -143,9 +157,12 @@ def pack_work(items: List[List[int]], group_size: int, device, pad_tiles: int = 
     if pad_tiles > n:
         ti = ti + [-1] * (pad_tiles - n)
         tr = tr + [0] * (pad_tiles - n)
-    it = torch.tensor(items if items else [[0] * 6], dtype=torch.int32, device=device)
-    return it, (torch.tensor(ti if ti else [-1], dtype=torch.int32, device=device),
-                torch.tensor(tr if tr else [0], dtype=torch.int32, device=device), max(n, pad_tiles))
+    flat_items = [x for it in (items if items else [[0] * 6]) for x in it]
+    ti = ti if ti else [-1]
+    tr = tr if tr else [0]
+    both = upload(flat_items + ti + tr, torch.int32, device)          # one copy for the three arrays
+    ni, nt = len(flat_items), len(ti)
+    return both[:ni].view(-1, 6), (both[ni:ni + nt], both[ni + nt:], max(n, pad_tiles))
 
 
 def attention_reference(q, k_cache, v_cache, meta: AttnMeta, scale, items, o_in=None, lse_in=None, o_part=None,
@@ -207,3 +224,65 @@ def attention_reference(q, k_cache, v_cache, meta: AttnMeta, scale, items, o_in=
             sc = torch.where(amax > 0, amax / FP8_MAX, torch.ones_like(amax))
             out_q.view(t_all, hq, d)[q0: q0 + qn] = (o / sc[..., None]).clamp(-FP8_MAX, FP8_MAX).to(out_q.dtype)
             out_qs[:, q0: q0 + qn] = sc.t()
+
+
+class PageTables:
+    """Page tables of one scheduling step's requests, uploaded once and shared by every forward of the
+    step (draft catch-up, every draft round, verify): only the small per-request arrays (prefix length,
+    query lengths) are uploaded per forward, in one packed copy. Cascade groups are computed once, with a
+    vectorised longest-common-prefix over the padded page matrix."""
+
+    def __init__(self, page_lists: Sequence[Sequence[int]], device, page_size: int):
+        import numpy as np
+        self.device = device
+        self.ps = page_size
+        self.h_indptr = [0]
+        self.h_pages: List[int] = []
+        for pl in page_lists:
+            self.h_pages.extend(pl)
+            self.h_indptr.append(len(self.h_pages))
+        i32 = dict(dtype=torch.int32)
+        both = upload(self.h_pages + self.h_indptr, torch.int32, device)
+        n = len(self.h_pages)
+        self.pages = both[:n] if n else torch.zeros(1, dtype=torch.int32, device=device)
+        self.page_indptr = both[n:]
+        lmax = max((len(pl) for pl in page_lists), default=0)
+        self.padded = np.full((len(page_lists), max(lmax, 1)), -1, dtype=np.int64)
+        for r, pl in enumerate(page_lists):
+            self.padded[r, :len(pl)] = pl
+
+    def groups(self, committed: Sequence[int], min_shared_pages: int = 1, min_group: int = 2):
+        """Consecutive requests sharing >= min_shared_pages committed pages: [(r_first, r_last, keys)]."""
+        import numpy as np
+        R = self.padded.shape[0]
+        if R < min_group:
+            return []
+        cp = np.asarray(committed, dtype=np.int64) // self.ps
+        lim = np.minimum(cp[1:], cp[:-1])                                   # [R-1]
+        cols = np.arange(self.padded.shape[1])[None, :]
+        eq = (self.padded[1:] == self.padded[:-1]) & (cols < lim[:, None]) & (self.padded[1:] >= 0)
+        lcp = np.where(eq.all(1), eq.shape[1], eq.argmin(1))                # consecutive LCP in pages
+        out, r = [], 0
+        while r < R:
+            e, shared = r, None
+            while e + 1 < R and lcp[e] >= min_shared_pages:
+                shared = lcp[e] if shared is None else min(shared, lcp[e])
+                e += 1
+            if e - r + 1 >= min_group and shared is not None and shared >= min_shared_pages:
+                out.append((r, e, int(shared) * self.ps))
+                r = e + 1
+            else:
+                r += 1
+        return out
+
+    def meta(self, prefix_len: Sequence[int], q_lens: Sequence[int], tree: Optional[torch.Tensor],
+             causal: bool) -> AttnMeta:
+        qs = [0]
+        for n in q_lens:
+            qs.append(qs[-1] + n)
+        kv = [p + n for p, n in zip(prefix_len, q_lens)]
+        packed = upload(list(prefix_len) + kv + qs, torch.int32, self.device)
+        R = len(prefix_len)
+        return AttnMeta(pages=self.pages, page_indptr=self.page_indptr, prefix_len=packed[:R], kv_len=packed[R:2 * R],
+                        q_start=packed[2 * R:], tree=tree, causal=causal, h_page_indptr=self.h_indptr,
+                        h_pages=self.h_pages, h_prefix_len=list(prefix_len), h_kv_len=kv, h_q_start=qs)

@@ -32,7 +32,7 @@ import torch
 from .. import ops
 from ..config import EngineConfig, ModelConfig, preset
 from ..models.llama import Communicator, ForwardBatch, LlamaModel, ModelWeights, random_packed_weights
-from .attn_meta import build_items, cascade_groups, make_meta, pack_work
+from .attn_meta import PageTables, build_items, cascade_groups, make_meta, pack_work, upload
 from .kv_pool import KVPool
 from .oracle import SamplingParams
 from .sampling import geometric_accept_len, sample_from, seeded_coins, target_probs
@@ -145,6 +145,10 @@ class LLMEngine:
         self.stats = {"steps": 0, "spec_steps": 0, "tokens_out": 0, "accepted": 0, "prefill_tokens": 0,
                       "h2d_bytes": 0, "d2h_bytes": 0}
         self.use_cascade = cfg.cache.enable_cascade
+        import os as _os
+        self._host_timing = _os.environ.get("PHX_HOST_TIMING") == "1"
+        self.host_times: Dict[str, float] = {}
+        self._mark_name, self._mark_t = None, 0.0
 
     # ------------------------------------------------------------------------------------------
     def _pages_from_memory(self, mc: ModelConfig, hkv: int, draft_layers: int) -> int:
@@ -414,12 +418,37 @@ class LLMEngine:
         gr = cascade_groups(meta, self.ps)
         return gr or None
 
+    def _clip_groups(self, groups, prefix):
+        """Groups whose shared keys do not exceed any member's visible prefix (catch-up prefixes are shorter
+        than the committed lengths the groups were computed from)."""
+        if not groups:
+            return None
+        out = []
+        for a, b, L in groups:
+            m = min(prefix[a:b + 1])
+            L2 = min(L, (m // self.ps) * self.ps)
+            if L2 > 0:
+                out.append((a, b, L2))
+        return out or None
+
     def _work(self, meta, groups):
         g = self.target.hq // self.target.hkv
         p1, p2 = build_items(meta, g, groups)
         return (pack_work(p1, g, self.device) if p1 else None), pack_work(p2, g, self.device)
 
+    def _mark(self, name: str) -> None:
+        """Host-side phase timer (PHX_HOST_TIMING=1): accumulates host wall time between marks per phase;
+        with the device running asynchronously this is the time the host spends enqueuing each phase
+        (the final commit phase includes waiting for the device)."""
+        if not self._host_timing:
+            return
+        now = time.perf_counter()
+        if self._mark_name is not None:
+            self.host_times[self._mark_name] = self.host_times.get(self._mark_name, 0.0) + now - self._mark_t
+        self._mark_name, self._mark_t = name, now
+
     def _spec_step(self, reqs: List[Request]) -> List[StepOutput]:
+        self._mark("setup")
         dev = self.device
         R, K, D, N = len(reqs), self.K, self.D, self.N
         scratch = 1 + (D - 1) * K
@@ -434,6 +463,7 @@ class LLMEngine:
         def slots_of(pos):  # pos [R, n] (device) -> slots
             return pt.gather(1, pos // self.ps) * self.ps + pos % self.ps
 
+        self._mark("draft_catchup")
         # ---- 1. draft catch-up: positions [dlen, committed] (root at `committed`) ----
         cu_tok, cu_pos, cu_slot, cu_hslot, last = [], [], [], [], []
         for r in reqs:
@@ -443,9 +473,10 @@ class LLMEngine:
                 cu_slot.append(self._slot(r, p))
                 cu_hslot.append(self._slot(r, p - 1) if p > 0 else 0)
             last.append(len(cu_tok) - 1)
-        meta = make_meta([r.pages for r in reqs], [r.dlen for r in reqs], [r.committed + 1 - r.dlen for r in reqs],
-                         None, True, dev)
-        w1, w2 = self._work(meta, self._groups(meta))
+        tables = PageTables([r.pages for r in reqs], dev, self.ps)
+        groups = (tables.groups(c_h) or None) if self.use_cascade else None
+        meta = tables.meta([r.dlen for r in reqs], [r.committed + 1 - r.dlen for r in reqs], None, True)
+        w1, w2 = self._work(meta, self._clip_groups(groups, [r.dlen for r in reqs]))
         fb = ForwardBatch(tokens=self._h2d(cu_tok, torch.int64), positions=self._h2d(cu_pos, torch.int32),
                           slots=self._h2d(cu_slot, torch.int64), meta=meta, work1=w1, work2=w2,
                           logits_rows=self._h2d(last, torch.int64))
@@ -456,6 +487,7 @@ class LLMEngine:
         root_feat = feat[fb.logits_rows] if feat is not None else None
 
         synth = self.cfg.spec.accept == "geometric" and K > 1
+        self._mark("draft_tree")
         # ---- 2. tree expansion ----
         lp, ti = self.dvocab.topk_logprobs(logits, K)          # [R, K]
         pool_tok, pool_score = [ti], [lp]
@@ -472,13 +504,10 @@ class LLMEngine:
             bits = front_bits_parent | (torch.ones_like(front_bits_parent) << sidx[None, :])
             pos = (c[:, None] + d).expand(R, K)
             sl = slots_of(c[:, None] + 1 + sidx[None, :])
-            dmeta = make_meta([r.pages for r in reqs], [r.committed + 1 for r in reqs], [K] * R, None, False, dev)
-            dmeta.tree = bits.reshape(-1)
-            dmeta.h_prefix_len = [ch + 1 for ch in c_h]
-            dmeta.h_kv_len = [ch + 1 + d * K for ch in c_h]
-            dmeta.kv_len = dmeta.prefix_len + d * K
+            dmeta = tables.meta([ch + 1 for ch in c_h], [K] * R, bits.reshape(-1), False)
             # draft scratch holds d*K entries after this round; keys [prefix, prefix + d*K)
-            dw1, dw2 = self._work(dmeta, self._groups(dmeta))
+            dmeta.h_kv_len = [ch + 1 + d * K for ch in c_h]
+            dw1, dw2 = self._work(dmeta, groups)
             fb = ForwardBatch(tokens=front_tok.reshape(-1), positions=pos.reshape(-1).to(torch.int32),
                               slots=sl.reshape(-1), meta=dmeta, work1=dw1, work2=dw2)
             lg, fe = self._draft_forward(fb, front_feat.reshape(R * K, -1) if front_feat is not None else None)
@@ -513,12 +542,13 @@ class LLMEngine:
         P_par = torch.cat(pool_par, 1)
         P_depth = torch.cat(pool_depth, 1)
 
+        self._mark("select")
         # ---- 3. select the verify tree ----
         nsel = N - 1
         adj = P_score - 1e-4 * P_depth.float()
         if synth:
             # spine nodes (best child of the spine at every depth) are pool entries 0, K, K+K*K, ...
-            spine = torch.tensor([0] + [K + (d - 1) * K * K for d in range(1, D)], device=dev)
+            spine = upload([0] + [K + (d - 1) * K * K for d in range(1, D)], torch.int64, dev)
             adj = adj.index_fill(1, spine, 0.0) + torch.zeros_like(adj).index_fill(1, spine, 1e6)
         _, sel = torch.topk(adj, nsel, dim=-1)
         key = P_depth.gather(1, sel).float() * 1e4 - adj.gather(1, sel)
@@ -539,21 +569,23 @@ class LLMEngine:
             pb = tbits.gather(1, parent.clamp(min=0))
             tbits = torch.where(depth == dd, pb | nb, tbits)
 
+        self._mark("verify")
         # ---- 4. verify ----
         vpos = c[:, None] + depth
         vslot = slots_of(c[:, None] + torch.arange(N, device=dev)[None, :])
-        vmeta = make_meta([r.pages for r in reqs], c_h, [N] * R, None, False, dev)
-        vmeta.tree = tbits.reshape(-1)
-        vw1, vw2 = self._work(vmeta, self._groups(vmeta))
+        vmeta = tables.meta(c_h, [N] * R, tbits.reshape(-1), False)
+        vw1, vw2 = self._work(vmeta, groups)
         fb = ForwardBatch(tokens=tokens.reshape(-1), positions=vpos.reshape(-1).to(torch.int32),
                           slots=vslot.reshape(-1), meta=vmeta, work1=vw1, work2=vw2)
         vlogits, vh = self.target.forward(fb, want_hidden=self.eagle)
         if self.pool.hidden is not None:
             self.pool.hidden[fb.slots] = vh
 
+        self._mark("accept")
         # ---- 5. accept ----
         acc_nodes, bonus = self._accept(reqs, vlogits.reshape(R, N, -1), tokens, parent, depth, c)
 
+        self._mark("commit_sync")
         # ---- 6. commit ----
         valid = acc_nodes >= 0
         jj = torch.arange(D, device=dev)[None, :].expand(R, D)
@@ -575,6 +607,8 @@ class LLMEngine:
             self.stats["accepted"] += n
             outs.append(self._emit(r, new))
         self.stats["spec_steps"] += 1
+        self._mark("host_tail")
+        self._mark_name = None
         return outs
 
     def _accept(self, reqs, logits, tokens, parent, depth, c):
@@ -590,7 +624,8 @@ class LLMEngine:
         if spec.accept == "geometric":
             steps = torch.tensor([r.steps for r in reqs])
             rid = torch.tensor([r.rid for r in reqs])
-            ngeo = geometric_accept_len(spec.accept_seed, steps, rid, spec.accept_p, spec.accept_cap).to(dev)
+            ngeo = upload(geometric_accept_len(spec.accept_seed, steps, rid, spec.accept_p, spec.accept_cap),
+                          torch.int64, dev)
         if greedy_all or spec.accept == "geometric":
             tgt = self.vocab.argmax(logits.reshape(R * N, -1)).reshape(R, N)
             for d in range(1, D + 1):
@@ -607,10 +642,11 @@ class LLMEngine:
                 alive &= has
             return acc, tgt.gather(1, cur[:, None])[:, 0]
         # seeded target-only tree sampling (per-request temperature / top-k / top-p)
-        temp = torch.tensor([r.params.temperature for r in reqs], device=dev)
-        topk = torch.tensor([r.params.top_k for r in reqs], device=dev)
-        topp = torch.tensor([r.params.top_p for r in reqs], device=dev)
-        coins = seeded_coins(torch.tensor([r.params.seed for r in reqs]), c.cpu(), D + 2).to(dev)
+        temp = upload([r.params.temperature for r in reqs], torch.float32, dev)
+        topk = upload([r.params.top_k for r in reqs], torch.int64, dev)
+        topp = upload([r.params.top_p for r in reqs], torch.float32, dev)
+        coins = upload(seeded_coins(torch.tensor([r.params.seed for r in reqs]),
+                                    torch.tensor([r.committed for r in reqs]), D + 2), torch.float32, dev)
         rows = torch.arange(R, device=dev)
         bonus = torch.zeros(R, dtype=torch.int64, device=dev)
         done = torch.zeros(R, dtype=torch.bool, device=dev)

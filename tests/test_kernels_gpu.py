@@ -299,3 +299,20 @@ def test_gdn_kernels_match_definitions():
     y2 = layer_g.forward(xb, ts.to(DEV), slot.to(DEV), wg, sg, mode="prefill")
     y2c = layer_c.forward(xb.float().cpu(), ts, slot, wc, sc, mode="prefill")
     assert _rel(y2.float().cpu(), y2c) < 3e-2 and _rel(sg.cpu(), sc) < 3e-2
+
+
+def test_moe_block_fp8_matches_oracle_and_routes_identically():
+    from phung5_b200.config import preset
+    from phung5_b200.models.llama import pack_weights
+    from phung5_b200.models.reference import moe_mlp
+    from phung5_b200.weights.init import random_weights
+    cfg = preset("small-moe-fp8")
+    w = random_weights(cfg, seed=0, std=0.02)
+    blk = pack_weights(cfg, w, DEV).layers[0].moe
+    xb = torch.randn(64, cfg.hidden).bfloat16().to(DEV)
+    y = blk(ops.act_quant(xb), xb).float().cpu()
+    ref = moe_mlp(xb.float().cpu(), w, "model.layers.0.", cfg)
+    assert ((y - ref).norm(dim=-1) / ref.norm(dim=-1)).max().item() < 0.08
+    ids, _ = blk.route(xb)
+    ref_ids = torch.topk(xb.float().cpu() @ w["model.layers.0.block_sparse_moe.gate.weight"].float().t(), 2, -1).indices
+    assert torch.equal(ids.cpu().sort(-1).values, ref_ids.sort(-1).values)
