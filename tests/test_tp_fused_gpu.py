@@ -83,7 +83,7 @@ def _worker(rank, world, port, q):
         dist.barrier()
         status = None
         if rank == 0:
-            fused.ar_norm(8, w.layers[0].post_norm, cfg.rms_eps)
+            fused.ar_norm(8 * world, w.layers[0].post_norm, cfg.rms_eps)
             torch.cuda.synchronize()
             status = int(ops.status_tensor(dev)[0].item())
             ops.status_tensor(dev).zero_()
@@ -97,10 +97,11 @@ def _worker(rank, world, port, q):
 def test_fused_tp2_equals_nccl_and_times_out_cleanly():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
+    world = min(4, torch.cuda.device_count())
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in procs])
