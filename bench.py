@@ -109,7 +109,7 @@ def main():
     ap.add_argument("--depth", type=int, default=6)
     ap.add_argument("--mode", default="tree", choices=["tree", "chain"])
     ap.add_argument("--num-draft", type=int, default=4)
-    ap.add_argument("--comm", default="nccl", choices=["nccl", "fused"])
+    ap.add_argument("--comm", default="fused", choices=["nccl", "fused"])
     ap.add_argument("--no-cascade", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override layer count (smoke runs only; not a bench value)")
     args = ap.parse_args()

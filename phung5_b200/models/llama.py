@@ -176,6 +176,9 @@ def random_packed_weights(cfg: ModelConfig, device, seed: int = 0, tp_rank: int 
     derived from (seed, layer, tensor, rank)."""
     fp8 = cfg.quant == "fp8_block"
     h, hd = cfg.hidden, cfg.head_dim
+    if cfg.num_heads % tp_size or cfg.num_kv_heads % tp_size or cfg.ffn % tp_size:
+        raise ValueError(f"{cfg.name}: heads {cfg.num_heads}/{cfg.num_kv_heads} and ffn {cfg.ffn} must divide "
+                         f"over {tp_size} tensor-parallel ranks")
     hq, hkv, f = cfg.num_heads // tp_size, cfg.num_kv_heads // tp_size, cfg.ffn // tp_size
     gen = torch.Generator(device=device)
 
