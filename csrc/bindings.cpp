@@ -50,6 +50,8 @@ void gdn_gates(torch::Tensor a, torch::Tensor b, torch::Tensor A_log, torch::Ten
 void causal_conv1d(torch::Tensor x, torch::Tensor window, torch::Tensor w, c10::optional<torch::Tensor> bias,
                    torch::Tensor tok_start, torch::Tensor slot, c10::optional<torch::Tensor> n_commit, torch::Tensor y);
 void gated_rmsnorm(torch::Tensor o, torch::Tensor z, torch::Tensor w, double eps, torch::Tensor y);
+torch::Tensor raster(torch::Tensor tris, torch::Tensor cols, torch::Tensor vp, int64_t W, int64_t H,
+                     std::vector<double> light, double ambient, double diffuse, double exposure, std::vector<double> bg);
 }  // namespace phx
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -71,4 +73,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_gates", &phx::gdn_gates);
   m.def("causal_conv1d", &phx::causal_conv1d);
   m.def("gated_rmsnorm", &phx::gated_rmsnorm);
+  m.def("raster", &phx::raster);
 }

@@ -1,0 +1,176 @@
+"""Scene previews without a graphics stack: three.js-style scene JSON -> world-space triangles -> the
+CUDA rasterizer (csrc/raster.cu; CPU tensors run its C++ restatement, the oracle).
+
+Supported scene JSON (the subset of three.js ObjectLoader JSON that the reference's serializer emits,
+pipeline_service/modules/js_checker/validator/serialize_worker.mjs): "geometries" with type
+BoxGeometry, SphereGeometry, CylinderGeometry, ConeGeometry, PlaneGeometry, TorusGeometry or
+BufferGeometry (data.attributes.position + optional data.index); "materials" with a "color" (int
+0xRRGGBB); and an "object" tree whose nodes carry a column-major 4x4 "matrix", "children", and
+"geometry"/"material" uuids. Views follow the reference's presets: camera on a sphere of radius 2
+around the unit-normalised object, vertical fov 49.1 degrees (renderer/render_service/renderer.js:10-15).
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Sequence, Tuple
+
+import torch
+
+from .. import ops
+
+
+def _box(w=1, h=1, d=1, **_):
+    x, y, z = w / 2, h / 2, d / 2
+    v = torch.tensor([[-x, -y, -z], [x, -y, -z], [x, y, -z], [-x, y, -z], [-x, -y, z], [x, -y, z], [x, y, z], [-x, y, z]])
+    f = [(0, 2, 1), (0, 3, 2), (4, 5, 6), (4, 6, 7), (0, 1, 5), (0, 5, 4), (3, 6, 2), (3, 7, 6), (1, 2, 6), (1, 6, 5),
+         (0, 4, 7), (0, 7, 3)]
+    return v, torch.tensor(f)
+
+
+def _lathe(profile: List[Tuple[float, float]], seg: int):
+    """Surface of revolution around y: profile [(radius, y)]."""
+    verts, faces = [], []
+    for (r, y) in profile:
+        for i in range(seg):
+            a = 2 * math.pi * i / seg
+            verts.append((r * math.sin(a), y, r * math.cos(a)))
+    for j in range(len(profile) - 1):
+        for i in range(seg):
+            a, b = j * seg + i, j * seg + (i + 1) % seg
+            c, d = a + seg, b + seg
+            faces += [(a, b, d), (a, d, c)]
+    return torch.tensor(verts, dtype=torch.float32), torch.tensor(faces)
+
+
+def _sphere(radius=1, widthSegments=24, heightSegments=12, **_):
+    prof = [(radius * math.sin(math.pi * k / heightSegments), radius * math.cos(math.pi * k / heightSegments))
+            for k in range(heightSegments + 1)]
+    return _lathe(prof, max(3, int(widthSegments)))
+
+
+def _cylinder(radiusTop=1, radiusBottom=1, height=1, radialSegments=24, **_):
+    h = height / 2
+    return _lathe([(0.0, h), (radiusTop, h), (radiusBottom, -h), (0.0, -h)], max(3, int(radialSegments)))
+
+
+def _cone(radius=1, height=1, radialSegments=24, **_):
+    return _cylinder(0.0, radius, height, radialSegments)
+
+
+def _plane(width=1, height=1, **_):
+    x, y = width / 2, height / 2
+    return torch.tensor([[-x, -y, 0], [x, -y, 0], [x, y, 0], [-x, y, 0]], dtype=torch.float32), torch.tensor([(0, 1, 2), (0, 2, 3)])
+
+
+def _torus(radius=1, tube=0.4, radialSegments=12, tubularSegments=32, **_):
+    verts, faces = [], []
+    R, T = int(radialSegments), int(tubularSegments)
+    for j in range(R):
+        for i in range(T):
+            u, v = 2 * math.pi * i / T, 2 * math.pi * j / R
+            verts.append(((radius + tube * math.cos(v)) * math.cos(u), (radius + tube * math.cos(v)) * math.sin(u),
+                          tube * math.sin(v)))
+    for j in range(R):
+        for i in range(T):
+            a, b = j * T + i, j * T + (i + 1) % T
+            c, d = ((j + 1) % R) * T + i, ((j + 1) % R) * T + (i + 1) % T
+            faces += [(a, b, d), (a, d, c)]
+    return torch.tensor(verts, dtype=torch.float32), torch.tensor(faces)
+
+
+_PRIMS = {"BoxGeometry": _box, "SphereGeometry": _sphere, "CylinderGeometry": _cylinder, "ConeGeometry": _cone,
+          "PlaneGeometry": _plane, "TorusGeometry": _torus}
+
+
+def _geometry(g: dict):
+    t = g.get("type")
+    if t in _PRIMS:
+        params = {k: v for k, v in g.items() if k not in ("type", "uuid")}
+        return _PRIMS[t](**params)
+    if t == "BufferGeometry":
+        data = g["data"]
+        pos = torch.tensor(data["attributes"]["position"]["array"], dtype=torch.float32).view(-1, 3)
+        if data.get("index"):
+            idx = torch.tensor(data["index"]["array"]).view(-1, 3)
+        else:
+            idx = torch.arange(pos.shape[0]).view(-1, 3)
+        return pos, idx
+    raise ValueError(f"unsupported geometry type {t!r}")
+
+
+def scene_triangles(scene: dict) -> Tuple[torch.Tensor, torch.Tensor]:
+    """-> (triangles [T, 3, 3] world space, colours [T, 3] linear RGB)."""
+    geoms = {g["uuid"]: g for g in scene.get("geometries", [])}
+    mats = {m["uuid"]: m for m in scene.get("materials", [])}
+    cache: Dict[str, tuple] = {}
+    tris, cols = [], []
+
+    def walk(node, parent):
+        m = torch.tensor(node.get("matrix", [1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1]), dtype=torch.float32)
+        world = parent @ m.view(4, 4).t()            # three.js matrices are column-major
+        gid = node.get("geometry")
+        if gid is not None and gid in geoms:
+            if gid not in cache:
+                cache[gid] = _geometry(geoms[gid])
+            v, f = cache[gid]
+            vh = torch.cat([v, torch.ones(v.shape[0], 1)], 1) @ world.t()
+            tris.append(vh[:, :3][f])
+            c = mats.get(node.get("material"), {}).get("color", 0xCCCCCC)
+            rgb = torch.tensor([(c >> 16) & 255, (c >> 8) & 255, c & 255], dtype=torch.float32) / 255.0
+            cols.append((rgb ** 2.2).expand(f.shape[0], 3))     # sRGB material colour -> linear
+        for ch in node.get("children", []):
+            walk(ch, world)
+
+    walk(scene.get("object", {}), torch.eye(4))
+    if not tris:
+        return torch.zeros(0, 3, 3), torch.zeros(0, 3)
+    return torch.cat(tris), torch.cat(cols)
+
+
+def normalise(tris: torch.Tensor) -> torch.Tensor:
+    """Centre on the bounding box and scale the largest extent to 1 (the reference frames views this way)."""
+    if tris.numel() == 0:
+        return tris
+    p = tris.reshape(-1, 3)
+    lo, hi = p.min(0).values, p.max(0).values
+    return (tris - (lo + hi) / 2) / float((hi - lo).max().clamp(min=1e-6))
+
+
+def view_projection(azimuth_deg: float, elevation_deg: float, radius: float = 2.0, fov_deg: float = 49.1,
+                    aspect: float = 1.0, near: float = 0.05, far: float = 20.0) -> torch.Tensor:
+    az, el = math.radians(azimuth_deg), math.radians(elevation_deg)
+    eye = torch.tensor([radius * math.cos(el) * math.sin(az), radius * math.sin(el), radius * math.cos(el) * math.cos(az)])
+    f = -eye / eye.norm()
+    up = torch.tensor([0.0, 1.0, 0.0])
+    s = torch.linalg.cross(f, up)
+    s = s / s.norm().clamp(min=1e-6)
+    u = torch.linalg.cross(s, f)
+    view = torch.eye(4)
+    view[0, :3], view[1, :3], view[2, :3] = s, u, -f
+    view[:3, 3] = torch.stack([-(s @ eye), -(u @ eye), f @ eye])
+    t = 1.0 / math.tan(math.radians(fov_deg) / 2)
+    proj = torch.zeros(4, 4)
+    proj[0, 0], proj[1, 1] = t / aspect, t
+    # view space looks down -z; depth in [0, 1] over [near, far], w = -z
+    proj[2, 2] = -far / (far - near)
+    proj[2, 3] = -far * near / (far - near)
+    proj[3, 2] = -1.0
+    return proj @ view
+
+
+def render(tris: torch.Tensor, cols: torch.Tensor, vp: torch.Tensor, size: int = 256, light=(0.4, 0.8, 0.6),
+           ambient: float = 0.35, diffuse: float = 0.9, exposure: float = 1.0, background=(1.0, 1.0, 1.0)) -> torch.Tensor:
+    """-> RGBA uint8 [size, size, 4]; CUDA tensors use the GPU rasterizer, CPU tensors its C++ restatement."""
+    return ops.ext().raster(tris.float().contiguous(), cols.float().contiguous(), vp.float(), size, size, list(light),
+                            ambient, diffuse, exposure, list(background))
+
+
+VIEW_PRESETS = {"front4": [(0, 15), (45, 15), (-45, 15), (90, 15)],
+                "judge": [(0, 15), (45, 25), (-45, 25), (90, 15), (180, 15), (0, 60)]}
+
+
+def render_views(scene: dict, preset: str = "front4", size: int = 256, device="cpu") -> List[torch.Tensor]:
+    tris, cols = scene_triangles(scene)
+    tris = normalise(tris).to(device)
+    cols = cols.to(device)
+    return [render(tris, cols, view_projection(a, e), size) for a, e in VIEW_PRESETS[preset]]
