@@ -1,0 +1,447 @@
+"""Candidate checker: mechanical repair -> static analysis -> sandboxed execution -> post-validation -> scene JSON.
+
+The reference runs three Node programs for this (pipeline_service/modules/js_checker/module.py:46-240 drives
+validator/{parse,staticAnalysis,execute,postValidation}.js and serialize_runner.mjs; repairs in
+mech_repair.py and three_repair.py). Here the same stages run in-process on the JavaScript interpreter of
+`jsvm.py`, whose AST the static rules walk directly.
+
+Failures are reported as {"stage", "rule", "detail"} records. Rule codes keep the reference's names
+(MISSING_DEFAULT_EXPORT, FORBIDDEN_IDENTIFIER, UNKNOWN_THREE_API, VERTEX_LIMIT_EXCEEDED, ...) because the
+coder's repair prompt quotes them back to the model. Limits follow the reference's post-validation
+(validator/postValidation.js:11-17): 250k vertices, 200 draw calls, depth 32, 50k instances, 4 MiB of
+texture data; execution gets a 5 s budget (execute.js:46).
+"""
+from __future__ import annotations
+
+import asyncio
+import difflib
+import hashlib
+import math
+import re
+from concurrent.futures import ThreadPoolExecutor
+from dataclasses import dataclass, field
+from typing import Any, Dict, List, Optional, Set
+
+from . import jsvm
+
+LIMITS = {"vertices": 250_000, "drawCalls": 200, "depth": 32, "instances": 50_000, "textureBytes": 4 * 1_048_576}
+LITERAL_BUDGET = 50 * 1024
+ROOT_TYPES = {"Group", "Mesh", "LineSegments", "Points", "Object3D", "InstancedMesh", "Line"}
+
+ALLOWED_ROOTS = {"Math", "Number", "String", "Array", "Object", "Boolean", "Error", "Infinity", "NaN", "undefined",
+                 "parseInt", "parseFloat", "isFinite", "isNaN", "console", "Float32Array", "Float64Array",
+                 "Uint8Array", "Uint8ClampedArray", "Uint16Array", "Uint32Array", "Int8Array", "Int16Array",
+                 "Int32Array", "arguments", "this"}
+FORBIDDEN_IDENTIFIERS = {"eval", "Function", "setTimeout", "setInterval", "setImmediate", "queueMicrotask", "fetch",
+                         "XMLHttpRequest", "WebSocket", "document", "window", "navigator", "localStorage",
+                         "sessionStorage", "indexedDB", "OffscreenCanvas", "HTMLCanvasElement", "crypto", "Date",
+                         "performance", "Proxy", "Reflect", "WeakRef", "FinalizationRegistry", "SharedArrayBuffer",
+                         "Atomics", "Worker", "process", "module", "global", "globalThis", "require", "importScripts",
+                         "self", "Buffer"}
+FORBIDDEN_PROPERTIES = {"constructor", "__proto__", "prototype", "__defineGetter__", "__defineSetter__",
+                        "__lookupGetter__", "__lookupSetter__", "caller", "callee"}
+# THREE members the interpreter implements (everything else is UNKNOWN or, if a real three.js name that is
+# excluded on purpose, FORBIDDEN)
+THREE_DISALLOWED_KNOWN = {"AmbientLight", "DirectionalLight", "PointLight", "SpotLight", "HemisphereLight",
+                          "RectAreaLight", "PerspectiveCamera", "OrthographicCamera", "WebGLRenderer",
+                          "TextureLoader", "ObjectLoader", "FileLoader", "ImageLoader", "GLTFLoader", "Fog",
+                          "FogExp2", "ShaderMaterial", "RawShaderMaterial", "VideoTexture", "CubeTexture",
+                          "AnimationMixer", "Clock", "Raycaster", "Audio", "AudioListener", "SkinnedMesh",
+                          "Skeleton", "Bone", "LOD", "Sprite", "SpriteMaterial", "CanvasTexture", "Texture",
+                          "MeshDepthMaterial", "MeshDistanceMaterial", "ShadowMaterial", "Scene"}
+THREE_BLOCKED_SUBMEMBERS = {"MathUtils": {"generateUUID"}}
+
+
+def three_allowed() -> Set[str]:
+    it = jsvm.Interp()
+    names = set(jsvm.make_three(it).props.keys())
+    return names - THREE_DISALLOWED_KNOWN
+
+
+THREE_ALLOWED = three_allowed()
+
+
+@dataclass
+class CheckResult:
+    ok: bool
+    failures: List[Dict[str, str]] = field(default_factory=list)
+    code: str = ""
+    scene: Optional[dict] = None
+    stats: Dict[str, Any] = field(default_factory=dict)
+    repaired: List[str] = field(default_factory=list)
+
+    @property
+    def digest(self) -> str:
+        return code_digest(self.code)
+
+    def summary(self) -> str:
+        return "; ".join(f"{f['rule']}: {f['detail']}" for f in self.failures[:6])
+
+
+def code_digest(code: str) -> str:
+    """Whitespace/comment-insensitive digest: candidates that differ only in formatting dedupe together."""
+    s = re.sub(r"//[^\n]*|/\*.*?\*/", "", code, flags=re.S)
+    s = re.sub(r"\s+", " ", s).strip()
+    return hashlib.sha1(s.encode()).hexdigest()[:16]
+
+
+# ------------------------------------------------------------------------------------------ mechanical repair
+
+_FENCE = re.compile(r"```(?:javascript|js|typescript|ts)?\s*\n(.*?)```", re.S | re.I)
+
+
+def extract_code(text: str) -> str:
+    """The module inside a model reply: the longest fenced block, else the text itself."""
+    blocks = _FENCE.findall(text or "")
+    if blocks:
+        with_export = [b for b in blocks if "export" in b]
+        return max(with_export or blocks, key=len).strip()
+    return (text or "").strip()
+
+
+def mechanical_repair(code: str) -> tuple:
+    """Fix the common, meaning-preserving mistakes of model-written modules. -> (code, [fixes])."""
+    fixes = []
+    c = code
+    new = re.sub(r"^\s*import\s+[^;\n]*?from\s+['\"][^'\"]+['\"]\s*;?\s*$", "", c, flags=re.M)
+    if new != c:
+        fixes.append("removed import statements")
+        c = new
+    if not re.search(r"\bexport\s+default\b", c):
+        m = re.search(r"\bexport\s+function\s+(\w+)", c)
+        if m:
+            c = c[:m.start()] + "export default function " + m.group(1) + c[m.end():]
+            fixes.append("export function -> export default function")
+        elif re.search(r"^\s*function\s+generate\s*\(", c, flags=re.M):
+            c = re.sub(r"^(\s*)function\s+generate\s*\(", r"\1export default function generate(", c, count=1, flags=re.M)
+            fixes.append("added export default to generate")
+    new = re.sub(r"\bexport\s+default\s+async\s+function", "export default function", c)
+    if new != c:
+        fixes.append("removed async from generate")
+        c = new
+    # three.js r125 removed the *BufferGeometry aliases
+    new = re.sub(r"\bTHREE\.(\w+)BufferGeometry\b", r"THREE.\1Geometry", c)
+    new = new.replace("THREE.Geometry(", "THREE.BufferGeometry(")
+    if new != c:
+        fixes.append("XBufferGeometry -> XGeometry")
+        c = new
+    names = set(re.findall(r"\bTHREE\.([A-Za-z_]\w*)", c))
+    for nm in sorted(names):
+        if nm in THREE_ALLOWED or nm in THREE_DISALLOWED_KNOWN:
+            continue
+        close = difflib.get_close_matches(nm, sorted(THREE_ALLOWED), n=1, cutoff=0.85)
+        if close:
+            c = re.sub(rf"\bTHREE\.{nm}\b", f"THREE.{close[0]}", c)
+            fixes.append(f"THREE.{nm} -> THREE.{close[0]}")
+    # lights are the renderer's job: drop their declarations, statements on them and their .add() calls
+    light_re = r"(?:AmbientLight|DirectionalLight|PointLight|SpotLight|HemisphereLight|RectAreaLight)"
+    light_vars = re.findall(rf"(?:const|let|var)\s+(\w+)\s*=\s*new\s+THREE\.{light_re}\b", c)
+    if light_vars:
+        for v in light_vars:
+            c = re.sub(rf"(?:const|let|var)\s+{v}\s*=\s*new\s+THREE\.{light_re}\b[^;\n]*;?", "", c)
+            c = re.sub(rf"(?<![\w.$]){v}\.[^;\n]*;", "", c)
+            c = re.sub(rf"[\w$.]+\.add\(\s*{v}\s*\)\s*;?", "", c)
+            c = re.sub(rf"(\.add\([^)]*?),\s*{v}\b", r"\1", c)
+            c = re.sub(rf"(\.add\(\s*){v}\s*,\s*", r"\1", c)
+        fixes.append(f"removed lights {sorted(set(light_vars))}")
+    return c, fixes
+
+
+# ------------------------------------------------------------------------------------------- static analysis
+
+
+def _walk(node, fn):
+    """Depth-first over the AST (tagged tuples, plus untagged tuples/lists of them); fn(node) returning False
+    stops the descent."""
+    if isinstance(node, tuple) and node and isinstance(node[0], str):
+        if fn(node) is False:
+            return
+        if node[0] == "objpat":       # entries are (key, target, default) with a plain-string key
+            for key, target, default in node[1]:
+                if isinstance(key, tuple):
+                    _walk(key, fn)
+                _walk(target, fn)
+                _walk(default, fn)
+            return
+        for ch in node[1:]:
+            _walk(ch, fn)
+    elif isinstance(node, (tuple, list)):
+        for ch in node:
+            _walk(ch, fn)
+
+
+def _declared_names(prog) -> Set[str]:
+    names: Set[str] = set()
+
+    def visit(n):
+        tag = n[0]
+        if tag in ("id",):
+            names.add(n[1])
+        elif tag == "fundecl":
+            names.add(n[1])
+        elif tag == "func":
+            if n[1]:
+                names.add(n[1] if isinstance(n[1], str) else "")
+        elif tag == "objpat" and n[2]:
+            names.add(n[2])
+        return True
+    _walk(prog, visit)
+    return names
+
+
+def static_analyze(prog) -> List[Dict[str, str]]:
+    fails: List[Dict[str, str]] = []
+
+    def fail(rule, detail):
+        fails.append({"stage": "static_analysis", "rule": rule, "detail": detail})
+
+    body = prog[1]
+    exports = [s for s in body if s[0] in ("export_default", "export_named", "export_decl")]
+    default = [s for s in exports if s[0] == "export_default"]
+    if not default:
+        fail("MISSING_DEFAULT_EXPORT", "no `export default` found")
+        return fails
+    if len(exports) > 1:
+        fail("MULTIPLE_TOP_LEVEL_EXPORTS", f"found {len(exports)} top-level exports, expected exactly 1")
+    fn = default[0][1]
+    if fn[0] == "ident":
+        target = next((s[2] for s in body if s[0] == "fundecl" and s[1] == fn[1]), None)
+        fn = target if target is not None else fn
+    if fn[0] != "func":
+        fail("DEFAULT_EXPORT_NOT_FUNCTION", "default export must be a function generate(THREE)")
+        return fails
+    params = fn[2]
+    three = params[0][0][1] if params and params[0][0][0] == "id" else None
+    if three is None:
+        fail("MISSING_THREE_PARAM", "generate must take THREE as its first parameter")
+    declared = _declared_names(prog)
+    literal_bytes = [0]
+    seen_forbidden: Set[str] = set()
+
+    def visit(n):
+        tag = n[0]
+        if tag == "ident":
+            nm = n[1]
+            if nm in FORBIDDEN_IDENTIFIERS:
+                if nm not in seen_forbidden:
+                    fail("FORBIDDEN_IDENTIFIER", f"`{nm}` is not allowed")
+                    seen_forbidden.add(nm)
+            elif nm == three:
+                fail("THREE_ALIAS_FORBIDDEN", f"`{three}` may only be used as `{three}.Member`")
+            elif nm not in declared and nm not in ALLOWED_ROOTS:
+                if nm not in seen_forbidden:
+                    fail("IDENTIFIER_NOT_ALLOWED", f"`{nm}` is not declared and not an allowed global")
+                    seen_forbidden.add(nm)
+            return True
+        if tag == "member":
+            obj, key, computed = n[1], n[2], n[4]
+            if key[0] == "lit" and isinstance(key[1], str) and key[1] in FORBIDDEN_PROPERTIES:
+                fail("FORBIDDEN_PROPERTY_ACCESS", f"`.{key[1]}` is not allowed")
+            if obj[0] == "ident" and obj[1] == three:
+                if computed or key[0] != "lit":
+                    fail("COMPUTED_PROPERTY_ACCESS", f"`{three}[...]` is not allowed")
+                else:
+                    nm = str(key[1])
+                    if nm not in THREE_ALLOWED:
+                        if nm in THREE_DISALLOWED_KNOWN:
+                            fail("FORBIDDEN_THREE_API", f"THREE.{nm} is excluded (lights, cameras, loaders and "
+                                                        f"renderers belong to the renderer)")
+                        else:
+                            fail("UNKNOWN_THREE_API", f"THREE.{nm} is not a supported three.js member")
+                _walk(key, visit)
+                return False
+            if obj[0] == "member" and obj[1][0] == "ident" and obj[1][1] == three and key[0] == "lit":
+                ns = obj[2][1] if obj[2][0] == "lit" else None
+                if ns in THREE_BLOCKED_SUBMEMBERS and key[1] in THREE_BLOCKED_SUBMEMBERS[ns]:
+                    fail("FORBIDDEN_THREE_API", f"THREE.{ns}.{key[1]} is not allowed")
+            _walk(obj, visit)
+            if key[0] != "lit":          # property names are not literals for the budget
+                _walk(key, visit)
+            return False
+        if tag == "lit":
+            v = n[1]
+            if isinstance(v, str):
+                literal_bytes[0] += len(v)
+            elif isinstance(v, float):
+                literal_bytes[0] += 8
+            return True
+        if tag == "tpl":
+            literal_bytes[0] += sum(len(p) for p in n[1] if isinstance(p, str))
+            return True
+        return True
+
+    # the default-exported function's parameter list declares THREE; uses of THREE elsewhere are aliases
+    _walk(body, visit)
+    if literal_bytes[0] > LITERAL_BUDGET:
+        fail("LITERAL_BUDGET_EXCEEDED", f"{literal_bytes[0]} bytes of literals (limit {LITERAL_BUDGET})")
+    return fails
+
+
+# --------------------------------------------------------------------------------------------- post-validation
+
+
+def declared_vertices(g) -> int:
+    """Vertex count three.js would build for a primitive's parameters (the preview mesh caps segments, the
+    limit must not)."""
+    p = g.params
+
+    def n(k, d):
+        v = p.get(k, d)
+        try:
+            return max(0, int(jsvm._to_num(v)))
+        except (TypeError, ValueError, OverflowError):
+            return d
+    t = g.gtype
+    if t == "BoxGeometry":
+        a, b, c = n("widthSegments", 1), n("heightSegments", 1), n("depthSegments", 1)
+        return 2 * ((a + 1) * (b + 1) + (a + 1) * (c + 1) + (b + 1) * (c + 1))
+    if t == "SphereGeometry":
+        return (n("widthSegments", 32) + 1) * (n("heightSegments", 16) + 1)
+    if t in ("CylinderGeometry", "ConeGeometry"):
+        r = n("radialSegments", 32)
+        return (r + 1) * (n("heightSegments", 1) + 1) + 2 * (2 * r + 1)
+    if t == "PlaneGeometry":
+        return (n("widthSegments", 1) + 1) * (n("heightSegments", 1) + 1)
+    if t == "TorusGeometry":
+        return (n("radialSegments", 12) + 1) * (n("tubularSegments", 48) + 1)
+    if t == "TorusKnotGeometry":
+        return (n("tubularSegments", 64) + 1) * (n("radialSegments", 8) + 1)
+    if t == "CircleGeometry":
+        return n("segments", 32) + 2
+    if t == "RingGeometry":
+        return (n("thetaSegments", 32) + 1) * (n("phiSegments", 1) + 1)
+    if t == "TubeGeometry":
+        return (n("tubularSegments", 64) + 1) * (n("radialSegments", 8) + 1)
+    if t == "LatheGeometry":
+        pts = p.get("points")
+        return (n("segments", 12) + 1) * (len(pts.items) if isinstance(pts, jsvm.JSArray) else 2)
+    if t == "CapsuleGeometry":
+        return (n("radialSegments", 8) + 1) * (2 * n("capSegments", 4) + 2)
+    return 0
+
+
+def post_validate(root) -> tuple:
+    """Walk the returned tree once with cycle detection. -> (failures, stats)."""
+    fails: List[Dict[str, str]] = []
+
+    def fail(rule, detail):
+        fails.append({"stage": "post_validation", "rule": rule, "detail": detail})
+
+    if not isinstance(root, jsvm.Object3D):
+        fail("INVALID_RETURN_TYPE", f"generate must return an Object3D, got {jsvm._typeof(root)}")
+        return fails, {}
+    if root.otype not in ROOT_TYPES:
+        fail("INVALID_ROOT_TYPE", f"root type {root.otype} is not one of {sorted(ROOT_TYPES)}")
+    stats = {"vertices": 0, "drawCalls": 0, "depth": 0, "instances": 0, "textureBytes": 0, "meshes": 0}
+    seen = set()
+    stack = [(root, 0)]
+    bad_numbers = False
+    while stack:
+        o, d = stack.pop()
+        if id(o) in seen:
+            fail("CYCLE_DETECTED", "the object graph contains a cycle")
+            break
+        seen.add(id(o))
+        stats["depth"] = max(stats["depth"], d)
+        if d > LIMITS["depth"]:
+            fail("DEPTH_LIMIT_EXCEEDED", f"walk exceeded max depth {LIMITS['depth']}")
+            break
+        for k in ("position", "rotation", "scale"):
+            if any(not math.isfinite(x) for x in o.props[k].v()):
+                bad_numbers = True
+        g = o.props.get("geometry")
+        if isinstance(g, jsvm.Geometry) and o.otype in ("Mesh", "InstancedMesh", "LineSegments", "Points", "Line"):
+            try:
+                v, _ = jsvm.geometry_mesh(g)
+                nv = max(int(v.shape[0]), declared_vertices(g))
+                if v.numel() and not bool(v.isfinite().all()):
+                    bad_numbers = True
+            except jsvm._Throw as e:
+                fail("GEOMETRY_ERROR", jsvm._to_str(e.value.props.get("message", "")) if isinstance(e.value, jsvm.JSObject) else "bad geometry")
+                nv = 0
+            if o.otype == "InstancedMesh":
+                cnt = int(jsvm._to_num(o.props.get("count", 0)))
+                stats["instances"] += cnt
+                stats["vertices"] += nv * cnt
+            else:
+                stats["vertices"] += nv
+            stats["drawCalls"] += 1
+            stats["meshes"] += 1
+            m = o.props.get("material")
+            for mm in (m.items if isinstance(m, jsvm.JSArray) else [m]):
+                if isinstance(mm, jsvm.Material):
+                    for val in mm.props.values():
+                        if isinstance(val, jsvm.Texture):
+                            stats["textureBytes"] += val.nbytes
+        for c in o.children():
+            stack.append((c, d + 1))
+    if bad_numbers:
+        fail("NON_FINITE_VALUE", "a transform or vertex is NaN or infinite")
+    for key, rule in (("vertices", "VERTEX_LIMIT_EXCEEDED"), ("drawCalls", "DRAW_CALL_LIMIT_EXCEEDED"),
+                      ("instances", "INSTANCE_LIMIT_EXCEEDED"), ("textureBytes", "TEXTURE_BYTES_EXCEEDED")):
+        if stats[key] > LIMITS[key]:
+            fail(rule, f"{stats[key]} {key} (limit {LIMITS[key]})")
+    if stats["meshes"] == 0 and not fails:
+        fail("EMPTY_SCENE", "the returned object contains no meshes")
+    return fails, stats
+
+
+# -------------------------------------------------------------------------------------------------- module
+
+
+@dataclass
+class CheckerSettings:
+    timeout_s: float = 5.0
+    max_steps: int = 20_000_000
+    repair: bool = True
+    workers: int = 4
+
+
+class JSChecker:
+    """check(code) -> CheckResult; check_async runs in a worker thread pool (the interpreter holds no
+    shared state, every call builds its own)."""
+
+    def __init__(self, settings: Optional[CheckerSettings] = None):
+        self.s = settings or CheckerSettings()
+        self._pool = ThreadPoolExecutor(max_workers=self.s.workers, thread_name_prefix="jscheck")
+        self.counts = {"checked": 0, "passed": 0}
+
+    def check(self, text: str, seed: int = 0) -> CheckResult:
+        self.counts["checked"] += 1
+        code = extract_code(text)
+        fixes: List[str] = []
+        if self.s.repair:
+            code, fixes = mechanical_repair(code)
+        try:
+            prog = jsvm.Parser(code).program()
+        except jsvm.JSError as e:
+            return CheckResult(False, [{"stage": "parse", "rule": "PARSE_ERROR", "detail": e.msg}], code, repaired=fixes)
+        except RecursionError:
+            return CheckResult(False, [{"stage": "parse", "rule": "PARSE_ERROR", "detail": "nesting too deep"}], code,
+                               repaired=fixes)
+        fails = static_analyze(prog)
+        if fails:
+            return CheckResult(False, fails, code, repaired=fixes)
+        res = jsvm.run_module(code, jsvm.Limits(steps=self.s.max_steps, seconds=self.s.timeout_s), seed=seed)
+        if res.error is not None:
+            rule = "EXECUTION_TIMEOUT" if res.error.startswith("TIMEOUT") else "EXECUTION_ERROR"
+            return CheckResult(False, [{"stage": "execution", "rule": rule, "detail": res.error}], code,
+                               stats={"steps": res.steps, "exec_s": res.seconds}, repaired=fixes)
+        fails, stats = post_validate(res.root)
+        stats.update({"steps": res.steps, "exec_s": round(res.seconds, 4)})
+        if fails:
+            return CheckResult(False, fails, code, stats=stats, repaired=fixes)
+        try:
+            scene = jsvm.to_scene_json(res.root)
+        except (ValueError, jsvm._Throw) as e:
+            return CheckResult(False, [{"stage": "serialize", "rule": "SERIALIZE_ERROR", "detail": str(e)[:200]}],
+                               code, stats=stats, repaired=fixes)
+        self.counts["passed"] += 1
+        return CheckResult(True, [], code, scene=scene, stats=stats, repaired=fixes)
+
+    async def check_async(self, text: str, seed: int = 0) -> CheckResult:
+        loop = asyncio.get_running_loop()
+        return await loop.run_in_executor(self._pool, self.check, text, seed)
+
+    def close(self):
+        self._pool.shutdown(wait=False, cancel_futures=True)

@@ -1,0 +1,3433 @@
+"""A sandboxed interpreter for the JavaScript subset that scene coders write, with a three.js object model.
+
+The reference executes each candidate module (`export default function generate(THREE) { ... }`) in a Node
+worker with a 5 s timeout and a 256 MB heap cap, then serialises the returned Object3D tree to three.js
+JSON (pipeline_service/modules/js_checker/validator/execute.js:46-47, serialize_worker.mjs). Node is not part
+of this framework, so candidates run here instead: a tokenizer, a recursive-descent parser and a
+tree-walking evaluator for ES2020 statements and expressions (let/const/var, functions and arrows with
+default/rest/destructured parameters, objects, arrays, spread, template literals, for/for-of/for-in/while,
+optional chaining, `??`), and a `THREE` namespace implemented natively (Object3D tree, primitive and
+buffer geometries with baked transforms, materials, Color, Vector2/3, Euler, Matrix4, InstancedMesh,
+MathUtils). Budgets replace the worker limits: an evaluation-step budget and a wall-clock deadline
+(timeout), and caps on array lengths and string sizes (heap).
+
+Isolation: JS values never reach Python attributes. Host objects answer only the property names their
+tables list, so no Python internals (`__class__`, builtins) are reachable from a candidate.
+
+`run_module(source)` -> `ModuleResult(root, error)`; `to_scene_json(root)` -> the scene JSON that
+`phung5_b200.render.scene` rasterises.
+"""
+from __future__ import annotations
+
+import math
+import re
+import struct
+import time
+import uuid as _uuid
+from dataclasses import dataclass, field
+from typing import Any, Callable, Dict, List, Optional, Tuple
+
+# --------------------------------------------------------------------------------------------------- errors
+
+
+class JSError(Exception):
+    """A JavaScript-level error (syntax, type, reference, or a thrown value)."""
+
+    def __init__(self, kind: str, msg: str):
+        super().__init__(f"{kind}: {msg}")
+        self.kind = kind
+        self.msg = msg
+
+
+class JSBudget(JSError):
+    pass
+
+
+class _Break(Exception):
+    pass
+
+
+class _Continue(Exception):
+    pass
+
+
+class _Return(Exception):
+    def __init__(self, value):
+        self.value = value
+
+
+class _Throw(Exception):
+    def __init__(self, value):
+        self.value = value
+
+
+class _Undefined:
+    _inst = None
+
+    def __new__(cls):
+        if cls._inst is None:
+            cls._inst = super().__new__(cls)
+        return cls._inst
+
+    def __repr__(self):
+        return "undefined"
+
+
+UNDEF = _Undefined()
+
+# ---------------------------------------------------------------------------------------------------- lexer
+
+_PUNCT = sorted("""
+>>>= ... === !== **= <<= >>= >>> &&= ||= ??= => == != <= >= && || ?? ?. ++ -- += -= *= /= %= &= |= ^= ** << >>
+{ } ( ) [ ] ; , < > + - * / % & | ^ ! ~ ? : = . @ #
+""".split(), key=len, reverse=True)
+_KEYWORDS = {"var", "let", "const", "function", "return", "if", "else", "for", "while", "do", "break", "continue",
+             "new", "true", "false", "null", "undefined", "typeof", "instanceof", "in", "of", "export", "default",
+             "import", "class", "this", "throw", "try", "catch", "finally", "switch", "case", "void", "delete",
+             "async", "await", "yield"}
+_ID_START = re.compile(r"[A-Za-z_$]")
+_ID_RE = re.compile(r"[A-Za-z0-9_$]*")
+_NUM_RE = re.compile(r"0[xX][0-9a-fA-F_]+|0[bB][01_]+|0[oO][0-7_]+|(?:\d[\d_]*\.?[\d_]*|\.\d[\d_]*)(?:[eE][+-]?\d+)?")
+
+
+@dataclass
+class Tok:
+    kind: str       # num, str, tpl, id, kw, p (punct), eof
+    val: Any
+    pos: int
+    nl: bool = False  # a line break precedes this token
+
+
+def tokenize(src: str) -> List[Tok]:
+    toks: List[Tok] = []
+    i, n, nl = 0, len(src), False
+    while i < n:
+        c = src[i]
+        if c in " \t\r\f\v﻿":
+            i += 1
+            continue
+        if c == "\n":
+            nl = True
+            i += 1
+            continue
+        if src.startswith("//", i):
+            j = src.find("\n", i)
+            i = n if j < 0 else j
+            continue
+        if src.startswith("/*", i):
+            j = src.find("*/", i + 2)
+            if j < 0:
+                raise JSError("SyntaxError", "unterminated comment")
+            nl = nl or "\n" in src[i:j]
+            i = j + 2
+            continue
+        start = i
+        if c.isdigit() or (c == "." and i + 1 < n and src[i + 1].isdigit()):
+            m = _NUM_RE.match(src, i)
+            text = m.group(0).replace("_", "")
+            if text[:2].lower() == "0x":
+                v = float(int(text[2:], 16))
+            elif text[:2].lower() == "0b":
+                v = float(int(text[2:], 2))
+            elif text[:2].lower() == "0o":
+                v = float(int(text[2:], 8))
+            else:
+                v = float(text)
+            i = m.end()
+            if i < n and src[i] == "n":
+                raise JSError("SyntaxError", "BigInt literals are not supported")
+            toks.append(Tok("num", v, start, nl))
+        elif c in "'\"":
+            s, i = _read_string(src, i + 1, c)
+            toks.append(Tok("str", s, start, nl))
+        elif c == "`":
+            parts, i = _read_template(src, i + 1)
+            toks.append(Tok("tpl", parts, start, nl))
+        elif _ID_START.match(c) or ord(c) > 127:
+            m = _ID_RE.match(src, i + 1)
+            j = m.end()
+            while j < n and ord(src[j]) > 127:
+                j += 1
+            word = src[i:j]
+            i = j
+            toks.append(Tok("kw" if word in _KEYWORDS else "id", word, start, nl))
+        else:
+            for p in _PUNCT:
+                if src.startswith(p, i):
+                    if p == "?." and i + 2 < n and src[i + 2].isdigit():
+                        continue   # `a ?.5 : b` is a conditional
+                    toks.append(Tok("p", p, start, nl))
+                    i += len(p)
+                    break
+            else:
+                raise JSError("SyntaxError", f"unexpected character {c!r} at {i}")
+        nl = False
+    toks.append(Tok("eof", None, n, nl))
+    return toks
+
+
+_ESC = {"n": "\n", "t": "\t", "r": "\r", "b": "\b", "f": "\f", "v": "\v", "0": "\0"}
+
+
+def _read_string(src, i, q):
+    out, n = [], len(src)
+    while i < n:
+        c = src[i]
+        if c == q:
+            return "".join(out), i + 1
+        if c == "\\":
+            i += 1
+            e = src[i] if i < n else ""
+            if e == "u":
+                if src[i + 1] == "{":
+                    j = src.index("}", i)
+                    out.append(chr(int(src[i + 2:j], 16)))
+                    i = j + 1
+                else:
+                    out.append(chr(int(src[i + 1:i + 5], 16)))
+                    i += 5
+                continue
+            if e == "x":
+                out.append(chr(int(src[i + 1:i + 3], 16)))
+                i += 3
+                continue
+            if e == "\n":
+                i += 1
+                continue
+            out.append(_ESC.get(e, e))
+            i += 1
+            continue
+        if c == "\n":
+            raise JSError("SyntaxError", "unterminated string")
+        out.append(c)
+        i += 1
+    raise JSError("SyntaxError", "unterminated string")
+
+
+def _read_template(src, i):
+    """-> ([str | expression-source], end)."""
+    parts, buf, n = [], [], len(src)
+    while i < n:
+        c = src[i]
+        if c == "`":
+            parts.append("".join(buf))
+            return parts, i + 1
+        if c == "\\":
+            e = src[i + 1]
+            buf.append(_ESC.get(e, e))
+            i += 2
+            continue
+        if c == "$" and i + 1 < n and src[i + 1] == "{":
+            parts.append("".join(buf))
+            buf = []
+            depth, j = 1, i + 2
+            while j < n and depth:
+                if src[j] == "{":
+                    depth += 1
+                elif src[j] == "}":
+                    depth -= 1
+                elif src[j] in "'\"":
+                    _, j = _read_string(src, j + 1, src[j])
+                    continue
+                elif src[j] == "`":
+                    _, j = _read_template(src, j + 1)
+                    continue
+                j += 1
+            parts.append(("expr", src[i + 2:j - 1]))
+            i = j
+            continue
+        buf.append(c)
+        i += 1
+    raise JSError("SyntaxError", "unterminated template literal")
+
+
+# --------------------------------------------------------------------------------------------------- parser
+# AST nodes are tuples: (tag, ...). Patterns: ("id", name) | ("objpat", [(key, pattern, default)], rest)
+# | ("arrpat", [(pattern | None, default)], rest) .
+
+_BINPREC = {"??": 1, "||": 2, "&&": 3, "|": 4, "^": 5, "&": 6, "==": 7, "!=": 7, "===": 7, "!==": 7,
+            "<": 8, ">": 8, "<=": 8, ">=": 8, "instanceof": 8, "in": 8, "<<": 9, ">>": 9, ">>>": 9,
+            "+": 10, "-": 10, "*": 11, "/": 11, "%": 11, "**": 12}
+_ASSIGN = {"=", "+=", "-=", "*=", "/=", "%=", "**=", "<<=", ">>=", ">>>=", "&=", "|=", "^=", "&&=", "||=", "??="}
+
+
+class Parser:
+    def __init__(self, src: str):
+        self.t = tokenize(src)
+        self.i = 0
+        self.no_in = False
+
+    # token helpers
+    @property
+    def cur(self) -> Tok:
+        return self.t[self.i]
+
+    def peek(self, k=1) -> Tok:
+        return self.t[min(self.i + k, len(self.t) - 1)]
+
+    def at(self, val, kind=None) -> bool:
+        c = self.cur
+        return c.val == val and c.kind in ((kind,) if kind else ("p", "kw"))
+
+    def eat(self, val, kind=None) -> bool:
+        if self.at(val, kind):
+            self.i += 1
+            return True
+        return False
+
+    def expect(self, val):
+        if not self.eat(val):
+            c = self.cur
+            raise JSError("SyntaxError", f"expected {val!r} but found {c.val!r} at {c.pos}")
+
+    def ident(self) -> str:
+        c = self.cur
+        if c.kind == "id" or (c.kind == "kw" and c.val in ("of", "async", "await", "yield", "undefined")):
+            self.i += 1
+            return c.val
+        raise JSError("SyntaxError", f"expected an identifier, found {c.val!r} at {c.pos}")
+
+    def semi(self):
+        if self.eat(";"):
+            return
+        c = self.cur
+        if c.nl or c.kind == "eof" or self.at("}"):
+            return
+        raise JSError("SyntaxError", f"unexpected token {c.val!r} at {c.pos}")
+
+    # program
+    def program(self):
+        body = []
+        while self.cur.kind != "eof":
+            body.append(self.statement(top=True))
+        return ("block", body)
+
+    def statement(self, top=False):
+        c = self.cur
+        if c.kind == "p":
+            if c.val == "{":
+                return self.block()
+            if c.val == ";":
+                self.i += 1
+                return ("empty",)
+        if c.kind == "kw":
+            v = c.val
+            if v in ("var", "let", "const"):
+                d = self.declaration()
+                self.semi()
+                return d
+            if v == "function":
+                return self.function_decl()
+            if v == "async" and self.peek().val == "function":
+                raise JSError("SyntaxError", "async functions are not supported")
+            if v == "return":
+                self.i += 1
+                if self.at(";") or self.at("}") or self.cur.nl or self.cur.kind == "eof":
+                    self.eat(";")
+                    return ("return", None)
+                e = self.expression()
+                self.semi()
+                return ("return", e)
+            if v == "if":
+                self.i += 1
+                self.expect("(")
+                test = self.expression()
+                self.expect(")")
+                cons = self.statement()
+                alt = self.statement() if self.eat("else") else None
+                return ("if", test, cons, alt)
+            if v == "for":
+                return self.for_stmt()
+            if v == "while":
+                self.i += 1
+                self.expect("(")
+                test = self.expression()
+                self.expect(")")
+                return ("while", test, self.statement())
+            if v == "do":
+                self.i += 1
+                body = self.statement()
+                self.expect("while")
+                self.expect("(")
+                test = self.expression()
+                self.expect(")")
+                self.eat(";")
+                return ("dowhile", body, test)
+            if v in ("break", "continue"):
+                self.i += 1
+                self.semi()
+                return (v,)
+            if v == "throw":
+                self.i += 1
+                e = self.expression()
+                self.semi()
+                return ("throw", e)
+            if v == "try":
+                return self.try_stmt()
+            if v == "switch":
+                return self.switch_stmt()
+            if v == "export":
+                if not top:
+                    raise JSError("SyntaxError", "export inside a block")
+                self.i += 1
+                if self.eat("default"):
+                    if self.at("function"):
+                        f = self.function_expr()
+                        self.eat(";")
+                        return ("export_default", f)
+                    e = self.assign()
+                    self.semi()
+                    return ("export_default", e)
+                if self.at("function"):
+                    f = self.function_decl()
+                    return ("export_named", f, f[1])
+                if self.cur.val in ("const", "let", "var"):
+                    d = self.declaration()
+                    self.semi()
+                    return ("export_decl", d)
+                raise JSError("SyntaxError", "unsupported export form")
+            if v == "import":
+                raise JSError("SyntaxError", "import statements are not allowed (THREE is passed to generate)")
+            if v == "class":
+                raise JSError("SyntaxError", "class declarations are not supported")
+        e = self.expression()
+        self.semi()
+        return ("expr", e)
+
+    def block(self):
+        self.expect("{")
+        body = []
+        while not self.at("}"):
+            if self.cur.kind == "eof":
+                raise JSError("SyntaxError", "unexpected end of input")
+            body.append(self.statement())
+        self.i += 1
+        return ("block", body)
+
+    def declaration(self):
+        kind = self.cur.val
+        self.i += 1
+        decls = []
+        while True:
+            target = self.pattern()
+            init = self.assign() if self.eat("=") else None
+            if init is None and kind == "const" and not (self.at("of") or self.at("in")):
+                raise JSError("SyntaxError", "missing initializer in const declaration")
+            decls.append((target, init))
+            if not self.eat(","):
+                break
+        return ("decl", kind, decls)
+
+    def pattern(self):
+        if self.eat("{"):
+            props, rest = [], None
+            while not self.at("}"):
+                if self.eat("..."):
+                    rest = self.ident()
+                    break
+                if self.eat("["):
+                    key = self.assign()
+                    self.expect("]")
+                    key = ("computed", key)
+                else:
+                    c = self.cur
+                    if c.kind in ("str", "num"):
+                        self.i += 1
+                        key = _prop_key(c.val)
+                    else:
+                        key = c.val
+                        self.i += 1
+                if self.eat(":"):
+                    target = self.pattern()
+                else:
+                    target = ("id", key)
+                default = self.assign() if self.eat("=") else None
+                props.append((key, target, default))
+                if not self.eat(","):
+                    break
+            self.expect("}")
+            return ("objpat", props, rest)
+        if self.eat("["):
+            elems, rest = [], None
+            while not self.at("]"):
+                if self.at(","):
+                    self.i += 1
+                    elems.append((None, None))
+                    continue
+                if self.eat("..."):
+                    rest = self.pattern()
+                    break
+                target = self.pattern()
+                default = self.assign() if self.eat("=") else None
+                elems.append((target, default))
+                if not self.eat(","):
+                    break
+            self.expect("]")
+            return ("arrpat", elems, rest)
+        return ("id", self.ident())
+
+    def params(self):
+        self.expect("(")
+        ps, rest = [], None
+        while not self.at(")"):
+            if self.eat("..."):
+                rest = self.pattern()
+                break
+            target = self.pattern()
+            default = self.assign() if self.eat("=") else None
+            ps.append((target, default))
+            if not self.eat(","):
+                break
+        self.expect(")")
+        return ps, rest
+
+    def function_decl(self):
+        self.expect("function")
+        if self.eat("*"):
+            raise JSError("SyntaxError", "generators are not supported")
+        name = self.ident()
+        ps, rest = self.params()
+        body = self.block()
+        return ("fundecl", name, ("func", name, ps, rest, body, False))
+
+    def function_expr(self):
+        self.expect("function")
+        if self.eat("*"):
+            raise JSError("SyntaxError", "generators are not supported")
+        name = self.ident() if not self.at("(") else None
+        ps, rest = self.params()
+        body = self.block()
+        return ("func", name, ps, rest, body, False)
+
+    def for_stmt(self):
+        self.expect("for")
+        if self.at("await"):
+            raise JSError("SyntaxError", "for await is not supported")
+        self.expect("(")
+        init = None
+        if self.cur.val in ("var", "let", "const") and self.cur.kind == "kw":
+            kind = self.cur.val
+            save = self.i
+            self.i += 1
+            target = self.pattern()
+            if self.at("of") or self.at("in"):
+                op = self.cur.val
+                self.i += 1
+                it = self.assign() if op == "of" else self.expression()
+                self.expect(")")
+                return ("forof" if op == "of" else "forin", kind, target, it, self.statement())
+            self.i = save
+            self.no_in = True
+            init = self.declaration()
+            self.no_in = False
+        elif not self.at(";"):
+            save = self.i
+            self.no_in = True
+            e = self.expression()
+            self.no_in = False
+            if self.at("of") or self.at("in"):
+                self.i = save
+                target = self.pattern()
+                op = self.cur.val
+                self.i += 1
+                it = self.assign() if op == "of" else self.expression()
+                self.expect(")")
+                return ("forof" if op == "of" else "forin", None, target, it, self.statement())
+            init = ("expr", e)
+        self.expect(";")
+        test = None if self.at(";") else self.expression()
+        self.expect(";")
+        update = None if self.at(")") else self.expression()
+        self.expect(")")
+        return ("for", init, test, update, self.statement())
+
+    def try_stmt(self):
+        self.expect("try")
+        body = self.block()
+        param, handler, fin = None, None, None
+        if self.eat("catch"):
+            if self.eat("("):
+                param = self.pattern()
+                self.expect(")")
+            handler = self.block()
+        if self.eat("finally"):
+            fin = self.block()
+        return ("try", body, param, handler, fin)
+
+    def switch_stmt(self):
+        self.expect("switch")
+        self.expect("(")
+        disc = self.expression()
+        self.expect(")")
+        self.expect("{")
+        cases = []
+        while not self.eat("}"):
+            if self.eat("default"):
+                test = None
+            else:
+                self.expect("case")
+                test = self.expression()
+            self.expect(":")
+            body = []
+            while not (self.at("case") or self.at("default") or self.at("}")):
+                body.append(self.statement())
+            cases.append((test, body))
+        return ("switch", disc, cases)
+
+    # expressions
+    def expression(self):
+        e = self.assign()
+        if self.at(","):
+            seq = [e]
+            while self.eat(","):
+                seq.append(self.assign())
+            return ("seq", seq)
+        return e
+
+    def _arrow_ahead(self) -> bool:
+        """At `(`: is this the parameter list of an arrow function?"""
+        depth, j = 0, self.i
+        while j < len(self.t):
+            tk = self.t[j]
+            if tk.kind == "p" and tk.val in "([{" and len(tk.val) == 1:
+                depth += 1
+            elif tk.kind == "p" and tk.val in ")]}" and len(tk.val) == 1:
+                depth -= 1
+                if depth == 0:
+                    nx = self.t[j + 1]
+                    return nx.kind == "p" and nx.val == "=>" and not nx.nl
+            elif tk.kind == "eof":
+                return False
+            j += 1
+        return False
+
+    def arrow_body(self, ps, rest):
+        if self.at("{"):
+            body = self.block()
+            return ("func", None, ps, rest, body, True)
+        save = self.no_in
+        self.no_in = False
+        e = self.assign()
+        self.no_in = save
+        return ("func", None, ps, rest, ("block", [("return", e)]), True)
+
+    def assign(self):
+        c = self.cur
+        if c.kind == "kw" and c.val == "async" and (self.peek().val == "(" or self.peek().kind == "id"):
+            raise JSError("SyntaxError", "async functions are not supported")
+        if (c.kind == "id" or (c.kind == "kw" and c.val in ("of",))) and self.peek().val == "=>" and self.peek().kind == "p":
+            self.i += 2
+            return self.arrow_body([(("id", c.val), None)], None)
+        if self.at("(") and self._arrow_ahead():
+            ps, rest = self.params()
+            self.expect("=>")
+            return self.arrow_body(ps, rest)
+        left = self.conditional()
+        if self.cur.kind == "p" and self.cur.val in _ASSIGN:
+            op = self.cur.val
+            self.i += 1
+            right = self.assign()
+            if op == "=" and left[0] in ("object", "array"):
+                return ("assign_pat", _to_pattern(left), right)
+            if left[0] not in ("ident", "member"):
+                raise JSError("SyntaxError", "invalid assignment target")
+            return ("assign", op, left, right)
+        return left
+
+    def conditional(self):
+        test = self.binary(0)
+        if self.eat("?"):
+            save = self.no_in
+            self.no_in = False
+            cons = self.assign()
+            self.no_in = save
+            self.expect(":")
+            alt = self.assign()
+            return ("cond", test, cons, alt)
+        return test
+
+    def binary(self, minp):
+        left = self.unary()
+        while True:
+            c = self.cur
+            op = c.val
+            if not ((c.kind == "p" or (c.kind == "kw" and op in ("instanceof", "in"))) and op in _BINPREC):
+                return left
+            if op == "in" and self.no_in:
+                return left
+            p = _BINPREC[op]
+            if p < minp or (p == minp and op != "**"):
+                if not (op == "**" and p >= minp):
+                    return left
+            self.i += 1
+            right = self.binary(p if op == "**" else p + 1)
+            if op in ("&&", "||", "??"):
+                left = ("logic", op, left, right)
+            else:
+                left = ("bin", op, left, right)
+
+    def unary(self):
+        c = self.cur
+        if c.kind == "p" and c.val in ("!", "-", "+", "~"):
+            self.i += 1
+            return ("unary", c.val, self.unary())
+        if c.kind == "p" and c.val in ("++", "--"):
+            self.i += 1
+            return ("update", c.val, True, self.unary())
+        if c.kind == "kw" and c.val in ("typeof", "void", "delete"):
+            self.i += 1
+            return ("unary", c.val, self.unary())
+        if c.kind == "kw" and c.val == "await":
+            raise JSError("SyntaxError", "await is not supported")
+        return self.postfix()
+
+    def postfix(self):
+        e = self.call_member(self.primary())
+        c = self.cur
+        if c.kind == "p" and c.val in ("++", "--") and not c.nl:
+            self.i += 1
+            return ("update", c.val, False, e)
+        return e
+
+    def args(self):
+        out = []
+        self.expect("(")
+        while not self.at(")"):
+            if self.eat("..."):
+                out.append(("spread", self.assign()))
+            else:
+                out.append(self.assign())
+            if not self.eat(","):
+                break
+        self.expect(")")
+        return out
+
+    def call_member(self, e, allow_call=True):
+        while True:
+            c = self.cur
+            if c.kind == "p" and c.val == ".":
+                self.i += 1
+                name = self.cur
+                if name.kind not in ("id", "kw"):
+                    raise JSError("SyntaxError", f"bad property name at {name.pos}")
+                self.i += 1
+                e = ("member", e, ("lit", name.val), False, False)
+            elif c.kind == "p" and c.val == "?.":
+                self.i += 1
+                if self.at("("):
+                    e = ("call", e, self.args(), True)
+                elif self.eat("["):
+                    k = self.expression()
+                    self.expect("]")
+                    e = ("member", e, k, True, True)
+                else:
+                    name = self.cur
+                    self.i += 1
+                    e = ("member", e, ("lit", name.val), True, False)
+            elif c.kind == "p" and c.val == "[":
+                self.i += 1
+                k = self.expression()
+                self.expect("]")
+                e = ("member", e, k, False, True)
+            elif c.kind == "p" and c.val == "(" and allow_call:
+                e = ("call", e, self.args(), False)
+            elif c.kind == "tpl":
+                raise JSError("SyntaxError", "tagged templates are not supported")
+            else:
+                return e
+
+    def primary(self):
+        c = self.cur
+        k = c.kind
+        if k == "num" or k == "str":
+            self.i += 1
+            return ("lit", c.val)
+        if k == "tpl":
+            self.i += 1
+            parts = [p if isinstance(p, str) else Parser(p[1]).expression_only() for p in c.val]
+            return ("tpl", parts)
+        if k == "id":
+            self.i += 1
+            return ("ident", c.val)
+        if k == "kw":
+            v = c.val
+            if v == "true" or v == "false":
+                self.i += 1
+                return ("lit", v == "true")
+            if v == "null":
+                self.i += 1
+                return ("lit", None)
+            if v == "undefined":
+                self.i += 1
+                return ("lit", UNDEF)
+            if v == "function":
+                return self.function_expr()
+            if v == "new":
+                self.i += 1
+                if self.at("."):
+                    raise JSError("SyntaxError", "new.target is not supported")
+                callee = self.call_member(self.primary(), allow_call=False)
+                a = self.args() if self.at("(") else []
+                return ("new", callee, a)
+            if v == "this":
+                self.i += 1
+                return ("this",)
+            if v in ("of", "async"):
+                self.i += 1
+                return ("ident", v)
+            if v == "class":
+                raise JSError("SyntaxError", "class expressions are not supported")
+            if v == "import":
+                raise JSError("SyntaxError", "dynamic import is not allowed")
+        if k == "p":
+            v = c.val
+            if v == "(":
+                self.i += 1
+                save = self.no_in
+                self.no_in = False
+                e = self.expression()
+                self.no_in = save
+                self.expect(")")
+                return e
+            if v == "[":
+                self.i += 1
+                items = []
+                while not self.at("]"):
+                    if self.at(","):
+                        self.i += 1
+                        items.append(("lit", UNDEF))
+                        continue
+                    if self.eat("..."):
+                        items.append(("spread", self.assign()))
+                    else:
+                        items.append(self.assign())
+                    if not self.eat(","):
+                        break
+                self.expect("]")
+                return ("array", items)
+            if v == "{":
+                return self.object_lit()
+        raise JSError("SyntaxError", f"unexpected token {c.val!r} at {c.pos}")
+
+    def object_lit(self):
+        self.expect("{")
+        props = []
+        while not self.at("}"):
+            if self.eat("..."):
+                props.append(("spread", self.assign()))
+            else:
+                c = self.cur
+                if c.kind in ("id", "kw") and c.val in ("get", "set") and self.peek().kind in ("id", "kw", "str") \
+                        and self.peek().val not in (",", ":", "("):
+                    raise JSError("SyntaxError", "getters/setters are not supported")
+                if self.eat("["):
+                    key = ("computed", self.assign())
+                    self.expect("]")
+                elif c.kind in ("id", "kw"):
+                    self.i += 1
+                    key = c.val
+                elif c.kind in ("str", "num"):
+                    self.i += 1
+                    key = _prop_key(c.val)
+                else:
+                    raise JSError("SyntaxError", f"bad object key {c.val!r} at {c.pos}")
+                if self.eat(":"):
+                    props.append(("kv", key, self.assign()))
+                elif self.at("("):
+                    ps, rest = self.params()
+                    body = self.block()
+                    props.append(("kv", key, ("func", key if isinstance(key, str) else None, ps, rest, body, False)))
+                elif self.at("="):       # shorthand with default: only valid as a pattern
+                    self.i += 1
+                    props.append(("shorthand_default", key, self.assign()))
+                else:
+                    props.append(("kv", key, ("ident", key)))
+            if not self.eat(","):
+                break
+        self.expect("}")
+        return ("object", props)
+
+    def expression_only(self):
+        e = self.expression()
+        if self.cur.kind != "eof":
+            raise JSError("SyntaxError", "bad template expression")
+        return e
+
+
+def _prop_key(v) -> str:
+    return _to_str(v) if not isinstance(v, str) else v
+
+
+def _to_pattern(node):
+    tag = node[0]
+    if tag == "ident":
+        return ("id", node[1])
+    if tag == "member":
+        return ("memberpat", node)
+    if tag == "array":
+        elems, rest = [], None
+        for it in node[1]:
+            if it[0] == "spread":
+                rest = _to_pattern(it[1])
+            elif it == ("lit", UNDEF):
+                elems.append((None, None))
+            elif it[0] == "assign" and it[1] == "=":
+                elems.append((_to_pattern(it[2]), it[3]))
+            else:
+                elems.append((_to_pattern(it), None))
+        return ("arrpat", elems, rest)
+    if tag == "object":
+        props, rest = [], None
+        for p in node[1]:
+            if p[0] == "spread":
+                rest = p[1][1]
+            elif p[0] == "shorthand_default":
+                props.append((p[1], ("id", p[1]), p[2]))
+            else:
+                val = p[2]
+                if val[0] == "assign" and val[1] == "=":
+                    props.append((p[1], _to_pattern(val[2]), val[3]))
+                else:
+                    props.append((p[1], _to_pattern(val), None))
+        return ("objpat", props, rest)
+    if tag == "assign_pat":
+        return node[1]
+    raise JSError("SyntaxError", "invalid destructuring target")
+
+
+# ---------------------------------------------------------------------------------------------- value model
+
+
+class JSObject:
+    """A plain JS object: ordered own properties."""
+    __slots__ = ("props",)
+    cls_name = "Object"
+
+    def __init__(self, props: Optional[dict] = None):
+        self.props = {} if props is None else props
+
+    def js_get(self, key: str):
+        return self.props.get(key, UNDEF)
+
+    def js_set(self, key: str, value):
+        self.props[key] = value
+
+    def js_keys(self) -> List[str]:
+        return list(self.props.keys())
+
+    def js_has(self, key: str) -> bool:
+        return key in self.props
+
+
+class JSArray:
+    __slots__ = ("items",)
+    cls_name = "Array"
+
+    def __init__(self, items: Optional[list] = None):
+        self.items = [] if items is None else items
+
+
+class JSFunction:
+    __slots__ = ("name", "params", "rest", "body", "env", "arrow", "this", "props")
+
+    def __init__(self, name, params, rest, body, env, arrow, this=UNDEF):
+        self.name, self.params, self.rest, self.body = name, params, rest, body
+        self.env, self.arrow, self.this = env, arrow, this
+        self.props = {}
+
+
+class Native:
+    """A host function: fn(this, args) -> value. `ctor` builds for `new` (and is used when callable as class)."""
+    __slots__ = ("name", "fn", "ctor", "props")
+
+    def __init__(self, name: str, fn: Optional[Callable] = None, ctor: Optional[Callable] = None,
+                 props: Optional[dict] = None):
+        self.name, self.fn, self.ctor = name, fn, ctor
+        self.props = props or {}
+
+
+class Env:
+    __slots__ = ("vars", "parent", "consts")
+
+    def __init__(self, parent: Optional["Env"] = None):
+        self.vars: Dict[str, Any] = {}
+        self.parent = parent
+        self.consts: set = set()
+
+    def lookup(self, name):
+        e = self
+        while e is not None:
+            if name in e.vars:
+                return e
+            e = e.parent
+        return None
+
+    def get(self, name):
+        e = self.lookup(name)
+        if e is None:
+            raise _Throw(_error_obj("ReferenceError", f"{name} is not defined"))
+        v = e.vars[name]
+        if v is _TDZ:
+            raise _Throw(_error_obj("ReferenceError", f"cannot access {name} before initialization"))
+        return v
+
+    def set(self, name, value):
+        e = self.lookup(name)
+        if e is None:
+            raise _Throw(_error_obj("ReferenceError", f"{name} is not defined"))
+        if name in e.consts:
+            raise _Throw(_error_obj("TypeError", f"assignment to constant variable {name}"))
+        e.vars[name] = value
+
+    def declare(self, name, value, const=False):
+        self.vars[name] = value
+        if const:
+            self.consts.add(name)
+
+
+_TDZ = object()
+
+
+def _error_obj(kind, msg):
+    return JSObject({"name": kind, "message": msg})
+
+
+def _num_to_str(v: float) -> str:
+    if v != v:
+        return "NaN"
+    if v in (math.inf, -math.inf):
+        return "Infinity" if v > 0 else "-Infinity"
+    if v == int(v) and abs(v) < 1e21:
+        return str(int(v))
+    r = repr(v)
+    if "e" in r:
+        m, e = r.split("e")
+        e = int(e)
+        return f"{m}e{'+' if e > 0 else '-'}{abs(e)}"
+    return r
+
+
+def _to_str(v) -> str:
+    if isinstance(v, str):
+        return v
+    if isinstance(v, bool):
+        return "true" if v else "false"
+    if isinstance(v, float):
+        return _num_to_str(v)
+    if isinstance(v, int):
+        return str(v)
+    if v is None:
+        return "null"
+    if v is UNDEF:
+        return "undefined"
+    if isinstance(v, JSArray):
+        return ",".join("" if x is None or x is UNDEF else _to_str(x) for x in v.items)
+    if isinstance(v, (JSFunction, Native)):
+        return f"function {getattr(v, 'name', '') or ''}() {{ [code] }}"
+    if isinstance(v, Host):
+        return v.to_string()
+    if isinstance(v, JSObject):
+        return "[object Object]"
+    return str(v)
+
+
+def _to_num(v) -> float:
+    if isinstance(v, bool):
+        return 1.0 if v else 0.0
+    if isinstance(v, (int, float)):
+        return float(v)
+    if v is None:
+        return 0.0
+    if v is UNDEF:
+        return math.nan
+    if isinstance(v, str):
+        s = v.strip()
+        if not s:
+            return 0.0
+        try:
+            if s[:2].lower() == "0x":
+                return float(int(s, 16))
+            return float(s)
+        except ValueError:
+            return math.nan
+    if isinstance(v, JSArray):
+        if not v.items:
+            return 0.0
+        if len(v.items) == 1:
+            return _to_num(v.items[0])
+    return math.nan
+
+
+def _truthy(v) -> bool:
+    if isinstance(v, bool):
+        return v
+    if isinstance(v, float):
+        return v != 0.0 and v == v
+    if isinstance(v, int):
+        return v != 0
+    if isinstance(v, str):
+        return v != ""
+    return not (v is None or v is UNDEF)
+
+
+def _typeof(v) -> str:
+    if v is UNDEF:
+        return "undefined"
+    if isinstance(v, bool):
+        return "boolean"
+    if isinstance(v, (int, float)):
+        return "number"
+    if isinstance(v, str):
+        return "string"
+    if isinstance(v, (JSFunction, Native)):
+        return "function"
+    return "object"
+
+
+def _strict_eq(a, b) -> bool:
+    ta, tb = _typeof(a), _typeof(b)
+    if ta != tb:
+        return False
+    if ta == "number":
+        return float(a) == float(b)
+    if ta in ("string", "boolean", "undefined"):
+        return a == b
+    return a is b
+
+
+def _loose_eq(a, b) -> bool:
+    if (a is None or a is UNDEF) and (b is None or b is UNDEF):
+        return True
+    if a is None or a is UNDEF or b is None or b is UNDEF:
+        return False
+    ta, tb = _typeof(a), _typeof(b)
+    if ta == tb:
+        return _strict_eq(a, b)
+    if ta in ("number", "string", "boolean") and tb in ("number", "string", "boolean"):
+        return _to_num(a) == _to_num(b)
+    return False
+
+
+def _to_int32(v) -> int:
+    x = _to_num(v)
+    if x != x or x in (math.inf, -math.inf):
+        return 0
+    x = int(x) & 0xFFFFFFFF
+    return x - (1 << 32) if x >= (1 << 31) else x
+
+
+def _index(v) -> Optional[int]:
+    if isinstance(v, (int, float)) and not isinstance(v, bool):
+        f = float(v)
+        if f == f and f == int(f) and f >= 0:
+            return int(f)
+    if isinstance(v, str) and v.isdigit():
+        return int(v)
+    return None
+
+
+# ----------------------------------------------------------------------------------------------- interpreter
+
+
+@dataclass
+class Limits:
+    steps: int = 20_000_000
+    seconds: float = 5.0
+    array_len: int = 2_000_000
+    string_len: int = 4_000_000
+
+
+class Interp:
+    def __init__(self, limits: Optional[Limits] = None, seed: int = 0):
+        self.lim = limits or Limits()
+        self.steps = 0
+        self.deadline = time.monotonic() + self.lim.seconds
+        self.rng_state = (seed * 2654435761 + 0x9E3779B9) & 0xFFFFFFFF or 1
+        self.globals = Env()
+        self.exports: Dict[str, Any] = {}
+        _install_globals(self)
+
+    # budget
+    def tick(self):
+        self.steps += 1
+        if self.steps > self.lim.steps:
+            raise JSBudget("RangeError", f"step budget of {self.lim.steps} exceeded")
+        if (self.steps & 0x3FFF) == 0 and time.monotonic() > self.deadline:
+            raise JSBudget("RangeError", f"execution exceeded {self.lim.seconds:.1f}s")
+
+    def random(self) -> float:
+        """xorshift32: deterministic Math.random for reproducible candidates."""
+        x = self.rng_state
+        x ^= (x << 13) & 0xFFFFFFFF
+        x ^= x >> 17
+        x ^= (x << 5) & 0xFFFFFFFF
+        self.rng_state = x & 0xFFFFFFFF
+        return self.rng_state / 4294967296.0
+
+    # statements
+    def run_program(self, prog):
+        env = self.globals
+        self.hoist(prog[1], env)
+        for st in prog[1]:
+            self.exec(st, env)
+
+    def hoist(self, body, env):
+        for st in body:
+            tag = st[0]
+            if tag == "fundecl":
+                env.declare(st[1], self.make_func(st[2], env))
+            elif tag == "export_named" and st[1][0] == "fundecl":
+                env.declare(st[2], self.make_func(st[1][2], env))
+            elif tag == "decl" and st[1] == "var":
+                for target, _ in st[2]:
+                    for nm in _pattern_names(target):
+                        if nm not in env.vars:
+                            env.declare(nm, UNDEF)
+            elif tag == "decl":
+                for target, _ in st[2]:
+                    for nm in _pattern_names(target):
+                        env.vars[nm] = _TDZ
+
+    def make_func(self, node, env, this=UNDEF):
+        _, name, ps, rest, body, arrow = node
+        return JSFunction(name, ps, rest, body, env, arrow, this)
+
+    def exec_block(self, body, env):
+        self.hoist(body, env)
+        for st in body:
+            self.exec(st, env)
+
+    def exec(self, st, env):
+        self.tick()
+        tag = st[0]
+        if tag == "expr":
+            self.eval(st[1], env)
+        elif tag == "decl":
+            kind = st[1]
+            for target, init in st[2]:
+                v = UNDEF if init is None else self.eval(init, env)
+                if kind == "var" and init is None:
+                    continue
+                self.bind(target, v, env, kind)
+        elif tag == "return":
+            raise _Return(UNDEF if st[1] is None else self.eval(st[1], env))
+        elif tag == "if":
+            if _truthy(self.eval(st[1], env)):
+                self.exec(st[2], Env(env) if st[2][0] == "block" else env) if st[2][0] != "block" \
+                    else self.exec_block(st[2][1], Env(env))
+            elif st[3] is not None:
+                if st[3][0] == "block":
+                    self.exec_block(st[3][1], Env(env))
+                else:
+                    self.exec(st[3], env)
+        elif tag == "block":
+            self.exec_block(st[1], Env(env))
+        elif tag == "for":
+            self.exec_for(st, env)
+        elif tag == "forof":
+            self.exec_forof(st, env)
+        elif tag == "forin":
+            _, kind, target, it, body = st
+            obj = self.eval(it, env)
+            keys = _own_keys(obj)
+            for k in keys:
+                self.tick()
+                loop = Env(env)
+                if kind is None:
+                    self.assign_pattern(target, k, env)
+                else:
+                    self.bind(target, k, loop, kind)
+                try:
+                    self.exec_body(body, loop)
+                except _Break:
+                    break
+                except _Continue:
+                    continue
+        elif tag == "while":
+            while _truthy(self.eval(st[1], env)):
+                self.tick()
+                try:
+                    self.exec_body(st[2], Env(env))
+                except _Break:
+                    break
+                except _Continue:
+                    continue
+        elif tag == "dowhile":
+            while True:
+                self.tick()
+                try:
+                    self.exec_body(st[1], Env(env))
+                except _Break:
+                    break
+                except _Continue:
+                    pass
+                if not _truthy(self.eval(st[2], env)):
+                    break
+        elif tag == "break":
+            raise _Break()
+        elif tag == "continue":
+            raise _Continue()
+        elif tag == "fundecl":
+            pass   # hoisted
+        elif tag == "empty":
+            pass
+        elif tag == "throw":
+            raise _Throw(self.eval(st[1], env))
+        elif tag == "try":
+            self.exec_try(st, env)
+        elif tag == "switch":
+            self.exec_switch(st, env)
+        elif tag == "export_default":
+            v = self.eval(st[1], env)
+            self.exports["default"] = v
+        elif tag == "export_named":
+            self.exports[st[2]] = env.get(st[2])
+        elif tag == "export_decl":
+            self.exec(st[1], env)
+            for target, _ in st[1][2]:
+                for nm in _pattern_names(target):
+                    self.exports[nm] = env.get(nm)
+        else:
+            raise JSError("SyntaxError", f"unsupported statement {tag}")
+
+    def exec_body(self, st, env):
+        if st[0] == "block":
+            self.exec_block(st[1], env)
+        else:
+            self.exec(st, env)
+
+    def exec_for(self, st, env):
+        _, init, test, update, body = st
+        loop_env = Env(env)
+        per_iter = init is not None and init[0] == "decl" and init[1] in ("let", "const")
+        if init is not None:
+            if init[0] == "decl":
+                self.hoist([init], loop_env)
+            self.exec(init, loop_env)
+        while True:
+            self.tick()
+            if test is not None and not _truthy(self.eval(test, loop_env)):
+                break
+            it_env = Env(loop_env)
+            if per_iter:   # closures capture a per-iteration copy of let bindings
+                it_env = Env(env)
+                it_env.vars.update(loop_env.vars)
+                it_env.consts = set(loop_env.consts)
+            try:
+                self.exec_body(body, Env(it_env))
+            except _Break:
+                break
+            except _Continue:
+                pass
+            if per_iter:
+                loop_env.vars.update({k: it_env.vars[k] for k in loop_env.vars})
+            if update is not None:
+                self.eval(update, loop_env)
+
+    def exec_forof(self, st, env):
+        _, kind, target, it, body = st
+        seq = self.iterate(self.eval(it, env))
+        for v in seq:
+            self.tick()
+            loop = Env(env)
+            if kind is None:
+                self.assign_pattern(target, v, env)
+            else:
+                self.bind(target, v, loop, kind)
+            try:
+                self.exec_body(body, loop)
+            except _Break:
+                break
+            except _Continue:
+                continue
+
+    def exec_try(self, st, env):
+        _, body, param, handler, fin = st
+        try:
+            self.exec_block(body[1], Env(env))
+        except (_Throw, JSError) as ex:
+            if isinstance(ex, JSBudget) or handler is None:
+                raise
+            val = ex.value if isinstance(ex, _Throw) else _error_obj(ex.kind, ex.msg)
+            henv = Env(env)
+            if param is not None:
+                self.bind(param, val, henv, "let")
+            self.exec_block(handler[1], henv)
+        finally:
+            if fin is not None:
+                self.exec_block(fin[1], Env(env))
+
+    def exec_switch(self, st, env):
+        _, disc, cases = st
+        d = self.eval(disc, env)
+        senv = Env(env)
+        matched = False
+        try:
+            for pass_default in (False, True):
+                for test, body in cases:
+                    if not matched:
+                        if test is None:
+                            if not pass_default:
+                                continue
+                        elif pass_default or not _strict_eq(d, self.eval(test, senv)):
+                            continue
+                        matched = True
+                    for s in body:
+                        self.exec(s, senv)
+                if matched:
+                    break
+        except _Break:
+            pass
+
+    def iterate(self, v) -> list:
+        if isinstance(v, JSArray):
+            return list(v.items)
+        if isinstance(v, str):
+            return list(v)
+        if isinstance(v, Host) and v.iterable() is not None:
+            return v.iterable()
+        raise _Throw(_error_obj("TypeError", f"{_typeof(v)} is not iterable"))
+
+    # binding
+    def bind(self, target, value, env, kind):
+        tag = target[0]
+        if tag == "id":
+            env.declare(target[1], value, const=(kind == "const"))
+        elif tag == "objpat":
+            self.destructure_obj(target, value, lambda p, v: self.bind(p, v, env, kind), env)
+        elif tag == "arrpat":
+            self.destructure_arr(target, value, lambda p, v: self.bind(p, v, env, kind), env)
+        else:
+            raise JSError("SyntaxError", "invalid binding")
+
+    def assign_pattern(self, target, value, env):
+        tag = target[0]
+        if tag == "id":
+            env.set(target[1], value)
+        elif tag == "memberpat":
+            m = target[1]
+            self.put(self.eval(m[1], env), self.member_key(m, env), value)
+        elif tag == "objpat":
+            self.destructure_obj(target, value, lambda p, v: self.assign_pattern(p, v, env), env)
+        elif tag == "arrpat":
+            self.destructure_arr(target, value, lambda p, v: self.assign_pattern(p, v, env), env)
+
+    def destructure_obj(self, target, value, put, env):
+        if value is None or value is UNDEF:
+            raise _Throw(_error_obj("TypeError", "cannot destructure undefined"))
+        used = []
+        for key, pat, default in target[1]:
+            k = _to_str(self.eval(key[1], env)) if isinstance(key, tuple) else key
+            used.append(k)
+            v = self.get(value, k)
+            if v is UNDEF and default is not None:
+                v = self.eval(default, env)
+            put(pat, v)
+        if target[2] is not None:
+            rest = JSObject({k: self.get(value, k) for k in _own_keys(value) if k not in used})
+            put(("id", target[2]), rest)
+
+    def destructure_arr(self, target, value, put, env):
+        items = self.iterate(value)
+        for i, (pat, default) in enumerate(target[1]):
+            if pat is None:
+                continue
+            v = items[i] if i < len(items) else UNDEF
+            if v is UNDEF and default is not None:
+                v = self.eval(default, env)
+            put(pat, v)
+        if target[2] is not None:
+            put(target[2], JSArray(items[len(target[1]):]))
+
+    # calls
+    def call(self, f, this, args):
+        self.tick()
+        if isinstance(f, JSFunction):
+            env = Env(f.env)
+            if not f.arrow:
+                env.declare("this", this if this is not UNDEF else f.this)
+                env.declare("arguments", JSArray(list(args)))
+            for i, (pat, default) in enumerate(f.params):
+                v = args[i] if i < len(args) else UNDEF
+                if v is UNDEF and default is not None:
+                    v = self.eval(default, env)
+                self.bind(pat, v, env, "let")
+            if f.rest is not None:
+                self.bind(f.rest, JSArray(list(args[len(f.params):])), env, "let")
+            try:
+                self.exec_block(f.body[1], env)
+            except _Return as r:
+                return r.value
+            return UNDEF
+        if isinstance(f, Native):
+            if f.fn is None:
+                raise _Throw(_error_obj("TypeError", f"class constructor {f.name} cannot be invoked without 'new'"))
+            return f.fn(self, this, list(args))
+        raise _Throw(_error_obj("TypeError", f"{_to_str(f)[:40]} is not a function"))
+
+    def construct(self, f, args):
+        self.tick()
+        if isinstance(f, Native) and f.ctor is not None:
+            return f.ctor(self, list(args))
+        if isinstance(f, JSFunction) and not f.arrow:
+            obj = JSObject()
+            env_this = obj
+            r = self.call(f, env_this, args)
+            return r if isinstance(r, (JSObject, JSArray, Host)) else obj
+        raise _Throw(_error_obj("TypeError", f"{getattr(f, 'name', _typeof(f))} is not a constructor"))
+
+    # property access
+    def get(self, obj, key):
+        if isinstance(obj, JSArray):
+            idx = _index(key)
+            if idx is not None:
+                return obj.items[idx] if idx < len(obj.items) else UNDEF
+            return _array_method(self, obj, _to_str(key))
+        if isinstance(obj, Host):
+            return obj.js_get(self, _to_str(key))
+        if isinstance(obj, JSObject):
+            k = _to_str(key)
+            v = obj.props.get(k, UNDEF)
+            if v is UNDEF and k in _OBJECT_PROTO:
+                return _OBJECT_PROTO[k](self, obj)
+            return v
+        if isinstance(obj, str):
+            idx = _index(key)
+            if idx is not None:
+                return obj[idx] if idx < len(obj) else UNDEF
+            return _string_method(self, obj, _to_str(key))
+        if isinstance(obj, (int, float)) and not isinstance(obj, bool):
+            return _number_method(self, float(obj), _to_str(key))
+        if isinstance(obj, (JSFunction, Native)):
+            k = _to_str(key)
+            if k in obj.props:
+                return obj.props[k]
+            if k == "name":
+                return obj.name or ""
+            if k in ("call", "apply", "bind"):
+                return _function_method(self, obj, k)
+            return UNDEF
+        if obj is None or obj is UNDEF:
+            raise _Throw(_error_obj("TypeError", f"cannot read properties of {_to_str(obj)} (reading '{_to_str(key)}')"))
+        return UNDEF
+
+    def put(self, obj, key, value):
+        if isinstance(obj, JSArray):
+            idx = _index(key)
+            if idx is not None:
+                if idx >= self.lim.array_len:
+                    raise JSBudget("RangeError", "array too large")
+                if idx >= len(obj.items):
+                    obj.items.extend([UNDEF] * (idx + 1 - len(obj.items)))
+                obj.items[idx] = value
+                return
+            if _to_str(key) == "length":
+                n = int(_to_num(value))
+                if n > self.lim.array_len:
+                    raise JSBudget("RangeError", "array too large")
+                del obj.items[n:]
+                obj.items.extend([UNDEF] * (n - len(obj.items)))
+                return
+            raise _Throw(_error_obj("TypeError", f"cannot set property {_to_str(key)} of an array"))
+        if isinstance(obj, Host):
+            obj.js_set(self, _to_str(key), value)
+            return
+        if isinstance(obj, JSObject):
+            obj.props[_to_str(key)] = value
+            return
+        if isinstance(obj, (JSFunction, Native)):
+            obj.props[_to_str(key)] = value
+            return
+        if obj is None or obj is UNDEF:
+            raise _Throw(_error_obj("TypeError", f"cannot set properties of {_to_str(obj)}"))
+        # primitives: silently ignored (sloppy mode)
+
+    def member_key(self, node, env):
+        k = node[2]
+        return k[1] if k[0] == "lit" else self.eval(k, env)
+
+    # expressions
+    def eval(self, e, env):
+        tag = e[0]
+        if tag == "lit":
+            return e[1]
+        if tag == "ident":
+            return env.get(e[1])
+        if tag == "member":
+            obj = self.eval(e[1], env)
+            if e[3] and (obj is None or obj is UNDEF):
+                return UNDEF
+            return self.get(obj, self.member_key(e, env))
+        if tag == "call":
+            callee = e[1]
+            if callee[0] == "member":
+                this = self.eval(callee[1], env)
+                if callee[3] and (this is None or this is UNDEF):
+                    return UNDEF
+                f = self.get(this, self.member_key(callee, env))
+            else:
+                this = UNDEF
+                f = self.eval(callee, env)
+            if e[3] and (f is None or f is UNDEF):
+                return UNDEF
+            if f is UNDEF or f is None:
+                name = callee[2][1] if callee[0] == "member" and callee[2][0] == "lit" else \
+                    (callee[1] if callee[0] == "ident" else "expression")
+                raise _Throw(_error_obj("TypeError", f"{name} is not a function"))
+            return self.call(f, this, self.eval_args(e[2], env))
+        if tag == "bin":
+            return self.binop(e[1], self.eval(e[2], env), self.eval(e[3], env))
+        if tag == "logic":
+            a = self.eval(e[2], env)
+            op = e[1]
+            if op == "&&":
+                return self.eval(e[3], env) if _truthy(a) else a
+            if op == "||":
+                return a if _truthy(a) else self.eval(e[3], env)
+            return self.eval(e[3], env) if (a is None or a is UNDEF) else a
+        if tag == "assign":
+            return self.assign(e, env)
+        if tag == "assign_pat":
+            v = self.eval(e[2], env)
+            self.assign_pattern(e[1], v, env)
+            return v
+        if tag == "unary":
+            op = e[1]
+            if op == "typeof":
+                if e[2][0] == "ident" and env.lookup(e[2][1]) is None:
+                    return "undefined"
+                return _typeof(self.eval(e[2], env))
+            if op == "delete":
+                t = e[2]
+                if t[0] == "member":
+                    obj = self.eval(t[1], env)
+                    if isinstance(obj, JSObject) and not isinstance(obj, Host):
+                        obj.props.pop(_to_str(self.member_key(t, env)), None)
+                return True
+            v = self.eval(e[2], env)
+            if op == "!":
+                return not _truthy(v)
+            if op == "-":
+                return -_to_num(v)
+            if op == "+":
+                return _to_num(v)
+            if op == "~":
+                return float(~_to_int32(v))
+            if op == "void":
+                return UNDEF
+        if tag == "update":
+            _, op, prefix, target = e
+            old = _to_num(self.eval(target, env))
+            new = old + (1.0 if op == "++" else -1.0)
+            self.store(target, new, env)
+            return new if prefix else old
+        if tag == "cond":
+            return self.eval(e[2], env) if _truthy(self.eval(e[1], env)) else self.eval(e[3], env)
+        if tag == "array":
+            out = []
+            for it in e[1]:
+                if it[0] == "spread":
+                    out.extend(self.iterate(self.eval(it[1], env)))
+                else:
+                    out.append(self.eval(it, env))
+            if len(out) > self.lim.array_len:
+                raise JSBudget("RangeError", "array too large")
+            return JSArray(out)
+        if tag == "object":
+            obj = JSObject()
+            for p in e[1]:
+                if p[0] == "spread":
+                    src = self.eval(p[1], env)
+                    for k in _own_keys(src):
+                        obj.props[k] = self.get(src, k)
+                elif p[0] == "shorthand_default":
+                    raise JSError("SyntaxError", "invalid shorthand property initializer")
+                else:
+                    key = p[1]
+                    k = _to_str(self.eval(key[1], env)) if isinstance(key, tuple) else key
+                    v = self.eval(p[2], env)
+                    if isinstance(v, JSFunction) and not v.arrow:
+                        v.this = obj
+                    obj.props[k] = v
+            return obj
+        if tag == "func":
+            return self.make_func(e, env)
+        if tag == "new":
+            return self.construct(self.eval(e[1], env), self.eval_args(e[2], env))
+        if tag == "tpl":
+            s = "".join(p if isinstance(p, str) else _to_str(self.eval(p, env)) for p in e[1])
+            if len(s) > self.lim.string_len:
+                raise JSBudget("RangeError", "string too large")
+            return s
+        if tag == "seq":
+            v = UNDEF
+            for x in e[1]:
+                v = self.eval(x, env)
+            return v
+        if tag == "this":
+            ev = env.lookup("this")
+            return ev.vars["this"] if ev is not None else UNDEF
+        if tag == "spread":
+            raise JSError("SyntaxError", "unexpected spread")
+        raise JSError("SyntaxError", f"unsupported expression {tag}")
+
+    def eval_args(self, args, env):
+        out = []
+        for a in args:
+            if a[0] == "spread":
+                out.extend(self.iterate(self.eval(a[1], env)))
+            else:
+                out.append(self.eval(a, env))
+        return out
+
+    def store(self, target, value, env):
+        if target[0] == "ident":
+            env.set(target[1], value)
+        elif target[0] == "member":
+            self.put(self.eval(target[1], env), self.member_key(target, env), value)
+        else:
+            raise JSError("SyntaxError", "invalid assignment target")
+
+    def assign(self, e, env):
+        _, op, target, rhs = e
+        if op == "=":
+            v = self.eval(rhs, env)
+            if isinstance(v, JSFunction) and v.name is None and target[0] == "ident":
+                v.name = target[1]
+            self.store(target, v, env)
+            return v
+        if target[0] == "member":
+            obj = self.eval(target[1], env)
+            key = self.member_key(target, env)
+            cur = self.get(obj, key)
+        else:
+            obj = key = None
+            cur = env.get(target[1])
+        if op in ("&&=", "||=", "??="):
+            keep = {"&&=": not _truthy(cur), "||=": _truthy(cur), "??=": not (cur is None or cur is UNDEF)}[op]
+            if keep:
+                return cur
+            v = self.eval(rhs, env)
+        else:
+            v = self.binop(op[:-1], cur, self.eval(rhs, env))
+        if target[0] == "member":
+            self.put(obj, key, v)
+        else:
+            env.set(target[1], v)
+        return v
+
+    def binop(self, op, a, b):
+        if op == "+":
+            if isinstance(a, str) or isinstance(b, str) or _is_objlike(a) or _is_objlike(b):
+                s = _to_str(a) + _to_str(b)
+                if len(s) > self.lim.string_len:
+                    raise JSBudget("RangeError", "string too large")
+                return s
+            return _to_num(a) + _to_num(b)
+        if op == "-":
+            return _to_num(a) - _to_num(b)
+        if op == "*":
+            return _to_num(a) * _to_num(b)
+        if op == "/":
+            x, y = _to_num(a), _to_num(b)
+            if y == 0:
+                if x == 0 or x != x:
+                    return math.nan
+                return math.copysign(math.inf, x) * math.copysign(1.0, y)
+            return x / y
+        if op == "%":
+            x, y = _to_num(a), _to_num(b)
+            if y == 0 or x != x or y != y or x in (math.inf, -math.inf):
+                return math.nan
+            return math.fmod(x, y)
+        if op == "**":
+            x, y = _to_num(a), _to_num(b)
+            try:
+                r = x ** y
+                return r if isinstance(r, float) else math.nan
+            except (OverflowError, ZeroDivisionError):
+                return math.inf
+        if op in ("===", "!=="):
+            r = _strict_eq(a, b)
+            return r if op == "===" else not r
+        if op in ("==", "!="):
+            r = _loose_eq(a, b)
+            return r if op == "==" else not r
+        if op in ("<", ">", "<=", ">="):
+            if isinstance(a, str) and isinstance(b, str):
+                x, y = a, b
+            else:
+                x, y = _to_num(a), _to_num(b)
+                if x != x or y != y:
+                    return False
+            return {"<": x < y, ">": x > y, "<=": x <= y, ">=": x >= y}[op]
+        if op == "&":
+            return float(_to_int32(a) & _to_int32(b))
+        if op == "|":
+            return float(_to_int32(a) | _to_int32(b))
+        if op == "^":
+            return float(_to_int32(a) ^ _to_int32(b))
+        if op == "<<":
+            return float(_to_int32(_to_int32(a) << (_to_int32(b) & 31)))
+        if op == ">>":
+            return float(_to_int32(a) >> (_to_int32(b) & 31))
+        if op == ">>>":
+            return float((_to_int32(a) & 0xFFFFFFFF) >> (_to_int32(b) & 31))
+        if op == "instanceof":
+            if isinstance(b, Native) and isinstance(a, Host):
+                return a.is_instance(b.name)
+            if isinstance(b, Native) and b.name == "Array":
+                return isinstance(a, JSArray)
+            if isinstance(b, Native) and b.name == "Object":
+                return isinstance(a, (JSObject, JSArray, Host))
+            return False
+        if op == "in":
+            k = _to_str(a)
+            if isinstance(b, JSArray):
+                i = _index(a)
+                return i is not None and i < len(b.items)
+            if isinstance(b, Host):
+                return b.js_get(self, k) is not UNDEF
+            if isinstance(b, JSObject):
+                return k in b.props
+            raise _Throw(_error_obj("TypeError", "cannot use 'in' on a primitive"))
+        raise JSError("SyntaxError", f"unsupported operator {op}")
+
+
+def _is_objlike(v):
+    return isinstance(v, (JSObject, JSArray)) and not isinstance(v, Host) or isinstance(v, JSArray)
+
+
+def _pattern_names(p) -> List[str]:
+    tag = p[0]
+    if tag == "id":
+        return [p[1]]
+    out = []
+    if tag == "objpat":
+        for _, t, _ in p[1]:
+            out += _pattern_names(t)
+        if p[2] is not None:
+            out.append(p[2])
+    elif tag == "arrpat":
+        for t, _ in p[1]:
+            if t is not None:
+                out += _pattern_names(t)
+        if p[2] is not None:
+            out += _pattern_names(p[2])
+    return out
+
+
+def _own_keys(v) -> List[str]:
+    if isinstance(v, JSArray):
+        return [str(i) for i in range(len(v.items))]
+    if isinstance(v, Host):
+        return v.own_keys()
+    if isinstance(v, JSObject):
+        return list(v.props.keys())
+    if isinstance(v, str):
+        return [str(i) for i in range(len(v))]
+    return []
+
+
+# -------------------------------------------------------------------------------------------- builtin library
+
+
+def _nat(name, fn):
+    return Native(name, fn=fn)
+
+
+def _arg(args, i, default=UNDEF):
+    return args[i] if i < len(args) else default
+
+
+def _num_arg(args, i, default=0.0):
+    v = _arg(args, i)
+    return default if v is UNDEF else _to_num(v)
+
+
+def _array_method(it: Interp, arr: JSArray, name: str):
+    a = arr.items
+    if name == "length":
+        return float(len(a))
+
+    def cb(f, *xs):
+        return it.call(f, UNDEF, list(xs))
+
+    m: Dict[str, Callable] = {
+        "push": lambda i, t, x: (a.extend(x), _check_len(it, a), float(len(a)))[-1],
+        "pop": lambda i, t, x: a.pop() if a else UNDEF,
+        "shift": lambda i, t, x: a.pop(0) if a else UNDEF,
+        "unshift": lambda i, t, x: (a.__setitem__(slice(0, 0), x), float(len(a)))[-1],
+        "map": lambda i, t, x: JSArray([cb(x[0], v, float(k), arr) for k, v in enumerate(list(a))]),
+        "forEach": lambda i, t, x: ([cb(x[0], v, float(k), arr) for k, v in enumerate(list(a))], UNDEF)[-1],
+        "filter": lambda i, t, x: JSArray([v for k, v in enumerate(list(a)) if _truthy(cb(x[0], v, float(k), arr))]),
+        "some": lambda i, t, x: any(_truthy(cb(x[0], v, float(k), arr)) for k, v in enumerate(list(a))),
+        "every": lambda i, t, x: all(_truthy(cb(x[0], v, float(k), arr)) for k, v in enumerate(list(a))),
+        "find": lambda i, t, x: next((v for k, v in enumerate(list(a)) if _truthy(cb(x[0], v, float(k), arr))), UNDEF),
+        "findIndex": lambda i, t, x: float(next((k for k, v in enumerate(list(a)) if _truthy(cb(x[0], v, float(k), arr))), -1)),
+        "indexOf": lambda i, t, x: float(next((k for k, v in enumerate(a) if _strict_eq(v, _arg(x, 0))), -1)),
+        "includes": lambda i, t, x: any(_strict_eq(v, _arg(x, 0)) or (_num_nan(v) and _num_nan(_arg(x, 0))) for v in a),
+        "join": lambda i, t, x: (_to_str(x[0]) if x and x[0] is not UNDEF else ",").join(
+            "" if v is None or v is UNDEF else _to_str(v) for v in a),
+        "slice": lambda i, t, x: JSArray(a[_slice_idx(x, 0, len(a), 0):_slice_idx(x, 1, len(a), len(a))]),
+        "concat": lambda i, t, x: JSArray(a + [w for y in x for w in (y.items if isinstance(y, JSArray) else [y])]),
+        "reverse": lambda i, t, x: (a.reverse(), arr)[-1],
+        "fill": lambda i, t, x: (_fill(a, x), arr)[-1],
+        "reduce": lambda i, t, x: _reduce(it, arr, x),
+        "sort": lambda i, t, x: (_sort(it, a, x), arr)[-1],
+        "splice": lambda i, t, x: _splice(a, x),
+        "flat": lambda i, t, x: JSArray([w for v in a for w in (v.items if isinstance(v, JSArray) else [v])]),
+        "flatMap": lambda i, t, x: JSArray([w for k, v in enumerate(list(a))
+                                            for r in [cb(x[0], v, float(k), arr)]
+                                            for w in (r.items if isinstance(r, JSArray) else [r])]),
+        "keys": lambda i, t, x: JSArray([float(k) for k in range(len(a))]),
+        "values": lambda i, t, x: JSArray(list(a)),
+        "entries": lambda i, t, x: JSArray([JSArray([float(k), v]) for k, v in enumerate(a)]),
+        "at": lambda i, t, x: (a[int(_num_arg(x, 0))] if -len(a) <= int(_num_arg(x, 0)) < len(a) else UNDEF),
+        "toString": lambda i, t, x: _to_str(arr),
+    }
+    f = m.get(name)
+    return _nat(name, f) if f is not None else UNDEF
+
+
+def _num_nan(v):
+    return isinstance(v, float) and v != v
+
+
+def _check_len(it, a):
+    if len(a) > it.lim.array_len:
+        raise JSBudget("RangeError", "array too large")
+
+
+def _slice_idx(x, i, n, default):
+    v = _arg(x, i)
+    if v is UNDEF:
+        return default
+    k = int(_to_num(v)) if _to_num(v) == _to_num(v) else 0
+    return max(0, n + k) if k < 0 else min(k, n)
+
+
+def _fill(a, x):
+    n = len(a)
+    lo, hi = _slice_idx(x, 1, n, 0), _slice_idx(x, 2, n, n)
+    for k in range(lo, hi):
+        a[k] = _arg(x, 0)
+
+
+def _reduce(it, arr, x):
+    a = list(arr.items)
+    k = 0
+    if len(x) > 1:
+        acc = x[1]
+    else:
+        if not a:
+            raise _Throw(_error_obj("TypeError", "reduce of empty array with no initial value"))
+        acc, k = a[0], 1
+    for j in range(k, len(a)):
+        acc = it.call(x[0], UNDEF, [acc, a[j], float(j), arr])
+    return acc
+
+
+def _sort(it, a, x):
+    import functools
+    f = _arg(x, 0)
+    if f is UNDEF:
+        a.sort(key=_to_str)
+    else:
+        a.sort(key=functools.cmp_to_key(lambda p, q: (lambda r: -1 if r < 0 else (1 if r > 0 else 0))(
+            _to_num(it.call(f, UNDEF, [p, q])))))
+
+
+def _splice(a, x):
+    n = len(a)
+    start = _slice_idx(x, 0, n, 0)
+    cnt = n - start if len(x) < 2 else max(0, min(int(_to_num(x[1])), n - start))
+    removed = a[start:start + cnt]
+    a[start:start + cnt] = x[2:]
+    return JSArray(removed)
+
+
+def _string_method(it, s: str, name: str):
+    if name == "length":
+        return float(len(s))
+    m = {
+        "toUpperCase": lambda i, t, x: s.upper(),
+        "toLowerCase": lambda i, t, x: s.lower(),
+        "trim": lambda i, t, x: s.strip(),
+        "slice": lambda i, t, x: s[_slice_idx(x, 0, len(s), 0):_slice_idx(x, 1, len(s), len(s))],
+        "substring": lambda i, t, x: s[max(0, int(_num_arg(x, 0))):(len(s) if len(x) < 2 else max(0, int(_num_arg(x, 1))))],
+        "charAt": lambda i, t, x: s[int(_num_arg(x, 0))] if 0 <= int(_num_arg(x, 0)) < len(s) else "",
+        "charCodeAt": lambda i, t, x: float(ord(s[int(_num_arg(x, 0))])) if 0 <= int(_num_arg(x, 0)) < len(s) else math.nan,
+        "indexOf": lambda i, t, x: float(s.find(_to_str(_arg(x, 0)))),
+        "includes": lambda i, t, x: _to_str(_arg(x, 0)) in s,
+        "startsWith": lambda i, t, x: s.startswith(_to_str(_arg(x, 0))),
+        "endsWith": lambda i, t, x: s.endswith(_to_str(_arg(x, 0))),
+        "split": lambda i, t, x: JSArray(list(s) if _to_str(_arg(x, 0, "")) == "" else s.split(_to_str(x[0]))),
+        "repeat": lambda i, t, x: _repeat(it, s, int(_num_arg(x, 0))),
+        "padStart": lambda i, t, x: s.rjust(int(_num_arg(x, 0)), (_to_str(_arg(x, 1, " ")) or " ")[0]),
+        "padEnd": lambda i, t, x: s.ljust(int(_num_arg(x, 0)), (_to_str(_arg(x, 1, " ")) or " ")[0]),
+        "replace": lambda i, t, x: s.replace(_to_str(_arg(x, 0)), _to_str(_arg(x, 1)), 1),
+        "replaceAll": lambda i, t, x: s.replace(_to_str(_arg(x, 0)), _to_str(_arg(x, 1))),
+        "toString": lambda i, t, x: s,
+    }
+    f = m.get(name)
+    return _nat(name, f) if f is not None else UNDEF
+
+
+def _repeat(it, s, n):
+    if n < 0 or len(s) * n > it.lim.string_len:
+        raise JSBudget("RangeError", "invalid repeat count")
+    return s * n
+
+
+def _number_method(it, v: float, name: str):
+    if name == "toFixed":
+        return _nat(name, lambda i, t, x: f"{v:.{int(_num_arg(x, 0))}f}")
+    if name == "toString":
+        return _nat(name, lambda i, t, x: _num_to_str(v))
+    if name == "toPrecision":
+        return _nat(name, lambda i, t, x: f"{v:.{int(_num_arg(x, 0))}g}")
+    return UNDEF
+
+
+def _function_method(it, f, name):
+    if name == "call":
+        return _nat(name, lambda i, t, x: it.call(f, _arg(x, 0), x[1:]))
+    if name == "apply":
+        return _nat(name, lambda i, t, x: it.call(f, _arg(x, 0), it.iterate(_arg(x, 1)) if len(x) > 1 and x[1] is not UNDEF else []))
+    return _nat(name, lambda i, t, x: _nat("bound", lambda i2, t2, y: it.call(f, _arg(x, 0), x[1:] + y)))
+
+
+_OBJECT_PROTO = {
+    "hasOwnProperty": lambda it, o: _nat("hasOwnProperty", lambda i, t, x: _to_str(_arg(x, 0)) in o.props),
+    "toString": lambda it, o: _nat("toString", lambda i, t, x: "[object Object]"),
+}
+
+
+def _install_globals(it: Interp):
+    g = it.globals
+    rnd = it.random
+
+    def mfn(f):
+        return lambda i, t, x: f(*[_to_num(v) for v in x])
+
+    def safe(f):
+        def w(*a):
+            try:
+                return float(f(*a))
+            except (ValueError, OverflowError, ZeroDivisionError):
+                return math.nan
+        return w
+
+    math_props = {
+        "PI": math.pi, "E": math.e, "SQRT2": math.sqrt(2), "LN2": math.log(2), "LN10": math.log(10),
+        "SQRT1_2": math.sqrt(0.5), "LOG2E": 1 / math.log(2), "LOG10E": 1 / math.log(10),
+    }
+    for nm, f in {"sin": math.sin, "cos": math.cos, "tan": math.tan, "asin": math.asin, "acos": math.acos,
+                  "atan": math.atan, "sqrt": math.sqrt, "exp": math.exp, "log": math.log, "log2": math.log2,
+                  "log10": math.log10, "cbrt": lambda v: math.copysign(abs(v) ** (1 / 3), v), "sinh": math.sinh,
+                  "cosh": math.cosh, "tanh": math.tanh, "abs": abs, "atan2": math.atan2,
+                  "floor": lambda v: float(math.floor(v)) if math.isfinite(v) else v,
+                  "ceil": lambda v: float(math.ceil(v)) if math.isfinite(v) else v,
+                  "round": lambda v: float(math.floor(v + 0.5)) if math.isfinite(v) else v,
+                  "trunc": lambda v: float(math.trunc(v)) if math.isfinite(v) else v,
+                  "sign": lambda v: v if v != v else float((v > 0) - (v < 0)),
+                  "pow": lambda a, b: a ** b, "hypot": lambda *v: math.hypot(*v),
+                  "fround": lambda v: struct.unpack("f", struct.pack("f", v))[0]}.items():
+        math_props[nm] = _nat(nm, mfn(safe(f)))
+    math_props["min"] = _nat("min", lambda i, t, x: min([_to_num(v) for v in x], default=math.inf))
+    math_props["max"] = _nat("max", lambda i, t, x: max([_to_num(v) for v in x], default=-math.inf))
+    math_props["random"] = _nat("random", lambda i, t, x: rnd())
+    g.declare("Math", JSObject(math_props))
+    g.declare("NaN", math.nan)
+    g.declare("Infinity", math.inf)
+    g.declare("undefined", UNDEF)
+    g.declare("parseFloat", _nat("parseFloat", lambda i, t, x: _parse_float(_to_str(_arg(x, 0)))))
+    g.declare("parseInt", _nat("parseInt", lambda i, t, x: _parse_int(_to_str(_arg(x, 0)), _arg(x, 1))))
+    g.declare("isNaN", _nat("isNaN", lambda i, t, x: _to_num(_arg(x, 0)) != _to_num(_arg(x, 0))))
+    g.declare("isFinite", _nat("isFinite", lambda i, t, x: math.isfinite(_to_num(_arg(x, 0)))))
+    g.declare("Number", Native("Number", fn=lambda i, t, x: _to_num(_arg(x, 0, 0.0)), props={
+        "isFinite": _nat("isFinite", lambda i, t, x: isinstance(_arg(x, 0), float) and math.isfinite(x[0])),
+        "isInteger": _nat("isInteger", lambda i, t, x: isinstance(_arg(x, 0), float) and math.isfinite(x[0]) and x[0] == int(x[0])),
+        "EPSILON": 2.0 ** -52, "MAX_SAFE_INTEGER": 2.0 ** 53 - 1, "MAX_VALUE": 1.7976931348623157e308,
+        "POSITIVE_INFINITY": math.inf, "NEGATIVE_INFINITY": -math.inf, "NaN": math.nan,
+        "parseFloat": _nat("parseFloat", lambda i, t, x: _parse_float(_to_str(_arg(x, 0))))}))
+    g.declare("String", Native("String", fn=lambda i, t, x: _to_str(_arg(x, 0, ""))))
+    g.declare("Boolean", Native("Boolean", fn=lambda i, t, x: _truthy(_arg(x, 0, False))))
+
+    def array_ctor(i, x):
+        if len(x) == 1 and isinstance(x[0], float):
+            n = int(x[0])
+            if n > it.lim.array_len or n < 0:
+                raise JSBudget("RangeError", "invalid array length")
+            return JSArray([UNDEF] * n)
+        return JSArray(list(x))
+
+    def array_from(i, t, x):
+        src = _arg(x, 0)
+        f = _arg(x, 1)
+        if isinstance(src, (JSArray, str)) or isinstance(src, Host):
+            items = it.iterate(src)
+        else:
+            n = int(_to_num(it.get(src, "length"))) if isinstance(src, JSObject) else 0
+            if n > it.lim.array_len or n < 0:
+                raise JSBudget("RangeError", "invalid array length")
+            items = [it.get(src, float(k)) for k in range(n)]
+        if f is not UNDEF:
+            items = [it.call(f, UNDEF, [v, float(k)]) for k, v in enumerate(items)]
+        return JSArray(items)
+
+    g.declare("Array", Native("Array", fn=lambda i, t, x: array_ctor(i, x), ctor=array_ctor, props={
+        "isArray": _nat("isArray", lambda i, t, x: isinstance(_arg(x, 0), JSArray)),
+        "from": _nat("from", array_from),
+        "of": _nat("of", lambda i, t, x: JSArray(list(x)))}))
+    g.declare("Object", Native("Object", fn=lambda i, t, x: JSObject(), ctor=lambda i, x: JSObject(), props={
+        "keys": _nat("keys", lambda i, t, x: JSArray(_own_keys(_arg(x, 0)))),
+        "values": _nat("values", lambda i, t, x: JSArray([it.get(x[0], k) for k in _own_keys(x[0])])),
+        "entries": _nat("entries", lambda i, t, x: JSArray([JSArray([k, it.get(x[0], k)]) for k in _own_keys(x[0])])),
+        "assign": _nat("assign", lambda i, t, x: _assign(it, x)),
+        "freeze": _nat("freeze", lambda i, t, x: _arg(x, 0)),
+        "fromEntries": _nat("fromEntries", lambda i, t, x: JSObject({_to_str(it.get(p, 0.0)): it.get(p, 1.0)
+                                                                       for p in it.iterate(_arg(x, 0))}))}))
+    g.declare("console", JSObject({k: _nat(k, lambda i, t, x: UNDEF) for k in ("log", "warn", "error", "info", "debug")}))
+    g.declare("Error", Native("Error", fn=lambda i, t, x: _error_obj("Error", _to_str(_arg(x, 0, ""))),
+                              ctor=lambda i, x: _error_obj("Error", _to_str(_arg(x, 0, "")))))
+    for cls in ("Float32Array", "Uint16Array", "Uint32Array", "Int32Array", "Uint8Array", "Float64Array", "Int16Array",
+                "Uint8ClampedArray", "Int8Array"):
+        g.declare(cls, _typed_array_ctor(it, cls))
+
+
+def _typed_array_ctor(it, cls):
+    def ctor(i, x):
+        src = _arg(x, 0, 0.0)
+        if isinstance(src, float):
+            n = int(src)
+            if n < 0 or n > it.lim.array_len:
+                raise JSBudget("RangeError", "invalid typed array length")
+            return JSArray([0.0] * n)
+        return JSArray([_to_num(v) for v in it.iterate(src)])
+    return Native(cls, ctor=ctor, props={"from": _nat("from", lambda i, t, x: ctor(i, [x[0]]))})
+
+
+def _assign(it, x):
+    tgt = _arg(x, 0)
+    for src in x[1:]:
+        if src is None or src is UNDEF:
+            continue
+        for k in _own_keys(src):
+            it.put(tgt, k, it.get(src, k))
+    return tgt
+
+
+def _parse_float(s: str) -> float:
+    m = re.match(r"\s*[+-]?(\d+\.?\d*(e[+-]?\d+)?|\.\d+(e[+-]?\d+)?|Infinity)", s, re.I)
+    if not m:
+        return math.nan
+    return float(m.group(0))
+
+
+def _parse_int(s: str, radix) -> float:
+    s = s.strip()
+    r = 10 if radix is UNDEF else int(_to_num(radix))
+    sign = -1 if s.startswith("-") else 1
+    s = s.lstrip("+-")
+    if (r in (0, 16) or radix is UNDEF) and s[:2].lower() == "0x":
+        s, r = s[2:], 16
+    r = r or 10
+    digits = "0123456789abcdefghijklmnopqrstuvwxyz"[:r]
+    out = ""
+    for ch in s.lower():
+        if ch not in digits:
+            break
+        out += ch
+    return float(sign * int(out, r)) if out else math.nan
+
+
+# --------------------------------------------------------------------------------------------- three.js model
+
+
+class Host(JSObject):
+    """A native object. Subclasses list readable/writable properties; everything else is an expando dict."""
+    __slots__ = ()
+    cls_name = "Host"
+    bases: Tuple[str, ...] = ()
+
+    def js_get(self, it, key):
+        v = self.props.get(key, UNDEF)
+        if v is not UNDEF:
+            return v
+        m = getattr(type(self), "js_methods", {}).get(key)
+        if m is not None:
+            return _nat(key, lambda i, t, x, _m=m, _s=self: _m(_s, i, x))
+        return self.get_special(it, key)
+
+    def get_special(self, it, key):
+        if key == "type":
+            return self.cls_name
+        if key == "isObject3D":
+            return isinstance(self, Object3D) or UNDEF
+        return UNDEF
+
+    def js_set(self, it, key, value):
+        if self.set_special(it, key, value):
+            return
+        self.props[key] = value
+
+    def set_special(self, it, key, value) -> bool:
+        return False
+
+    def own_keys(self):
+        return list(self.props.keys())
+
+    def iterable(self):
+        return None
+
+    def is_instance(self, name):
+        return name == self.cls_name or name in self.bases
+
+    def to_string(self):
+        return f"[object {self.cls_name}]"
+
+
+class Vec(Host):
+    """Vector2 / Vector3 / Euler: numeric components held in props."""
+    __slots__ = ("comps", "kind")
+
+    def __init__(self, comps=("x", "y", "z"), vals=None, cls_name="Vector3"):
+        super().__init__({c: float(v) for c, v in zip(comps, vals or [0.0] * len(comps))})
+        self.comps = comps
+        self.kind = cls_name
+        self.props["is" + cls_name] = True
+        if cls_name == "Euler":
+            self.props["order"] = "XYZ"
+
+    @property
+    def cls_name(self):
+        return self.kind
+
+    def is_instance(self, name):
+        return name == self.kind
+
+    def v(self):
+        return [_to_num(self.props[c]) for c in self.comps]
+
+    def setv(self, vals):
+        for c, x in zip(self.comps, vals):
+            self.props[c] = float(x)
+        return self
+
+    def set_special(self, it, key, value):
+        if key in self.comps:
+            self.props[key] = _to_num(value)
+            return True
+        return False
+
+
+def _vec_methods():
+    def new_like(s, vals):
+        return Vec(s.comps, vals, s.kind)
+
+    def other(x, s):
+        o = _arg(x, 0)
+        if not isinstance(o, Vec):
+            raise _Throw(_error_obj("TypeError", f"{s.kind} method expects a vector"))
+        return o.v()
+
+    def length(s):
+        return math.sqrt(sum(c * c for c in s.v()))
+
+    return {
+        "set": lambda s, i, x: s.setv([_num_arg(x, k) for k in range(len(s.comps))]),
+        "setScalar": lambda s, i, x: s.setv([_num_arg(x, 0)] * len(s.comps)),
+        "copy": lambda s, i, x: s.setv(other(x, s)),
+        "clone": lambda s, i, x: new_like(s, s.v()),
+        "add": lambda s, i, x: s.setv([a + b for a, b in zip(s.v(), other(x, s))]),
+        "sub": lambda s, i, x: s.setv([a - b for a, b in zip(s.v(), other(x, s))]),
+        "addScalar": lambda s, i, x: s.setv([a + _num_arg(x, 0) for a in s.v()]),
+        "multiplyScalar": lambda s, i, x: s.setv([a * _num_arg(x, 0) for a in s.v()]),
+        "divideScalar": lambda s, i, x: s.setv([a / (_num_arg(x, 0) or math.inf) for a in s.v()]),
+        "multiply": lambda s, i, x: s.setv([a * b for a, b in zip(s.v(), other(x, s))]),
+        "addVectors": lambda s, i, x: s.setv([a + b for a, b in zip(_arg(x, 0).v(), _arg(x, 1).v())]),
+        "subVectors": lambda s, i, x: s.setv([a - b for a, b in zip(_arg(x, 0).v(), _arg(x, 1).v())]),
+        "negate": lambda s, i, x: s.setv([-a for a in s.v()]),
+        "length": lambda s, i, x: length(s),
+        "lengthSq": lambda s, i, x: sum(c * c for c in s.v()),
+        "normalize": lambda s, i, x: s.setv([a / (length(s) or 1.0) for a in s.v()]),
+        "setLength": lambda s, i, x: s.setv([a / (length(s) or 1.0) * _num_arg(x, 0) for a in s.v()]),
+        "dot": lambda s, i, x: sum(a * b for a, b in zip(s.v(), other(x, s))),
+        "cross": lambda s, i, x: s.setv(_cross(s.v(), other(x, s))),
+        "crossVectors": lambda s, i, x: s.setv(_cross(_arg(x, 0).v(), _arg(x, 1).v())),
+        "distanceTo": lambda s, i, x: math.sqrt(sum((a - b) ** 2 for a, b in zip(s.v(), other(x, s)))),
+        "lerp": lambda s, i, x: s.setv([a + (b - a) * _num_arg(x, 1) for a, b in zip(s.v(), other(x, s))]),
+        "lerpVectors": lambda s, i, x: s.setv([a + (b - a) * _num_arg(x, 2) for a, b in zip(_arg(x, 0).v(), _arg(x, 1).v())]),
+        "equals": lambda s, i, x: s.v() == other(x, s),
+        "toArray": lambda s, i, x: JSArray(s.v()),
+        "fromArray": lambda s, i, x: s.setv([_to_num(v) for v in it_items(_arg(x, 0))][int(_num_arg(x, 1)):]),
+        "applyAxisAngle": lambda s, i, x: s.setv(_rot_axis(s.v(), other(x, s), _num_arg(x, 1))),
+        "applyEuler": lambda s, i, x: s.setv(_mat3_apply(_euler_mat(_arg(x, 0).v()), s.v())),
+        "applyMatrix4": lambda s, i, x: s.setv(_mat4_point(_arg(x, 0).m, s.v())),
+        "rotateAround": lambda s, i, x: s.setv(_rot2(s.v(), _arg(x, 0).v(), _num_arg(x, 1))),
+        "angle": lambda s, i, x: math.atan2(s.v()[1], s.v()[0]) % (2 * math.pi),
+    }
+
+
+def it_items(v):
+    return v.items if isinstance(v, JSArray) else []
+
+
+Vec.js_methods = _vec_methods()
+
+
+def _cross(a, b):
+    return [a[1] * b[2] - a[2] * b[1], a[2] * b[0] - a[0] * b[2], a[0] * b[1] - a[1] * b[0]]
+
+
+def _rot2(p, c, ang):
+    x, y = p[0] - c[0], p[1] - c[1]
+    cs, sn = math.cos(ang), math.sin(ang)
+    return [c[0] + x * cs - y * sn, c[1] + x * sn + y * cs]
+
+
+def _rot_axis(v, axis, ang):
+    n = math.sqrt(sum(a * a for a in axis)) or 1.0
+    k = [a / n for a in axis]
+    cs, sn = math.cos(ang), math.sin(ang)
+    kxv = _cross(k, v)
+    kdv = sum(a * b for a, b in zip(k, v))
+    return [v[j] * cs + kxv[j] * sn + k[j] * kdv * (1 - cs) for j in range(3)]
+
+
+def _euler_mat(e):
+    """Rotation matrix of an XYZ Euler (three.js default order): R = Rx * Ry * Rz."""
+    x, y, z = e[:3]
+    a, b = math.cos(x), math.sin(x)
+    c, d = math.cos(y), math.sin(y)
+    ee, f = math.cos(z), math.sin(z)
+    return [[c * ee, -c * f, d],
+            [a * f + b * ee * d, a * ee - b * f * d, -b * c],
+            [b * f - a * ee * d, b * ee + a * f * d, a * c]]
+
+
+def _mat3_apply(m, v):
+    return [sum(m[r][k] * v[k] for k in range(3)) for r in range(3)]
+
+
+def _mat3_to_euler(m):
+    y = math.asin(max(-1.0, min(1.0, m[0][2])))
+    if abs(m[0][2]) < 0.9999999:
+        x = math.atan2(-m[1][2], m[2][2])
+        z = math.atan2(-m[0][1], m[0][0])
+    else:
+        x = math.atan2(m[2][1], m[1][1])
+        z = 0.0
+    return [x, y, z]
+
+
+def _mat_mul(a, b):
+    n = len(a)
+    return [[sum(a[r][k] * b[k][c] for k in range(n)) for c in range(n)] for r in range(n)]
+
+
+def _mat4_point(m, v):
+    """m: row-major 4x4 list; v: 3 coords."""
+    w = m[3][0] * v[0] + m[3][1] * v[1] + m[3][2] * v[2] + m[3][3]
+    w = w or 1.0
+    return [(m[r][0] * v[0] + m[r][1] * v[1] + m[r][2] * v[2] + m[r][3]) / w for r in range(3)]
+
+
+def _compose(pos, rot, scl):
+    r = _euler_mat(rot)
+    return [[r[0][0] * scl[0], r[0][1] * scl[1], r[0][2] * scl[2], pos[0]],
+            [r[1][0] * scl[0], r[1][1] * scl[1], r[1][2] * scl[2], pos[1]],
+            [r[2][0] * scl[0], r[2][1] * scl[1], r[2][2] * scl[2], pos[2]],
+            [0.0, 0.0, 0.0, 1.0]]
+
+
+def _ident4():
+    return [[1.0 if r == c else 0.0 for c in range(4)] for r in range(4)]
+
+
+class Matrix4(Host):
+    __slots__ = ("m",)
+    cls_name = "Matrix4"
+
+    def __init__(self, m=None):
+        super().__init__({"isMatrix4": True})
+        self.m = m or _ident4()
+
+    def get_special(self, it, key):
+        if key == "elements":
+            return JSArray([self.m[r][c] for c in range(4) for r in range(4)])
+        return super().get_special(it, key)
+
+    def _rot(self, axis, a):
+        cs, sn = math.cos(a), math.sin(a)
+        m = _ident4()
+        i, j = {"x": (1, 2), "y": (2, 0), "z": (0, 1)}[axis]
+        m[i][i], m[i][j], m[j][i], m[j][j] = cs, -sn, sn, cs
+        self.m = m
+        return self
+
+    js_methods = {
+        "identity": lambda s, i, x: (setattr(s, "m", _ident4()), s)[-1],
+        "copy": lambda s, i, x: (setattr(s, "m", [row[:] for row in _arg(x, 0).m]), s)[-1],
+        "clone": lambda s, i, x: Matrix4([row[:] for row in s.m]),
+        "makeTranslation": lambda s, i, x: (setattr(s, "m", _compose(
+            _arg(x, 0).v() if isinstance(_arg(x, 0), Vec) else [_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2)],
+            [0, 0, 0], [1, 1, 1])), s)[-1],
+        "makeScale": lambda s, i, x: (setattr(s, "m", _compose([0, 0, 0], [0, 0, 0],
+                                                                [_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2)])), s)[-1],
+        "makeRotationX": lambda s, i, x: s._rot("x", _num_arg(x, 0)),
+        "makeRotationY": lambda s, i, x: s._rot("y", _num_arg(x, 0)),
+        "makeRotationZ": lambda s, i, x: s._rot("z", _num_arg(x, 0)),
+        "makeRotationFromEuler": lambda s, i, x: (setattr(s, "m", _compose([0, 0, 0], _arg(x, 0).v(), [1, 1, 1])), s)[-1],
+        "compose": lambda s, i, x: (setattr(s, "m", _compose(_arg(x, 0).v(), _quat_or_euler(_arg(x, 1)), _arg(x, 2).v())), s)[-1],
+        "multiply": lambda s, i, x: (setattr(s, "m", _mat_mul(s.m, _arg(x, 0).m)), s)[-1],
+        "premultiply": lambda s, i, x: (setattr(s, "m", _mat_mul(_arg(x, 0).m, s.m)), s)[-1],
+        "multiplyMatrices": lambda s, i, x: (setattr(s, "m", _mat_mul(_arg(x, 0).m, _arg(x, 1).m)), s)[-1],
+        "setPosition": lambda s, i, x: (_set_pos(s.m, _arg(x, 0).v() if isinstance(_arg(x, 0), Vec)
+                                                 else [_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2)]), s)[-1],
+    }
+
+
+def _set_pos(m, p):
+    m[0][3], m[1][3], m[2][3] = p
+
+
+class Quaternion(Host):
+    """Held as a rotation matrix; enough for setFromEuler / setFromAxisAngle / Matrix4.compose."""
+    __slots__ = ("r",)
+    cls_name = "Quaternion"
+
+    def __init__(self):
+        super().__init__({"isQuaternion": True})
+        self.r = _euler_mat([0, 0, 0])
+
+    js_methods = {
+        "setFromEuler": lambda s, i, x: (setattr(s, "r", _euler_mat(_arg(x, 0).v())), s)[-1],
+        "setFromAxisAngle": lambda s, i, x: (setattr(s, "r", _axis_mat(_arg(x, 0).v(), _num_arg(x, 1))), s)[-1],
+        "identity": lambda s, i, x: (setattr(s, "r", _euler_mat([0, 0, 0])), s)[-1],
+        "multiply": lambda s, i, x: (setattr(s, "r", _mat_mul(s.r, _arg(x, 0).r)), s)[-1],
+        "clone": lambda s, i, x: _quat_copy(s),
+        "copy": lambda s, i, x: (setattr(s, "r", [row[:] for row in _arg(x, 0).r]), s)[-1],
+    }
+
+
+def _quat_copy(q):
+    n = Quaternion()
+    n.r = [row[:] for row in q.r]
+    return n
+
+
+def _axis_mat(axis, ang):
+    cols = [_rot_axis(e, axis, ang) for e in ([1, 0, 0], [0, 1, 0], [0, 0, 1])]
+    return [[cols[c][r] for c in range(3)] for r in range(3)]
+
+
+def _quat_or_euler(q):
+    if isinstance(q, Quaternion):
+        return _mat3_to_euler(q.r)
+    if isinstance(q, Vec):
+        return q.v()
+    return [0.0, 0.0, 0.0]
+
+
+_NAMED_COLORS = {"white": 0xFFFFFF, "black": 0x000000, "red": 0xFF0000, "green": 0x008000, "blue": 0x0000FF,
+                 "yellow": 0xFFFF00, "orange": 0xFFA500, "purple": 0x800080, "gray": 0x808080, "grey": 0x808080,
+                 "brown": 0xA52A2A, "pink": 0xFFC0CB, "cyan": 0x00FFFF, "magenta": 0xFF00FF, "silver": 0xC0C0C0,
+                 "gold": 0xFFD700, "navy": 0x000080, "teal": 0x008080, "maroon": 0x800000, "olive": 0x808000,
+                 "lime": 0x00FF00, "beige": 0xF5F5DC, "tan": 0xD2B48C, "skyblue": 0x87CEEB, "darkgreen": 0x006400,
+                 "forestgreen": 0x228B22, "saddlebrown": 0x8B4513, "sienna": 0xA0522D, "ivory": 0xFFFFF0,
+                 "khaki": 0xF0E68C, "coral": 0xFF7F50, "salmon": 0xFA8072, "chocolate": 0xD2691E,
+                 "darkgray": 0xA9A9A9, "darkgrey": 0xA9A9A9, "lightgray": 0xD3D3D3, "lightgrey": 0xD3D3D3,
+                 "dimgray": 0x696969, "wheat": 0xF5DEB3, "crimson": 0xDC143C, "indigo": 0x4B0082, "violet": 0xEE82EE}
+
+
+class Color(Host):
+    """sRGB components in [0, 1] (three.js keeps linear internally; the scene JSON stores the sRGB hex)."""
+    __slots__ = ()
+    cls_name = "Color"
+
+    def __init__(self, r=1.0, g=1.0, b=1.0):
+        super().__init__({"r": r, "g": g, "b": b, "isColor": True})
+
+    def rgb(self):
+        return [_to_num(self.props[c]) for c in "rgb"]
+
+    def set_any(self, x):
+        a = _arg(x, 0)
+        if len(x) >= 3:
+            return self.set_rgb(_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2))
+        if isinstance(a, Color):
+            return self.set_rgb(*a.rgb())
+        if isinstance(a, (int, float)) and not isinstance(a, bool):
+            h = int(a) & 0xFFFFFF
+            return self.set_rgb(((h >> 16) & 255) / 255, ((h >> 8) & 255) / 255, (h & 255) / 255)
+        if isinstance(a, str):
+            s = a.strip().lower()
+            if s.startswith("#"):
+                s = s[1:]
+                if len(s) == 3:
+                    s = "".join(ch * 2 for ch in s)
+                try:
+                    h = int(s[:6], 16)
+                except ValueError:
+                    return self
+                return self.set_any([float(h)])
+            m = re.match(r"rgb\(\s*(\d+)\s*,\s*(\d+)\s*,\s*(\d+)\s*\)", s)
+            if m:
+                return self.set_rgb(*(int(g) / 255 for g in m.groups()))
+            m = re.match(r"hsl\(\s*([\d.]+)\s*,\s*([\d.]+)%\s*,\s*([\d.]+)%\s*\)", s)
+            if m:
+                return self.set_hsl(float(m.group(1)) / 360, float(m.group(2)) / 100, float(m.group(3)) / 100)
+            if s in _NAMED_COLORS:
+                return self.set_any([float(_NAMED_COLORS[s])])
+        return self
+
+    def set_rgb(self, r, g, b):
+        self.props.update({"r": float(r), "g": float(g), "b": float(b)})
+        return self
+
+    def set_hsl(self, h, s, l):
+        h = h % 1.0
+        s = min(max(s, 0.0), 1.0)
+        l = min(max(l, 0.0), 1.0)
+        if s == 0:
+            return self.set_rgb(l, l, l)
+        p = l * (1 + s) if l <= 0.5 else l + s - l * s
+        q = 2 * l - p
+
+        def hue(t):
+            t %= 1.0
+            if t < 1 / 6:
+                return q + (p - q) * 6 * t
+            if t < 1 / 2:
+                return p
+            if t < 2 / 3:
+                return q + (p - q) * 6 * (2 / 3 - t)
+            return q
+        return self.set_rgb(hue(h + 1 / 3), hue(h), hue(h - 1 / 3))
+
+    def get_hsl(self):
+        r, g, b = self.rgb()
+        mx, mn = max(r, g, b), min(r, g, b)
+        l = (mx + mn) / 2
+        if mx == mn:
+            return 0.0, 0.0, l
+        d = mx - mn
+        s = d / (2 - mx - mn) if l > 0.5 else d / (mx + mn)
+        if mx == r:
+            h = (g - b) / d + (6 if g < b else 0)
+        elif mx == g:
+            h = (b - r) / d + 2
+        else:
+            h = (r - g) / d + 4
+        return h / 6, s, l
+
+    def hex(self) -> int:
+        r, g, b = (max(0, min(255, int(round(c * 255)))) for c in self.rgb())
+        return (r << 16) | (g << 8) | b
+
+    def set_special(self, it, key, value):
+        if key in ("r", "g", "b"):
+            self.props[key] = _to_num(value)
+            return True
+        return False
+
+    js_methods = {
+        "set": lambda s, i, x: s.set_any(x),
+        "setHex": lambda s, i, x: s.set_any([float(int(_num_arg(x, 0)))]),
+        "setRGB": lambda s, i, x: s.set_rgb(_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2)),
+        "setHSL": lambda s, i, x: s.set_hsl(_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2)),
+        "setStyle": lambda s, i, x: s.set_any(x[:1]),
+        "setScalar": lambda s, i, x: s.set_rgb(*[_num_arg(x, 0)] * 3),
+        "getHex": lambda s, i, x: float(s.hex()),
+        "getHexString": lambda s, i, x: f"{s.hex():06x}",
+        "getStyle": lambda s, i, x: f"rgb({','.join(str(int(round(c * 255))) for c in s.rgb())})",
+        "getHSL": lambda s, i, x: _hsl_out(s, _arg(x, 0)),
+        "offsetHSL": lambda s, i, x: (lambda h: s.set_hsl(h[0] + _num_arg(x, 0), h[1] + _num_arg(x, 1),
+                                                         h[2] + _num_arg(x, 2)))(s.get_hsl()),
+        "clone": lambda s, i, x: Color(*s.rgb()),
+        "copy": lambda s, i, x: s.set_rgb(*_arg(x, 0).rgb()),
+        "multiplyScalar": lambda s, i, x: s.set_rgb(*[c * _num_arg(x, 0) for c in s.rgb()]),
+        "multiply": lambda s, i, x: s.set_rgb(*[a * b for a, b in zip(s.rgb(), _arg(x, 0).rgb())]),
+        "add": lambda s, i, x: s.set_rgb(*[a + b for a, b in zip(s.rgb(), _arg(x, 0).rgb())]),
+        "addScalar": lambda s, i, x: s.set_rgb(*[c + _num_arg(x, 0) for c in s.rgb()]),
+        "lerp": lambda s, i, x: s.set_rgb(*[a + (b - a) * _num_arg(x, 1) for a, b in zip(s.rgb(), _arg(x, 0).rgb())]),
+        "lerpColors": lambda s, i, x: s.set_rgb(*[a + (b - a) * _num_arg(x, 2)
+                                                  for a, b in zip(_arg(x, 0).rgb(), _arg(x, 1).rgb())]),
+        "convertSRGBToLinear": lambda s, i, x: s,
+        "convertLinearToSRGB": lambda s, i, x: s,
+        "equals": lambda s, i, x: s.rgb() == _arg(x, 0).rgb(),
+    }
+
+
+def _hsl_out(c, target):
+    h, s, l = c.get_hsl()
+    o = target if isinstance(target, JSObject) else JSObject()
+    o.props.update({"h": h, "s": s, "l": l})
+    return o
+
+
+# geometries: record type + params + baked transforms; triangulated only at serialisation
+
+_GEOM_PARAMS = {
+    "BoxGeometry": ("width", "height", "depth", "widthSegments", "heightSegments", "depthSegments"),
+    "SphereGeometry": ("radius", "widthSegments", "heightSegments", "phiStart", "phiLength", "thetaStart", "thetaLength"),
+    "CylinderGeometry": ("radiusTop", "radiusBottom", "height", "radialSegments", "heightSegments", "openEnded",
+                         "thetaStart", "thetaLength"),
+    "ConeGeometry": ("radius", "height", "radialSegments", "heightSegments", "openEnded", "thetaStart", "thetaLength"),
+    "PlaneGeometry": ("width", "height", "widthSegments", "heightSegments"),
+    "CircleGeometry": ("radius", "segments", "thetaStart", "thetaLength"),
+    "RingGeometry": ("innerRadius", "outerRadius", "thetaSegments", "phiSegments", "thetaStart", "thetaLength"),
+    "TorusGeometry": ("radius", "tube", "radialSegments", "tubularSegments", "arc"),
+    "TorusKnotGeometry": ("radius", "tube", "tubularSegments", "radialSegments", "p", "q"),
+    "CapsuleGeometry": ("radius", "length", "capSegments", "radialSegments"),
+    "IcosahedronGeometry": ("radius", "detail"),
+    "OctahedronGeometry": ("radius", "detail"),
+    "TetrahedronGeometry": ("radius", "detail"),
+    "DodecahedronGeometry": ("radius", "detail"),
+    "LatheGeometry": ("points", "segments", "phiStart", "phiLength"),
+    "TubeGeometry": ("path", "tubularSegments", "radius", "radialSegments", "closed"),
+    "ExtrudeGeometry": ("shapes", "options"),
+    "ShapeGeometry": ("shapes", "curveSegments"),
+}
+_GEOM_DEFAULTS = {
+    "BoxGeometry": (1, 1, 1, 1, 1, 1), "SphereGeometry": (1, 32, 16, 0, 2 * math.pi, 0, math.pi),
+    "CylinderGeometry": (1, 1, 1, 32, 1, False, 0, 2 * math.pi), "ConeGeometry": (1, 1, 32, 1, False, 0, 2 * math.pi),
+    "PlaneGeometry": (1, 1, 1, 1), "CircleGeometry": (1, 32, 0, 2 * math.pi),
+    "RingGeometry": (0.5, 1, 32, 1, 0, 2 * math.pi), "TorusGeometry": (1, 0.4, 12, 48, 2 * math.pi),
+    "TorusKnotGeometry": (1, 0.4, 64, 8, 2, 3), "CapsuleGeometry": (1, 1, 4, 8), "IcosahedronGeometry": (1, 0),
+    "OctahedronGeometry": (1, 0), "TetrahedronGeometry": (1, 0), "DodecahedronGeometry": (1, 0),
+    "LatheGeometry": (None, 12, 0, 2 * math.pi), "TubeGeometry": (None, 64, 1, 8, False),
+    "ExtrudeGeometry": (None, None), "ShapeGeometry": (None, 12),
+}
+
+
+class Geometry(Host):
+    __slots__ = ("gtype", "params", "xform", "buffer", "id_")
+    cls_name = "BufferGeometry"
+    bases = ("BufferGeometry",)
+
+    def __init__(self, gtype="BufferGeometry", params=None):
+        super().__init__({"isBufferGeometry": True})
+        self.gtype = gtype
+        self.params = params or {}
+        self.xform = _ident4()
+        self.buffer: Dict[str, Any] = {}
+        self.id_ = _uuid.uuid4().hex
+
+    def get_special(self, it, key):
+        if key == "type":
+            return self.gtype
+        if key == "parameters":
+            return JSObject({k: v for k, v in self.params.items()})
+        if key == "attributes":
+            return JSObject(dict(self.buffer))
+        if key == "uuid":
+            return self.id_
+        return super().get_special(it, key)
+
+    def is_instance(self, name):
+        return name in (self.gtype, "BufferGeometry")
+
+    def apply(self, m):
+        self.xform = _mat_mul(m, self.xform)
+        return self
+
+    js_methods = {
+        "translate": lambda s, i, x: s.apply(_compose([_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2)], [0, 0, 0], [1, 1, 1])),
+        "scale": lambda s, i, x: s.apply(_compose([0, 0, 0], [0, 0, 0], [_num_arg(x, 0, 1.0), _num_arg(x, 1, 1.0), _num_arg(x, 2, 1.0)])),
+        "rotateX": lambda s, i, x: s.apply(_compose([0, 0, 0], [_num_arg(x, 0), 0, 0], [1, 1, 1])),
+        "rotateY": lambda s, i, x: s.apply(_compose([0, 0, 0], [0, _num_arg(x, 0), 0], [1, 1, 1])),
+        "rotateZ": lambda s, i, x: s.apply(_compose([0, 0, 0], [0, 0, _num_arg(x, 0)], [1, 1, 1])),
+        "applyMatrix4": lambda s, i, x: s.apply(_arg(x, 0).m),
+        "center": lambda s, i, x: _geom_center(s),
+        "computeVertexNormals": lambda s, i, x: UNDEF,
+        "computeBoundingBox": lambda s, i, x: UNDEF,
+        "computeBoundingSphere": lambda s, i, x: UNDEF,
+        "clone": lambda s, i, x: _geom_clone(s),
+        "dispose": lambda s, i, x: UNDEF,
+        "setAttribute": lambda s, i, x: (s.buffer.__setitem__(_to_str(_arg(x, 0)), _arg(x, 1)), s)[-1],
+        "getAttribute": lambda s, i, x: s.buffer.get(_to_str(_arg(x, 0)), UNDEF),
+        "setIndex": lambda s, i, x: (s.buffer.__setitem__("__index", _arg(x, 0)), s)[-1],
+        "setFromPoints": lambda s, i, x: (s.buffer.__setitem__("position", BufferAttribute(
+            [c for p in it_items(_arg(x, 0)) for c in (p.v() + [0.0])[:3]], 3)), s)[-1],
+    }
+
+
+def _geom_clone(g: Geometry) -> Geometry:
+    n = Geometry(g.gtype, dict(g.params))
+    n.xform = [row[:] for row in g.xform]
+    n.buffer = dict(g.buffer)
+    return n
+
+
+def _geom_center(g: Geometry):
+    v, _ = geometry_mesh(g)
+    if v.shape[0]:
+        c = (v.min(0).values + v.max(0).values) / 2
+        g.apply(_compose([-float(c[0]), -float(c[1]), -float(c[2])], [0, 0, 0], [1, 1, 1]))
+    return g
+
+
+class BufferAttribute(Host):
+    __slots__ = ("array", "item")
+    cls_name = "BufferAttribute"
+
+    def __init__(self, array, item_size):
+        super().__init__({"isBufferAttribute": True})
+        self.array = [float(_to_num(a)) for a in array]
+        self.item = int(item_size)
+
+    def get_special(self, it, key):
+        if key == "count":
+            return float(len(self.array) // max(self.item, 1))
+        if key == "itemSize":
+            return float(self.item)
+        if key == "array":
+            return JSArray(list(self.array))
+        return super().get_special(it, key)
+
+    def _set(self, i, k, v):
+        j = int(i) * self.item + k
+        if 0 <= j < len(self.array):
+            self.array[j] = float(v)
+        return self
+
+    def _get(self, i, k):
+        j = int(i) * self.item + k
+        return self.array[j] if 0 <= j < len(self.array) else UNDEF
+
+    js_methods = {
+        "setXYZ": lambda s, i, x: (s._set(_num_arg(x, 0), 0, _num_arg(x, 1)), s._set(_num_arg(x, 0), 1, _num_arg(x, 2)),
+                                   s._set(_num_arg(x, 0), 2, _num_arg(x, 3)))[-1],
+        "setXY": lambda s, i, x: (s._set(_num_arg(x, 0), 0, _num_arg(x, 1)), s._set(_num_arg(x, 0), 1, _num_arg(x, 2)))[-1],
+        "setX": lambda s, i, x: s._set(_num_arg(x, 0), 0, _num_arg(x, 1)),
+        "setY": lambda s, i, x: s._set(_num_arg(x, 0), 1, _num_arg(x, 1)),
+        "setZ": lambda s, i, x: s._set(_num_arg(x, 0), 2, _num_arg(x, 1)),
+        "getX": lambda s, i, x: s._get(_num_arg(x, 0), 0),
+        "getY": lambda s, i, x: s._get(_num_arg(x, 0), 1),
+        "getZ": lambda s, i, x: s._get(_num_arg(x, 0), 2),
+    }
+
+
+class Material(Host):
+    __slots__ = ("mtype",)
+    cls_name = "Material"
+
+    def __init__(self, mtype, params: Optional[JSObject] = None):
+        super().__init__({"isMaterial": True, "color": Color(1, 1, 1), "opacity": 1.0, "transparent": False,
+                          "side": 0.0, "visible": True, "wireframe": False})
+        self.mtype = mtype
+        if isinstance(params, JSObject):
+            for k, v in params.props.items():
+                self.js_set(None, k, v)
+
+    def get_special(self, it, key):
+        if key == "type":
+            return self.mtype
+        return super().get_special(it, key)
+
+    def is_instance(self, name):
+        return name in (self.mtype, "Material")
+
+    def set_special(self, it, key, value):
+        if key in ("color", "emissive", "specular", "sheenColor", "attenuationColor"):
+            c = Color(0, 0, 0)
+            c.set_any([value])
+            self.props[key] = c
+            return True
+        return False
+
+    js_methods = {
+        "clone": lambda s, i, x: _mat_clone(s),
+        "dispose": lambda s, i, x: UNDEF,
+        "setValues": lambda s, i, x: ([s.js_set(i, k, v) for k, v in _arg(x, 0).props.items()], UNDEF)[-1],
+    }
+
+
+def _mat_clone(m: Material):
+    n = Material(m.mtype)
+    for k, v in m.props.items():
+        n.props[k] = Color(*v.rgb()) if isinstance(v, Color) else v
+    return n
+
+
+class Texture(Host):
+    __slots__ = ("nbytes",)
+    cls_name = "Texture"
+
+    def __init__(self, nbytes=0):
+        super().__init__({"isTexture": True, "repeat": Vec(("x", "y"), [1, 1], "Vector2"),
+                          "offset": Vec(("x", "y"), [0, 0], "Vector2")})
+        self.nbytes = nbytes
+
+    js_methods = {"clone": lambda s, i, x: Texture(s.nbytes), "dispose": lambda s, i, x: UNDEF}
+
+
+class Object3D(Host):
+    __slots__ = ("otype", "id_")
+    cls_name = "Object3D"
+
+    def __init__(self, otype="Object3D", geometry=None, material=None):
+        super().__init__({"isObject3D": True, "name": "", "visible": True, "castShadow": False,
+                          "receiveShadow": False, "userData": JSObject(), "parent": None,
+                          "position": Vec(("x", "y", "z"), None, "Vector3"),
+                          "rotation": Vec(("x", "y", "z"), None, "Euler"),
+                          "scale": Vec(("x", "y", "z"), [1, 1, 1], "Vector3"),
+                          "children": JSArray(), "matrix": Matrix4(), "matrixAutoUpdate": True})
+        self.otype = otype
+        self.id_ = _uuid.uuid4().hex
+        if geometry is not None:
+            self.props["geometry"] = geometry
+        if material is not None:
+            self.props["material"] = material
+
+    def get_special(self, it, key):
+        if key == "type":
+            return self.otype
+        if key == "uuid":
+            return self.id_
+        if key == "quaternion":
+            q = Quaternion()
+            q.r = _euler_mat(self.props["rotation"].v())
+            return q
+        if key == "up":
+            return Vec(("x", "y", "z"), [0, 1, 0], "Vector3")
+        return super().get_special(it, key)
+
+    def is_instance(self, name):
+        return name in (self.otype, "Object3D") or (self.otype == "InstancedMesh" and name == "Mesh")
+
+    def set_special(self, it, key, value):
+        if key in ("position", "rotation", "scale"):
+            raise _Throw(_error_obj("TypeError", f"cannot assign to read only property '{key}' of object"))
+        return False
+
+    def local(self):
+        return _compose(self.props["position"].v(), self.props["rotation"].v(), self.props["scale"].v())
+
+    def children(self) -> list:
+        return self.props["children"].items
+
+    def add(self, objs):
+        for o in objs:
+            if not isinstance(o, Object3D):
+                raise _Throw(_error_obj("TypeError", "add() expects Object3D instances"))
+            if o is self:
+                continue
+            old = o.props.get("parent")
+            if isinstance(old, Object3D):
+                old.children()[:] = [c for c in old.children() if c is not o]
+            o.props["parent"] = self
+            self.children().append(o)
+        return self
+
+    def rotate_local(self, axis, ang):
+        r = _euler_mat(self.props["rotation"].v())
+        a = {"x": [1, 0, 0], "y": [0, 1, 0], "z": [0, 0, 1]}[axis]
+        self.props["rotation"].setv(_mat3_to_euler(_mat_mul(r, _axis_mat(a, ang))))
+        return self
+
+    def look_at(self, target):
+        p = self.props["position"].v()
+        f = [t - q for t, q in zip(target, p)]
+        n = math.sqrt(sum(c * c for c in f)) or 1.0
+        z = [c / n for c in f]                      # objects look down +z
+        up = [0.0, 1.0, 0.0] if abs(z[1]) < 0.999 else [0.0, 0.0, 1.0]
+        x = _cross(up, z)
+        xn = math.sqrt(sum(c * c for c in x)) or 1.0
+        x = [c / xn for c in x]
+        y = _cross(z, x)
+        m = [[x[0], y[0], z[0]], [x[1], y[1], z[1]], [x[2], y[2], z[2]]]
+        self.props["rotation"].setv(_mat3_to_euler(m))
+        return self
+
+    js_methods = {
+        "add": lambda s, i, x: s.add(x),
+        "remove": lambda s, i, x: (s.children().__setitem__(slice(None), [c for c in s.children() if all(c is not o for o in x)]), s)[-1],
+        "clear": lambda s, i, x: (s.children().clear(), s)[-1],
+        "rotateX": lambda s, i, x: s.rotate_local("x", _num_arg(x, 0)),
+        "rotateY": lambda s, i, x: s.rotate_local("y", _num_arg(x, 0)),
+        "rotateZ": lambda s, i, x: s.rotate_local("z", _num_arg(x, 0)),
+        "rotateOnAxis": lambda s, i, x: (s.props["rotation"].setv(_mat3_to_euler(_mat_mul(_euler_mat(s.props["rotation"].v()),
+                                                                                         _axis_mat(_arg(x, 0).v(), _num_arg(x, 1))))), s)[-1],
+        "translateX": lambda s, i, x: (s.props["position"].setv(_add3(s.props["position"].v(), _mat3_apply(_euler_mat(s.props["rotation"].v()), [_num_arg(x, 0), 0, 0]))), s)[-1],
+        "translateY": lambda s, i, x: (s.props["position"].setv(_add3(s.props["position"].v(), _mat3_apply(_euler_mat(s.props["rotation"].v()), [0, _num_arg(x, 0), 0]))), s)[-1],
+        "translateZ": lambda s, i, x: (s.props["position"].setv(_add3(s.props["position"].v(), _mat3_apply(_euler_mat(s.props["rotation"].v()), [0, 0, _num_arg(x, 0)]))), s)[-1],
+        "lookAt": lambda s, i, x: s.look_at(_arg(x, 0).v() if isinstance(_arg(x, 0), Vec) else [_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2)]),
+        "updateMatrix": lambda s, i, x: (setattr(s.props["matrix"], "m", s.local()), UNDEF)[-1],
+        "updateMatrixWorld": lambda s, i, x: UNDEF,
+        "traverse": lambda s, i, x: (_traverse(i, s, _arg(x, 0)), UNDEF)[-1],
+        "clone": lambda s, i, x: _obj_clone(s),
+        "getObjectByName": lambda s, i, x: _find_name(s, _to_str(_arg(x, 0))),
+        "setMatrixAt": lambda s, i, x: (s.props.setdefault("__inst", {}).__setitem__(int(_num_arg(x, 0)), [row[:] for row in _arg(x, 1).m]), UNDEF)[-1],
+        "setColorAt": lambda s, i, x: UNDEF,
+        "getMatrixAt": lambda s, i, x: (setattr(_arg(x, 1), "m", [row[:] for row in s.props.get("__inst", {}).get(int(_num_arg(x, 0)), _ident4())]), UNDEF)[-1],
+        "applyMatrix4": lambda s, i, x: _apply_obj_matrix(s, _arg(x, 0).m),
+    }
+
+
+def _add3(a, b):
+    return [p + q for p, q in zip(a, b)]
+
+
+def _apply_obj_matrix(o: Object3D, m):
+    full = _mat_mul(m, o.local())
+    pos = [full[0][3], full[1][3], full[2][3]]
+    sc = [math.sqrt(sum(full[r][c] ** 2 for r in range(3))) for c in range(3)]
+    rot = [[full[r][c] / (sc[c] or 1.0) for c in range(3)] for r in range(3)]
+    o.props["position"].setv(pos)
+    o.props["scale"].setv(sc)
+    o.props["rotation"].setv(_mat3_to_euler(rot))
+    return o
+
+
+def _traverse(it, o, f):
+    it.call(f, UNDEF, [o])
+    for c in list(o.children()):
+        _traverse(it, c, f)
+
+
+def _find_name(o, name):
+    if o.props.get("name") == name:
+        return o
+    for c in o.children():
+        r = _find_name(c, name)
+        if r is not UNDEF:
+            return r
+    return UNDEF
+
+
+def _obj_clone(o: Object3D) -> Object3D:
+    n = Object3D(o.otype, o.props.get("geometry"), o.props.get("material"))
+    for k, v in o.props.items():
+        if k in ("children", "parent", "matrix"):
+            continue
+        if isinstance(v, Vec):
+            n.props[k].setv(v.v())
+        elif k not in ("position", "rotation", "scale"):
+            n.props[k] = v
+    for c in o.children():
+        n.add([_obj_clone(c)])
+    return n
+
+
+class Shape(Host):
+    """Shape / Path / CurvePath: polyline outline from moveTo/lineTo/curves (sampled)."""
+    __slots__ = ("pts", "holes_")
+    cls_name = "Shape"
+
+    def __init__(self, pts=None):
+        super().__init__({})
+        self.pts: List[List[float]] = [list(p.v()[:2]) for p in pts] if pts else []
+        self.holes_: List["Shape"] = []
+
+    def get_special(self, it, key):
+        if key == "holes":
+            return _HolesProxy(self)
+        return super().get_special(it, key)
+
+    def _quad(self, x):
+        cx, cy, ex, ey = (_num_arg(x, k) for k in range(4))
+        sx, sy = self.pts[-1] if self.pts else (0.0, 0.0)
+        for k in range(1, 9):
+            t = k / 8
+            self.pts.append([(1 - t) ** 2 * sx + 2 * (1 - t) * t * cx + t * t * ex,
+                             (1 - t) ** 2 * sy + 2 * (1 - t) * t * cy + t * t * ey])
+        return self
+
+    def _bez(self, x):
+        c1x, c1y, c2x, c2y, ex, ey = (_num_arg(x, k) for k in range(6))
+        sx, sy = self.pts[-1] if self.pts else (0.0, 0.0)
+        for k in range(1, 13):
+            t = k / 12
+            u = 1 - t
+            self.pts.append([u ** 3 * sx + 3 * u * u * t * c1x + 3 * u * t * t * c2x + t ** 3 * ex,
+                             u ** 3 * sy + 3 * u * u * t * c1y + 3 * u * t * t * c2y + t ** 3 * ey])
+        return self
+
+    def _arc(self, x, absolute):
+        cx, cy, r, a0, a1 = (_num_arg(x, k) for k in range(5))
+        cw = _truthy(_arg(x, 5, False))
+        if not absolute and self.pts:
+            cx += self.pts[-1][0]
+            cy += self.pts[-1][1]
+        span = a1 - a0
+        if cw and span > 0:
+            span -= 2 * math.pi
+        elif not cw and span < 0:
+            span += 2 * math.pi
+        for k in range(17):
+            a = a0 + span * k / 16
+            self.pts.append([cx + r * math.cos(a), cy + r * math.sin(a)])
+        return self
+
+    js_methods = {
+        "moveTo": lambda s, i, x: (s.pts.append([_num_arg(x, 0), _num_arg(x, 1)]), s)[-1],
+        "lineTo": lambda s, i, x: (s.pts.append([_num_arg(x, 0), _num_arg(x, 1)]), s)[-1],
+        "quadraticCurveTo": lambda s, i, x: s._quad(x),
+        "bezierCurveTo": lambda s, i, x: s._bez(x),
+        "absarc": lambda s, i, x: s._arc(x, True),
+        "arc": lambda s, i, x: s._arc(x, False),
+        "closePath": lambda s, i, x: s,
+        "getPoints": lambda s, i, x: JSArray([Vec(("x", "y"), p, "Vector2") for p in s.pts]),
+        "setFromPoints": lambda s, i, x: (setattr(s, "pts", [list(p.v()[:2]) for p in it_items(_arg(x, 0))]), s)[-1],
+    }
+
+
+class _HolesProxy(Host):
+    __slots__ = ("shape",)
+
+    def __init__(self, shape):
+        super().__init__({})
+        self.shape = shape
+
+    js_methods = {"push": lambda s, i, x: (s.shape.holes_.extend(v for v in x if isinstance(v, Shape)),
+                                           float(len(s.shape.holes_)))[-1]}
+
+
+class Curve(Host):
+    """CatmullRomCurve3 / LineCurve3 / QuadraticBezierCurve3 / CubicBezierCurve3: getPoint(t) in [0, 1]."""
+    __slots__ = ("kind_", "ctrl", "closed")
+    cls_name = "Curve"
+
+    def __init__(self, kind, ctrl, closed=False):
+        super().__init__({})
+        self.kind_, self.ctrl, self.closed = kind, ctrl, closed
+
+    def point(self, t):
+        c = self.ctrl
+        if self.kind_ == "line":
+            return [a + (b - a) * t for a, b in zip(c[0], c[1])]
+        if self.kind_ == "quad":
+            u = 1 - t
+            return [u * u * a + 2 * u * t * b + t * t * d for a, b, d in zip(*c)]
+        if self.kind_ == "cubic":
+            u = 1 - t
+            return [u ** 3 * a + 3 * u * u * t * b + 3 * u * t * t * d + t ** 3 * e for a, b, d, e in zip(*c)]
+        # centripetal-free uniform Catmull-Rom through the control points
+        n = len(c)
+        if n == 1:
+            return list(c[0])
+        segs = n if self.closed else n - 1
+        f = t * segs
+        k = min(int(f), segs - 1)
+        w = f - k
+
+        def P(j):
+            return c[j % n] if self.closed else c[max(0, min(n - 1, j))]
+        p0, p1, p2, p3 = P(k - 1), P(k), P(k + 1), P(k + 2)
+        return [0.5 * (2 * b + (-a + d) * w + (2 * a - 5 * b + 4 * d - e) * w * w + (-a + 3 * b - 3 * d + e) * w ** 3)
+                for a, b, d, e in zip(p0, p1, p2, p3)]
+
+    js_methods = {
+        "getPoint": lambda s, i, x: Vec(("x", "y", "z"), s.point(_num_arg(x, 0)), "Vector3"),
+        "getPoints": lambda s, i, x: JSArray([Vec(("x", "y", "z"), s.point(k / max(1, int(_num_arg(x, 0, 50.0)))), "Vector3")
+                                              for k in range(int(_num_arg(x, 0, 50.0)) + 1)]),
+    }
+
+
+def _ctor(cls_name, build):
+    return Native(cls_name, ctor=lambda it, x: build(it, x))
+
+
+def _geom_ctor(gtype):
+    names = _GEOM_PARAMS[gtype]
+    defaults = _GEOM_DEFAULTS[gtype]
+
+    def build(it, x):
+        params = {}
+        for k, nm in enumerate(names):
+            v = _arg(x, k)
+            params[nm] = defaults[k] if v is UNDEF else (_to_num(v) if isinstance(v, (int, float, bool)) and not isinstance(v, bool) else v)
+        return Geometry(gtype, params)
+    return Native(gtype, ctor=build)
+
+
+def _vec_ctor(name, comps):
+    return Native(name, ctor=lambda it, x: Vec(comps, [_num_arg(x, k) for k in range(len(comps))], name))
+
+
+def make_three(it: Interp) -> JSObject:
+    mats = ("MeshStandardMaterial", "MeshPhysicalMaterial", "MeshBasicMaterial", "MeshLambertMaterial",
+            "MeshPhongMaterial", "MeshToonMaterial", "MeshNormalMaterial", "MeshMatcapMaterial",
+            "LineBasicMaterial", "LineDashedMaterial", "PointsMaterial", "SpriteMaterial")
+    three: Dict[str, Any] = {}
+    for g in _GEOM_PARAMS:
+        three[g] = _geom_ctor(g)
+    three["BufferGeometry"] = Native("BufferGeometry", ctor=lambda i, x: Geometry())
+    for m in mats:
+        three[m] = Native(m, ctor=lambda i, x, _m=m: Material(_m, _arg(x, 0) if x else None))
+    for cls in ("Float32BufferAttribute", "BufferAttribute", "Uint16BufferAttribute", "Uint32BufferAttribute",
+                "Int32BufferAttribute"):
+        three[cls] = Native(cls, ctor=lambda i, x: BufferAttribute(i.iterate(_arg(x, 0)) if isinstance(_arg(x, 0), JSArray)
+                                                                   else [], _num_arg(x, 1, 3.0)))
+    three["Group"] = Native("Group", ctor=lambda i, x: Object3D("Group"))
+    three["Object3D"] = Native("Object3D", ctor=lambda i, x: Object3D("Object3D"))
+    three["Scene"] = Native("Scene", ctor=lambda i, x: Object3D("Group"))
+    for t in ("Mesh", "LineSegments", "Line", "LineLoop", "Points", "Sprite"):
+        three[t] = Native(t, ctor=lambda i, x, _t=t: Object3D(_t, _arg(x, 0) if x else Geometry(),
+                                                               _arg(x, 1) if len(x) > 1 else Material("MeshBasicMaterial")))
+    three["InstancedMesh"] = Native("InstancedMesh", ctor=lambda i, x: _instanced(x))
+    three["Vector2"] = _vec_ctor("Vector2", ("x", "y"))
+    three["Vector3"] = _vec_ctor("Vector3", ("x", "y", "z"))
+    three["Euler"] = _vec_ctor("Euler", ("x", "y", "z"))
+    three["Matrix4"] = Native("Matrix4", ctor=lambda i, x: Matrix4())
+    three["Quaternion"] = Native("Quaternion", ctor=lambda i, x: Quaternion())
+    three["Color"] = Native("Color", ctor=lambda i, x: Color().set_any(x) if x else Color())
+    three["Shape"] = Native("Shape", ctor=lambda i, x: Shape(it_items(_arg(x, 0)) if x else None))
+    three["Path"] = Native("Path", ctor=lambda i, x: Shape(it_items(_arg(x, 0)) if x else None))
+    three["CatmullRomCurve3"] = Native("CatmullRomCurve3", ctor=lambda i, x: Curve(
+        "catmull", [p.v() for p in it_items(_arg(x, 0))], _truthy(_arg(x, 1, False))))
+    three["LineCurve3"] = Native("LineCurve3", ctor=lambda i, x: Curve("line", [_arg(x, 0).v(), _arg(x, 1).v()]))
+    three["QuadraticBezierCurve3"] = Native("QuadraticBezierCurve3", ctor=lambda i, x: Curve(
+        "quad", [_arg(x, k).v() for k in range(3)]))
+    three["CubicBezierCurve3"] = Native("CubicBezierCurve3", ctor=lambda i, x: Curve(
+        "cubic", [_arg(x, k).v() for k in range(4)]))
+    for t in ("Texture", "CanvasTexture", "DataTexture"):
+        three[t] = Native(t, ctor=lambda i, x: Texture(len(it_items(_arg(x, 0))) if x else 0))
+    for name, val in {"DoubleSide": 2.0, "FrontSide": 0.0, "BackSide": 1.0, "RepeatWrapping": 1000.0,
+                      "ClampToEdgeWrapping": 1001.0, "MirroredRepeatWrapping": 1002.0, "NearestFilter": 1003.0,
+                      "LinearFilter": 1006.0, "SRGBColorSpace": "srgb", "LinearSRGBColorSpace": "srgb-linear",
+                      "AdditiveBlending": 2.0, "NormalBlending": 1.0, "FlatShading": 1.0, "SmoothShading": 2.0,
+                      "RGBAFormat": 1023.0, "UnsignedByteType": 1009.0, "FloatType": 1015.0}.items():
+        three[name] = val
+    rnd = it.random
+    three["MathUtils"] = JSObject({
+        "degToRad": _nat("degToRad", lambda i, t, x: _num_arg(x, 0) * math.pi / 180),
+        "radToDeg": _nat("radToDeg", lambda i, t, x: _num_arg(x, 0) * 180 / math.pi),
+        "clamp": _nat("clamp", lambda i, t, x: max(_num_arg(x, 1), min(_num_arg(x, 2), _num_arg(x, 0)))),
+        "lerp": _nat("lerp", lambda i, t, x: _num_arg(x, 0) + (_num_arg(x, 1) - _num_arg(x, 0)) * _num_arg(x, 2)),
+        "mapLinear": _nat("mapLinear", lambda i, t, x: _num_arg(x, 3) + (_num_arg(x, 0) - _num_arg(x, 1)) *
+                          (_num_arg(x, 4) - _num_arg(x, 3)) / ((_num_arg(x, 2) - _num_arg(x, 1)) or 1.0)),
+        "smoothstep": _nat("smoothstep", lambda i, t, x: _smoothstep(_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2))),
+        "randFloat": _nat("randFloat", lambda i, t, x: _num_arg(x, 0) + rnd() * (_num_arg(x, 1) - _num_arg(x, 0))),
+        "randFloatSpread": _nat("randFloatSpread", lambda i, t, x: _num_arg(x, 0) * (0.5 - rnd())),
+        "randInt": _nat("randInt", lambda i, t, x: float(math.floor(_num_arg(x, 0) + rnd() * (_num_arg(x, 1) - _num_arg(x, 0) + 1)))),
+        "seededRandom": _nat("seededRandom", lambda i, t, x: rnd()),
+        "DEG2RAD": math.pi / 180, "RAD2DEG": 180 / math.pi})
+    return JSObject(three)
+
+
+def _smoothstep(x, lo, hi):
+    if x <= lo:
+        return 0.0
+    if x >= hi:
+        return 1.0
+    t = (x - lo) / (hi - lo)
+    return t * t * (3 - 2 * t)
+
+
+def _instanced(x):
+    o = Object3D("InstancedMesh", _arg(x, 0), _arg(x, 1))
+    o.props["count"] = _num_arg(x, 2)
+    o.props["__inst"] = {}
+    o.props["instanceMatrix"] = JSObject({"needsUpdate": False})
+    return o
+
+
+# ---------------------------------------------------------------------------------- triangulation & export
+
+
+def geometry_mesh(g: Geometry):
+    """-> (vertices [V, 3] float32 tensor, faces [F, 3] int64) with the geometry's baked transform applied."""
+    import torch
+
+    from ..render import scene as S
+    p = g.params
+    t = g.gtype
+
+    def n(key, d=0.0):
+        v = p.get(key, d)
+        return _to_num(v) if v is not UNDEF and v is not None else d
+
+    if t == "BoxGeometry":
+        v, f = S._box(n("width", 1), n("height", 1), n("depth", 1))
+    elif t in ("SphereGeometry",):
+        v, f = S._sphere(n("radius", 1), min(int(n("widthSegments", 32)), 64), min(int(n("heightSegments", 16)), 48))
+    elif t in ("IcosahedronGeometry", "OctahedronGeometry", "TetrahedronGeometry", "DodecahedronGeometry"):
+        seg = {"IcosahedronGeometry": 6, "OctahedronGeometry": 4, "TetrahedronGeometry": 3, "DodecahedronGeometry": 8}[t]
+        seg = seg * (1 + int(n("detail", 0)))
+        v, f = S._sphere(n("radius", 1), max(seg, 3), max(seg // 2, 2))
+    elif t == "CylinderGeometry":
+        v, f = S._cylinder(n("radiusTop", 1), n("radiusBottom", 1), n("height", 1), min(int(n("radialSegments", 32)), 64))
+    elif t == "ConeGeometry":
+        v, f = S._cone(n("radius", 1), n("height", 1), min(int(n("radialSegments", 32)), 64))
+    elif t == "PlaneGeometry":
+        v, f = S._plane(n("width", 1), n("height", 1))
+    elif t == "CircleGeometry":
+        v, f = _fan(n("radius", 1), 0.0, min(int(n("segments", 32)), 96), n("thetaStart", 0), n("thetaLength", 2 * math.pi))
+    elif t == "RingGeometry":
+        v, f = _fan(n("outerRadius", 1), n("innerRadius", 0.5), min(int(n("thetaSegments", 32)), 96),
+                    n("thetaStart", 0), n("thetaLength", 2 * math.pi))
+    elif t == "TorusGeometry":
+        v, f = S._torus(n("radius", 1), n("tube", 0.4), min(int(n("radialSegments", 12)), 32),
+                        min(int(n("tubularSegments", 48)), 96))
+    elif t == "CapsuleGeometry":
+        r, L = n("radius", 1), n("length", 1)
+        prof = [(r * math.sin(math.pi / 2 * k / 6), L / 2 + r * math.cos(math.pi / 2 * k / 6)) for k in range(7)]
+        prof += [(r * math.cos(math.pi / 2 * k / 6), -L / 2 - r * math.sin(math.pi / 2 * k / 6)) for k in range(7)]
+        v, f = S._lathe([(0.0, L / 2 + r)] + prof + [(0.0, -L / 2 - r)], min(int(n("radialSegments", 8)) * 2, 48))
+    elif t == "LatheGeometry":
+        pts = [q.v()[:2] for q in it_items(p.get("points"))] or [[0, 0], [1, 0]]
+        v, f = S._lathe([(a, b) for a, b in pts], min(max(int(n("segments", 12)), 3), 96))
+    elif t == "TorusKnotGeometry":
+        v, f = _knot(n("radius", 1), n("tube", 0.4), min(int(n("tubularSegments", 64)), 128),
+                     min(int(n("radialSegments", 8)), 16), n("p", 2), n("q", 3))
+    elif t == "TubeGeometry":
+        path = p.get("path")
+        if not isinstance(path, Curve):
+            raise _Throw(_error_obj("TypeError", "TubeGeometry needs a Curve path"))
+        v, f = _tube(path, min(int(n("tubularSegments", 64)), 256), n("radius", 1), min(int(n("radialSegments", 8)), 24))
+    elif t in ("ExtrudeGeometry", "ShapeGeometry"):
+        shapes = p.get("shapes")
+        shapes = it_items(shapes) if isinstance(shapes, JSArray) else [shapes]
+        depth = 0.0
+        opts = p.get("options")
+        if t == "ExtrudeGeometry":
+            depth = _to_num(opts.props.get("depth", opts.props.get("amount", 1.0))) if isinstance(opts, JSObject) else 1.0
+        vs, fs, off = [], [], 0
+        for sh in shapes:
+            if isinstance(sh, Shape) and len(sh.pts) >= 3:
+                vv, ff = _extrude(sh.pts, depth)
+                vs.append(vv)
+                fs.append(ff + off)
+                off += vv.shape[0]
+        if not vs:
+            v, f = torch.zeros(0, 3), torch.zeros(0, 3, dtype=torch.long)
+        else:
+            v, f = torch.cat(vs), torch.cat(fs)
+    elif t == "BufferGeometry":
+        pos = g.buffer.get("position")
+        if not isinstance(pos, BufferAttribute) or pos.item < 2:
+            v, f = torch.zeros(0, 3), torch.zeros(0, 3, dtype=torch.long)
+        else:
+            arr = torch.tensor(pos.array, dtype=torch.float32).view(-1, pos.item)
+            v = torch.zeros(arr.shape[0], 3)
+            v[:, :min(3, pos.item)] = arr[:, :3]
+            idx = g.buffer.get("__index")
+            if isinstance(idx, BufferAttribute):
+                ia = idx.array
+            elif isinstance(idx, JSArray):
+                ia = [_to_num(q) for q in idx.items]
+            else:
+                ia = list(range(v.shape[0]))
+            ia = [int(q) for q in ia[: len(ia) // 3 * 3]]
+            f = torch.tensor(ia, dtype=torch.long).view(-1, 3) if ia else torch.zeros(0, 3, dtype=torch.long)
+            if f.numel() and (f.max() >= v.shape[0] or f.min() < 0):
+                raise _Throw(_error_obj("RangeError", "index out of range in BufferGeometry"))
+    else:
+        raise _Throw(_error_obj("TypeError", f"unsupported geometry {t}"))
+    m = torch.tensor(g.xform, dtype=torch.float32)
+    if v.shape[0]:
+        v = torch.cat([v.float(), torch.ones(v.shape[0], 1)], 1) @ m.t()
+        v = v[:, :3]
+    return v.float(), f.long()
+
+
+def _fan(r_out, r_in, seg, t0, tl):
+    import torch
+    seg = max(seg, 3)
+    verts, faces = [], []
+    for k in range(seg + 1):
+        a = t0 + tl * k / seg
+        verts.append((r_out * math.cos(a), r_out * math.sin(a), 0.0))
+        verts.append((r_in * math.cos(a), r_in * math.sin(a), 0.0))
+    for k in range(seg):
+        a, b, c, d = 2 * k, 2 * k + 1, 2 * k + 2, 2 * k + 3
+        faces += [(a, c, b), (b, c, d)]
+    return torch.tensor(verts, dtype=torch.float32), torch.tensor(faces)
+
+
+def _knot(R, r, tseg, rseg, p, q):
+    import torch
+
+    def c(u):
+        qu = q * u
+        cs = math.cos(qu)
+        return [R * (2 + cs) * 0.5 * math.cos(p * u), R * (2 + cs) * 0.5 * math.sin(p * u), R * math.sin(qu) * 0.5]
+    ctrl = [c(2 * math.pi * k / tseg) for k in range(tseg)]
+    return _tube(Curve("catmull", ctrl, True), tseg, r, rseg)
+
+
+def _tube(curve: Curve, tseg, radius, rseg):
+    import torch
+    pts = [curve.point(k / tseg) for k in range(tseg + 1)]
+    verts, faces = [], []
+    prev_n = None
+    for k, pt in enumerate(pts):
+        a = pts[max(k - 1, 0)]
+        b = pts[min(k + 1, len(pts) - 1)]
+        tng = [y - x for x, y in zip(a, b)]
+        tn = math.sqrt(sum(x * x for x in tng)) or 1.0
+        tng = [x / tn for x in tng]
+        ref = prev_n or ([0.0, 1.0, 0.0] if abs(tng[1]) < 0.9 else [1.0, 0.0, 0.0])
+        nrm = _cross(_cross(tng, ref), tng)
+        nn = math.sqrt(sum(x * x for x in nrm)) or 1.0
+        nrm = [x / nn for x in nrm]
+        prev_n = nrm
+        bn = _cross(tng, nrm)
+        for j in range(rseg):
+            ang = 2 * math.pi * j / rseg
+            verts.append([pt[i] + radius * (math.cos(ang) * nrm[i] + math.sin(ang) * bn[i]) for i in range(3)])
+    for k in range(tseg):
+        for j in range(rseg):
+            a, b = k * rseg + j, k * rseg + (j + 1) % rseg
+            faces += [(a, b, b + rseg), (a, b + rseg, a + rseg)]
+    return torch.tensor(verts, dtype=torch.float32), torch.tensor(faces)
+
+
+def _extrude(pts, depth):
+    """Ear-clipped cap(s) plus side walls of a simple polygon in the xy plane, extruded along +z."""
+    import torch
+    poly = [tuple(p) for p in pts]
+    if len(poly) > 1 and poly[0] == poly[-1]:
+        poly = poly[:-1]
+    area = sum(poly[i][0] * poly[(i + 1) % len(poly)][1] - poly[(i + 1) % len(poly)][0] * poly[i][1]
+               for i in range(len(poly)))
+    if area < 0:
+        poly = poly[::-1]
+    tri = _ear_clip(poly)
+    n = len(poly)
+    verts = [(x, y, 0.0) for x, y in poly] + [(x, y, depth) for x, y in poly]
+    faces = [(c, b, a) for a, b, c in tri] + [(a + n, b + n, c + n) for a, b, c in tri]
+    if depth != 0.0:
+        for i in range(n):
+            j = (i + 1) % n
+            faces += [(i, j, j + n), (i, j + n, i + n)]
+    return torch.tensor(verts, dtype=torch.float32), torch.tensor(faces, dtype=torch.long)
+
+
+def _ear_clip(poly):
+    idx = list(range(len(poly)))
+    out = []
+
+    def inside(p, a, b, c):
+        def s(p1, p2, p3):
+            return (p1[0] - p3[0]) * (p2[1] - p3[1]) - (p2[0] - p3[0]) * (p1[1] - p3[1])
+        d1, d2, d3 = s(p, a, b), s(p, b, c), s(p, c, a)
+        return not ((d1 < 0 or d2 < 0 or d3 < 0) and (d1 > 0 or d2 > 0 or d3 > 0))
+
+    guard = 0
+    while len(idx) > 3 and guard < 10000:
+        guard += 1
+        for k in range(len(idx)):
+            i0, i1, i2 = idx[k - 1], idx[k], idx[(k + 1) % len(idx)]
+            a, b, c = poly[i0], poly[i1], poly[i2]
+            if (b[0] - a[0]) * (c[1] - a[1]) - (b[1] - a[1]) * (c[0] - a[0]) <= 0:
+                continue
+            if any(inside(poly[j], a, b, c) for j in idx if j not in (i0, i1, i2)):
+                continue
+            out.append((i0, i1, i2))
+            idx.pop(k)
+            break
+        else:
+            break
+    if len(idx) == 3:
+        out.append(tuple(idx))
+    return out
+
+
+@dataclass
+class ModuleResult:
+    root: Any = None
+    error: Optional[str] = None
+    steps: int = 0
+    seconds: float = 0.0
+    texture_bytes: int = 0
+
+
+def run_module(source: str, limits: Optional[Limits] = None, seed: int = 0) -> ModuleResult:
+    """Evaluate a module and call its default export with THREE. Never raises for JS-level failures."""
+    t0 = time.monotonic()
+    it = Interp(limits, seed)
+    try:
+        prog = Parser(source).program()
+        it.run_program(prog)
+        gen = it.exports.get("default")
+        if gen is None:
+            gen = it.exports.get("generate")
+        if gen is None:
+            ev = it.globals.lookup("generate")
+            gen = ev.vars["generate"] if ev is not None else None
+        if not isinstance(gen, (JSFunction, Native)):
+            return ModuleResult(error="NO_DEFAULT_EXPORT: module must `export default function generate(THREE)`",
+                                steps=it.steps, seconds=time.monotonic() - t0)
+        root = it.call(gen, UNDEF, [make_three(it)])
+        return ModuleResult(root=root, steps=it.steps, seconds=time.monotonic() - t0)
+    except JSBudget as e:
+        return ModuleResult(error=f"TIMEOUT: {e.msg}", steps=it.steps, seconds=time.monotonic() - t0)
+    except JSError as e:
+        return ModuleResult(error=f"{e.kind}: {e.msg}", steps=it.steps, seconds=time.monotonic() - t0)
+    except _Throw as e:
+        v = e.value
+        msg = f"{_to_str(v.props.get('name', 'Error'))}: {_to_str(v.props.get('message', ''))}" \
+            if isinstance(v, JSObject) and not isinstance(v, Host) else f"Uncaught {_to_str(v)}"
+        return ModuleResult(error=f"RUNTIME: {msg}", steps=it.steps, seconds=time.monotonic() - t0)
+    except (_Break, _Continue, _Return):
+        return ModuleResult(error="SyntaxError: illegal break/continue/return", steps=it.steps,
+                            seconds=time.monotonic() - t0)
+    except RecursionError:
+        return ModuleResult(error="RangeError: maximum call stack size exceeded", steps=it.steps,
+                            seconds=time.monotonic() - t0)
+
+
+def _col_major(m):
+    return [m[r][c] for c in range(4) for r in range(4)]
+
+
+def to_scene_json(root: Object3D, max_depth: int = 64) -> dict:
+    """Object3D tree -> the scene JSON of render/scene.py (geometries baked to BufferGeometry where needed)."""
+    geoms: Dict[int, dict] = {}
+    mats: Dict[int, dict] = {}
+
+    def geom_ref(g: Geometry) -> str:
+        key = id(g)
+        if key not in geoms:
+            v, f = geometry_mesh(g)
+            geoms[key] = {"uuid": g.id_ + f"-{len(geoms)}", "type": "BufferGeometry",
+                          "data": {"attributes": {"position": {"itemSize": 3, "type": "Float32Array",
+                                                               "array": v.reshape(-1).tolist()}},
+                                   "index": {"type": "Uint32Array", "array": f.reshape(-1).tolist()}}}
+        return geoms[key]["uuid"]
+
+    def mat_ref(m) -> Optional[str]:
+        if isinstance(m, JSArray):
+            m = next((x for x in m.items if isinstance(x, Material)), None)
+        if not isinstance(m, Material):
+            return None
+        key = id(m)
+        if key not in mats:
+            col = m.props.get("color")
+            mats[key] = {"uuid": f"m{len(mats)}", "type": m.mtype,
+                         "color": col.hex() if isinstance(col, Color) else 0xCCCCCC,
+                         "opacity": _to_num(m.props.get("opacity", 1.0))}
+        return mats[key]["uuid"]
+
+    def node(o: Object3D, depth: int) -> dict:
+        if depth > max_depth:
+            raise ValueError("scene depth limit exceeded")
+        d = {"uuid": o.id_, "type": o.otype, "matrix": _col_major(o.local()), "children": []}
+        if not _truthy(o.props.get("visible", True)):
+            d["visible"] = False
+            return d
+        g = o.props.get("geometry")
+        if isinstance(g, Geometry) and o.otype in ("Mesh", "InstancedMesh"):
+            gid, mid = geom_ref(g), mat_ref(o.props.get("material"))
+            if o.otype == "InstancedMesh":
+                count = int(_to_num(o.props.get("count", 0)))
+                inst = o.props.get("__inst", {})
+                for k in range(count):
+                    d["children"].append({"uuid": f"{o.id_}-{k}", "type": "Mesh", "geometry": gid, "material": mid,
+                                          "matrix": _col_major(inst.get(k, _ident4())), "children": []})
+            else:
+                d["geometry"], d["material"] = gid, mid
+        for c in o.children():
+            d["children"].append(node(c, depth + 1))
+        return d
+
+    obj = node(root, 0)
+    return {"metadata": {"version": 4.6, "type": "Object", "generator": "phung5_b200.app.jsvm"},
+            "geometries": list(geoms.values()), "materials": list(mats.values()), "object": obj}

@@ -1,0 +1,184 @@
+"""First-iteration stages: K coders at once -> dedup -> validate -> streaming single-elimination bracket ->
+optional round robin among the last four.
+
+Reference: `multigen_first_iter` (pipeline_service/pipeline/stages.py:1048-1217), `_CandidateFactory`
+(:702-950), `_resolve_bracket` (:589-677), `_round_robin_top4` (:320-427).
+
+- Leaves: position k runs coder k (coders are assigned round-robin over the configured coder pool, seed
+  `task.seed + k`), the checker, dedup by whitespace-insensitive code digest (the first position to reach
+  a digest keeps it), judge-view renders (white + gray) and view embeddings. A leaf that fails or
+  duplicates is a walkover for its opponent (no judge call).
+- Bracket: pairing is by position, independent of which leaves drop, so results are reproducible for a
+  seed. A duel starts as soon as both of its subtree winners are known, so judging overlaps coding and
+  rendering of other leaves.
+- Draws are settled by a coin keyed on (seed, stem, positions): reproducible, no bias toward a side.
+- Round robin: when enabled and the bracket had at least 4 live semifinalists, all 6 pairs of the last
+  four are judged; 1 point per win (a draw is settled by the coin first); ties go to the bracket winner.
+"""
+from __future__ import annotations
+
+import asyncio
+import hashlib
+import time
+from dataclasses import dataclass
+from typing import Awaitable, Callable, Dict, List, Optional, Sequence
+
+from .agents import JudgeAgent, SceneCoderAgent
+from .jscheck import code_digest
+from .renderer import RendererModule
+from .schemas import JudgeVerdict
+from .state import Candidate, PipelineTask
+
+
+def coin(seed: int, *keys) -> bool:
+    h = hashlib.sha256(repr((seed,) + keys).encode()).digest()
+    return h[0] & 1 == 1
+
+
+@dataclass
+class StageLimits:
+    coder: asyncio.Semaphore
+    judge: asyncio.Semaphore
+    render: asyncio.Semaphore
+
+
+class CandidateFactory:
+    """Builds one Candidate per bracket position (or None)."""
+
+    def __init__(self, task: PipelineTask, coders: Sequence[SceneCoderAgent], renderer: RendererModule, embedder,
+                 limits: StageLimits, prompt_url: str, plan: Optional[str] = None, deadline: Optional[float] = None,
+                 on_event: Optional[Callable[[str, dict], None]] = None):
+        self.task, self.coders, self.renderer, self.embedder = task, coders, renderer, embedder
+        self.limits, self.prompt_url, self.plan, self.deadline = limits, prompt_url, plan, deadline
+        self.seen: Dict[str, int] = {}
+        self.on_event = on_event or (lambda kind, d: None)
+
+    def _left(self) -> Optional[float]:
+        return None if self.deadline is None else self.deadline - time.monotonic()
+
+    async def build(self, k: int) -> Optional[Candidate]:
+        coder = self.coders[k % len(self.coders)]
+        t = self.task
+        try:
+            async with self.limits.coder:
+                left = self._left()
+                if left is not None and left <= 0:
+                    return None
+                res = await asyncio.wait_for(coder.generate(self.prompt_url, t.seed + k, plan=self.plan), left)
+        except (asyncio.TimeoutError, Exception) as e:  # noqa: BLE001 - a failed leaf is a walkover
+            t.js_errors.append(f"k{k} {coder.name}: {type(e).__name__}: {str(e)[:160]}")
+            self.on_event("coder_error", {"k": k})
+            return None
+        t.n_generated += 1
+        if not res.check.ok:
+            t.js_errors.append(f"k{k} {coder.name}: {res.check.summary()[:300]}")
+            self.on_event("invalid", {"k": k})
+            return None
+        t.n_valid += 1
+        dg = code_digest(res.check.code)
+        if dg in self.seen:
+            t.n_duplicates += 1
+            self.on_event("duplicate", {"k": k, "of": self.seen[dg]})
+            return None
+        self.seen[dg] = k
+        cand = Candidate(code=res.check.code, digest=dg, coder=coder.name, scene=res.check.scene,
+                         stats={**res.check.stats, "k": k, "repairs": res.repairs})
+        try:
+            async with self.limits.render:
+                views = await self.renderer.judge_views(cand.scene, gray=True)
+        except (asyncio.TimeoutError, Exception) as e:  # noqa: BLE001
+            t.js_errors.append(f"k{k} render: {type(e).__name__}: {str(e)[:160]}")
+            self.on_event("render_error", {"k": k})
+            return None
+        cand.views, cand.gray_views = views["white"], views.get("gray", [])
+        if self.embedder is not None:
+            cand.embed = await self.embedder.embed(cand.views)
+        t.candidates.append(cand)
+        if t.js_code is None:          # something to salvage if the deadline hits before any duel
+            t.js_code, t.scene_json, t.lead_round = cand.code, cand.scene, 0
+        self.on_event("candidate", {"k": k})
+        return cand
+
+
+DuelFn = Callable[[Candidate, Candidate, str], Awaitable[Candidate]]
+
+
+def make_duel(task: PipelineTask, judge: JudgeAgent, limits: StageLimits, prompt_url: str, ref_vec,
+              on_duel: Optional[Callable[[float, float], None]] = None) -> DuelFn:
+    async def duel(left: Candidate, right: Candidate, label: str) -> Candidate:
+        tq = time.monotonic()
+        async with limits.judge:
+            ts = time.monotonic()
+            v: JudgeVerdict = await judge.duel(prompt_url, left, right, task.seed, ref_vec)
+        te = time.monotonic()
+        if on_duel is not None:
+            on_duel(te - ts, ts - tq)
+        task.duels += 1
+        if v.winner == "draw":
+            w = left if coin(task.seed, task.stem, label, left.digest, right.digest) else right
+            how = f"{v.decided_by} -> coin"
+        else:
+            w = left if v.winner == "A" else right
+            how = v.decided_by
+        task.judge_log.append({"label": label, "left": left.stats.get("k"), "right": right.stats.get("k"),
+                               "winner": w.stats.get("k"), "decided_by": how, "verdict": v.winner})
+        w.wins += 1
+        rnd = int(label[1:].split()[0]) if label.startswith("R") and label[1:2].isdigit() else 0
+        if rnd >= task.lead_round:     # the deepest bracket winner so far leads (salvage)
+            task.js_code, task.scene_json, task.lead_round = w.code, w.scene, rnd
+        return w
+    return duel
+
+
+async def resolve_bracket(leaves: Dict[int, "asyncio.Future"], duel: DuelFn, n: int) -> tuple:
+    """-> (winner or None, the live winners of the bracket's four quarter subtrees when n >= 4)."""
+    semis: List[Candidate] = []
+
+    async def winner_of(lo: int, hi: int, depth: int) -> Optional[Candidate]:
+        if hi - lo <= 1:
+            res = await leaves[lo]
+        else:
+            mid = (lo + hi) // 2
+            left, right = await asyncio.gather(winner_of(lo, mid, depth + 1), winner_of(mid, hi, depth + 1))
+            if left is None:
+                res = right
+            elif right is None:
+                res = left
+            else:
+                rnd = (hi - lo - 1).bit_length()
+                res = await duel(left, right, f"R{rnd} {lo}-{hi}")
+        if depth == 2 and res is not None:
+            semis.append(res)
+        return res
+
+    if n == 0:
+        return None, []
+    w = await winner_of(0, n, 0)
+    return w, semis
+
+
+async def round_robin(cands: List[Candidate], duel: DuelFn, bracket_winner: Candidate) -> Candidate:
+    pts = {id(c): 0.0 for c in cands}
+    pairs = [(a, b) for i, a in enumerate(cands) for b in cands[i + 1:]]
+    winners = await asyncio.gather(*(duel(a, b, f"RR {a.stats.get('k')}-{b.stats.get('k')}") for a, b in pairs))
+    for w in winners:
+        pts[id(w)] += 1.0
+    for c in cands:
+        c.rr_points = pts[id(c)]
+    best = max(pts.values())
+    top = [c for c in cands if pts[id(c)] == best]
+    return bracket_winner if any(c is bracket_winner for c in top) else top[0]
+
+
+async def multigen_first_iter(task: PipelineTask, factory: CandidateFactory, duel: DuelFn, k: int,
+                              use_round_robin: bool = False) -> Optional[Candidate]:
+    leaves = {i: asyncio.ensure_future(factory.build(i)) for i in range(k)}
+    try:
+        winner, semis = await resolve_bracket(leaves, duel, k)
+    finally:
+        for f in leaves.values():
+            if not f.done():
+                f.cancel()
+    if winner is not None and use_round_robin and len(semis) >= 4:
+        winner = await round_robin(semis[:4], duel, winner)
+    return winner
