@@ -395,16 +395,39 @@ class CheckerSettings:
     max_steps: int = 20_000_000
     repair: bool = True
     workers: int = 4
+    processes: bool = False          # a process pool (true parallelism) instead of threads
+    pin_reserve: int = 14            # process pool: leave this many CPUs of the quota to the rest of the host
+
+
+def _check_in_process(settings: "CheckerSettings", text: str, seed: int) -> "CheckResult":
+    return JSChecker(settings, _inline=True).check(text, seed)
+
+
+def _pin_worker(cpus):
+    from ..utils.affinity import pin_current_process
+    pin_current_process(cpus)
 
 
 class JSChecker:
-    """check(code) -> CheckResult; check_async runs in a worker thread pool (the interpreter holds no
-    shared state, every call builds its own)."""
+    """check(code) -> CheckResult. check_async runs in a pool: threads by default (the interpreter keeps no
+    shared state, every call builds its own), or processes pinned to the CPU set of
+    `utils.affinity.worker_cpus` so checks run in parallel without taking the engines' cores."""
 
-    def __init__(self, settings: Optional[CheckerSettings] = None):
+    def __init__(self, settings: Optional[CheckerSettings] = None, _inline: bool = False):
         self.s = settings or CheckerSettings()
-        self._pool = ThreadPoolExecutor(max_workers=self.s.workers, thread_name_prefix="jscheck")
         self.counts = {"checked": 0, "passed": 0}
+        self._pool = None
+        if _inline:
+            return
+        if self.s.processes:
+            import multiprocessing as mp
+            from concurrent.futures import ProcessPoolExecutor
+            from ..utils.affinity import worker_cpus
+            cpus = worker_cpus(reserve=self.s.pin_reserve)
+            self._pool = ProcessPoolExecutor(max_workers=self.s.workers, mp_context=mp.get_context("spawn"),
+                                             initializer=_pin_worker, initargs=(cpus,))
+        else:
+            self._pool = ThreadPoolExecutor(max_workers=self.s.workers, thread_name_prefix="jscheck")
 
     def check(self, text: str, seed: int = 0) -> CheckResult:
         self.counts["checked"] += 1
@@ -441,7 +464,13 @@ class JSChecker:
 
     async def check_async(self, text: str, seed: int = 0) -> CheckResult:
         loop = asyncio.get_running_loop()
+        if self.s.processes:
+            self.counts["checked"] += 1
+            r = await loop.run_in_executor(self._pool, _check_in_process, self.s, text, seed)
+            self.counts["passed"] += int(r.ok)
+            return r
         return await loop.run_in_executor(self._pool, self.check, text, seed)
 
     def close(self):
-        self._pool.shutdown(wait=False, cancel_futures=True)
+        if self._pool is not None:
+            self._pool.shutdown(wait=False, cancel_futures=True)

@@ -208,3 +208,21 @@ class LoadBalancedClient:
             return r.json()
         finally:
             self.inflight[i] -= 1
+
+
+def main(argv=None):
+    """python -m phung5_b200.serve.router --port 8001 --upstream http://127.0.0.1:8101 --upstream ..."""
+    import argparse
+
+    import uvicorn
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, required=True)
+    ap.add_argument("--upstream", action="append", required=True)
+    ap.add_argument("--drain-timeout", type=float, default=120.0)
+    args = ap.parse_args(argv)
+    uvicorn.run(build_proxy(args.upstream, args.drain_timeout), host=args.host, port=args.port, log_level="warning")
+
+
+if __name__ == "__main__":
+    main()

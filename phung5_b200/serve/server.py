@@ -15,6 +15,7 @@ per-request streams. Endpoints mirror what the reference's clients use of SGLang
   POST /release_memory_occupation, /resume_memory_occupation   (SGLang names, same actions)
 
     python -m phung5_b200.serve.server --model llama3-8b --port 8001 [--spec tree] [--device cuda]
+    torchrun --nproc-per-node 8 -m phung5_b200.serve.server --model llama3-70b-fp8   (tensor parallel; rank 0 serves)
 """
 from __future__ import annotations
 
@@ -46,10 +47,18 @@ class _Pending:
 
 
 class AsyncEngine:
-    """Drives an LLMEngine from a background thread; thread-safe submission, asyncio streams out."""
+    """Drives an LLMEngine from a background thread; thread-safe submission, asyncio streams out.
 
-    def __init__(self, engine, metrics: Optional[EngineMetrics] = None):
+    Tensor parallel serving: with `group` (a gloo process group over the TP ranks) this thread runs on
+    rank 0 and, every loop iteration, broadcasts what it is about to apply (control ops, new requests and
+    its step count) to the other ranks, which run `tp_worker_loop`; every rank then applies the same
+    commands and takes the same engine step, so the replicated scheduler state never diverges. When idle,
+    the broadcast is a heartbeat every 50 ms."""
+
+    def __init__(self, engine, metrics: Optional[EngineMetrics] = None, group=None):
         self.engine = engine
+        self.group = group
+        self.steps = 0
         self.metrics = metrics or EngineMetrics()
         self._submit: "queue.Queue[_Pending]" = queue.Queue()
         self._control: "queue.Queue" = queue.Queue()
@@ -65,21 +74,27 @@ class AsyncEngine:
         eng = self.engine
         while not self._stop:
             try:
+                ops, subs = [], []
                 while True:
                     try:
-                        op, fut, loop = self._control.get_nowait()
+                        ops.append(self._control.get_nowait())
                     except queue.Empty:
                         break
+                while True:
+                    try:
+                        subs.append(self._submit.get_nowait())
+                    except queue.Empty:
+                        break
+                if self.group is not None:
+                    _broadcast_cmds({"ops": [o[0] for o in ops], "reqs": [(p.prompt, p.params) for p in subs],
+                                     "steps": self.steps, "stop": False}, self.group)
+                for op, fut, loop in ops:
                     try:
                         getattr(eng, op)()
                         loop.call_soon_threadsafe(fut.set_result, True)
                     except Exception as e:  # pragma: no cover - surfaced to the caller
                         loop.call_soon_threadsafe(fut.set_exception, e)
-                while True:
-                    try:
-                        p = self._submit.get_nowait()
-                    except queue.Empty:
-                        break
+                for p in subs:
                     p.rid = eng.add_request(p.prompt, p.params)
                     self._streams[p.rid] = p
                 if not eng.has_work():
@@ -88,6 +103,7 @@ class AsyncEngine:
                     continue
                 t0 = time.perf_counter()
                 outs = eng.step()
+                self.steps += 1
                 dt = time.perf_counter() - t0
                 self.metrics.observe_step(dt, outs, eng)
                 for o in outs:
@@ -132,6 +148,33 @@ class AsyncEngine:
         self._stop = True
         self._wake.set()
         self._thread.join(timeout=5)
+        if self.group is not None:
+            _broadcast_cmds({"ops": [], "reqs": [], "steps": self.steps, "stop": True}, self.group)
+
+
+def _broadcast_cmds(cmds: Optional[dict], group) -> dict:
+    import torch.distributed as dist
+    box = [cmds]
+    dist.broadcast_object_list(box, src=0, group=group)
+    return box[0]
+
+
+def tp_worker_loop(engine, group) -> None:
+    """Ranks 1..TP-1 of a tensor-parallel server: apply rank 0's commands, take the same steps."""
+    steps = 0
+    while True:
+        cmds = _broadcast_cmds(None, group)
+        if cmds["stop"]:
+            return
+        if cmds["steps"] != steps:
+            raise RuntimeError(f"TP ranks diverged: rank 0 took {cmds['steps']} steps, this rank {steps}")
+        for op in cmds["ops"]:
+            getattr(engine, op)()
+        for prompt, params in cmds["reqs"]:
+            engine.add_request(prompt, params)
+        if engine.has_work():
+            engine.step()
+            steps += 1
 
 
 def _sampling(body: dict, default_max: int = 256) -> SamplingParams:
@@ -244,17 +287,37 @@ def main(argv=None):
     ap.add_argument("--spec", default="tree", choices=["off", "chain", "tree"])
     ap.add_argument("--tokenizer", default=None)
     ap.add_argument("--num-pages", type=int, default=0)
+    ap.add_argument("--comm", default="fused", choices=["nccl", "fused"],
+                    help="tensor-parallel collectives when launched with torchrun over several GPUs")
     args = ap.parse_args(argv)
+    import os
+
     import uvicorn
-    from ..config import CacheConfig, DraftConfig, EngineConfig, SpecConfig, preset
+    from ..config import CacheConfig, DraftConfig, EngineConfig, ParallelConfig, SpecConfig, preset
     from ..engine.engine import LLMEngine
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    comm, group, device = None, None, args.device
+    if world > 1:
+        import torch.distributed as dist
+        from ..parallel.comm import NcclCommunicator, init_distributed
+        rank, world, local = init_distributed()
+        device = f"cuda:{local}"
+        comm = NcclCommunicator()
+        if args.comm == "fused":
+            from ..parallel.fused import FusedCommunicator
+            comm = FusedCommunicator()
+        group = dist.new_group(backend="gloo")
     spec = SpecConfig(enabled=args.spec != "off", mode=args.spec if args.spec != "off" else "chain")
     cfg = EngineConfig(model=preset(args.model), spec=spec, draft=DraftConfig(kind="eagle"),
-                       cache=CacheConfig(num_pages=args.num_pages))
-    eng = LLMEngine(cfg, device=args.device)
-    aeng = AsyncEngine(eng)
+                       cache=CacheConfig(num_pages=args.num_pages), parallel=ParallelConfig(tp=world, comm=args.comm))
+    eng = LLMEngine(cfg, device=device, comm=comm)
+    if group is not None and comm.rank != 0:
+        tp_worker_loop(eng, group)
+        return
+    aeng = AsyncEngine(eng, group=group)
     uvicorn.run(build_app(aeng, __import__("phung5_b200.serve.tokenizer", fromlist=["load_tokenizer"]).load_tokenizer(
         args.tokenizer), args.model), host=args.host, port=args.port, log_level="warning")
+    aeng.shutdown()
 
 
 if __name__ == "__main__":

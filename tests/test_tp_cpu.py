@@ -112,3 +112,69 @@ def test_tp2_fused_forward_plumbing_matches_oracle():
     ref = RefModel(preset("tiny"), random_weights(preset("tiny"), seed=0, std=0.05))
     for p, o in zip(prompts, outs):
         assert o == greedy_generate(ref, p, 12)
+
+
+def _serve_worker(rank, world, port, q):
+    """Rank 0 drives AsyncEngine (the HTTP server's engine thread) with two concurrent requests; rank 1 runs
+    the TP worker loop. Both must take identical steps and rank 0's streams must equal the oracle."""
+    import asyncio
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from phung5_b200.engine.engine import LLMEngine
+        from phung5_b200.engine.oracle import SamplingParams
+        from phung5_b200.models.llama import pack_weights
+        from phung5_b200.parallel.comm import NcclCommunicator
+        from phung5_b200.serve.server import AsyncEngine, tp_worker_loop
+        from phung5_b200.weights.init import random_weights
+        tcfg, dcfg = preset("tiny"), preset("tiny-draft")
+        tw = random_weights(tcfg, seed=0, std=0.05)
+        dw = random_weights(dcfg, seed=1, std=0.05)
+        comm = NcclCommunicator()
+        group = dist.new_group(backend="gloo")
+        ecfg = EngineConfig(model=tcfg, spec=SpecConfig(mode="tree", tree_nodes=10, topk=3, depth=3),
+                            draft=DraftConfig(kind="model"), cache=CacheConfig(page_size=16, num_pages=200))
+        eng = LLMEngine(ecfg, device="cpu", target=pack_weights(tcfg, tw, "cpu", rank, world, dtype=torch.float32),
+                        drafter=pack_weights(dcfg, dw, "cpu", rank, world, dtype=torch.float32), comm=comm,
+                        dtype=torch.float32, max_context=1024)
+        if rank != 0:
+            tp_worker_loop(eng, group)
+            q.put((rank, None, None))
+            return
+        g = torch.Generator().manual_seed(5)
+        prompts = [torch.randint(0, 4096, (30,), generator=g).tolist() for _ in range(2)]
+        aeng = AsyncEngine(eng, group=group)
+
+        async def one(p):
+            toks = []
+            async for o in aeng.generate(p, SamplingParams(max_new_tokens=12)):
+                toks += o.new_tokens
+            return toks
+
+        async def both():
+            return await asyncio.gather(*(one(p) for p in prompts))
+        outs = asyncio.run(both())
+        aeng.shutdown()
+        q.put((rank, outs, prompts))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_server_loop_matches_oracle():
+    from phung5_b200.engine.oracle import greedy_generate
+    from phung5_b200.models.reference import RefModel
+    from phung5_b200.weights.init import random_weights
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_serve_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=180) for _ in procs], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+    assert all(p.exitcode == 0 for p in procs)
+    outs, prompts = res[0][1], res[0][2]
+    ref = RefModel(preset("tiny"), random_weights(preset("tiny"), seed=0, std=0.05))
+    for p, o in zip(prompts, outs):
+        assert o == greedy_generate(ref, p, 12)
