@@ -1,0 +1,167 @@
+"""Kernel self-test: every sm_100a kernel against its plain-torch definition on small shapes.
+
+The reference's patch kits each carry a `--check` (compile, import probe, GPU bitwise self-test) with
+distinct exit codes (e.g. docker/opt/v5/topkbf_normcfg/topkbf/apply_topkbf.py). Here the kernels are part
+of the package, so one command checks them all on the current GPU:
+
+    python -m phung5_b200.ops.selftest [--json out.json]
+exit 0: all pass; 7: a kernel disagrees with its definition; 8: the extension is missing or no GPU.
+Each check uses the same tolerance as the test suite and reports its error metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import sys
+import time
+from typing import Callable, Dict, List, Tuple
+
+import torch
+
+
+def _rel(a, b) -> float:
+    a, b = a.float().cpu(), b.float().cpu()
+    return ((a - b).norm() / b.norm().clamp(min=1e-12)).item()
+
+
+def _checks() -> List[Tuple[str, Callable[[], Tuple[bool, float]]]]:
+    from .. import ops
+    from ..weights.quant import dequant_act_block, gemm_fp8_block_ref, quant_act_block, quant_weight_block
+    dev = "cuda"
+
+    def gemm_fp8():
+        x = torch.randn(200, 512, device=dev)
+        w = torch.randn(384, 512, device=dev) * 0.05
+        xq, xs = quant_act_block(x)
+        wq, ws = quant_weight_block(w)
+        e = _rel(ops.gemm_fp8_block(xq, xs, wq, ws), gemm_fp8_block_ref(xq, xs, wq, ws))
+        return e < 5e-3, e
+
+    def gemm_bf16():
+        x = torch.randn(300, 1024, device=dev).bfloat16()
+        w = (torch.randn(640, 1024, device=dev) * 0.05).bfloat16()
+        e = _rel(ops.gemm_bf16(x, w), x.float() @ w.float().t())
+        return e < 5e-3, e
+
+    def gemm_grouped():
+        sizes = [100, 0, 37]
+        x = torch.randn(sum(sizes), 256, device=dev)
+        xq, xs = quant_act_block(x)
+        ws_, ss_ = zip(*[quant_weight_block(torch.randn(256, 256, device=dev) * 0.05) for _ in sizes])
+        off = torch.tensor([0, 100, 100, 137], dtype=torch.int32, device=dev)
+        out = ops.gemm_grouped((xq, xs), torch.cat(ws_), torch.cat(ss_), off, 256)
+        errs = [_rel(out[a:b], gemm_fp8_block_ref(xq[a:b], xs[:, a:b].contiguous(), ws_[g], ss_[g]))
+                for g, (a, b) in enumerate([(0, 100), (100, 100), (100, 137)]) if b > a]
+        return max(errs) < 5e-3, max(errs)
+
+    def norm_quant():
+        h = torch.randn(33, 1024, device=dev).bfloat16()
+        d = torch.randn(33, 1024, device=dev).bfloat16()
+        w = (1 + 0.1 * torch.randn(1024, device=dev)).bfloat16()
+        hf = (h.float() + d.float()).bfloat16().float()
+        q, s, y = ops.add_rmsnorm_quant(h, d, w, 1e-5, quant=True, out_bf16=True)
+        ref = hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-5) * w.float()
+        e = max(_rel(y, ref), _rel(dequant_act_block(q, s), ref))
+        return e < 4e-2, e
+
+    def silu_quant():
+        gu = torch.randn(37, 2 * 512, device=dev).bfloat16()
+        q, s, y = ops.silu_mul_quant(gu, quant=True, out_bf16=True)
+        ref = torch.nn.functional.silu(gu[:, :512].float()) * gu[:, 512:].float()
+        e = max(_rel(y, ref), _rel(dequant_act_block(q, s), ref))
+        return e < 4e-2, e
+
+    def topk():
+        x = (torch.randn(64, 32000, device=dev) * 2).bfloat16()
+        lp, idx, lse = ops.topk_logprobs(x, 8, temperature=0.7)
+        xf = x.float() / 0.7
+        rl = torch.logsumexp(xf, -1)
+        rv, _ = torch.topk(xf, 8, dim=-1)
+        e = max((lse - rl).abs().max().item(), (lp - (rv - rl[:, None])).abs().max().item())
+        ok = e < 1e-3 and torch.equal(xf.gather(1, idx), rv)
+        return ok, e
+
+    def attention():
+        from ..engine.attn_meta import build_items, make_meta, pack_work
+        g = torch.Generator().manual_seed(0)
+        hq, hkv, d, ps = 8, 2, 128, 64
+        q_lens, prefix = [40, 9], [150, 64]
+        need = [(p + n + ps - 1) // ps for p, n in zip(prefix, q_lens)]
+        perm = torch.randperm(sum(need) + 1, generator=g).tolist()
+        pages, k0 = [], 0
+        for n in need:
+            pages.append(perm[k0:k0 + n])
+            k0 += n
+        kc = torch.randn(len(perm), hkv, ps, d, generator=g).bfloat16()
+        vc = torch.randn(len(perm), hkv, ps, d, generator=g).bfloat16()
+        q = torch.randn(sum(q_lens), hq, d, generator=g).bfloat16()
+        scale = 1 / math.sqrt(d)
+        meta = make_meta(pages, prefix, q_lens, None, True, "cpu")
+        _, p2 = build_items(meta, hq // hkv)
+        ref = torch.zeros(q.shape[0], hq * d)
+        ops.paged_attention(q, kc, vc, meta, scale, out=ref, items=p2)
+        gm = make_meta(pages, prefix, q_lens, None, True, dev)
+        out = torch.zeros(q.shape[0], hq * d, device=dev, dtype=torch.bfloat16)
+        it, tl = pack_work(p2, hq // hkv, dev, rows=ops.attn_rows())
+        ops.paged_attention(q.to(dev), kc.to(dev), vc.to(dev), gm, scale, out=out, items=it, tiles=tl)
+        e = _rel(out, ref)
+        return e < 1e-2, e
+
+    def raster():
+        from ..render import scene as S
+        sc = {"geometries": [{"uuid": "g", "type": "BoxGeometry", "width": 1, "height": 0.6, "depth": 0.4}],
+              "materials": [{"uuid": "m", "color": 0x3366CC}],
+              "object": {"children": [{"geometry": "g", "material": "m"}]}}
+        tris, cols = S.scene_triangles(sc)
+        vp = S.view_projection(30, 20)
+        a = S.render(tris, cols, vp, 96)
+        b = S.render(tris.to(dev), cols.to(dev), vp, 96).cpu()
+        diff = (a.int() - b.int()).abs()
+        frac = (diff.amax(-1) > 1).float().mean().item()
+        return frac < 0.01, frac
+
+    return [("gemm_fp8_block", gemm_fp8), ("gemm_bf16", gemm_bf16), ("gemm_grouped", gemm_grouped),
+            ("add_rmsnorm_quant", norm_quant), ("silu_mul_quant", silu_quant), ("topk_logprobs", topk),
+            ("paged_attention", attention), ("raster", raster)]
+
+
+def run() -> Dict[str, dict]:
+    from .. import ops
+    out = {}
+    for name, fn in _checks():
+        t0 = time.perf_counter()
+        try:
+            ok, metric = fn()
+            torch.cuda.synchronize()
+            ops.check_status()
+            out[name] = {"ok": bool(ok), "metric": float(metric), "ms": round(1e3 * (time.perf_counter() - t0), 1)}
+        except Exception as e:  # noqa: BLE001 - reported per kernel
+            out[name] = {"ok": False, "error": f"{type(e).__name__}: {str(e)[:200]}"}
+    return out
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--json")
+    args = ap.parse_args(argv)
+    if not torch.cuda.is_available():
+        print("selftest: no CUDA device", file=sys.stderr)
+        return 8
+    try:
+        from .. import ops
+        ops.ext()
+    except Exception as e:  # noqa: BLE001
+        print(f"selftest: extension unavailable: {e}", file=sys.stderr)
+        return 8
+    res = run()
+    for k, v in res.items():
+        print(f"{k:20s} {'PASS' if v['ok'] else 'FAIL'} {v.get('metric', v.get('error'))}")
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump(res, f, indent=1)
+    return 0 if all(v["ok"] for v in res.values()) else 7
+
+
+if __name__ == "__main__":
+    sys.exit(main())

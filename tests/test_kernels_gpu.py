@@ -334,3 +334,9 @@ def test_rasterizer_matches_cpu_restatement():
         diff = (a.int() - b.int()).abs().amax(-1)
         # edge-coverage or last-bit differences (device FMA contraction vs host) on a few pixels only
         assert (diff > 2).float().mean().item() < 0.01
+
+
+def test_selftest_cli_passes():
+    from phung5_b200.ops import selftest
+    res = selftest.run()
+    assert all(v["ok"] for v in res.values()), res
