@@ -37,8 +37,11 @@ void gemm_fp8_grouped(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torc
                       torch::Tensor out, torch::Tensor status);
 void gemm_bf16_grouped(torch::Tensor x, torch::Tensor w, torch::Tensor offsets, torch::Tensor out,
                        torch::Tensor status);
-void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M, int64_t H, double eps, int64_t epoch,
-                torch::Tensor w, bool out_bf16, torch::Tensor status, std::vector<int64_t> offsets, int64_t s_ld);
+void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M, int64_t H, double eps,
+                torch::Tensor w, bool out_bf16, bool push_h, torch::Tensor status, std::vector<int64_t> offsets,
+                int64_t s_ld);
+void tp_allgather(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t nbytes, torch::Tensor status,
+                  std::vector<int64_t> offsets);
 void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
                    torch::Tensor state, torch::Tensor tok_start, torch::Tensor slot, double scale, torch::Tensor out,
                    bool write_state, c10::optional<torch::Tensor> st_k, c10::optional<torch::Tensor> st_v,
@@ -68,6 +71,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_attention_tc", &phx::paged_attention_tc);
   m.def("topk_logprobs", &phx::topk_logprobs);
   m.def("tp_ar_norm", &phx::tp_ar_norm);
+  m.def("tp_allgather", &phx::tp_allgather);
   m.def("gdn_recurrent", &phx::gdn_recurrent);
   m.def("gdn_fold", &phx::gdn_fold);
   m.def("gdn_gates", &phx::gdn_gates);

@@ -15,6 +15,13 @@
 //      every rank's outputs are complete when the kernel retires.
 // Every spin is bounded by a %globaltimer deadline; on expiry the kernel records kErrTimeoutPeer and
 // skips its work instead of hanging.
+// Epochs live on the device (a word next to the CTA counter): every CTA reads epoch = word + 1 at entry and
+// the last CTA stores it after the end barrier, so launches captured in a CUDA graph advance the barrier
+// protocol on every replay exactly as eager launches do.
+// The residual h is only read by the rank that owns a row, so it is pushed to the peers only when asked
+// (push_h: the last layer, when the caller needs the full pre-norm hidden state).
+// tp_allgather_kernel uses the same barriers to copy a small staging block of every rank into slot
+// [rank] of every peer's gather region (vocab-sharded top-k / argmax candidates).
 // The reference has no tensor parallelism (configuration.yaml: tensor_parallel_size 1 everywhere); this is
 // the fused "GEMM -> reduce-scatter -> +residual -> RMSNorm -> FP8 quant -> all-gather" path of the
 // B200 design (the all-gather pushes the quantized rows the next GEMM consumes).
@@ -30,9 +37,9 @@ struct TpArgs {
   const uint64_t* peer_base;  // [W] base address of every rank's workspace (device array)
   int rank, world, M, H;
   float eps;
-  uint32_t epoch;
   const __nv_bfloat16* w;     // norm weight [H], local
   int out_bf16;               // 0: fp8 q + scales, 1: bf16 y
+  int push_h;                 // 1: store the new residual rows into every rank's h (else only locally)
   int* status;
   // byte offsets inside the workspace
   uint64_t off_partial, off_h, off_y, off_q, off_s, off_flags, off_counter;
@@ -67,21 +74,49 @@ __device__ __forceinline__ bool wait_flags(const uint32_t* flags, int W, uint32_
   return fail == 0;
 }
 
+// end barrier: the last CTA of this rank's launch publishes slot [1][rank] to every peer, waits for all
+// peers' slot [1], then stores the epoch for the next launch (all CTAs of this launch have read it).
+__device__ __forceinline__ void end_barrier(uint8_t* mine, uint64_t off_flags, uint64_t off_counter, uint32_t epoch,
+                                            int W, int rank, const uint64_t* peer_base, int* status) {
+  __shared__ int is_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    unsigned int* cnt = reinterpret_cast<unsigned int*>(mine + off_counter);
+    const unsigned int old = atomicAdd(cnt, 1u);
+    is_last = old == gridDim.x - 1;
+    if (is_last) *cnt = 0;  // the next launch starts after this one retires
+  }
+  __syncthreads();
+  if (is_last) {
+    uint32_t* my_flags = reinterpret_cast<uint32_t*>(mine + off_flags);
+    if (threadIdx.x < W) {
+      __threadfence_system();
+      st_release_sys(reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(peer_base[threadIdx.x]) + off_flags) +
+                         W + rank,
+                     epoch);
+    }
+    wait_flags(my_flags + W, W, epoch, status);
+    if (threadIdx.x == 0) reinterpret_cast<volatile uint32_t*>(mine + off_counter)[1] = epoch;
+  }
+}
+
 template <int MAXC>
 __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
   __shared__ float red[32];
-  __shared__ int is_last;
   const int W = a.world;
   auto base = [&](int p) { return reinterpret_cast<uint8_t*>(a.peer_base[p]); };
   uint8_t* mine = base(a.rank);
   uint32_t* my_flags = reinterpret_cast<uint32_t*>(mine + a.off_flags);
+  uint32_t* epoch_word = reinterpret_cast<uint32_t*>(mine + a.off_counter) + 1;
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(epoch_word) + 1u;
 
   // ---- 1. start barrier ----
   if (blockIdx.x == 0 && threadIdx.x < W) {
     __threadfence_system();
-    st_release_sys(reinterpret_cast<uint32_t*>(base(threadIdx.x) + a.off_flags) + a.rank, a.epoch);
+    st_release_sys(reinterpret_cast<uint32_t*>(base(threadIdx.x) + a.off_flags) + a.rank, epoch);
   }
-  const bool ok = wait_flags(my_flags, W, a.epoch, a.status);
+  const bool ok = wait_flags(my_flags, W, epoch, a.status);
 
   // ---- 2./3. reduce my rows, normalize, push to every rank ----
   const int H = a.H, nch = H / 8;
@@ -123,7 +158,10 @@ __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
           ss += r.x * r.x + r.y * r.y;
         }
         const uint4 out = make_uint4(nh[0], nh[1], nh[2], nh[3]);
-        for (int p = 0; p < W; ++p) *reinterpret_cast<uint4*>(base(p) + a.off_h + off) = out;
+        if (a.push_h)
+          for (int p = 0; p < W; ++p) *reinterpret_cast<uint4*>(base(p) + a.off_h + off) = out;
+        else
+          *reinterpret_cast<uint4*>(mine + a.off_h + off) = out;
       }
     }
     // RMSNorm statistics
@@ -181,27 +219,12 @@ __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
     }
   }
 
-  // ---- 4. end barrier (last CTA of this rank) ----
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    unsigned int* cnt = reinterpret_cast<unsigned int*>(mine + a.off_counter);
-    const unsigned int old = atomicAdd(cnt, 1u);
-    is_last = old == gridDim.x - 1;
-    if (is_last) *cnt = 0;  // the next launch starts after this one retires
-  }
-  __syncthreads();
-  if (is_last) {
-    if (threadIdx.x < W) {
-      __threadfence_system();
-      st_release_sys(reinterpret_cast<uint32_t*>(base(threadIdx.x) + a.off_flags) + W + a.rank, a.epoch);
-    }
-    wait_flags(my_flags + W, W, a.epoch, a.status);
-  }
+  end_barrier(mine, a.off_flags, a.off_counter, epoch, W, a.rank, a.peer_base, a.status);
 }
 
-void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M, int64_t H, double eps, int64_t epoch,
-                torch::Tensor w, bool out_bf16, torch::Tensor status, std::vector<int64_t> offsets, int64_t s_ld) {
+void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M, int64_t H, double eps,
+                torch::Tensor w, bool out_bf16, bool push_h, torch::Tensor status, std::vector<int64_t> offsets,
+                int64_t s_ld) {
   TORCH_CHECK(peer_base.is_cuda() && peer_base.scalar_type() == at::kLong && peer_base.numel() == world);
   TORCH_CHECK(H % 128 == 0 && world >= 1 && world <= 32 && offsets.size() == 7);
   if (M == 0) return;
@@ -214,9 +237,9 @@ void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M,
   a.M = (int)M;
   a.H = (int)H;
   a.eps = (float)eps;
-  a.epoch = (uint32_t)epoch;
   a.w = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   a.out_bf16 = out_bf16 ? 1 : 0;
+  a.push_h = push_h ? 1 : 0;
   a.status = status.data_ptr<int>();
   a.off_partial = offsets[0];
   a.off_h = offsets[1];
@@ -234,6 +257,58 @@ void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M,
   else if (maxc <= 4) tp_ar_norm_kernel<4><<<grid, 256, 0, stream>>>(a);
   else if (maxc <= 8) tp_ar_norm_kernel<8><<<grid, 256, 0, stream>>>(a);
   else TORCH_CHECK(false, "hidden size too large");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+struct GatherArgs {
+  const uint64_t* peer_base;
+  int rank, world;
+  int64_t n16;                // 16-byte words per rank
+  uint64_t off_src, off_dst, off_flags, off_counter;
+  int* status;
+};
+
+// copy this rank's staging block [n16 x 16 B] into slot [rank] of every rank's gather region
+__global__ void __launch_bounds__(256) tp_allgather_kernel(const GatherArgs a) {
+  const int W = a.world;
+  auto base = [&](int p) { return reinterpret_cast<uint8_t*>(a.peer_base[p]); };
+  uint8_t* mine = base(a.rank);
+  uint32_t* my_flags = reinterpret_cast<uint32_t*>(mine + a.off_flags);
+  const uint32_t epoch = reinterpret_cast<volatile uint32_t*>(mine + a.off_counter)[1] + 1u;
+  if (blockIdx.x == 0 && threadIdx.x < W) {
+    __threadfence_system();
+    st_release_sys(reinterpret_cast<uint32_t*>(base(threadIdx.x) + a.off_flags) + a.rank, epoch);
+  }
+  // start barrier: every peer has finished reading its gather region from the previous exchange
+  const bool ok = wait_flags(my_flags, W, epoch, a.status);
+  if (ok) {
+    const uint4* src = reinterpret_cast<const uint4*>(mine + a.off_src);
+    const uint64_t dst_off = a.off_dst + (uint64_t)a.rank * (uint64_t)a.n16 * 16u;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.n16; i += (int64_t)gridDim.x * blockDim.x) {
+      const uint4 v = src[i];
+      for (int p = 0; p < W; ++p) reinterpret_cast<uint4*>(base(p) + dst_off)[i] = v;
+    }
+  }
+  end_barrier(mine, a.off_flags, a.off_counter, epoch, W, a.rank, a.peer_base, a.status);
+}
+
+void tp_allgather(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t nbytes, torch::Tensor status,
+                  std::vector<int64_t> offsets) {
+  TORCH_CHECK(peer_base.is_cuda() && peer_base.numel() == world && offsets.size() == 4);
+  TORCH_CHECK(nbytes > 0 && nbytes % 16 == 0, "gather block must be a positive multiple of 16 bytes");
+  const at::cuda::CUDAGuard guard(peer_base.device());
+  GatherArgs a;
+  a.peer_base = reinterpret_cast<const uint64_t*>(peer_base.data_ptr<int64_t>());
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.n16 = nbytes / 16;
+  a.off_src = offsets[0];
+  a.off_dst = offsets[1];
+  a.off_flags = offsets[2];
+  a.off_counter = offsets[3];
+  a.status = status.data_ptr<int>();
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((a.n16 + 255) / 256, 64));
+  tp_allgather_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -251,6 +251,11 @@ class PageTables:
         for r, pl in enumerate(page_lists):
             self.padded[r, :len(pl)] = pl
 
+    def padded_device(self, device, dtype=torch.int64) -> torch.Tensor:
+        """[R, max pages] page table on the device (unused entries 0)."""
+        import numpy as np
+        return upload(torch.from_numpy(np.where(self.padded < 0, 0, self.padded)), dtype, device)
+
     def groups(self, committed: Sequence[int], min_shared_pages: int = 1, min_group: int = 2):
         """Consecutive requests sharing >= min_shared_pages committed pages: [(r_first, r_last, keys)]."""
         import numpy as np

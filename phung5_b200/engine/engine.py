@@ -90,6 +90,26 @@ class _VocabOps:
         return logits if self.comm.size == 1 else self.comm.all_gather_vocab(logits)
 
 
+class _EagerMeta:
+    """Attention metadata of the speculative step's forwards, built on the host per forward (page tables
+    shared by the step, per-forward lengths and work lists uploaded in one copy each)."""
+
+    def __init__(self, eng: "LLMEngine", tables: PageTables, groups, c_h: List[int]):
+        self.eng, self.tables, self.groups, self.c_h = eng, tables, groups, c_h
+
+    def draft(self, d: int, bits: torch.Tensor):
+        e, R = self.eng, len(self.c_h)
+        dmeta = self.tables.meta([ch + 1 for ch in self.c_h], [e.K] * R, bits, False)
+        # the draft scratch holds d*K entries after this round; keys [prefix, prefix + d*K)
+        dmeta.h_kv_len = [ch + 1 + d * e.K for ch in self.c_h]
+        return (dmeta,) + e._work(dmeta, self.groups)
+
+    def verify(self, tbits: torch.Tensor):
+        e, R = self.eng, len(self.c_h)
+        vmeta = self.tables.meta(self.c_h, [e.N] * R, tbits, False)
+        return (vmeta,) + e._work(vmeta, self.groups)
+
+
 class LLMEngine:
     def __init__(self, cfg: EngineConfig, device="cuda", target: Optional[ModelWeights] = None,
                  drafter=None, comm: Optional[Communicator] = None, num_pages: Optional[int] = None,
@@ -147,6 +167,11 @@ class LLMEngine:
         self.use_cascade = cfg.cache.enable_cascade
         import os as _os
         self._host_timing = _os.environ.get("PHX_HOST_TIMING") == "1"
+        # CUDA graphs of the speculative step (one per batch size): on by default on CUDA
+        self._graphs = {} if (self.device.type == "cuda" and _os.environ.get("PHX_GRAPHS", "1") != "0") else None
+        self._graph_cache = 4
+        self._has_moe = any(lw.moe is not None for lw in self.tw.layers)
+        self._consts: Dict[object, torch.Tensor] = {}
         self.host_times: Dict[str, float] = {}
         self._mark_name, self._mark_t = None, 0.0
 
@@ -454,17 +479,50 @@ class LLMEngine:
         scratch = 1 + (D - 1) * K
         for r in reqs:
             self._ensure_pages(r, r.committed + max(N, scratch) + 1)
-        maxp = max(len(r.pages) for r in reqs)
-        pt = self._h2d([r.pages + [0] * (maxp - len(r.pages)) for r in reqs], torch.int64)  # [R, maxp]
         c_h = [r.committed for r in reqs]
-        c = self._h2d(c_h, torch.int64)
-        ridx = torch.arange(R, device=dev)
-
-        def slots_of(pos):  # pos [R, n] (device) -> slots
-            return pt.gather(1, pos // self.ps) * self.ps + pos % self.ps
+        tables = PageTables([r.pages for r in reqs], dev, self.ps)
+        groups = (tables.groups(c_h) or None) if self.use_cascade else None
 
         self._mark("draft_catchup")
-        # ---- 1. draft catch-up: positions [dlen, committed] (root at `committed`) ----
+        logits, root_feat = self._catchup(reqs, tables, groups)
+        mode, ngeo_h = self._accept_mode(reqs)
+
+        graph = self._spec_graph(R, mode)
+        if graph is not None:
+            self._mark("graph_replay")
+            packed_dev = graph.run(reqs, tables, groups, c_h, logits, root_feat, ngeo_h)
+        else:
+            self._mark("draft_tree")
+            pt = tables.padded_device(dev)
+            c = upload(c_h, torch.int64, dev)
+            roots = upload([r.root for r in reqs], torch.int64, dev)
+            ngeo = upload(ngeo_h, torch.int64, dev) if ngeo_h is not None else None
+            packed_dev = self._spec_core(_EagerMeta(self, tables, groups, c_h), pt, c, roots, logits, root_feat,
+                                         mode, ngeo, reqs)
+
+        self._mark("commit_sync")
+        packed = packed_dev.cpu()
+        self.stats["d2h_bytes"] += packed.numel() * packed.element_size()
+        outs = []
+        for i, r in enumerate(reqs):
+            n = int(packed[i, 0])
+            new = [int(x) for x in packed[i, 1:1 + n]] + [int(packed[i, -1])]
+            r.tokens += new
+            r.committed += 1 + n
+            r.root = new[-1]
+            r.steps += 1
+            r.accepted.append(n)
+            self.stats["accepted"] += n
+            outs.append(self._emit(r, new))
+        self.stats["spec_steps"] += 1
+        self._mark("host_tail")
+        self._mark_name = None
+        return outs
+
+    def _catchup(self, reqs: List[Request], tables: "PageTables", groups):
+        """Draft forward over each request's positions [dlen, committed] (the root at `committed`): the
+        drafter's KV catches up with the tokens accepted last step. -> (logits [R, V_local] of the roots,
+        root features [R, H] or None)."""
         cu_tok, cu_pos, cu_slot, cu_hslot, last = [], [], [], [], []
         for r in reqs:
             for p in range(r.dlen, r.committed + 1):
@@ -473,22 +531,56 @@ class LLMEngine:
                 cu_slot.append(self._slot(r, p))
                 cu_hslot.append(self._slot(r, p - 1) if p > 0 else 0)
             last.append(len(cu_tok) - 1)
-        tables = PageTables([r.pages for r in reqs], dev, self.ps)
-        groups = (tables.groups(c_h) or None) if self.use_cascade else None
         meta = tables.meta([r.dlen for r in reqs], [r.committed + 1 - r.dlen for r in reqs], None, True)
         w1, w2 = self._work(meta, self._clip_groups(groups, [r.dlen for r in reqs]))
-        fb = ForwardBatch(tokens=self._h2d(cu_tok, torch.int64), positions=self._h2d(cu_pos, torch.int32),
-                          slots=self._h2d(cu_slot, torch.int64), meta=meta, work1=w1, work2=w2,
-                          logits_rows=self._h2d(last, torch.int64))
-        hid_in = self.pool.hidden[self._h2d(cu_hslot, torch.int64)] if self.eagle else None
+        packed = self._h2d(cu_tok + cu_slot + cu_hslot + last + cu_pos, torch.int64)
+        T, R = len(cu_tok), len(reqs)
+        fb = ForwardBatch(tokens=packed[:T], positions=packed[3 * T + R:].to(torch.int32), slots=packed[T:2 * T],
+                          meta=meta, work1=w1, work2=w2, logits_rows=packed[3 * T:3 * T + R])
+        hid_in = self.pool.hidden[packed[2 * T:3 * T]] if self.eagle else None
         logits, feat = self._draft_forward(fb, hid_in)
         for r in reqs:
             r.dlen = r.committed + 1
-        root_feat = feat[fb.logits_rows] if feat is not None else None
+        return logits, (feat[fb.logits_rows] if feat is not None else None)
 
-        synth = self.cfg.spec.accept == "geometric" and K > 1
-        self._mark("draft_tree")
-        # ---- 2. tree expansion ----
+    def _accept_mode(self, reqs: List[Request]):
+        """("geometric", accept lengths) | ("greedy", None) | ("sample", None)."""
+        spec = self.cfg.spec
+        if spec.accept == "geometric":
+            steps = torch.tensor([r.steps for r in reqs])
+            rid = torch.tensor([r.rid for r in reqs])
+            return "geometric", geometric_accept_len(spec.accept_seed, steps, rid, spec.accept_p, spec.accept_cap)
+        if all(r.params.temperature <= 0 for r in reqs):
+            return "greedy", None
+        return "sample", None
+
+    def _spec_graph(self, R: int, mode: str):
+        """The CUDA-graph runner for this batch shape, or None to run the step eagerly."""
+        if (self._graphs is None or mode == "sample" or self.K <= 1 or not self.eagle or self._has_moe
+                or (self.comm.size != 1 and not getattr(self.comm, "fused", False))):
+            return None
+        g = self._graphs.get(R)
+        if g is None:
+            from .spec_graph import SpecGraph
+            if len(self._graphs) >= self._graph_cache:
+                self._graphs.pop(next(iter(self._graphs)))
+            g = SpecGraph(self, R)
+            self._graphs[R] = g
+        return g
+
+    def _spec_core(self, mp, pt, c, roots, logits, root_feat, mode, ngeo, reqs=None):
+        """Tree expansion, selection, verification, acceptance and the KV move of one speculative step, on
+        device tensors only (no host synchronisation unless mode == "sample"). `mp` supplies the attention
+        metadata and work lists of the draft rounds and of verification. Returns packed [R, 2 + D] int64:
+        accepted count, accepted tokens (-1 padded), bonus token."""
+        dev = self.device
+        R, K, D, N = pt.shape[0], self.K, self.D, self.N
+
+        def slots_of(pos):  # pos [R, n] (device) -> slots
+            return pt.gather(1, pos // self.ps) * self.ps + pos % self.ps
+
+        synth = mode == "geometric" and K > 1
+        # ---- tree expansion ----
         lp, ti = self.dvocab.topk_logprobs(logits, K)          # [R, K]
         pool_tok, pool_score = [ti], [lp]
         pool_par = [torch.full((R, K), -1, dtype=torch.int64, device=dev)]
@@ -504,10 +596,7 @@ class LLMEngine:
             bits = front_bits_parent | (torch.ones_like(front_bits_parent) << sidx[None, :])
             pos = (c[:, None] + d).expand(R, K)
             sl = slots_of(c[:, None] + 1 + sidx[None, :])
-            dmeta = tables.meta([ch + 1 for ch in c_h], [K] * R, bits.reshape(-1), False)
-            # draft scratch holds d*K entries after this round; keys [prefix, prefix + d*K)
-            dmeta.h_kv_len = [ch + 1 + d * K for ch in c_h]
-            dw1, dw2 = self._work(dmeta, groups)
+            dmeta, dw1, dw2 = mp.draft(d, bits.reshape(-1))
             fb = ForwardBatch(tokens=front_tok.reshape(-1), positions=pos.reshape(-1).to(torch.int32),
                               slots=sl.reshape(-1), meta=dmeta, work1=dw1, work2=dw2)
             lg, fe = self._draft_forward(fb, front_feat.reshape(R * K, -1) if front_feat is not None else None)
@@ -543,12 +632,12 @@ class LLMEngine:
         P_depth = torch.cat(pool_depth, 1)
 
         self._mark("select")
-        # ---- 3. select the verify tree ----
+        # ---- select the verify tree ----
         nsel = N - 1
         adj = P_score - 1e-4 * P_depth.float()
         if synth:
             # spine nodes (best child of the spine at every depth) are pool entries 0, K, K+K*K, ...
-            spine = upload([0] + [K + (d - 1) * K * K for d in range(1, D)], torch.int64, dev)
+            spine = self._spine_index(dev)
             adj = adj.index_fill(1, spine, 0.0) + torch.zeros_like(adj).index_fill(1, spine, 1e6)
         _, sel = torch.topk(adj, nsel, dim=-1)
         key = P_depth.gather(1, sel).float() * 1e4 - adj.gather(1, sel)
@@ -561,7 +650,6 @@ class LLMEngine:
                             torch.where(par_pool < 0, torch.zeros_like(par_pool),
                                         node_of.gather(1, par_pool.clamp(min=0)))], 1)      # [R, N]
         depth = torch.cat([torch.zeros(R, 1, dtype=torch.int64, device=dev), P_depth.gather(1, sel)], 1)
-        roots = self._h2d([r.root for r in reqs], torch.int64)
         tokens = torch.cat([roots[:, None], P_tok.gather(1, sel)], 1)
         nb = torch.ones(R, N, dtype=torch.int64, device=dev) << torch.arange(N, device=dev)[None, :]
         tbits = nb.clone()
@@ -570,11 +658,10 @@ class LLMEngine:
             tbits = torch.where(depth == dd, pb | nb, tbits)
 
         self._mark("verify")
-        # ---- 4. verify ----
+        # ---- verify ----
         vpos = c[:, None] + depth
         vslot = slots_of(c[:, None] + torch.arange(N, device=dev)[None, :])
-        vmeta = tables.meta(c_h, [N] * R, tbits.reshape(-1), False)
-        vw1, vw2 = self._work(vmeta, groups)
+        vmeta, vw1, vw2 = mp.verify(tbits.reshape(-1))
         fb = ForwardBatch(tokens=tokens.reshape(-1), positions=vpos.reshape(-1).to(torch.int32),
                           slots=vslot.reshape(-1), meta=vmeta, work1=vw1, work2=vw2)
         vlogits, vh = self.target.forward(fb, want_hidden=self.eagle)
@@ -582,65 +669,63 @@ class LLMEngine:
             self.pool.hidden[fb.slots] = vh
 
         self._mark("accept")
-        # ---- 5. accept ----
-        acc_nodes, bonus = self._accept(reqs, vlogits.reshape(R, N, -1), tokens, parent, depth, c)
+        # ---- accept ----
+        vl = vlogits.reshape(R, N, -1)
+        if mode == "sample":
+            acc_nodes, bonus = self._accept_sample(reqs, vl, tokens, parent)
+        else:
+            acc_nodes, bonus = self._accept_static(vl, tokens, parent, ngeo)
 
-        self._mark("commit_sync")
-        # ---- 6. commit ----
+        # ---- commit: move the accepted nodes' KV to the committed positions (fixed shape, masked) ----
         valid = acc_nodes >= 0
         jj = torch.arange(D, device=dev)[None, :].expand(R, D)
-        src = slots_of(c[:, None] + acc_nodes.clamp(min=0))
         dst = slots_of(c[:, None] + 1 + jj)
-        self.pool.move_slots(src[valid], dst[valid])
+        src = torch.where(valid, slots_of(c[:, None] + acc_nodes.clamp(min=0)), dst)
+        self.pool.move_slots(src.reshape(-1), dst.reshape(-1))
         acc_tok = torch.where(valid, tokens.gather(1, acc_nodes.clamp(min=0)), torch.full_like(acc_nodes, -1))
-        packed = torch.cat([valid.sum(1, keepdim=True), acc_tok, bonus[:, None]], 1).cpu()
-        self.stats["d2h_bytes"] += packed.numel() * packed.element_size()
-        outs = []
-        for i, r in enumerate(reqs):
-            n = int(packed[i, 0])
-            new = [int(x) for x in packed[i, 1:1 + n]] + [int(packed[i, -1])]
-            r.tokens += new
-            r.committed += 1 + n
-            r.root = new[-1]
-            r.steps += 1
-            r.accepted.append(n)
-            self.stats["accepted"] += n
-            outs.append(self._emit(r, new))
-        self.stats["spec_steps"] += 1
-        self._mark("host_tail")
-        self._mark_name = None
-        return outs
+        return torch.cat([valid.sum(1, keepdim=True), acc_tok, bonus[:, None]], 1)
 
-    def _accept(self, reqs, logits, tokens, parent, depth, c):
-        """Returns (accepted node ids [R, D] (-1 = none), bonus tokens [R])."""
+    def _spine_index(self, dev) -> torch.Tensor:
+        key = ("spine", str(dev))
+        t = self._consts.get(key)
+        if t is None:
+            K, D = self.K, self.D
+            t = upload([0] + [K + (d - 1) * K * K for d in range(1, D)], torch.int64, dev)
+            self._consts[key] = t
+        return t
+
+    def _accept_static(self, logits, tokens, parent, ngeo):
+        """Greedy (target argmax along the tree) or synthetic geometric acceptance; device ops only.
+        Returns (accepted node ids [R, D] (-1 = none), bonus tokens [R])."""
         dev = self.device
-        R, N, D = len(reqs), self.N, self.D
-        greedy_all = all(r.params.temperature <= 0 for r in reqs)
+        R, N, D = tokens.shape[0], self.N, self.D
         cur = torch.zeros(R, dtype=torch.int64, device=dev)
         alive = torch.ones(R, dtype=torch.bool, device=dev)
         acc = torch.full((R, D), -1, dtype=torch.int64, device=dev)
         nidx = torch.arange(N, device=dev)[None, :]
-        spec = self.cfg.spec
-        if spec.accept == "geometric":
-            steps = torch.tensor([r.steps for r in reqs])
-            rid = torch.tensor([r.rid for r in reqs])
-            ngeo = upload(geometric_accept_len(spec.accept_seed, steps, rid, spec.accept_p, spec.accept_cap),
-                          torch.int64, dev)
-        if greedy_all or spec.accept == "geometric":
-            tgt = self.vocab.argmax(logits.reshape(R * N, -1)).reshape(R, N)
-            for d in range(1, D + 1):
-                kids = parent == cur[:, None]
-                if spec.accept == "geometric":
-                    match = kids & (d <= ngeo)[:, None]
-                else:
-                    match = kids & (tokens == tgt.gather(1, cur[:, None]))
-                match &= alive[:, None]
-                has = match.any(1)
-                first = torch.where(match, nidx.expand(R, N), torch.full_like(tokens, N)).min(1).values
-                acc[:, d - 1] = torch.where(has, first, torch.full_like(first, -1))
-                cur = torch.where(has, first, cur)
-                alive &= has
-            return acc, tgt.gather(1, cur[:, None])[:, 0]
+        tgt = self.vocab.argmax(logits.reshape(R * N, -1)).reshape(R, N)
+        for d in range(1, D + 1):
+            kids = parent == cur[:, None]
+            if ngeo is not None:
+                match = kids & (d <= ngeo)[:, None]
+            else:
+                match = kids & (tokens == tgt.gather(1, cur[:, None]))
+            match &= alive[:, None]
+            has = match.any(1)
+            first = torch.where(match, nidx.expand(R, N), torch.full_like(tokens, N)).min(1).values
+            acc[:, d - 1] = torch.where(has, first, torch.full_like(first, -1))
+            cur = torch.where(has, first, cur)
+            alive &= has
+        return acc, tgt.gather(1, cur[:, None])[:, 0]
+
+    def _accept_sample(self, reqs, logits, tokens, parent):
+        """Seeded target-only tree sampling (per-request temperature / top-k / top-p). Returns (accepted
+        node ids [R, D] (-1 = none), bonus tokens [R])."""
+        dev = self.device
+        R, N, D = len(reqs), self.N, self.D
+        cur = torch.zeros(R, dtype=torch.int64, device=dev)
+        acc = torch.full((R, D), -1, dtype=torch.int64, device=dev)
+        nidx = torch.arange(N, device=dev)[None, :]
         # seeded target-only tree sampling (per-request temperature / top-k / top-p)
         temp = upload([r.params.temperature for r in reqs], torch.float32, dev)
         topk = upload([r.params.top_k for r in reqs], torch.int64, dev)

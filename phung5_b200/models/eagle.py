@@ -81,15 +81,42 @@ class EagleHead:
         self.cfg = target_w.cfg
 
     def forward(self, fb: ForwardBatch, hidden_in: torch.Tensor):
-        """Returns (logits [rows, V_local], output feature [T, H] (pre-norm))."""
+        """Returns (logits [rows, V_local], output feature [T, H] (pre-norm)). On a fused communicator the
+        feature is a view of its workspace, valid until the next forward."""
         e = self.tw.embed[fb.tokens]
         cat = torch.cat([e, hidden_in.to(torch.bfloat16)], -1)
         if self.ew.fc.fp8:
             z = self.ew.fc(ops.act_quant(cat))
         else:
             z = self.ew.fc(cat)
+        comm = self.runner.comm
+        m = z.shape[0]
+        if getattr(comm, "fused", False) and 0 < m <= comm.max_tokens and comm.hidden == self.cfg.hidden:
+            return self._forward_fused(fb, z)
         h = z
         delta = self.runner.layer(0, h, None, fb)
         _, _, y = ops.add_rmsnorm_quant(h, delta, self.ew.norm, self.cfg.rms_eps, quant=False, out_bf16=True)
+        rows = y if fb.logits_rows is None else y[fb.logits_rows]
+        return ops.gemm_bf16(rows, self.tw.lm_head), h
+
+    def _forward_fused(self, fb: ForwardBatch, z: torch.Tensor):
+        """The head's layer on the fused communicator: residual in the symmetric workspace, o_proj / down_proj
+        partials reduced by `ar_norm` (+ RMSNorm + quant), the final norm's reduction also gathering the
+        residual rows every rank needs as the next round's feature."""
+        comm, cfg, lw, r = self.runner.comm, self.cfg, self.ew.layer, self.runner
+        m = z.shape[0]
+        fp8 = lw.qkv.fp8
+        h = comm.h(m)
+        h.copy_(z)
+        xq, xs, xb = ops.add_rmsnorm_quant(h, None, lw.in_norm, cfg.rms_eps, quant=fp8, out_bf16=not fp8)
+        qkv = lw.qkv((xq, xs) if fp8 else xb)
+        q = ops.rope_kv_write(qkv, fb.positions, fb.slots, r.cos_sin, r.kv_k[0], r.kv_v[0], r.hq, r.hkv, cfg.head_dim)
+        a = r.attention(0, q, fb, fp8)
+        lw.o(a, out=comm.partial(m))
+        x = comm.ar_norm(m, lw.post_norm, cfg.rms_eps, out_bf16=not fp8)
+        gu = lw.gu(x)
+        aq, as_, ab = ops.silu_mul_quant(gu, quant=fp8, out_bf16=not fp8)
+        lw.down((aq, as_) if fp8 else ab, out=comm.partial(m))
+        y = comm.ar_norm(m, self.ew.norm, cfg.rms_eps, out_bf16=True, push_h=True)
         rows = y if fb.logits_rows is None else y[fb.logits_rows]
         return ops.gemm_bf16(rows, self.tw.lm_head), h

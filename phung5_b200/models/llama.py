@@ -328,7 +328,7 @@ class LlamaModel:
                 lw.down((aq, as_) if fp8 else ab, out=comm.partial(m))
             last = li == n - 1
             wnext = self.w.final_norm if last else self.w.layers[li + 1].in_norm
-            x = comm.ar_norm(m, wnext, cfg.rms_eps, out_bf16=last or not fp8)
+            x = comm.ar_norm(m, wnext, cfg.rms_eps, out_bf16=last or not fp8, push_h=last and want_hidden)
         rows = x if fb.logits_rows is None else x[fb.logits_rows]
         logits = ops.gemm_bf16(rows, self.w.lm_head)
         return logits, (h if want_hidden else None)

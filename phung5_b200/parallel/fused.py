@@ -8,10 +8,15 @@ mapped into every peer, exchanged at rendezvous) holding, for up to `max_tokens`
     q       [M, H] e4m3   normalized rows, block-scaled fp8 (input of the next GEMM)
     s       [H/128, Mmax] fp32 scales of q
     flags   [2, W] u32    barrier flags (epochs)
+    counter [4] u32       CTA counter of the end barrier, device epoch
+    gsrc    [G] bytes     staging block of `gather` (this rank's candidates)
+    gdst    [W, G] bytes  every rank's staging block after `gather`
 `ar_norm(M, w)` runs csrc/tp_fused.cu: reduce-scatter of the partials with P2P loads, + residual,
 RMSNorm, fp8 quant, all-gather of the results with P2P stores, in one kernel. The engine's model uses
-it when the communicator reports `fused = True` (models/llama.py, forward_fused); the EAGLE head and
-anything larger than the workspace keep the NCCL path of the base class.
+it when the communicator reports `fused = True` (models/llama.py, forward_fused; the EAGLE head's layer
+too); anything larger than the workspace keeps the NCCL path of the base class. `gather` exchanges small
+blocks (vocab-sharded top-k and argmax candidates) with P2P stores. Barrier epochs are kept on the device,
+so every kernel here can be captured in a CUDA graph; no NCCL call remains on the decode path.
 
 `FusedEmulator` gives the same interface on CPU ranks (gloo all-reduce + the op definitions) so the
 fused forward's plumbing is tested without GPUs.
@@ -25,13 +30,17 @@ from .. import ops
 from .comm import NcclCommunicator
 
 
+GATHER_BYTES = 1 << 20
+
+
 class _Workspace:
     def __init__(self, max_tokens: int, hidden: int, device, world: int, alloc):
         self.mmax, self.h = max_tokens, hidden
         mh = max_tokens * hidden
         off, o = {}, 0
         for name, nbytes in (("partial", 2 * mh), ("h", 2 * mh), ("y", 2 * mh), ("q", mh),
-                             ("s", 4 * (hidden // 128) * max_tokens), ("flags", 4 * 2 * world), ("counter", 16)):
+                             ("s", 4 * (hidden // 128) * max_tokens), ("flags", 4 * 2 * world), ("counter", 16),
+                             ("gsrc", GATHER_BYTES), ("gdst", GATHER_BYTES * world)):
             off[name] = o
             o += (nbytes + 255) // 256 * 256
         self.off = off
@@ -62,7 +71,6 @@ class FusedCommunicator(NcclCommunicator):
         self.ws.view("counter", torch.int32, (4,)).zero_()
         torch.cuda.synchronize(dev)
         dist.barrier(group=self.group)
-        self.epoch = 0
         self.max_tokens = max_tokens
         self.hidden = hidden
 
@@ -72,17 +80,57 @@ class FusedCommunicator(NcclCommunicator):
     def h(self, m: int) -> torch.Tensor:
         return self.ws.view("h", torch.bfloat16, (m, self.hidden))
 
-    def ar_norm(self, m: int, w: torch.Tensor, eps: float, out_bf16: bool = False):
-        """h += sum over ranks of partial; returns the normalized rows: (q, s) fp8 or y bf16."""
-        self.epoch += 1
+    def ar_norm(self, m: int, w: torch.Tensor, eps: float, out_bf16: bool = False, push_h: bool = False):
+        """h += sum over ranks of partial (rows this rank owns; every row on every rank with push_h);
+        returns the normalized rows on every rank: (q, s) fp8 or y bf16."""
         off = [self.ws.off[k] for k in ("partial", "h", "y", "q", "s", "flags", "counter")]
-        ops.ext().tp_ar_norm(self.peer_base, self.rank, self.size, m, self.hidden, eps, self.epoch, w, out_bf16,
+        ops.ext().tp_ar_norm(self.peer_base, self.rank, self.size, m, self.hidden, eps, w, out_bf16, push_h,
                              ops.status_tensor(self.device), off, m)
         if out_bf16:
             return self.ws.view("y", torch.bfloat16, (m, self.hidden))
         q = self.ws.view("q", torch.float8_e4m3fn, (m, self.hidden))
         s = self.ws.view("s", torch.float32, (self.hidden // 128, m))
         return q, s
+
+
+    def gather(self, parts):
+        """All-gather of small tensors (one exchange for all parts): -> [[world, *p.shape] for p in parts]."""
+        offs, o = [], 0
+        for p in parts:
+            offs.append(o)
+            o += (p.numel() * p.element_size() + 15) // 16 * 16
+        if o > GATHER_BYTES:
+            return [super(FusedCommunicator, self)._gather(p) for p in parts]
+        src = self.ws.buf[self.ws.off["gsrc"]:]
+        for p, a in zip(parts, offs):
+            nb = p.numel() * p.element_size()
+            src[a:a + nb].copy_(p.contiguous().view(-1).view(torch.uint8))
+        off = [self.ws.off[k] for k in ("gsrc", "gdst", "flags", "counter")]
+        ops.ext().tp_allgather(self.peer_base, self.rank, self.size, o, ops.status_tensor(self.device), off)
+        dst = self.ws.buf[self.ws.off["gdst"]: self.ws.off["gdst"] + self.size * o].view(self.size, o)
+        out = []
+        for p, a in zip(parts, offs):
+            nb = p.numel() * p.element_size()
+            out.append(dst[:, a:a + nb].contiguous().view(p.dtype).view((self.size,) + tuple(p.shape)))
+        return out
+
+    def _gather(self, x: torch.Tensor) -> torch.Tensor:
+        if not x.is_cuda:
+            return super()._gather(x)
+        return self.gather([x])[0]
+
+    def topk_logprobs_merge(self, v: torch.Tensor, i: torch.Tensor, lse: torch.Tensor, k: int):
+        gv, gi, gl = self.gather([v.float(), i, lse.float()])
+        tot = torch.logsumexp(gl, 0)
+        vv = gv.permute(1, 0, 2).reshape(v.shape[0], -1)
+        ii = gi.permute(1, 0, 2).reshape(v.shape[0], -1)
+        tv, ti = torch.topk(vv, k, dim=-1)
+        return tv - tot, ii.gather(1, ti)
+
+    def argmax_merge(self, v: torch.Tensor, i: torch.Tensor) -> torch.Tensor:
+        gv, gi = self.gather([v.float(), i])
+        best = gv.argmax(0)
+        return gi.gather(0, best[None])[0]
 
 
 class FusedEmulator(NcclCommunicator):
@@ -102,7 +150,7 @@ class FusedEmulator(NcclCommunicator):
     def h(self, m):
         return self._h[:m]
 
-    def ar_norm(self, m, w, eps, out_bf16=False):
+    def ar_norm(self, m, w, eps, out_bf16=False, push_h=False):
         p = self._partial[:m].clone()
         self.all_reduce(p)
         q, s, y = ops.add_rmsnorm_quant(self._h[:m], p, w, eps, quant=not out_bf16, out_bf16=out_bf16)

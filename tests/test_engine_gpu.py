@@ -106,3 +106,27 @@ def test_engine_geometric_synthetic_acceptance():
     assert all(len(o) == 40 for o in outs)
     mean_acc = eng.stats["accepted"] / max(1, sum(len(r.accepted) for r in eng.reqs.values()))
     assert 1.2 < mean_acc < 3.0, mean_acc   # E[min(Geom(0.3), 6)] ~= 2.06
+
+
+@pytest.mark.parametrize("accept", ["greedy", "geometric"])
+def test_graph_replayed_step_equals_eager_step(accept, monkeypatch):
+    """The CUDA-graph speculative step (static buffers, device-built metadata) must emit exactly the tokens
+    of the eager step: same kernels on the same inputs. 16 requests sharing a 128-token prefix (cascade
+    groups)."""
+    cfg = preset("small-fp8")
+    kw = dict(mode="tree", tree_nodes=64, topk=8, depth=6)
+    if accept == "geometric":
+        kw["accept"] = "geometric"
+    prompts = _prompts(16, 256, cfg.vocab, seed=4, shared=128)
+    outs = {}
+    for graphs in ("1", "0"):
+        monkeypatch.setenv("PHX_GRAPHS", graphs)
+        eng = LLMEngine(EngineConfig(model=cfg, spec=SpecConfig(**kw), draft=DraftConfig(kind="eagle"),
+                                     cache=CacheConfig(num_pages=512)), device="cuda", max_context=4096)
+        outs[graphs] = eng.generate(prompts, SamplingParams(max_new_tokens=48))
+        ops.check_status()
+        if graphs == "1":       # requests finish at different steps: one graph per live batch size
+            assert eng._graphs and sum(g.replays for g in eng._graphs.values()) >= 5
+        del eng
+        torch.cuda.empty_cache()
+    assert outs["1"] == outs["0"]

@@ -178,3 +178,52 @@ def test_tp2_server_loop_matches_oracle():
     ref = RefModel(preset("tiny"), random_weights(preset("tiny"), seed=0, std=0.05))
     for p, o in zip(prompts, outs):
         assert o == greedy_generate(ref, p, 12)
+
+
+def _eagle_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from phung5_b200.engine.engine import LLMEngine
+        from phung5_b200.engine.oracle import SamplingParams
+        from phung5_b200.models.llama import pack_weights
+        from phung5_b200.parallel.comm import NcclCommunicator
+        from phung5_b200.parallel.fused import FusedEmulator
+        from phung5_b200.weights.init import random_weights
+        tcfg = preset("tiny")
+        tw = random_weights(tcfg, seed=0, std=0.05)
+        g = torch.Generator().manual_seed(9)
+        prompts = [torch.randint(0, 4096, (40,), generator=g).tolist() for _ in range(3)]
+        outs = []
+        for comm in (NcclCommunicator(), FusedEmulator(max_tokens=512, hidden=tcfg.hidden)):
+            ecfg = EngineConfig(model=tcfg, spec=SpecConfig(mode="tree", tree_nodes=10, topk=3, depth=3),
+                                draft=DraftConfig(kind="eagle"), cache=CacheConfig(page_size=16, num_pages=200))
+            eng = LLMEngine(ecfg, device="cpu", target=pack_weights(tcfg, tw, "cpu", rank, world, dtype=torch.float32),
+                            comm=comm, dtype=torch.float32, max_context=1024)
+            outs.append(eng.generate(prompts, SamplingParams(max_new_tokens=12)))
+        q.put((rank, outs, prompts))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_eagle_head_fused_path_matches_nccl_path():
+    """The EAGLE head's layer on the fused communicator (workspace residual, ar_norm reductions) drafts the
+    same trees as on the NCCL path; both emit the target's greedy tokens."""
+    from phung5_b200.engine.oracle import greedy_generate
+    from phung5_b200.models.reference import RefModel
+    from phung5_b200.weights.init import random_weights
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_eagle_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=180) for _ in procs], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+    assert all(p.exitcode == 0 for p in procs)
+    (nccl_out, fused_out), prompts = res[0][1], res[0][2]
+    assert nccl_out == fused_out and res[1][1][1] == fused_out
+    ref = RefModel(preset("tiny"), random_weights(preset("tiny"), seed=0, std=0.05))
+    for p, o in zip(prompts, fused_out):
+        assert o == greedy_generate(ref, p, 12)

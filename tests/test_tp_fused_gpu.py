@@ -44,13 +44,30 @@ def _worker(rank, world, port, q):
         parts = [torch.randn(m, hd, generator=torch.Generator().manual_seed(100 + r)).bfloat16() for r in range(world)]
         h0 = torch.randn(m, hd, generator=torch.Generator().manual_seed(7)).bfloat16()
         wn = (1 + 0.1 * torch.randn(hd, generator=torch.Generator().manual_seed(8))).bfloat16()
+        tot = sum(p.float() for p in parts).bfloat16()
+        h_ref = (h0.float() + tot.float()).bfloat16()
+        # without push_h only the rows this rank owns get the new residual
         fused.partial(m).copy_(parts[rank])
         fused.h(m).copy_(h0)
         torch.cuda.synchronize()
-        qf, sf = fused.ar_norm(m, wn.to(dev), cfg.rms_eps)
+        fused.ar_norm(m, wn.to(dev), cfg.rms_eps)
         torch.cuda.synchronize()
-        tot = sum(p.float() for p in parts).bfloat16()
-        h_ref = (h0.float() + tot.float()).bfloat16()
+        per = (m + world - 1) // world
+        own = torch.zeros(m, dtype=torch.bool)
+        own[rank * per:(rank + 1) * per] = True
+        hl = fused.h(m).cpu()
+        h_local_ok = torch.equal(hl[own], h_ref[own]) and torch.equal(hl[~own], h0[~own])
+        # with push_h every rank holds every new residual row
+        fused.partial(m).copy_(parts[rank])
+        fused.h(m).copy_(h0)
+        torch.cuda.synchronize()
+        qf, sf = fused.ar_norm(m, wn.to(dev), cfg.rms_eps, push_h=True)
+        torch.cuda.synchronize()
+        # small all-gather of mixed dtypes in one exchange
+        ga, gb = fused.gather([torch.full((3, 5), float(rank), device=dev),
+                               torch.arange(7, device=dev, dtype=torch.int64) + 100 * rank])
+        gather_ok = (torch.equal(ga.cpu(), torch.stack([torch.full((3, 5), float(r)) for r in range(world)]))
+                     and torch.equal(gb.cpu(), torch.stack([torch.arange(7) + 100 * r for r in range(world)])))
         hf = h_ref.float()
         y_ref = hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + cfg.rms_eps) * wn.float()
         deq = qf.float().cpu().view(m, hd // 128, 128) * sf.cpu().t()[..., None]
@@ -88,7 +105,7 @@ def _worker(rank, world, port, q):
             status = int(ops.status_tensor(dev)[0].item())
             ops.status_tensor(dev).zero_()
         dist.barrier()
-        q.put((rank, rel, relh, status, h_exact, y_err))
+        q.put((rank, rel, relh, status, h_exact and h_local_ok and gather_ok, y_err))
     finally:
         import torch.distributed as dist2
         dist2.destroy_process_group()
@@ -118,9 +135,77 @@ def test_fused_tp2_equals_nccl_and_times_out_cleanly():
         p.join(timeout=60)
     assert all(p.exitcode == 0 for p in procs)
     for rank, rel, relh, status, h_exact, y_err in res:
-        assert h_exact                          # reduce + residual add is the bf16 definition exactly
+        assert h_exact          # reduce + residual add is the bf16 definition exactly; own rows; gather
         assert y_err <= 1.0 / 15, y_err         # fp8 rows within one e4m3 step of the definition
         # whole 2-layer fp8 model: every activation is re-quantized, so tiny order differences compound
         assert rel < 5e-2, rel
         assert relh < 5e-2, relh
     assert res[0][3] == 4     # kErrTimeoutPeer
+
+
+def _engine_worker(rank, world, port, q):
+    """TP2 engine on the fused communicator (EAGLE head on the fused path, fused vocab merges): the
+    CUDA-graph speculative step must emit the eager step's tokens on every rank."""
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from phung5_b200 import ops
+        from phung5_b200.config import CacheConfig, DraftConfig, EngineConfig, SpecConfig, preset
+        from phung5_b200.engine.engine import LLMEngine
+        from phung5_b200.engine.oracle import SamplingParams
+        from phung5_b200.parallel.fused import FusedCommunicator
+        cfg = preset("small-fp8")
+        g = torch.Generator().manual_seed(6)
+        shared = torch.randint(0, cfg.vocab, (128,), generator=g).tolist()
+        prompts = [shared + torch.randint(0, cfg.vocab, (64,), generator=g).tolist() for _ in range(8)]
+        outs, replays = {}, 0
+        for graphs in ("1", "0"):
+            os.environ["PHX_GRAPHS"] = graphs
+            comm = FusedCommunicator(max_tokens=1024, hidden=cfg.hidden)
+            spec = SpecConfig(mode="tree", tree_nodes=64, topk=8, depth=6, accept="geometric")
+            eng = LLMEngine(EngineConfig(model=cfg, spec=spec, draft=DraftConfig(kind="eagle"),
+                                         cache=CacheConfig(num_pages=256)), device=f"cuda:{rank}", comm=comm,
+                            max_context=2048)
+            outs[graphs] = eng.generate(prompts, SamplingParams(max_new_tokens=40))
+            ops.check_status()
+            if graphs == "1":
+                replays = sum(gr.replays for gr in eng._graphs.values())
+            del eng
+            torch.cuda.synchronize()
+            dist.barrier()
+        q.put((rank, outs["1"] == outs["0"], replays, outs["1"][0][:8]))
+    finally:
+        import torch.distributed as dist2
+        dist2.destroy_process_group()
+
+
+def test_fused_tp2_graph_step_equals_eager():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_engine_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    import queue as _queue
+    import time as _time
+    res, t0 = [], _time.time()
+    while len(res) < world:
+        try:
+            res.append(q.get(timeout=5))
+        except _queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            assert not dead and _time.time() - t0 < 300, f"worker failed: {dead}"
+    for p in procs:
+        p.join(timeout=60)
+    assert all(p.exitcode == 0 for p in procs)
+    res.sort()
+    assert all(ok for _, ok, _, _ in res), res
+    assert all(n >= 3 for _, _, n, _ in res), res   # graphs are cached per live batch size
+    assert res[0][3] == res[1][3]            # both ranks emit the same tokens
