@@ -39,7 +39,9 @@ void gemm_bf16_grouped(torch::Tensor x, torch::Tensor w, torch::Tensor offsets, 
                        torch::Tensor status);
 void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M, int64_t H, double eps,
                 torch::Tensor w, bool out_bf16, bool push_h, torch::Tensor status, std::vector<int64_t> offsets,
-                int64_t s_ld);
+                int64_t s_ld, int64_t off_recv);
+void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tensor w, c10::optional<torch::Tensor> ws,
+                  torch::Tensor peer_base, int64_t off_recv, int64_t rows_per, int64_t rank, torch::Tensor status);
 void tp_allgather(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t nbytes, torch::Tensor status,
                   std::vector<int64_t> offsets);
 void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
@@ -72,6 +74,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("topk_logprobs", &phx::topk_logprobs);
   m.def("tp_ar_norm", &phx::tp_ar_norm);
   m.def("tp_allgather", &phx::tp_allgather);
+  m.def("gemm_scatter", &phx::gemm_scatter);
   m.def("gdn_recurrent", &phx::gdn_recurrent);
   m.def("gdn_fold", &phx::gdn_fold);
   m.def("gdn_gates", &phx::gdn_gates);

@@ -47,9 +47,16 @@ struct GemmSmem {
   int abort;
 };
 
-template <int BN>
+// the scatter epilogue stages each warp's 32 output rows in shared memory (8 warps x 32 rows x (BN/2 + 8)
+// bf16); BN = 256 gives up one operand stage for it
+template <int BN, bool SCATTER = false>
 constexpr int gemm_stages() {
-  return BN == 256 ? 4 : 6;
+  return BN == 256 ? (SCATTER ? 3 : 4) : (SCATTER ? 5 : 6);
+}
+
+template <int BN>
+constexpr int scatter_row_bytes() {
+  return BN + 16;   // BN/2 bf16 columns per epilogue warp row, padded by 16 bytes against bank conflicts
 }
 
 // Output tile t -> rows [m0, m_end) of A / out, rows [b0, b0 + BN) of B, output columns [n0, n0 + BN),
@@ -96,13 +103,23 @@ __device__ __forceinline__ TileInfo tile_info(int t, int M, int N, int m_tiles, 
   return ti;
 }
 
-template <int BN, bool FP8>
+// Scatter epilogue of a row-parallel projection under tensor parallelism: output row r is stored, over
+// NVLink, into rank owner(r) = r / rows_per's receive buffer at slot [rank][r - owner*rows_per] (each
+// rank's workspace base in peer_base). The reduce-scatter then reads only local memory, and the transfer
+// overlaps the remaining tiles' MMAs. peer_base == nullptr: plain stores to `out`.
+struct ScatterArgs {
+  const uint64_t* peer_base;
+  uint64_t off_recv;
+  int rows_per, rank;
+};
+
+template <int BN, bool FP8, bool SCATTER>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       __nv_bfloat16* __restrict__ out, int M, int N, int K, int ldc, const float* __restrict__ sa,
                       const float* __restrict__ sb, int* status, const int* __restrict__ grp_off, int groups,
-                      int max_tiles) {
-  constexpr int STAGES = gemm_stages<BN>();
+                      int max_tiles, const ScatterArgs sc) {
+  constexpr int STAGES = gemm_stages<BN, SCATTER>();
   constexpr int BKE = FP8 ? 128 : 64;  // K elements per 128-byte stage row
   constexpr uint32_t IDESC = idesc_make(kBM, BN, FP8 ? 0 : 1);
   constexpr int NBUF = 512 / BN;        // TMEM accumulators (all 512 columns)
@@ -276,7 +293,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) mbar_arrive(&s.tempty[tb]);
         if (++tb == NBUF) tb = 0, tphase ^= 1;
       }
-      if (row < ti.m_end && row < M && col_ok) {
+      if constexpr (SCATTER) {
+        // stage the warp's 32 rows, then store them row-contiguously (2 or 4 rows per warp instruction) into
+        // each row's owner receive slot: NVLink writes of whole 256/128-byte row segments
+        constexpr int ROWB = scatter_row_bytes<BN>();
+        uint8_t* st = reinterpret_cast<uint8_t*>(&s) + ((sizeof(Smem) + 127) & ~size_t(127)) + (size_t)ew * 32 * ROWB;
+#pragma unroll
+        for (int c = 0; c < CPT / 8; ++c) {
+          uint4 v;
+          v.x = pack_bf16x2(acc[4 * c + 0].x, acc[4 * c + 0].y);
+          v.y = pack_bf16x2(acc[4 * c + 1].x, acc[4 * c + 1].y);
+          v.z = pack_bf16x2(acc[4 * c + 2].x, acc[4 * c + 2].y);
+          v.w = pack_bf16x2(acc[4 * c + 3].x, acc[4 * c + 3].y);
+          *reinterpret_cast<uint4*>(st + lane * ROWB + c * 16) = v;
+        }
+        __syncwarp();
+        constexpr int CH = CPT / 8;      // 16-byte chunks per staged row
+        constexpr int RPI = 32 / CH;     // rows per warp instruction
+#pragma unroll 4
+        for (int it = 0; it < 32 / RPI; ++it) {
+          const int rl = it * RPI + lane / CH, ch = lane % CH;
+          const int grow = ti.m0 + sub * 32 + rl, gcol = col0 + ch * 8;
+          if (grow < ti.m_end && grow < M && gcol < N) {
+            const int owner = grow / sc.rows_per;
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(sc.peer_base[owner] + sc.off_recv) +
+                                 ((size_t)sc.rank * sc.rows_per + (grow - owner * sc.rows_per)) * ldc + gcol;
+            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(st + rl * ROWB + ch * 16);
+          }
+        }
+        __syncwarp();
+      } else if (row < ti.m_end && row < M && col_ok) {
         __nv_bfloat16* dst = out + (size_t)row * ldc + col0;
         const bool full_cols = col0 + CPT <= N;
 #pragma unroll
@@ -292,6 +338,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   epi_done:;
+    if (SCATTER) __threadfence_system();   // peer stores ordered before the reduction's release flags
   }
 
   tc_fence_before();
@@ -313,12 +360,12 @@ int num_sms() {
   return n;
 }
 
-template <int BN, bool FP8>
-void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, const float* sa,
-                 const float* sb, int* status, cudaStream_t stream, int max_ctas, const int* grp_off = nullptr,
-                 int groups = 0) {
+template <int BN, bool FP8, bool SCATTER = false>
+void launch_gemm_ptr(const torch::Tensor& a, const torch::Tensor& b, __nv_bfloat16* out_ptr, int ldc, int n_out,
+                     const float* sa, const float* sb, int* status, cudaStream_t stream, int max_ctas,
+                     const int* grp_off, int groups, ScatterArgs sc) {
   const int M = a.size(0), K = a.size(1);
-  const int N = grp_off ? (int)out.size(1) : (int)b.size(0);   // grouped: b holds groups * N rows
+  const int N = grp_off ? n_out : (int)b.size(0);   // grouped: b holds groups * N rows
   const CUtensorMapDataType dt = FP8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int esz = FP8 ? 1 : 2;
   const uint32_t box_inner = 128 / esz;
@@ -326,21 +373,30 @@ void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& 
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tb = make_tmap_2d(b.data_ptr(), dt, K, b.size(0), (uint64_t)b.stride(0) * esz, box_inner, BN,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
-  constexpr int STAGES = gemm_stages<BN>();
-  const size_t smem = sizeof(GemmSmem<BN, STAGES>) + 1024;
+  constexpr int STAGES = gemm_stages<BN, SCATTER>();
+  const size_t smem = ((sizeof(GemmSmem<BN, STAGES>) + 127) & ~size_t(127)) + 1024 +
+                      (SCATTER ? (size_t)kEpiWarps * 32 * scatter_row_bytes<BN>() : 0);
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8, SCATTER>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr_set = true;
   }
   // grouped: at most M/128 + groups row tiles in total (one partial tile per group)
   const int m_tiles_bound = grp_off ? (M + kBM - 1) / kBM + groups : (M + kBM - 1) / kBM;
   const int tiles = m_tiles_bound * ((N + BN - 1) / BN);
   int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
-  gemm_sm100_kernel<BN, FP8><<<grid, kGemmThreads, smem, stream>>>(
-      ta, tb, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), M, N, K, (int)out.stride(0), sa, sb, status, grp_off,
-      groups, tiles);
+  gemm_sm100_kernel<BN, FP8, SCATTER><<<grid, kGemmThreads, smem, stream>>>(ta, tb, out_ptr, M, N, K, ldc, sa, sb,
+                                                                             status, grp_off, groups, tiles, sc);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+template <int BN, bool FP8>
+void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, const float* sa,
+                 const float* sb, int* status, cudaStream_t stream, int max_ctas, const int* grp_off = nullptr,
+                 int groups = 0) {
+  launch_gemm_ptr<BN, FP8, false>(a, b, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (int)out.stride(0),
+                           (int)out.size(1), sa, sb, status, stream, max_ctas, grp_off, groups,
+                           ScatterArgs{nullptr, 0, 1, 0});
 }
 
 static int pick_bn(int M, int N) {
@@ -423,6 +479,40 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tenso
     launch_gemm<256, false>(x, w, out, nullptr, nullptr, status.data_ptr<int>(), stream, (int)max_ctas);
   else
     launch_gemm<128, false>(x, w, out, nullptr, nullptr, status.data_ptr<int>(), stream, (int)max_ctas);
+}
+
+// Row-parallel projection with the scatter epilogue (see ScatterArgs): fp8 (ws defined) or bf16 operands.
+void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tensor w, c10::optional<torch::Tensor> ws,
+                  torch::Tensor peer_base, int64_t off_recv, int64_t rows_per, int64_t rank, torch::Tensor status) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && peer_base.is_cuda() && peer_base.scalar_type() == at::kLong);
+  const int M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && N % 8 == 0 && x.stride(1) == 1 && w.stride(1) == 1);
+  TORCH_CHECK(rows_per > 0 && (int64_t)rows_per * peer_base.numel() >= M);
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const ScatterArgs sc{reinterpret_cast<const uint64_t*>(peer_base.data_ptr<int64_t>()), (uint64_t)off_recv,
+                       (int)rows_per, (int)rank};
+  const int b = pick_bn(M, N);
+  if (ws.has_value()) {
+    TORCH_CHECK(x.scalar_type() == at::kFloat8_e4m3fn && w.scalar_type() == at::kFloat8_e4m3fn && K % 128 == 0);
+    TORCH_CHECK(xs->is_contiguous() && xs->size(0) == K / 128 && xs->size(1) == M);
+    TORCH_CHECK(ws->is_contiguous() && ws->size(0) == (N + 127) / 128 && ws->size(1) == K / 128);
+    const float* sa = xs->data_ptr<float>();
+    const float* sb = ws->data_ptr<float>();
+    if (b == 256)
+      launch_gemm_ptr<256, true, true>(x, w, nullptr, N, N, sa, sb, status.data_ptr<int>(), stream, 0, nullptr, 0, sc);
+    else
+      launch_gemm_ptr<128, true, true>(x, w, nullptr, N, N, sa, sb, status.data_ptr<int>(), stream, 0, nullptr, 0, sc);
+  } else {
+    TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && K % 64 == 0);
+    if (b == 256)
+      launch_gemm_ptr<256, false, true>(x, w, nullptr, N, N, nullptr, nullptr, status.data_ptr<int>(), stream, 0, nullptr, 0,
+                                  sc);
+    else
+      launch_gemm_ptr<128, false, true>(x, w, nullptr, N, N, nullptr, nullptr, status.data_ptr<int>(), stream, 0, nullptr, 0,
+                                  sc);
+  }
 }
 
 }  // namespace phx

@@ -29,6 +29,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace phx {
@@ -40,6 +42,8 @@ struct TpArgs {
   const __nv_bfloat16* w;     // norm weight [H], local
   int out_bf16;               // 0: fp8 q + scales, 1: bf16 y
   int push_h;                 // 1: store the new residual rows into every rank's h (else only locally)
+  int recv;                   // 1: partials were pushed into this rank's receive slots (gemm_scatter); 0: pull
+  uint64_t off_recv;          // receive buffer [W][rows_per][H] bf16
   int* status;
   // byte offsets inside the workspace
   uint64_t off_partial, off_h, off_y, off_q, off_s, off_flags, off_counter;
@@ -101,10 +105,12 @@ __device__ __forceinline__ void end_barrier(uint8_t* mine, uint64_t off_flags, u
   }
 }
 
-template <int MAXC>
+// WT: the world size as a compile-time constant (2, 4, 8) so the W peer loads of a 16-byte chunk are all
+// issued before the first is consumed; 0 = runtime world size.
+template <int MAXC, int WT>
 __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
   __shared__ float red[32];
-  const int W = a.world;
+  const int W = WT > 0 ? WT : a.world;
   auto base = [&](int p) { return reinterpret_cast<uint8_t*>(a.peer_base[p]); };
   uint8_t* mine = base(a.rank);
   uint32_t* my_flags = reinterpret_cast<uint32_t*>(mine + a.off_flags);
@@ -133,8 +139,7 @@ __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[e] = 0.f;
         const size_t off = ((size_t)row * H + c * 8) * 2;
-        for (int p = 0; p < W; ++p) {
-          const uint4 v = *reinterpret_cast<const uint4*>(base(p) + a.off_partial + off);
+        auto add = [&](const uint4 v) {
           const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -142,6 +147,21 @@ __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
             acc[2 * e] += f.x;
             acc[2 * e + 1] += f.y;
           }
+        };
+        // source of rank p's partial of this row: its pushed copy in my receive slot p, or its partial buffer
+        const size_t roff = ((size_t)(row - r0) * H + c * 8) * 2, rstride = (size_t)rows_per * H * 2;
+        auto src = [&](int p) -> const uint4* {
+          return a.recv ? reinterpret_cast<const uint4*>(mine + a.off_recv + p * rstride + roff)
+                        : reinterpret_cast<const uint4*>(base(p) + a.off_partial + off);
+        };
+        if constexpr (WT > 0) {
+          uint4 v[WT];
+#pragma unroll
+          for (int p = 0; p < WT; ++p) v[p] = *src(p);
+#pragma unroll
+          for (int p = 0; p < WT; ++p) add(v[p]);
+        } else {
+          for (int p = 0; p < W; ++p) add(*src(p));
         }
         const uint4 hv = *reinterpret_cast<const uint4*>(mine + a.off_h + off);
         const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
@@ -224,7 +244,7 @@ __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
 
 void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M, int64_t H, double eps,
                 torch::Tensor w, bool out_bf16, bool push_h, torch::Tensor status, std::vector<int64_t> offsets,
-                int64_t s_ld) {
+                int64_t s_ld, int64_t off_recv) {
   TORCH_CHECK(peer_base.is_cuda() && peer_base.scalar_type() == at::kLong && peer_base.numel() == world);
   TORCH_CHECK(H % 128 == 0 && world >= 1 && world <= 32 && offsets.size() == 7);
   if (M == 0) return;
@@ -240,6 +260,8 @@ void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M,
   a.w = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   a.out_bf16 = out_bf16 ? 1 : 0;
   a.push_h = push_h ? 1 : 0;
+  a.recv = off_recv >= 0 ? 1 : 0;
+  a.off_recv = off_recv >= 0 ? (uint64_t)off_recv : 0;
   a.status = status.data_ptr<int>();
   a.off_partial = offsets[0];
   a.off_h = offsets[1];
@@ -252,11 +274,18 @@ void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M,
   const int rows_per = (int)((M + world - 1) / world);
   const int grid = std::max(1, std::min(rows_per, 148 * 4));
   const int maxc = (int)((H / 8 + 255) / 256);
-  if (maxc <= 1) tp_ar_norm_kernel<1><<<grid, 256, 0, stream>>>(a);
-  else if (maxc <= 2) tp_ar_norm_kernel<2><<<grid, 256, 0, stream>>>(a);
-  else if (maxc <= 4) tp_ar_norm_kernel<4><<<grid, 256, 0, stream>>>(a);
-  else if (maxc <= 8) tp_ar_norm_kernel<8><<<grid, 256, 0, stream>>>(a);
-  else TORCH_CHECK(false, "hidden size too large");
+  auto launch = [&](auto wt) {
+    constexpr int WT = decltype(wt)::value;
+    if (maxc <= 1) tp_ar_norm_kernel<1, WT><<<grid, 256, 0, stream>>>(a);
+    else if (maxc <= 2) tp_ar_norm_kernel<2, WT><<<grid, 256, 0, stream>>>(a);
+    else if (maxc <= 4) tp_ar_norm_kernel<4, WT><<<grid, 256, 0, stream>>>(a);
+    else if (maxc <= 8) tp_ar_norm_kernel<8, WT><<<grid, 256, 0, stream>>>(a);
+    else TORCH_CHECK(false, "hidden size too large");
+  };
+  if (world == 2) launch(std::integral_constant<int, 2>{});
+  else if (world == 4) launch(std::integral_constant<int, 4>{});
+  else if (world == 8) launch(std::integral_constant<int, 8>{});
+  else launch(std::integral_constant<int, 0>{});
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -102,8 +102,19 @@ def _verify_case(reqs=64, nodes=64, prefix=4096, suffix=600, hq=64, hkv=8):
     return q, kc, vc, meta
 
 
-def case_attention(which, impl):
-    q, kc, vc, meta = _verify_case()
+def case_silu_quant(m, f):
+    gu = torch.randn(m, 2 * f, device="cuda", dtype=torch.bfloat16)
+    fn = lambda: ops.silu_mul_quant(gu, quant=True, out_bf16=False)
+    return fn, m * (2 * f * 2 + f + 4 * f // 128), "bytes"
+
+
+def case_topk(rows, v, k):
+    x = torch.randn(rows, v, device="cuda", dtype=torch.bfloat16)
+    return (lambda: ops.topk_logprobs(x, k)), rows * v * 2, "bytes"
+
+
+def case_attention(which, impl, hq=64, hkv=8):
+    q, kc, vc, meta = _verify_case(hq=hq, hkv=hkv)
     t, hq = q.shape[0], q.shape[1]
     g = hq // kc.shape[1]
     groups = cascade_groups(meta, 64)
@@ -140,6 +151,23 @@ CASES = {
     "attn_prefix_mma": lambda: case_attention("prefix", "mma"),
     "attn_suffix_tc": lambda: case_attention("suffix", "tc"),
     "attn_suffix_mma": lambda: case_attention("suffix", "mma"),
+    # per-rank shapes of tensor parallelism over 8 GPUs (Llama-3-70B, 64 requests x 64-node verify)
+    "gemm_fp8_qkv_tp8": lambda: case_gemm_fp8(4096, 1280, 8192),
+    "gemm_fp8_o_tp8": lambda: case_gemm_fp8(4096, 8192, 1024),
+    "gemm_fp8_down_tp8": lambda: case_gemm_fp8(4096, 8192, 3584),
+    "gemm_bf16_lm_head_tp8": lambda: case_gemm_bf16(4096, 16032, 8192),
+    "attn_prefix_tc_tp8": lambda: case_attention("prefix", "tc", hq=8, hkv=1),
+    "attn_suffix_tc_tp8": lambda: case_attention("suffix", "tc", hq=8, hkv=1),
+    "silu_mul_quant_tp8": lambda: case_silu_quant(4096, 3584),
+    "silu_mul_quant": lambda: case_silu_quant(4096, 28672),
+    "topk8_draft_tp8": lambda: case_topk(512, 16032, 8),
+    "topk8_draft": lambda: case_topk(512, 128256, 8),
+    "argmax_verify": lambda: case_topk(4096, 128256, 1),
+    # draft-round shapes (512 = 64 requests x top-8 frontier)
+    "gemm_fp8_draft_qkv_tp8": lambda: case_gemm_fp8(512, 1280, 8192),
+    "gemm_fp8_draft_gate_up_tp8": lambda: case_gemm_fp8(512, 7168, 8192),
+    "gemm_fp8_draft_fc": lambda: case_gemm_fp8(512, 8192, 16384),
+    "gemm_bf16_draft_lm_head_tp8": lambda: case_gemm_bf16(512, 16032, 8192),
 }
 
 
@@ -153,11 +181,16 @@ def main():
         fn, flops, kind = CASES[name]()
         ms = time_it(fn, args.iters)
         ops.check_status()
-        tf = flops / ms / 1e9
-        denom = pk["bf16_tflops"] * (2 if kind == "fp8" else 1)
-        print(json.dumps({"kernel": name, "ms": round(ms, 4), "tflops": round(tf, 1),
-                          "frac_of_" + pk["src"]: round(tf / denom, 3),
-                          "denominator_tflops": denom, "kind": kind}))
+        if kind == "bytes":
+            gbs = flops / ms / 1e6
+            print(json.dumps({"kernel": name, "ms": round(ms, 4), "gb_s": round(gbs, 1),
+                              "frac_of_" + pk["src"]: round(gbs / pk["hbm_gbs"], 3), "denominator_gbs": pk["hbm_gbs"]}))
+        else:
+            tf = flops / ms / 1e9
+            denom = pk["bf16_tflops"] * (2 if kind == "fp8" else 1)
+            print(json.dumps({"kernel": name, "ms": round(ms, 4), "tflops": round(tf, 1),
+                              "frac_of_" + pk["src"]: round(tf / denom, 3),
+                              "denominator_tflops": denom, "kind": kind}))
         torch.cuda.empty_cache()
 
 

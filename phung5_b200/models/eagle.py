@@ -112,11 +112,11 @@ class EagleHead:
         qkv = lw.qkv((xq, xs) if fp8 else xb)
         q = ops.rope_kv_write(qkv, fb.positions, fb.slots, r.cos_sin, r.kv_k[0], r.kv_v[0], r.hq, r.hkv, cfg.head_dim)
         a = r.attention(0, q, fb, fp8)
-        lw.o(a, out=comm.partial(m))
-        x = comm.ar_norm(m, lw.post_norm, cfg.rms_eps, out_bf16=not fp8)
+        comm.project(lw.o, a, m)
+        x = comm.ar_norm(m, lw.post_norm, cfg.rms_eps, out_bf16=not fp8, recv=True)
         gu = lw.gu(x)
         aq, as_, ab = ops.silu_mul_quant(gu, quant=fp8, out_bf16=not fp8)
-        lw.down((aq, as_) if fp8 else ab, out=comm.partial(m))
-        y = comm.ar_norm(m, self.ew.norm, cfg.rms_eps, out_bf16=True, push_h=True)
+        comm.project(lw.down, (aq, as_) if fp8 else ab, m)
+        y = comm.ar_norm(m, self.ew.norm, cfg.rms_eps, out_bf16=True, push_h=True, recv=True)
         rows = y if fb.logits_rows is None else y[fb.logits_rows]
         return ops.gemm_bf16(rows, self.tw.lm_head), h

@@ -301,8 +301,9 @@ class LlamaModel:
 
     def forward_fused(self, fb: ForwardBatch, want_hidden: bool = False):
         """Tensor-parallel forward on a fused communicator (parallel/fused.py): the residual stream lives in
-        the communicator's symmetric workspace, o_proj / down_proj write their partial sums into it, and one
-        `ar_norm` kernel per reduction does reduce-scatter + residual add + RMSNorm + quant + all-gather."""
+        the communicator's symmetric workspace, o_proj / down_proj store each output row into its owner's
+        receive slot from the GEMM epilogue (`project`), and one `ar_norm` kernel per reduction adds the
+        slots + residual, normalizes, quantizes and all-gathers the rows the next GEMM reads."""
         comm, cfg = self.comm, self.cfg
         m = fb.tokens.shape[0]
         h = comm.h(m)
@@ -317,18 +318,21 @@ class LlamaModel:
             q = ops.rope_kv_write(qkv, fb.positions, fb.slots, self.cos_sin, self.kv_k[li], self.kv_v[li], self.hq,
                                   self.hkv, cfg.head_dim)
             a = self.attention(li, q, fb, fp8)
-            lw.o(a, out=comm.partial(m))
+            comm.project(lw.o, a, m)
             if lw.moe is not None:
-                yb = comm.ar_norm(m, lw.post_norm, cfg.rms_eps, out_bf16=True)
+                yb = comm.ar_norm(m, lw.post_norm, cfg.rms_eps, out_bf16=True, recv=True)
                 comm.partial(m).copy_(lw.moe(ops.act_quant(yb) if fp8 else yb, yb))
+                recv = False
             else:
-                x = comm.ar_norm(m, lw.post_norm, cfg.rms_eps, out_bf16=not fp8)
+                x = comm.ar_norm(m, lw.post_norm, cfg.rms_eps, out_bf16=not fp8, recv=True)
                 gu = lw.gu(x)
                 aq, as_, ab = ops.silu_mul_quant(gu, quant=fp8, out_bf16=not fp8)
-                lw.down((aq, as_) if fp8 else ab, out=comm.partial(m))
+                comm.project(lw.down, (aq, as_) if fp8 else ab, m)
+                recv = True
             last = li == n - 1
             wnext = self.w.final_norm if last else self.w.layers[li + 1].in_norm
-            x = comm.ar_norm(m, wnext, cfg.rms_eps, out_bf16=last or not fp8, push_h=last and want_hidden)
+            x = comm.ar_norm(m, wnext, cfg.rms_eps, out_bf16=last or not fp8, push_h=last and want_hidden,
+                             recv=recv)
         rows = x if fb.logits_rows is None else x[fb.logits_rows]
         logits = ops.gemm_bf16(rows, self.w.lm_head)
         return logits, (h if want_hidden else None)

@@ -11,6 +11,8 @@ mapped into every peer, exchanged at rendezvous) holding, for up to `max_tokens`
     counter [4] u32       CTA counter of the end barrier, device epoch
     gsrc    [G] bytes     staging block of `gather` (this rank's candidates)
     gdst    [W, G] bytes  every rank's staging block after `gather`
+    recv    [W, ceil(M/W), H] bf16  row-parallel projection outputs pushed by each rank for the rows this
+                          rank owns (`project`: the GEMM's epilogue stores them over NVLink)
 `ar_norm(M, w)` runs csrc/tp_fused.cu: reduce-scatter of the partials with P2P loads, + residual,
 RMSNorm, fp8 quant, all-gather of the results with P2P stores, in one kernel. The engine's model uses
 it when the communicator reports `fused = True` (models/llama.py, forward_fused; the EAGLE head's layer
@@ -40,7 +42,8 @@ class _Workspace:
         off, o = {}, 0
         for name, nbytes in (("partial", 2 * mh), ("h", 2 * mh), ("y", 2 * mh), ("q", mh),
                              ("s", 4 * (hidden // 128) * max_tokens), ("flags", 4 * 2 * world), ("counter", 16),
-                             ("gsrc", GATHER_BYTES), ("gdst", GATHER_BYTES * world)):
+                             ("gsrc", GATHER_BYTES), ("gdst", GATHER_BYTES * world),
+                             ("recv", 2 * hidden * world * ((max_tokens + world - 1) // world))):
             off[name] = o
             o += (nbytes + 255) // 256 * 256
         self.off = off
@@ -80,12 +83,23 @@ class FusedCommunicator(NcclCommunicator):
     def h(self, m: int) -> torch.Tensor:
         return self.ws.view("h", torch.bfloat16, (m, self.hidden))
 
-    def ar_norm(self, m: int, w: torch.Tensor, eps: float, out_bf16: bool = False, push_h: bool = False):
-        """h += sum over ranks of partial (rows this rank owns; every row on every rank with push_h);
-        returns the normalized rows on every rank: (q, s) fp8 or y bf16."""
+    def project(self, lin, x, m: int) -> None:
+        """Row-parallel projection (o_proj / down_proj) whose output rows are stored straight into their owner's
+        receive slot by the GEMM epilogue (a reduce-scatter's transfer, overlapped with the GEMM); follow with
+        `ar_norm(..., recv=True)`."""
+        rows_per = (m + self.size - 1) // self.size
+        xq, xs = x if lin.fp8 else (x, None)
+        ops.ext().gemm_scatter(xq, xs, lin.w, lin.ws, self.peer_base, self.ws.off["recv"], rows_per, self.rank,
+                               ops.status_tensor(self.device))
+
+    def ar_norm(self, m: int, w: torch.Tensor, eps: float, out_bf16: bool = False, push_h: bool = False,
+                recv: bool = False):
+        """h += sum over ranks of the projection partials (pulled from every rank's `partial`, or, with recv,
+        read from the receive slots `project` filled) for the rows this rank owns (every row on every rank with
+        push_h); returns the normalized rows on every rank: (q, s) fp8 or y bf16."""
         off = [self.ws.off[k] for k in ("partial", "h", "y", "q", "s", "flags", "counter")]
         ops.ext().tp_ar_norm(self.peer_base, self.rank, self.size, m, self.hidden, eps, w, out_bf16, push_h,
-                             ops.status_tensor(self.device), off, m)
+                             ops.status_tensor(self.device), off, m, self.ws.off["recv"] if recv else -1)
         if out_bf16:
             return self.ws.view("y", torch.bfloat16, (m, self.hidden))
         q = self.ws.view("q", torch.float8_e4m3fn, (m, self.hidden))
@@ -150,7 +164,10 @@ class FusedEmulator(NcclCommunicator):
     def h(self, m):
         return self._h[:m]
 
-    def ar_norm(self, m, w, eps, out_bf16=False, push_h=False):
+    def project(self, lin, x, m):
+        self._partial[:m].copy_(lin(x))
+
+    def ar_norm(self, m, w, eps, out_bf16=False, push_h=False, recv=False):
         p = self._partial[:m].clone()
         self.all_reduce(p)
         q, s, y = ops.add_rmsnorm_quant(self._h[:m], p, w, eps, quant=not out_bf16, out_bf16=out_bf16)

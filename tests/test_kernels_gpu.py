@@ -340,3 +340,34 @@ def test_selftest_cli_passes():
     from phung5_b200.ops import selftest
     res = selftest.run()
     assert all(v["ok"] for v in res.values()), res
+
+
+@pytest.mark.parametrize("fp8,m,n,k", [(True, 4096, 8192, 1024), (True, 300, 1024, 512), (False, 200, 512, 256),
+                                       (True, 77, 256, 128)])
+def test_gemm_scatter_epilogue(fp8, m, n, k):
+    """The row-parallel projection's scatter epilogue: row r lands in buffer owner(r) = r // rows_per at slot
+    [rank][r - owner * rows_per]. Four local buffers stand in for the peers' receive regions."""
+    world, rank = 4, 1
+    rows_per = (m + world - 1) // world
+    x = torch.randn(m, k, device=DEV)
+    w = torch.randn(n, k, device=DEV) * 0.05
+    bufs = [torch.full((world, rows_per, n), 3.0, device=DEV, dtype=torch.bfloat16) for _ in range(world)]
+    base = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device=DEV)
+    if fp8:
+        xq, xs = quant_act_block(x)
+        wq, ws = quant_weight_block(w)
+        ops.ext().gemm_scatter(xq, xs, wq, ws, base, 0, rows_per, rank, ops.status_tensor(DEV))
+        ref = ops.gemm_fp8_block(xq, xs, wq, ws)
+    else:
+        xb, wb = x.bfloat16(), w.bfloat16()
+        ops.ext().gemm_scatter(xb, None, wb, None, base, 0, rows_per, rank, ops.status_tensor(DEV))
+        ref = ops.gemm_bf16(xb, wb)
+    torch.cuda.synchronize()
+    for o in range(world):
+        r0, r1 = o * rows_per, min(m, (o + 1) * rows_per)
+        got = bufs[o][rank, : r1 - r0]
+        assert torch.equal(got, ref[r0:r1])                    # same kernel math: bitwise
+        assert bool((bufs[o][rank, r1 - r0:] == 3.0).all())    # nothing past the owner's rows
+        for other in range(world):
+            if other != rank:
+                assert bool((bufs[o][other] == 3.0).all())     # other ranks' slots untouched
