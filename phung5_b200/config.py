@@ -138,6 +138,7 @@ class CacheConfig:
     mem_fraction: float = 0.85
     enable_prefix_cache: bool = True
     enable_cascade: bool = True
+    max_seqs: int = 256  # hybrid GDN models: recurrent state slots (concurrent requests)
 
 
 @dataclass
@@ -183,6 +184,8 @@ PRESETS: Dict[str, ModelConfig] = {
     "hybrid-gdn-small": ModelConfig(name="hybrid-gdn-small", arch="hybrid_gdn", num_layers=8, hidden=1024,
                                     num_heads=8, num_kv_heads=2, head_dim=128, ffn=2816, vocab=32000,
                                     rope_theta=1e7, full_attn_every=4, gdn_heads=8),
+    "tiny-hybrid": ModelConfig(name="tiny-hybrid", arch="hybrid_gdn", num_layers=4, hidden=256, num_heads=4,
+                               num_kv_heads=2, head_dim=64, ffn=688, vocab=4096, full_attn_every=2, gdn_heads=2),
     # small GPU test shapes
     "small-fp8": ModelConfig(name="small-fp8", num_layers=2, hidden=1024, num_heads=8, num_kv_heads=2,
                              head_dim=128, ffn=2816 + 256, vocab=8192, rope_theta=5e5, quant="fp8_block"),

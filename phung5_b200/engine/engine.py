@@ -56,6 +56,7 @@ class Request:
     t_arrive: float = 0.0
     t_first: float = 0.0
     t_done: float = 0.0
+    gslot: int = -1           # hybrid models: GDN state slot
 
 
 @dataclass
@@ -120,7 +121,19 @@ class LLMEngine:
         self.dtype = dtype
         mc = cfg.model
         tp = self.comm.size
-        if target is None:
+        self.hybrid = mc.arch == "hybrid_gdn"
+        gdn_layers = None
+        if self.hybrid:
+            if tp > 1:
+                raise ValueError("hybrid GDN models run with tensor_parallel_size 1 (replicate them for scale-out)")
+            if cfg.spec.enabled and cfg.spec.mode == "tree":
+                raise ValueError("hybrid GDN models verify chains only: set spec.mode = 'chain'")
+            if target is None:
+                from ..models.hybrid import random_hybrid
+                target, gdn_layers = random_hybrid(mc, self.device, seed=cfg.seed, dtype=dtype)
+            else:
+                target, gdn_layers = target
+        elif target is None:
             target = random_packed_weights(mc, self.device, seed=cfg.seed, tp_rank=self.comm.rank, tp_size=tp)
         self.tw = target
         self.ps = cfg.cache.page_size
@@ -134,14 +147,23 @@ class LLMEngine:
         draft_layers = 0
         if self.spec_on:
             draft_layers = 1 if self.eagle else (drafter.cfg.num_layers if drafter is not None else cfg.draft.num_layers)
+        n_kv_layers = len(target.layers)        # hybrid: only the full-attention layers have a KV cache
         if num_pages is None:
-            num_pages = cfg.cache.num_pages or self._pages_from_memory(mc, hkv, draft_layers)
-        self.pool = KVPool(mc.num_layers, num_pages, hkv, self.ps, mc.head_dim, self.device,
+            num_pages = cfg.cache.num_pages or self._pages_from_memory(mc, hkv, draft_layers, n_kv_layers)
+        self.pool = KVPool(n_kv_layers, num_pages, hkv, self.ps, mc.head_dim, self.device,
                            draft_layers=draft_layers, hidden=mc.hidden if (self.spec_on and self.eagle) else 0,
                            dtype=dtype)
         self.cos_sin = ops.rope_table(max_context + 2 * self.ps, mc.head_dim, mc.rope_theta, self.device)
         self.max_context = max_context
-        self.target = LlamaModel(target, self.pool.k, self.pool.v, self.cos_sin, self.comm)
+        if self.hybrid:
+            from ..models.hybrid import GdnPool, HybridModel, gdn_heads
+            g0 = next(g for g in gdn_layers if g is not None)
+            self.gdn_pool = GdnPool(sum(g is not None for g in gdn_layers), cfg.cache.max_seqs, g0.gdn.conv_channels,
+                                    g0.gdn.conv_w.shape[1], gdn_heads(mc)[1], self.device, dtype)
+            self.target = HybridModel(target, gdn_layers, self.pool.k, self.pool.v, self.cos_sin, self.gdn_pool,
+                                      self.comm)
+        else:
+            self.target = LlamaModel(target, self.pool.k, self.pool.v, self.cos_sin, self.comm)
         self.drafter = None
         if self.spec_on:
             if self.eagle:
@@ -152,7 +174,9 @@ class LLMEngine:
             else:
                 dw = drafter
                 if dw is None:
-                    dcfg = preset("tiny-draft") if mc.name == "tiny" else ModelConfig(**{**mc.to_dict(), "num_layers": cfg.draft.num_layers})
+                    dcfg = preset("tiny-draft") if mc.name == "tiny" else ModelConfig(
+                        **{**mc.to_dict(), "num_layers": cfg.draft.num_layers,
+                           "arch": "llama" if mc.arch == "hybrid_gdn" else mc.arch})
                     dw = random_packed_weights(dcfg, self.device, seed=cfg.seed + 1, tp_rank=self.comm.rank, tp_size=tp)
                 self.drafter = LlamaModel(dw, self.pool.dk, self.pool.dv, self.cos_sin, self.comm)
         self.vocab = _VocabOps(self.comm, target.vocab_start)
@@ -170,14 +194,14 @@ class LLMEngine:
         # CUDA graphs of the speculative step (one per batch size): on by default on CUDA
         self._graphs = {} if (self.device.type == "cuda" and _os.environ.get("PHX_GRAPHS", "1") != "0") else None
         self._graph_cache = 4
-        self._has_moe = any(lw.moe is not None for lw in self.tw.layers)
+        self._has_moe = any(getattr(lw, "moe", None) is not None for lw in self.tw.layers)
         self._consts: Dict[object, torch.Tensor] = {}
         self.host_times: Dict[str, float] = {}
         self._mark_name, self._mark_t = None, 0.0
 
     # ------------------------------------------------------------------------------------------
-    def _pages_from_memory(self, mc: ModelConfig, hkv: int, draft_layers: int) -> int:
-        per = KVPool.bytes_per_page(mc.num_layers, hkv, self.ps, mc.head_dim, draft_layers,
+    def _pages_from_memory(self, mc: ModelConfig, hkv: int, draft_layers: int, kv_layers: int) -> int:
+        per = KVPool.bytes_per_page(kv_layers, hkv, self.ps, mc.head_dim, draft_layers,
                                     mc.hidden if self.eagle else 0)
         if self.device.type == "cuda":
             free, _ = torch.cuda.mem_get_info(self.device)
@@ -305,7 +329,18 @@ class LLMEngine:
             return t.to(self.device, non_blocking=True)
         return t
 
+    def _gdn_batch(self, lens: List[int], reqs: List[Request], mode: str):
+        from ..models.hybrid import GdnBatch
+        ts = [0]
+        for n in lens:
+            ts.append(ts[-1] + n)
+        packed = self._h2d(ts + [r.gslot for r in reqs], torch.int32)
+        return GdnBatch(tok_start=packed[:len(ts)], slot=packed[len(ts):], mode=mode)
+
     def _finish(self, r: Request) -> None:
+        if self.hybrid and r.gslot >= 0:
+            self.gdn_pool.release(r.gslot)
+            r.gslot = -1
         r.finished = True
         r.t_done = time.perf_counter()
         n_full = min(r.committed, len(r.tokens)) // self.ps
@@ -345,8 +380,11 @@ class LLMEngine:
         local_keys: Dict[int, int] = {}
         while self.waiting and budget > 0:
             r = self.waiting[0]
-            if r.prefilled == 0 and not r.pages:
-                # prefix cache (and pages being written by requests earlier in this pass)
+            if self.hybrid and r.gslot < 0:
+                r.gslot = self.gdn_pool.alloc()
+            if r.prefilled == 0 and not r.pages and not self.hybrid:
+                # prefix cache (and pages being written by requests earlier in this pass); hybrid models
+                # recompute prompts: a cached KV prefix carries no GDN state
                 n_match = (r.prompt_len - 1) // self.ps
                 keys = self.pool.prefix.chain_keys(r.tokens, self.ps, n_match)
                 pages = self.pool.prefix.match(r.tokens, (r.prompt_len - 1))
@@ -385,6 +423,8 @@ class LLMEngine:
         fb = ForwardBatch(tokens=self._h2d(toks, torch.int64), positions=self._h2d(pos, torch.int32),
                           slots=self._h2d(slots, torch.int64), meta=meta, work2=pack_work(p2, g, self.device),
                           logits_rows=self._h2d(last_rows, torch.int64))
+        if self.hybrid:
+            fb.gdn = self._gdn_batch([e - s for _, s, e in batch], [r for r, _, _ in batch], "prefill")
         logits, h = self.target.forward(fb, want_hidden=True)
         if self.pool.hidden is not None:
             self.pool.hidden[fb.slots] = h
@@ -417,6 +457,8 @@ class LLMEngine:
                           positions=self._h2d([r.committed for r in reqs], torch.int32),
                           slots=self._h2d([self._slot(r, r.committed) for r in reqs], torch.int64), meta=meta,
                           work2=pack_work(p2, g, self.device))
+        if self.hybrid:
+            fb.gdn = self._gdn_batch([1] * len(reqs), reqs, "prefill")
         logits, _ = self.target.forward(fb)
         nxt = self._first_token(logits, reqs) if any(r.params.temperature > 0 for r in reqs) else \
             self.vocab.argmax(logits).tolist()
@@ -556,7 +598,7 @@ class LLMEngine:
 
     def _spec_graph(self, R: int, mode: str):
         """The CUDA-graph runner for this batch shape, or None to run the step eagerly."""
-        if (self._graphs is None or mode == "sample" or self.K <= 1 or not self.eagle or self._has_moe
+        if (self._graphs is None or mode == "sample" or self.K <= 1 or not self.eagle or self._has_moe or self.hybrid
                 or (self.comm.size != 1 and not getattr(self.comm, "fused", False))):
             return None
         g = self._graphs.get(R)
@@ -664,6 +706,8 @@ class LLMEngine:
         vmeta, vw1, vw2 = mp.verify(tbits.reshape(-1))
         fb = ForwardBatch(tokens=tokens.reshape(-1), positions=vpos.reshape(-1).to(torch.int32),
                           slots=vslot.reshape(-1), meta=vmeta, work1=vw1, work2=vw2)
+        if self.hybrid:      # chain: request r's N verify tokens are rows [r*N, (r+1)*N)
+            fb.gdn = self._gdn_batch([N] * R, reqs, "verify")
         vlogits, vh = self.target.forward(fb, want_hidden=self.eagle)
         if self.pool.hidden is not None:
             self.pool.hidden[fb.slots] = vh
@@ -678,6 +722,8 @@ class LLMEngine:
 
         # ---- commit: move the accepted nodes' KV to the committed positions (fixed shape, masked) ----
         valid = acc_nodes >= 0
+        if self.hybrid:      # fold the root and the accepted chain into the GDN states
+            self.target.commit(valid.sum(1) + 1)
         jj = torch.arange(D, device=dev)[None, :].expand(R, D)
         dst = slots_of(c[:, None] + 1 + jj)
         src = torch.where(valid, slots_of(c[:, None] + acc_nodes.clamp(min=0)), dst)

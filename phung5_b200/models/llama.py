@@ -228,6 +228,7 @@ class ForwardBatch:
     work1: Optional[tuple] = None  # cascade pass-1 (items, tiles) or None
     work2: tuple = None            # main pass (items, tiles)
     logits_rows: Optional[torch.Tensor] = None  # rows whose logits are needed (None = all)
+    gdn: Optional[object] = None  # hybrid models: models.hybrid.GdnBatch (ragged token ranges, state slots, mode)
 
 
 class Communicator:

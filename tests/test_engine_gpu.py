@@ -130,3 +130,39 @@ def test_graph_replayed_step_equals_eager_step(accept, monkeypatch):
         del eng
         torch.cuda.empty_cache()
     assert outs["1"] == outs["0"]
+
+
+def test_hybrid_gdn_engine_chain_speculation_on_gpu():
+    """Hybrid GDN + attention model on the GDN kernels: chain speculation with a drafter that proposes the
+    target's own greedy continuation accepts whole chains (verify + fold of 1 + num_draft tokens per step)
+    and reproduces plain decoding; bf16 near-ties may flip an occasional token."""
+    cfg = preset("hybrid-gdn-small")
+    g = torch.Generator().manual_seed(13)
+    prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in (200, 130, 257, 64)]
+
+    def make(spec_on):
+        spec = SpecConfig(enabled=spec_on, mode="chain", num_draft=4)
+        return LLMEngine(EngineConfig(model=cfg, spec=spec, draft=DraftConfig(kind="model", num_layers=1),
+                                      cache=CacheConfig(num_pages=128, max_seqs=8)), device="cuda", max_context=2048)
+    base_eng = make(False)
+    base = base_eng.generate(prompts, SamplingParams(max_new_tokens=24))
+    ops.check_status()
+    del base_eng
+    seqs = [p + o for p, o in zip(prompts, base)]
+    eng = make(True)
+
+    def oracle_draft(fb, hidden_in):
+        rows = fb.logits_rows if fb.logits_rows is not None else torch.arange(fb.tokens.shape[0], device="cuda")
+        pos, tok = fb.positions.tolist(), fb.tokens.tolist()
+        logits = torch.zeros(rows.shape[0], cfg.vocab, device="cuda", dtype=torch.bfloat16)
+        for j, i in enumerate(rows.tolist()):
+            nxt = next((s[pos[i] + 1] for s in seqs if pos[i] + 1 < len(s) and s[pos[i]] == tok[i]), 0)
+            logits[j, nxt] = 10.0
+        return logits, None
+    eng._draft_forward = oracle_draft
+    out = eng.generate(prompts, SamplingParams(max_new_tokens=24))
+    ops.check_status()
+    same = sum(a == b for o, b0 in zip(out, base) for a, b in zip(o, b0))
+    assert same >= 0.9 * sum(len(b) for b in base), (out, base)
+    acc = [a for r in eng.reqs.values() for a in r.accepted]
+    assert sum(acc) >= 2 * len(acc)
