@@ -215,7 +215,7 @@ class JudgeAgent:
                 return neutral
 
     # S1
-    async def _s1(self, prompt, A: CandidateViews, B: CandidateViews, seed) -> dict:
+    async def _s1(self, prompt, A: CandidateViews, B: CandidateViews, seed, early_stop: bool = True) -> dict:
         neutral = AnglePenalty(penalty_a=5, penalty_b=5, reason="JSON_FAILED")
         total_w = sum(w for _, w, _ in self.s.s1_angles)
         acc, used_w, angles = 0.0, 0.0, []
@@ -237,7 +237,7 @@ class JudgeAgent:
             angles.append({"view": view, "diff": d, "pen_a": pa, "pen_b": pb, "contradictory": contradictory})
             rest = total_w - used_w
             # the weighted mean cannot cross the threshold back: stop
-            if i < len(self.s.s1_angles) - 1 and abs(acc) - rest * 10 >= self.s.s1_threshold * total_w:
+            if early_stop and i < len(self.s.s1_angles) - 1 and abs(acc) - rest * 10 >= self.s.s1_threshold * total_w:
                 break
         mean = acc / used_w
         mean_a, mean_b = sum_a / used_w, sum_b / used_w
@@ -314,11 +314,12 @@ class JudgeAgent:
             return None
         return "A" if sa > sb else "B"
 
-    async def duel(self, prompt_url: str, a: Candidate, b: Candidate, seed: int, ref_vec=None) -> JudgeVerdict:
+    async def duel(self, prompt_url: str, a: Candidate, b: Candidate, seed: int, ref_vec=None,
+                   early_stop: bool = True) -> JudgeVerdict:
         purpose_var.set("judge")
         A, B = CandidateViews(a), CandidateViews(b)
         detail: Dict[str, Any] = {}
-        s1 = await self._s1(prompt_url, A, B, seed)
+        s1 = await self._s1(prompt_url, A, B, seed, early_stop)
         detail["s1"] = s1
         winner, by = s1["choice"], "S1"
         if winner == "draw" and self.s.max_stage >= 2:

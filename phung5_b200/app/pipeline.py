@@ -106,13 +106,17 @@ class Orchestrator:
             cand_deadline = cd if deadline is None else min(deadline, cd)
         factory = CandidateFactory(task, self.coders, self.renderer, self.embedder, self.limits, prompt_url,
                                    plan_text, cand_deadline)
-        duel = make_duel(task, self.judge, self.limits, prompt_url, ref_vec, on_duel=self.stats.duel) \
-            if self.judge is not None else None
+        duel = make_duel(task, self.judge, self.limits, prompt_url, ref_vec, on_duel=self.stats.duel,
+                         es_max_round=self.s.pipeline.s1_early_stop_max_round) if self.judge is not None else None
         k = self.k
         if self.budget_k is not None:
             k = self.budget_k.initial(k)
         if k > 1 and duel is not None:
-            best = await multigen_first_iter(task, factory, duel, k, self.s.pipeline.round_robin)
+            pc = self.s.pipeline
+            rr = pc.round_robin
+            if rr == 8 and task.batch_pos >= task.batch_size - pc.round_robin_tail:
+                rr = 4                    # the batch's last prompts keep the cheaper 4-player round robin
+            best = await multigen_first_iter(task, factory, duel, k, rr, pc.shadow, pc.shadow_max_duels)
         else:
             best = None
             for i in range(max(1, k)):
@@ -265,6 +269,9 @@ class GenerationPipeline:
         deadline = t_start + eff
         task_deadline = self.s.event_bus.task_deadline_s
 
+        for i, t in enumerate(tasks):
+            t.batch_pos, t.batch_size = i, len(tasks)
+
         async def one(task: PipelineTask):
             attempt = 0
             while True:
@@ -276,7 +283,8 @@ class GenerationPipeline:
                     self.state.record_task(res)
                     return
                 attempt += 1
-                task = PipelineTask(stem=task.stem, image_url=task.image_url, seed=task.seed + 7 * attempt)
+                task = PipelineTask(stem=task.stem, image_url=task.image_url, seed=task.seed + 7 * attempt,
+                                    batch_pos=task.batch_pos, batch_size=task.batch_size)
 
         try:
             await asyncio.wait_for(asyncio.gather(*(one(t) for t in tasks)), timeout=eff)

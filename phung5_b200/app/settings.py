@@ -50,7 +50,11 @@ class PipelineConfig(BaseModel):
     prompt_timeout: float = 120.0
     use_planner: bool = False
     refinement_enabled: bool = False
-    round_robin: bool = False
+    round_robin: int = 0               # 0 off; 4: the last four (quarter winners) play all pairs; 8: the last eight
+    round_robin_tail: int = 4          # with 8: the batch's last N prompts keep the 4-player round robin
+    s1_early_stop_max_round: int = 0   # judge S1 early stop only in bracket rounds <= this (0 = every round)
+    shadow: List[str] = Field(default_factory=list)   # selection features to record without shipping: rr4, rr8
+    shadow_max_duels: int = 12
     max_attempts: int = 3
     salvage: bool = True
     seed_offset: int = 0

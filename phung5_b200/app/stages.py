@@ -12,8 +12,13 @@ Reference: `multigen_first_iter` (pipeline_service/pipeline/stages.py:1048-1217)
   seed. A duel starts as soon as both of its subtree winners are known, so judging overlaps coding and
   rendering of other leaves.
 - Draws are settled by a coin keyed on (seed, stem, positions): reproducible, no bias toward a side.
-- Round robin: when enabled and the bracket had at least 4 live semifinalists, all 6 pairs of the last
-  four are judged; 1 point per win (a draw is settled by the coin first); ties go to the bracket winner.
+- Round robin: with `round_robin = 4` (or 8) and at least that many live winners of the bracket's quarter
+  (eighth) subtrees, all pairs of them are judged; 1 point per win (a draw is settled by the coin first); ties
+  go to the bracket winner. Verdicts already computed in the bracket are reused, not re-judged.
+- Judge alignment (reference pgh_jalign.py): S1 early stop can be limited to the first bracket rounds.
+- Shadow picks (reference pgh_shadow.py): after the shipped pick is final, the pick a listed feature would
+  have made (rr4 / rr8) is computed with a bounded number of extra duels and recorded on the task, never
+  shipped.
 """
 from __future__ import annotations
 
@@ -104,12 +109,21 @@ DuelFn = Callable[[Candidate, Candidate, str], Awaitable[Candidate]]
 
 
 def make_duel(task: PipelineTask, judge: JudgeAgent, limits: StageLimits, prompt_url: str, ref_vec,
-              on_duel: Optional[Callable[[float, float], None]] = None) -> DuelFn:
+              on_duel: Optional[Callable[[float, float], None]] = None, es_max_round: int = 0) -> DuelFn:
+    cache: Dict[tuple, Candidate] = {}
+
     async def duel(left: Candidate, right: Candidate, label: str) -> Candidate:
+        key = (left.digest, right.digest)
+        if key in cache:                    # a pair the bracket already judged (round robin reuses it)
+            return cache[key]
+        if (right.digest, left.digest) in cache:
+            return cache[(right.digest, left.digest)]
+        rnd_s = label[1:].split()[0] if label.startswith("R") and label[1:2].isdigit() else ""
+        early = not (es_max_round > 0 and rnd_s and int(rnd_s) > es_max_round)
         tq = time.monotonic()
         async with limits.judge:
             ts = time.monotonic()
-            v: JudgeVerdict = await judge.duel(prompt_url, left, right, task.seed, ref_vec)
+            v: JudgeVerdict = await judge.duel(prompt_url, left, right, task.seed, ref_vec, early_stop=early)
         te = time.monotonic()
         if on_duel is not None:
             on_duel(te - ts, ts - tq)
@@ -126,12 +140,14 @@ def make_duel(task: PipelineTask, judge: JudgeAgent, limits: StageLimits, prompt
         rnd = int(label[1:].split()[0]) if label.startswith("R") and label[1:2].isdigit() else 0
         if rnd >= task.lead_round:     # the deepest bracket winner so far leads (salvage)
             task.js_code, task.scene_json, task.lead_round = w.code, w.scene, rnd
+        cache[key] = w
         return w
     return duel
 
 
-async def resolve_bracket(leaves: Dict[int, "asyncio.Future"], duel: DuelFn, n: int) -> tuple:
-    """-> (winner or None, the live winners of the bracket's four quarter subtrees when n >= 4)."""
+async def resolve_bracket(leaves: Dict[int, "asyncio.Future"], duel: DuelFn, n: int, tops=None) -> tuple:
+    """-> (winner or None, the live winners of the bracket's four quarter subtrees when n >= 4). `tops`, a dict
+    {depth: []}, also collects the live winners of the subtrees at other depths (3 = eighths)."""
     semis: List[Candidate] = []
 
     async def winner_of(lo: int, hi: int, depth: int) -> Optional[Candidate]:
@@ -149,6 +165,8 @@ async def resolve_bracket(leaves: Dict[int, "asyncio.Future"], duel: DuelFn, n: 
                 res = await duel(left, right, f"R{rnd} {lo}-{hi}")
         if depth == 2 and res is not None:
             semis.append(res)
+        if tops is not None and depth in tops and res is not None:
+            tops[depth].append(res)
         return res
 
     if n == 0:
@@ -171,14 +189,48 @@ async def round_robin(cands: List[Candidate], duel: DuelFn, bracket_winner: Cand
 
 
 async def multigen_first_iter(task: PipelineTask, factory: CandidateFactory, duel: DuelFn, k: int,
-                              use_round_robin: bool = False) -> Optional[Candidate]:
+                              round_robin_size: int = 0, shadow: Sequence[str] = (),
+                              shadow_max_duels: int = 12) -> Optional[Candidate]:
     leaves = {i: asyncio.ensure_future(factory.build(i)) for i in range(k)}
+    tops = {3: []}
     try:
-        winner, semis = await resolve_bracket(leaves, duel, k)
+        winner, semis = await resolve_bracket(leaves, duel, k, tops)
     finally:
         for f in leaves.values():
             if not f.done():
                 f.cancel()
-    if winner is not None and use_round_robin and len(semis) >= 4:
-        winner = await round_robin(semis[:4], duel, winner)
+    if winner is None:
+        return None
+    players = {4: semis, 8: tops[3]}
+    bracket_winner = winner
+    if round_robin_size in players and len(players[round_robin_size]) >= round_robin_size:
+        winner = await round_robin(players[round_robin_size][:round_robin_size], duel, winner)
+    if shadow:
+        task.shadow = await shadow_picks(task, shadow, players, duel, bracket_winner, shadow_max_duels)
+        task.shadow["shipped"] = winner.stats.get("k")
     return winner
+
+
+async def shadow_picks(task: PipelineTask, features: Sequence[str], players: Dict[int, List[Candidate]], duel: DuelFn,
+                       bracket_winner: Candidate, max_duels: int) -> dict:
+    """What each listed selection feature would have picked (recorded on the task, not shipped). Extra duels are
+    bounded by max_duels; pairs already judged come from the duel cache."""
+    out: Dict[str, object] = {}
+    budget = [max_duels]
+
+    async def capped(a, b, label):
+        if budget[0] <= 0:
+            raise RuntimeError("shadow duel budget spent")
+        budget[0] -= 1
+        return await duel(a, b, "SH " + label)
+    for f in features:
+        n = {"rr4": 4, "rr8": 8}.get(f)
+        if n is None or len(players.get(n, [])) < n:
+            out[f] = None
+            continue
+        try:
+            pick = await round_robin(players[n][:n], capped, bracket_winner)
+            out[f] = pick.stats.get("k")
+        except RuntimeError:
+            out[f] = "budget"
+    return out

@@ -77,6 +77,9 @@ class PipelineTask:
     attempts: int = 0
     salvaged: bool = False
     lead_round: int = -1                            # bracket round of the current leader (salvage)
+    shadow: Optional[dict] = None                   # shadow picks: what unshipped selection features would pick
+    batch_pos: int = 0
+    batch_size: int = 1
 
     @property
     def elapsed(self) -> float:
@@ -95,7 +98,7 @@ class PipelineTask:
              "attempts": self.attempts, "code_bytes": len(self.js_code or "")}
         if full:
             d.update({"osd": self.osd, "js_code": self.js_code, "js_errors": self.js_errors[-10:],
-                      "critic": self.critic_report, "judge_log": self.judge_log[-32:],
+                      "critic": self.critic_report, "judge_log": self.judge_log[-32:], "shadow": self.shadow,
                       "score_history": self.score_history})
         elif self.osd:
             d["osd_preview"] = (self.osd[:80] + "...") if len(self.osd) > 80 else self.osd

@@ -500,3 +500,36 @@ def test_health_watcher_transitions():
         await w.tick()
         assert st.status == MinerStatus.REPLACE
     run(go())
+
+
+def test_round_robin_eight_reuses_bracket_verdicts_and_records_shadow_picks():
+    from phung5_b200.app.stages import multigen_first_iter
+    from phung5_b200.app.state import PipelineTask
+
+    class Factory:
+        async def build(self, i):
+            return _cand(i)
+
+    calls = []
+
+    async def raw(a, b, label):
+        calls.append((a.stats["k"], b.stats["k"], label))
+        # a non-transitive preference: higher k wins except 7 always loses to 2
+        if {a.stats["k"], b.stats["k"]} == {2, 7}:
+            return a if a.stats["k"] == 2 else b
+        return a if a.stats["k"] > b.stats["k"] else b
+
+    cache = {}
+
+    async def duel(a, b, label):          # the pair cache of make_duel
+        key = tuple(sorted((a.digest, b.digest)))
+        if key not in cache:
+            cache[key] = await raw(a, b, label)
+        return cache[key]
+
+    task = PipelineTask(stem="s", image_url="x")
+    w = run(multigen_first_iter(task, Factory(), duel, 16, round_robin_size=8, shadow=["rr4"], shadow_max_duels=12))
+    assert task.shadow["shipped"] == w.stats["k"]
+    assert task.shadow["rr4"] is not None
+    pairs = {tuple(sorted(c[:2])) for c in calls}
+    assert len(pairs) == len(calls)                  # no pair was judged twice
