@@ -35,6 +35,7 @@ from ..models.llama import Communicator, ForwardBatch, LlamaModel, ModelWeights,
 from .attn_meta import PageTables, build_items, cascade_groups, make_meta, pack_work, upload
 from .kv_pool import KVPool
 from .oracle import SamplingParams
+from ..utils import nvtx as _nvtx
 from .sampling import geometric_accept_len, sample_from, seeded_coins, target_probs
 
 
@@ -198,6 +199,7 @@ class LLMEngine:
         self._consts: Dict[object, torch.Tensor] = {}
         self.host_times: Dict[str, float] = {}
         self._mark_name, self._mark_t = None, 0.0
+        self._nvtx_open = False
 
     # ------------------------------------------------------------------------------------------
     def _pages_from_memory(self, mc: ModelConfig, hkv: int, draft_layers: int, kv_layers: int) -> int:
@@ -507,6 +509,12 @@ class LLMEngine:
         """Host-side phase timer (PHX_HOST_TIMING=1): accumulates host wall time between marks per phase;
         with the device running asynchronously this is the time the host spends enqueuing each phase
         (the final commit phase includes waiting for the device)."""
+        if _nvtx.ON:
+            if self._nvtx_open:
+                _nvtx.pop()
+            self._nvtx_open = name != "host_tail"
+            if self._nvtx_open:
+                _nvtx.push(name)
         if not self._host_timing:
             return
         now = time.perf_counter()

@@ -29,6 +29,7 @@ from typing import Dict, List, Optional, Tuple
 import torch
 
 from .. import ops
+from ..utils import nvtx as _nvtx
 from ..config import ModelConfig
 from ..weights.quant import FP8_DTYPE, quant_weight_block
 
@@ -314,6 +315,7 @@ class LlamaModel:
         x = (xq, xs) if fp8 else xb
         n = cfg.num_layers
         for li in range(n):
+            _nvtx.push(f"layer{li}")
             lw = self.w.layers[li]
             qkv = lw.qkv(x)
             q = ops.rope_kv_write(qkv, fb.positions, fb.slots, self.cos_sin, self.kv_k[li], self.kv_v[li], self.hq,
@@ -334,6 +336,7 @@ class LlamaModel:
             wnext = self.w.final_norm if last else self.w.layers[li + 1].in_norm
             x = comm.ar_norm(m, wnext, cfg.rms_eps, out_bf16=last or not fp8, push_h=last and want_hidden,
                              recv=recv)
+            _nvtx.pop()
         rows = x if fb.logits_rows is None else x[fb.logits_rows]
         logits = ops.gemm_bf16(rows, self.w.lm_head)
         return logits, (h if want_hidden else None)
@@ -347,7 +350,9 @@ class LlamaModel:
         h = self.w.embed[fb.tokens]
         delta = None
         for li in range(self.cfg.num_layers):
+            _nvtx.push(f"layer{li}")
             delta = self.layer(li, h, delta, fb)
+            _nvtx.pop()
         _, _, y = ops.add_rmsnorm_quant(h, delta, self.w.final_norm, self.cfg.rms_eps, quant=False, out_bf16=True)
         rows = y if fb.logits_rows is None else y[fb.logits_rows]
         logits = ops.gemm_bf16(rows, self.w.lm_head)

@@ -77,6 +77,17 @@ class FusedCommunicator(NcclCommunicator):
         self.max_tokens = max_tokens
         self.hidden = hidden
 
+    def reset(self) -> None:
+        """Collective recovery after a kernel reported a peer timeout (status 4): every rank calls it between
+        steps; the barrier flags, CTA counter and device epoch go back to zero on every rank, between two
+        host barriers, so the next fused launch starts in step again."""
+        dist.barrier(group=self.group)
+        torch.cuda.synchronize(self.device)
+        self.ws.view("flags", torch.int32, (2 * self.size,)).zero_()
+        self.ws.view("counter", torch.int32, (4,)).zero_()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+
     def partial(self, m: int) -> torch.Tensor:
         return self.ws.view("partial", torch.bfloat16, (m, self.hidden))
 

@@ -371,3 +371,32 @@ def test_gemm_scatter_epilogue(fp8, m, n, k):
         for other in range(world):
             if other != rank:
                 assert bool((bufs[o][other] == 3.0).all())     # other ranks' slots untouched
+
+
+def test_kernels_are_deterministic():
+    """Same inputs, same bits: GEMMs (fp8 and bf16), the fused norm/quant, top-k and paged attention are run
+    twice; no kernel here reduces with atomics, so any difference would be a race."""
+    x = torch.randn(1000, 1024, device=DEV)
+    w = torch.randn(1280, 1024, device=DEV) * 0.05
+    xq, xs = quant_act_block(x)
+    wq, ws = quant_weight_block(w)
+    runs = []
+    for _ in range(2):
+        out = [ops.gemm_fp8_block(xq, xs, wq, ws).clone(), ops.gemm_bf16(x.bfloat16(), w.bfloat16()).clone()]
+        h = x[:, :512].bfloat16().clone()
+        q, s, y = ops.add_rmsnorm_quant(h, x[:, 512:].bfloat16(), torch.ones(512, device=DEV, dtype=torch.bfloat16),
+                                        1e-5, quant=True, out_bf16=True)
+        out += [h, q.view(torch.uint8), s, y]
+        lp, idx, lse = ops.topk_logprobs(out[1], 8)
+        out += [lp, idx, lse]
+        qa, kc, vc, meta = _paged_case(9, [64, 17], [300, 500], tree=True)
+        gm = _to(meta, DEV)
+        _, p2 = build_items(meta, 4)
+        it, tl = pack_work(p2, 4, DEV)
+        o = torch.zeros(qa.shape[0], 8 * 128, device=DEV, dtype=torch.bfloat16)
+        ops.paged_attention(qa.to(DEV), kc.to(DEV), vc.to(DEV), gm, 1 / math.sqrt(128), out=o, items=it, tiles=tl)
+        out.append(o)
+        torch.cuda.synchronize()
+        runs.append(out)
+    for a, b in zip(*runs):
+        assert torch.equal(a, b)

@@ -1,6 +1,7 @@
 """The fused NVLink all-reduce + RMSNorm + FP8 quant kernel (csrc/tp_fused.cu) on 2 GPUs: the fused
 forward equals the NCCL forward, and a peer that never arrives makes the bounded wait report
-kErrTimeoutPeer through the status word instead of hanging (NVLS is not used by this kernel)."""
+kErrTimeoutPeer through the status word instead of hanging; a collective reset then restores a working
+communicator (NVLS is not used by this kernel)."""
 import os
 import socket
 
@@ -105,7 +106,15 @@ def _worker(rank, world, port, q):
             status = int(ops.status_tensor(dev)[0].item())
             ops.status_tensor(dev).zero_()
         dist.barrier()
-        q.put((rank, rel, relh, status, h_exact and h_local_ok and gather_ok, y_err))
+        # recovery: the communicator is reset collectively and the next reduction is complete and correct
+        fused.reset()
+        fused.partial(m).copy_(parts[rank])
+        fused.h(m).copy_(h0)
+        torch.cuda.synchronize()
+        fused.ar_norm(m, wn.to(dev), cfg.rms_eps, push_h=True)
+        torch.cuda.synchronize()
+        recovered = int(ops.status_tensor(dev)[0].item()) == 0 and torch.equal(fused.h(m).cpu(), h_ref)
+        q.put((rank, rel, relh, status, h_exact and h_local_ok and gather_ok and recovered, y_err))
     finally:
         import torch.distributed as dist2
         dist2.destroy_process_group()
