@@ -188,7 +188,7 @@ class LLMEngine:
         self.running: List[Request] = []
         self._next_rid = 0
         self.stats = {"steps": 0, "spec_steps": 0, "tokens_out": 0, "accepted": 0, "prefill_tokens": 0,
-                      "h2d_bytes": 0, "d2h_bytes": 0}
+                      "h2d_bytes": 0, "d2h_bytes": 0, "graph_replays": 0}
         self.use_cascade = cfg.cache.enable_cascade
         import os as _os
         self._host_timing = _os.environ.get("PHX_HOST_TIMING") == "1"
@@ -541,6 +541,7 @@ class LLMEngine:
         if graph is not None:
             self._mark("graph_replay")
             packed_dev = graph.run(reqs, tables, groups, c_h, logits, root_feat, ngeo_h)
+            self.stats["graph_replays"] += 1
         else:
             self._mark("draft_tree")
             pt = tables.padded_device(dev)

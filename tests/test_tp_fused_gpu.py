@@ -182,7 +182,7 @@ def _engine_worker(rank, world, port, q):
             outs[graphs] = eng.generate(prompts, SamplingParams(max_new_tokens=40))
             ops.check_status()
             if graphs == "1":
-                replays = sum(gr.replays for gr in eng._graphs.values())
+                replays = eng.stats["graph_replays"]
             del eng
             torch.cuda.synchronize()
             dist.barrier()
@@ -216,5 +216,5 @@ def test_fused_tp2_graph_step_equals_eager():
     assert all(p.exitcode == 0 for p in procs)
     res.sort()
     assert all(ok for _, ok, _, _ in res), res
-    assert all(n >= 3 for _, _, n, _ in res), res   # graphs are cached per live batch size
+    assert all(n >= 5 for _, _, n, _ in res), res
     assert res[0][3] == res[1][3]            # both ranks emit the same tokens
