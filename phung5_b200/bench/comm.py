@@ -9,6 +9,9 @@ Times, with CUDA events after warm-up and the maximum over ranks:
   nccl     torch.distributed all_reduce of the same [M, H] bf16 partial (the unfused baseline's collective).
 NVLink bytes per ar_norm per GPU: (W-1)/W of the partial rows read (bf16) plus (W-1)/W of the fp8 rows and
 scales written; reported against the measured peer-copy bandwidth of 770 GB/s per direction.
+o_proj / down_proj + reduction: the fused path (GEMM epilogue stores rows to their owners, reduction over local
+slots) against GEMM + pulling reduction, each as a fraction of the path's roofline (the slower of the GEMM's
+FLOPs at the fp8 peak and its NVLink bytes at 770 GB/s).
 """
 from __future__ import annotations
 
@@ -62,28 +65,38 @@ def main():
         x = torch.randn(m, H, device=dev, dtype=torch.bfloat16)
         ms = _time(lambda: dist.all_reduce(x), args.iters)
         out.append({"op": "nccl_all_reduce", "M": m, "H": H, "ms": round(ms, 4)})
-    # row-parallel o_proj (K = 8192 / W) then the reduction: separate GEMM + pull, vs scatter epilogue + local sum
+    # row-parallel projections then the reduction: separate GEMM + pull, vs scatter epilogue + local sum.
+    # Roofline of the fused path: the slower of the GEMM at the fp8 peak (2 x the bf16 figure) and the bytes
+    # that must cross NVLink (reduce-scatter of bf16 rows + all-gather of fp8 rows and scales) at 770 GB/s.
     from ..models.llama import Linear
     from .. import ops
     from ..weights.quant import quant_weight_block
-    kdim = 8192 // world
-    wq, ws = quant_weight_block(torch.randn(H, kdim, device=dev) * 0.02)
-    lin = Linear(wq, ws)
+    from .kernels import peaks
+    fp8_tflops = 2 * peaks()["bf16_tflops"]
     m = 4096
-    xq, xs = ops.act_quant(torch.randn(m, kdim, device=dev, dtype=torch.bfloat16))
-    comm.h(m).zero_()
+    for name, kfull in (("o_proj", 8192), ("down_proj", 28672)):
+        kdim = kfull // world
+        wq, ws = quant_weight_block(torch.randn(H, kdim, device=dev) * 0.02)
+        lin = Linear(wq, ws)
+        xq, xs = ops.act_quant(torch.randn(m, kdim, device=dev, dtype=torch.bfloat16))
+        comm.h(m).zero_()
 
-    def pull():
-        lin((xq, xs), out=comm.partial(m))
-        comm.ar_norm(m, w, 1e-5)
+        def pull():
+            lin((xq, xs), out=comm.partial(m))
+            comm.ar_norm(m, w, 1e-5)
 
-    def push():
-        comm.project(lin, (xq, xs), m)
-        comm.ar_norm(m, w, 1e-5, recv=True)
-    gemm_ms = _time(lambda: lin((xq, xs), out=comm.partial(m)), args.iters)
-    out.append({"op": "o_proj_gemm_alone", "M": m, "K": kdim, "ms": round(gemm_ms, 4)})
-    out.append({"op": "o_proj_then_ar_norm_pull", "M": m, "K": kdim, "ms": round(_time(pull, args.iters), 4)})
-    out.append({"op": "o_proj_scatter_then_ar_norm_recv", "M": m, "K": kdim, "ms": round(_time(push, args.iters), 4)})
+        def push():
+            comm.project(lin, (xq, xs), m)
+            comm.ar_norm(m, w, 1e-5, recv=True)
+        flops = 2.0 * m * H * kdim
+        nv = (world - 1) / world * m * H * (2 + 1 + 4 / 128)
+        roof_ms = max(flops / fp8_tflops / 1e9, nv / NVLINK_GBS / 1e6)
+        gemm_ms = _time(lambda: lin((xq, xs), out=comm.partial(m)), args.iters)
+        out.append({"op": f"{name}_gemm_alone", "M": m, "K": kdim, "ms": round(gemm_ms, 4)})
+        for tag, fn in (("then_ar_norm_pull", pull), ("scatter_then_ar_norm_recv", push)):
+            ms = _time(fn, args.iters)
+            out.append({"op": f"{name}_{tag}", "M": m, "K": kdim, "ms": round(ms, 4), "roofline_ms": round(roof_ms, 4),
+                        "frac_of_roofline": round(roof_ms / ms, 3)})
     v = torch.randn(512, 8, device=dev)
     i = torch.randint(0, 1000, (512, 8), device=dev)
     lse = torch.randn(512, 1, device=dev)

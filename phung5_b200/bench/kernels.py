@@ -108,6 +108,52 @@ def case_silu_quant(m, f):
     return fn, m * (2 * f * 2 + f + 4 * f // 128), "bytes"
 
 
+def case_rmsnorm_quant(m, h):
+    hx = torch.randn(m, h, device="cuda", dtype=torch.bfloat16)
+    dx = torch.randn(m, h, device="cuda", dtype=torch.bfloat16)
+    w = torch.ones(h, device="cuda", dtype=torch.bfloat16)
+    # read h, delta; write h, fp8 q, scales
+    return (lambda: ops.add_rmsnorm_quant(hx, dx, w, 1e-5, quant=True)), m * h * (2 + 2 + 2 + 1) + m * h // 32, "bytes"
+
+
+def case_rope_kv(m, hq, hkv):
+    d, ps = 128, 64
+    qkv = torch.randn(m, (hq + 2 * hkv) * d, device="cuda", dtype=torch.bfloat16)
+    pos = torch.randint(0, 8000, (m,), device="cuda", dtype=torch.int32)
+    slots = torch.randperm(m, device="cuda").to(torch.int64)
+    cs = ops.rope_table(8192, d, 5e5, "cuda")
+    kc = torch.zeros((m + ps - 1) // ps, hkv, ps, d, device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    fn = lambda: ops.rope_kv_write(qkv, pos, slots, cs, kc, vc, hq, hkv, d)
+    return fn, m * (hq + 2 * hkv) * d * 2 * 2, "bytes"
+
+
+def case_gdn_verify(reqs, n, hk, hv):
+    from ..ops import gdn as G
+    t = reqs * n
+    q = torch.randn(t, hk, 128, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(t, hk, 128, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(t, hv, 128, device="cuda", dtype=torch.bfloat16)
+    g = -torch.rand(t, hv, device="cuda")
+    beta = torch.rand(t, hv, device="cuda")
+    state = torch.randn(reqs, hv, 128, 128, device="cuda") * 0.01
+    ts = torch.arange(reqs + 1, device="cuda", dtype=torch.int32) * n
+    slot = torch.arange(reqs, device="cuda", dtype=torch.int32)
+    fn = lambda: G.gdn_recurrent(q, k, v, g, beta, state, ts, slot, 0.088, write_state=False, stash=True)
+    # state read once per request, q/k/v read, out + stash written
+    return fn, reqs * hv * 128 * 128 * 4 + t * (2 * hk + hv) * 128 * 2 + t * hv * 128 * (2 + 8), "bytes"
+
+
+def case_raster(ntri, size):
+    from ..render import scene as S
+    g = torch.Generator().manual_seed(0)
+    tris = ((torch.rand(ntri, 3, 3, generator=g) - 0.5) * 0.2 + (torch.rand(ntri, 1, 3, generator=g) - 0.5)).cuda()
+    cols = torch.rand(ntri, 3, generator=g).cuda()
+    vp = S.view_projection(30, 20)
+    fn = lambda: S.render(tris, cols, vp, size)
+    return fn, ntri * 9 * 4 + size * size * (8 + 4), "bytes"
+
+
 def case_topk(rows, v, k):
     x = torch.randn(rows, v, device="cuda", dtype=torch.bfloat16)
     return (lambda: ops.topk_logprobs(x, k)), rows * v * 2, "bytes"
@@ -160,6 +206,10 @@ CASES = {
     "attn_suffix_tc_tp8": lambda: case_attention("suffix", "tc", hq=8, hkv=1),
     "silu_mul_quant_tp8": lambda: case_silu_quant(4096, 3584),
     "silu_mul_quant": lambda: case_silu_quant(4096, 28672),
+    "add_rmsnorm_quant": lambda: case_rmsnorm_quant(4096, 8192),
+    "rope_kv_write": lambda: case_rope_kv(4096, 64, 8),
+    "gdn_verify_64x8": lambda: case_gdn_verify(64, 8, 16, 32),
+    "raster_100k_512": lambda: case_raster(100_000, 512),
     "topk8_draft_tp8": lambda: case_topk(512, 16032, 8),
     "topk8_draft": lambda: case_topk(512, 128256, 8),
     "argmax_verify": lambda: case_topk(4096, 128256, 1),
