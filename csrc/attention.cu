@@ -299,11 +299,12 @@ __global__ void __launch_bounds__(128, 2) paged_attention_kernel(const AttnParam
         *reinterpret_cast<uint32_t*>(p.out + obase + n * 8) = pack_bf16x2(o[n][2 * h], o[n][2 * h + 1]);
     }
     if (p.out_q) {
-      const float sc = amax > 0.f ? amax / kFp8Max : 1.f;
+      float isc;
+      const float sc = fp8_block_scale(amax, &isc);
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
         __nv_fp8x2_storage_t v =
-            __nv_cvt_float2_to_fp8x2(make_float2(o[n][2 * h] / sc, o[n][2 * h + 1] / sc), __NV_SATFINITE, __NV_E4M3);
+            __nv_cvt_float2_to_fp8x2(make_float2(o[n][2 * h] * isc, o[n][2 * h + 1] * isc), __NV_SATFINITE, __NV_E4M3);
         *reinterpret_cast<__nv_fp8x2_storage_t*>(p.out_q + obase + n * 8) = v;
       }
       if ((lane & 3) == 0) p.out_qs[(size_t)head * p.T + tok] = sc;

@@ -424,7 +424,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 32; ++e) amax = fmaxf(amax, fabsf(o[e]));
         }
       }
-      const float sc = amax > 0.f ? amax / kFp8Max : 1.f;
+      float isc;
+      const float sc = fp8_block_scale(amax, &isc);
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float o[32];
@@ -439,8 +440,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.out) *reinterpret_cast<uint4*>(p.out + off) = b16;
           if (p.out_q)
             *reinterpret_cast<uint2*>(p.out_q + off) =
-                make_uint2(pack_fp8x4(o[e] / sc, o[e + 1] / sc, o[e + 2] / sc, o[e + 3] / sc),
-                           pack_fp8x4(o[e + 4] / sc, o[e + 5] / sc, o[e + 6] / sc, o[e + 7] / sc));
+                make_uint2(pack_fp8x4(o[e] * isc, o[e + 1] * isc, o[e + 2] * isc, o[e + 3] * isc),
+                           pack_fp8x4(o[e + 4] * isc, o[e + 5] * isc, o[e + 6] * isc, o[e + 7] * isc));
         }
       }
       if (row_ok) {

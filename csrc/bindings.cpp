@@ -3,7 +3,7 @@
 
 namespace phx {
 void gemm_fp8_block(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor out,
-                    torch::Tensor status, int64_t bn, int64_t max_ctas);
+                    torch::Tensor status, int64_t bn, int64_t max_ctas, bool hws);
 void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tensor status, int64_t bn,
                int64_t max_ctas);
 void add_rmsnorm_quant(torch::Tensor h, c10::optional<torch::Tensor> delta, torch::Tensor w, double eps,
@@ -34,14 +34,15 @@ void paged_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_
 void topk_logprobs(torch::Tensor logits, int64_t k, double temperature, torch::Tensor lp, torch::Tensor idx,
                    c10::optional<torch::Tensor> lse, int64_t vocab_offset);
 void gemm_fp8_grouped(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor offsets,
-                      torch::Tensor out, torch::Tensor status);
+                      torch::Tensor out, torch::Tensor status, bool hws);
 void gemm_bf16_grouped(torch::Tensor x, torch::Tensor w, torch::Tensor offsets, torch::Tensor out,
                        torch::Tensor status);
 void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M, int64_t H, double eps,
                 torch::Tensor w, bool out_bf16, bool push_h, torch::Tensor status, std::vector<int64_t> offsets,
                 int64_t s_ld, int64_t off_recv);
 void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tensor w, c10::optional<torch::Tensor> ws,
-                  torch::Tensor peer_base, int64_t off_recv, int64_t rows_per, int64_t rank, torch::Tensor status);
+                  torch::Tensor peer_base, int64_t off_recv, int64_t rows_per, int64_t rank, torch::Tensor status,
+                  bool hws);
 void tp_allgather(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t nbytes, torch::Tensor status,
                   std::vector<int64_t> offsets);
 void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,

@@ -27,6 +27,7 @@ enum : int {
   kErrTimeoutEpilogue = 3,
   kErrTimeoutPeer = 4,
   kErrBadArgs = 5,
+  kErrScaleNotPow2 = 6,   // a block scale handed to the hardware-scaled GEMM is not a positive power of two
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -162,6 +163,27 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
       "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc)
       : "memory");
 }
+// D[tmem] (+)= (A * 2^sfa) * (B * 2^sfb)^T, e4m3 x e4m3 -> f32, one UE8M0 scale per row (A) / column (B) per
+// 32-deep K step, read from TMEM at tsfa / tsfb (byte 0 of each 32-bit column: scale-factor id 0).
+__device__ __forceinline__ void umma_f8_bs(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc,
+                                           uint32_t tsfa, uint32_t tsfb) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(tsfa), "r"(tsfb)
+      : "memory");
+}
+// Shared -> TMEM copy of a 32-row x 16-byte matrix into 4 consecutive columns of lanes 0-31, repeated into
+// the other three lane quarters (the replicated layout block scale factors use). Ordered before later
+// tcgen05.mma of the same thread.
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+// generic-proxy shared-memory writes -> visible to the async proxy (TMA, tcgen05.cp, tcgen05.mma)
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 // Arrive on an mbarrier once all previously issued tcgen05 async ops of this thread complete.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -213,6 +235,23 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
   return d;
 }
 
+// UMMA shared-memory descriptor for a non-swizzled K-major matrix of 8-row x 16-byte core matrices stored
+// row after row (16 B apart, 128 B per core matrix); both byte offsets are 128 B, [61,64) layout = 0.
+__device__ __forceinline__ uint64_t sdesc_plain(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFF) >> 4);
+  d |= static_cast<uint64_t>(128 >> 4) << 16;
+  d |= static_cast<uint64_t>(128 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  return d;
+}
+
+// Instruction descriptor of the block-scaled kind::mxf8f6f4 MMA: e4m3 A and B (formats 0), K-major, f32
+// accumulate, UE8M0 scales (bit 23), scale-factor ids 0 (bits [4,6) for B, [29,31) for A).
+__host__ __device__ constexpr uint32_t idesc_make_bs(int m, int n) {
+  return (1u << 23) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
 // Instruction descriptor (dense, K-major A and B, f32 accumulate).
 // a/b format: kind::f8f6f4 -> 0 = E4M3; kind::f16 -> 0 = F16, 1 = BF16.
 __host__ __device__ constexpr uint32_t idesc_make(int m, int n, int ab_format) {
@@ -233,6 +272,22 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
   __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&u);
   return __bfloat1622float2(v);
 }
+// Block scale for e4m3: the smallest power of two >= amax / 448 (1 for an all-zero block), with its exact
+// reciprocal. Built from the IEEE fields of amax / 448: round the exponent up unless the mantissa is zero. A
+// power-of-two scale is exactly representable as UE8M0, the scale format tcgen05 applies in hardware, and
+// quantizing by multiplying with its reciprocal is exact.
+__device__ __forceinline__ float fp8_block_scale(float amax, float* inv) {
+  if (!(amax > 0.f)) {
+    *inv = 1.f;
+    return 1.f;
+  }
+  const uint32_t bits = __float_as_uint(amax / kFp8Max);
+  int e = static_cast<int>((bits >> 23) & 0xFF) + ((bits & 0x7FFFFF) ? 1 : 0);
+  e = e < 1 ? 1 : (e > 253 ? 253 : e);
+  *inv = __uint_as_float(static_cast<uint32_t>(254 - e) << 23);
+  return __uint_as_float(static_cast<uint32_t>(e) << 23);
+}
+
 // four floats -> four e4m3 bytes (saturating, round to nearest even)
 __device__ __forceinline__ uint32_t pack_fp8x4(float a, float b, float c, float d) {
   __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);

@@ -13,11 +13,19 @@
 //               ring of SWIZZLE_128B tiles, one mbarrier (full/empty) pair per stage.
 //   warp 1      allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=BN, K=32 fp8 or 16 bf16 per
 //               instruction, 4 per stage) into one of two TMEM accumulators and commits to mbarriers.
-//   warps 2-9   epilogue. fp8: every 128-wide K block lands in a fresh TMEM accumulator; the epilogue
-//               reads it with tcgen05.ld and adds it, scaled by xs[kb,row]*ws[nblk,kb], into fp32
-//               registers (exact fp32 scale application per K block), while the MMA fills the other
-//               accumulator with the next K block. bf16: the MMA accumulates the whole K range in TMEM
-//               and the epilogue drains it once per tile, overlapped with the next tile's MMAs.
+//   warps 2-9   epilogue. bf16, and fp8 with hardware scaling (HWS, the default): the MMA accumulates the
+//               whole K range in TMEM and the epilogue drains it once per tile into registers, frees the
+//               accumulator, then converts and stores while the next tile's MMAs run.
+//               fp8 with software promotion (HWS off): every 128-wide K block lands in a fresh TMEM
+//               accumulator; the epilogue reads it with tcgen05.ld and adds it, scaled by
+//               xs[kb,row]*ws[nblk,kb], into fp32 registers, while the MMA fills the other accumulator.
+//   HWS: the block scales are powers of two (see fp8_block_scale), so they are exact UE8M0 values and the
+//   tensor core applies them itself: tcgen05.mma kind::mxf8f6f4.block_scale reads one scale per A row and
+//   per B column for each 32-deep K step from TMEM. Per stage the producer warp converts the stage's 128
+//   activation scales and BN/128 weight scales to exponent bytes in shared memory, in the replicated
+//   32-lane x 4-column layout, and the MMA thread moves them to TMEM with tcgen05.cp (.32x128b.warpx4)
+//   right before the stage's four MMAs (cp -> mma from one thread runs in issue order). A scale that is
+//   not a positive power of two sets kErrScaleNotPow2 in the status word.
 //   Tiles are walked M-fastest so CTAs running together share weight (B) columns in L2.
 //   No TMA multicast and no clusters: every CTA loads its own tiles.
 #include <ATen/cuda/CUDAContext.h>
@@ -34,10 +42,13 @@ constexpr int kBM = 128;
 constexpr int kEpiWarps = 8;
 constexpr int kGemmThreads = 64 + kEpiWarps * 32;  // producer warp, MMA warp, 8 epilogue warps
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool HWS = false>
 struct GemmSmem {
   uint8_t a[STAGES][kBM * 128];
   uint8_t b[STAGES][BN * 128];
+  // HWS scale-factor staging, per stage: activation scales (32 lanes x 16 B: byte 4c of lane l = row 32c+l),
+  // then BN/128 groups of weight scales in the same shape (column 32c+l of the group's 128)
+  uint8_t sf[HWS ? STAGES : 1][HWS ? 512 * (1 + BN / 128) : 16];
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   uint64_t tfull[512 / BN];
@@ -113,19 +124,25 @@ struct ScatterArgs {
   int rows_per, rank;
 };
 
-template <int BN, bool FP8, bool SCATTER>
+template <int BN, bool FP8, bool SCATTER, bool HWS>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       __nv_bfloat16* __restrict__ out, int M, int N, int K, int ldc, const float* __restrict__ sa,
                       const float* __restrict__ sb, int* status, const int* __restrict__ grp_off, int groups,
                       int max_tiles, const ScatterArgs sc) {
+  static_assert(!HWS || FP8, "hardware scaling is an fp8 mode");
   constexpr int STAGES = gemm_stages<BN, SCATTER>();
   constexpr int BKE = FP8 ? 128 : 64;  // K elements per 128-byte stage row
-  constexpr uint32_t IDESC = idesc_make(kBM, BN, FP8 ? 0 : 1);
-  constexpr int NBUF = 512 / BN;        // TMEM accumulators (all 512 columns)
+  constexpr uint32_t IDESC = HWS ? idesc_make_bs(kBM, BN) : idesc_make(kBM, BN, FP8 ? 0 : 1);
+  // TMEM accumulators: all 512 columns, except under HWS, where columns [256, 256 + STAGES * SF_COLS) hold
+  // the stages' scale factors (BN = 256: one accumulator, freed as soon as the epilogue has drained it)
+  constexpr int NBUF = HWS ? 256 / BN : 512 / BN;
+  constexpr int SF_COLS = 4 + BN / 32;  // per stage: 4 columns of A scales, BN/32 of B scales
+  static_assert(!HWS || 256 + STAGES * SF_COLS <= 512, "scale factors exceed TMEM");
   constexpr uint32_t TMEM_COLS = 512;
   constexpr int CPT = BN / 2;  // columns per epilogue thread
-  using Smem = GemmSmem<BN, STAGES>;
+  constexpr bool PROMOTE = FP8 && !HWS;   // per-K-block software scale promotion
+  using Smem = GemmSmem<BN, STAGES, HWS>;
 
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023));
@@ -163,7 +180,81 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = s.tmem_base;
   volatile int* abort = &s.abort;
 
-  if (warp == 0) {
+  if (warp == 0 && HWS) {
+    // ---------------- TMA producer + scale-factor staging (whole warp) ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0;
+    bool bad = false;
+    float fa[4] = {1.f, 1.f, 1.f, 1.f}, fb[BN / 128];
+#pragma unroll
+    for (int g = 0; g < BN / 128; ++g) fb[g] = 1.f;
+    // the scales of the next (tile, k block) are loaded one step ahead of their stage
+    auto load_sf = [&](int tt, int kb) {
+      if (tt >= num_tiles) return;
+      const TileInfo ti = tile_info<BN>(tt, M, N, m_tiles, n_tiles, grp_off, groups);
+      if (!ti.valid) return;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int r = ti.m0 + 32 * c + lane;
+        fa[c] = sa[(size_t)kb * M + (r < M ? r : M - 1)];
+      }
+      const int nb_last = ti.sb_base + (N + 127) / 128 - 1;
+#pragma unroll
+      for (int g = 0; g < BN / 128; ++g) {
+        const int nb = ti.sb_base + (ti.n0 >> 7) + g;
+        fb[g] = sb[(size_t)(nb < nb_last ? nb : nb_last) * kblocks + kb];
+      }
+    };
+    auto ue8m0 = [&](float v) -> uint32_t {
+      const uint32_t u = __float_as_uint(v);
+      bad |= (u & 0x807FFFFFu) != 0u || (u >> 23) == 0u;
+      return (u >> 23) & 0xFFu;
+    };
+    load_sf(blockIdx.x, 0);
+    for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x) {
+      const TileInfo ti = tile_info<BN>(t, M, N, m_tiles, n_tiles, grp_off, groups);
+      if (!ti.valid) break;
+      bool ok = true;
+      for (int ks = 0; ks < ksteps; ++ks) {
+        const uint4 wa = make_uint4(ue8m0(fa[0]), ue8m0(fa[1]), ue8m0(fa[2]), ue8m0(fa[3]));
+        uint32_t wb[BN / 128];
+#pragma unroll
+        for (int g = 0; g < BN / 128; ++g) wb[g] = ue8m0(fb[g]);
+        if (ks + 1 < ksteps) load_sf(t, ks + 1);
+        else load_sf(t + gridDim.x, 0);
+        int got = 1;
+        if (lane == 0) got = mbar_wait(&s.empty[stage], phase ^ 1, status, kErrTimeoutProducer, abort);
+        if (!__shfl_sync(0xffffffffu, got, 0)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sf = s.sf[stage];
+        *reinterpret_cast<uint4*>(sf + 16 * lane) = wa;
+#pragma unroll
+        for (int g = 0; g < BN / 128; ++g)
+          *reinterpret_cast<uint4*>(sf + 512 * (1 + g) + 16 * lane) = make_uint4(wb[g], wb[g], wb[g], wb[g]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&s.full[stage], (kBM + BN) * 128);
+          tma_load_2d(&tmA, &s.full[stage], s.a[stage], ks * BKE, ti.m0);
+          tma_load_2d(&tmB, &s.full[stage], s.b[stage], ks * BKE, ti.b0);
+        }
+        ++issued;
+        if (++stage == STAGES) stage = 0, phase ^= 1;
+      }
+      if (!ok) break;
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicCAS(status, 0, kErrScaleNotPow2);
+    if (lane == 0) {
+      volatile int never = 0;
+      for (int i = 0; i < STAGES && i < issued; ++i) {
+        if (--stage < 0) stage = STAGES - 1, phase ^= 1;
+        mbar_wait(&s.full[stage], phase, nullptr, 0, &never);
+      }
+    }
+  } else if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       int stage = 0;
@@ -198,8 +289,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x) {
         if (grp_off && !tile_info<BN>(t, M, N, m_tiles, n_tiles, grp_off, groups).valid) break;
         for (int ks = 0; ks < ksteps; ++ks) {
-          const bool new_acc = FP8 || ks == 0;
-          const bool end_acc = FP8 || ks == ksteps - 1;
+          const bool new_acc = PROMOTE || ks == 0;
+          const bool end_acc = PROMOTE || ks == ksteps - 1;
           if (new_acc) {
             if (!mbar_wait(&s.tempty[tb], tphase ^ 1, status, kErrTimeoutMma, abort)) goto mma_done;
             tc_fence_after();
@@ -210,10 +301,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint64_t da = sdesc_sw128(smem_u32(s.a[stage]));
             const uint64_t db = sdesc_sw128(smem_u32(s.b[stage]));
             const uint32_t dtm = tmem_base + tb * BN;
+            const uint32_t tsf = tmem_base + 256 + stage * SF_COLS;   // HWS: this stage's scale columns
+            if constexpr (HWS) {
+              const uint32_t sfs = smem_u32(s.sf[stage]);
+              tmem_cp_32x128b_x4(tsf, sdesc_plain(sfs));
+#pragma unroll
+              for (int g = 0; g < BN / 128; ++g) tmem_cp_32x128b_x4(tsf + 4 + 4 * g, sdesc_plain(sfs + 512 * (1 + g)));
+            }
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const uint32_t acc = new_acc ? (k > 0) : 1u;
-              if (FP8)
+              if constexpr (HWS)
+                umma_f8_bs(dtm, da + 2 * k, db + 2 * k, IDESC, acc, tsf, tsf + 4);
+              else if constexpr (FP8)
                 umma_f8(dtm, da + 2 * k, db + 2 * k, IDESC, acc);
               else
                 umma_f16(dtm, da + 2 * k, db + 2 * k, IDESC, acc);
@@ -240,13 +340,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int tb = 0;
     uint32_t tphase = 0;
     float2 acc[CPT / 2];          // packed pairs: the promotion uses the f32x2 FMA (half the issue slots)
-    const int epi_blocks = FP8 ? kblocks : 1;
+    const int epi_blocks = PROMOTE ? kblocks : 1;
     // the scales of the next (tile, k block) are loaded one step ahead, so their latency overlaps the
     // current block's TMEM drain
     int t = blockIdx.x;
     float sa_next = 0.f, sb_next = 0.f;
     auto load_scales = [&](int tt, int kb) {
-      if (!FP8 || tt >= num_tiles) return;
+      if (!PROMOTE || tt >= num_tiles) return;
       const TileInfo ti = tile_info<BN>(tt, M, N, m_tiles, n_tiles, grp_off, groups);
       if (!ti.valid) return;
       const int rr = ti.m0 + sub * 32 + lane;
@@ -262,7 +362,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int col0 = ti.n0 + half * CPT;
       const bool col_ok = col0 < N;
       for (int kb = 0; kb < epi_blocks; ++kb) {
-        const float scale = FP8 ? sa_next * sb_next : 1.f;
+        const float scale = PROMOTE ? sa_next * sb_next : 1.f;
         if (kb + 1 < epi_blocks) load_scales(t, kb + 1);
         else load_scales(t + gridDim.x, 0);
         const bool ok = mbar_wait(&s.tfull[tb], tphase, status, kErrTimeoutEpilogue, abort);
@@ -282,7 +382,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int j = 0; j < BATCH / 2; ++j) {
             const float2 v = make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
             float2& a = acc[(c0 >> 1) + j];
-            if (FP8)
+            if (PROMOTE)
               a = kb == 0 ? __fmul2_rn(v, s2) : __ffma2_rn(v, s2, a);
             else
               a = v;
@@ -360,7 +460,7 @@ int num_sms() {
   return n;
 }
 
-template <int BN, bool FP8, bool SCATTER = false>
+template <int BN, bool FP8, bool SCATTER = false, bool HWS = false>
 void launch_gemm_ptr(const torch::Tensor& a, const torch::Tensor& b, __nv_bfloat16* out_ptr, int ldc, int n_out,
                      const float* sa, const float* sb, int* status, cudaStream_t stream, int max_ctas,
                      const int* grp_off, int groups, ScatterArgs sc) {
@@ -374,27 +474,28 @@ void launch_gemm_ptr(const torch::Tensor& a, const torch::Tensor& b, __nv_bfloat
   CUtensorMap tb = make_tmap_2d(b.data_ptr(), dt, K, b.size(0), (uint64_t)b.stride(0) * esz, box_inner, BN,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
   constexpr int STAGES = gemm_stages<BN, SCATTER>();
-  const size_t smem = ((sizeof(GemmSmem<BN, STAGES>) + 127) & ~size_t(127)) + 1024 +
+  const size_t smem = ((sizeof(GemmSmem<BN, STAGES, HWS>) + 127) & ~size_t(127)) + 1024 +
                       (SCATTER ? (size_t)kEpiWarps * 32 * scatter_row_bytes<BN>() : 0);
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8, SCATTER>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8, SCATTER, HWS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
     attr_set = true;
   }
   // grouped: at most M/128 + groups row tiles in total (one partial tile per group)
   const int m_tiles_bound = grp_off ? (M + kBM - 1) / kBM + groups : (M + kBM - 1) / kBM;
   const int tiles = m_tiles_bound * ((N + BN - 1) / BN);
   int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
-  gemm_sm100_kernel<BN, FP8, SCATTER><<<grid, kGemmThreads, smem, stream>>>(ta, tb, out_ptr, M, N, K, ldc, sa, sb,
-                                                                             status, grp_off, groups, tiles, sc);
+  gemm_sm100_kernel<BN, FP8, SCATTER, HWS><<<grid, kGemmThreads, smem, stream>>>(
+      ta, tb, out_ptr, M, N, K, ldc, sa, sb, status, grp_off, groups, tiles, sc);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-template <int BN, bool FP8>
+template <int BN, bool FP8, bool HWS = false>
 void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, const float* sa,
                  const float* sb, int* status, cudaStream_t stream, int max_ctas, const int* grp_off = nullptr,
                  int groups = 0) {
-  launch_gemm_ptr<BN, FP8, false>(a, b, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (int)out.stride(0),
+  launch_gemm_ptr<BN, FP8, false, HWS>(a, b, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (int)out.stride(0),
                            (int)out.size(1), sa, sb, status, stream, max_ctas, grp_off, groups,
                            ScatterArgs{nullptr, 0, 1, 0});
 }
@@ -408,8 +509,9 @@ static int pick_bn(int M, int N) {
   return 256;
 }
 
+// hws: the tensor core applies the (power-of-two) block scales; otherwise the epilogue promotes per K block.
 void gemm_fp8_block(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor out,
-                    torch::Tensor status, int64_t bn, int64_t max_ctas) {
+                    torch::Tensor status, int64_t bn, int64_t max_ctas, bool hws) {
   TORCH_CHECK(xq.is_cuda() && wq.is_cuda() && out.is_cuda());
   TORCH_CHECK(xq.scalar_type() == at::kFloat8_e4m3fn && wq.scalar_type() == at::kFloat8_e4m3fn);
   TORCH_CHECK(out.scalar_type() == at::kBFloat16);
@@ -425,18 +527,22 @@ void gemm_fp8_block(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch:
   const at::cuda::CUDAGuard guard(xq.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   const int b = bn > 0 ? (int)bn : pick_bn(M, N);
-  if (b == 256)
-    launch_gemm<256, true>(xq, wq, out, xs.data_ptr<float>(), ws.data_ptr<float>(), status.data_ptr<int>(), stream,
-                           (int)max_ctas);
-  else
-    launch_gemm<128, true>(xq, wq, out, xs.data_ptr<float>(), ws.data_ptr<float>(), status.data_ptr<int>(), stream,
-                           (int)max_ctas);
+  const float* sa = xs.data_ptr<float>();
+  const float* sb = ws.data_ptr<float>();
+  int* st = status.data_ptr<int>();
+  if (hws) {
+    if (b == 256) launch_gemm<256, true, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
+    else launch_gemm<128, true, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
+  } else {
+    if (b == 256) launch_gemm<256, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
+    else launch_gemm<128, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
+  }
 }
 
 // Grouped block-scaled FP8 GEMM (MoE experts): xq [Mtot, K] rows sorted by group, group e = rows
 // [offsets[e], offsets[e+1]) (device int32 [G+1]); wq [G*N, K]; ws [G*ceil(N/128), K/128]; out [Mtot, N].
 void gemm_fp8_grouped(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor offsets,
-                      torch::Tensor out, torch::Tensor status) {
+                      torch::Tensor out, torch::Tensor status, bool hws) {
   TORCH_CHECK(xq.scalar_type() == at::kFloat8_e4m3fn && wq.scalar_type() == at::kFloat8_e4m3fn);
   TORCH_CHECK(offsets.scalar_type() == at::kInt && offsets.is_cuda() && offsets.dim() == 1);
   const int M = xq.size(0), K = xq.size(1), N = out.size(1), G = offsets.size(0) - 1;
@@ -446,8 +552,12 @@ void gemm_fp8_grouped(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torc
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(xq.device());
   auto stream = at::cuda::getCurrentCUDAStream();
-  launch_gemm<256, true>(xq, wq, out, xs.data_ptr<float>(), ws.data_ptr<float>(), status.data_ptr<int>(), stream, 0,
-                         offsets.data_ptr<int>(), G);
+  if (hws)
+    launch_gemm<256, true, true>(xq, wq, out, xs.data_ptr<float>(), ws.data_ptr<float>(), status.data_ptr<int>(),
+                                 stream, 0, offsets.data_ptr<int>(), G);
+  else
+    launch_gemm<256, true>(xq, wq, out, xs.data_ptr<float>(), ws.data_ptr<float>(), status.data_ptr<int>(), stream, 0,
+                           offsets.data_ptr<int>(), G);
 }
 
 // Grouped bf16 GEMM (bf16 MoE experts); same layout as gemm_fp8_grouped without scales.
@@ -483,7 +593,8 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tenso
 
 // Row-parallel projection with the scatter epilogue (see ScatterArgs): fp8 (ws defined) or bf16 operands.
 void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tensor w, c10::optional<torch::Tensor> ws,
-                  torch::Tensor peer_base, int64_t off_recv, int64_t rows_per, int64_t rank, torch::Tensor status) {
+                  torch::Tensor peer_base, int64_t off_recv, int64_t rows_per, int64_t rank, torch::Tensor status,
+                  bool hws) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && peer_base.is_cuda() && peer_base.scalar_type() == at::kLong);
   const int M = x.size(0), K = x.size(1), N = w.size(0);
   TORCH_CHECK(w.size(1) == K && N % 8 == 0 && x.stride(1) == 1 && w.stride(1) == 1);
@@ -500,10 +611,14 @@ void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tenso
     TORCH_CHECK(ws->is_contiguous() && ws->size(0) == (N + 127) / 128 && ws->size(1) == K / 128);
     const float* sa = xs->data_ptr<float>();
     const float* sb = ws->data_ptr<float>();
-    if (b == 256)
-      launch_gemm_ptr<256, true, true>(x, w, nullptr, N, N, sa, sb, status.data_ptr<int>(), stream, 0, nullptr, 0, sc);
-    else
-      launch_gemm_ptr<128, true, true>(x, w, nullptr, N, N, sa, sb, status.data_ptr<int>(), stream, 0, nullptr, 0, sc);
+    int* st = status.data_ptr<int>();
+    if (hws) {
+      if (b == 256) launch_gemm_ptr<256, true, true, true>(x, w, nullptr, N, N, sa, sb, st, stream, 0, nullptr, 0, sc);
+      else launch_gemm_ptr<128, true, true, true>(x, w, nullptr, N, N, sa, sb, st, stream, 0, nullptr, 0, sc);
+    } else {
+      if (b == 256) launch_gemm_ptr<256, true, true>(x, w, nullptr, N, N, sa, sb, st, stream, 0, nullptr, 0, sc);
+      else launch_gemm_ptr<128, true, true>(x, w, nullptr, N, N, sa, sb, st, stream, 0, nullptr, 0, sc);
+    }
   } else {
     TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && K % 64 == 0);
     if (b == 256)

@@ -8,7 +8,8 @@
 //   act_quant         : bf16 [M, K] -> block-scaled fp8.
 //   rope_kv_write     : rotate-half RoPE of q and k from the fused qkv projection, q to a packed
 //                       [M, Hq, D] buffer, k and v into the paged cache [pages, Hkv, page, D].
-// Scale = amax / 448 per 128-block (1 for an all-zero block); q = v / scale, saturating to e4m3.
+// Scale = the smallest power of two >= amax / 448 per 128-block (1 for an all-zero block); q = v * (1 / scale),
+// saturating to e4m3 (a power-of-two scale is exact in UE8M0, the scale format of the hardware-scaled GEMM).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -47,10 +48,11 @@ __device__ __forceinline__ void quant_store8(const float (&y)[8], int chunk, int
   for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(y[j]));
   amax = halfwarp_max(amax);
   if (!valid) return;
-  const float scale = amax > 0.f ? amax / kFp8Max : 1.0f;
+  float inv;
+  const float scale = fp8_block_scale(amax, &inv);
   uint2 pk;
-  pk.x = pack_fp8x4(y[0] / scale, y[1] / scale, y[2] / scale, y[3] / scale);
-  pk.y = pack_fp8x4(y[4] / scale, y[5] / scale, y[6] / scale, y[7] / scale);
+  pk.x = pack_fp8x4(y[0] * inv, y[1] * inv, y[2] * inv, y[3] * inv);
+  pk.y = pack_fp8x4(y[4] * inv, y[5] * inv, y[6] * inv, y[7] * inv);
   *reinterpret_cast<uint2*>(q + (size_t)row * ld_q + chunk * 8) = pk;
   if ((chunk & 15) == 0) qs[(size_t)(chunk >> 4) * M + row] = scale;
 }

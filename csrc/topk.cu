@@ -2,6 +2,7 @@
 //
 //   topk_logprobs(logits [R, V] bf16, k, temperature) -> (logprob [R, k] fp32, index [R, k] int64,
 //                                                         lse [R] fp32)
+// Without an lse output (argmax use) the kernel skips the exponentials and returns the raw x/T values.
 // logprob = x/T - logsumexp(x/T) of the k largest x (ties toward the lower index), with T applied by
 // IEEE division (the reference's verify top-k divides with div.rn.f32,
 // docker/opt/v5/topkbf_normcfg/topkbf/kopt_topkbf.py:134-141). k = 1 is argmax.
@@ -83,13 +84,15 @@ __device__ __forceinline__ void warp_select(float* vals, int* idxs, int n, float
   }
 }
 
-template <int K>
+template <int K, bool LSE>
 __global__ void __launch_bounds__(kTopkThreads) topk_stage1(const __nv_bfloat16* __restrict__ logits, int V, int ld,
                                                             int splits, int chunk, float temp,
                                                             float* __restrict__ pv, int* __restrict__ pi,
                                                             float* __restrict__ pm, float* __restrict__ ps) {
   __shared__ float sv[kTopkThreads * K];
   __shared__ int si[kTopkThreads * K];
+  __shared__ float wv[(kTopkThreads / 32) * K];
+  __shared__ int wi[(kTopkThreads / 32) * K];
   __shared__ float red_m[kTopkThreads / 32], red_s[kTopkThreads / 32];
   const int row = blockIdx.x / splits, sp = blockIdx.x % splits;
   const int v0 = sp * chunk, v1 = min(V, v0 + chunk);
@@ -101,25 +104,38 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stage1(const __nv_bfloat16*
   auto take = [&](float val, int idx) {
     if (scaled) val = __fdiv_rn(val, temp);
     if (val == -INFINITY) return;
-    if (val > m) {
-      s = s * expf(m - val) + 1.f;
-      m = val;
-    } else {
-      s += expf(val - m);
+    if constexpr (LSE) {
+      if (val > m) {
+        s = s * expf(m - val) + 1.f;
+        m = val;
+      } else {
+        s += expf(val - m);
+      }
     }
     tk.push(val, idx);
   };
   if ((ld % 8) == 0) {
     // 16-byte vector body over whole 8-element groups (v0 is a multiple of 8), then the < 8 tail
     const int vend = v0 + ((v1 - v0) / 8) * 8;
-    for (int v = v0 + threadIdx.x * 8; v < vend; v += kTopkThreads * 8) {
-      const uint4 w = *reinterpret_cast<const uint4*>(x + v);
-      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    // argmax (K = 1): four 16-byte loads in flight per thread before any is consumed, the scan is otherwise
+    // latency-bound; K > 1 keeps one (measured faster there: the register top-k list competes for registers)
+    constexpr int U = K == 1 ? 4 : 1, STEP = kTopkThreads * 8;
+    for (int vb = v0 + threadIdx.x * 8; vb < vend; vb += U * STEP) {
+      uint4 w[U];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = unpack_bf16x2(ww[e]);
-        take(f.x, v + 2 * e);
-        take(f.y, v + 2 * e + 1);
+      for (int u = 0; u < U; ++u)
+        if (vb + u * STEP < vend) w[u] = __ldcs(reinterpret_cast<const uint4*>(x + vb + u * STEP));
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int v = vb + u * STEP;
+        if (v >= vend) break;
+        const uint32_t ww[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_bf16x2(ww[e]);
+          take(f.x, v + 2 * e);
+          take(f.y, v + 2 * e + 1);
+        }
       }
     }
     for (int t = vend + threadIdx.x; t < v1; t += kTopkThreads) take(__bfloat162float(x[t]), t);
@@ -137,6 +153,9 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stage1(const __nv_bfloat16*
   if (lane == 0) red_m[w] = bm, red_s[w] = bs;
 #pragma unroll
   for (int k = 0; k < K; ++k) sv[threadIdx.x * K + k] = tk.v[k], si[threadIdx.x * K + k] = tk.i[k];
+  __syncwarp();
+  // two-level selection: every warp reduces its 32 threads' lists to K, then warp 0 selects from 8 x K
+  warp_select<K>(sv + w * 32 * K, si + w * 32 * K, 32 * K, wv + w * K, wi + w * K);
   __syncthreads();
   if (w == 0) {
     float cm = lane < kTopkThreads / 32 ? red_m[lane] : -INFINITY;
@@ -147,7 +166,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stage1(const __nv_bfloat16*
       ms_combine(cm, cs, om, os);
     }
     const size_t base = (size_t)blockIdx.x * K;
-    warp_select<K>(sv, si, kTopkThreads * K, pv + base, pi + base);
+    warp_select<K>(wv, wi, (kTopkThreads / 32) * K, pv + base, pi + base);
     if (lane == 0) pm[blockIdx.x] = cm, ps[blockIdx.x] = cs;
   }
 }
@@ -155,7 +174,8 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stage1(const __nv_bfloat16*
 template <int K>
 __global__ void topk_stage2(int rows, int splits, int k_out, const float* __restrict__ pv, const int* __restrict__ pi,
                             const float* __restrict__ pm, const float* __restrict__ ps, float* __restrict__ out_lp,
-                            int64_t* __restrict__ out_idx, float* __restrict__ out_lse, int vocab_offset) {
+                            int64_t* __restrict__ out_idx, float* __restrict__ out_lse, int vocab_offset,
+                            bool with_lse) {
   extern __shared__ uint8_t smem[];
   const int warps = blockDim.x >> 5;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -178,7 +198,7 @@ __global__ void topk_stage2(int rows, int splits, int k_out, const float* __rest
   __shared__ float ov[32][kTopkMaxK];
   __shared__ int oi[32][kTopkMaxK];
   warp_select<K>(vals, idxs, splits * K, ov[w], oi[w]);
-  const float lse = m + logf(s);
+  const float lse = with_lse ? m + logf(s) : 0.f;
   if (lane < k_out) {
     out_lp[(size_t)row * k_out + lane] = ov[w][lane] - lse;
     out_idx[(size_t)row * k_out + lane] = (int64_t)oi[w][lane] + vocab_offset;
@@ -199,7 +219,8 @@ static void run_topk(const torch::Tensor& logits, int64_t k, double temperature,
   auto pi = torch::empty({R * splits * K}, opts.dtype(at::kInt));
   auto pm = torch::empty({R * splits}, opts);
   auto ps = torch::empty({R * splits}, opts);
-  topk_stage1<K><<<R * splits, kTopkThreads, 0, stream>>>(
+  auto stage1 = lse ? topk_stage1<K, true> : topk_stage1<K, false>;
+  stage1<<<R * splits, kTopkThreads, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), V, ld, splits, chunk, (float)temperature,
       pv.data_ptr<float>(), pi.data_ptr<int>(), pm.data_ptr<float>(), ps.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -207,7 +228,8 @@ static void run_topk(const torch::Tensor& logits, int64_t k, double temperature,
   const size_t smem = (size_t)warps * splits * K * 8;
   topk_stage2<K><<<(R + warps - 1) / warps, warps * 32, smem, stream>>>(
       R, splits, (int)k, pv.data_ptr<float>(), pi.data_ptr<int>(), pm.data_ptr<float>(), ps.data_ptr<float>(),
-      lp.data_ptr<float>(), idx.data_ptr<int64_t>(), lse ? lse->data_ptr<float>() : nullptr, (int)vocab_offset);
+      lp.data_ptr<float>(), idx.data_ptr<int64_t>(), lse ? lse->data_ptr<float>() : nullptr, (int)vocab_offset,
+      lse.has_value());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

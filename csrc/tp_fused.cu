@@ -225,9 +225,10 @@ __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         if (valid) {
-          const float sc = amax > 0.f ? amax / kFp8Max : 1.f;
-          const uint2 q = make_uint2(pack_fp8x4(y[0] / sc, y[1] / sc, y[2] / sc, y[3] / sc),
-                                     pack_fp8x4(y[4] / sc, y[5] / sc, y[6] / sc, y[7] / sc));
+          float isc;
+          const float sc = fp8_block_scale(amax, &isc);
+          const uint2 q = make_uint2(pack_fp8x4(y[0] * isc, y[1] * isc, y[2] * isc, y[3] * isc),
+                                     pack_fp8x4(y[4] * isc, y[5] * isc, y[6] * isc, y[7] * isc));
           const size_t qoff = (size_t)row * H + c * 8;
           const size_t soff = ((size_t)(c >> 4) * a.s_ld + row) * 4;
           for (int p = 0; p < W; ++p) {

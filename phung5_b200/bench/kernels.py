@@ -18,7 +18,7 @@ import torch
 
 from .. import ops
 from ..engine.attn_meta import build_items, cascade_groups, make_meta, pack_work
-from ..weights.quant import FP8_DTYPE
+from ..weights.quant import FP8_DTYPE, pow2_scale
 
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
@@ -62,7 +62,7 @@ def case_gemm_fp8(m, n, k, bn=0):
     x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
     xq, xs = ops.act_quant(x)
     wq = (torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.05).to(FP8_DTYPE)
-    ws = torch.rand((n + 127) // 128, k // 128, device="cuda") * 0.01
+    ws = pow2_scale(torch.rand((n + 127) // 128, k // 128, device="cuda") * 4.48)   # ~1e-2, UE8M0-exact
     out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
     fn = lambda: ops.gemm_fp8_block(xq, xs, wq, ws, out=out, bn=bn)
     return fn, 2.0 * m * n * k, "fp8"
@@ -154,9 +154,9 @@ def case_raster(ntri, size):
     return fn, ntri * 9 * 4 + size * size * (8 + 4), "bytes"
 
 
-def case_topk(rows, v, k):
+def case_topk(rows, v, k, with_lse=True):
     x = torch.randn(rows, v, device="cuda", dtype=torch.bfloat16)
-    return (lambda: ops.topk_logprobs(x, k)), rows * v * 2, "bytes"
+    return (lambda: ops.topk_logprobs(x, k, with_lse=with_lse)), rows * v * 2, "bytes"
 
 
 def case_attention(which, impl, hq=64, hkv=8):
@@ -200,6 +200,8 @@ CASES = {
     # per-rank shapes of tensor parallelism over 8 GPUs (Llama-3-70B, 64 requests x 64-node verify)
     "gemm_fp8_qkv_tp8": lambda: case_gemm_fp8(4096, 1280, 8192),
     "gemm_fp8_o_tp8": lambda: case_gemm_fp8(4096, 8192, 1024),
+    "gemm_fp8_o_tp8_bn128": lambda: case_gemm_fp8(4096, 8192, 1024, bn=128),
+    "gemm_fp8_down_tp8_bn128": lambda: case_gemm_fp8(4096, 8192, 3584, bn=128),
     "gemm_fp8_down_tp8": lambda: case_gemm_fp8(4096, 8192, 3584),
     "gemm_bf16_lm_head_tp8": lambda: case_gemm_bf16(4096, 16032, 8192),
     "attn_prefix_tc_tp8": lambda: case_attention("prefix", "tc", hq=8, hkv=1),
@@ -212,7 +214,7 @@ CASES = {
     "raster_100k_512": lambda: case_raster(100_000, 512),
     "topk8_draft_tp8": lambda: case_topk(512, 16032, 8),
     "topk8_draft": lambda: case_topk(512, 128256, 8),
-    "argmax_verify": lambda: case_topk(4096, 128256, 1),
+    "argmax_verify": lambda: case_topk(4096, 128256, 1, with_lse=False),
     # draft-round shapes (512 = 64 requests x top-8 frontier)
     "gemm_fp8_draft_qkv_tp8": lambda: case_gemm_fp8(512, 1280, 8192),
     "gemm_fp8_draft_gate_up_tp8": lambda: case_gemm_fp8(512, 7168, 8192),

@@ -168,7 +168,7 @@ def pack_work(items: List[List[int]], group_size: int, device, pad_tiles: int = 
 def attention_reference(q, k_cache, v_cache, meta: AttnMeta, scale, items, o_in=None, lse_in=None, o_part=None,
                         lse_part=None, out=None, out_q=None, out_qs=None):
     """Plain-torch definition of one attention pass over a work list (fp32 math)."""
-    from ..weights.quant import FP8_MAX
+    from ..weights.quant import FP8_MAX, pow2_scale
     t_all, hq, d = q.shape
     hkv = k_cache.shape[1]
     ps = k_cache.shape[2]
@@ -221,7 +221,7 @@ def attention_reference(q, k_cache, v_cache, meta: AttnMeta, scale, items, o_in=
             out.view(t_all, hq, d)[q0: q0 + qn] = o.to(out.dtype)
         if out_q is not None:
             amax = o.abs().amax(-1)
-            sc = torch.where(amax > 0, amax / FP8_MAX, torch.ones_like(amax))
+            sc = pow2_scale(amax)
             out_q.view(t_all, hq, d)[q0: q0 + qn] = (o / sc[..., None]).clamp(-FP8_MAX, FP8_MAX).to(out_q.dtype)
             out_qs[:, q0: q0 + qn] = sc.t()
 

@@ -83,7 +83,7 @@ class _VocabOps:
         return self.comm.topk_logprobs_merge(lp + lse[:, None], i, lse[:, None], k)
 
     def argmax(self, logits: torch.Tensor) -> torch.Tensor:
-        lp, i, lse = ops.topk_logprobs(logits, 1, vocab_offset=self.v0)
+        lp, i, lse = ops.topk_logprobs(logits, 1, vocab_offset=self.v0, with_lse=False)
         if self.comm.size == 1:
             return i[:, 0]
         return self.comm.argmax_merge(lp[:, 0] + lse, i[:, 0])

@@ -31,7 +31,7 @@ import torch
 from .. import ops
 from ..utils import nvtx as _nvtx
 from ..config import ModelConfig
-from ..weights.quant import FP8_DTYPE, quant_weight_block
+from ..weights.quant import FP8_DTYPE, ensure_pow2, quant_weight_block
 
 
 @dataclass
@@ -105,8 +105,9 @@ def _pack_linear(parts: List[Tuple[torch.Tensor, Optional[torch.Tensor]]], devic
                 ws_list.append(q)
                 ss_list.append(s)
             else:
-                ws_list.append(w.to(device))
-                ss_list.append(s.to(device).float())
+                q, s = ensure_pow2(w.to(device), s.to(device))
+                ws_list.append(q)
+                ss_list.append(s)
         else:
             if s is not None:
                 from .reference import dequant_block_fp8

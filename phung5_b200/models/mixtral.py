@@ -25,7 +25,7 @@ import torch
 
 from .. import ops
 from ..config import ModelConfig
-from ..weights.quant import quant_weight_block
+from ..weights.quant import ensure_pow2, quant_weight_block
 
 
 @dataclass
@@ -105,7 +105,7 @@ def pack_moe(cfg: ModelConfig, wd: Dict[str, torch.Tensor], prefix: str, device,
         if want_fp8:
             if s is None:
                 return quant_weight_block(w.to(device).float())
-            return w.to(device), s.to(device).float()
+            return ensure_pow2(w.to(device), s.to(device))
         if s is not None:
             from .reference import dequant_block_fp8
             w = dequant_block_fp8(w, s)

@@ -11,6 +11,7 @@ instead of hanging; `check_status()` raises if any kernel reported a timeout.
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional, Tuple
 
 import torch
@@ -27,7 +28,8 @@ except ImportError as e:  # pragma: no cover - depends on the build
 _STATUS = {}
 
 STATUS_CODES = {1: "timeout in TMA producer", 2: "timeout in MMA issuer", 3: "timeout in epilogue",
-                4: "timeout waiting for a peer rank", 5: "bad arguments"}
+                4: "timeout waiting for a peer rank", 5: "bad arguments",
+                6: "fp8 block scale is not a power of two (hardware-scaled GEMM)"}
 
 
 _LAUNCHES = [0]
@@ -76,15 +78,23 @@ def check_status(device=None) -> None:
 # GEMMs
 # ------------------------------------------------------------------------------------------------
 
+# The tensor core applies the block scales itself (tcgen05 kind::mxf8f6f4, UE8M0 scales): every scale the
+# framework produces is a power of two. PHX_FP8_PROMOTE=1 selects the software per-K-block promotion instead
+# (any fp32 scales).
+FP8_HW_SCALE = os.environ.get("PHX_FP8_PROMOTE", "0") != "1"
+
+
 def gemm_fp8_block(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
-                   out: Optional[torch.Tensor] = None, bn: int = 0, max_ctas: int = 0) -> torch.Tensor:
+                   out: Optional[torch.Tensor] = None, bn: int = 0, max_ctas: int = 0,
+                   hw_scale: Optional[bool] = None) -> torch.Tensor:
     """Block-scaled FP8 linear: xq [M,K] e4m3, xs [K/128, M] fp32, wq [N,K] e4m3, ws [N/128, K/128]
-    fp32 -> bf16 [M, N]."""
+    fp32 -> bf16 [M, N]. hw_scale (default FP8_HW_SCALE) needs power-of-two scales."""
     m, n = xq.shape[0], wq.shape[0]
     if out is None:
         out = torch.empty(m, n, dtype=torch.bfloat16, device=xq.device)
     if xq.is_cuda:
-        ext().gemm_fp8_block(xq, xs, wq, ws, out, status_tensor(xq.device), bn, max_ctas)
+        hws = FP8_HW_SCALE if hw_scale is None else hw_scale
+        ext().gemm_fp8_block(xq, xs, wq, ws, out, status_tensor(xq.device), bn, max_ctas, hws)
     else:
         out.copy_(gemm_fp8_block_ref(xq, xs, wq, ws).to(out.dtype))
     return out
@@ -115,7 +125,7 @@ def gemm_grouped(x, w: torch.Tensor, ws: Optional[torch.Tensor], offsets: torch.
                           device=xq.device)
     if xq.is_cuda:
         if ws is not None:
-            ext().gemm_fp8_grouped(x[0], x[1], w, ws, offsets, out, status_tensor(xq.device))
+            ext().gemm_fp8_grouped(x[0], x[1], w, ws, offsets, out, status_tensor(xq.device), FP8_HW_SCALE)
         else:
             ext().gemm_bf16_grouped(x, w, offsets, out, status_tensor(xq.device))
         return out
@@ -136,20 +146,23 @@ def gemm_grouped(x, w: torch.Tensor, ws: Optional[torch.Tensor], offsets: torch.
 # sampling
 # ------------------------------------------------------------------------------------------------
 
-def topk_logprobs(logits: torch.Tensor, k: int, temperature: float = 1.0, vocab_offset: int = 0):
+def topk_logprobs(logits: torch.Tensor, k: int, temperature: float = 1.0, vocab_offset: int = 0,
+                  with_lse: bool = True):
     """Fused top-k of log-softmax(logits / T) per row: returns (logprobs [R, k] fp32, indices [R, k] int64
     (+ vocab_offset), logsumexp [R] fp32). On a vocab shard the results are shard-local (the lse of the
-    shard), which a tensor-parallel merge combines."""
+    shard), which a tensor-parallel merge combines. with_lse=False (argmax use) skips the normalisation:
+    the values are x / T and lse is 0."""
     r = logits.shape[0]
     if logits.is_cuda:
         lp = torch.empty(r, k, dtype=torch.float32, device=logits.device)
         idx = torch.empty(r, k, dtype=torch.int64, device=logits.device)
-        lse = torch.empty(r, dtype=torch.float32, device=logits.device)
-        ext().topk_logprobs(logits.contiguous() if logits.stride(-1) != 1 else logits, k, temperature, lp, idx, lse,
-                            vocab_offset)
-        return lp, idx, lse
+        if with_lse:
+            lse = torch.empty(r, dtype=torch.float32, device=logits.device)
+        ext().topk_logprobs(logits.contiguous() if logits.stride(-1) != 1 else logits, k, temperature, lp, idx,
+                            lse if with_lse else None, vocab_offset)
+        return lp, idx, (lse if with_lse else torch.zeros(r, dtype=torch.float32, device=logits.device))
     x = logits.float() / temperature
-    lse = torch.logsumexp(x, -1)
+    lse = torch.logsumexp(x, -1) if with_lse else torch.zeros(r, dtype=torch.float32)
     v, i = torch.topk(x, k, dim=-1)
     return v - lse[:, None], i + vocab_offset, lse
 

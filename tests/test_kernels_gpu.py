@@ -51,6 +51,42 @@ def test_gemm_fp8_block_persistent_small_grid():
     assert _rel(out, ref) < 5e-3
 
 
+@pytest.mark.parametrize("m,n,k,bn", [(200, 384, 512, 128), (300, 512, 1024, 256), (4096, 1280, 1024, 0),
+                                      (77, 1000, 256, 0), (1000, 2048, 8192, 256)])
+def test_gemm_fp8_hw_scale_matches_promotion(m, n, k, bn):
+    """The tensor core's UE8M0 block scaling (kind::mxf8f6f4) equals the software per-K-block promotion, and
+    both match the fp32 oracle; the quantizers' scales are powers of two."""
+    from phung5_b200.weights.quant import is_pow2
+    g = torch.Generator(device=DEV).manual_seed(3 * m + n + k)
+    x = torch.randn(m, k, device=DEV, generator=g) * torch.rand(m, 1, device=DEV, generator=g) * 4
+    w = torch.randn(n, k, device=DEV, generator=g) * 0.05
+    xq, xs = quant_act_block(x)
+    wq, ws = quant_weight_block(w)
+    assert is_pow2(xs) and is_pow2(ws)
+    hw = ops.gemm_fp8_block(xq, xs, wq, ws, bn=bn, hw_scale=True)
+    sw = ops.gemm_fp8_block(xq, xs, wq, ws, bn=bn, hw_scale=False)
+    ops.check_status()
+    ref = gemm_fp8_block_ref(xq, xs, wq, ws)
+    assert _rel(hw, ref) < 5e-3 and _rel(hw, sw) < 5e-3
+
+
+def test_gemm_fp8_hw_scale_flags_non_pow2_scales():
+    """A weight scale that is not a power of two cannot be a UE8M0 value: the hardware-scaled GEMM records it in
+    the status word; the promotion path takes any fp32 scale."""
+    x = torch.randn(256, 512, device=DEV)
+    w = torch.randn(256, 512, device=DEV) * 0.05
+    xq, xs = quant_act_block(x)
+    wq, ws = quant_weight_block(w)
+    ws = ws * 1.3
+    ops.gemm_fp8_block(xq, xs, wq, ws, hw_scale=True)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="power of two"):
+        ops.check_status()
+    out = ops.gemm_fp8_block(xq, xs, wq, ws, hw_scale=False)
+    ops.check_status()
+    assert _rel(out, gemm_fp8_block_ref(xq, xs, wq, ws)) < 5e-3
+
+
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (300, 640, 1024), (2048, 4096, 4096), (77, 128256, 512),
                                    (50, 4000, 4096), (130, 200, 128)])
 def test_gemm_bf16(m, n, k):
@@ -62,6 +98,8 @@ def test_gemm_bf16(m, n, k):
 
 
 def _deq_close(q, s, ref, tol=1.0 / 15):
+    from phung5_b200.weights.quant import is_pow2
+    assert is_pow2(s)                     # every activation scale is exact in UE8M0
     deq = dequant_act_block(q.float().to(FP8_DTYPE) if q.dtype != FP8_DTYPE else q, s)
     m, k = ref.shape
     blk_amax = ref.abs().view(m, k // 128, 128).amax(-1, keepdim=True).clamp(min=1e-6)
@@ -342,9 +380,10 @@ def test_selftest_cli_passes():
     assert all(v["ok"] for v in res.values()), res
 
 
-@pytest.mark.parametrize("fp8,m,n,k", [(True, 4096, 8192, 1024), (True, 300, 1024, 512), (False, 200, 512, 256),
-                                       (True, 77, 256, 128)])
-def test_gemm_scatter_epilogue(fp8, m, n, k):
+@pytest.mark.parametrize("fp8,m,n,k,hws", [(True, 4096, 8192, 1024, True), (True, 300, 1024, 512, True),
+                                           (False, 200, 512, 256, False), (True, 77, 256, 128, True),
+                                           (True, 300, 1024, 512, False)])
+def test_gemm_scatter_epilogue(fp8, m, n, k, hws):
     """The row-parallel projection's scatter epilogue: row r lands in buffer owner(r) = r // rows_per at slot
     [rank][r - owner * rows_per]. Four local buffers stand in for the peers' receive regions."""
     world, rank = 4, 1
@@ -356,11 +395,11 @@ def test_gemm_scatter_epilogue(fp8, m, n, k):
     if fp8:
         xq, xs = quant_act_block(x)
         wq, ws = quant_weight_block(w)
-        ops.ext().gemm_scatter(xq, xs, wq, ws, base, 0, rows_per, rank, ops.status_tensor(DEV))
-        ref = ops.gemm_fp8_block(xq, xs, wq, ws)
+        ops.ext().gemm_scatter(xq, xs, wq, ws, base, 0, rows_per, rank, ops.status_tensor(DEV), hws)
+        ref = ops.gemm_fp8_block(xq, xs, wq, ws, hw_scale=hws)
     else:
         xb, wb = x.bfloat16(), w.bfloat16()
-        ops.ext().gemm_scatter(xb, None, wb, None, base, 0, rows_per, rank, ops.status_tensor(DEV))
+        ops.ext().gemm_scatter(xb, None, wb, None, base, 0, rows_per, rank, ops.status_tensor(DEV), False)
         ref = ops.gemm_bf16(xb, wb)
     torch.cuda.synchronize()
     for o in range(world):
@@ -400,3 +439,12 @@ def test_kernels_are_deterministic():
         runs.append(out)
     for a, b in zip(*runs):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("r,v", [(4096, 128256), (7, 1000)])
+def test_argmax_without_lse(r, v):
+    x = (torch.randn(r, v, device=DEV) * 2).bfloat16()
+    val, idx, lse = ops.topk_logprobs(x, 1, with_lse=False)
+    rv, ri = torch.topk(x.float(), 1, dim=-1)
+    assert torch.equal(val, rv) and torch.equal(lse, torch.zeros_like(lse))
+    assert torch.equal(x.float().gather(1, idx), rv)

@@ -60,3 +60,25 @@ def test_gemm_fp8_ref_close_to_dense():
     out = ops.gemm_fp8_block(xq, xs, wq, ws)
     dense = x @ w.t()
     assert ((out.float() - dense).norm() / dense.norm()) < 0.08
+
+
+def test_pow2_block_scales_and_checkpoint_requant():
+    """Block scales are the smallest power of two >= amax / 448 (exact UE8M0 values); a checkpoint with arbitrary
+    fp32 scales is requantized once to power-of-two scales, within one e4m3 rounding of the original weight."""
+    from phung5_b200.weights.quant import FP8_MAX, ensure_pow2, is_pow2, pow2_scale
+    amax = torch.tensor([0.0, 448.0, 449.0, 1.0, 3e-30, 224.0 * 2 ** -20])
+    s = pow2_scale(amax)
+    assert is_pow2(s) and s[0] == 1 and s[1] == 1 and s[2] == 2 and s[5] == 2 ** -21
+    assert ((amax / s) <= FP8_MAX).all() and ((amax / s)[1:] > FP8_MAX / 2).all()
+    w = torch.randn(256, 384) * 0.03
+    xq, xs = quant_act_block(torch.randn(8, 384))
+    wq, ws = quant_weight_block(w)
+    assert is_pow2(xs) and is_pow2(ws)
+    assert ensure_pow2(wq, ws)[0] is wq                                     # already powers of two: unchanged
+    ws_odd = ws * 0.77                                                      # a checkpoint's own scales
+    q2, s2 = ensure_pow2(wq, ws_odd)
+    assert is_pow2(s2)
+    deq = lambda q, sc: q.float() * sc.repeat_interleave(128, 0).repeat_interleave(128, 1)
+    orig = deq(wq, ws_odd)
+    blk = orig.abs().view(2, 128, 3, 128).amax((1, 3)).repeat_interleave(128, 0).repeat_interleave(128, 1)
+    assert ((deq(q2, s2) - orig).abs() / blk).max() <= 1 / 16 + 1e-6
