@@ -3,7 +3,7 @@
 
 namespace phx {
 void gemm_fp8_block(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor out,
-                    torch::Tensor status, int64_t bn, int64_t max_ctas, bool hws);
+                    torch::Tensor status, int64_t bn, int64_t max_ctas, bool hws, bool pair);
 void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tensor status, int64_t bn,
                int64_t max_ctas);
 void add_rmsnorm_quant(torch::Tensor h, c10::optional<torch::Tensor> delta, torch::Tensor w, double eps,
@@ -42,7 +42,7 @@ void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M,
                 int64_t s_ld, int64_t off_recv);
 void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tensor w, c10::optional<torch::Tensor> ws,
                   torch::Tensor peer_base, int64_t off_recv, int64_t rows_per, int64_t rank, torch::Tensor status,
-                  bool hws);
+                  bool hws, bool pair);
 void tp_allgather(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t nbytes, torch::Tensor status,
                   std::vector<int64_t> offsets);
 void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,

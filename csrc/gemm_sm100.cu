@@ -27,7 +27,19 @@
 //   right before the stage's four MMAs (cp -> mma from one thread runs in issue order). A scale that is
 //   not a positive power of two sets kErrScaleNotPow2 in the status word.
 //   Tiles are walked M-fastest so CTAs running together share weight (B) columns in L2.
-//   No TMA multicast and no clusters: every CTA loads its own tiles.
+//   PAIR (hardware-scaled fp8, BN = 256): clusters of two CTAs on neighbouring SMs run one 256 x 256 tile with
+//   tcgen05.mma.cta_group::2 (M = 256): each CTA stages its own 128 rows of A and its own 128 rows of B,
+//   and the pair leader's MMA reads both CTAs' halves, so a CTA moves 32 KB per 128-deep K block for a
+//   128 x 256 x 128 product instead of 48 KB: 1.5x the FLOPs per byte of L2 -> shared-memory traffic, the
+//   bound of the single-CTA tile. Each CTA's TMA counts its bytes on the leader's full barrier; the
+//   non-leader also arrives there after staging its scale factors; the leader commits MMA completion to
+//   both CTAs' empty / tfull barriers, and both CTAs' epilogues release the leader's accumulator.
+//   Measured on B200 (Llama-3-70B verify shapes): with the cluster-scope release of the per-stage peer
+//   arrive the pair runs at about half the single-CTA rate (the release waits out the peer's in-flight
+//   copies, so the ring degenerates to one stage); with a relaxed arrive it reaches 0.85-1.0x of it.
+//   Under the 1 kW power cap (about 1.35 GHz sustained) the tensor-pipe clock, not operand traffic, bounds
+//   these GEMMs, so the pair is opt-in (PHX_GEMM_PAIR=1) and the single-CTA tile is the default.
+//   No TMA multicast anywhere: every CTA loads its own tiles.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
@@ -42,10 +54,10 @@ constexpr int kBM = 128;
 constexpr int kEpiWarps = 8;
 constexpr int kGemmThreads = 64 + kEpiWarps * 32;  // producer warp, MMA warp, 8 epilogue warps
 
-template <int BN, int STAGES, bool HWS = false>
+template <int BN, int STAGES, bool HWS = false, int BROWS = BN>
 struct GemmSmem {
   uint8_t a[STAGES][kBM * 128];
-  uint8_t b[STAGES][BN * 128];
+  uint8_t b[STAGES][BROWS * 128];      // BROWS = BN, or BN/2 per CTA of a pair
   // HWS scale-factor staging, per stage: activation scales (32 lanes x 16 B: byte 4c of lane l = row 32c+l),
   // then BN/128 groups of weight scales in the same shape (column 32c+l of the group's 128)
   uint8_t sf[HWS ? STAGES : 1][HWS ? 512 * (1 + BN / 128) : 16];
@@ -60,9 +72,9 @@ struct GemmSmem {
 
 // the scatter epilogue stages each warp's 32 output rows in shared memory (8 warps x 32 rows x (BN/2 + 8)
 // bf16); BN = 256 gives up one operand stage for it
-template <int BN, bool SCATTER = false>
+template <int BN, bool SCATTER = false, bool PAIR = false>
 constexpr int gemm_stages() {
-  return BN == 256 ? (SCATTER ? 3 : 4) : (SCATTER ? 5 : 6);
+  return PAIR ? (SCATTER ? 4 : 6) : BN == 256 ? (SCATTER ? 3 : 4) : (SCATTER ? 5 : 6);
 }
 
 template <int BN>
@@ -80,13 +92,13 @@ struct TileInfo {
   bool valid;
 };
 
-template <int BN>
+template <int BN, int BMT = kBM>
 __device__ __forceinline__ TileInfo tile_info(int t, int M, int N, int m_tiles, int n_tiles, const int* grp_off,
                                               int groups) {
   TileInfo ti;
   if (!grp_off) {
     const int m_blk = t % m_tiles, n_blk = t / m_tiles;
-    ti.m0 = m_blk * kBM;
+    ti.m0 = m_blk * BMT;
     ti.m_end = M;
     ti.n0 = n_blk * BN;
     ti.b0 = ti.n0;
@@ -124,16 +136,19 @@ struct ScatterArgs {
   int rows_per, rank;
 };
 
-template <int BN, bool FP8, bool SCATTER, bool HWS>
+template <int BN, bool FP8, bool SCATTER, bool HWS, bool PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       __nv_bfloat16* __restrict__ out, int M, int N, int K, int ldc, const float* __restrict__ sa,
                       const float* __restrict__ sb, int* status, const int* __restrict__ grp_off, int groups,
                       int max_tiles, const ScatterArgs sc) {
   static_assert(!HWS || FP8, "hardware scaling is an fp8 mode");
-  constexpr int STAGES = gemm_stages<BN, SCATTER>();
+  static_assert(!PAIR || (HWS && BN == 256), "CTA pairs run the hardware-scaled 256-wide tile");
+  constexpr int STAGES = gemm_stages<BN, SCATTER, PAIR>();
   constexpr int BKE = FP8 ? 128 : 64;  // K elements per 128-byte stage row
-  constexpr uint32_t IDESC = HWS ? idesc_make_bs(kBM, BN) : idesc_make(kBM, BN, FP8 ? 0 : 1);
+  constexpr int BMT = PAIR ? 2 * kBM : kBM;   // output rows per tile (both CTAs of a pair)
+  constexpr int BROWS = PAIR ? BN / 2 : BN;   // B rows staged by this CTA
+  constexpr uint32_t IDESC = HWS ? idesc_make_bs(BMT, BN) : idesc_make(kBM, BN, FP8 ? 0 : 1);
   // TMEM accumulators: all 512 columns, except under HWS, where columns [256, 256 + STAGES * SF_COLS) hold
   // the stages' scale factors (BN = 256: one accumulator, freed as soon as the epilogue has drained it)
   constexpr int NBUF = HWS ? 256 / BN : 512 / BN;
@@ -142,14 +157,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr uint32_t TMEM_COLS = 512;
   constexpr int CPT = BN / 2;  // columns per epilogue thread
   constexpr bool PROMOTE = FP8 && !HWS;   // per-K-block software scale promotion
-  using Smem = GemmSmem<BN, STAGES, HWS>;
+  using Smem = GemmSmem<BN, STAGES, HWS, BROWS>;
 
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>(smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023));
 
   const int warp = warp_id();
   const int lane = lane_id();
-  const int m_tiles = (M + kBM - 1) / kBM;
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;   // 0 = pair leader
+  const bool leader = crank == 0;
+  const int unit = PAIR ? blockIdx.x / 2 : blockIdx.x;     // this CTA's pair (or CTA) index, and the count
+  const int units = PAIR ? gridDim.x / 2 : gridDim.x;
+  const int my_row0 = PAIR ? kBM * static_cast<int>(crank) : 0;   // this CTA's rows within a tile
+  const int m_tiles = (M + BMT - 1) / BMT;
   const int n_tiles = (N + BN - 1) / BN;
   const int num_tiles = grp_off ? max_tiles : m_tiles * n_tiles;
   const int ksteps = K / BKE;          // smem stages per tile
@@ -157,12 +177,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
-      mbar_init(&s.full[i], 1);
+      mbar_init(&s.full[i], PAIR ? 2 : 1);         // pair: the leader's expect_tx + the peer's arrive
       mbar_init(&s.empty[i], 1);
     }
     for (int i = 0; i < NBUF; ++i) {
       mbar_init(&s.tfull[i], 1);
-      mbar_init(&s.tempty[i], kEpiWarps);
+      mbar_init(&s.tempty[i], PAIR ? 2 * kEpiWarps : kEpiWarps);   // pair: both CTAs' epilogue warps
     }
     mbar_init(&s.done, 1);
     s.abort = 0;
@@ -171,11 +191,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tmap(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(&s.tmem_base, TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(&s.tmem_base, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&s.tmem_base, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();   // both CTAs' barriers and TMEM exist before either CTA uses them
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = s.tmem_base;
   volatile int* abort = &s.abort;
@@ -192,11 +218,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // the scales of the next (tile, k block) are loaded one step ahead of their stage
     auto load_sf = [&](int tt, int kb) {
       if (tt >= num_tiles) return;
-      const TileInfo ti = tile_info<BN>(tt, M, N, m_tiles, n_tiles, grp_off, groups);
+      const TileInfo ti = tile_info<BN, BMT>(tt, M, N, m_tiles, n_tiles, grp_off, groups);
       if (!ti.valid) return;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const int r = ti.m0 + 32 * c + lane;
+        const int r = ti.m0 + my_row0 + 32 * c + lane;
         fa[c] = sa[(size_t)kb * M + (r < M ? r : M - 1)];
       }
       const int nb_last = ti.sb_base + (N + 127) / 128 - 1;
@@ -211,9 +237,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bad |= (u & 0x807FFFFFu) != 0u || (u >> 23) == 0u;
       return (u >> 23) & 0xFFu;
     };
-    load_sf(blockIdx.x, 0);
-    for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x) {
-      const TileInfo ti = tile_info<BN>(t, M, N, m_tiles, n_tiles, grp_off, groups);
+    load_sf(unit, 0);
+    for (int t = unit; t < num_tiles && !*abort; t += units) {
+      const TileInfo ti = tile_info<BN, BMT>(t, M, N, m_tiles, n_tiles, grp_off, groups);
       if (!ti.valid) break;
       bool ok = true;
       for (int ks = 0; ks < ksteps; ++ks) {
@@ -222,7 +248,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
         for (int g = 0; g < BN / 128; ++g) wb[g] = ue8m0(fb[g]);
         if (ks + 1 < ksteps) load_sf(t, ks + 1);
-        else load_sf(t + gridDim.x, 0);
+        else load_sf(t + units, 0);
         int got = 1;
         if (lane == 0) got = mbar_wait(&s.empty[stage], phase ^ 1, status, kErrTimeoutProducer, abort);
         if (!__shfl_sync(0xffffffffu, got, 0)) {
@@ -237,9 +263,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive_expect_tx(&s.full[stage], (kBM + BN) * 128);
-          tma_load_2d(&tmA, &s.full[stage], s.a[stage], ks * BKE, ti.m0);
-          tma_load_2d(&tmB, &s.full[stage], s.b[stage], ks * BKE, ti.b0);
+          if constexpr (PAIR) {
+            // both halves count on the leader's barrier; the peer's arrive also publishes its scale factors
+            const uint32_t fbar = mapa_shared(smem_u32(&s.full[stage]), 0);
+            if (leader) mbar_arrive_expect_tx(&s.full[stage], 2 * (kBM + BROWS) * 128);
+            tma_load_2d_pair(&tmA, fbar, s.a[stage], ks * BKE, ti.m0 + my_row0);
+            tma_load_2d_pair(&tmB, fbar, s.b[stage], ks * BKE, ti.b0 + BROWS * static_cast<int>(crank));
+            if (!leader) mbar_arrive_cluster(fbar);
+          } else {
+            mbar_arrive_expect_tx(&s.full[stage], (kBM + BN) * 128);
+            tma_load_2d(&tmA, &s.full[stage], s.a[stage], ks * BKE, ti.m0);
+            tma_load_2d(&tmB, &s.full[stage], s.b[stage], ks * BKE, ti.b0);
+          }
         }
         ++issued;
         if (++stage == STAGES) stage = 0, phase ^= 1;
@@ -247,7 +282,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!ok) break;
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicCAS(status, 0, kErrScaleNotPow2);
-    if (lane == 0) {
+    if (lane == 0 && leader) {   // a pair's copies all count on the leader's barriers
       volatile int never = 0;
       for (int i = 0; i < STAGES && i < issued; ++i) {
         if (--stage < 0) stage = STAGES - 1, phase ^= 1;
@@ -260,8 +295,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x) {
-        const TileInfo ti = tile_info<BN>(t, M, N, m_tiles, n_tiles, grp_off, groups);
+      for (int t = unit; t < num_tiles && !*abort; t += units) {
+        const TileInfo ti = tile_info<BN, BMT>(t, M, N, m_tiles, n_tiles, grp_off, groups);
         if (!ti.valid) break;
         for (int ks = 0; ks < ksteps; ++ks) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1, status, kErrTimeoutProducer, abort)) break;
@@ -280,29 +315,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (a pair's leader issues for both CTAs) ----------------
       int stage = 0;
       uint32_t phase = 0;
       int tb = 0;
       uint32_t tphase = 0;
-      for (int t = blockIdx.x; t < num_tiles && !*abort; t += gridDim.x) {
-        if (grp_off && !tile_info<BN>(t, M, N, m_tiles, n_tiles, grp_off, groups).valid) break;
+      for (int t = unit; t < num_tiles && !*abort; t += units) {
+        if (grp_off && !tile_info<BN, BMT>(t, M, N, m_tiles, n_tiles, grp_off, groups).valid) break;
         for (int ks = 0; ks < ksteps; ++ks) {
           const bool new_acc = PROMOTE || ks == 0;
           const bool end_acc = PROMOTE || ks == ksteps - 1;
           if (new_acc) {
-            if (!mbar_wait(&s.tempty[tb], tphase ^ 1, status, kErrTimeoutMma, abort)) goto mma_done;
+            if (!mbar_wait<PAIR>(&s.tempty[tb], tphase ^ 1, status, kErrTimeoutMma, abort)) goto mma_done;
             tc_fence_after();
           }
-          if (!mbar_wait(&s.full[stage], phase, status, kErrTimeoutMma, abort)) goto mma_done;
+          if (!mbar_wait<PAIR>(&s.full[stage], phase, status, kErrTimeoutMma, abort)) goto mma_done;
           tc_fence_after();
           {
             const uint64_t da = sdesc_sw128(smem_u32(s.a[stage]));
             const uint64_t db = sdesc_sw128(smem_u32(s.b[stage]));
             const uint32_t dtm = tmem_base + tb * BN;
             const uint32_t tsf = tmem_base + 256 + stage * SF_COLS;   // HWS: this stage's scale columns
-            if constexpr (HWS) {
+            if constexpr (PAIR) {
+              const uint32_t sfs = smem_u32(s.sf[stage]);
+              tmem_cp_32x128b_x4_pair(tsf, sdesc_plain(sfs));
+#pragma unroll
+              for (int g = 0; g < BN / 128; ++g)
+                tmem_cp_32x128b_x4_pair(tsf + 4 + 4 * g, sdesc_plain(sfs + 512 * (1 + g)));
+            } else if constexpr (HWS) {
               const uint32_t sfs = smem_u32(s.sf[stage]);
               tmem_cp_32x128b_x4(tsf, sdesc_plain(sfs));
 #pragma unroll
@@ -311,15 +352,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const uint32_t acc = new_acc ? (k > 0) : 1u;
-              if constexpr (HWS)
+              if constexpr (PAIR)
+                umma_f8_bs_pair(dtm, da + 2 * k, db + 2 * k, IDESC, acc, tsf, tsf + 4);
+              else if constexpr (HWS)
                 umma_f8_bs(dtm, da + 2 * k, db + 2 * k, IDESC, acc, tsf, tsf + 4);
               else if constexpr (FP8)
                 umma_f8(dtm, da + 2 * k, db + 2 * k, IDESC, acc);
               else
                 umma_f16(dtm, da + 2 * k, db + 2 * k, IDESC, acc);
             }
-            umma_commit(&s.empty[stage]);
-            if (end_acc) umma_commit(&s.tfull[tb]);
+            if constexpr (PAIR) {
+              // release the stage in both CTAs (each producer waits on its own empty barrier), and hand a
+              // finished accumulator to both CTAs' epilogues
+              const uint32_t eb = smem_u32(&s.empty[stage]);
+              umma_commit_pair(mapa_shared(eb, 0));
+              umma_commit_pair(mapa_shared(eb, 1));
+              if (end_acc) {
+                const uint32_t fb = smem_u32(&s.tfull[tb]);
+                umma_commit_pair(mapa_shared(fb, 0));
+                umma_commit_pair(mapa_shared(fb, 1));
+              }
+            } else {
+              umma_commit(&s.empty[stage]);
+              if (end_acc) umma_commit(&s.tfull[tb]);
+            }
           }
           if (++stage == STAGES) stage = 0, phase ^= 1;
           if (end_acc)
@@ -328,7 +384,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     mma_done:
       // all issued MMAs complete before teardown
-      umma_commit(&s.done);
+      if constexpr (PAIR) umma_commit_pair(smem_u32(&s.done));
+      else umma_commit(&s.done);
       volatile int never = 0;
       mbar_wait(&s.done, 0, nullptr, 0, &never);
     }
@@ -343,29 +400,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int epi_blocks = PROMOTE ? kblocks : 1;
     // the scales of the next (tile, k block) are loaded one step ahead, so their latency overlaps the
     // current block's TMEM drain
-    int t = blockIdx.x;
+    int t = unit;
     float sa_next = 0.f, sb_next = 0.f;
     auto load_scales = [&](int tt, int kb) {
       if (!PROMOTE || tt >= num_tiles) return;
-      const TileInfo ti = tile_info<BN>(tt, M, N, m_tiles, n_tiles, grp_off, groups);
+      const TileInfo ti = tile_info<BN, BMT>(tt, M, N, m_tiles, n_tiles, grp_off, groups);
       if (!ti.valid) return;
-      const int rr = ti.m0 + sub * 32 + lane;
+      const int rr = ti.m0 + my_row0 + sub * 32 + lane;
       const int c0 = ti.n0 + half * CPT;
       sa_next = sa[(size_t)kb * M + (rr < M ? rr : M - 1)];
       sb_next = c0 < N ? sb[(size_t)(ti.sb_base + (c0 >> 7)) * kblocks + kb] : 0.f;
     };
     load_scales(t, 0);
-    for (; t < num_tiles && !*abort; t += gridDim.x) {
-      const TileInfo ti = tile_info<BN>(t, M, N, m_tiles, n_tiles, grp_off, groups);
+    for (; t < num_tiles && !*abort; t += units) {
+      const TileInfo ti = tile_info<BN, BMT>(t, M, N, m_tiles, n_tiles, grp_off, groups);
       if (!ti.valid) break;
-      const int row = ti.m0 + sub * 32 + lane;
+      const int row = ti.m0 + my_row0 + sub * 32 + lane;
       const int col0 = ti.n0 + half * CPT;
       const bool col_ok = col0 < N;
       for (int kb = 0; kb < epi_blocks; ++kb) {
         const float scale = PROMOTE ? sa_next * sb_next : 1.f;
         if (kb + 1 < epi_blocks) load_scales(t, kb + 1);
-        else load_scales(t + gridDim.x, 0);
-        const bool ok = mbar_wait(&s.tfull[tb], tphase, status, kErrTimeoutEpilogue, abort);
+        else load_scales(t + units, 0);
+        const bool ok = mbar_wait<PAIR>(&s.tfull[tb], tphase, status, kErrTimeoutEpilogue, abort);
         if (!__all_sync(0xffffffffu, ok)) goto epi_done;
         tc_fence_after();
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + tb * BN + half * CPT;
@@ -390,7 +447,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&s.tempty[tb]);
+        if (lane == 0) {
+          if constexpr (PAIR) mbar_arrive_cluster(mapa_shared(smem_u32(&s.tempty[tb]), 0));   // the leader's
+          else mbar_arrive(&s.tempty[tb]);
+        }
         if (++tb == NBUF) tb = 0, tphase ^= 1;
       }
       if constexpr (SCATTER) {
@@ -413,7 +473,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 4
         for (int it = 0; it < 32 / RPI; ++it) {
           const int rl = it * RPI + lane / CH, ch = lane % CH;
-          const int grow = ti.m0 + sub * 32 + rl, gcol = col0 + ch * 8;
+          const int grow = ti.m0 + my_row0 + sub * 32 + rl, gcol = col0 + ch * 8;
           if (grow < ti.m_end && grow < M && gcol < N) {
             const int owner = grow / sc.rows_per;
             __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(sc.peer_base[owner] + sc.off_recv) +
@@ -442,9 +502,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();   // the leader's MMAs into the peer's TMEM and reads of its smem are done
+  else __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+  if (warp == 1) {
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tmem_dealloc(tmem_base, TMEM_COLS);
+  }
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -460,10 +524,11 @@ int num_sms() {
   return n;
 }
 
-template <int BN, bool FP8, bool SCATTER = false, bool HWS = false>
+template <int BN, bool FP8, bool SCATTER = false, bool HWS = false, bool PAIR = false>
 void launch_gemm_ptr(const torch::Tensor& a, const torch::Tensor& b, __nv_bfloat16* out_ptr, int ldc, int n_out,
                      const float* sa, const float* sb, int* status, cudaStream_t stream, int max_ctas,
                      const int* grp_off, int groups, ScatterArgs sc) {
+  static_assert(!PAIR || HWS, "CTA pairs run the hardware-scaled kernel");
   const int M = a.size(0), K = a.size(1);
   const int N = grp_off ? n_out : (int)b.size(0);   // grouped: b holds groups * N rows
   const CUtensorMapDataType dt = FP8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -471,31 +536,63 @@ void launch_gemm_ptr(const torch::Tensor& a, const torch::Tensor& b, __nv_bfloat
   const uint32_t box_inner = 128 / esz;
   CUtensorMap ta = make_tmap_2d(a.data_ptr(), dt, K, M, (uint64_t)a.stride(0) * esz, box_inner, kBM,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tb = make_tmap_2d(b.data_ptr(), dt, K, b.size(0), (uint64_t)b.stride(0) * esz, box_inner, BN,
+  constexpr int BROWS = PAIR ? BN / 2 : BN;
+  CUtensorMap tb = make_tmap_2d(b.data_ptr(), dt, K, b.size(0), (uint64_t)b.stride(0) * esz, box_inner, BROWS,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
-  constexpr int STAGES = gemm_stages<BN, SCATTER>();
-  const size_t smem = ((sizeof(GemmSmem<BN, STAGES, HWS>) + 127) & ~size_t(127)) + 1024 +
+  constexpr int STAGES = gemm_stages<BN, SCATTER, PAIR>();
+  const size_t smem = ((sizeof(GemmSmem<BN, STAGES, HWS, BROWS>) + 127) & ~size_t(127)) + 1024 +
                       (SCATTER ? (size_t)kEpiWarps * 32 * scatter_row_bytes<BN>() : 0);
+  auto kern = gemm_sm100_kernel<BN, FP8, SCATTER, HWS, PAIR>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8, SCATTER, HWS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     attr_set = true;
   }
+  constexpr int BMT = PAIR ? 2 * kBM : kBM;
   // grouped: at most M/128 + groups row tiles in total (one partial tile per group)
-  const int m_tiles_bound = grp_off ? (M + kBM - 1) / kBM + groups : (M + kBM - 1) / kBM;
+  const int m_tiles_bound = grp_off ? (M + BMT - 1) / BMT + groups : (M + BMT - 1) / BMT;
   const int tiles = m_tiles_bound * ((N + BN - 1) / BN);
-  int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
-  gemm_sm100_kernel<BN, FP8, SCATTER, HWS><<<grid, kGemmThreads, smem, stream>>>(
-      ta, tb, out_ptr, M, N, K, ldc, sa, sb, status, grp_off, groups, tiles, sc);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if constexpr (PAIR) {
+    // clusters of two CTAs; as many pairs as can be resident at once (a GPC with an odd SM count leaves one
+    // SM out), each walking tiles persistently
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    static int max_pairs = 0;
+    if (!max_pairs) {
+      cfg.gridDim = dim3(2 * (num_sms() / 2));
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        (void)cudaGetLastError();
+        n = num_sms() / 2 - 4;
+      }
+      max_pairs = n;
+    }
+    int pairs = std::min(tiles, max_ctas > 0 ? std::max(1, max_ctas / 2) : max_pairs);
+    cfg.gridDim = dim3(2 * pairs);
+    C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, out_ptr, M, N, K, ldc, sa, sb, status, grp_off, groups,
+                                      tiles, sc));
+  } else {
+    int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
+    kern<<<grid, kGemmThreads, smem, stream>>>(ta, tb, out_ptr, M, N, K, ldc, sa, sb, status, grp_off, groups, tiles,
+                                               sc);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
 }
 
-template <int BN, bool FP8, bool HWS = false>
+template <int BN, bool FP8, bool HWS = false, bool PAIR = false>
 void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, const float* sa,
                  const float* sb, int* status, cudaStream_t stream, int max_ctas, const int* grp_off = nullptr,
                  int groups = 0) {
-  launch_gemm_ptr<BN, FP8, false, HWS>(a, b, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (int)out.stride(0),
+  launch_gemm_ptr<BN, FP8, false, HWS, PAIR>(a, b, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (int)out.stride(0),
                            (int)out.size(1), sa, sb, status, stream, max_ctas, grp_off, groups,
                            ScatterArgs{nullptr, 0, 1, 0});
 }
@@ -510,8 +607,9 @@ static int pick_bn(int M, int N) {
 }
 
 // hws: the tensor core applies the (power-of-two) block scales; otherwise the epilogue promotes per K block.
+// pair: run 256 x 256 tiles on CTA pairs (hardware scaling, BN = 256, more than one 128-row block)
 void gemm_fp8_block(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor out,
-                    torch::Tensor status, int64_t bn, int64_t max_ctas, bool hws) {
+                    torch::Tensor status, int64_t bn, int64_t max_ctas, bool hws, bool pair) {
   TORCH_CHECK(xq.is_cuda() && wq.is_cuda() && out.is_cuda());
   TORCH_CHECK(xq.scalar_type() == at::kFloat8_e4m3fn && wq.scalar_type() == at::kFloat8_e4m3fn);
   TORCH_CHECK(out.scalar_type() == at::kBFloat16);
@@ -531,7 +629,8 @@ void gemm_fp8_block(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch:
   const float* sb = ws.data_ptr<float>();
   int* st = status.data_ptr<int>();
   if (hws) {
-    if (b == 256) launch_gemm<256, true, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
+    if (b == 256 && pair && M > kBM) launch_gemm<256, true, true, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
+    else if (b == 256) launch_gemm<256, true, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
     else launch_gemm<128, true, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
   } else {
     if (b == 256) launch_gemm<256, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
@@ -594,7 +693,7 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tenso
 // Row-parallel projection with the scatter epilogue (see ScatterArgs): fp8 (ws defined) or bf16 operands.
 void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tensor w, c10::optional<torch::Tensor> ws,
                   torch::Tensor peer_base, int64_t off_recv, int64_t rows_per, int64_t rank, torch::Tensor status,
-                  bool hws) {
+                  bool hws, bool pair) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && peer_base.is_cuda() && peer_base.scalar_type() == at::kLong);
   const int M = x.size(0), K = x.size(1), N = w.size(0);
   TORCH_CHECK(w.size(1) == K && N % 8 == 0 && x.stride(1) == 1 && w.stride(1) == 1);
@@ -613,7 +712,9 @@ void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tenso
     const float* sb = ws->data_ptr<float>();
     int* st = status.data_ptr<int>();
     if (hws) {
-      if (b == 256) launch_gemm_ptr<256, true, true, true>(x, w, nullptr, N, N, sa, sb, st, stream, 0, nullptr, 0, sc);
+      if (b == 256 && pair && M > kBM)
+        launch_gemm_ptr<256, true, true, true, true>(x, w, nullptr, N, N, sa, sb, st, stream, 0, nullptr, 0, sc);
+      else if (b == 256) launch_gemm_ptr<256, true, true, true>(x, w, nullptr, N, N, sa, sb, st, stream, 0, nullptr, 0, sc);
       else launch_gemm_ptr<128, true, true, true>(x, w, nullptr, N, N, sa, sb, st, stream, 0, nullptr, 0, sc);
     } else {
       if (b == 256) launch_gemm_ptr<256, true, true>(x, w, nullptr, N, N, sa, sb, st, stream, 0, nullptr, 0, sc);

@@ -82,11 +82,14 @@ def check_status(device=None) -> None:
 # framework produces is a power of two. PHX_FP8_PROMOTE=1 selects the software per-K-block promotion instead
 # (any fp32 scales).
 FP8_HW_SCALE = os.environ.get("PHX_FP8_PROMOTE", "0") != "1"
+# PHX_GEMM_PAIR=1: hardware-scaled 256-wide tiles run as 256 x 256 tiles on CTA pairs (tcgen05 cta_group::2,
+# clusters of two). Off by default: measured no faster than the single-CTA tile under the power cap.
+GEMM_PAIR = os.environ.get("PHX_GEMM_PAIR", "0") == "1"
 
 
 def gemm_fp8_block(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
                    out: Optional[torch.Tensor] = None, bn: int = 0, max_ctas: int = 0,
-                   hw_scale: Optional[bool] = None) -> torch.Tensor:
+                   hw_scale: Optional[bool] = None, pair: Optional[bool] = None) -> torch.Tensor:
     """Block-scaled FP8 linear: xq [M,K] e4m3, xs [K/128, M] fp32, wq [N,K] e4m3, ws [N/128, K/128]
     fp32 -> bf16 [M, N]. hw_scale (default FP8_HW_SCALE) needs power-of-two scales."""
     m, n = xq.shape[0], wq.shape[0]
@@ -94,7 +97,8 @@ def gemm_fp8_block(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: tor
         out = torch.empty(m, n, dtype=torch.bfloat16, device=xq.device)
     if xq.is_cuda:
         hws = FP8_HW_SCALE if hw_scale is None else hw_scale
-        ext().gemm_fp8_block(xq, xs, wq, ws, out, status_tensor(xq.device), bn, max_ctas, hws)
+        ext().gemm_fp8_block(xq, xs, wq, ws, out, status_tensor(xq.device), bn, max_ctas, hws,
+                             GEMM_PAIR if pair is None else pair)
     else:
         out.copy_(gemm_fp8_block_ref(xq, xs, wq, ws).to(out.dtype))
     return out

@@ -101,7 +101,7 @@ class FusedCommunicator(NcclCommunicator):
         rows_per = (m + self.size - 1) // self.size
         xq, xs = x if lin.fp8 else (x, None)
         ops.ext().gemm_scatter(xq, xs, lin.w, lin.ws, self.peer_base, self.ws.off["recv"], rows_per, self.rank,
-                               ops.status_tensor(self.device), ops.FP8_HW_SCALE)
+                               ops.status_tensor(self.device), ops.FP8_HW_SCALE, ops.GEMM_PAIR)
 
     def ar_norm(self, m: int, w: torch.Tensor, eps: float, out_bf16: bool = False, push_h: bool = False,
                 recv: bool = False):

@@ -70,6 +70,23 @@ def test_gemm_fp8_hw_scale_matches_promotion(m, n, k, bn):
     assert _rel(hw, ref) < 5e-3 and _rel(hw, sw) < 5e-3
 
 
+@pytest.mark.parametrize("m,n,k,max_ctas", [(300, 512, 1024, 0), (129, 768, 512, 0), (4096, 1280, 1024, 0),
+                                            (1024, 2048, 2048, 4), (4096, 8192, 1024, 0)])
+def test_gemm_fp8_cta_pair_matches_single_cta(m, n, k, max_ctas):
+    """256 x 256 tiles on CTA pairs (tcgen05 cta_group::2, each CTA staging half of A and half of B) give the
+    single-CTA result: rows past M in the second CTA, a 2-pair persistent grid walking many tiles."""
+    g = torch.Generator(device=DEV).manual_seed(m * 7 + n + k)
+    x = torch.randn(m, k, device=DEV, generator=g)
+    w = torch.randn(n, k, device=DEV, generator=g) * 0.05
+    xq, xs = quant_act_block(x)
+    wq, ws = quant_weight_block(w)
+    one = ops.gemm_fp8_block(xq, xs, wq, ws, bn=256, max_ctas=max_ctas, hw_scale=True, pair=False)
+    two = ops.gemm_fp8_block(xq, xs, wq, ws, bn=256, max_ctas=max_ctas, hw_scale=True, pair=True)
+    ops.check_status()
+    ref = gemm_fp8_block_ref(xq, xs, wq, ws)
+    assert _rel(two, ref) < 5e-3 and _rel(two, one) < 1e-3
+
+
 def test_gemm_fp8_hw_scale_flags_non_pow2_scales():
     """A weight scale that is not a power of two cannot be a UE8M0 value: the hardware-scaled GEMM records it in
     the status word; the promotion path takes any fp32 scale."""
@@ -395,11 +412,11 @@ def test_gemm_scatter_epilogue(fp8, m, n, k, hws):
     if fp8:
         xq, xs = quant_act_block(x)
         wq, ws = quant_weight_block(w)
-        ops.ext().gemm_scatter(xq, xs, wq, ws, base, 0, rows_per, rank, ops.status_tensor(DEV), hws)
+        ops.ext().gemm_scatter(xq, xs, wq, ws, base, 0, rows_per, rank, ops.status_tensor(DEV), hws, hws)
         ref = ops.gemm_fp8_block(xq, xs, wq, ws, hw_scale=hws)
     else:
         xb, wb = x.bfloat16(), w.bfloat16()
-        ops.ext().gemm_scatter(xb, None, wb, None, base, 0, rows_per, rank, ops.status_tensor(DEV), False)
+        ops.ext().gemm_scatter(xb, None, wb, None, base, 0, rows_per, rank, ops.status_tensor(DEV), False, False)
         ref = ops.gemm_bf16(xb, wb)
     torch.cuda.synchronize()
     for o in range(world):
