@@ -34,7 +34,7 @@ void paged_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_
 void topk_logprobs(torch::Tensor logits, int64_t k, double temperature, torch::Tensor lp, torch::Tensor idx,
                    c10::optional<torch::Tensor> lse, int64_t vocab_offset);
 void gemm_fp8_grouped(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor offsets,
-                      torch::Tensor out, torch::Tensor status, bool hws);
+                      torch::Tensor out, torch::Tensor status, bool hws, c10::optional<torch::Tensor> rows);
 void gemm_bf16_grouped(torch::Tensor x, torch::Tensor w, torch::Tensor offsets, torch::Tensor out,
                        torch::Tensor status);
 void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M, int64_t H, double eps,
@@ -43,6 +43,7 @@ void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M,
 void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tensor w, c10::optional<torch::Tensor> ws,
                   torch::Tensor peer_base, int64_t off_recv, int64_t rows_per, int64_t rank, torch::Tensor status,
                   bool hws, bool pair);
+void moe_combine(torch::Tensor y, torch::Tensor pos, torch::Tensor w, torch::Tensor local, torch::Tensor out);
 void tp_allgather(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t nbytes, torch::Tensor status,
                   std::vector<int64_t> offsets);
 void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
@@ -76,6 +77,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_ar_norm", &phx::tp_ar_norm);
   m.def("tp_allgather", &phx::tp_allgather);
   m.def("gemm_scatter", &phx::gemm_scatter);
+  m.def("moe_combine", &phx::moe_combine);
   m.def("gdn_recurrent", &phx::gdn_recurrent);
   m.def("gdn_fold", &phx::gdn_fold);
   m.def("gdn_gates", &phx::gdn_gates);

@@ -127,6 +127,16 @@ __device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* ba
       "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+// TMA gather4: rows y0..y3 of a 2-D map whose box is one row high (`box_inner` columns from x) land in four
+// consecutive shared-memory rows at dst, swizzled by the map's mode exactly as a four-row box would be.
+__device__ __forceinline__ void tma_gather4(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y0, int y1,
+                                            int y2, int y3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3)
+      : "memory");
+}
 // CTA pair (cluster of 2, cta_group::2): this CTA's tile lands in its own shared memory; the transaction
 // bytes are counted on the mbarrier at `bar_cl`, a shared::cluster address (the pair leader's barrier).
 // No multicast: each CTA loads only its own half.

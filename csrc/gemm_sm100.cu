@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       __nv_bfloat16* __restrict__ out, int M, int N, int K, int ldc, const float* __restrict__ sa,
                       const float* __restrict__ sb, int* status, const int* __restrict__ grp_off, int groups,
-                      int max_tiles, const ScatterArgs sc) {
+                      int max_tiles, const ScatterArgs sc, const int* __restrict__ a_rows, int sa_ld) {
   static_assert(!HWS || FP8, "hardware scaling is an fp8 mode");
   static_assert(!PAIR || (HWS && BN == 256), "CTA pairs run the hardware-scaled 256-wide tile");
   constexpr int STAGES = gemm_stages<BN, SCATTER, PAIR>();
@@ -212,43 +212,74 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t phase = 0;
     int issued = 0;
     bool bad = false;
-    float fa[4] = {1.f, 1.f, 1.f, 1.f}, fb[BN / 128];
+    // a_rows (dispatch fused into the A loads): A row r of the GEMM is row a_rows[r] of the activation
+    // matrix, fetched with TMA gather4 (lane l: rows 4l..4l+3 of the tile) and scaled by that row's scales.
+    auto src_row = [&](int r) { r = r < M ? r : M - 1; return a_rows ? a_rows[r] : r; };
+    // Scale prefetch, LA stages ahead: an L2 round trip (~0.45 us) is longer than one stage's MMAs
+    // (~0.3 us), so loading a stage's scales only one stage ahead left the producer waiting on them and
+    // the ring under-filled (ncu: tensor pipe 41 % active, long-scoreboard stalls dominant). Slot 0 of the
+    // ring is the current stage; a cursor (la_t, la_ks) walks the (tile, k block) sequence LA stages
+    // ahead; srow are the cursor tile's scale rows for this lane.
+    constexpr int LA = 4;
+    float fa_r[LA][4], fb_r[LA][BN / 128];
+    int la_t = unit, la_ks = 0;
+    int srow[4] = {0, 0, 0, 0};
+    TileInfo la_ti;
+    la_ti.valid = false;
+    auto la_load = [&](float (&fa)[4], float (&fb)[BN / 128]) {
 #pragma unroll
-    for (int g = 0; g < BN / 128; ++g) fb[g] = 1.f;
-    // the scales of the next (tile, k block) are loaded one step ahead of their stage
-    auto load_sf = [&](int tt, int kb) {
-      if (tt >= num_tiles) return;
-      const TileInfo ti = tile_info<BN, BMT>(tt, M, N, m_tiles, n_tiles, grp_off, groups);
-      if (!ti.valid) return;
+      for (int c = 0; c < 4; ++c) fa[c] = 1.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int r = ti.m0 + my_row0 + 32 * c + lane;
-        fa[c] = sa[(size_t)kb * M + (r < M ? r : M - 1)];
+      for (int g = 0; g < BN / 128; ++g) fb[g] = 1.f;
+      if (la_t >= num_tiles) return;
+      if (la_ks == 0) {
+        la_ti = tile_info<BN, BMT>(la_t, M, N, m_tiles, n_tiles, grp_off, groups);
+        if (la_ti.valid) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) srow[c] = src_row(la_ti.m0 + my_row0 + 32 * c + lane);
+        }
       }
-      const int nb_last = ti.sb_base + (N + 127) / 128 - 1;
+      if (la_ti.valid) {
 #pragma unroll
-      for (int g = 0; g < BN / 128; ++g) {
-        const int nb = ti.sb_base + (ti.n0 >> 7) + g;
-        fb[g] = sb[(size_t)(nb < nb_last ? nb : nb_last) * kblocks + kb];
+        for (int c = 0; c < 4; ++c) fa[c] = sa[(size_t)la_ks * sa_ld + srow[c]];
+        const int nb_last = la_ti.sb_base + (N + 127) / 128 - 1;
+#pragma unroll
+        for (int g = 0; g < BN / 128; ++g) {
+          const int nb = la_ti.sb_base + (la_ti.n0 >> 7) + g;
+          fb[g] = sb[(size_t)(nb < nb_last ? nb : nb_last) * kblocks + la_ks];
+        }
       }
+      if (++la_ks == ksteps) la_ks = 0, la_t += units;
     };
+    int g4[4] = {0, 0, 0, 0};
     auto ue8m0 = [&](float v) -> uint32_t {
       const uint32_t u = __float_as_uint(v);
       bad |= (u & 0x807FFFFFu) != 0u || (u >> 23) == 0u;
       return (u >> 23) & 0xFFu;
     };
-    load_sf(unit, 0);
+#pragma unroll
+    for (int j = 0; j < LA; ++j) la_load(fa_r[j], fb_r[j]);
     for (int t = unit; t < num_tiles && !*abort; t += units) {
       const TileInfo ti = tile_info<BN, BMT>(t, M, N, m_tiles, n_tiles, grp_off, groups);
       if (!ti.valid) break;
+      if (a_rows) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) g4[i] = src_row(ti.m0 + 4 * lane + i);
+      }
       bool ok = true;
       for (int ks = 0; ks < ksteps; ++ks) {
-        const uint4 wa = make_uint4(ue8m0(fa[0]), ue8m0(fa[1]), ue8m0(fa[2]), ue8m0(fa[3]));
+        const uint4 wa = make_uint4(ue8m0(fa_r[0][0]), ue8m0(fa_r[0][1]), ue8m0(fa_r[0][2]), ue8m0(fa_r[0][3]));
         uint32_t wb[BN / 128];
 #pragma unroll
-        for (int g = 0; g < BN / 128; ++g) wb[g] = ue8m0(fb[g]);
-        if (ks + 1 < ksteps) load_sf(t, ks + 1);
-        else load_sf(t + units, 0);
+        for (int g = 0; g < BN / 128; ++g) wb[g] = ue8m0(fb_r[0][g]);
+#pragma unroll
+        for (int j = 0; j + 1 < LA; ++j) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) fa_r[j][c] = fa_r[j + 1][c];
+#pragma unroll
+          for (int g = 0; g < BN / 128; ++g) fb_r[j][g] = fb_r[j + 1][g];
+        }
+        la_load(fa_r[LA - 1], fb_r[LA - 1]);
         int got = 1;
         if (lane == 0) got = mbar_wait(&s.empty[stage], phase ^ 1, status, kErrTimeoutProducer, abort);
         if (!__shfl_sync(0xffffffffu, got, 0)) {
@@ -272,9 +303,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (!leader) mbar_arrive_cluster(fbar);
           } else {
             mbar_arrive_expect_tx(&s.full[stage], (kBM + BN) * 128);
-            tma_load_2d(&tmA, &s.full[stage], s.a[stage], ks * BKE, ti.m0);
+            if (!a_rows) tma_load_2d(&tmA, &s.full[stage], s.a[stage], ks * BKE, ti.m0);
             tma_load_2d(&tmB, &s.full[stage], s.b[stage], ks * BKE, ti.b0);
           }
+        }
+        if (!PAIR && a_rows) {
+          __syncwarp();   // the stage's transaction count is armed before any gather lands
+          tma_gather4(&tmA, &s.full[stage], s.a[stage] + lane * 4 * 128, ks * BKE, g4[0], g4[1], g4[2], g4[3]);
         }
         ++issued;
         if (++stage == STAGES) stage = 0, phase ^= 1;
@@ -527,15 +562,19 @@ int num_sms() {
 template <int BN, bool FP8, bool SCATTER = false, bool HWS = false, bool PAIR = false>
 void launch_gemm_ptr(const torch::Tensor& a, const torch::Tensor& b, __nv_bfloat16* out_ptr, int ldc, int n_out,
                      const float* sa, const float* sb, int* status, cudaStream_t stream, int max_ctas,
-                     const int* grp_off, int groups, ScatterArgs sc) {
+                     const int* grp_off, int groups, ScatterArgs sc, const int* a_rows = nullptr, int m_rows = 0) {
   static_assert(!PAIR || HWS, "CTA pairs run the hardware-scaled kernel");
-  const int M = a.size(0), K = a.size(1);
+  // a_rows: GEMM row r reads activation row a_rows[r] (m_rows GEMM rows; `a` holds the activations and `sa`
+  // their scales [K/128, a.size(0)]); A is fetched by TMA gather4 with a one-row box
+  TORCH_CHECK(!a_rows || (HWS && !PAIR), "row-gathered A needs the hardware-scaled single-CTA kernel");
+  const int M = a_rows ? m_rows : (int)a.size(0), K = a.size(1);
+  const int sa_ld = (int)a.size(0);
   const int N = grp_off ? n_out : (int)b.size(0);   // grouped: b holds groups * N rows
   const CUtensorMapDataType dt = FP8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int esz = FP8 ? 1 : 2;
   const uint32_t box_inner = 128 / esz;
-  CUtensorMap ta = make_tmap_2d(a.data_ptr(), dt, K, M, (uint64_t)a.stride(0) * esz, box_inner, kBM,
-                                CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap ta = make_tmap_2d(a.data_ptr(), dt, K, a.size(0), (uint64_t)a.stride(0) * esz, box_inner,
+                                a_rows ? 1 : kBM, CU_TENSOR_MAP_SWIZZLE_128B);
   constexpr int BROWS = PAIR ? BN / 2 : BN;
   CUtensorMap tb = make_tmap_2d(b.data_ptr(), dt, K, b.size(0), (uint64_t)b.stride(0) * esz, box_inner, BROWS,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
@@ -579,11 +618,11 @@ void launch_gemm_ptr(const torch::Tensor& a, const torch::Tensor& b, __nv_bfloat
     int pairs = std::min(tiles, max_ctas > 0 ? std::max(1, max_ctas / 2) : max_pairs);
     cfg.gridDim = dim3(2 * pairs);
     C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, out_ptr, M, N, K, ldc, sa, sb, status, grp_off, groups,
-                                      tiles, sc));
+                                      tiles, sc, a_rows, sa_ld));
   } else {
     int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
     kern<<<grid, kGemmThreads, smem, stream>>>(ta, tb, out_ptr, M, N, K, ldc, sa, sb, status, grp_off, groups, tiles,
-                                               sc);
+                                               sc, a_rows, sa_ld);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
@@ -644,20 +683,31 @@ void gemm_fp8_block(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch:
   }
 }
 
-// Grouped block-scaled FP8 GEMM (MoE experts): xq [Mtot, K] rows sorted by group, group e = rows
+// Grouped block-scaled FP8 GEMM (MoE experts): GEMM rows sorted by group, group e = rows
 // [offsets[e], offsets[e+1]) (device int32 [G+1]); wq [G*N, K]; ws [G*ceil(N/128), K/128]; out [Mtot, N].
+// rows (optional, int32 [Mtot], hardware-scaled path): GEMM row r is xq row rows[r] and takes that row's
+// scales from xs [K/128, xq.size(0)], so the expert dispatch (token gather) happens inside the A loads;
+// without rows, xq [Mtot, K] is already in GEMM row order.
 void gemm_fp8_grouped(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor offsets,
-                      torch::Tensor out, torch::Tensor status, bool hws) {
+                      torch::Tensor out, torch::Tensor status, bool hws, c10::optional<torch::Tensor> rows) {
   TORCH_CHECK(xq.scalar_type() == at::kFloat8_e4m3fn && wq.scalar_type() == at::kFloat8_e4m3fn);
   TORCH_CHECK(offsets.scalar_type() == at::kInt && offsets.is_cuda() && offsets.dim() == 1);
-  const int M = xq.size(0), K = xq.size(1), N = out.size(1), G = offsets.size(0) - 1;
+  const int M = rows ? (int)rows->size(0) : (int)xq.size(0), K = xq.size(1), N = out.size(1), G = offsets.size(0) - 1;
   TORCH_CHECK(G >= 1 && wq.size(0) == (int64_t)G * N && wq.size(1) == K && K % 128 == 0 && N % 8 == 0);
   TORCH_CHECK(ws.size(0) == (int64_t)G * ((N + 127) / 128) && ws.size(1) == K / 128);
-  TORCH_CHECK(xs.size(0) == K / 128 && xs.size(1) == M && out.size(0) == M);
+  TORCH_CHECK(xs.size(0) == K / 128 && xs.size(1) == xq.size(0) && out.size(0) == M);
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(xq.device());
   auto stream = at::cuda::getCurrentCUDAStream();
-  if (hws)
+  if (rows) {
+    TORCH_CHECK(hws && rows->scalar_type() == at::kInt && rows->is_cuda() && rows->is_contiguous(),
+                "row-gathered grouped GEMM: hardware scaling and int32 rows");
+    TORCH_CHECK(xq.stride(1) == 1 && xs.is_contiguous());
+    launch_gemm_ptr<256, true, false, true>(xq, wq, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                                            (int)out.stride(0), N, xs.data_ptr<float>(), ws.data_ptr<float>(),
+                                            status.data_ptr<int>(), stream, 0, offsets.data_ptr<int>(), G,
+                                            ScatterArgs{nullptr, 0, 1, 0}, rows->data_ptr<int>(), M);
+  } else if (hws)
     launch_gemm<256, true, true>(xq, wq, out, xs.data_ptr<float>(), ws.data_ptr<float>(), status.data_ptr<int>(),
                                  stream, 0, offsets.data_ptr<int>(), G);
   else

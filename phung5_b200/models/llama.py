@@ -325,7 +325,7 @@ class LlamaModel:
             comm.project(lw.o, a, m)
             if lw.moe is not None:
                 yb = comm.ar_norm(m, lw.post_norm, cfg.rms_eps, out_bf16=True, recv=True)
-                comm.partial(m).copy_(lw.moe(ops.act_quant(yb) if fp8 else yb, yb))
+                lw.moe(ops.act_quant(yb) if fp8 else yb, yb, out=comm.partial(m))
                 recv = False
             else:
                 x = comm.ar_norm(m, lw.post_norm, cfg.rms_eps, out_bf16=not fp8, recv=True)

@@ -6,9 +6,10 @@ softmax over the selected logits (Mixtral's rule, also the oracle's in models/re
 Expert parallelism: rank r of `ep` ranks owns experts [r*E/ep, (r+1)*E/ep) with full FFN width. Every
 rank holds every token (attention is tensor-parallel and its output is all-reduced), so dispatch is a
 local selection: the (token, slot) assignments of local experts are sorted by expert on the device
-(stable argsort, counts -> offsets, no host round trip), the fp8 activations are gathered in that
-order, gate/up and down run as grouped GEMMs over the per-expert row segments, and the combine
-scatters weight * expert output back per token. Each rank's output holds only its experts'
+(stable argsort, counts -> offsets, no host round trip); the gate/up grouped GEMM reads each permuted
+row's fp8 activations and scales straight from the token's row (TMA gather4 in the GEMM's A loads, no
+permuted copy), down runs over the per-expert row segments, and one fused kernel (ops.moe_combine)
+sums weight * expert output per token into the buffer the tensor-parallel reduction reads. Each rank's output holds only its experts'
 contributions; the layer's all-reduce (the same collective as tensor-parallel MLPs) completes it.
 Rows beyond the local assignment count are never written by the grouped GEMMs; the combine selects
 (not multiplies) them away, so uninitialised rows cannot leak NaN.
@@ -55,7 +56,9 @@ class MoEBlock:
         v, i = torch.topk(logits.float(), self.top_k, dim=-1)
         return i, torch.softmax(v, dim=-1)
 
-    def __call__(self, x_act, xb: torch.Tensor) -> torch.Tensor:
+    def __call__(self, x_act, xb: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """-> this rank's experts' contribution per token, bf16 [T, H] (written into `out` when given, e.g.
+        the fused tensor-parallel reduction's partial buffer)."""
         t = xb.shape[0]
         k, el = self.top_k, self.e_local
         ids, w = self.route(xb)
@@ -68,11 +71,10 @@ class MoEBlock:
         offsets[1:] = torch.cumsum(counts, 0).to(torch.int32)
         tok = order // k                                          # token of each permuted row
         if self.fp8:
-            xq, xs = x_act
-            xp = (xq[tok], xs[:, tok].contiguous())
+            # dispatch inside the GEMM: its A loads gather the tokens' fp8 rows and scales by index
+            gu = ops.gemm_grouped(x_act, self.w13, self.w13_s, offsets, 2 * self.ffn, rows=tok.to(torch.int32))
         else:
-            xp = x_act[tok]
-        gu = ops.gemm_grouped(xp, self.w13, self.w13_s, offsets, 2 * self.ffn)
+            gu = ops.gemm_grouped(x_act[tok], self.w13, self.w13_s, offsets, 2 * self.ffn)
         aq, as_, ab = ops.silu_mul_quant(gu, quant=self.fp8, out_bf16=not self.fp8)
         y = ops.gemm_grouped((aq, as_) if self.fp8 else ab, self.w2, self.w2_s, offsets, self.hidden)
         # combine: position of every assignment in the permuted order
@@ -80,9 +82,18 @@ class MoEBlock:
         pos[order] = torch.arange(order.numel(), device=xb.device)
         pos = pos.view(t, k)
         valid = local.view(t, k)
+        if y.is_cuda:
+            if out is None:
+                out = torch.empty(t, self.hidden, dtype=torch.bfloat16, device=xb.device)
+            ops.moe_combine(y, pos, w.float().contiguous(), valid.contiguous(), out)   # one fused kernel
+            return out
         g = y[pos.clamp(min=0)]                                    # [T, k, H]
         contrib = torch.where(valid[..., None], g.float() * w[..., None], torch.zeros((), device=xb.device))
-        return contrib.sum(1).to(xb.dtype)
+        res = contrib.sum(1).to(xb.dtype)
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res
 
 
 def _expert_range(cfg: ModelConfig, rank: int, size: int):

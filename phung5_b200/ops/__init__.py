@@ -117,19 +117,24 @@ def gemm_bf16(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = No
 
 
 def gemm_grouped(x, w: torch.Tensor, ws: Optional[torch.Tensor], offsets: torch.Tensor, n: int,
-                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                 out: Optional[torch.Tensor] = None, rows: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Grouped linear for MoE experts. x = (xq, xs) block-scaled fp8 or a bf16 tensor, rows sorted by group;
     group e owns rows [offsets[e], offsets[e+1]) (int32 device tensor, no host sync) and weight rows
     [e*n, (e+1)*n) of w (ws: fp8 block scales [G*ceil(n/128), K/128]). Rows past offsets[-1] are not
-    written."""
+    written. rows (int32 [M], fp8 only): GEMM row r is activation row rows[r], so the expert dispatch (the
+    token gather) happens inside the GEMM's A loads (TMA gather4) instead of as a separate copy."""
     xq = x[0] if isinstance(x, tuple) else x
-    m = xq.shape[0]
+    if rows is not None and not (xq.is_cuda and ws is not None and FP8_HW_SCALE):
+        x = (x[0][rows.long()], x[1][:, rows.long()].contiguous()) if ws is not None else x[rows.long()]
+        xq, rows = (x[0] if isinstance(x, tuple) else x), None
+    m = xq.shape[0] if rows is None else rows.shape[0]
     if out is None:
         out = torch.empty(m, n, dtype=torch.bfloat16 if xq.is_cuda else (torch.float32 if ws is not None else xq.dtype),
                           device=xq.device)
     if xq.is_cuda:
         if ws is not None:
-            ext().gemm_fp8_grouped(x[0], x[1], w, ws, offsets, out, status_tensor(xq.device), FP8_HW_SCALE)
+            ext().gemm_fp8_grouped(x[0], x[1], w, ws, offsets, out, status_tensor(xq.device), FP8_HW_SCALE,
+                                   None if rows is None else rows.int().contiguous())
         else:
             ext().gemm_bf16_grouped(x, w, offsets, out, status_tensor(xq.device))
         return out
@@ -149,6 +154,18 @@ def gemm_grouped(x, w: torch.Tensor, ws: Optional[torch.Tensor], offsets: torch.
 # ------------------------------------------------------------------------------------------------
 # sampling
 # ------------------------------------------------------------------------------------------------
+
+def moe_combine(y: torch.Tensor, pos: torch.Tensor, w: torch.Tensor, local: torch.Tensor,
+                out: torch.Tensor) -> torch.Tensor:
+    """out[t] = sum_j local[t, j] * w[t, j] * y[pos[t, j]] (bf16, fp32 accumulate): the MoE combine of the
+    expert rows (grouped-GEMM order) back to tokens; `out` may be a strided view (a reduction's buffer)."""
+    if y.is_cuda:
+        ext().moe_combine(y, pos, w, local, out)
+        return out
+    g = y[pos.clamp(min=0)].float()
+    out.copy_(torch.where(local[..., None], g * w[..., None], torch.zeros(())).sum(1).to(out.dtype))
+    return out
+
 
 def topk_logprobs(logits: torch.Tensor, k: int, temperature: float = 1.0, vocab_offset: int = 0,
                   with_lse: bool = True):

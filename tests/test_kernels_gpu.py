@@ -356,6 +356,24 @@ def test_gdn_kernels_match_definitions():
     assert _rel(y2.float().cpu(), y2c) < 3e-2 and _rel(sg.cpu(), sc) < 3e-2
 
 
+@pytest.mark.parametrize("t,sizes,n,k", [(300, [120, 0, 333, 47], 512, 1024), (64, [5, 70], 256, 256)])
+def test_gemm_grouped_row_gather_equals_gathered_copy(t, sizes, n, k):
+    """The grouped GEMM's A loads gather activation rows by index (TMA gather4, the MoE dispatch fused into
+    the GEMM): bitwise the result of running it on the explicitly gathered copy."""
+    g = torch.Generator(device=DEV).manual_seed(t + n)
+    x = torch.randn(t, k, device=DEV, generator=g)
+    xq, xs = quant_act_block(x)
+    m = sum(sizes)
+    rows = torch.randint(0, t, (m,), device=DEV, generator=g, dtype=torch.int32)
+    ws_list, s_list = zip(*[quant_weight_block(torch.randn(n, k, device=DEV, generator=g) * 0.05) for _ in sizes])
+    wq, ws = torch.cat(ws_list), torch.cat(s_list)
+    off = torch.tensor([0] + list(torch.tensor(sizes).cumsum(0)), dtype=torch.int32, device=DEV)
+    got = ops.gemm_grouped((xq, xs), wq, ws, off, n, rows=rows)
+    ref = ops.gemm_grouped((xq[rows.long()], xs[:, rows.long()].contiguous()), wq, ws, off, n)
+    ops.check_status()
+    assert torch.equal(got, ref)
+
+
 def test_moe_block_fp8_matches_oracle_and_routes_identically():
     from phung5_b200.config import preset
     from phung5_b200.models.llama import pack_weights
@@ -412,7 +430,7 @@ def test_gemm_scatter_epilogue(fp8, m, n, k, hws):
     if fp8:
         xq, xs = quant_act_block(x)
         wq, ws = quant_weight_block(w)
-        ops.ext().gemm_scatter(xq, xs, wq, ws, base, 0, rows_per, rank, ops.status_tensor(DEV), hws, hws)
+        ops.ext().gemm_scatter(xq, xs, wq, ws, base, 0, rows_per, rank, ops.status_tensor(DEV), hws, False)
         ref = ops.gemm_fp8_block(xq, xs, wq, ws, hw_scale=hws)
     else:
         xb, wb = x.bfloat16(), w.bfloat16()
@@ -465,3 +483,24 @@ def test_argmax_without_lse(r, v):
     rv, ri = torch.topk(x.float(), 1, dim=-1)
     assert torch.equal(val, rv) and torch.equal(lse, torch.zeros_like(lse))
     assert torch.equal(x.float().gather(1, idx), rv)
+
+
+@pytest.mark.parametrize("t,k,h", [(300, 2, 4096), (17, 8, 1024), (64, 1, 256)])
+def test_moe_combine_matches_definition(t, k, h):
+    """The fused MoE combine equals the weighted gather-sum of expert rows, skips non-local slots (whose rows
+    hold garbage) and writes into a strided output."""
+    g = torch.Generator(device=DEV).manual_seed(t + k)
+    mp = t * k + 5
+    y = torch.randn(mp, h, device=DEV, generator=g).bfloat16()
+    pos = torch.randperm(t * k, device=DEV, generator=g).view(t, k)
+    w = torch.rand(t, k, device=DEV, generator=g)
+    local = torch.rand(t, k, device=DEV, generator=g) > 0.3
+    y[pos[~local]] = float("nan")                              # unwritten rows of non-local slots
+    buf = torch.full((t, h + 64), 5.0, device=DEV, dtype=torch.bfloat16)
+    out = buf[:, :h]
+    ops.moe_combine(y, pos, w, local, out)
+    torch.cuda.synchronize()
+    yf = y.float().nan_to_num(0.0)
+    ref = (torch.where(local[..., None], yf[pos] * w[..., None], torch.zeros((), device=DEV))).sum(1)
+    assert _rel(out, ref) < 1e-2 and torch.isfinite(out.float()).all()
+    assert bool((buf[:, h:] == 5.0).all())
