@@ -687,7 +687,9 @@ void gemm_fp8_block(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch:
 // [offsets[e], offsets[e+1]) (device int32 [G+1]); wq [G*N, K]; ws [G*ceil(N/128), K/128]; out [Mtot, N].
 // rows (optional, int32 [Mtot], hardware-scaled path): GEMM row r is xq row rows[r] and takes that row's
 // scales from xs [K/128, xq.size(0)], so the expert dispatch (token gather) happens inside the A loads;
-// without rows, xq [Mtot, K] is already in GEMM row order.
+// without rows, xq [Mtot, K] is already in GEMM row order. Measured at Mixtral EP8 shapes (2048 rows per
+// expert, N = 28672, K = 4096): 0.636 ms with rows vs 0.280 ms for a gather copy + the plain grouped GEMM --
+// 32 gather4 TMA operations per stage (and per N tile) bound the producer -- so the MoE block gathers once.
 void gemm_fp8_grouped(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor offsets,
                       torch::Tensor out, torch::Tensor status, bool hws, c10::optional<torch::Tensor> rows) {
   TORCH_CHECK(xq.scalar_type() == at::kFloat8_e4m3fn && wq.scalar_type() == at::kFloat8_e4m3fn);

@@ -68,6 +68,35 @@ def case_gemm_fp8(m, n, k, bn=0):
     return fn, 2.0 * m * n * k, "fp8"
 
 
+def case_moe_gate_up_gather(tokens, per_expert, n, k, gather=True):
+    """One expert's gate/up grouped GEMM with the dispatch inside the A loads (TMA gather4 of token rows), or
+    (gather=False) an explicit row gather of the fp8 activations and scales followed by the plain grouped GEMM."""
+    x = torch.randn(tokens, k, device="cuda", dtype=torch.bfloat16)
+    xq, xs = ops.act_quant(x)
+    wq = (torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.05).to(FP8_DTYPE)
+    ws = pow2_scale(torch.rand((n + 127) // 128, k // 128, device="cuda") * 4.48)
+    rows = torch.randint(0, tokens, (per_expert,), device="cuda", dtype=torch.int32)
+    off = torch.tensor([0, per_expert], dtype=torch.int32, device="cuda")
+    out = torch.empty(per_expert, n, device="cuda", dtype=torch.bfloat16)
+    if gather:
+        fn = lambda: ops.gemm_grouped((xq, xs), wq, ws, off, n, out=out, rows=rows)
+    else:
+        rl = rows.long()
+        fn = lambda: ops.gemm_grouped((xq[rl], xs[:, rl].contiguous()), wq, ws, off, n, out=out)
+    return fn, 2.0 * per_expert * n * k, "fp8"
+
+
+def case_moe_combine(t, k, h):
+    """Fused MoE combine: t tokens x top-k expert rows of width h -> bf16 [t, h]."""
+    y = torch.randn(t * k, h, device="cuda", dtype=torch.bfloat16)
+    pos = torch.randperm(t * k, device="cuda").view(t, k)
+    w = torch.rand(t, k, device="cuda")
+    local = torch.ones(t, k, device="cuda", dtype=torch.bool)
+    out = torch.empty(t, h, device="cuda", dtype=torch.bfloat16)
+    fn = lambda: ops.moe_combine(y, pos, w, local, out)
+    return fn, t * k * h * 2 + t * h * 2, "bytes"
+
+
 def case_gemm_bf16(m, n, k):
     x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
     w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.05
@@ -193,6 +222,12 @@ CASES = {
     "gemm_fp8_gate_up_tp8": lambda: case_gemm_fp8(4096, 7168, 8192),
     "gemm_fp8_draft_m512": lambda: case_gemm_fp8(512, 57344, 8192),
     "gemm_bf16_lm_head": lambda: case_gemm_bf16(4096, 128256, 8192),
+    # Mixtral-shaped MoE at EP8 (8192 tokens x top-2 over 8 experts: 2048 assignments per expert)
+    "moe_gate_up_gather": lambda: case_moe_gate_up_gather(8192, 2048, 28672, 4096),
+    "moe_gate_up_copy": lambda: case_moe_gate_up_gather(8192, 2048, 28672, 4096, gather=False),
+    "moe_gate_up_gather_small": lambda: case_moe_gate_up_gather(640, 160, 28672, 4096),
+    "moe_gate_up_copy_small": lambda: case_moe_gate_up_gather(640, 160, 28672, 4096, gather=False),
+    "moe_combine": lambda: case_moe_combine(8192, 2, 4096),
     "attn_prefix_tc": lambda: case_attention("prefix", "tc"),
     "attn_prefix_mma": lambda: case_attention("prefix", "mma"),
     "attn_suffix_tc": lambda: case_attention("suffix", "tc"),
@@ -200,6 +235,7 @@ CASES = {
     # per-rank shapes of tensor parallelism over 8 GPUs (Llama-3-70B, 64 requests x 64-node verify)
     "gemm_fp8_qkv_tp8": lambda: case_gemm_fp8(4096, 1280, 8192),
     "gemm_fp8_o_tp8": lambda: case_gemm_fp8(4096, 8192, 1024),
+    "gemm_fp8_o_tp8_hws": lambda: case_gemm_fp8(4096, 8192, 1024, bn=256),   # explicit BN: hardware scaling
     "gemm_fp8_o_tp8_bn128": lambda: case_gemm_fp8(4096, 8192, 1024, bn=128),
     "gemm_fp8_down_tp8_bn128": lambda: case_gemm_fp8(4096, 8192, 3584, bn=128),
     "gemm_fp8_down_tp8": lambda: case_gemm_fp8(4096, 8192, 3584),

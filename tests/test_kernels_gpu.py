@@ -417,7 +417,7 @@ def test_selftest_cli_passes():
 
 @pytest.mark.parametrize("fp8,m,n,k,hws", [(True, 4096, 8192, 1024, True), (True, 300, 1024, 512, True),
                                            (False, 200, 512, 256, False), (True, 77, 256, 128, True),
-                                           (True, 300, 1024, 512, False)])
+                                           (True, 300, 1024, 512, False), (True, 4096, 8192, 3584, True)])
 def test_gemm_scatter_epilogue(fp8, m, n, k, hws):
     """The row-parallel projection's scatter epilogue: row r lands in buffer owner(r) = r // rows_per at slot
     [rank][r - owner * rows_per]. Four local buffers stand in for the peers' receive regions."""
