@@ -355,10 +355,13 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
   p.num_tiles = (int)num_tiles;
   p.scale_log2 = (float)softmax_scale * kLog2e;
   const int smem = 5 * 64 * 256;
-  static bool attr = false;
-  if (!attr) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool attr[64] = {};   // the opt-in belongs to each device's context
+  TORCH_CHECK(dev < 64, "device index out of range");
+  if (!attr[dev]) {
     cudaFuncSetAttribute(paged_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
+    attr[dev] = true;
   }
   dim3 grid((unsigned)num_tiles, Hkv);
   paged_attention_kernel<<<grid, 128, smem, stream>>>(p);

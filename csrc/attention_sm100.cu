@@ -510,10 +510,13 @@ void paged_attention_tc(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_
   p.num_tiles = (int)num_tiles;
   p.scale_log2 = (float)softmax_scale * kLog2e;
   const size_t smem = sizeof(Smem) + 1024;
-  static bool attr = false;
-  if (!attr) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool attr[64] = {};   // the opt-in belongs to each device's context
+  TORCH_CHECK(dev < 64, "device index out of range");
+  if (!attr[dev]) {
     cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = true;
+    attr[dev] = true;
   }
   dim3 grid((unsigned)num_tiles, Hkv);
   attn_kernel<<<grid, kThreads, smem, stream>>>(tq, tk, tv, p);

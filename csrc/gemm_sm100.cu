@@ -582,10 +582,14 @@ void launch_gemm_ptr(const torch::Tensor& a, const torch::Tensor& b, __nv_bfloat
   const size_t smem = ((sizeof(GemmSmem<BN, STAGES, HWS, BROWS>) + 127) & ~size_t(127)) + 1024 +
                       (SCATTER ? (size_t)kEpiWarps * 32 * scatter_row_bytes<BN>() : 0);
   auto kern = gemm_sm100_kernel<BN, FP8, SCATTER, HWS, PAIR>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  // per device: a process may drive several GPUs (the attribute belongs to each device's context)
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static bool attr_set[64] = {};
+  TORCH_CHECK(dev < 64, "device index out of range");
+  if (!attr_set[dev]) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr_set = true;
+    attr_set[dev] = true;
   }
   constexpr int BMT = PAIR ? 2 * kBM : kBM;
   // grouped: at most M/128 + groups row tiles in total (one partial tile per group)
@@ -605,7 +609,8 @@ void launch_gemm_ptr(const torch::Tensor& a, const torch::Tensor& b, __nv_bfloat
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    static int max_pairs = 0;
+    static int max_pairs_dev[64] = {};
+    int& max_pairs = max_pairs_dev[dev];
     if (!max_pairs) {
       cfg.gridDim = dim3(2 * (num_sms() / 2));
       int n = 0;
