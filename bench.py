@@ -1,7 +1,7 @@
 """Headline benchmark: output tokens/s (and p50 TPOT) of Llama-3-70B-shaped block-scaled FP8
 speculative decoding with tensor parallelism over the GPUs of one node.
 
-Workload: 64 requests sharing one 4096-token random prefix plus 512-token unique
+Workload (Llama-3-70B FP8 serving benchmark): 64 requests sharing one 4096-token random prefix plus 512-token unique
 random suffixes; an EAGLE-style one-layer draft head builds a 64-node top-k=8 tree (depth 6) per
 request per step; the target verifies the tree with cascade attention over the shared prefix;
 256 output tokens per request. Weights are random-init (no checkpoints offline), token ids are

@@ -43,6 +43,8 @@ void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M,
 void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tensor w, c10::optional<torch::Tensor> ws,
                   torch::Tensor peer_base, int64_t off_recv, int64_t rows_per, int64_t rank, torch::Tensor status,
                   bool hws, bool pair);
+void gemm_fp8_swiglu(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor q,
+                     torch::Tensor qs, torch::Tensor status);
 void moe_combine(torch::Tensor y, torch::Tensor pos, torch::Tensor w, torch::Tensor local, torch::Tensor out);
 void tp_allgather(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t nbytes, torch::Tensor status,
                   std::vector<int64_t> offsets);
@@ -78,6 +80,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_allgather", &phx::tp_allgather);
   m.def("gemm_scatter", &phx::gemm_scatter);
   m.def("moe_combine", &phx::moe_combine);
+  m.def("gemm_fp8_swiglu", &phx::gemm_fp8_swiglu);
   m.def("gdn_recurrent", &phx::gdn_recurrent);
   m.def("gdn_fold", &phx::gdn_fold);
   m.def("gdn_gates", &phx::gdn_gates);

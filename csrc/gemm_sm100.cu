@@ -66,6 +66,7 @@ struct GemmSmem {
   uint64_t tfull[512 / BN];
   uint64_t tempty[512 / BN];
   uint64_t done;
+  uint64_t up_ready, up_free;   // SWIGLU epilogue: up-half warps -> gate-half warps hand-off of staged rows
   uint32_t tmem_base;
   int abort;
 };
@@ -136,15 +137,29 @@ struct ScatterArgs {
   int rows_per, rank;
 };
 
-template <int BN, bool FP8, bool SCATTER, bool HWS, bool PAIR>
+// SwiGLU epilogue of the gate/up projection (hardware-scaled fp8, BN = 256). The weight rows are interleaved
+// in 128-row blocks (gate block j, then up block j), so output tile n0 holds gate columns [n0/2, n0/2 + 128)
+// in its first 128 columns and the matching up columns in the other 128. The epilogue writes
+// a = bf16(silu(bf16(g)) * bf16(u)) quantized to e4m3 with one power-of-two scale per 128 columns:
+// q [M, F] (row stride F) and qs [F/128, M] -- bitwise what the GEMM's bf16 [g | u] output followed by
+// silu_mul_quant produces, without the [M, 2F] bf16 round trip through HBM.
+struct SwigluArgs {
+  uint8_t* q;
+  float* qs;
+  int F;
+};
+
+template <int BN, bool FP8, bool SCATTER, bool HWS, bool PAIR, bool SWIGLU = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       __nv_bfloat16* __restrict__ out, int M, int N, int K, int ldc, const float* __restrict__ sa,
                       const float* __restrict__ sb, int* status, const int* __restrict__ grp_off, int groups,
-                      int max_tiles, const ScatterArgs sc, const int* __restrict__ a_rows, int sa_ld) {
+                      int max_tiles, const ScatterArgs sc, const int* __restrict__ a_rows, int sa_ld,
+                      const SwigluArgs sw) {
   static_assert(!HWS || FP8, "hardware scaling is an fp8 mode");
   static_assert(!PAIR || (HWS && BN == 256), "CTA pairs run the hardware-scaled 256-wide tile");
-  constexpr int STAGES = gemm_stages<BN, SCATTER, PAIR>();
+  static_assert(!SWIGLU || (HWS && BN == 256 && !PAIR && !SCATTER), "SwiGLU epilogue: single-CTA hardware-scaled BN=256");
+  constexpr int STAGES = gemm_stages<BN, SCATTER || SWIGLU, PAIR>();
   constexpr int BKE = FP8 ? 128 : 64;  // K elements per 128-byte stage row
   constexpr int BMT = PAIR ? 2 * kBM : kBM;   // output rows per tile (both CTAs of a pair)
   constexpr int BROWS = PAIR ? BN / 2 : BN;   // B rows staged by this CTA
@@ -185,6 +200,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&s.tempty[i], PAIR ? 2 * kEpiWarps : kEpiWarps);   // pair: both CTAs' epilogue warps
     }
     mbar_init(&s.done, 1);
+    mbar_init(&s.up_ready, 4);   // the four up-half epilogue warps
+    mbar_init(&s.up_free, 4);    // the four gate-half epilogue warps
     s.abort = 0;
     fence_mbar_init();
     prefetch_tmap(&tmA);
@@ -436,6 +453,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // the scales of the next (tile, k block) are loaded one step ahead, so their latency overlaps the
     // current block's TMEM drain
     int t = unit;
+    int swg_iter = 0;             // SWIGLU: tiles handed through the staging buffer so far (mbarrier phase)
     float sa_next = 0.f, sb_next = 0.f;
     auto load_scales = [&](int tt, int kb) {
       if (!PROMOTE || tt >= num_tiles) return;
@@ -488,7 +506,63 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (++tb == NBUF) tb = 0, tphase ^= 1;
       }
-      if constexpr (SCATTER) {
+      if constexpr (SWIGLU) {
+        // up-half warps stage their rows' up values (bf16) in shared memory; gate-half warps combine them with
+        // their gate values, quantize each row's 128 outputs and store them. Two mbarriers with bounded waits
+        // hand the staging buffer back and forth (a timed-out wait abandons the tile loop, never hangs).
+        constexpr int ROWB = scatter_row_bytes<BN>();
+        uint8_t* st = reinterpret_cast<uint8_t*>(&s) + ((sizeof(Smem) + 127) & ~size_t(127));
+        uint8_t* my_row = st + (size_t)(sub * 32 + lane) * ROWB;
+        const uint32_t sphase = swg_iter & 1;
+        if (half == 1) {
+          // wait until the gate half has consumed the previous tile's rows
+          const bool ok2 = swg_iter == 0 || mbar_wait(&s.up_free, sphase ^ 1, status, kErrTimeoutEpilogue, abort);
+          if (!__all_sync(0xffffffffu, ok2)) goto epi_done;
+#pragma unroll
+          for (int c = 0; c < CPT / 8; ++c)
+            *reinterpret_cast<uint4*>(my_row + c * 16) =
+                make_uint4(pack_bf16x2(acc[4 * c + 0].x, acc[4 * c + 0].y), pack_bf16x2(acc[4 * c + 1].x, acc[4 * c + 1].y),
+                           pack_bf16x2(acc[4 * c + 2].x, acc[4 * c + 2].y), pack_bf16x2(acc[4 * c + 3].x, acc[4 * c + 3].y));
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.up_ready);
+        } else {
+          const bool ok2 = mbar_wait(&s.up_ready, sphase, status, kErrTimeoutEpilogue, abort);
+          if (!__all_sync(0xffffffffu, ok2)) goto epi_done;
+          float amax = 0.f;
+#pragma unroll
+          for (int c = 0; c < CPT / 8; ++c) {
+            const uint4 uv = *reinterpret_cast<const uint4*>(my_row + c * 16);
+            const uint32_t uw[4] = {uv.x, uv.y, uv.z, uv.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 g = unpack_bf16x2(pack_bf16x2(acc[4 * c + j].x, acc[4 * c + j].y));
+              const float2 u = unpack_bf16x2(uw[j]);
+              const float2 a = unpack_bf16x2(pack_bf16x2(g.x / (1.f + expf(-g.x)) * u.x, g.y / (1.f + expf(-g.y)) * u.y));
+              acc[4 * c + j] = a;
+              amax = fmaxf(amax, fmaxf(fabsf(a.x), fabsf(a.y)));
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s.up_free);
+          float inv;
+          const float scale = fp8_block_scale(amax, &inv);
+          if (row < ti.m_end && row < M) {
+            const int oc = ti.n0 >> 1;   // output column block of this tile
+            uint8_t* qrow = sw.q + (size_t)row * sw.F + oc;
+#pragma unroll
+            for (int c = 0; c < CPT / 16; ++c) {
+              uint4 v;
+              v.x = pack_fp8x4(acc[8 * c + 0].x * inv, acc[8 * c + 0].y * inv, acc[8 * c + 1].x * inv, acc[8 * c + 1].y * inv);
+              v.y = pack_fp8x4(acc[8 * c + 2].x * inv, acc[8 * c + 2].y * inv, acc[8 * c + 3].x * inv, acc[8 * c + 3].y * inv);
+              v.z = pack_fp8x4(acc[8 * c + 4].x * inv, acc[8 * c + 4].y * inv, acc[8 * c + 5].x * inv, acc[8 * c + 5].y * inv);
+              v.w = pack_fp8x4(acc[8 * c + 6].x * inv, acc[8 * c + 6].y * inv, acc[8 * c + 7].x * inv, acc[8 * c + 7].y * inv);
+              *reinterpret_cast<uint4*>(qrow + c * 16) = v;
+            }
+            sw.qs[(size_t)(oc >> 7) * M + row] = scale;
+          }
+        }
+        ++swg_iter;
+      } else if constexpr (SCATTER) {
         // stage the warp's 32 rows, then store them row-contiguously (2 or 4 rows per warp instruction) into
         // each row's owner receive slot: NVLink writes of whole 256/128-byte row segments
         constexpr int ROWB = scatter_row_bytes<BN>();
@@ -559,10 +633,11 @@ int num_sms() {
   return n;
 }
 
-template <int BN, bool FP8, bool SCATTER = false, bool HWS = false, bool PAIR = false>
+template <int BN, bool FP8, bool SCATTER = false, bool HWS = false, bool PAIR = false, bool SWIGLU = false>
 void launch_gemm_ptr(const torch::Tensor& a, const torch::Tensor& b, __nv_bfloat16* out_ptr, int ldc, int n_out,
                      const float* sa, const float* sb, int* status, cudaStream_t stream, int max_ctas,
-                     const int* grp_off, int groups, ScatterArgs sc, const int* a_rows = nullptr, int m_rows = 0) {
+                     const int* grp_off, int groups, ScatterArgs sc, const int* a_rows = nullptr, int m_rows = 0,
+                     SwigluArgs sw = SwigluArgs{nullptr, nullptr, 0}) {
   static_assert(!PAIR || HWS, "CTA pairs run the hardware-scaled kernel");
   // a_rows: GEMM row r reads activation row a_rows[r] (m_rows GEMM rows; `a` holds the activations and `sa`
   // their scales [K/128, a.size(0)]); A is fetched by TMA gather4 with a one-row box
@@ -578,10 +653,10 @@ void launch_gemm_ptr(const torch::Tensor& a, const torch::Tensor& b, __nv_bfloat
   constexpr int BROWS = PAIR ? BN / 2 : BN;
   CUtensorMap tb = make_tmap_2d(b.data_ptr(), dt, K, b.size(0), (uint64_t)b.stride(0) * esz, box_inner, BROWS,
                                 CU_TENSOR_MAP_SWIZZLE_128B);
-  constexpr int STAGES = gemm_stages<BN, SCATTER, PAIR>();
+  constexpr int STAGES = gemm_stages<BN, SCATTER || SWIGLU, PAIR>();
   const size_t smem = ((sizeof(GemmSmem<BN, STAGES, HWS, BROWS>) + 127) & ~size_t(127)) + 1024 +
-                      (SCATTER ? (size_t)kEpiWarps * 32 * scatter_row_bytes<BN>() : 0);
-  auto kern = gemm_sm100_kernel<BN, FP8, SCATTER, HWS, PAIR>;
+                      ((SCATTER || SWIGLU) ? (size_t)kEpiWarps * 32 * scatter_row_bytes<BN>() : 0);
+  auto kern = gemm_sm100_kernel<BN, FP8, SCATTER, HWS, PAIR, SWIGLU>;
   // per device: a process may drive several GPUs (the attribute belongs to each device's context)
   int dev = 0;
   cudaGetDevice(&dev);
@@ -623,11 +698,11 @@ void launch_gemm_ptr(const torch::Tensor& a, const torch::Tensor& b, __nv_bfloat
     int pairs = std::min(tiles, max_ctas > 0 ? std::max(1, max_ctas / 2) : max_pairs);
     cfg.gridDim = dim3(2 * pairs);
     C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, out_ptr, M, N, K, ldc, sa, sb, status, grp_off, groups,
-                                      tiles, sc, a_rows, sa_ld));
+                                      tiles, sc, a_rows, sa_ld, sw));
   } else {
     int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
     kern<<<grid, kGemmThreads, smem, stream>>>(ta, tb, out_ptr, M, N, K, ldc, sa, sb, status, grp_off, groups, tiles,
-                                               sc, a_rows, sa_ld);
+                                               sc, a_rows, sa_ld, sw);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
@@ -686,6 +761,27 @@ void gemm_fp8_block(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch:
     if (b == 256) launch_gemm<256, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
     else launch_gemm<128, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
   }
+}
+
+// Gate/up projection with the SwiGLU + FP8 quant epilogue (see SwigluArgs): wq / ws hold the gate and up
+// weights interleaved in 128-row blocks ([2F, K] / [2F/128, K/128]); q [M, F] e4m3 and qs [F/128, M] fp32 out.
+void gemm_fp8_swiglu(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor q,
+                     torch::Tensor qs, torch::Tensor status) {
+  TORCH_CHECK(xq.is_cuda() && xq.scalar_type() == at::kFloat8_e4m3fn && wq.scalar_type() == at::kFloat8_e4m3fn);
+  TORCH_CHECK(q.scalar_type() == at::kFloat8_e4m3fn && q.is_contiguous() && qs.scalar_type() == at::kFloat &&
+              qs.is_contiguous());
+  const int M = xq.size(0), K = xq.size(1), N = wq.size(0), F = N / 2;
+  TORCH_CHECK(wq.size(1) == K && K % 128 == 0 && N % 256 == 0, "gemm_fp8_swiglu: K % 128 == 0, 2F % 256 == 0");
+  TORCH_CHECK(xq.stride(1) == 1 && wq.stride(1) == 1 && xs.is_contiguous() && xs.size(0) == K / 128 && xs.size(1) == M);
+  TORCH_CHECK(ws.is_contiguous() && ws.size(0) == N / 128 && ws.size(1) == K / 128);
+  TORCH_CHECK(q.size(0) == M && q.size(1) == F && qs.size(0) == F / 128 && qs.size(1) == M);
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(xq.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  launch_gemm_ptr<256, true, false, true, false, true>(
+      xq, wq, nullptr, N, N, xs.data_ptr<float>(), ws.data_ptr<float>(), status.data_ptr<int>(), stream, 0, nullptr,
+      0, ScatterArgs{nullptr, 0, 1, 0}, nullptr, 0,
+      SwigluArgs{reinterpret_cast<uint8_t*>(q.data_ptr()), qs.data_ptr<float>(), F});
 }
 
 // Grouped block-scaled FP8 GEMM (MoE experts): GEMM rows sorted by group, group e = rows

@@ -97,6 +97,22 @@ def case_moe_combine(t, k, h):
     return fn, t * k * h * 2 + t * h * 2, "bytes"
 
 
+def case_gemm_swiglu(m, f, k, fused=True):
+    """Gate/up projection + SwiGLU + FP8 quant: one GEMM with the fused epilogue, or (fused=False) the GEMM's
+    bf16 [gate | up] output followed by silu_mul_quant."""
+    from ..models.llama import interleave_gate_up
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    xq, xs = ops.act_quant(x)
+    wq = (torch.randn(2 * f, k, device="cuda", dtype=torch.bfloat16) * 0.05).to(FP8_DTYPE)
+    ws = pow2_scale(torch.rand(2 * f // 128, k // 128, device="cuda") * 4.48)
+    if fused:
+        wi, si = interleave_gate_up(wq, ws)
+        fn = lambda: ops.gemm_fp8_swiglu(xq, xs, wi, si)
+    else:
+        fn = lambda: ops.silu_mul_quant(ops.gemm_fp8_block(xq, xs, wq, ws), quant=True, out_bf16=False)
+    return fn, 2.0 * m * 2 * f * k, "fp8"
+
+
 def case_gemm_bf16(m, n, k):
     x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
     w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.05
@@ -222,6 +238,10 @@ CASES = {
     "gemm_fp8_gate_up_tp8": lambda: case_gemm_fp8(4096, 7168, 8192),
     "gemm_fp8_draft_m512": lambda: case_gemm_fp8(512, 57344, 8192),
     "gemm_bf16_lm_head": lambda: case_gemm_bf16(4096, 128256, 8192),
+    "gate_up_swiglu_fused": lambda: case_gemm_swiglu(4096, 28672, 8192),
+    "gate_up_swiglu_unfused": lambda: case_gemm_swiglu(4096, 28672, 8192, fused=False),
+    "gate_up_swiglu_fused_tp8": lambda: case_gemm_swiglu(4096, 3584, 8192),
+    "gate_up_swiglu_unfused_tp8": lambda: case_gemm_swiglu(4096, 3584, 8192, fused=False),
     # Mixtral-shaped MoE at EP8 (8192 tokens x top-2 over 8 experts: 2048 assignments per expert)
     "moe_gate_up_gather": lambda: case_moe_gate_up_gather(8192, 2048, 28672, 4096),
     "moe_gate_up_copy": lambda: case_moe_gate_up_gather(8192, 2048, 28672, 4096, gather=False),

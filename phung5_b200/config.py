@@ -88,9 +88,9 @@ class ModelConfig:
 class DraftConfig:
     """Draft proposer.
 
-    kind: "model" (a small standalone LM with its own embeddings and head) or
+    kind: "model" (a small standalone LM with its own embeddings and head, the CPU fp32 speculative-decode check) or
     "eagle" (a one-layer head fed fc([embed(token); target hidden]) that reuses the target's
-    embedding and lm_head).
+    embedding and lm_head, the Llama-3-8B EAGLE benchmark).
     """
 
     kind: str = "model"
@@ -162,7 +162,7 @@ class EngineConfig:
 # ---------------------------------------------------------------------------------------------
 
 PRESETS: Dict[str, ModelConfig] = {
-    # BASELINE config 1 target / draft (CPU fp32)
+    # the CPU fp32 speculative-decode check target / draft (CPU fp32)
     "tiny": ModelConfig(name="tiny", num_layers=4, hidden=256, num_heads=4, num_kv_heads=4, head_dim=64,
                         ffn=688, vocab=4096, rope_theta=1e4, rms_eps=1e-5),
     "tiny-draft": ModelConfig(name="tiny-draft", num_layers=1, hidden=256, num_heads=4, num_kv_heads=4,

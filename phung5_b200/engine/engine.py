@@ -18,7 +18,7 @@ One speculative step for the R running requests (all on device, one host round t
   5. accept: greedy match, seeded target-only tree sampling, or the synthetic geometric length;
   6. commit: accepted nodes' KV rows and hidden states move to their final slots; one D2H copy of
      (accepted count, tokens, bonus) per step feeds the host scheduler.
-The reference performs the same step inside SGLang's DFlash worker (SURVEY 3.4) with chain drafts.
+The reference performs the same step inside SGLang's DFlash worker with chain drafts.
 """
 from __future__ import annotations
 

@@ -1,6 +1,6 @@
 """Unbatched CPU speculative decoder over the fp32 oracle models.
 
-This is BASELINE config 1's reference path (target-only greedy vs speculative greedy must produce the
+This is the reference path of the CPU fp32 speculative-decode check (target-only greedy vs speculative greedy must produce the
 same tokens) and the behavioural oracle for the batched engine: the engine's per-request outputs are
 checked token-for-token against `OracleSpecDecoder`.
 
@@ -10,7 +10,7 @@ Step structure (one speculative step of one request):
   2. verify: one target forward over all tree nodes (root = pending token) with the ancestor mask;
   3. accept: walk the tree with the accept rule (engine/sampling.py), keep the KV rows of the root
      and accepted nodes, emit accepted tokens + the bonus token, which becomes the next root.
-This mirrors the reference's DFlash verify step (SURVEY 3.4: draft -> target verify -> target
+This mirrors the reference's DFlash verify step (draft -> target verify -> target
 probs -> accept -> commit), done per request in plain torch.
 """
 from __future__ import annotations

@@ -9,7 +9,7 @@ The dynamic tree is built EAGLE-2 style: starting from the root, `depth` rounds 
 candidate carries the cumulative draft log-probability of its path; the final tree keeps the
 N - 1 best candidates (ties broken toward shallower nodes so the kept set is ancestor-closed) and
 orders them by (depth, score). The reference's DFlash path only drafts chains (tree verify raises in
-docker/opt/kern/braw/kernels.py:477-478); the tree follows BASELINE config 2's 64-node top-k=8 tree.
+docker/opt/kern/braw/kernels.py:477-478); the tree is the benchmark's 64-node top-k=8 tree.
 """
 from __future__ import annotations
 

@@ -3,7 +3,7 @@
 Input at position t: z = fc([embed(x_t); f_{t-1}]) where f_{t-1} is the target's last-layer hidden
 state (pre-norm) at position t-1 (or the head's own output feature when drafting past committed
 tokens); one decoder layer over the head's own paged KV (same page table as the target, separate
-tensors); the head's final norm; the target's lm_head. BASELINE config 2 names this drafter
+tensors); the head's final norm; the target's lm_head. The Llama-3-8B benchmark names this drafter
 ("1-layer EAGLE-style head fed target hidden state + token embedding"); the reference's coder uses a
 DFlash drafter inside SGLang (configuration.yaml:54).
 """

@@ -6,7 +6,7 @@
     o = gated delta rule over the request's tokens               (state [HV, 128, 128] per slot)
     y = out_proj(rmsnorm(o) * w * silu(z))
 
-Speculative verification (the reference's DFlash verify on its GDN layers, SURVEY 3.4 step 3c) runs the
+Speculative verification (the reference's DFlash verify on its GDN layers) runs the
 draft window from the committed state without modifying it (`mode="verify"`), keeping a stash; after
 acceptance `commit(n_accept)` folds the accepted prefix into the state and advances the conv window —
 the reference's braw verify + fold (docker/opt/kern/braw/kernels.py) and its conv-window commit.

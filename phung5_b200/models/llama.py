@@ -17,7 +17,7 @@ Per layer (fp8_block):
   delta    = gemm_fp8_block(aq, as, Wd)  -> reduce
 bf16 models run the same sequence with bf16 activations and gemm_bf16.
 The reference runs these layers inside SGLang with its FP8 GEMM table and fused SiLU+quant patches
-(SURVEY 3.4 step 3: docker/opt/v5/wq/kopt_wq.py:92-116, docker/opt/v5/fusedq/fusedq.py:289-329).
+(docker/opt/v5/wq/kopt_wq.py:92-116, docker/opt/v5/fusedq/fusedq.py:289-329).
 """
 from __future__ import annotations
 
@@ -40,6 +40,9 @@ class Linear:
 
     w: torch.Tensor
     ws: Optional[torch.Tensor] = None
+    # gate/up weights whose 128-row blocks were interleaved (gate j, up j) for the fused SwiGLU epilogue; the
+    # plain call still returns the [gate | up] layout
+    gu_interleaved: bool = False
 
     @property
     def fp8(self) -> bool:
@@ -52,8 +55,40 @@ class Linear:
     def __call__(self, x, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if self.fp8:
             xq, xs = x
+            if self.gu_interleaved:
+                y = ops.gemm_fp8_block(xq, xs, self.w, self.ws)
+                m, n = y.shape
+                y = y.view(m, n // 256, 2, 128).transpose(1, 2).reshape(m, n)
+                return out.copy_(y) if out is not None else y
             return ops.gemm_fp8_block(xq, xs, self.w, self.ws, out=out)
         return ops.gemm_bf16(x, self.w, out=out)
+
+    def swiglu(self, x):
+        """Gate/up projection followed by SwiGLU: fp8 -> (q [M, F] e4m3, scales [F/128, M]) from one GEMM whose
+        epilogue does the SwiGLU and the quant (weights interleaved in place on the first call); bf16 -> the
+        bf16 activation [M, F]."""
+        if not self.fp8:
+            return ops.silu_mul_quant(self(x), quant=False, out_bf16=True)[2]
+        xq, xs = x
+        f = self.w.shape[0] // 2
+        if xq.is_cuda and ops.SWIGLU_FUSED and ops.FP8_HW_SCALE and f % 128 == 0:
+            if not self.gu_interleaved:
+                self.w, self.ws = interleave_gate_up(self.w, self.ws)
+                self.gu_interleaved = True
+            return ops.gemm_fp8_swiglu(xq, xs, self.w, self.ws)
+        q, s, _ = ops.silu_mul_quant(self(x), quant=True, out_bf16=False)
+        return q, s
+
+
+def interleave_gate_up(w: torch.Tensor, ws: torch.Tensor):
+    """[gate; up] rows (2F x K) and their 128-row block scales -> rows in 128-row blocks gate 0, up 0, gate 1,
+    up 1, ... (the layout of the fused SwiGLU epilogue: each 256-wide output tile pairs a gate block with its
+    up block)."""
+    n, k = w.shape
+    f = n // 2
+    w2 = w.view(2, f // 128, 128, k).transpose(0, 1).reshape(n, k).contiguous()
+    s2 = ws.view(2, f // 128, ws.shape[1]).transpose(0, 1).reshape(ws.shape[0], ws.shape[1]).contiguous()
+    return w2, s2
 
 
 @dataclass
@@ -298,9 +333,8 @@ class LlamaModel:
                                            out_bf16=(not fp8) or lw.moe is not None)
         if lw.moe is not None:
             return self.comm.all_reduce(lw.moe((xq, xs) if fp8 else xb, xb))
-        gu = lw.gu((xq, xs) if fp8 else xb)
-        aq, as_, ab = ops.silu_mul_quant(gu, quant=fp8, out_bf16=not fp8)
-        return self.comm.all_reduce(lw.down((aq, as_) if fp8 else ab))
+        act = lw.gu.swiglu((xq, xs) if fp8 else xb)          # fp8: SwiGLU + quant in the GEMM epilogue
+        return self.comm.all_reduce(lw.down(act))
 
     def forward_fused(self, fb: ForwardBatch, want_hidden: bool = False):
         """Tensor-parallel forward on a fused communicator (parallel/fused.py): the residual stream lives in
@@ -329,9 +363,7 @@ class LlamaModel:
                 recv = False
             else:
                 x = comm.ar_norm(m, lw.post_norm, cfg.rms_eps, out_bf16=not fp8, recv=True)
-                gu = lw.gu(x)
-                aq, as_, ab = ops.silu_mul_quant(gu, quant=fp8, out_bf16=not fp8)
-                comm.project(lw.down, (aq, as_) if fp8 else ab, m)
+                comm.project(lw.down, lw.gu.swiglu(x), m)   # fp8: SwiGLU + quant in the GEMM epilogue
                 recv = True
             last = li == n - 1
             wnext = self.w.final_norm if last else self.w.layers[li + 1].in_norm

@@ -1,4 +1,4 @@
-"""Mixtral-style sparse MoE block on the grouped tcgen05 GEMMs.
+"""Mixtral-style sparse MoE block (the Mixtral-8x7B EP8 workload) on the grouped tcgen05 GEMMs.
 
 Routing: router logits = x @ W_gate^T (replicated [E, H]); each token takes its top-k experts, weights =
 softmax over the selected logits (Mixtral's rule, also the oracle's in models/reference.py).
@@ -15,7 +15,7 @@ contributions; the layer's all-reduce (the same collective as tensor-parallel ML
 Rows beyond the local assignment count are never written by the grouped GEMMs; the combine selects
 (not multiplies) them away, so uninitialised rows cannot leak NaN.
 
-The reference serves no MoE model (EP row); this follows BASELINE config 4.
+The reference serves no MoE model; this follows the Mixtral-8x7B EP8 workload.
 """
 from __future__ import annotations
 

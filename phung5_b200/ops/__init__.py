@@ -82,6 +82,8 @@ def check_status(device=None) -> None:
 # framework produces is a power of two. PHX_FP8_PROMOTE=1 selects the software per-K-block promotion instead
 # (any fp32 scales).
 FP8_HW_SCALE = os.environ.get("PHX_FP8_PROMOTE", "0") != "1"
+# PHX_SWIGLU_FUSED=1: the gate/up projection runs SwiGLU + FP8 quant in its GEMM epilogue.
+SWIGLU_FUSED = os.environ.get("PHX_SWIGLU_FUSED", "0") == "1"
 # PHX_GEMM_PAIR=1: hardware-scaled 256-wide tiles run as 256 x 256 tiles on CTA pairs (tcgen05 cta_group::2,
 # clusters of two). Off by default: measured no faster than the single-CTA tile under the power cap.
 GEMM_PAIR = os.environ.get("PHX_GEMM_PAIR", "0") == "1"
@@ -154,6 +156,17 @@ def gemm_grouped(x, w: torch.Tensor, ws: Optional[torch.Tensor], offsets: torch.
 # ------------------------------------------------------------------------------------------------
 # sampling
 # ------------------------------------------------------------------------------------------------
+
+def gemm_fp8_swiglu(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor):
+    """Gate/up projection with the SwiGLU + FP8 quant epilogue. wq [2F, K] / ws [2F/128, K/128] hold the gate
+    and up weights interleaved in 128-row blocks (models.llama.interleave_gate_up). -> (q [M, F] e4m3,
+    scales [F/128, M]), equal to silu_mul_quant of the plain gate/up GEMM's bf16 output."""
+    m, f = xq.shape[0], wq.shape[0] // 2
+    q = torch.empty(m, f, dtype=FP8_DTYPE, device=xq.device)
+    s = torch.empty(f // 128, m, dtype=torch.float32, device=xq.device)
+    ext().gemm_fp8_swiglu(xq, xs, wq, ws, q, s, status_tensor(xq.device))
+    return q, s
+
 
 def moe_combine(y: torch.Tensor, pos: torch.Tensor, w: torch.Tensor, local: torch.Tensor,
                 out: torch.Tensor) -> torch.Tensor:

@@ -1,4 +1,4 @@
-"""Block-scaled FP8 (e4m3) quantization, the checkpoint format of BASELINE config 3.
+"""Block-scaled FP8 (e4m3) quantization, the checkpoint format of block-scaled FP8 Llama-3-70B.
 
 Weights: one fp32 scale per 128x128 block, stored HF-style as ``<name>_scale_inv`` [ceil(N/128),
 ceil(K/128)] so that ``w_fp32 ~= w_fp8 * scale_inv`` (the DeepSeek/Qwen FP8 checkpoint layout).

@@ -504,3 +504,29 @@ def test_moe_combine_matches_definition(t, k, h):
     ref = (torch.where(local[..., None], yf[pos] * w[..., None], torch.zeros((), device=DEV))).sum(1)
     assert _rel(out, ref) < 1e-2 and torch.isfinite(out.float()).all()
     assert bool((buf[:, h:] == 5.0).all())
+
+
+@pytest.mark.parametrize("m,f,k", [(300, 384, 1024), (77, 128, 256), (4096, 3584, 8192)])
+def test_gemm_swiglu_epilogue_equals_gemm_then_silu_quant(m, f, k):
+    """The gate/up GEMM with the SwiGLU + FP8 quant epilogue (weights interleaved in 128-row blocks) is bitwise
+    the plain GEMM's bf16 [gate | up] output followed by silu_mul_quant; the interleaved Linear's plain call
+    still returns the [gate | up] layout."""
+    from phung5_b200.models.llama import Linear
+    g = torch.Generator(device=DEV).manual_seed(m + f + k)
+    x = torch.randn(m, k, device=DEV, generator=g)
+    w = torch.randn(2 * f, k, device=DEV, generator=g) * 0.05
+    xq, xs = quant_act_block(x)
+    wq, ws = quant_weight_block(w)
+    gu = ops.gemm_fp8_block(xq, xs, wq, ws, bn=256, hw_scale=True)
+    q_ref, s_ref, _ = ops.silu_mul_quant(gu, quant=True, out_bf16=False)
+    lin = Linear(wq.clone(), ws.clone())
+    fused = ops.SWIGLU_FUSED
+    ops.SWIGLU_FUSED = True
+    try:
+        q, s = lin.swiglu((xq, xs))
+    finally:
+        ops.SWIGLU_FUSED = fused
+    ops.check_status()
+    assert lin.gu_interleaved
+    assert torch.equal(q.view(torch.uint8), q_ref.view(torch.uint8)) and torch.equal(s, s_ref)
+    assert torch.equal(lin((xq, xs)), gu)

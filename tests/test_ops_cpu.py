@@ -82,3 +82,15 @@ def test_pow2_block_scales_and_checkpoint_requant():
     orig = deq(wq, ws_odd)
     blk = orig.abs().view(2, 128, 3, 128).amax((1, 3)).repeat_interleave(128, 0).repeat_interleave(128, 1)
     assert ((deq(q2, s2) - orig).abs() / blk).max() <= 1 / 16 + 1e-6
+
+
+def test_gate_up_interleave_layout():
+    """128-row blocks of [gate; up] interleave as gate 0, up 0, gate 1, up 1, ... with their block scales."""
+    from phung5_b200.models.llama import interleave_gate_up
+    f, k = 384, 256
+    w = torch.arange(2 * f, dtype=torch.float32)[:, None].expand(2 * f, k).contiguous()
+    ws = torch.arange(2 * f // 128, dtype=torch.float32)[:, None].expand(2 * f // 128, k // 128).contiguous()
+    w2, s2 = interleave_gate_up(w, ws)
+    order = [r for j in range(f // 128) for r in list(range(128 * j, 128 * j + 128)) + list(range(f + 128 * j, f + 128 * j + 128))]
+    assert torch.equal(w2[:, 0], torch.tensor(order, dtype=torch.float32))
+    assert s2[:, 0].tolist() == [0, 3, 1, 4, 2, 5]

@@ -1,4 +1,4 @@
-"""CPU fp32 greedy speculative decode equals target-only greedy decode."""
+"""CPU fp32 check: CPU fp32 greedy speculative decode equals target-only greedy decode."""
 import torch
 
 from phung5_b200.config import SpecConfig, preset
