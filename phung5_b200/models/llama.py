@@ -12,8 +12,7 @@ Per layer (fp8_block):
   (aq, as) = paged_attention(q, ...)                 fp8 output, one scale per (token, head)
   o        = gemm_fp8_block(aq, as, Wo)  -> reduce
   (xq, xs) = add_rmsnorm_quant(h, o, w_post)
-  gu       = gemm_fp8_block(xq, xs, Wgu)
-  (aq, as) = silu_mul_quant(gu)
+  (aq, as) = gemm_fp8_swiglu(xq, xs, Wgu)            tcgen05, SwiGLU + fp8 quant in the epilogue
   delta    = gemm_fp8_block(aq, as, Wd)  -> reduce
 bf16 models run the same sequence with bf16 activations and gemm_bf16.
 The reference runs these layers inside SGLang with its FP8 GEMM table and fused SiLU+quant patches

@@ -82,8 +82,9 @@ def check_status(device=None) -> None:
 # framework produces is a power of two. PHX_FP8_PROMOTE=1 selects the software per-K-block promotion instead
 # (any fp32 scales).
 FP8_HW_SCALE = os.environ.get("PHX_FP8_PROMOTE", "0") != "1"
-# PHX_SWIGLU_FUSED=1: the gate/up projection runs SwiGLU + FP8 quant in its GEMM epilogue.
-SWIGLU_FUSED = os.environ.get("PHX_SWIGLU_FUSED", "0") == "1"
+# The gate/up projection runs SwiGLU + FP8 quant in its GEMM epilogue (PHX_SWIGLU_FUSED=0: GEMM, then
+# silu_mul_quant). Measured 1.877 -> 1.630 ms at 4096 x 57344 x 8192, 0.314 -> 0.280 ms at the TP8 shape.
+SWIGLU_FUSED = os.environ.get("PHX_SWIGLU_FUSED", "1") != "0"
 # PHX_GEMM_PAIR=1: hardware-scaled 256-wide tiles run as 256 x 256 tiles on CTA pairs (tcgen05 cta_group::2,
 # clusters of two). Off by default: measured no faster than the single-CTA tile under the power cap.
 GEMM_PAIR = os.environ.get("PHX_GEMM_PAIR", "0") == "1"
