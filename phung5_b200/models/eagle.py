@@ -114,9 +114,7 @@ class EagleHead:
         a = r.attention(0, q, fb, fp8)
         comm.project(lw.o, a, m)
         x = comm.ar_norm(m, lw.post_norm, cfg.rms_eps, out_bf16=not fp8, recv=True)
-        gu = lw.gu(x)
-        aq, as_, ab = ops.silu_mul_quant(gu, quant=fp8, out_bf16=not fp8)
-        comm.project(lw.down, (aq, as_) if fp8 else ab, m)
+        comm.project(lw.down, lw.gu.swiglu(x), m)      # fp8: SwiGLU + quant in the gate/up GEMM epilogue
         y = comm.ar_norm(m, self.ew.norm, cfg.rms_eps, out_bf16=True, push_h=True, recv=True)
         rows = y if fb.logits_rows is None else y[fb.logits_rows]
         return ops.gemm_bf16(rows, self.tw.lm_head), h

@@ -72,6 +72,29 @@ def _checks() -> List[Tuple[str, Callable[[], Tuple[bool, float]]]]:
         e = max(_rel(y, ref), _rel(dequant_act_block(q, s), ref))
         return e < 4e-2, e
 
+    def gemm_swiglu():
+        from ..models.llama import interleave_gate_up
+        x = torch.randn(150, 512, device=dev)
+        w = torch.randn(512, 512, device=dev) * 0.05          # [gate; up], F = 256
+        xq, xs = quant_act_block(x)
+        wq, ws = quant_weight_block(w)
+        gu = ops.gemm_fp8_block(xq, xs, wq, ws, bn=256, hw_scale=True)
+        q_ref, s_ref, _ = ops.silu_mul_quant(gu, quant=True, out_bf16=False)
+        q, s = ops.gemm_fp8_swiglu(xq, xs, *interleave_gate_up(wq, ws))
+        e = (dequant_act_block(q, s) - dequant_act_block(q_ref, s_ref)).abs().max().item()
+        return e == 0.0, e
+
+    def moe_combine():
+        y = torch.randn(40, 256, device=dev).bfloat16()
+        pos = torch.randperm(40, device=dev).view(20, 2)
+        w = torch.rand(20, 2, device=dev)
+        local = torch.rand(20, 2, device=dev) > 0.3
+        out = torch.empty(20, 256, device=dev, dtype=torch.bfloat16)
+        ops.moe_combine(y, pos, w, local, out)
+        ref = torch.where(local[..., None], y.float()[pos] * w[..., None], torch.zeros((), device=dev)).sum(1)
+        e = _rel(out, ref) if ref.norm() > 0 else 0.0
+        return e < 1e-2, e
+
     def topk():
         x = (torch.randn(64, 32000, device=dev) * 2).bfloat16()
         lp, idx, lse = ops.topk_logprobs(x, 8, temperature=0.7)
@@ -123,7 +146,8 @@ def _checks() -> List[Tuple[str, Callable[[], Tuple[bool, float]]]]:
 
     return [("gemm_fp8_block", gemm_fp8), ("gemm_bf16", gemm_bf16), ("gemm_grouped", gemm_grouped),
             ("add_rmsnorm_quant", norm_quant), ("silu_mul_quant", silu_quant), ("topk_logprobs", topk),
-            ("paged_attention", attention), ("raster", raster)]
+            ("paged_attention", attention), ("raster", raster), ("gemm_fp8_swiglu", gemm_swiglu),
+            ("moe_combine", moe_combine)]
 
 
 def run() -> Dict[str, dict]:
