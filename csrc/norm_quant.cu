@@ -238,9 +238,11 @@ __global__ void rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, int 
 // ------------------------------------------------------------------------------------------------
 // host wrappers
 // ------------------------------------------------------------------------------------------------
+// one CTA per row: up to 512 threads, so a thread holds at most two 8-element chunks of an 8192-wide row (more
+// resident CTAs per SM than 256 threads x four chunks, whose registers limited occupancy to half the warps)
 static int norm_threads(int H) {
   int nch = H / 8;
-  int t = nch >= 256 ? 256 : ((nch + 15) / 16) * 16;
+  int t = nch >= 512 ? 512 : nch >= 256 ? 256 : ((nch + 15) / 16) * 16;
   return std::max(32, ((t + 31) / 32) * 32);
 }
 
