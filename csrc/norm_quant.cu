@@ -235,6 +235,58 @@ __global__ void rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, int 
   }
 }
 
+// Wide variant (the hot path): two heads per warp (16 lanes each), four rotary pairs per lane with 8-byte q/k
+// loads and 16-byte float4 cos/sin loads, v copied in 16-byte chunks, 32-bit slot arithmetic. The per-element
+// arithmetic is the narrow kernel's, so the outputs are identical; the host checks the alignment it needs
+// (D % 8 == 0, 16-byte-aligned rows) and otherwise launches the narrow kernel.
+__global__ void rope_kv_write_wide_kernel(const __nv_bfloat16* __restrict__ qkv, int ld_qkv, const int* __restrict__ pos,
+                                          const int64_t* __restrict__ slots, const float2* __restrict__ cos_sin,
+                                          __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_cache,
+                                          __nv_bfloat16* __restrict__ v_cache, int M, int Hq, int Hkv, int D,
+                                          int page_size) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31, l16 = lane & 15;
+  const int head = (blockIdx.x * warps + (threadIdx.x >> 5)) * 2 + (lane >> 4);
+  const int tok = blockIdx.y;
+  const int nh = Hq + 2 * Hkv;
+  if (head >= nh || tok >= M) return;
+  const __nv_bfloat16* src = qkv + (size_t)tok * ld_qkv + (size_t)head * D;
+  const int half = D / 2;
+  __nv_bfloat16* dst;
+  if (head < Hq) {
+    dst = q_out + ((size_t)tok * Hq + head) * D;
+  } else {
+    const int64_t slot = slots ? slots[tok] : -1;
+    if (slot < 0) return;
+    const int s = static_cast<int>(slot);                  // pool slots fit in 31 bits (host check)
+    const int kvh = head < Hq + Hkv ? head - Hq : head - Hq - Hkv;
+    const int page = s / page_size, off = s - page * page_size;
+    __nv_bfloat16* base = head < Hq + Hkv ? k_cache : v_cache;
+    dst = base + (((size_t)page * Hkv + kvh) * page_size + off) * D;
+  }
+  if (head >= Hq + Hkv) {  // v: plain copy
+    for (int d = l16 * 8; d < D; d += 128)
+      *reinterpret_cast<uint4*>(dst + d) = *reinterpret_cast<const uint4*>(src + d);
+    return;
+  }
+  const float2* cs = cos_sin + (size_t)pos[tok] * half;
+  for (int d = l16 * 4; d < half; d += 64) {
+    const uint2 a = *reinterpret_cast<const uint2*>(src + d);
+    const uint2 b = *reinterpret_cast<const uint2*>(src + d + half);
+    const float4 c01 = *reinterpret_cast<const float4*>(cs + d);       // (cos, sin) of d and d + 1
+    const float4 c23 = *reinterpret_cast<const float4*>(cs + d + 2);   // (cos, sin) of d + 2 and d + 3
+    const float2 x1a = unpack_bf16x2(a.x), x1b = unpack_bf16x2(a.y);
+    const float2 x2a = unpack_bf16x2(b.x), x2b = unpack_bf16x2(b.y);
+    uint2 o1, o2;
+    o1.x = pack_bf16x2(x1a.x * c01.x - x2a.x * c01.y, x1a.y * c01.z - x2a.y * c01.w);
+    o1.y = pack_bf16x2(x1b.x * c23.x - x2b.x * c23.y, x1b.y * c23.z - x2b.y * c23.w);
+    o2.x = pack_bf16x2(x2a.x * c01.x + x1a.x * c01.y, x2a.y * c01.z + x1a.y * c01.w);
+    o2.y = pack_bf16x2(x2b.x * c23.x + x1b.x * c23.y, x2b.y * c23.z + x1b.y * c23.w);
+    *reinterpret_cast<uint2*>(dst + d) = o1;
+    *reinterpret_cast<uint2*>(dst + d + half) = o2;
+  }
+}
+
 // ------------------------------------------------------------------------------------------------
 // host wrappers
 // ------------------------------------------------------------------------------------------------
@@ -320,6 +372,23 @@ void rope_kv_write(torch::Tensor qkv, torch::Tensor pos, c10::optional<torch::Te
   auto stream = at::cuda::getCurrentCUDAStream();
   const int nh = Hq + 2 * Hkv;
   const int warps = 8;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool wide = D % 8 == 0 && qkv.stride(0) % 8 == 0 && al16(qkv.data_ptr()) && al16(q_out.data_ptr()) &&
+                    cos_sin.is_contiguous() && al16(cos_sin.data_ptr()) &&
+                    (!k_cache || (al16(k_cache->data_ptr()) && k_cache->size(0) * page_size < (1LL << 31))) &&
+                    (!v_cache || al16(v_cache->data_ptr()));
+  if (wide) {
+    dim3 grid((nh + 2 * warps - 1) / (2 * warps), M);
+    rope_kv_write_wide_kernel<<<grid, warps * 32, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), (int)qkv.stride(0), pos.data_ptr<int>(),
+        slots ? slots->data_ptr<int64_t>() : nullptr, reinterpret_cast<const float2*>(cos_sin.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()),
+        k_cache ? reinterpret_cast<__nv_bfloat16*>(k_cache->data_ptr()) : nullptr,
+        v_cache ? reinterpret_cast<__nv_bfloat16*>(v_cache->data_ptr()) : nullptr, M, (int)Hq, (int)Hkv, (int)D,
+        (int)page_size);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   dim3 grid((nh + warps - 1) / warps, M);
   rope_kv_write_kernel<<<grid, warps * 32, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), (int)qkv.stride(0), pos.data_ptr<int>(),

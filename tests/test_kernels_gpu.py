@@ -157,8 +157,9 @@ def test_act_quant():
     _deq_close(q.cpu(), qs.cpu(), x.float().cpu())
 
 
-def test_rope_kv_write():
-    hq, hkv, d, ps, npages = 8, 2, 128, 64, 10
+@pytest.mark.parametrize("hq,hkv,d", [(8, 2, 128), (4, 4, 64), (5, 1, 128)])
+def test_rope_kv_write(hq, hkv, d):
+    ps, npages = 64, 10
     m = 37
     qkv = torch.randn(m, (hq + 2 * hkv) * d, device=DEV).bfloat16()
     pos = torch.randint(0, 4000, (m,), device=DEV, dtype=torch.int32)
