@@ -94,3 +94,27 @@ def test_gate_up_interleave_layout():
     order = [r for j in range(f // 128) for r in list(range(128 * j, 128 * j + 128)) + list(range(f + 128 * j, f + 128 * j + 128))]
     assert torch.equal(w2[:, 0], torch.tensor(order, dtype=torch.float32))
     assert s2[:, 0].tolist() == [0, 3, 1, 4, 2, 5]
+
+
+def test_loader_requantizes_non_pow2_checkpoint_scales():
+    """An FP8 checkpoint whose weight_scale_inv values are not powers of two goes through the loader with every
+    packed scale a power of two, and each packed weight stays within one e4m3 step of the checkpoint's."""
+    from phung5_b200.config import preset
+    from phung5_b200.models.llama import pack_weights
+    from phung5_b200.models.reference import dequant_block_fp8
+    from phung5_b200.weights.init import random_weights
+    from phung5_b200.weights.quant import is_pow2
+    cfg = preset("small-fp8")
+    wd = random_weights(cfg, seed=1, std=0.02)
+    for name in [n for n in wd if n.endswith("_scale_inv")]:
+        wd[name] = wd[name] * 0.77                                # a checkpoint's own (non-power-of-two) scales
+    pw = pack_weights(cfg, wd, "cpu")
+    lw = pw.layers[0]
+    for lin in (lw.qkv, lw.o, lw.gu, lw.down):
+        assert is_pow2(lin.ws)
+    p = "model.layers.0.self_attn.o_proj.weight"
+    orig = dequant_block_fp8(wd[p], wd[p + "_scale_inv"])
+    got = dequant_block_fp8(lw.o.w, lw.o.ws)
+    n, k = orig.shape
+    blk = orig.abs().view(n // 128, 128, k // 128, 128).amax((1, 3)).repeat_interleave(128, 0).repeat_interleave(128, 1)
+    assert ((got - orig).abs() / blk).max() <= 1 / 16 + 1e-6
