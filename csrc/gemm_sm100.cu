@@ -7,6 +7,10 @@
 //     (docker/opt/v5/wq/kopt_wq_gemm.cuh:47-221, per-token x per-channel scales); this kernel is the
 //     Blackwell design for the block-scaled format.
 //   gemm_bf16: out[M,N] (bf16) = x[M,K] . w[N,K]^T, fp32 accumulate (lm_head, bf16 models).
+//   gemm_fp8_swiglu: the gate/up projection with SwiGLU + FP8 quant in the epilogue (SwigluArgs).
+//   gemm_fp8_grouped / gemm_bf16_grouped: MoE experts over device-side row offsets; optional row gather
+//     inside the A loads (TMA gather4).
+//   gemm_scatter: row-parallel projection whose epilogue stores rows into their owner rank's receive slot.
 //
 // Design (one persistent CTA per SM, 320 threads):
 //   warp 0      TMA producer: 128-byte-wide K slices of A (128 rows) and B (BN rows) into a STAGES-deep
@@ -25,7 +29,8 @@
 //   activation scales and BN/128 weight scales to exponent bytes in shared memory, in the replicated
 //   32-lane x 4-column layout, and the MMA thread moves them to TMEM with tcgen05.cp (.32x128b.warpx4)
 //   right before the stage's four MMAs (cp -> mma from one thread runs in issue order). A scale that is
-//   not a positive power of two sets kErrScaleNotPow2 in the status word.
+//   not a positive power of two sets kErrScaleNotPow2 in the status word. The producer loads the scales
+//   four stages ahead of their stage (an L2 round trip outlasts a stage's MMAs).
 //   Tiles are walked M-fastest so CTAs running together share weight (B) columns in L2.
 //   PAIR (hardware-scaled fp8, BN = 256): clusters of two CTAs on neighbouring SMs run one 256 x 256 tile with
 //   tcgen05.mma.cta_group::2 (M = 256): each CTA stages its own 128 rows of A and its own 128 rows of B,
