@@ -32,10 +32,15 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const in
   }
   for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    // every slot's row chunk is requested before any is used (the loads overlap); same summation order
+    uint4 vr[MAXK];
+#pragma unroll
+    for (int j = 0; j < MAXK; ++j)
+      vr[j] = ok[j] ? *reinterpret_cast<const uint4*>(y + (size_t)rows[j] * H + c * 8) : make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int j = 0; j < MAXK; ++j) {
       if (ok[j]) {
-        const uint4 v = *reinterpret_cast<const uint4*>(y + (size_t)rows[j] * H + c * 8);
+        const uint4 v = vr[j];
         const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
