@@ -369,11 +369,14 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
 }
 
 // Launch on raw pointers (used by entry points that manage their own buffers).
-void launch_paged_attention_raw(const AttnParams& p, int num_tiles, cudaStream_t stream) {
-  const int smem = 5 * 64 * 256;
-  cudaFuncSetAttribute(paged_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+cudaError_t paged_attention_raw_setup() {
+  return cudaFuncSetAttribute(paged_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 5 * 64 * 256);
+}
+
+cudaError_t launch_paged_attention_raw(const AttnParams& p, int num_tiles, cudaStream_t stream) {
   dim3 grid((unsigned)num_tiles, p.Hkv);
-  paged_attention_kernel<<<grid, 128, smem, stream>>>(p);
+  paged_attention_kernel<<<grid, 128, 5 * 64 * 256, stream>>>(p);
+  return cudaGetLastError();
 }
 
 }  // namespace phx

@@ -30,7 +30,12 @@ struct AttnParams {
   float scale_log2;
 };
 
-// Launch the paged attention kernel for `num_tiles` row tiles x p.Hkv KV heads on `stream`.
-void launch_paged_attention_raw(const AttnParams& p, int num_tiles, cudaStream_t stream);
+// One-time set-up of the raw launcher on the current device: opts the kernel into its dynamic shared
+// memory. Call once per device (with that device current) before launch_paged_attention_raw.
+cudaError_t paged_attention_raw_setup();
+
+// Launch the paged attention kernel for `num_tiles` row tiles x p.Hkv KV heads on `stream`; returns the
+// launch's error code. Sets no attribute and allocates nothing.
+cudaError_t launch_paged_attention_raw(const AttnParams& p, int num_tiles, cudaStream_t stream);
 
 }  // namespace phx

@@ -15,8 +15,11 @@
 //   * head_dim must be 128 and the KV page size 64 (the kernel's tile shape); the work lists must be
 //     built with 64 query rows per tile (tile_row0 multiples of 64).
 //   * Runs on the current device and on `stream`, which must belong to it. The first call on a device
-//     looks up the device address of the array (cudaGetSymbolAddress); make that first call before any
-//     stream capture. Later calls only launch kernels.
+//     sets it up: it looks up the device address of the array (cudaGetSymbolAddress) and opts the
+//     attention kernel into its dynamic shared memory (cudaFuncSetAttribute); make that first call before
+//     any stream capture. Later calls read the cached address and launch kernels (up to three).
+//   * A pass with tiles needs its whole work list: num_tiles1 > 0 (or num_tiles2 > 0) with a NULL
+//     items/tile_item/tile_row0 pointer of that pass returns PHX_NOALLOC_ERR_BAD_ARGS without launching.
 //   * All calls share the array and each call overwrites it (the LSE rows are reset at the start of
 //     every call). Calls that overlap on the GPU — on different streams, or from several host threads
 //     without ordering — race on it; order them on one stream.

@@ -1,67 +1,114 @@
 """Per-batch accounting for the results header: LLM calls per role, duels, renders, engine counters, cgroup CPU.
 
-Reference: `BatchStats` (pipeline_service/pipeline/batch_stats.py:109-271), `parse_vllm_metrics` (:58) and the
-cgroup reader. Engine counters come from this framework's server `/metrics` (phx_* series, summed over
+Reference: `BatchStats` (pipeline_service/pipeline/batch_stats.py:109-271), which also scrapes engine
+counters and cgroup CPU time. Engine counters come from this framework's server `/metrics` (phx_* series, summed over
 replicas); the CPU axis is cgroup v2 `cpu.stat` (v1 cpuacct fallback).
 Header tokens: end=<s> coder=<n>/<err>/<p50 s>/<ctok> judge=... duels=<n>/<p50>/<p95>/<wait p95>
 render=<n>/<fail>/<p50>/<p95> tail=<s since last coder reply> <tag>=<tokens>/<steps>/<accept> cpu=<cores>/<thr%>.
 """
 from __future__ import annotations
 
-import re
 import time
+from collections import Counter
 from pathlib import Path
-from typing import Any, Dict, List, Optional
+from typing import Any, Dict, List, NamedTuple, Optional
 
 from .session import CALL_LOG, CallLog
 
-_METRIC = re.compile(r"^([a-zA-Z_:][a-zA-Z0-9_:]*)(\{[^}]*\})?\s+([-+0-9.eEinfNa]+)")
 ENGINE_COUNTERS = ("phx_generated_tokens_total", "phx_engine_steps_total", "phx_accepted_draft_tokens_total")
 ENGINE_GAUGES = ("phx_num_running", "phx_num_waiting", "phx_kv_free_pages")
 
 
-def parse_metrics(text: str, names=ENGINE_COUNTERS + ENGINE_GAUGES) -> Dict[str, float]:
-    """Sum every labelled series of the whitelisted metrics."""
-    out: Dict[str, float] = {}
-    for line in text.splitlines():
-        if not line or line[0] == "#":
+def _close_brace(s: str) -> int:
+    """Index of the '}' that closes the label set opening s (s[0] == '{'); quoted label values may hold
+    braces, spaces and escaped quotes. -1 if the set is not closed."""
+    in_str = escaped = False
+    for i in range(1, len(s)):
+        ch = s[i]
+        if in_str:
+            if escaped:
+                escaped = False
+            elif ch == "\\":
+                escaped = True
+            elif ch == '"':
+                in_str = False
+        elif ch == '"':
+            in_str = True
+        elif ch == "}":
+            return i
+    return -1
+
+
+def iter_samples(text: str):
+    """(metric name, value) of every sample line of a Prometheus text exposition (labels and the optional
+    timestamp are skipped; malformed lines are ignored)."""
+    for raw in text.splitlines():
+        line = raw.strip()
+        if not line or line.startswith("#"):
             continue
-        m = _METRIC.match(line)
-        if not m or m.group(1) not in names:
+        cut = next((i for i, ch in enumerate(line) if ch == "{" or ch.isspace()), len(line))
+        name, rest = line[:cut], line[cut:]
+        if rest.startswith("{"):
+            end = _close_brace(rest)
+            if end < 0:
+                continue
+            rest = rest[end + 1:]
+        fields = rest.split()
+        if not fields:
             continue
         try:
-            out[m.group(1)] = out.get(m.group(1), 0.0) + float(m.group(3))
+            yield name, float(fields[0])
         except ValueError:
             continue
-    return out
 
 
-def read_cgroup_cpu(root: str = "/sys/fs/cgroup") -> Optional[Dict[str, float]]:
-    """cgroup v2 cpu.stat (microseconds) or the v1 cpuacct equivalents; None when neither is readable."""
+def parse_metrics(text: str, names=ENGINE_COUNTERS + ENGINE_GAUGES) -> Dict[str, float]:
+    """Per metric name in `names`: the sum over all of its labelled series."""
+    wanted = set(names)
+    totals: Counter = Counter()
+    for name, value in iter_samples(text):
+        if name in wanted:
+            totals[name] += value
+    return dict(totals)
+
+
+class CpuTimes(NamedTuple):
+    """CPU time charged to this cgroup since it was created."""
+    used_s: float
+    throttled_s: float
+    periods: int
+    throttled_periods: int
+
+
+def _int_table(path: Path) -> Dict[str, int]:
+    """'key value' lines with integer values (cgroup stat files); {} if the file cannot be read."""
     try:
-        p = Path(root) / "cpu.stat"
-        if p.exists():
-            d = {}
-            for line in p.read_text().splitlines():
-                k, _, v = line.partition(" ")
-                if v.strip().lstrip("-").isdigit():
-                    d[k] = float(v)
-            if "usage_usec" in d:
-                return {"usage_usec": d["usage_usec"], "nr_throttled": d.get("nr_throttled", 0.0),
-                        "throttled_usec": d.get("throttled_usec", 0.0), "nr_periods": d.get("nr_periods", 0.0)}
-        acct = Path(root) / "cpuacct" / "cpuacct.usage"
-        st = Path(root) / "cpu" / "cpu.stat"
-        if acct.exists():
-            d = {"usage_usec": float(acct.read_text().strip()) / 1000.0}
-            if st.exists():
-                for line in st.read_text().splitlines():
-                    k, _, v = line.partition(" ")
-                    if v.strip().isdigit():
-                        d[{"throttled_time": "throttled_usec"}.get(k, k)] = float(v) / (1000.0 if k == "throttled_time" else 1)
-            return d
+        lines = path.read_text().splitlines()
     except OSError:
+        return {}
+    table = {}
+    for line in lines:
+        parts = line.split()
+        if len(parts) == 2 and parts[1].isdigit():
+            table[parts[0]] = int(parts[1])
+    return table
+
+
+def read_cgroup_cpu(root: str = "/sys/fs/cgroup") -> Optional[CpuTimes]:
+    """CPU usage and throttling of this cgroup: cgroup v2 `cpu.stat` (microseconds), else the v1 pair
+    `cpuacct/cpuacct.usage` (nanoseconds) + `cpu/cpu.stat`; None when neither is readable."""
+    base = Path(root)
+    v2 = _int_table(base / "cpu.stat")
+    if "usage_usec" in v2:
+        return CpuTimes(v2["usage_usec"] * 1e-6, v2.get("throttled_usec", 0) * 1e-6, v2.get("nr_periods", 0),
+                        v2.get("nr_throttled", 0))
+    try:
+        used_ns = int((base / "cpuacct" / "cpuacct.usage").read_text().strip())
+    except (OSError, ValueError):
         return None
-    return None
+    v1 = _int_table(base / "cpu" / "cpu.stat")
+    return CpuTimes(used_ns * 1e-9, v1.get("throttled_time", 0) * 1e-9, v1.get("nr_periods", 0),
+                    v1.get("nr_throttled", 0))
 
 
 def cpu_quota(root: str = "/sys/fs/cgroup") -> Optional[float]:
@@ -106,7 +153,7 @@ class BatchStats:
         self.render = {"n": 0, "fail": 0, "lat": []}
         self.engine: Dict[str, List[Dict[str, float]]] = {}
         self.cpu0 = read_cgroup_cpu()
-        self.cpu1: Optional[Dict[str, float]] = None
+        self.cpu1: Optional[CpuTimes] = None
         self.roles: Dict[str, str] = {}
 
     def end(self) -> None:
@@ -153,8 +200,8 @@ class BatchStats:
                 parts.append(f"{name}={dtok:.0f}/{dst:.0f}/{(dacc / dst if dst else 0):.2f}")
         if self.cpu0 and self.cpu1:
             wall = max(1e-6, (self.ended_at or end) - self.started_at)
-            cores = (self.cpu1["usage_usec"] - self.cpu0["usage_usec"]) / 1e6 / wall
-            thr = (self.cpu1.get("throttled_usec", 0) - self.cpu0.get("throttled_usec", 0)) / 1e6 / wall
+            cores = (self.cpu1.used_s - self.cpu0.used_s) / wall
+            thr = (self.cpu1.throttled_s - self.cpu0.throttled_s) / wall
             parts.append(f"cpu={cores:.1f}/{100 * thr:.0f}")
         return parts
 

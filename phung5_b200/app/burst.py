@@ -1,9 +1,10 @@
 """Burst controller: in the judge-only tail of a batch, lend the coder GPUs to extra judge replicas.
 
 Reference: `BurstController` (pipeline_service/llm/burst.py:43-225, setup :227-258) with the proxy's
-`to_judge` / `to_coder` swaps (docker/opt/sgl/lb_proxy.py:171-240). Once every prompt of the batch has
-launched its coders and no coder call is in flight, coding is over for the batch while judging continues;
-the coder engines behind the proxy are parked (drained, weights released with /sleep) and sleeping judge
+`to_judge` / `to_coder` swaps (docker/opt/sgl/lb_proxy.py:171-240). A per-batch ledger records which prompts
+have started coding and which coder calls are open; once every prompt has been seen and no call is open,
+coding is over for the batch while judging continues. After a quiet period with no batch event, the coder
+engines behind the proxy are parked (drained, weights released with /sleep) and sleeping judge
 replicas on the same GPUs are woken and added to the judge's `LoadBalancedClient`. Any coder call
 (a retry, a refinement, the next batch) first swaps back: judge replicas leave the client, drain and sleep,
 the coder engines are unparked.
@@ -17,11 +18,29 @@ from __future__ import annotations
 import asyncio
 import logging
 import time
-from typing import List, Optional, Set
+from typing import Dict, FrozenSet, Iterable, List, Optional, Set
 
 import httpx
 
 log = logging.getLogger("phung5_b200.app")
+
+
+class _Ledger:
+    """Coding progress of the running batch: which prompts have started coding (or finished), and which coder
+    calls are open. Coding is over once every prompt of the batch has been seen and no call is open."""
+
+    def __init__(self, size: int, stems: Optional[Iterable[str]]):
+        self.size = size
+        self.stems: Optional[FrozenSet[str]] = frozenset(stems) if stems is not None else None
+        self.seen: Set[str] = set()
+        self.open_calls: Dict[int, str] = {}
+
+    def see(self, stem: str) -> None:
+        if self.stems is None or stem in self.stems:
+            self.seen.add(stem)
+
+    def coding_over(self) -> bool:
+        return not self.open_calls and len(self.seen) >= self.size
 
 
 class BurstController:
@@ -35,80 +54,77 @@ class BurstController:
         self.delay_s, self.drain_s = delay_s, drain_s
         self.state = "coder"
         self.lock = asyncio.Lock()
-        self.gen = 0
-        self.n: Optional[int] = None
-        self.stems: Optional[Set[str]] = None
-        self.pending = 0
-        self.launched: Set[str] = set()
-        self.done: Set[str] = set()
+        self.ledger: Optional[_Ledger] = None
         self.events: List[dict] = []
-        self._timer: Optional[asyncio.TimerHandle] = None
-        self._tasks: Set[asyncio.Task] = set()
+        self._activity = 0                      # bumped by every batch event; the quiet-period watcher reads it
+        self._next_call = 0
+        self._watcher: Optional[asyncio.Task] = None
+        self._background: Set[asyncio.Task] = set()
         self.t0 = time.time()
 
     def _ev(self, what: str, **kw):
-        self.events.append({"t": round(time.time() - self.t0, 2), "gen": self.gen, "what": what, **kw})
+        self.events.append({"t": round(time.time() - self.t0, 2), "what": what, **kw})
         log.info("[burst] %s %s", what, kw or "")
 
-    def _spawn(self, coro):
-        t = asyncio.get_running_loop().create_task(coro)
-        self._tasks.add(t)
-        t.add_done_callback(self._tasks.discard)
-        return t
+    def _run_later(self, coro) -> asyncio.Task:
+        task = asyncio.get_running_loop().create_task(coro)
+        self._background.add(task)                  # keep a reference until it finishes
+        task.add_done_callback(self._background.discard)
+        return task
 
     # ---------------------------------------------------------------------------------------- batch events
+    # The pipeline reports batch and coder-call events; when coding is over the controller waits for a quiet
+    # period of delay_s with no new event and only then lends the coder GPUs to the judge.
 
     def batch_start(self, n: int, stems=None) -> None:
-        self.gen += 1
-        self.n, self.stems = n, (set(stems) if stems is not None else None)
-        self.pending, self.launched, self.done = 0, set(), set()
+        self.ledger = _Ledger(n, stems)
         self.t0 = time.time()
-        self._cancel()
         self._ev("batch_start", n=n)
+        self._activity_changed()
 
     def batch_end(self) -> None:
-        self.n = None
-        self._cancel()
+        self.ledger = None
         self._ev("batch_end", state=self.state)
+        self._activity_changed()
         if self.state == "judge":
-            self._spawn(self.ensure_coder("batch end"))
+            self._run_later(self.ensure_coder("batch end"))
 
-    def coder_begin(self, stem: str, k: int = 1) -> int:
-        self.pending += k
-        self.launched.add(stem)
-        self._cancel()
-        return self.gen
+    def coder_begin(self, stem: str) -> int:
+        """Register one coder call; returns its id for coder_end."""
+        self._next_call += 1
+        if self.ledger is not None:
+            self.ledger.open_calls[self._next_call] = stem
+            self.ledger.see(stem)
+        self._activity_changed()
+        return self._next_call
 
-    def coder_end(self, gen: int) -> None:
-        if gen != self.gen:
-            return
-        self.pending -= 1
-        self._maybe_arm()
+    def coder_end(self, call_id: int) -> None:
+        # calls opened before the current batch started are not in its ledger and change nothing
+        if self.ledger is not None and self.ledger.open_calls.pop(call_id, None) is not None:
+            self._activity_changed()
 
     def task_done(self, stem: str) -> None:
-        self.done.add(stem)
-        self._maybe_arm()
+        if self.ledger is not None:
+            self.ledger.see(stem)
+            self._activity_changed()
 
-    def _maybe_arm(self) -> None:
-        seen = self.launched | self.done
-        if self.stems is not None:
-            seen &= self.stems
-        if self.n is not None and self.pending <= 0 and len(seen) >= self.n and self.state == "coder" \
-                and self._timer is None:
-            loop = asyncio.get_running_loop()
-            gen = self.gen
-            self._timer = loop.call_later(self.delay_s, lambda: self._spawn(self._fire(gen)))
+    def _judge_tail(self) -> bool:
+        return self.state == "coder" and self.ledger is not None and self.ledger.coding_over()
+
+    def _activity_changed(self) -> None:
+        self._activity += 1
+        if self._judge_tail() and (self._watcher is None or self._watcher.done()):
+            self._watcher = self._run_later(self._swap_after_quiet_period())
             self._ev("armed", delay=self.delay_s)
 
-    def _cancel(self):
-        if self._timer is not None:
-            self._timer.cancel()
-            self._timer = None
-
-    async def _fire(self, gen: int):
-        self._timer = None
-        if gen != self.gen or self.n is None or self.pending > 0:
-            return
+    async def _swap_after_quiet_period(self) -> None:
+        while True:
+            before = self._activity
+            await asyncio.sleep(self.delay_s)
+            if not self._judge_tail():
+                return
+            if self._activity == before:
+                break
         await self.to_judge()
 
     # ------------------------------------------------------------------------------------------------ swaps
@@ -181,8 +197,8 @@ class BurstCoderBackend:
 
     async def chat(self, body: dict) -> dict:
         await self.ctrl.ensure_coder("coder call")
-        gen = self.ctrl.coder_begin(body.get("metadata", {}).get("stem", f"anon{self.ctrl.pending}"))
+        call = self.ctrl.coder_begin(body.get("metadata", {}).get("stem", "?"))
         try:
             return await self.inner.chat(body)
         finally:
-            self.ctrl.coder_end(gen)
+            self.ctrl.coder_end(call)

@@ -2,7 +2,8 @@
 
 `NcclCommunicator` is the baseline: torch.distributed collectives (NCCL on GPU, gloo on CPU) issued
 between separate kernels. The fused path (`parallel/fused.py`) replaces the reductions after o_proj
-and down_proj with in-kernel NVLink peer / multimem traffic.
+and down_proj with kernels that move the rows themselves over NVLink: peer loads and stores of the
+symmetric workspace, or NVLS multimem reductions and broadcasts where the GPUs support multicast.
 
 Vocab-sharded helpers keep the exchange tiny: each rank sends its local top-k (value, global index)
 and its local log-sum-exp; the global log-softmax top-k follows exactly from those (the largest k

@@ -281,6 +281,9 @@ def test_batch_stats_parsing_and_header():
     text = "# HELP x\nphx_generated_tokens_total{rank=\"0\"} 100\nphx_generated_tokens_total{rank=\"1\"} 50\n" \
            "phx_engine_steps_total 10\nother_metric 5\n"
     assert parse_metrics(text) == {"phx_generated_tokens_total": 150.0, "phx_engine_steps_total": 10.0}
+    # label values may hold spaces, braces and escaped quotes; a timestamp may follow the value
+    odd = 'phx_num_running{route="a b}c",q="x\\"y"} 3 1700000000\nphx_num_running 2\nphx_num_waiting{bad 1\n'
+    assert parse_metrics(odd) == {"phx_num_running": 5.0}
     st = BatchStats(CallLog())
     st.engine_snapshot("vc", text)
     st.engine_snapshot("vc", text.replace("100", "400").replace("steps_total 10", "steps_total 40"))

@@ -46,18 +46,43 @@ def test_burst_swaps_in_the_judge_tail_and_back():
 
     async def go():
         ctrl.batch_start(2, ["a", "b"])
-        g = ctrl.coder_begin("a")
-        ctrl.coder_begin("b")
-        ctrl.coder_end(g)
+        ca = ctrl.coder_begin("a")
+        cb = ctrl.coder_begin("b")
+        ctrl.coder_end(ca)
+        ctrl.coder_end(ca)                           # a repeated end changes nothing
         await asyncio.sleep(0.05)
-        assert ctrl.state == "coder"                 # a coder call is still in flight
-        ctrl.coder_end(g)
+        assert ctrl.state == "coder"                 # b's coder call is still in flight
+        ctrl.coder_end(cb)
         await asyncio.sleep(0.1)
         assert ctrl.state == "judge" and all(lb.active[i] for i in idx)
         assert ("POST", "http://proxy/park") in net.calls and ("POST", "http://c0j/wake_up") in net.calls
         assert await ctrl.ensure_coder("refine")
         assert ctrl.state == "coder" and not any(lb.active[i] for i in idx)
         assert net.calls[-1] == ("POST", "http://proxy/unpark")
+    run(go())
+
+
+def test_burst_waits_for_every_prompt_and_a_quiet_period():
+    net = FakeNet()
+    lb, idx, ctrl = _burst(net, delay=0.05)
+
+    async def go():
+        ctrl.batch_start(3, ["a", "b", "c"])
+        ctrl.coder_end(ctrl.coder_begin("a"))
+        ctrl.task_done("x")                          # not a prompt of this batch
+        ctrl.coder_end(ctrl.coder_begin("b"))
+        await asyncio.sleep(0.12)
+        assert ctrl.state == "coder"                 # prompt c has not started coding
+        ctrl.task_done("c")
+        await asyncio.sleep(0.03)
+        ctrl.task_done("a")                          # activity inside the quiet period delays the swap
+        await asyncio.sleep(0.03)
+        assert ctrl.state == "coder"
+        await asyncio.sleep(0.1)
+        assert ctrl.state == "judge"
+        ctrl.batch_end()
+        await asyncio.sleep(0.02)
+        assert ctrl.state == "coder"                 # the batch end swaps back
     run(go())
 
 

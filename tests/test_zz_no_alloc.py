@@ -97,6 +97,47 @@ def test_noalloc_matches_regular_entry_point_twice():
         assert ((deq2 - deq).norm() / deq.norm()).item() < 4e-2
 
 
+def _partly_shared_case(seed):
+    """Requests 0 and 1 share their first six pages; request 2 shares nothing, so the prefix pass covers
+    none of its rows."""
+    from phung5_b200.engine.attn_meta import make_meta
+    from tests.test_kernels_gpu import _to
+    g = torch.Generator().manual_seed(seed)
+    q_lens, prefix, hq, hkv, ps = [64, 40, 50], [600, 620, 300], 8, 2, 64
+    need = [(p + n + ps - 1) // ps for p, n in zip(prefix, q_lens)]
+    npages = 6 + (need[0] - 6) + (need[1] - 6) + need[2] + 1
+    perm = torch.randperm(npages, generator=g).tolist()
+    lists = [perm[:6] + perm[6:need[0]], perm[:6] + perm[need[0]:need[0] + need[1] - 6]]
+    lists.append(perm[need[0] + need[1] - 6:need[0] + need[1] - 6 + need[2]])
+    kc = torch.randn(npages, hkv, ps, 128, generator=g).bfloat16()
+    vc = torch.randn(npages, hkv, ps, 128, generator=g).bfloat16()
+    q = torch.randn(sum(q_lens), hq, 128, generator=g).bfloat16()
+    bits = []
+    for n in q_lens:            # a chain per request: node i sees nodes 0..i
+        bits += [(1 << (i + 1)) - 1 - ((1 << 64) if i == 63 else 0) for i in range(n)]
+    meta = make_meta(lists, prefix, q_lens, torch.tensor(bits, dtype=torch.int64), causal=False, device="cpu")
+    return q.to(DEV), kc.to(DEV), vc.to(DEV), meta, _to(meta, DEV)
+
+
+def test_noalloc_ignores_stale_partials_of_a_larger_call():
+    """A large cascade call fills the shared array; a smaller call whose prefix pass covers only some requests
+    must not pick up the earlier call's partials for the other rows (their LSE is reset to -inf)."""
+    lib = _lib()
+    scale = 1 / math.sqrt(128)
+    big = _case(9, [64, 64, 64, 64], [900, 960, 700, 1000], 10)
+    small = _partly_shared_case(10)
+    for q, kc, vc, meta, gm in (big, small):
+        out, oq, osc, p1, p2 = _regular(q, kc, vc, meta, gm, scale)
+        if q is small[0]:
+            assert p1, "the small case must still run a prefix pass for requests 0 and 1"
+        rc, out2, _, _ = _noalloc(lib, q, kc, vc, meta, gm, scale, p1, p2)
+        assert rc == 0, lib.phx_noalloc_strerror(rc)
+        rel = ((out2.float() - out.float()).norm() / out.float().norm()).item()
+        assert rel < 1e-2, rel
+        per_row = ((out2.float() - out.float()).norm(dim=1) / out.float().norm(dim=1)).max().item()
+        assert per_row < 3e-2, per_row
+
+
 def test_noalloc_rejects_oversized_calls():
     lib = _lib()
     q, kc, vc, meta, gm = _case(4, [64, 64, 9], [640, 700, 520], 8)
