@@ -93,6 +93,28 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
+def _write_op_timing(rep, comm, rank, world, steps, ms):
+    """PHX_OP_TIMING=1 (eager steps): per (phase, kernel) device ms per step, max over ranks, written as JSON to
+    PHX_OP_TIMING_OUT (default op_timing.json) by rank 0."""
+    reps = [rep]
+    if comm is not None:
+        import torch.distributed as dist
+        reps = [None] * world
+        dist.all_gather_object(reps, rep)
+    out = {"steps": steps, "ms_per_step_max": 0.0, "kernels": {}, "phases": {}}
+    for r in reps:
+        for k, (v, n) in r["kernels"].items():
+            cur = out["kernels"].get(k, [0.0, 0])
+            out["kernels"][k] = [max(cur[0], round(v / steps, 4)), n // steps]
+        for k, v in r["phases"].items():
+            out["phases"][k] = max(out["phases"].get(k, 0.0), round(v / steps, 4))
+    ms_all = [ms] if comm is None else [comm.max_float(ms)]
+    out["ms_per_step_max"] = round(ms_all[0] / steps, 3)
+    if rank == 0:
+        with open(os.environ.get("PHX_OP_TIMING_OUT", "op_timing.json"), "w") as f:
+            json.dump(out, f, indent=1, sort_keys=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -181,6 +203,7 @@ def main():
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     phys = int(vis.split(",")[local]) if vis else local
     profile = os.environ.get("PHX_PROFILE_TIMED") == "1"   # ncu --profile-from-start off captures only this
+    ops.timing_reset()
     with ClockSampler(phys) as clk:
         if profile:
             torch.cuda.profiler.start()
@@ -194,6 +217,8 @@ def main():
     barrier()
     launches = ops.launches() - l0
     ms = ev0.elapsed_time(ev1)
+    if ops.OP_TIMING:
+        _write_op_timing(ops.timing_report(), comm, rank, world, args.steps, ms)
     ms = comm.max_float(ms) if comm is not None else ms
     tokens = eng.stats["tokens_out"] - n_before
     live = [r for r in eng.running]

@@ -44,15 +44,58 @@ def _time(fn, iters):
     return float(t.item())
 
 
+def ar_norm_sweep(comm, world, iters, H=8192, tokens=(1, 16, 128, 1024, 8192)):
+    """Fused-kernel sweep (a): TP all-reduce + residual + RMSNorm + FP8 quant at hidden 8192 over `tokens`, bf16
+    partials and residual ~N(0, 1), unit norm weight. Fused: one ar_norm launch (reduce-scatter by peer loads,
+    norm + quant of the owned rows, all-gather of the fp8 rows and scales by peer stores). Baseline: NCCL
+    all_reduce of the bf16 partial, then the add + RMSNorm + FP8 quant kernel on every rank. Roofline: the bytes
+    that must cross NVLink per GPU ((W-1)/W of the bf16 rows in, (W-1)/W of the fp8 rows + scales out) at the
+    measured 770 GB/s peer-copy rate."""
+    from .. import ops
+    dev = comm.device
+    w = torch.ones(H, device=dev, dtype=torch.bfloat16)
+    rows = []
+    for m in tokens:
+        g = torch.Generator(device=dev).manual_seed(11 + comm.rank)
+        part = torch.randn(m, H, device=dev, dtype=torch.bfloat16, generator=g)
+        h0 = torch.randn(m, H, device=dev, dtype=torch.bfloat16, generator=torch.Generator(device=dev).manual_seed(5))
+
+        comm.partial(m).copy_(part)
+        comm.h(m).copy_(h0)
+        x = part.clone()
+        h = h0.clone()
+
+        def nccl():
+            dist.all_reduce(x)
+            ops.add_rmsnorm_quant(h, x, w, 1e-5)
+        f_ms = _time(lambda: comm.ar_norm(m, w, 1e-5), iters)
+        n_ms = _time(nccl, iters)
+        nv = (world - 1) / world * m * H * (2 + 1 + 4 / 128)
+        roof = nv / NVLINK_GBS / 1e6
+        rows.append({"op": "sweep_ar_norm_quant", "tokens": m, "H": H, "fused_ms": round(f_ms, 4),
+                     "nccl_plus_kernel_ms": round(n_ms, 4), "speedup": round(n_ms / f_ms, 2),
+                     "roofline_ms": round(roof, 5), "fused_frac_of_roofline": round(roof / f_ms, 3)})
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--hidden", type=int, default=8192)
+    ap.add_argument("--sweep", action="store_true", help="only the fused-kernel sweep (tokens 1..8192, sampling)")
     args = ap.parse_args()
     rank, world, local = init_distributed()
     dev = torch.device("cuda", local)
     H = args.hidden
-    comm = FusedCommunicator(max_tokens=4096, hidden=H)
+    comm = FusedCommunicator(max_tokens=8192, hidden=H)
+    if args.sweep:
+        out = ar_norm_sweep(comm, world, args.iters, H)
+        if rank == 0:
+            for o in out:
+                print(json.dumps({"world": world, **o}))
+        dist.barrier()
+        dist.destroy_process_group()
+        return
     w = torch.ones(H, device=dev, dtype=torch.bfloat16)
     out = []
     for m in (4096, 512):

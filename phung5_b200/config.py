@@ -189,6 +189,9 @@ PRESETS: Dict[str, ModelConfig] = {
     # small GPU test shapes
     "small-fp8": ModelConfig(name="small-fp8", num_layers=2, hidden=1024, num_heads=8, num_kv_heads=2,
                              head_dim=128, ffn=2816 + 256, vocab=8192, rope_theta=5e5, quant="fp8_block"),
+    # 8 KV heads: divides over 2, 4 and 8 tensor-parallel ranks (per-rank FFN 384 = 3 x 128 at 8 ranks)
+    "small-fp8-kv8": ModelConfig(name="small-fp8-kv8", num_layers=2, hidden=1024, num_heads=16, num_kv_heads=8,
+                                 head_dim=128, ffn=3072, vocab=8192, rope_theta=5e5, quant="fp8_block"),
     "small-bf16": ModelConfig(name="small-bf16", num_layers=2, hidden=1024, num_heads=8, num_kv_heads=2,
                               head_dim=128, ffn=3072, vocab=8192, rope_theta=5e5),
     "small-moe-fp8": ModelConfig(name="small-moe-fp8", arch="mixtral", num_layers=2, hidden=1024, num_heads=8,

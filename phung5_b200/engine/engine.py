@@ -509,6 +509,7 @@ class LLMEngine:
         """Host-side phase timer (PHX_HOST_TIMING=1): accumulates host wall time between marks per phase;
         with the device running asynchronously this is the time the host spends enqueuing each phase
         (the final commit phase includes waiting for the device)."""
+        ops.set_phase(name)
         if _nvtx.ON:
             if self._nvtx_open:
                 _nvtx.pop()

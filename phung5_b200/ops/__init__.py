@@ -44,7 +44,66 @@ def ext():
     _LAUNCHES[0] += 1
     if _C is None:
         raise RuntimeError(f"phung5_b200._C is not built (python setup.py build_ext --inplace): {_C_ERR}")
-    return _C
+    return _TIMED if OP_TIMING else _C
+
+
+# ------------------------------------------------------------------------------------------------
+# Per-kernel-class device timing (PHX_OP_TIMING=1, eager steps only: a graph replay issues no ext() call).
+# Every native launch is bracketed by two CUDA events on the launching stream and filed under
+# (phase, binding name); `set_phase` marks engine phase boundaries with an event as well, so a phase's
+# device time minus its native kernels' time is the time of torch glue kernels and idle gaps.
+# ------------------------------------------------------------------------------------------------
+
+OP_TIMING = os.environ.get("PHX_OP_TIMING", "0") == "1"
+_TIMING_LOG: list = []          # (phase, name, start event, end event)
+_PHASE_LOG: list = []           # (phase, event at its start)
+_PHASE = ["-"]
+
+
+class _TimedExt:
+    def __getattr__(self, name):
+        fn = getattr(_C, name)
+
+        def call(*args, **kw):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            r = fn(*args, **kw)
+            b.record()
+            _TIMING_LOG.append((_PHASE[0], name, a, b))
+            return r
+        return call
+
+
+_TIMED = _TimedExt()
+
+
+def set_phase(name: str) -> None:
+    if not OP_TIMING or not torch.cuda.is_available():
+        return
+    _PHASE[0] = name
+    e = torch.cuda.Event(enable_timing=True)
+    e.record()
+    _PHASE_LOG.append((name, e))
+
+
+def timing_reset() -> None:
+    _TIMING_LOG.clear()
+    _PHASE_LOG.clear()
+
+
+def timing_report() -> dict:
+    """{"kernels": {"phase/name": [ms, launches]}, "phases": {phase: ms}} since the last reset (synchronizes)."""
+    torch.cuda.synchronize()
+    kern: dict = {}
+    for ph, name, a, b in _TIMING_LOG:
+        k = f"{ph}/{name}"
+        ms, n = kern.get(k, (0.0, 0))
+        kern[k] = (ms + a.elapsed_time(b), n + 1)
+    phases: dict = {}
+    for (ph, a), (_, b) in zip(_PHASE_LOG, _PHASE_LOG[1:]):
+        phases[ph] = phases.get(ph, 0.0) + a.elapsed_time(b)
+    return {"kernels": {k: [round(v[0], 4), v[1]] for k, v in kern.items()},
+            "phases": {k: round(v, 4) for k, v in phases.items()}}
 
 
 def native_available() -> bool:
