@@ -134,6 +134,8 @@ def main():
     ap.add_argument("--comm", default="fused", choices=["nccl", "fused"])
     ap.add_argument("--no-cascade", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override layer count (smoke runs only; not a bench value)")
+    ap.add_argument("--model-path", default=None, help="HF checkpoint directory instead of random-init weights")
+    ap.add_argument("--draft-path", default=None, help="EAGLE head checkpoint directory (with --model-path)")
     args = ap.parse_args()
 
     if args.impl == "reference":
@@ -155,7 +157,14 @@ def main():
         from phung5_b200.parallel.fused import FusedCommunicator
         comm = FusedCommunicator()
 
-    mc = preset(args.model)
+    target = drafter = None
+    if args.model_path:
+        from phung5_b200.weights.loader import load_eagle, load_model
+        mc, target = load_model(args.model_path, dev, rank, world)
+        if args.draft_path:
+            drafter = load_eagle(args.draft_path, mc, dev, rank, world)
+    else:
+        mc = preset(args.model)
     if args.layers:
         mc.num_layers = args.layers
     spec = SpecConfig(mode=args.mode, tree_nodes=args.tree_nodes, topk=args.topk, depth=args.depth,
@@ -169,7 +178,8 @@ def main():
                         cache=CacheConfig(page_size=64, num_pages=num_pages, enable_cascade=not args.no_cascade),
                         max_prefill_tokens=8192, seed=0)
     t0 = time.time()
-    eng = LLMEngine(ecfg, device=dev, comm=comm, max_context=args.prefix + args.suffix + args.out_tokens + 512)
+    eng = LLMEngine(ecfg, device=dev, comm=comm, target=target, drafter=drafter,
+                    max_context=args.prefix + args.suffix + args.out_tokens + 512)
     torch.cuda.synchronize()
     t_init = time.time() - t0
 
@@ -246,7 +256,8 @@ def main():
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp8_block+bf16",
-            "data": "synthetic token ids, random-init weights, geometric(p=0.3, cap 6) synthetic acceptance",
+            "data": "synthetic token ids, " + ("checkpoint weights" if args.model_path else "random-init weights")
+                    + ", geometric(p=0.3, cap 6) synthetic acceptance",
             "config": {"model": mc.name + (f"-{mc.num_layers}L" if args.layers else ""), "global_batch": args.batch,
                        "seq_len": args.prefix + args.suffix, "shared_prefix": args.prefix, "suffix": args.suffix,
                        "out_tokens": args.out_tokens, "spec": args.mode,

@@ -61,6 +61,12 @@ void causal_conv1d(torch::Tensor x, torch::Tensor window, torch::Tensor w, c10::
 void gated_rmsnorm(torch::Tensor o, torch::Tensor z, torch::Tensor w, double eps, torch::Tensor y);
 torch::Tensor raster(torch::Tensor tris, torch::Tensor cols, torch::Tensor vp, int64_t W, int64_t H,
                      std::vector<double> light, double ambient, double diffuse, double exposure, std::vector<double> bg);
+void sample_candidates(torch::Tensor logits, int64_t kc, c10::optional<torch::Tensor> temp, int64_t rows_per_temp,
+                       int64_t vocab_offset, torch::Tensor cv, torch::Tensor ci, c10::optional<torch::Tensor> cms);
+int64_t sample_chunks(int64_t vocab);
+void spec_accept(torch::Tensor cv, torch::Tensor ci, int64_t ranks, int64_t nch, int64_t kc, torch::Tensor tokens,
+                 torch::Tensor parent, torch::Tensor temp, torch::Tensor top_k, torch::Tensor top_p,
+                 torch::Tensor seed, torch::Tensor committed, int64_t D, torch::Tensor acc, torch::Tensor bonus);
 }  // namespace phx
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -87,4 +93,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("causal_conv1d", &phx::causal_conv1d);
   m.def("gated_rmsnorm", &phx::gated_rmsnorm);
   m.def("raster", &phx::raster);
+  m.def("sample_candidates", &phx::sample_candidates);
+  m.def("sample_chunks", &phx::sample_chunks);
+  m.def("spec_accept", &phx::spec_accept);
 }

@@ -36,7 +36,7 @@ from .attn_meta import PageTables, build_items, cascade_groups, make_meta, pack_
 from .kv_pool import KVPool
 from .oracle import SamplingParams
 from ..utils import nvtx as _nvtx
-from .sampling import geometric_accept_len, sample_from, seeded_coins, target_probs
+from .sampling import geometric_accept_len, sample_from, seeded_coins, target_probs, tree_accept_reference
 
 
 @dataclass
@@ -538,7 +538,7 @@ class LLMEngine:
         logits, root_feat = self._catchup(reqs, tables, groups)
         mode, ngeo_h = self._accept_mode(reqs)
 
-        graph = self._spec_graph(R, mode)
+        graph = self._spec_graph(R, mode, reqs)
         if graph is not None:
             self._mark("graph_replay")
             packed_dev = graph.run(reqs, tables, groups, c_h, logits, root_feat, ngeo_h)
@@ -606,23 +606,29 @@ class LLMEngine:
             return "greedy", None
         return "sample", None
 
-    def _spec_graph(self, R: int, mode: str):
-        """The CUDA-graph runner for this batch shape, or None to run the step eagerly."""
-        if (self._graphs is None or mode == "sample" or self.K <= 1 or not self.eagle or self._has_moe or self.hybrid
-                or (self.comm.size != 1 and not getattr(self.comm, "fused", False))):
+    def _spec_graph(self, R: int, mode: str, reqs: List[Request]):
+        """The CUDA-graph runner for this batch shape and accept mode, or None to run the step eagerly. Seeded
+        sampling is captured when the device accept path serves every request."""
+        if (self._graphs is None or self.K <= 1 or not self.eagle or self._has_moe or self.hybrid
+                or (self.comm.size != 1 and not getattr(self.comm, "fused", False))
+                or (mode == "sample" and not self._device_sampling(reqs))):
             return None
-        g = self._graphs.get(R)
+        kc = ops.sample_kc([r.params.top_k for r in reqs], [r.params.temperature for r in reqs]) \
+            if mode == "sample" else 0
+        key = (R, mode, kc)
+        g = self._graphs.get(key)
         if g is None:
             from .spec_graph import SpecGraph
             if len(self._graphs) >= self._graph_cache:
                 self._graphs.pop(next(iter(self._graphs)))
-            g = SpecGraph(self, R)
-            self._graphs[R] = g
+            g = SpecGraph(self, R, mode, kc)
+            self._graphs[key] = g
         return g
 
-    def _spec_core(self, mp, pt, c, roots, logits, root_feat, mode, ngeo, reqs=None):
+    def _spec_core(self, mp, pt, c, roots, logits, root_feat, mode, ngeo, reqs=None, sp=None):
         """Tree expansion, selection, verification, acceptance and the KV move of one speculative step, on
-        device tensors only (no host synchronisation unless mode == "sample"). `mp` supplies the attention
+        device tensors only (no host synchronisation unless mode == "sample" takes the dense torch definition).
+        `sp`: sampling tensors (mode "sample"; None: uploaded from reqs). `mp` supplies the attention
         metadata and work lists of the draft rounds and of verification. Returns packed [R, 2 + D] int64:
         accepted count, accepted tokens (-1 padded), bonus token."""
         dev = self.device
@@ -726,7 +732,7 @@ class LLMEngine:
         # ---- accept ----
         vl = vlogits.reshape(R, N, -1)
         if mode == "sample":
-            acc_nodes, bonus = self._accept_sample(reqs, vl, tokens, parent)
+            acc_nodes, bonus = self._accept_sample(reqs, vl, tokens, parent, c, sp)
         else:
             acc_nodes, bonus = self._accept_static(vl, tokens, parent, ngeo)
 
@@ -774,49 +780,35 @@ class LLMEngine:
             alive &= has
         return acc, tgt.gather(1, cur[:, None])[:, 0]
 
-    def _accept_sample(self, reqs, logits, tokens, parent):
-        """Seeded target-only tree sampling (per-request temperature / top-k / top-p). Returns (accepted
-        node ids [R, D] (-1 = none), bonus tokens [R])."""
+    def sample_tensors(self, reqs: List[Request]):
+        """Per-request sampling parameters as device tensors: (temperature fp32, top_k int32, top_p fp32, seed
+        int64, candidates per chunk) for the device accept path."""
         dev = self.device
-        R, N, D = len(reqs), self.N, self.D
-        cur = torch.zeros(R, dtype=torch.int64, device=dev)
-        acc = torch.full((R, D), -1, dtype=torch.int64, device=dev)
-        nidx = torch.arange(N, device=dev)[None, :]
-        # seeded target-only tree sampling (per-request temperature / top-k / top-p)
-        temp = upload([r.params.temperature for r in reqs], torch.float32, dev)
-        topk = upload([r.params.top_k for r in reqs], torch.int64, dev)
-        topp = upload([r.params.top_p for r in reqs], torch.float32, dev)
-        coins = upload(seeded_coins(torch.tensor([r.params.seed for r in reqs]),
-                                    torch.tensor([r.committed for r in reqs]), D + 2), torch.float32, dev)
-        rows = torch.arange(R, device=dev)
-        bonus = torch.zeros(R, dtype=torch.int64, device=dev)
-        done = torch.zeros(R, dtype=torch.bool, device=dev)
-        for d in range(1, D + 2):
-            lg = self.vocab.full(logits[rows, cur])
-            p = target_probs(lg, temp, topk, topp)                        # [R, V]
-            kids = (parent == cur[:, None]) & ~done[:, None] & (d <= D)
-            kp = torch.where(kids, p.gather(1, tokens.clamp(min=0)), torch.zeros_like(p[:, :N]))
-            cum = torch.cumsum(kp, 1)
-            u = coins[:, d - 1]
-            hit = kids & (u[:, None] < cum)
-            has = hit.any(1) & ~done
-            first = torch.where(hit, nidx.expand(R, N), torch.full_like(tokens, N)).min(1).values
-            # rows that stop here draw the bonus from p minus the children's tokens
-            stop = ~has & ~done
-            if stop.any():
-                hitcnt = torch.zeros(p.shape, dtype=torch.int32, device=dev).scatter_add_(
-                    1, tokens.clamp(min=0), kids.to(torch.int32))
-                q = p.masked_fill(hitcnt > 0, 0.0)
-                empty = q.sum(1) <= 0
-                q = torch.where(empty[:, None], p, q)
-                samp = sample_from(q, coins[:, D + 1])
-                greedy_rows = temp <= 0
-                samp = torch.where(greedy_rows, p.argmax(1), samp)
-                bonus = torch.where(stop, samp, bonus)
-            if d <= D:
-                acc[:, d - 1] = torch.where(has, first, torch.full_like(first, -1))
-                cur = torch.where(has, first, cur)
-            done |= stop
-            if bool(done.all()):
-                break
-        return acc, bonus
+        temps = [r.params.temperature for r in reqs]
+        ks = [r.params.top_k for r in reqs]
+        return (upload(temps, torch.float32, dev), upload(ks, torch.int32, dev),
+                upload([r.params.top_p for r in reqs], torch.float32, dev),
+                upload([r.params.seed & 0xFFFFFFFF for r in reqs], torch.int64, dev), ops.sample_kc(ks, temps))
+
+    def _device_sampling(self, reqs: List[Request]) -> bool:
+        return self.device.type == "cuda" and ops.device_sampling_ok([r.params.top_k for r in reqs],
+                                                                      [r.params.temperature for r in reqs])
+
+    def _accept_sample(self, reqs, logits, tokens, parent, c, sp=None):
+        """Seeded target-only tree sampling (per-request temperature / top-k / top-p). On the GPU, for greedy
+        rows and 1 <= top_k <= 64, one candidate kernel per vocab shard plus one accept kernel (csrc/sample.cu),
+        no host synchronisation (used inside the step's CUDA graph, where `sp` holds static buffers); otherwise
+        the dense torch definition (engine/sampling.py). Returns (accepted node ids [R, D] (-1 = none), bonus
+        tokens [R])."""
+        R, N, D = tokens.shape[0], self.N, self.D
+        if sp is None:
+            sp = self.sample_tensors(reqs)
+        temp, topk, topp, seed, kc = sp
+        if reqs is None or self._device_sampling(reqs):
+            gather = None if self.comm.size == 1 else self.comm.gather
+            return ops.spec_sample_accept(logits.reshape(R * N, -1), tokens, parent, temp, topk, topp, seed, c, D, kc,
+                                          self.vocab.v0, gather)
+        coins = seeded_coins(seed, c, D + 2)
+        rows = torch.arange(R, device=self.device)
+        return tree_accept_reference(lambda cur: self.vocab.full(logits[rows, cur]), tokens, parent, temp,
+                                     topk.long(), topp, coins, D)

@@ -76,7 +76,8 @@ def target_probs(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.T
     x = x / t[:, None]
     v = x.shape[-1]
     k = torch.where(top_k <= 0, torch.full_like(top_k, v), top_k).clamp(max=v)
-    sv, si = torch.sort(x, dim=-1, descending=True)
+    # stable: equal values keep vocab order, so the top-k cut and the nucleus break ties toward the lower index
+    sv, si = torch.sort(x, dim=-1, descending=True, stable=True)
     pos = torch.arange(v, device=x.device)[None, :]
     keep = pos < k[:, None]
     sv = sv.masked_fill(~keep, float("-inf"))
@@ -91,6 +92,52 @@ def target_probs(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.T
         onehot = torch.zeros_like(x).scatter_(-1, logits.float().argmax(-1, keepdim=True), 1.0)
         probs = torch.where(greedy[:, None], onehot, probs)
     return probs
+
+
+def tree_accept_reference(logits, tokens: torch.Tensor, parent: torch.Tensor, temp: torch.Tensor, top_k: torch.Tensor,
+                          top_p: torch.Tensor, coins: torch.Tensor, depth: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Seeded target-only tree sampling for a batch (the definition the device path implements).
+
+    logits: callable(rows [R] node ids) -> full-vocab logits [R, V] of each request's node (so a
+    vocab-sharded caller can gather only the visited rows), or a tensor [R, N, V]. tokens/parent [R, N]
+    (parent -1 for the root), per-request temp/top_k/top_p [R], coins [R, depth + 2] (column d-1 for depth d,
+    column depth+1 for the bonus draw). Returns (accepted node ids [R, depth], -1 padded; bonus tokens [R])."""
+    R, N = tokens.shape
+    D = depth
+    dev = tokens.device
+    get = logits if callable(logits) else (lambda cur: logits[torch.arange(R, device=dev), cur])
+    cur = torch.zeros(R, dtype=torch.int64, device=dev)
+    acc = torch.full((R, D), -1, dtype=torch.int64, device=dev)
+    nidx = torch.arange(N, device=dev)[None, :]
+    bonus = torch.zeros(R, dtype=torch.int64, device=dev)
+    done = torch.zeros(R, dtype=torch.bool, device=dev)
+    for d in range(1, D + 2):
+        p = target_probs(get(cur), temp, top_k, top_p)                       # [R, V]
+        kids = (parent == cur[:, None]) & ~done[:, None] & (d <= D)
+        kp = torch.where(kids, p.gather(1, tokens.clamp(min=0)), torch.zeros_like(p[:, :N]))
+        cum = torch.cumsum(kp, 1)
+        u = coins[:, d - 1]
+        hit = kids & (u[:, None] < cum)
+        has = hit.any(1) & ~done
+        first = torch.where(hit, nidx.expand(R, N), torch.full_like(tokens, N)).min(1).values
+        # rows that stop here draw the bonus from p minus the children's tokens
+        stop = ~has & ~done
+        if stop.any():
+            hitcnt = torch.zeros(p.shape, dtype=torch.int32, device=dev).scatter_add_(
+                1, tokens.clamp(min=0), kids.to(torch.int32))
+            q = p.masked_fill(hitcnt > 0, 0.0)
+            empty = q.sum(1) <= 0
+            q = torch.where(empty[:, None], p, q)
+            samp = sample_from(q, coins[:, D + 1])
+            samp = torch.where(temp <= 0, p.argmax(1), samp)
+            bonus = torch.where(stop, samp, bonus)
+        if d <= D:
+            acc[:, d - 1] = torch.where(has, first, torch.full_like(first, -1))
+            cur = torch.where(has, first, cur)
+        done |= stop
+        if bool(done.all()):
+            break
+    return acc, bonus
 
 
 def sample_from(probs: torch.Tensor, coin: torch.Tensor) -> torch.Tensor:

@@ -17,8 +17,10 @@ prefix c+1 and kv_hi = c+1+d*K, verification prefix c and kv_hi = c+N; the main-
 item per request with a fixed number of tiles. The catch-up forward (variable length: 1 + accepted tokens
 per request) runs eagerly and hands its root logits and features to the graph through static buffers.
 
-Used for greedy and synthetic (geometric) acceptance on dense models at TP1; seeded sampling, MoE
-(data-dependent routing) and tensor parallelism run the same `_spec_core` eagerly.
+Used for greedy, synthetic (geometric) and seeded-sampling acceptance on dense models, at TP1 and on the
+fused tensor-parallel communicator (the sampled graph needs every request on the device accept path: greedy or
+1 <= top_k <= 64; its per-request temperature, top_k, top_p and seed are static buffers filled per step). MoE
+(data-dependent routing), hybrid GDN models and the NCCL communicator run the same `_spec_core` eagerly.
 """
 from __future__ import annotations
 
@@ -75,8 +77,9 @@ class _StaticMeta:
 
 
 class SpecGraph:
-    def __init__(self, eng, R: int):
+    def __init__(self, eng, R: int, mode: str = "greedy", kc: int = 0):
         self.eng, self.R = eng, R
+        self.mode, self.kc = mode, kc
         dev = eng.device
         ps = eng.ps
         self.P = math.ceil((eng.max_context + 2 * ps) / ps) + 1
@@ -85,7 +88,8 @@ class SpecGraph:
         self.G = max(1, R // 2)                                       # groups have >= 2 requests
         self.T1 = {n: math.ceil(R * n * g / rows) + self.G + 1 for n in (eng.K, eng.N)}
         # packed int32 inputs: pt | c | roots | ngeo | shared | (items1, ti1, tr1) for K then N
-        sizes = [("pt", R * self.P), ("c", R), ("roots", R), ("ngeo", R), ("shared", R)]
+        sizes = [("pt", R * self.P), ("c", R), ("roots", R), ("ngeo", R), ("shared", R),
+                 ("temp", R), ("topk", R), ("topp", R), ("seed", R)]      # temp / topp hold fp32 bits
         for n in (eng.K, eng.N):
             sizes += [(f"items1_{n}", 6 * self.G), (f"ti1_{n}", self.T1[n]), (f"tr1_{n}", self.T1[n])]
         self.layout, off = {}, 0
@@ -121,6 +125,13 @@ class SpecGraph:
                            ("ngeo", ngeo_h.tolist() if ngeo_h is not None else [0] * R)):
             o, n = self.layout[name]
             h[o:o + n] = vals
+        if self.mode == "sample":
+            for name, vals, dt in (("temp", [r.params.temperature for r in reqs], np.float32),
+                                   ("topk", [r.params.top_k for r in reqs], np.int32),
+                                   ("topp", [r.params.top_p for r in reqs], np.float32),
+                                   ("seed", [r.params.seed & 0xFFFFFFFF for r in reqs], np.uint32)):
+                o, n = self.layout[name]
+                h[o:o + n] = np.asarray(vals, dtype=dt).view(np.int32)
         shared = [0] * R
         for a, b, L in (groups or []):
             for r in range(a, b + 1):
@@ -159,9 +170,13 @@ class SpecGraph:
         pt = self._view("pt", (R, P)).long()
         c = self._view("c").long()
         roots = self._view("roots").long()
-        mode = "geometric" if eng.cfg.spec.accept == "geometric" else "greedy"
+        mode = self.mode
         ngeo = self._view("ngeo").long() if mode == "geometric" else None
-        return eng._spec_core(mp, pt, c, roots, self.logits, self.feat, mode, ngeo)
+        sp = None
+        if mode == "sample":
+            sp = (self._view("temp").view(torch.float32), self._view("topk"), self._view("topp").view(torch.float32),
+                  self._view("seed").long() & 0xFFFFFFFF, self.kc)
+        return eng._spec_core(mp, pt, c, roots, self.logits, self.feat, mode, ngeo, sp=sp)
 
     def _capture(self) -> None:
         eng = self.eng

@@ -261,6 +261,50 @@ def topk_logprobs(logits: torch.Tensor, k: int, temperature: float = 1.0, vocab_
     return v - lse[:, None], i + vocab_offset, lse
 
 
+SAMPLE_MAX_TOPK = 64
+# PHX_DEVICE_SAMPLING=0 sends every sampled request to the dense torch definition (engine/sampling.py)
+DEVICE_SAMPLING = os.environ.get("PHX_DEVICE_SAMPLING", "1") != "0"
+
+
+def sample_kc(top_ks, temps) -> int:
+    """Candidates per vocab chunk for the device sampling path: 16 if every sampled request keeps at most 16
+    tokens, else 64 (greedy rows need 1)."""
+    ks = [k for k, t in zip(top_ks, temps) if t > 0]
+    return 16 if all(1 <= k <= 16 for k in ks) else 64
+
+
+def device_sampling_ok(top_ks, temps) -> bool:
+    """The device path serves greedy rows and rows with 1 <= top_k <= 64 (no host synchronisation); other rows
+    (no top-k cut, or a larger one) take the dense torch definition."""
+    return DEVICE_SAMPLING and all(t <= 0 or 1 <= k <= SAMPLE_MAX_TOPK for k, t in zip(top_ks, temps))
+
+
+def spec_sample_accept(logits: torch.Tensor, tokens: torch.Tensor, parent: torch.Tensor, temp: torch.Tensor,
+                       top_k: torch.Tensor, top_p: torch.Tensor, seed: torch.Tensor, committed: torch.Tensor,
+                       depth: int, kc: int, vocab_offset: int = 0, gather=None):
+    """Seeded target-only tree acceptance on the device (csrc/sample.cu). logits [R*N, V_local] bf16 verify rows
+    of this rank's vocab shard (request r's node j at row r*N + j), tokens/parent [R, N] int64, per-request
+    temp/top_p fp32, top_k int32, seed/committed int64. `gather(parts)` exchanges the shard candidates across
+    tensor-parallel ranks ([W, ...] per part); None on one GPU. Returns (accepted node ids [R, D] int64, -1
+    padded; bonus tokens [R] int64) -- the definition of engine.sampling.tree_accept_reference restricted to
+    greedy rows and 1 <= top_k <= kc."""
+    R, N = tokens.shape
+    rows, vl = logits.shape
+    nch = int(ext().sample_chunks(vl))
+    cv = torch.empty(rows, nch, kc, dtype=torch.float32, device=logits.device)
+    ci = torch.empty(rows, nch, kc, dtype=torch.int32, device=logits.device)
+    ext().sample_candidates(logits, kc, temp, N, vocab_offset, cv, ci, None)
+    ranks = 1
+    if gather is not None:
+        cv, ci = gather([cv, ci])
+        ranks = cv.shape[0]
+    acc = torch.empty(R, depth, dtype=torch.int64, device=logits.device)
+    bonus = torch.empty(R, dtype=torch.int64, device=logits.device)
+    ext().spec_accept(cv, ci, ranks, nch, kc, tokens.contiguous(), parent.contiguous(), temp, top_k, top_p, seed,
+                      committed, depth, acc, bonus)
+    return acc, bonus
+
+
 # ------------------------------------------------------------------------------------------------
 # norms / activations / quant
 # ------------------------------------------------------------------------------------------------

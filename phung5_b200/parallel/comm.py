@@ -58,6 +58,10 @@ class NcclCommunicator(Communicator):
         dist.all_gather_into_tensor(flat, x, group=self.group)
         return flat.view((self.size,) + tuple(x.shape))
 
+    def gather(self, parts):
+        """All-gather of several tensors: -> [[world, *p.shape] for p in parts]."""
+        return [self._gather(p) for p in parts]
+
     def all_gather_vocab(self, x: torch.Tensor) -> torch.Tensor:
         g = self._gather(x)                       # [tp, rows, V/tp]
         return g.permute(1, 0, 2).reshape(x.shape[0], -1)

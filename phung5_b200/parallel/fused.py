@@ -32,7 +32,7 @@ from .. import ops
 from .comm import NcclCommunicator
 
 
-GATHER_BYTES = 1 << 20
+GATHER_BYTES = 4 << 20   # verify-row sampling candidates: 4096 rows x 64 x (value, index) = 2 MB
 
 
 class _Workspace:

@@ -286,6 +286,9 @@ def main(argv=None):
     ap.add_argument("--device", default="cuda")
     ap.add_argument("--spec", default="tree", choices=["off", "chain", "tree"])
     ap.add_argument("--tokenizer", default=None)
+    ap.add_argument("--model-path", default=None,
+                    help="HF checkpoint directory (config.json + safetensors); overrides --model's random weights")
+    ap.add_argument("--draft-path", default=None, help="EAGLE head checkpoint directory (else a random head)")
     ap.add_argument("--num-pages", type=int, default=0)
     ap.add_argument("--comm", default="fused", choices=["nccl", "fused"],
                     help="tensor-parallel collectives when launched with torchrun over several GPUs")
@@ -308,15 +311,24 @@ def main(argv=None):
             comm = FusedCommunicator()
         group = dist.new_group(backend="gloo")
     spec = SpecConfig(enabled=args.spec != "off", mode=args.spec if args.spec != "off" else "chain")
-    cfg = EngineConfig(model=preset(args.model), spec=spec, draft=DraftConfig(kind="eagle"),
+    target = drafter = None
+    model_cfg = preset(args.model) if args.model_path is None else None
+    if args.model_path is not None:
+        from ..weights.loader import load_eagle, load_model
+        rank_ = comm.rank if comm is not None else 0
+        model_cfg, target = load_model(args.model_path, device, rank_, world)
+        if args.draft_path is not None:
+            drafter = load_eagle(args.draft_path, model_cfg, device, rank_, world)
+    cfg = EngineConfig(model=model_cfg, spec=spec, draft=DraftConfig(kind="eagle"),
                        cache=CacheConfig(num_pages=args.num_pages), parallel=ParallelConfig(tp=world, comm=args.comm))
-    eng = LLMEngine(cfg, device=device, comm=comm)
+    eng = LLMEngine(cfg, device=device, comm=comm, target=target, drafter=drafter)
     if group is not None and comm.rank != 0:
         tp_worker_loop(eng, group)
         return
     aeng = AsyncEngine(eng, group=group)
     uvicorn.run(build_app(aeng, __import__("phung5_b200.serve.tokenizer", fromlist=["load_tokenizer"]).load_tokenizer(
-        args.tokenizer), args.model), host=args.host, port=args.port, log_level="warning")
+        args.tokenizer), model_cfg.name if args.model_path else args.model), host=args.host, port=args.port,
+        log_level="warning")
     aeng.shutdown()
 
 
