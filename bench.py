@@ -262,7 +262,8 @@ def main():
                        "seq_len": args.prefix + args.suffix, "shared_prefix": args.prefix, "suffix": args.suffix,
                        "out_tokens": args.out_tokens, "spec": args.mode,
                        "tree_nodes": args.tree_nodes if args.mode == "tree" else args.num_draft + 1,
-                       "topk": args.topk, "depth": args.depth if args.mode == "tree" else args.num_draft, "parallelism": f"tp{world}", "comm": args.comm if world > 1 else "none",
+                       "topk": args.topk, "depth": args.depth if args.mode == "tree" else args.num_draft, "parallelism": f"tp{world}",
+                       "comm": (args.comm + ("+nvls" if getattr(comm, "mc", 0) else "")) if world > 1 else "none",
                        "cascade": not args.no_cascade, "l2": "inputs larger than L2 (weights stream every step)"},
             "p50_tpot_ms": round(statistics.median(tpot), 3) if tpot else None,
             "tokens_per_step": round(tokens / args.steps, 2),
@@ -278,6 +279,10 @@ def main():
         print(json.dumps(line))
     if comm is not None:
         import torch.distributed as dist
+        eng._graphs = None          # release the step graphs (they hold the fused kernels) before teardown
+        del eng
+        if hasattr(comm, "close"):
+            comm.close()
         dist.barrier()
         dist.destroy_process_group()
 

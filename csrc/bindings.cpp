@@ -39,7 +39,7 @@ void gemm_bf16_grouped(torch::Tensor x, torch::Tensor w, torch::Tensor offsets, 
                        torch::Tensor status);
 void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M, int64_t H, double eps,
                 torch::Tensor w, bool out_bf16, bool push_h, torch::Tensor status, std::vector<int64_t> offsets,
-                int64_t s_ld, int64_t off_recv);
+                int64_t s_ld, int64_t off_recv, int64_t mc_base);
 void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tensor w, c10::optional<torch::Tensor> ws,
                   torch::Tensor peer_base, int64_t off_recv, int64_t rows_per, int64_t rank, torch::Tensor status,
                   bool hws, bool pair);
@@ -47,7 +47,7 @@ void gemm_fp8_swiglu(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch
                      torch::Tensor qs, torch::Tensor status);
 void moe_combine(torch::Tensor y, torch::Tensor pos, torch::Tensor w, torch::Tensor local, torch::Tensor out);
 void tp_allgather(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t nbytes, torch::Tensor status,
-                  std::vector<int64_t> offsets);
+                  std::vector<int64_t> offsets, int64_t mc_base);
 void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
                    torch::Tensor state, torch::Tensor tok_start, torch::Tensor slot, double scale, torch::Tensor out,
                    bool write_state, c10::optional<torch::Tensor> st_k, c10::optional<torch::Tensor> st_v,
@@ -62,7 +62,8 @@ void gated_rmsnorm(torch::Tensor o, torch::Tensor z, torch::Tensor w, double eps
 torch::Tensor raster(torch::Tensor tris, torch::Tensor cols, torch::Tensor vp, int64_t W, int64_t H,
                      std::vector<double> light, double ambient, double diffuse, double exposure, std::vector<double> bg);
 void sample_candidates(torch::Tensor logits, int64_t kc, c10::optional<torch::Tensor> temp, int64_t rows_per_temp,
-                       int64_t vocab_offset, torch::Tensor cv, torch::Tensor ci, c10::optional<torch::Tensor> cms);
+                       int64_t vocab_offset, torch::Tensor cv, torch::Tensor ci, c10::optional<torch::Tensor> cms,
+                       torch::Tensor status);
 int64_t sample_chunks(int64_t vocab);
 void spec_accept(torch::Tensor cv, torch::Tensor ci, int64_t ranks, int64_t nch, int64_t kc, torch::Tensor tokens,
                  torch::Tensor parent, torch::Tensor temp, torch::Tensor top_k, torch::Tensor top_p,

@@ -28,6 +28,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <algorithm>
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace phx {
@@ -77,11 +80,14 @@ __device__ __forceinline__ void find_crossing(const uint32_t* hist, uint32_t nee
   }
 }
 
+// Exact fallback for the chunks where the fast kernel's candidate set overflowed (heavy ties at the
+// threshold): the chunk is staged in shared memory and radix-selected. Only CTAs whose overflow flag is set
+// do any work.
 template <int KC, bool LSE>
-__global__ void __launch_bounds__(kCandThreads) sample_candidates_kernel(
+__global__ void __launch_bounds__(kCandThreads) sample_candidates_exact_kernel(
     const __nv_bfloat16* __restrict__ logits, int V, int ld, int nchunks, int vocab_offset,
     const float* __restrict__ temp, int rows_per_temp, float* __restrict__ cv, int* __restrict__ ci,
-    float* __restrict__ cms) {
+    float* __restrict__ cms, const int* __restrict__ overflow, int items) {
   __shared__ __align__(16) uint16_t keys[kCandChunk];
   __shared__ uint32_t hist[256];
   __shared__ uint32_t wcnt[kCandThreads / 32];
@@ -89,7 +95,10 @@ __global__ void __launch_bounds__(kCandThreads) sample_candidates_kernel(
   __shared__ uint32_t s_above, s_gt;
   __shared__ float red[kCandThreads / 32];
 
-  const int row = blockIdx.x, chunk = blockIdx.y;
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+  if (!overflow[item]) continue;
+  __syncthreads();   // the previous item's shared-memory readers are done
+  const int row = item / nchunks, chunk = item % nchunks;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int c0 = chunk * kCandChunk;
   const int n = min(kCandChunk, V - c0);
@@ -216,6 +225,259 @@ __global__ void __launch_bounds__(kCandThreads) sample_candidates_kernel(
       cms[((size_t)row * nchunks + chunk) * 2 + 1] = tot;
     }
   }
+}  // items
+}
+
+// Fast path. Each thread holds 32 keys of the chunk in registers (four 16-byte loads). The KC-th largest of
+// the 512 per-thread maxima, tau, is a lower bound of the chunk's KC-th largest key (those KC maxima are KC
+// distinct elements), so every top-KC element has key >= tau, and for realistic logits only a few hundred
+// elements do. They are compacted into shared memory as 64-bit (key, ~index) words -- descending order of
+// the word is value descending, index ascending -- and sorted there (bitonic). More than kCandCap of them
+// (heavy ties at tau) sets the chunk's overflow flag and leaves it to the exact kernel.
+constexpr int kCandCap = 2048;
+
+// in-place bitonic sort, descending, of n (a power of two) 64-bit words in shared memory; all threads call it
+__device__ __forceinline__ void bitonic_desc_u64(uint64_t* v, int n) {
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        const int o = j ^ stride;
+        if (o > j) {
+          const uint64_t x = v[j], y = v[o];
+          const bool desc = (j & size) == 0;
+          if (desc ? (y > x) : (x > y)) {
+            v[j] = y;
+            v[o] = x;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Shared memory of the fast path: two 32 KB chunk buffers (the next chunk is fetched by a bulk copy while
+// the current one is processed), the candidate words and small scratch.
+struct CandSmem {
+  uint16_t buf[2][kCandChunk];
+  uint64_t cand[kCandCap];
+  uint32_t hist[256];
+  float red[kCandThreads / 32];
+  uint64_t full[2];
+  int bin;
+  uint32_t above, cnt;
+};
+
+// One chunk (n columns at src: global or shared memory, 16-byte aligned when vec) -> its KC candidates.
+template <int KC, bool LSE>
+__device__ __forceinline__ void cand_chunk(CandSmem& sm, const uint16_t* src, int n, bool vec, float T, int gcol0,
+                                           float* cvp, int* cip, float* cmsp, int* ovf) {
+  constexpr int PER = kCandChunk / kCandThreads;   // 32 keys per thread
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t kp[PER / 2];
+#pragma unroll
+  for (int j = 0; j < PER / 8; ++j) {
+    const int v = tid + j * kCandThreads;
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if (vec) {
+      if (v * 8 < n) {
+        const uint4 q = reinterpret_cast<const uint4*>(src)[v];
+        w[0] = q.x, w[1] = q.y, w[2] = q.z, w[3] = q.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (v * 8 + e < n) w[e / 2] |= (uint32_t)src[v * 8 + e] << (16 * (e & 1));
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int el = v * 8 + 2 * e;
+      const uint32_t lo = el < n ? bf16_key(w[e] & 0xffffu) : 0u;   // key 0 marks padding
+      const uint32_t hi = el + 1 < n ? bf16_key(w[e] >> 16) : 0u;
+      kp[j * 4 + e] = lo | (hi << 16);
+    }
+  }
+  uint32_t tmax = 0;
+#pragma unroll
+  for (int j = 0; j < PER / 2; ++j) tmax = max(tmax, max(kp[j] & 0xffffu, kp[j] >> 16));
+
+  // ---- tau = KC-th largest per-thread maximum (radix select over 512 values) ----
+  for (int i = tid; i < 256; i += kCandThreads) sm.hist[i] = 0;
+  if (tid == 0) sm.cnt = 0;
+  __syncthreads();
+  const uint32_t need = (uint32_t)min(KC, kCandThreads);
+  {
+    const uint32_t b = tmax >> 8;
+    const unsigned peers = __match_any_sync(0xffffffffu, b);
+    if (lane == __ffs(peers) - 1) atomicAdd(&sm.hist[b], (uint32_t)__popc(peers));
+  }
+  __syncthreads();
+  if (warp == 0) find_crossing(sm.hist, need, &sm.bin, &sm.above);
+  __syncthreads();
+  const uint32_t hi_bin = (uint32_t)sm.bin, above_hi = sm.above;
+  __syncthreads();
+  for (int i = tid; i < 256; i += kCandThreads) sm.hist[i] = 0;
+  __syncthreads();
+  {
+    const bool in = (tmax >> 8) == hi_bin;
+    const uint32_t b = in ? (tmax & 0xffu) : 0x100u + lane;
+    const unsigned peers = __match_any_sync(0xffffffffu, b);
+    if (in && lane == __ffs(peers) - 1) atomicAdd(&sm.hist[b], (uint32_t)__popc(peers));
+  }
+  __syncthreads();
+  if (warp == 0) find_crossing(sm.hist, need - above_hi, &sm.bin, &sm.above);
+  __syncthreads();
+  const uint32_t tau = max((hi_bin << 8) | (uint32_t)sm.bin, 1u);
+
+  // ---- compact the keys >= tau (warp-aggregated slots) ----
+#pragma unroll
+  for (int j = 0; j < PER / 2; ++j) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t k = h ? (kp[j] >> 16) : (kp[j] & 0xffffu);
+      const bool take = k >= tau;
+      const unsigned m = __ballot_sync(0xffffffffu, take);
+      if (m) {
+        uint32_t base = 0;
+        if (lane == __ffs(m) - 1) base = atomicAdd(&sm.cnt, (uint32_t)__popc(m));
+        base = __shfl_sync(0xffffffffu, base, __ffs(m) - 1);
+        if (take) {
+          const uint32_t slot = base + __popc(m & ((1u << lane) - 1u));
+          const int e = (tid + (j / 4) * kCandThreads) * 8 + (j % 4) * 2 + h;
+          if (slot < (uint32_t)kCandCap) sm.cand[slot] = ((uint64_t)k << 32) | (uint64_t)(0xffffffffu - (uint32_t)e);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const uint32_t cnt = sm.cnt;
+  if (tid == 0) *ovf = cnt > (uint32_t)kCandCap ? 1 : 0;
+  if (cnt > (uint32_t)kCandCap) return;     // the exact kernel takes this chunk (uniform branch)
+  auto emit = [&](int j, uint64_t w) {
+    const float x = key_value((uint32_t)(w >> 32));
+    cvp[j] = T == 1.0f ? x : __fdiv_rn(x, T);
+    cip[j] = gcol0 + (int)(0xffffffffu - (uint32_t)(w & 0xffffffffu));
+  };
+  uint32_t top = 0;   // largest key (for the LSE)
+  if (cnt <= 512) {
+    // rank selection: each candidate counts the candidates above it (distinct words, no ties)
+    for (int j = tid; j < (int)cnt; j += kCandThreads) {
+      const uint64_t w = sm.cand[j];
+      int rank = 0;
+      for (int q = 0; q < (int)cnt; ++q) rank += sm.cand[q] > w;
+      if (rank < KC) emit(rank, w);
+    }
+    if constexpr (LSE) {
+      uint32_t mk = 0;
+      for (int j = tid; j < (int)cnt; j += kCandThreads) mk = max(mk, (uint32_t)(sm.cand[j] >> 32));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mk = max(mk, __shfl_xor_sync(0xffffffffu, mk, o));
+      if (lane == 0) sm.red[warp] = __uint_as_float(mk);
+      __syncthreads();
+      for (int w = 0; w < kCandThreads / 32; ++w) top = max(top, __float_as_uint(sm.red[w]));
+      __syncthreads();
+    }
+  } else {
+    int P = 1024;
+    while (P < (int)cnt) P <<= 1;
+    for (int j = (int)cnt + tid; j < P; j += kCandThreads) sm.cand[j] = 0ull;
+    __syncthreads();
+    bitonic_desc_u64(sm.cand, P);
+    for (int j = tid; j < KC; j += kCandThreads) emit(j, sm.cand[j]);
+    top = (uint32_t)(sm.cand[0] >> 32);
+  }
+  for (int j = (int)cnt + tid; j < KC; j += kCandThreads) {   // fewer than KC columns: pad
+    cvp[j] = -INFINITY;
+    cip[j] = 0x7fffffff;
+  }
+  if constexpr (LSE) {
+    const float m0 = key_value(top);
+    const float mt = T == 1.0f ? m0 : __fdiv_rn(m0, T);
+    float ssum = 0.f;
+    if (mt != -INFINITY) {
+#pragma unroll
+      for (int j = 0; j < PER / 2; ++j) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t k = h ? (kp[j] >> 16) : (kp[j] & 0xffffu);
+          if (k) {
+            const float x = key_value(k);
+            ssum += expf((T == 1.0f ? x : __fdiv_rn(x, T)) - mt);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+    if (lane == 0) sm.red[warp] = ssum;
+    __syncthreads();
+    if (tid == 0) {
+      float tot = 0.f;
+      for (int w = 0; w < kCandThreads / 32; ++w) tot += sm.red[w];
+      cmsp[0] = mt;
+      cmsp[1] = tot;
+    }
+  }
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Persistent over (row, chunk) items. tma: rows are 16-byte aligned and chunk widths multiples of 8, so each
+// chunk is fetched into shared memory by one bulk copy issued an item ahead; else keys are read directly.
+template <int KC, bool LSE>
+__global__ void __launch_bounds__(kCandThreads, 2) sample_candidates_kernel(
+    const __nv_bfloat16* __restrict__ logits, int V, int ld, int nchunks, int items, int vocab_offset,
+    const float* __restrict__ temp, int rows_per_temp, float* __restrict__ cv, int* __restrict__ ci,
+    float* __restrict__ cms, int* __restrict__ overflow, int tma, int* status) {
+  extern __shared__ __align__(16) uint8_t cand_smem_raw[];
+  CandSmem& sm = *reinterpret_cast<CandSmem*>(cand_smem_raw);
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x;
+  auto src_of = [&](int item, int* n) {
+    const int row = item / nchunks, chunk = item % nchunks;
+    *n = min(kCandChunk, V - chunk * kCandChunk);
+    return reinterpret_cast<const uint16_t*>(logits + (size_t)row * ld + (size_t)chunk * kCandChunk);
+  };
+  auto issue = [&](int item, int b) {
+    int n;
+    const uint16_t* src = src_of(item, &n);
+    mbar_arrive_expect_tx(&sm.full[b], (uint32_t)n * 2u);
+    bulk_load(sm.buf[b], src, (uint32_t)n * 2u, &sm.full[b]);
+  };
+  if (tid == 0) {
+    abort_flag = 0;
+    mbar_init(&sm.full[0], 1);
+    mbar_init(&sm.full[1], 1);
+    fence_mbar_init();
+    if (tma && (int)blockIdx.x < items) issue(blockIdx.x, 0);
+  }
+  __syncthreads();
+  int it = 0;
+  for (int item = blockIdx.x; item < items; item += gridDim.x, ++it) {
+    const int b = it & 1;
+    if (tma && tid == 0 && item + (int)gridDim.x < items) issue(item + gridDim.x, b ^ 1);
+    int n;
+    const uint16_t* src = src_of(item, &n);
+    if (tma) {
+      if (!mbar_wait(&sm.full[b], (uint32_t)((it >> 1) & 1), status, kErrTimeoutProducer, &abort_flag)) {
+        // a copy that never lands: report and stop (the other copy of this CTA has landed or was never issued)
+        break;
+      }
+      src = sm.buf[b];
+    }
+    const int row = item / nchunks, chunk = item % nchunks;
+    float T = temp ? temp[row / rows_per_temp] : 1.0f;
+    if (!(T > 0.f)) T = 1.0f;   // greedy rows: argmax of the raw logits
+    const bool vec = tma || (n % 8 == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0);
+    cand_chunk<KC, LSE>(sm, src, n, vec, T, vocab_offset + chunk * kCandChunk, cv + (size_t)item * KC,
+                        ci + (size_t)item * KC, cms ? cms + (size_t)item * 2 : nullptr, overflow + item);
+    __syncthreads();
+  }
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -275,13 +537,22 @@ struct AcceptArgs {
   int64_t* bonus;           // [R]
 };
 
-__device__ __forceinline__ bool cand_better(float a, int ia, float b, int ib) { return a > b || (a == b && ia < ib); }
+// order-preserving 32-bit image of an fp32 value
+__device__ __forceinline__ uint32_t f32_key(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float f32_of_key(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
 
 __global__ void __launch_bounds__(kAcceptThreads) spec_accept_kernel(const AcceptArgs a) {
-  __shared__ float sv[kMaxCand];
-  __shared__ int si[kMaxCand];
-  __shared__ float kp[kMaxNodes];      // target probability of each node's token under the current node
-  __shared__ float pk[kMaxCand];       // kept probabilities (sorted order), first k entries
+  __shared__ uint64_t cand[kMaxCand];  // (value key, ~vocab index): descending = value desc, index asc
+  __shared__ float pk[64];             // kept probabilities in sorted order (first k)
+  __shared__ int tk[64];               // their vocab indices
+  __shared__ int64_t s_tok[kMaxNodes];
+  __shared__ int64_t s_par[kMaxNodes];
+  __shared__ float kp[kMaxNodes];      // target probability of each child's token under the current node
   __shared__ int s_next, s_k, s_done;
 
   const int r = blockIdx.x, tid = threadIdx.x;
@@ -292,142 +563,127 @@ __global__ void __launch_bounds__(kAcceptThreads) spec_accept_kernel(const Accep
   int P = 1;
   while (P < n_all) P <<= 1;
   const float top_p = a.top_p[r];
-  int cur = 0;
+  const int64_t seed = a.seed[r], committed = a.committed[r];
+  for (int j = tid; j < N; j += kAcceptThreads) {
+    s_tok[j] = a.tokens[(int64_t)r * N + j];
+    s_par[j] = a.parent[(int64_t)r * N + j];
+  }
   for (int j = tid; j < D; j += kAcceptThreads) a.acc[(int64_t)r * D + j] = -1;
+  int cur = 0;
   for (int d = 1; d <= D + 1; ++d) {
     const int64_t row = (int64_t)r * N + cur;
-    // ---- gather this node's candidates and sort them (value desc, index asc) ----
+    // ---- this node's candidates from every shard / chunk, sorted ----
     for (int j = tid; j < P; j += kAcceptThreads) {
+      uint64_t w = 0ull;
       if (j < n_all) {
         const int s = j / a.KC, q = j % a.KC;
         const int64_t o = (int64_t)(s / a.nch) * a.rank_stride + row * a.row_stride + (s % a.nch) * a.KC + q;
-        sv[j] = a.cv[o];
-        si[j] = a.ci[o];
-      } else {
-        sv[j] = -INFINITY;
-        si[j] = 0x7fffffff;
+        const int idx = a.ci[o];
+        if (idx != 0x7fffffff) w = ((uint64_t)f32_key(a.cv[o]) << 32) | (uint64_t)(0xffffffffu - (uint32_t)idx);
       }
+      cand[j] = w;
     }
     __syncthreads();
-    for (int size = 2; size <= P; size <<= 1) {
-      for (int stride = size >> 1; stride > 0; stride >>= 1) {
-        for (int j = tid; j < P; j += kAcceptThreads) {
-          const int o = j ^ stride;
-          if (o > j) {
-            const bool desc = (j & size) == 0;   // overall descending
-            const bool sw = desc ? cand_better(sv[o], si[o], sv[j], si[j]) : cand_better(sv[j], si[j], sv[o], si[o]);
-            if (sw) {
-              const float tv = sv[j];
-              const int ti = si[j];
-              sv[j] = sv[o];
-              si[j] = si[o];
-              sv[o] = tv;
-              si[o] = ti;
-            }
-          }
-        }
-        __syncthreads();
-      }
-    }
+    bitonic_desc_u64(cand, P);
     // ---- target distribution over the kept tokens ----
-    if (tid == 0) {
-      int k = greedy ? 1 : min(max(a.top_k[r], 1), min(a.KC, n_all));
-      const float m = sv[0];
-      float s = 0.f;
-      for (int i = 0; i < k; ++i) {
-        pk[i] = expf(sv[i] - m);
-        s += pk[i];
-      }
-      for (int i = 0; i < k; ++i) pk[i] = pk[i] / s;
-      if (!greedy && top_p < 1.0f) {
-        float cum = 0.f, kept = 0.f;
+    if (tid < 32) {
+      const int k = greedy ? 1 : min(max(a.top_k[r], 1), min(a.KC, n_all));
+      for (int i = tid; i < k; i += 32) tk[i] = (int)(0xffffffffu - (uint32_t)(cand[i] & 0xffffffffu));
+      if (tid == 0) {
+        const float m = f32_of_key((uint32_t)(cand[0] >> 32));
+        float ssum = 0.f;
         for (int i = 0; i < k; ++i) {
-          cum += pk[i];
-          if (!((cum - pk[i]) < top_p)) pk[i] = 0.f;
-          kept += pk[i];
+          pk[i] = expf(f32_of_key((uint32_t)(cand[i] >> 32)) - m);
+          ssum += pk[i];
         }
-        for (int i = 0; i < k; ++i) pk[i] = pk[i] / kept;
+        for (int i = 0; i < k; ++i) pk[i] = pk[i] / ssum;
+        if (!greedy && top_p < 1.0f) {
+          float cum = 0.f, kept = 0.f;
+          for (int i = 0; i < k; ++i) {
+            cum += pk[i];
+            if (!((cum - pk[i]) < top_p)) pk[i] = 0.f;
+            kept += pk[i];
+          }
+          for (int i = 0; i < k; ++i) pk[i] = pk[i] / kept;
+        }
+        s_k = k;
       }
-      s_k = k;
     }
     __syncthreads();
     const int k = s_k;
-    // ---- probability of every child's token (nodes whose parent is cur) ----
+    // ---- probability of every child's token ----
     for (int j = tid; j < N; j += kAcceptThreads) {
       float p = 0.f;
-      if (j > 0 && d <= D && a.parent[(int64_t)r * N + j] == cur) {
-        const int64_t tok = a.tokens[(int64_t)r * N + j];
+      if (j > 0 && d <= D && s_par[j] == cur) {
+        const int64_t tok = s_tok[j];
         for (int i = 0; i < k; ++i)
-          if (si[i] == tok) p = pk[i];
+          if (tk[i] == tok) p = pk[i];
       }
       kp[j] = p;
     }
     __syncthreads();
     if (tid == 0) {
-      const int64_t committed = a.committed[r];
-      const float u = seeded_coin(a.seed[r], committed, d - 1);
+      const float u = seeded_coin(seed, committed, d - 1);
       int next = -1;
       float cum = 0.f;
       for (int j = 1; j < N && d <= D; ++j) {
-        if (a.parent[(int64_t)r * N + j] != cur) continue;
+        if (s_par[j] != cur) continue;
         cum += kp[j];
         if (u < cum) {
           next = j;
           break;
         }
       }
-      s_done = 0;
-      if (next >= 0) {
-        a.acc[(int64_t)r * D + (d - 1)] = next;
-        s_next = next;
-      } else {
-        // bonus: the target distribution without the children's tokens (all of it if that leaves no mass),
-        // inverse CDF in vocab-index order with the final coin
+      s_done = next < 0;
+      s_next = next;
+      if (next >= 0) a.acc[(int64_t)r * D + (d - 1)] = next;
+    }
+    __syncthreads();
+    if (s_done) {
+      // bonus: the target distribution without the children's tokens (all of it if that leaves no mass),
+      // inverse CDF in vocab-index order with the final coin
+      if (tid < k) {          // zero the kept tokens that are children of cur (k <= 64 threads)
+        bool child = false;
+        for (int j = 1; j < N && d <= D; ++j) child |= (s_par[j] == cur && s_tok[j] == tk[tid]);
+        kp[tid] = child ? 0.f : pk[tid];     // kp is free now: reuse it for q
+      }
+      __syncthreads();
+      if (tid == 0) {
         int64_t tok;
         if (greedy) {
-          tok = si[0];
+          tok = tk[0];
         } else {
-          float q[64 + 1];   // k <= KC <= 64
-          int ord[64 + 1];
           double tot = 0.0;
-          for (int i = 0; i < k; ++i) {
-            q[i] = pk[i];
-            for (int j = 1; j < N && d <= D; ++j)
-              if (a.parent[(int64_t)r * N + j] == cur && a.tokens[(int64_t)r * N + j] == si[i]) q[i] = 0.f;
-            tot += q[i];
-          }
-          if (!(tot > 0.0))
-            for (int i = 0; i < k; ++i) q[i] = pk[i];
-          // order the kept tokens by vocab index
+          for (int i = 0; i < k; ++i) tot += (double)kp[i];
+          const bool empty = !(tot > 0.0);
+          int ord[64];
           for (int i = 0; i < k; ++i) ord[i] = i;
-          for (int i = 1; i < k; ++i) {
+          for (int i = 1; i < k; ++i) {          // kept tokens by vocab index
             const int x = ord[i];
             int j = i - 1;
-            while (j >= 0 && si[ord[j]] > si[x]) {
+            while (j >= 0 && tk[ord[j]] > tk[x]) {
               ord[j + 1] = ord[j];
               --j;
             }
             ord[j + 1] = x;
           }
-          double c = 0.0;
           tot = 0.0;
-          for (int i = 0; i < k; ++i) tot += (double)q[ord[i]];
-          const double target = (double)seeded_coin(a.seed[r], committed, D + 1) * tot;
-          tok = si[ord[k - 1]];
+          for (int i = 0; i < k; ++i) tot += (double)(empty ? pk[ord[i]] : kp[ord[i]]);
+          const double target = (double)seeded_coin(seed, committed, D + 1) * tot;
+          double c = 0.0;
+          tok = tk[ord[k - 1]];
           for (int i = 0; i < k; ++i) {
-            c += (double)q[ord[i]];
+            c += (double)(empty ? pk[ord[i]] : kp[ord[i]]);
             if (c > target) {
-              tok = si[ord[i]];
+              tok = tk[ord[i]];
               break;
             }
           }
         }
         a.bonus[r] = tok;
-        s_done = 1;
       }
+      break;
     }
-    __syncthreads();
-    if (s_done) break;
     cur = s_next;
     __syncthreads();
   }
@@ -438,7 +694,8 @@ __global__ void __launch_bounds__(kAcceptThreads) spec_accept_kernel(const Accep
 // ------------------------------------------------------------------------------------------------
 
 void sample_candidates(torch::Tensor logits, int64_t kc, c10::optional<torch::Tensor> temp, int64_t rows_per_temp,
-                       int64_t vocab_offset, torch::Tensor cv, torch::Tensor ci, c10::optional<torch::Tensor> cms) {
+                       int64_t vocab_offset, torch::Tensor cv, torch::Tensor ci, c10::optional<torch::Tensor> cms,
+                       torch::Tensor status) {
   TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == at::kBFloat16 && logits.dim() == 2);
   TORCH_CHECK(logits.stride(1) == 1, "logits rows must be contiguous");
   const int rows = (int)logits.size(0), V = (int)logits.size(1);
@@ -450,29 +707,50 @@ void sample_candidates(torch::Tensor logits, int64_t kc, c10::optional<torch::Te
   if (rows == 0) return;
   const at::cuda::CUDAGuard guard(logits.device());
   auto stream = at::cuda::getCurrentCUDAStream();
-  dim3 grid(rows, nchunks);
+  const int items = rows * nchunks;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = std::min(items, 2 * sms);
+  const int smem = (int)sizeof(CandSmem);
   const float* tp = temp ? temp->data_ptr<float>() : nullptr;
   auto* lp = reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr());
   float* cmsp = cms ? cms->data_ptr<float>() : nullptr;
   const int ld = (int)logits.stride(0);
-#define PHX_CAND(KC)                                                                                             \
-  if (cms)                                                                                                       \
-    sample_candidates_kernel<KC, true><<<grid, kCandThreads, 0, stream>>>(lp, V, ld, nchunks, (int)vocab_offset, \
-                                                                          tp, (int)rows_per_temp,                 \
-                                                                          cv.data_ptr<float>(),                   \
-                                                                          ci.data_ptr<int>(), cmsp);              \
-  else                                                                                                           \
-    sample_candidates_kernel<KC, false><<<grid, kCandThreads, 0, stream>>>(lp, V, ld, nchunks, (int)vocab_offset, \
-                                                                           tp, (int)rows_per_temp,                 \
-                                                                           cv.data_ptr<float>(),                   \
-                                                                           ci.data_ptr<int>(), nullptr);
-  if (kc == 1) { PHX_CAND(1) }
-  else if (kc == 8) { PHX_CAND(8) }
-  else if (kc == 16) { PHX_CAND(16) }
-  else if (kc == 64) { PHX_CAND(64) }
+  // bulk copies need 16-byte aligned rows and whole 16-byte chunk widths
+  const int tma = ((reinterpret_cast<uintptr_t>(lp) & 15u) == 0 && (ld % 8) == 0 && (V % 8) == 0) ? 1 : 0;
+  auto ovf = torch::empty({items}, logits.options().dtype(at::kInt));
+  int* ovp = ovf.data_ptr<int>();
+  int* st = status.data_ptr<int>();
+  static bool attr[64][8] = {};   // per device and instantiation: the dynamic shared-memory opt-in
+  TORCH_CHECK(dev < 64, "device index out of range");
+  auto run = [&](auto kcv, auto lsev, int slot) {
+    constexpr int KC = decltype(kcv)::value;
+    constexpr bool LSE = decltype(lsev)::value;
+    if (!attr[dev][slot]) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(sample_candidates_kernel<KC, LSE>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      attr[dev][slot] = true;
+    }
+    sample_candidates_kernel<KC, LSE><<<grid, kCandThreads, smem, stream>>>(
+        lp, V, ld, nchunks, items, (int)vocab_offset, tp, (int)rows_per_temp, cv.data_ptr<float>(),
+        ci.data_ptr<int>(), cmsp, ovp, tma, st);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    sample_candidates_exact_kernel<KC, LSE><<<grid, kCandThreads, 0, stream>>>(
+        lp, V, ld, nchunks, (int)vocab_offset, tp, (int)rows_per_temp, cv.data_ptr<float>(), ci.data_ptr<int>(),
+        cmsp, ovp, items);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  };
+  const bool l = cms.has_value();
+  if (kc == 1) l ? run(std::integral_constant<int, 1>{}, std::true_type{}, 0)
+                 : run(std::integral_constant<int, 1>{}, std::false_type{}, 1);
+  else if (kc == 8) l ? run(std::integral_constant<int, 8>{}, std::true_type{}, 2)
+                      : run(std::integral_constant<int, 8>{}, std::false_type{}, 3);
+  else if (kc == 16) l ? run(std::integral_constant<int, 16>{}, std::true_type{}, 4)
+                       : run(std::integral_constant<int, 16>{}, std::false_type{}, 5);
+  else if (kc == 64) l ? run(std::integral_constant<int, 64>{}, std::true_type{}, 6)
+                       : run(std::integral_constant<int, 64>{}, std::false_type{}, 7);
   else TORCH_CHECK(false, "candidate count must be 1, 8, 16 or 64");
-#undef PHX_CAND
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 int64_t sample_chunks(int64_t vocab) { return (vocab + kCandChunk - 1) / kCandChunk; }

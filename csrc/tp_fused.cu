@@ -48,6 +48,7 @@ struct TpArgs {
   // byte offsets inside the workspace
   uint64_t off_partial, off_h, off_y, off_q, off_s, off_flags, off_counter;
   int s_ld;                   // row stride (elements) of the scale matrix [H/128, s_ld]
+  uint64_t mc_base;           // multicast (NVLS) address of the workspace, 0 = none: see tp_ar_norm_kernel
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -57,6 +58,28 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+// NVLS (NVLink SHARP) multimem accesses through the workspace's multicast address: one load returns the
+// sum of the W ranks' copies (reduced in the switch), one store writes every rank's copy.
+__device__ __forceinline__ uint4 mm_ld_reduce_bf16x8(const void* mc) {
+  uint4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(mc)
+               : "memory");
+  return r;
+}
+__device__ __forceinline__ void mm_st16(void* mc, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(mc), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void mm_st8(void* mc, uint2 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1,%2};" ::"l"(mc), "r"(v.x), "r"(v.y) : "memory");
+}
+__device__ __forceinline__ void mm_st4(void* mc, uint32_t v) {
+  asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(mc), "r"(v) : "memory");
 }
 
 // wait until flags[slot0 + i] >= epoch for i < W (threads 0..W-1 each poll one); false on timeout
@@ -107,11 +130,14 @@ __device__ __forceinline__ void end_barrier(uint8_t* mine, uint64_t off_flags, u
 
 // WT: the world size as a compile-time constant (2, 4, 8) so the W peer loads of a 16-byte chunk are all
 // issued before the first is consumed; 0 = runtime world size.
-template <int MAXC, int WT>
+// NV: the reduce-scatter (pull mode) is one multimem.ld_reduce per 16 bytes (the switch sums the W partials in
+// bf16) and the all-gather of the results is one multimem.st per 16/8/4 bytes instead of W peer stores.
+template <int MAXC, int WT, bool NV>
 __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
   __shared__ float red[32];
   const int W = WT > 0 ? WT : a.world;
   auto base = [&](int p) { return reinterpret_cast<uint8_t*>(a.peer_base[p]); };
+  uint8_t* const mc = reinterpret_cast<uint8_t*>(a.mc_base);
   uint8_t* mine = base(a.rank);
   uint32_t* my_flags = reinterpret_cast<uint32_t*>(mine + a.off_flags);
   uint32_t* epoch_word = reinterpret_cast<uint32_t*>(mine + a.off_counter) + 1;
@@ -154,7 +180,9 @@ __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
           return a.recv ? reinterpret_cast<const uint4*>(mine + a.off_recv + p * rstride + roff)
                         : reinterpret_cast<const uint4*>(base(p) + a.off_partial + off);
         };
-        if constexpr (WT > 0) {
+        if (NV && !a.recv) {
+          add(mm_ld_reduce_bf16x8(mc + a.off_partial + off));
+        } else if constexpr (WT > 0) {
           uint4 v[WT];
 #pragma unroll
           for (int p = 0; p < WT; ++p) v[p] = *src(p);
@@ -178,7 +206,9 @@ __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
           ss += r.x * r.x + r.y * r.y;
         }
         const uint4 out = make_uint4(nh[0], nh[1], nh[2], nh[3]);
-        if (a.push_h)
+        if (a.push_h && NV)
+          mm_st16(mc + a.off_h + off, out);
+        else if (a.push_h)
           for (int p = 0; p < W; ++p) *reinterpret_cast<uint4*>(base(p) + a.off_h + off) = out;
         else
           *reinterpret_cast<uint4*>(mine + a.off_h + off) = out;
@@ -216,7 +246,10 @@ __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
           const uint4 out = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
                                        pack_bf16x2(y[6], y[7]));
           const size_t off = ((size_t)row * H + c * 8) * 2;
-          for (int p = 0; p < W; ++p) *reinterpret_cast<uint4*>(base(p) + a.off_y + off) = out;
+          if constexpr (NV)
+            mm_st16(mc + a.off_y + off, out);
+          else
+            for (int p = 0; p < W; ++p) *reinterpret_cast<uint4*>(base(p) + a.off_y + off) = out;
         }
       } else if (__any_sync(0xffffffffu, valid)) {
         float amax = 0.f;
@@ -231,9 +264,14 @@ __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
                                      pack_fp8x4(y[4] * isc, y[5] * isc, y[6] * isc, y[7] * isc));
           const size_t qoff = (size_t)row * H + c * 8;
           const size_t soff = ((size_t)(c >> 4) * a.s_ld + row) * 4;
-          for (int p = 0; p < W; ++p) {
-            *reinterpret_cast<uint2*>(base(p) + a.off_q + qoff) = q;
-            if ((c & 15) == 0) *reinterpret_cast<float*>(base(p) + a.off_s + soff) = sc;
+          if constexpr (NV) {
+            mm_st8(mc + a.off_q + qoff, q);
+            if ((c & 15) == 0) mm_st4(mc + a.off_s + soff, __float_as_uint(sc));
+          } else {
+            for (int p = 0; p < W; ++p) {
+              *reinterpret_cast<uint2*>(base(p) + a.off_q + qoff) = q;
+              if ((c & 15) == 0) *reinterpret_cast<float*>(base(p) + a.off_s + soff) = sc;
+            }
           }
         }
       }
@@ -245,7 +283,7 @@ __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
 
 void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M, int64_t H, double eps,
                 torch::Tensor w, bool out_bf16, bool push_h, torch::Tensor status, std::vector<int64_t> offsets,
-                int64_t s_ld, int64_t off_recv) {
+                int64_t s_ld, int64_t off_recv, int64_t mc_base) {
   TORCH_CHECK(peer_base.is_cuda() && peer_base.scalar_type() == at::kLong && peer_base.numel() == world);
   TORCH_CHECK(H % 128 == 0 && world >= 1 && world <= 32 && offsets.size() == 7);
   if (M == 0) return;
@@ -272,16 +310,22 @@ void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M,
   a.off_flags = offsets[5];
   a.off_counter = offsets[6];
   a.s_ld = (int)s_ld;
+  a.mc_base = (uint64_t)mc_base;
   const int rows_per = (int)((M + world - 1) / world);
   const int grid = std::max(1, std::min(rows_per, 148 * 4));
   const int maxc = (int)((H / 8 + 255) / 256);
-  auto launch = [&](auto wt) {
+  auto launch_nv = [&](auto wt, auto nv) {
     constexpr int WT = decltype(wt)::value;
-    if (maxc <= 1) tp_ar_norm_kernel<1, WT><<<grid, 256, 0, stream>>>(a);
-    else if (maxc <= 2) tp_ar_norm_kernel<2, WT><<<grid, 256, 0, stream>>>(a);
-    else if (maxc <= 4) tp_ar_norm_kernel<4, WT><<<grid, 256, 0, stream>>>(a);
-    else if (maxc <= 8) tp_ar_norm_kernel<8, WT><<<grid, 256, 0, stream>>>(a);
+    constexpr bool NV = decltype(nv)::value;
+    if (maxc <= 1) tp_ar_norm_kernel<1, WT, NV><<<grid, 256, 0, stream>>>(a);
+    else if (maxc <= 2) tp_ar_norm_kernel<2, WT, NV><<<grid, 256, 0, stream>>>(a);
+    else if (maxc <= 4) tp_ar_norm_kernel<4, WT, NV><<<grid, 256, 0, stream>>>(a);
+    else if (maxc <= 8) tp_ar_norm_kernel<8, WT, NV><<<grid, 256, 0, stream>>>(a);
     else TORCH_CHECK(false, "hidden size too large");
+  };
+  auto launch = [&](auto wt) {
+    if (mc_base != 0) launch_nv(wt, std::true_type{});
+    else launch_nv(wt, std::false_type{});
   };
   if (world == 2) launch(std::integral_constant<int, 2>{});
   else if (world == 4) launch(std::integral_constant<int, 4>{});
@@ -296,6 +340,7 @@ struct GatherArgs {
   int64_t n16;                // 16-byte words per rank
   uint64_t off_src, off_dst, off_flags, off_counter;
   int* status;
+  uint64_t mc_base;           // multicast address of the workspace (0: peer stores)
 };
 
 // copy this rank's staging block [n16 x 16 B] into slot [rank] of every rank's gather region
@@ -316,14 +361,17 @@ __global__ void __launch_bounds__(256) tp_allgather_kernel(const GatherArgs a) {
     const uint64_t dst_off = a.off_dst + (uint64_t)a.rank * (uint64_t)a.n16 * 16u;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.n16; i += (int64_t)gridDim.x * blockDim.x) {
       const uint4 v = src[i];
-      for (int p = 0; p < W; ++p) reinterpret_cast<uint4*>(base(p) + dst_off)[i] = v;
+      if (a.mc_base)
+        mm_st16(reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(a.mc_base) + dst_off) + i, v);
+      else
+        for (int p = 0; p < W; ++p) reinterpret_cast<uint4*>(base(p) + dst_off)[i] = v;
     }
   }
   end_barrier(mine, a.off_flags, a.off_counter, epoch, W, a.rank, a.peer_base, a.status);
 }
 
 void tp_allgather(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t nbytes, torch::Tensor status,
-                  std::vector<int64_t> offsets) {
+                  std::vector<int64_t> offsets, int64_t mc_base) {
   TORCH_CHECK(peer_base.is_cuda() && peer_base.numel() == world && offsets.size() == 4);
   TORCH_CHECK(nbytes > 0 && nbytes % 16 == 0, "gather block must be a positive multiple of 16 bytes");
   const at::cuda::CUDAGuard guard(peer_base.device());
@@ -337,7 +385,8 @@ void tp_allgather(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t 
   a.off_flags = offsets[2];
   a.off_counter = offsets[3];
   a.status = status.data_ptr<int>();
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((a.n16 + 255) / 256, 64));
+  a.mc_base = (uint64_t)mc_base;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((a.n16 + 255) / 256, 148));
   tp_allgather_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -69,12 +69,20 @@ def ar_norm_sweep(comm, world, iters, H=8192, tokens=(1, 16, 128, 1024, 8192)):
             dist.all_reduce(x)
             ops.add_rmsnorm_quant(h, x, w, 1e-5)
         f_ms = _time(lambda: comm.ar_norm(m, w, 1e-5), iters)
+        mc, comm.mc = comm.mc, 0
+        p_ms = _time(lambda: comm.ar_norm(m, w, 1e-5), iters)        # peer loads / stores only
+        comm.mc = mc
         n_ms = _time(nccl, iters)
         nv = (world - 1) / world * m * H * (2 + 1 + 4 / 128)
-        roof = nv / NVLINK_GBS / 1e6
-        rows.append({"op": "sweep_ar_norm_quant", "tokens": m, "H": H, "fused_ms": round(f_ms, 4),
-                     "nccl_plus_kernel_ms": round(n_ms, 4), "speedup": round(n_ms / f_ms, 2),
-                     "roofline_ms": round(roof, 5), "fused_frac_of_roofline": round(roof / f_ms, 3)})
+        # with NVLS the busier direction carries each GPU's partial rows for the other owners (read by the
+        # switch) plus its own result rows once (the switch copies them to every rank)
+        nv_mc = ((world - 1) / world * 2 + (1 + 4 / 128) / world) * m * H
+        roof = (nv_mc if mc else nv) / NVLINK_GBS / 1e6
+        rows.append({"op": "sweep_ar_norm_quant", "tokens": m, "H": H, "nvls": bool(mc), "fused_ms": round(f_ms, 4),
+                     "fused_p2p_ms": round(p_ms, 4), "nccl_plus_kernel_ms": round(n_ms, 4),
+                     "speedup": round(n_ms / f_ms, 2), "roofline_ms": round(roof, 5),
+                     "fused_frac_of_roofline": round(roof / f_ms, 3),
+                     "p2p_frac_of_roofline": round(nv / NVLINK_GBS / 1e6 / p_ms, 3)})
     return rows
 
 
@@ -93,7 +101,7 @@ def main():
         if rank == 0:
             for o in out:
                 print(json.dumps({"world": world, **o}))
-        dist.barrier()
+        comm.close()
         dist.destroy_process_group()
         return
     w = torch.ones(H, device=dev, dtype=torch.bfloat16)
@@ -148,7 +156,7 @@ def main():
     if rank == 0:
         for o in out:
             print(json.dumps({"world": world, **o}))
-    dist.barrier()
+    comm.close()
     dist.destroy_process_group()
 
 

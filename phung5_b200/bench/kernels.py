@@ -204,6 +204,36 @@ def case_topk(rows, v, k, with_lse=True):
     return (lambda: ops.topk_logprobs(x, k, with_lse=with_lse)), rows * v * 2, "bytes"
 
 
+def case_sample_candidates(rows, v, kc, lse=False):
+    """Device sampling stage 1: top-kc of x / T per 16384-column chunk (+ chunk max / sum-exp)."""
+    x = torch.randn(rows, v, device="cuda", dtype=torch.bfloat16) * 2
+    nch = int(ops.ext().sample_chunks(v))
+    cv = torch.empty(rows, nch, kc, device="cuda")
+    ci = torch.empty(rows, nch, kc, device="cuda", dtype=torch.int32)
+    cms = torch.empty(rows, nch, 2, device="cuda") if lse else None
+    temp = torch.full((rows,), 0.8, device="cuda")
+    return (lambda: ops.ext().sample_candidates(x, kc, temp, 1, 0, cv, ci, cms, ops.status_tensor(x.device))), rows * v * 2, "bytes"
+
+
+def case_spec_accept(R=64, N=64, D=6, ranks=8, nch=1, kc=64):
+    """Device sampling stage 2: the seeded accept walk of 64 requests over 64-node trees (8 candidate lists)."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    cv = torch.randn(ranks, R * N, nch, kc, device="cuda", generator=g)
+    ci = torch.randint(0, 128256, (ranks, R * N, nch, kc), device="cuda", dtype=torch.int32, generator=g)
+    parent = torch.cat([torch.full((R, 1), -1, device="cuda", dtype=torch.int64),
+                        (torch.arange(1, N, device="cuda") - 1)[None].expand(R, N - 1) // 8], 1).contiguous()
+    tokens = ci[0, :N * R, 0, 0].view(R, N).long().contiguous()
+    temp = torch.full((R,), 0.9, device="cuda")
+    topk = torch.full((R,), 50, device="cuda", dtype=torch.int32)
+    topp = torch.full((R,), 0.9, device="cuda")
+    seed = torch.arange(R, device="cuda", dtype=torch.int64)
+    com = torch.full((R,), 4600, device="cuda", dtype=torch.int64)
+    acc = torch.empty(R, D, device="cuda", dtype=torch.int64)
+    bonus = torch.empty(R, device="cuda", dtype=torch.int64)
+    fn = lambda: ops.ext().spec_accept(cv, ci, ranks, nch, kc, tokens, parent, temp, topk, topp, seed, com, D, acc, bonus)
+    return fn, cv.numel() * 8, "bytes"
+
+
 def case_attention(which, impl, hq=64, hkv=8):
     q, kc, vc, meta = _verify_case(hq=hq, hkv=hkv)
     t, hq = q.shape[0], q.shape[1]
@@ -271,6 +301,12 @@ CASES = {
     "topk8_draft_tp8": lambda: case_topk(512, 16032, 8),
     "topk8_draft": lambda: case_topk(512, 128256, 8),
     "argmax_verify": lambda: case_topk(4096, 128256, 1, with_lse=False),
+    "sample_cand_verify": lambda: case_sample_candidates(4096, 128256, 64),
+    "sample_cand_verify_tp8": lambda: case_sample_candidates(4096, 16032, 64),
+    "sample_cand_k16_verify": lambda: case_sample_candidates(4096, 128256, 16),
+    "sample_cand_top8_lse_draft": lambda: case_sample_candidates(512, 128256, 8, lse=True),
+    "sample_cand_top8_lse_draft_tp8": lambda: case_sample_candidates(512, 16032, 8, lse=True),
+    "spec_accept_64x64": lambda: case_spec_accept(),
     # draft-round shapes (512 = 64 requests x top-8 frontier)
     "gemm_fp8_draft_qkv_tp8": lambda: case_gemm_fp8(512, 1280, 8192),
     "gemm_fp8_draft_gate_up_tp8": lambda: case_gemm_fp8(512, 7168, 8192),

@@ -293,7 +293,7 @@ def spec_sample_accept(logits: torch.Tensor, tokens: torch.Tensor, parent: torch
     nch = int(ext().sample_chunks(vl))
     cv = torch.empty(rows, nch, kc, dtype=torch.float32, device=logits.device)
     ci = torch.empty(rows, nch, kc, dtype=torch.int32, device=logits.device)
-    ext().sample_candidates(logits, kc, temp, N, vocab_offset, cv, ci, None)
+    ext().sample_candidates(logits, kc, temp, N, vocab_offset, cv, ci, None, status_tensor(logits.device))
     ranks = 1
     if gather is not None:
         cv, ci = gather([cv, ci])

@@ -14,7 +14,10 @@ mapped into every peer, exchanged at rendezvous) holding, for up to `max_tokens`
     recv    [W, ceil(M/W), H] bf16  row-parallel projection outputs pushed by each rank for the rows this
                           rank owns (`project`: the GEMM's epilogue stores them over NVLink)
 `ar_norm(M, w)` runs csrc/tp_fused.cu: reduce-scatter of the partials with P2P loads, + residual,
-RMSNorm, fp8 quant, all-gather of the results with P2P stores, in one kernel. The engine's model uses
+RMSNorm, fp8 quant, all-gather of the results with P2P stores, in one kernel. Where the GPUs support
+NVLink multicast (NVLS), the reduce-scatter is one multimem.ld_reduce per 16 bytes through the workspace's
+multicast address and the all-gather one multimem.st (each rank sends its rows once; the switch copies
+them to every rank); PHX_NVLS=0 keeps the peer loads and stores. The engine's model uses
 it when the communicator reports `fused = True` (models/llama.py, forward_fused; the EAGLE head's layer
 too); anything larger than the workspace keeps the NCCL path of the base class. `gather` exchanges small
 blocks (vocab-sharded top-k and argmax candidates) with P2P stores. Barrier epochs are kept on the device,
@@ -24,6 +27,8 @@ so every kernel here can be captured in a CUDA graph; no NCCL call remains on th
 fused forward's plumbing is tested without GPUs.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 import torch.distributed as dist
@@ -70,6 +75,15 @@ class FusedCommunicator(NcclCommunicator):
         grp = self.group or dist.group.WORLD
         self.handle = symm.rendezvous(self.ws.buf, grp.group_name)
         self.peer_base = torch.tensor(list(self.handle.buffer_ptrs), dtype=torch.int64, device=dev)
+        # NVLS: the workspace's multicast address (every rank's copy behind one NVSwitch address) when the GPUs
+        # and driver support it; PHX_NVLS=0 keeps every transfer on peer loads and stores.
+        mc = 0
+        if os.environ.get("PHX_NVLS", "1") != "0":
+            try:
+                mc = int(self.handle.multicast_ptr or 0)
+            except (RuntimeError, AttributeError):
+                mc = 0
+        self.mc = mc
         self.ws.view("flags", torch.int32, (2 * self.size,)).zero_()
         self.ws.view("counter", torch.int32, (4,)).zero_()
         torch.cuda.synchronize(dev)
@@ -85,6 +99,20 @@ class FusedCommunicator(NcclCommunicator):
         torch.cuda.synchronize(self.device)
         self.ws.view("flags", torch.int32, (2 * self.size,)).zero_()
         self.ws.view("counter", torch.int32, (4,)).zero_()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        """Collective teardown: every rank calls it (between steps, nothing in flight) before the process group is
+        destroyed. The symmetric workspace, its peer mappings and its multicast object are released together,
+        between two barriers, so no rank unmaps memory a peer is still bound to."""
+        dist.barrier(group=self.group)
+        torch.cuda.synchronize(self.device)
+        self.handle = None
+        self.ws = None
+        self.peer_base = None
+        import gc
+        gc.collect()
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
 
@@ -110,7 +138,7 @@ class FusedCommunicator(NcclCommunicator):
         push_h); returns the normalized rows on every rank: (q, s) fp8 or y bf16."""
         off = [self.ws.off[k] for k in ("partial", "h", "y", "q", "s", "flags", "counter")]
         ops.ext().tp_ar_norm(self.peer_base, self.rank, self.size, m, self.hidden, eps, w, out_bf16, push_h,
-                             ops.status_tensor(self.device), off, m, self.ws.off["recv"] if recv else -1)
+                             ops.status_tensor(self.device), off, m, self.ws.off["recv"] if recv else -1, self.mc)
         if out_bf16:
             return self.ws.view("y", torch.bfloat16, (m, self.hidden))
         q = self.ws.view("q", torch.float8_e4m3fn, (m, self.hidden))
@@ -131,7 +159,7 @@ class FusedCommunicator(NcclCommunicator):
             nb = p.numel() * p.element_size()
             src[a:a + nb].copy_(p.contiguous().view(-1).view(torch.uint8))
         off = [self.ws.off[k] for k in ("gsrc", "gdst", "flags", "counter")]
-        ops.ext().tp_allgather(self.peer_base, self.rank, self.size, o, ops.status_tensor(self.device), off)
+        ops.ext().tp_allgather(self.peer_base, self.rank, self.size, o, ops.status_tensor(self.device), off, self.mc)
         dst = self.ws.buf[self.ws.off["gdst"]: self.ws.off["gdst"] + self.size * o].view(self.size, o)
         out = []
         for p, a in zip(parts, offs):

@@ -62,7 +62,7 @@ def test_candidates_are_exact_topk(V, kc):
     nch = int(ops.ext().sample_chunks(V))
     cv = torch.empty(rows, nch, kc, device=DEV)
     ci = torch.empty(rows, nch, kc, device=DEV, dtype=torch.int32)
-    ops.ext().sample_candidates(x, kc, temp, 3, 1000, cv, ci, None)
+    ops.ext().sample_candidates(x, kc, temp, 3, 1000, cv, ci, None, ops.status_tensor(x.device))
     torch.cuda.synchronize()
     xf = x.float() / temp.repeat_interleave(3)[:, None]
     for c in range(nch):
@@ -75,6 +75,23 @@ def test_candidates_are_exact_topk(V, kc):
         key_got = sorted(zip(got_v.flatten().tolist(), got_i.flatten().tolist()))
         key_want = sorted(zip(sv[:, :kc].flatten().tolist(), want_i.flatten().tolist()))
         assert key_got == key_want, c
+
+
+def test_candidates_with_massive_ties_take_the_exact_path():
+    """A flat row (every logit equal) overflows the fast path's candidate buffer; the exact radix kernel then
+    returns the lowest indices."""
+    x = torch.zeros(3, 40000, device=DEV, dtype=torch.bfloat16)
+    x[1, 777] = 1.0                                    # one clear winner, the rest tied
+    cv = torch.empty(3, 3, 16, device=DEV)
+    ci = torch.empty(3, 3, 16, device=DEV, dtype=torch.int32)
+    cms = torch.empty(3, 3, 2, device=DEV)
+    ops.ext().sample_candidates(x, 16, None, 1, 0, cv, ci, cms, ops.status_tensor(x.device))
+    torch.cuda.synchronize()
+    assert torch.equal(ci[0, 0].sort().values.cpu(), torch.arange(16, dtype=torch.int32))
+    assert torch.equal(ci[0, 2].sort().values.cpu(), torch.arange(32768, 32768 + 16, dtype=torch.int32))
+    got = ci[1, 0].sort().values.cpu().tolist()
+    assert 777 in got and got == sorted([777] + list(range(15)))
+    assert torch.allclose(cms[0, :, 1].cpu(), torch.tensor([16384.0, 16384.0, 40000 - 32768.0]))
 
 
 @pytest.mark.parametrize("V,ranks", [(40000, 1), (128256, 1), (128256, 8), (64128, 2)])
@@ -93,7 +110,7 @@ def test_accept_walk_matches_torch_definition(V, ranks):
         ci = torch.empty(ranks, R * N, nch, 64, device=DEV, dtype=torch.int32)
         for w in range(ranks):
             ops.ext().sample_candidates(x[:, w * vs:(w + 1) * vs].contiguous(), 64, temps, N, w * vs, cv[w], ci[w],
-                                        None)
+                                        None, ops.status_tensor(x.device))
         acc = torch.empty(R, D, dtype=torch.int64, device=DEV)
         bonus = torch.empty(R, dtype=torch.int64, device=DEV)
         ops.ext().spec_accept(cv, ci, ranks, nch, 64, tokens, parent, temps, top_k, top_p, seed, committed, D, acc,
