@@ -2851,6 +2851,10 @@ class Object3D(Host):
         "rotateX": lambda s, i, x: s.rotate_local("x", _num_arg(x, 0)),
         "rotateY": lambda s, i, x: s.rotate_local("y", _num_arg(x, 0)),
         "rotateZ": lambda s, i, x: s.rotate_local("z", _num_arg(x, 0)),
+        # world axis: the rotation composes on the left (the object turns about a world-space axis through its
+        # own origin; its position is unchanged)
+        "rotateOnWorldAxis": lambda s, i, x: (s.props["rotation"].setv(_mat3_to_euler(_mat_mul(
+            _axis_mat(_arg(x, 0).v(), _num_arg(x, 1)), _euler_mat(s.props["rotation"].v())))), s)[-1],
         "rotateOnAxis": lambda s, i, x: (s.props["rotation"].setv(_mat3_to_euler(_mat_mul(_euler_mat(s.props["rotation"].v()),
                                                                                          _axis_mat(_arg(x, 0).v(), _num_arg(x, 1))))), s)[-1],
         "translateX": lambda s, i, x: (s.props["position"].setv(_add3(s.props["position"].v(), _mat3_apply(_euler_mat(s.props["rotation"].v()), [_num_arg(x, 0), 0, 0]))), s)[-1],
@@ -3046,6 +3050,56 @@ def _geom_ctor(gtype):
     return Native(gtype, ctor=build)
 
 
+def world_bbox(root: "Object3D"):
+    """World-space (min, max) corners of every mesh under `root` (its own transform included), or None."""
+    import numpy as np
+    sc = to_scene_json(root)
+    geoms = {g["uuid"]: g for g in sc["geometries"]}
+    lo, hi = np.full(3, np.inf), np.full(3, -np.inf)
+
+    def walk(nd, parent):
+        m = np.asarray(nd.get("matrix"), dtype=np.float64).reshape(4, 4).T
+        w = parent @ m
+        g = geoms.get(nd.get("geometry"))
+        if g is not None and not nd.get("visible", True) is False:
+            v = np.asarray(g["data"]["attributes"]["position"]["array"], dtype=np.float64).reshape(-1, 3)
+            if len(v):
+                p = v @ w[:3, :3].T + w[:3, 3]
+                lo[:] = np.minimum(lo, p.min(0))
+                hi[:] = np.maximum(hi, p.max(0))
+        for c in nd.get("children", []):
+            walk(c, w)
+    walk(sc["object"], np.eye(4))
+    return None if not np.isfinite(lo).all() else (lo.tolist(), hi.tolist())
+
+
+class Box3(Host):
+    """THREE.Box3 subset: setFromObject (world bounds of an object's meshes), getCenter, getSize, isEmpty."""
+    cls_name = "Box3"
+
+    def __init__(self):
+        super().__init__({"min": Vec(("x", "y", "z"), [math.inf] * 3, "Vector3"),
+                          "max": Vec(("x", "y", "z"), [-math.inf] * 3, "Vector3"), "isBox3": True})
+
+    def set_from(self, o):
+        bb = world_bbox(o) if isinstance(o, Object3D) else None
+        self.props["min"].setv(bb[0] if bb else [math.inf] * 3)
+        self.props["max"].setv(bb[1] if bb else [-math.inf] * 3)
+        return self
+
+    def empty(self):
+        return any(a > b for a, b in zip(self.props["min"].v(), self.props["max"].v()))
+
+    js_methods = {
+        "setFromObject": lambda s, i, x: s.set_from(_arg(x, 0)),
+        "isEmpty": lambda s, i, x: s.empty(),
+        "getCenter": lambda s, i, x: _arg(x, 0).setv([0.0] * 3 if s.empty() else
+                                                     [(a + b) / 2 for a, b in zip(s.props["min"].v(), s.props["max"].v())]),
+        "getSize": lambda s, i, x: _arg(x, 0).setv([0.0] * 3 if s.empty() else
+                                                   [b - a for a, b in zip(s.props["min"].v(), s.props["max"].v())]),
+    }
+
+
 def _vec_ctor(name, comps):
     return Native(name, ctor=lambda it, x: Vec(comps, [_num_arg(x, k) for k in range(len(comps))], name))
 
@@ -3065,6 +3119,7 @@ def make_three(it: Interp) -> JSObject:
         three[cls] = Native(cls, ctor=lambda i, x: BufferAttribute(i.iterate(_arg(x, 0)) if isinstance(_arg(x, 0), JSArray)
                                                                    else [], _num_arg(x, 1, 3.0)))
     three["Group"] = Native("Group", ctor=lambda i, x: Object3D("Group"))
+    three["Box3"] = Native("Box3", ctor=lambda i, x: Box3())
     three["Object3D"] = Native("Object3D", ctor=lambda i, x: Object3D("Object3D"))
     three["Scene"] = Native("Scene", ctor=lambda i, x: Object3D("Group"))
     for t in ("Mesh", "LineSegments", "Line", "LineLoop", "Points", "Sprite"):

@@ -104,8 +104,14 @@ class Orchestrator:
         if self.s.pipeline.candidate_deadline_s > 0:
             cd = time.monotonic() + self.s.pipeline.candidate_deadline_s
             cand_deadline = cd if deadline is None else min(deadline, cd)
+        orient = None
+        if self.s.orientation.enabled:
+            from .orient import OrientSettings
+            o = self.s.orientation
+            orient = OrientSettings(enabled=True, img_size=o.img_size, min_side_margin=o.min_side_margin)
+        checker = getattr(self.coders[0], "checker", None) if self.coders else None
         factory = CandidateFactory(task, self.coders, self.renderer, self.embedder, self.limits, prompt_url,
-                                   plan_text, cand_deadline)
+                                   plan_text, cand_deadline, ref_vec=ref_vec, checker=checker, orient=orient)
         duel = make_duel(task, self.judge, self.limits, prompt_url, ref_vec, on_duel=self.stats.duel,
                          es_max_round=self.s.pipeline.s1_early_stop_max_round) if self.judge is not None else None
         k = self.k

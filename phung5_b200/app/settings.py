@@ -136,6 +136,13 @@ class EmbedderConfig(BaseModel):
     batch_size: int = 8
 
 
+class OrientationConfig(BaseModel):
+    """Orientation stage (app/orient.py): probe renders + embeddings decide a rotation written into the module."""
+    enabled: bool = True
+    img_size: int = 160
+    min_side_margin: float = 0.0
+
+
 class EventBusConfig(BaseModel):
     max_iter: int = 2
     task_deadline_s: float = 2700.0
@@ -157,6 +164,7 @@ class Settings(BaseModel):
     warmup: bool = True
     llm_clients: Dict[str, LLMClientConfig] = Field(default_factory=dict)
     embedder: EmbedderConfig = Field(default_factory=EmbedderConfig)
+    orientation: OrientationConfig = Field(default_factory=OrientationConfig)
     actors: ActorsConfig = Field(default_factory=ActorsConfig)
     event_bus: EventBusConfig = Field(default_factory=EventBusConfig)
     burst: BurstConfig = Field(default_factory=BurstConfig)

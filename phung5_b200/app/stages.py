@@ -52,9 +52,12 @@ class CandidateFactory:
 
     def __init__(self, task: PipelineTask, coders: Sequence[SceneCoderAgent], renderer: RendererModule, embedder,
                  limits: StageLimits, prompt_url: str, plan: Optional[str] = None, deadline: Optional[float] = None,
-                 on_event: Optional[Callable[[str, dict], None]] = None):
+                 on_event: Optional[Callable[[str, dict], None]] = None, ref_vec=None, checker=None,
+                 orient=None):
         self.task, self.coders, self.renderer, self.embedder = task, coders, renderer, embedder
         self.limits, self.prompt_url, self.plan, self.deadline = limits, prompt_url, plan, deadline
+        # orientation stage (app/orient.py): needs the prompt's embedding and a checker for the rewritten module
+        self.ref_vec, self.checker, self.orient = ref_vec, checker, orient
         self.seen: Dict[str, int] = {}
         self.on_event = on_event or (lambda kind, d: None)
 
@@ -88,6 +91,14 @@ class CandidateFactory:
         self.seen[dg] = k
         cand = Candidate(code=res.check.code, digest=dg, coder=coder.name, scene=res.check.scene,
                          stats={**res.check.stats, "k": k, "repairs": res.repairs})
+        if self.orient is not None and self.orient.enabled and self.checker is not None and self.ref_vec is not None:
+            from .orient import orient_candidate
+            async with self.limits.render:
+                cand.code, cand.scene, ores = await orient_candidate(
+                    cand.code, cand.scene, renderer=self.renderer, embedder=self.embedder, ref_vec=self.ref_vec,
+                    checker=self.checker, settings=self.orient)
+            cand.stats["orient"] = ores.reason if not ores.applied else f"{ores.best}:{len(ores.steps)}"
+            self.on_event("orient", {"k": k, "applied": ores.applied, "best": ores.best})
         try:
             async with self.limits.render:
                 views = await self.renderer.judge_views(cand.scene, gray=True)
