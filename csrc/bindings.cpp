@@ -68,6 +68,9 @@ int64_t sample_chunks(int64_t vocab);
 void spec_accept(torch::Tensor cv, torch::Tensor ci, int64_t ranks, int64_t nch, int64_t kc, torch::Tensor tokens,
                  torch::Tensor parent, torch::Tensor temp, torch::Tensor top_k, torch::Tensor top_p,
                  torch::Tensor seed, torch::Tensor committed, int64_t D, torch::Tensor acc, torch::Tensor bonus);
+torch::Tensor raster_pbr(torch::Tensor tris, torch::Tensor cols, torch::Tensor mats, torch::Tensor vp,
+                         std::vector<double> eye, torch::Tensor lights, double ambient, std::vector<double> hemi,
+                         double exposure, std::vector<double> bg, int64_t W, int64_t H);
 }  // namespace phx
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -94,6 +97,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("causal_conv1d", &phx::causal_conv1d);
   m.def("gated_rmsnorm", &phx::gated_rmsnorm);
   m.def("raster", &phx::raster);
+  m.def("raster_pbr", &phx::raster_pbr);
   m.def("sample_candidates", &phx::sample_candidates);
   m.def("sample_chunks", &phx::sample_chunks);
   m.def("spec_accept", &phx::spec_accept);

@@ -3459,6 +3459,9 @@ def to_scene_json(root: Object3D, max_depth: int = 64) -> dict:
             mats[key] = {"uuid": f"m{len(mats)}", "type": m.mtype,
                          "color": col.hex() if isinstance(col, Color) else 0xCCCCCC,
                          "opacity": _to_num(m.props.get("opacity", 1.0))}
+            if m.mtype in ("MeshStandardMaterial", "MeshPhysicalMaterial"):
+                mats[key]["roughness"] = _to_num(m.props.get("roughness", 1.0))
+                mats[key]["metalness"] = _to_num(m.props.get("metalness", 0.0))
         return mats[key]["uuid"]
 
     def node(o: Object3D, depth: int) -> dict:

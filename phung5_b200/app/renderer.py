@@ -38,6 +38,7 @@ class RendererSettings:
     grid_gap: int = 4
     timeout_s: float = 30.0
     device: str = "auto"        # "auto" -> cuda when available
+    lighting: str = "studio"    # render/scene.py LIGHTING rig (standard-material shading); "lambert": flat rig
 
 
 def to_png(img: torch.Tensor) -> bytes:
@@ -90,18 +91,24 @@ class RendererModule:
         return st
 
     def _geometry(self, scene: dict):
-        tris, cols = S.scene_triangles(scene)
-        return S.normalise(tris), cols
+        tris, cols, mats = S.scene_triangles(scene, with_materials=True)
+        return S.normalise(tris), cols, mats
 
     def render_sync(self, scene: dict, views: Sequence, size: int, background=WHITE, yaw: float = 0.0) -> List[torch.Tensor]:
         """Render `views` [(azimuth, elevation)] of a scene; `yaw` rotates the object about +y first."""
-        tris, cols = self._geometry(scene)
+        tris, cols, mats = self._geometry(scene)
         st = self._stream()
         ctx = torch.cuda.stream(st) if st is not None else _null()
         with ctx:
             tris = tris.to(self.device, non_blocking=False)
             cols = cols.to(self.device)
-            out = [S.render(tris, cols, S.view_projection(a + yaw, e), size, background=background) for a, e in views]
+            mats = mats.to(self.device)
+            if self.s.lighting == "lambert":
+                out = [S.render(tris, cols, S.view_projection(a + yaw, e), size, background=background)
+                       for a, e in views]
+            else:
+                out = [S.render_pbr(tris, cols, mats, a + yaw, e, size, self.s.lighting, background=background)
+                       for a, e in views]
             if st is not None:
                 st.synchronize()
         return out

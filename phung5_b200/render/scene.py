@@ -12,7 +12,7 @@ around the unit-normalised object, vertical fov 49.1 degrees (renderer/render_se
 from __future__ import annotations
 
 import math
-from typing import Dict, List, Sequence, Tuple
+from typing import Optional, Dict, List, Sequence, Tuple
 
 import torch
 
@@ -98,12 +98,13 @@ def _geometry(g: dict):
     raise ValueError(f"unsupported geometry type {t!r}")
 
 
-def scene_triangles(scene: dict) -> Tuple[torch.Tensor, torch.Tensor]:
-    """-> (triangles [T, 3, 3] world space, colours [T, 3] linear RGB)."""
+def scene_triangles(scene: dict, with_materials: bool = False):
+    """-> (triangles [T, 3, 3] world space, colours [T, 3] linear RGB[, materials [T, 2] (roughness,
+    metalness)]); materials default to the standard material's roughness 1, metalness 0."""
     geoms = {g["uuid"]: g for g in scene.get("geometries", [])}
     mats = {m["uuid"]: m for m in scene.get("materials", [])}
     cache: Dict[str, tuple] = {}
-    tris, cols = [], []
+    tris, cols, pbr = [], [], []
 
     def walk(node, parent):
         m = torch.tensor(node.get("matrix", [1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1]), dtype=torch.float32)
@@ -118,13 +119,18 @@ def scene_triangles(scene: dict) -> Tuple[torch.Tensor, torch.Tensor]:
             c = mats.get(node.get("material"), {}).get("color", 0xCCCCCC)
             rgb = torch.tensor([(c >> 16) & 255, (c >> 8) & 255, c & 255], dtype=torch.float32) / 255.0
             cols.append((rgb ** 2.2).expand(f.shape[0], 3))     # sRGB material colour -> linear
+            md = mats.get(node.get("material"), {})
+            pbr.append(torch.tensor([float(md.get("roughness", 1.0)), float(md.get("metalness", 0.0))]).expand(
+                f.shape[0], 2))
         for ch in node.get("children", []):
             walk(ch, world)
 
     walk(scene.get("object", {}), torch.eye(4))
     if not tris:
-        return torch.zeros(0, 3, 3), torch.zeros(0, 3)
-    return torch.cat(tris), torch.cat(cols)
+        empty = (torch.zeros(0, 3, 3), torch.zeros(0, 3))
+        return empty + (torch.zeros(0, 2),) if with_materials else empty
+    out = (torch.cat(tris), torch.cat(cols))
+    return out + (torch.cat(pbr),) if with_materials else out
 
 
 def normalise(tris: torch.Tensor) -> torch.Tensor:
@@ -163,6 +169,37 @@ def render(tris: torch.Tensor, cols: torch.Tensor, vp: torch.Tensor, size: int =
     """-> RGBA uint8 [size, size, 4]; CUDA tensors use the GPU rasterizer, CPU tensors its C++ restatement."""
     return ops.ext().raster(tris.float().contiguous(), cols.float().contiguous(), vp.float(), size, size, list(light),
                             ambient, diffuse, exposure, list(background))
+
+
+# Light rigs for raster_pbr (csrc/raster.cu): lights (direction towards the light, intensity, follows the
+# camera), ambient, hemisphere environment (sky, ground linear RGB, intensity). Modelled on the reference's
+# page rigs (render_service/object-page.html:37-110): "studio" = key / fill / rim lights over a white-to-grey
+# hemisphere, "neutral" = a camera-following key light in a grey room with a bright ceiling, "follow" = ambient +
+# a camera-following light.
+LIGHTING = {
+    "studio": {"lights": [(2, 3, 2, 1.2, 0), (-2, 1, 1, 0.4, 0), (0, 2, -3, 0.3, 0)], "ambient": 0.12,
+               "hemi": (1.0, 1.0, 1.0, 0.058, 0.058, 0.058, 0.8)},
+    "neutral": {"lights": [(0, 0, 1, 1.1, 1)], "ambient": 0.0, "hemi": (1.2, 1.2, 1.2, 0.32, 0.32, 0.32, 0.9)},
+    "follow": {"lights": [(0, 0, 1, 1.5, 1)], "ambient": 0.4, "hemi": (0, 0, 0, 0, 0, 0, 0.0)},
+}
+
+
+def camera_eye(azimuth_deg: float, elevation_deg: float, radius: float = 2.0) -> List[float]:
+    az, el = math.radians(azimuth_deg), math.radians(elevation_deg)
+    return [radius * math.cos(el) * math.sin(az), radius * math.sin(el), radius * math.cos(el) * math.cos(az)]
+
+
+def render_pbr(tris: torch.Tensor, cols: torch.Tensor, mats: Optional[torch.Tensor], azimuth_deg: float,
+               elevation_deg: float, size: int = 256, lighting: str = "studio", exposure: float = 1.0,
+               background=(1.0, 1.0, 1.0)) -> torch.Tensor:
+    """Standard-material render (GGX + hemisphere environment) of one view -> RGBA uint8 [size, size, 4]; CUDA
+    tensors use the GPU kernel, CPU tensors its C++ restatement."""
+    rig = LIGHTING[lighting]
+    lights = torch.tensor(rig["lights"], dtype=torch.float32).view(-1, 5)
+    m = mats.float().contiguous() if mats is not None else torch.zeros(0, 2, device=tris.device)
+    return ops.ext().raster_pbr(tris.float().contiguous(), cols.float().contiguous(), m,
+                                view_projection(azimuth_deg, elevation_deg), camera_eye(azimuth_deg, elevation_deg),
+                                lights, float(rig["ambient"]), list(rig["hemi"]), exposure, list(background), size, size)
 
 
 VIEW_PRESETS = {"front4": [(0, 15), (45, 15), (-45, 15), (90, 15)],

@@ -410,6 +410,23 @@ def test_rasterizer_matches_cpu_restatement():
         assert (diff > 2).float().mean().item() < 0.01
 
 
+def test_standard_material_rasterizer_matches_cpu_restatement():
+    from phung5_b200.render.scene import normalise, render_pbr, scene_triangles
+    from tests.test_render_cpu import SCENE
+    tris, cols, mats = scene_triangles(SCENE, with_materials=True)
+    tris = normalise(tris)
+    g = torch.Generator().manual_seed(1)
+    extra = torch.rand(2000, 3, 3, generator=g) - 0.5
+    tris = torch.cat([tris, extra * 0.8])
+    cols = torch.cat([cols, torch.rand(2000, 3, generator=g)])
+    mats = torch.cat([mats, torch.rand(2000, 2, generator=g)])
+    for (az, el), rig in zip([(0, 15), (70, 30), (200, -20)], ["studio", "neutral", "follow"]):
+        a = render_pbr(tris.to(DEV), cols.to(DEV), mats.to(DEV), az, el, 256, rig).cpu()
+        b = render_pbr(tris, cols, mats, az, el, 256, rig)
+        diff = (a.int() - b.int()).abs().amax(-1)
+        assert (diff > 2).float().mean().item() < 0.01
+
+
 def test_selftest_cli_passes():
     from phung5_b200.ops import selftest
     res = selftest.run()
