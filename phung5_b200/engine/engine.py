@@ -58,6 +58,7 @@ class Request:
     t_first: float = 0.0
     t_done: float = 0.0
     gslot: int = -1           # hybrid models: GDN state slot
+    mm: List[Tuple[int, torch.Tensor]] = field(default_factory=list)   # (prompt position, image features [n, H])
 
 
 @dataclass
@@ -212,11 +213,21 @@ class LLMEngine:
         return 512
 
     # ------------------------------------------------------------------------------------------
-    def add_request(self, prompt: Sequence[int], params: Optional[SamplingParams] = None) -> int:
+    def add_request(self, prompt: Sequence[int], params: Optional[SamplingParams] = None,
+                    mm: Optional[Sequence[Tuple[int, torch.Tensor]]] = None) -> int:
+        """mm: image inputs as (position, features [n, hidden]): prompt[position:position + n] are the image's
+        placeholder ids (models/vision.py), whose token embeddings prefill replaces by the features."""
         rid = self._next_rid
         self._next_rid += 1
         r = Request(rid=rid, tokens=list(prompt), prompt_len=len(prompt), params=params or SamplingParams(),
                     t_arrive=time.perf_counter())
+        if mm:
+            if self.hybrid:
+                raise ValueError("image inputs are served by the attention-only models")
+            for pos, f in mm:
+                if pos < 0 or pos + f.shape[0] > len(prompt) or f.shape[-1] != self.cfg.model.hidden:
+                    raise ValueError("image features do not fit the prompt's placeholder span")
+            r.mm = [(int(pos), f.to(self.device)) for pos, f in mm]
         self.reqs[rid] = r
         self.waiting.append(r)
         return rid
@@ -339,6 +350,18 @@ class LLMEngine:
         packed = self._h2d(ts + [r.gslot for r in reqs], torch.int32)
         return GdnBatch(tok_start=packed[:len(ts)], slot=packed[len(ts):], mode=mode)
 
+    @staticmethod
+    def _cache_tokens(r: Request) -> List[int]:
+        """Prefix-cache key of a request's tokens: image rows enter as negative ids, so a page holding image KV
+        never matches text that happens to use the same placeholder ids."""
+        if not r.mm:
+            return r.tokens
+        t = list(r.tokens)
+        for pos, f in r.mm:
+            for i in range(pos, pos + f.shape[0]):
+                t[i] = -1 - t[i]
+        return t
+
     def _finish(self, r: Request) -> None:
         if self.hybrid and r.gslot >= 0:
             self.gdn_pool.release(r.gslot)
@@ -346,7 +369,7 @@ class LLMEngine:
         r.finished = True
         r.t_done = time.perf_counter()
         n_full = min(r.committed, len(r.tokens)) // self.ps
-        self.pool.prefix.insert(r.tokens, r.pages, n_full)
+        self.pool.prefix.insert(self._cache_tokens(r), r.pages, n_full)
         self.pool.prefix.release(r.pages)
         r.pages = []
 
@@ -388,8 +411,9 @@ class LLMEngine:
                 # prefix cache (and pages being written by requests earlier in this pass); hybrid models
                 # recompute prompts: a cached KV prefix carries no GDN state
                 n_match = (r.prompt_len - 1) // self.ps
-                keys = self.pool.prefix.chain_keys(r.tokens, self.ps, n_match)
-                pages = self.pool.prefix.match(r.tokens, (r.prompt_len - 1))
+                ctoks = self._cache_tokens(r)
+                keys = self.pool.prefix.chain_keys(ctoks, self.ps, n_match)
+                pages = self.pool.prefix.match(ctoks, (r.prompt_len - 1))
                 for k in keys[len(pages):]:
                     p = local_keys.get(k)
                     if p is None:
@@ -403,7 +427,7 @@ class LLMEngine:
             start = r.prefilled
             end = min(r.prompt_len, start + budget)
             self._ensure_pages(r, end)
-            for i, k in enumerate(self.pool.prefix.chain_keys(r.tokens, self.ps, end // self.ps)):
+            for i, k in enumerate(self.pool.prefix.chain_keys(self._cache_tokens(r), self.ps, end // self.ps)):
                 local_keys.setdefault(k, r.pages[i])
             batch.append((r, start, end))
             budget -= end - start
@@ -413,7 +437,14 @@ class LLMEngine:
             else:
                 break
         toks, pos, slots, last_rows = [], [], [], []
+        mm_rows, mm_feats = [], []
         for r, s, e in batch:
+            base = len(toks)
+            for ipos, f in r.mm:                  # image rows of this chunk get the image features
+                a, b = max(ipos, s), min(ipos + f.shape[0], e)
+                if a < b:
+                    mm_rows += list(range(base + a - s, base + b - s))
+                    mm_feats.append(f[a - ipos:b - ipos])
             toks += r.tokens[s:e]
             pos += list(range(s, e))
             slots += [self._slot(r, p) for p in range(s, e)]
@@ -425,6 +456,9 @@ class LLMEngine:
         fb = ForwardBatch(tokens=self._h2d(toks, torch.int64), positions=self._h2d(pos, torch.int32),
                           slots=self._h2d(slots, torch.int64), meta=meta, work2=pack_work(p2, g, self.device),
                           logits_rows=self._h2d(last_rows, torch.int64))
+        if mm_rows:
+            fb.mm_rows = self._h2d(mm_rows, torch.int64)
+            fb.mm_feats = torch.cat(mm_feats)
         if self.hybrid:
             fb.gdn = self._gdn_batch([e - s for _, s, e in batch], [r for r, _, _ in batch], "prefill")
         logits, h = self.target.forward(fb, want_hidden=True)

@@ -41,11 +41,12 @@ def _probs(logits: torch.Tensor, sp: SamplingParams) -> torch.Tensor:
                         torch.full((r,), sp.top_p))
 
 
-def greedy_generate(model: RefModel, prompt: List[int], n: int) -> List[int]:
-    """Target-only greedy decode: prefill the prompt, then one token per forward."""
+def greedy_generate(model: RefModel, prompt: List[int], n: int, embeds=None) -> List[int]:
+    """Target-only greedy decode: prefill the prompt, then one token per forward. embeds: (rows, features)
+    replacing those prompt rows' token embeddings (image inputs)."""
     kv = model.new_cache()
     toks = torch.tensor(prompt, dtype=torch.int64)
-    logits, _ = model.forward(toks, torch.arange(len(prompt)), kv)
+    logits, _ = model.forward(toks, torch.arange(len(prompt)), kv, embeds=embeds)
     out = [int(logits[-1].argmax())]
     while len(out) < n:
         pos = torch.tensor([kv.length()])

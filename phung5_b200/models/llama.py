@@ -265,6 +265,15 @@ class ForwardBatch:
     work2: tuple = None            # main pass (items, tiles)
     logits_rows: Optional[torch.Tensor] = None  # rows whose logits are needed (None = all)
     gdn: Optional[object] = None  # hybrid models: models.hybrid.GdnBatch (ragged token ranges, state slots, mode)
+    mm_rows: Optional[torch.Tensor] = None   # rows whose input embedding is an image feature (models/vision.py)
+    mm_feats: Optional[torch.Tensor] = None  # [len(mm_rows), H]
+
+    def embed(self, table: torch.Tensor) -> torch.Tensor:
+        """Input embeddings of the batch: token embeddings, image features at the image rows."""
+        h = table[self.tokens]
+        if self.mm_rows is not None:
+            h[self.mm_rows] = self.mm_feats.to(h.dtype)
+        return h
 
 
 class Communicator:
@@ -343,7 +352,7 @@ class LlamaModel:
         comm, cfg = self.comm, self.cfg
         m = fb.tokens.shape[0]
         h = comm.h(m)
-        h.copy_(self.w.embed[fb.tokens])
+        h.copy_(fb.embed(self.w.embed))
         fp8 = self.w.layers[0].qkv.fp8
         xq, xs, xb = ops.add_rmsnorm_quant(h, None, self.w.layers[0].in_norm, cfg.rms_eps, quant=fp8, out_bf16=not fp8)
         x = (xq, xs) if fp8 else xb
@@ -379,7 +388,7 @@ class LlamaModel:
         if (getattr(comm, "fused", False) and 0 < fb.tokens.shape[0] <= comm.max_tokens
                 and comm.hidden == self.cfg.hidden):
             return self.forward_fused(fb, want_hidden)
-        h = self.w.embed[fb.tokens]
+        h = fb.embed(self.w.embed)
         delta = None
         for li in range(self.cfg.num_layers):
             _nvtx.push(f"layer{li}")

@@ -159,13 +159,17 @@ class RefModel:
         return RefKV()
 
     def forward(self, tokens: torch.Tensor, positions: torch.Tensor, kv: RefKV,
-                mask: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
-        """tokens/positions [T] -> (logits [T, V] fp32, last-layer hidden before the final norm [T, H])."""
+                mask: Optional[torch.Tensor] = None, embeds: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
+                ) -> Tuple[torch.Tensor, torch.Tensor]:
+        """tokens/positions [T] -> (logits [T, V] fp32, last-layer hidden before the final norm [T, H]).
+        embeds: (rows, features) replacing those rows' token embeddings (image inputs)."""
         cfg, w = self.cfg, self.w
         t = tokens.shape[0]
         if mask is None:
             mask = causal_mask(kv.length(), t)
         x = w["model.embed_tokens.weight"].float()[tokens]
+        if embeds is not None:
+            x[embeds[0]] = embeds[1].float()
         for i in range(cfg.num_layers):
             x = decoder_layer(x, w, f"model.layers.{i}.", cfg, positions, kv, i, mask)
         hn = rms_norm(x, w["model.norm.weight"], cfg.rms_eps)

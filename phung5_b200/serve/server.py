@@ -8,7 +8,9 @@ per-request streams. Endpoints mirror what the reference's clients use of SGLang
   GET  /health                      200 while serving, 503 while asleep or after an engine error
   GET  /v1/models
   POST /v1/completions              prompt: str | [int]; max_tokens, temperature, top_p, top_k, seed, stream
-  POST /v1/chat/completions         messages (chat template of the tokenizer); same sampling fields
+  POST /v1/chat/completions         messages (chat template of the tokenizer); same sampling fields; with a vision
+                                    tower, `image_url` content parts (data URLs) -- sent once with a `uuid`, later
+                                    by `uuid` alone; an unknown uuid answers 400 so the client resends in full
   GET  /get_load                    {"num_running", "num_waiting"}
   GET  /metrics                     Prometheus text (tokens, accept length, step latency, TPOT)
   POST /sleep, /wake_up             weights to host memory and back (vLLM names)
@@ -44,6 +46,7 @@ class _Pending:
     out: "asyncio.Queue"
     loop: asyncio.AbstractEventLoop
     rid: int = -1
+    mm: Optional[list] = None          # image inputs: [(position, features [n, H])]
 
 
 class AsyncEngine:
@@ -86,7 +89,8 @@ class AsyncEngine:
                     except queue.Empty:
                         break
                 if self.group is not None:
-                    _broadcast_cmds({"ops": [o[0] for o in ops], "reqs": [(p.prompt, p.params) for p in subs],
+                    _broadcast_cmds({"ops": [o[0] for o in ops],
+                                     "reqs": [(p.prompt, p.params, _mm_to_host(p.mm)) for p in subs],
                                      "steps": self.steps, "stop": False}, self.group)
                 for op, fut, loop in ops:
                     try:
@@ -95,7 +99,7 @@ class AsyncEngine:
                     except Exception as e:  # pragma: no cover - surfaced to the caller
                         loop.call_soon_threadsafe(fut.set_exception, e)
                 for p in subs:
-                    p.rid = eng.add_request(p.prompt, p.params)
+                    p.rid = eng.add_request(p.prompt, p.params, mm=p.mm)
                     self._streams[p.rid] = p
                 if not eng.has_work():
                     self._wake.wait(0.05)
@@ -121,10 +125,10 @@ class AsyncEngine:
                 time.sleep(0.1)
 
     # -- asyncio side ---------------------------------------------------------------------------
-    async def generate(self, prompt: List[int], params: SamplingParams) -> AsyncIterator:
+    async def generate(self, prompt: List[int], params: SamplingParams, mm: Optional[list] = None) -> AsyncIterator:
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
-        self._submit.put(_Pending(prompt, params, q, loop))
+        self._submit.put(_Pending(prompt, params, q, loop, mm=mm))
         self._wake.set()
         while True:
             o = await q.get()
@@ -152,6 +156,11 @@ class AsyncEngine:
             _broadcast_cmds({"ops": [], "reqs": [], "steps": self.steps, "stop": True}, self.group)
 
 
+def _mm_to_host(mm):
+    """Image features travel to the other tensor-parallel ranks with the request (host copies)."""
+    return None if not mm else [(pos, f.detach().to("cpu")) for pos, f in mm]
+
+
 def _broadcast_cmds(cmds: Optional[dict], group) -> dict:
     import torch.distributed as dist
     box = [cmds]
@@ -170,8 +179,8 @@ def tp_worker_loop(engine, group) -> None:
             raise RuntimeError(f"TP ranks diverged: rank 0 took {cmds['steps']} steps, this rank {steps}")
         for op in cmds["ops"]:
             getattr(engine, op)()
-        for prompt, params in cmds["reqs"]:
-            engine.add_request(prompt, params)
+        for prompt, params, mm in cmds["reqs"]:
+            engine.add_request(prompt, params, mm=mm)
         if engine.has_work():
             engine.step()
             steps += 1
@@ -185,7 +194,51 @@ def _sampling(body: dict, default_max: int = 256) -> SamplingParams:
                                              or default_max))
 
 
-def build_app(aeng: AsyncEngine, tokenizer, model_name: str = "phung5_b200"):
+class UnknownImage(Exception):
+    """A content part referenced an image uuid the encoder cache does not hold (evicted or never sent)."""
+
+
+def encode_chat(tokenizer, messages: List[dict], vision=None, vocab: int = 0):
+    """Chat messages -> (token ids, image inputs [(position, features)]). Without image parts this is the
+    tokenizer's chat template. With them (and a vision encoder) each message is laid out as the role header, its
+    text parts, and for each image part the image's placeholder ids (models/vision.py), whose rows prefill
+    feeds with the image features. An image part is {"type": "image_url", "image_url": {"url": "data:..."}}
+    with an optional "uuid" (the client's key), or {"type": "image_url", "uuid": ...} alone for an image sent
+    before."""
+    has_image = any(isinstance(m.get("content"), list) and any(isinstance(p, dict) and p.get("type") == "image_url"
+                                                                for p in m["content"]) for m in messages)
+    if not has_image or vision is None:
+        return tokenizer.encode(tokenizer.apply_chat_template(messages)), []
+    from ..models.vision import image_placeholders
+    ids: List[int] = []
+    mm = []
+    for m in messages:
+        ids += tokenizer.encode(f"<|{m.get('role', 'user')}|>\n")
+        c = m.get("content", "")
+        parts = c if isinstance(c, list) else [{"type": "text", "text": c}]
+        for p in parts:
+            if not isinstance(p, dict):
+                continue
+            if p.get("type") == "image_url":
+                url = (p.get("image_url") or {}).get("url")
+                key = p.get("uuid")
+                if url:
+                    digest, feats = vision.encode(url, digest=key)
+                else:
+                    feats = vision.lookup(key) if key else None
+                    digest = key
+                    if feats is None:
+                        raise UnknownImage(key)
+                mm.append((len(ids), feats))
+                ids += image_placeholders(digest, feats.shape[0], vocab)
+            elif p.get("type") == "text":
+                ids += tokenizer.encode(p.get("text", ""))
+        ids += tokenizer.encode("\n")
+    ids += tokenizer.encode("<|assistant|>\n")
+    return ids, mm
+
+
+def build_app(aeng: AsyncEngine, tokenizer, model_name: str = "phung5_b200", vision=None):
     app = FastAPI(title="phung5_b200")
 
     @app.get("/health")
@@ -227,14 +280,14 @@ def build_app(aeng: AsyncEngine, tokenizer, model_name: str = "phung5_b200"):
     async def resume():
         return await _control("wake_up")
 
-    async def _complete(ids: List[int], body: dict, chat: bool):
+    async def _complete(ids: List[int], body: dict, chat: bool, mm: Optional[list] = None):
         sp = _sampling(body)
         rid = f"{'chatcmpl' if chat else 'cmpl'}-{uuid.uuid4().hex[:16]}"
         created = int(time.time())
         if body.get("stream"):
             async def events():
                 n = 0
-                async for o in aeng.generate(ids, sp):
+                async for o in aeng.generate(ids, sp, mm):
                     n += len(o.new_tokens)
                     text = tokenizer.decode(o.new_tokens)
                     if chat:
@@ -249,7 +302,7 @@ def build_app(aeng: AsyncEngine, tokenizer, model_name: str = "phung5_b200"):
                 yield "data: [DONE]\n\n"
             return StreamingResponse(events(), media_type="text/event-stream")
         toks: List[int] = []
-        async for o in aeng.generate(ids, sp):
+        async for o in aeng.generate(ids, sp, mm):
             toks += o.new_tokens
         text = tokenizer.decode(toks)
         usage = {"prompt_tokens": len(ids), "completion_tokens": len(toks), "total_tokens": len(ids) + len(toks)}
@@ -272,8 +325,12 @@ def build_app(aeng: AsyncEngine, tokenizer, model_name: str = "phung5_b200"):
     @app.post("/v1/chat/completions")
     async def chat(req: Request):
         body = await req.json()
-        ids = tokenizer.encode(tokenizer.apply_chat_template(body.get("messages", [])))
-        return await _complete(ids, body, chat=True)
+        try:
+            ids, mm = encode_chat(tokenizer, body.get("messages", []), vision, aeng.engine.cfg.model.vocab)
+        except UnknownImage as e:
+            return JSONResponse({"error": f"unknown image uuid {e.args[0]!r}: send the image in full"},
+                                status_code=400)
+        return await _complete(ids, body, chat=True, mm=mm)
 
     return app
 
@@ -289,6 +346,7 @@ def main(argv=None):
     ap.add_argument("--model-path", default=None,
                     help="HF checkpoint directory (config.json + safetensors); overrides --model's random weights")
     ap.add_argument("--draft-path", default=None, help="EAGLE head checkpoint directory (else a random head)")
+    ap.add_argument("--vision", action="store_true", help="serve image inputs with a (seeded random) vision tower")
     ap.add_argument("--num-pages", type=int, default=0)
     ap.add_argument("--comm", default="fused", choices=["nccl", "fused"],
                     help="tensor-parallel collectives when launched with torchrun over several GPUs")
@@ -326,9 +384,15 @@ def main(argv=None):
         tp_worker_loop(eng, group)
         return
     aeng = AsyncEngine(eng, group=group)
+    vision = None
+    if args.vision:
+        import torch
+        from ..models.vision import VisionConfig, VisionEncoder
+        vision = VisionEncoder(VisionConfig(out_hidden=model_cfg.hidden), device=device,
+                               dtype=torch.bfloat16 if str(device).startswith("cuda") else torch.float32)
     uvicorn.run(build_app(aeng, __import__("phung5_b200.serve.tokenizer", fromlist=["load_tokenizer"]).load_tokenizer(
-        args.tokenizer), model_cfg.name if args.model_path else args.model), host=args.host, port=args.port,
-        log_level="warning")
+        args.tokenizer), model_cfg.name if args.model_path else args.model, vision=vision), host=args.host,
+        port=args.port, log_level="warning")
     aeng.shutdown()
 
 
