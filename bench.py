@@ -35,16 +35,21 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "output tok/s at Llama-3-70B FP8 TP8 spec decode, max over ranks; p50 TPOT"
+# Mixtral-8x7B FP8 MoE (EP over the GPUs, attention tensor-parallel), k=4 chain speculation, batch 128 x 2048-token
+# prompts, 128 output tokens: `--workload mixtral`
+MIXTRAL_METRIC = "output tok/s at Mixtral-8x7B FP8 EP8 spec decode (k=4 chain), max over ranks; p50 TPOT"
+WORKLOADS = {"mixtral": dict(model="mixtral-8x7b-fp8", batch=128, prefix=0, suffix=2048, out_tokens=128, mode="chain",
+                             num_draft=4)}
 
 
-def reference_arm(args):
+def reference_arm(args, metric=METRIC):
     """The reference (huypg-zenai/phung5) is an application around external SGLang/vLLM engines: it has no
     setup.py/pyproject (pip refuses to install it) and its inference engines are downloaded at container
     start, so its own serving path cannot run offline here."""
     line = {"impl": "reference",
             "unavailable": "reference is not installable (no setup.py/pyproject.toml) and its SGLang/vLLM "
                            "engines are fetched from the network at start; no offline build of its serving path",
-            "metric": METRIC, "n_gpus": args.gpus}
+            "metric": metric, "n_gpus": args.gpus}
     print(json.dumps(line))
 
 
@@ -121,6 +126,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default=None, choices=[None, *WORKLOADS],
+                    help="a named workload preset (overrides model / batch / prompt / spec flags)")
     ap.add_argument("--model", default="llama3-70b-fp8")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--prefix", type=int, default=4096)
@@ -137,9 +144,14 @@ def main():
     ap.add_argument("--model-path", default=None, help="HF checkpoint directory instead of random-init weights")
     ap.add_argument("--draft-path", default=None, help="EAGLE head checkpoint directory (with --model-path)")
     args = ap.parse_args()
+    metric = METRIC
+    if args.workload:
+        for k, v in WORKLOADS[args.workload].items():
+            setattr(args, k, v)
+        metric = MIXTRAL_METRIC
 
     if args.impl == "reference":
-        reference_arm(args)
+        reference_arm(args, metric)
         return
 
     from phung5_b200 import ops
@@ -184,7 +196,7 @@ def main():
     t_init = time.time() - t0
 
     g = torch.Generator().manual_seed(1234)
-    prefix = torch.randint(0, mc.vocab, (args.prefix,), generator=g).tolist()
+    prefix = torch.randint(0, mc.vocab, (args.prefix,), generator=g).tolist() if args.prefix else []
     prompts = [prefix + torch.randint(0, mc.vocab, (args.suffix,), generator=g).tolist() for _ in range(args.batch)]
     sp = SamplingParams(temperature=0.0, max_new_tokens=args.out_tokens)
     for p in prompts:
@@ -253,7 +265,7 @@ def main():
     value = tokens / (ms / 1e3)
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "metric": metric, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp8_block+bf16",
             "data": "synthetic token ids, " + ("checkpoint weights" if args.model_path else "random-init weights")

@@ -643,7 +643,7 @@ class LLMEngine:
     def _spec_graph(self, R: int, mode: str, reqs: List[Request]):
         """The CUDA-graph runner for this batch shape and accept mode, or None to run the step eagerly. Seeded
         sampling is captured when the device accept path serves every request."""
-        if (self._graphs is None or self.K <= 1 or not self.eagle or self._has_moe or self.hybrid
+        if (self._graphs is None or not self.eagle or self.hybrid
                 or (self.comm.size != 1 and not getattr(self.comm, "fused", False))
                 or (mode == "sample" and not self._device_sampling(reqs))):
             return None

@@ -20,7 +20,8 @@ per request) runs eagerly and hands its root logits and features to the graph th
 Used for greedy, synthetic (geometric) and seeded-sampling acceptance on dense models, at TP1 and on the
 fused tensor-parallel communicator (the sampled graph needs every request on the device accept path: greedy or
 1 <= top_k <= 64; its per-request temperature, top_k, top_p and seed are static buffers filled per step). MoE
-(data-dependent routing), hybrid GDN models and the NCCL communicator run the same `_spec_core` eagerly.
+layers are captured too (routing, expert sort and segment offsets are device-side and sync-free); hybrid GDN
+models and the NCCL communicator run the same `_spec_core` eagerly.
 """
 from __future__ import annotations
 

@@ -67,7 +67,10 @@ class MoEBlock:
         local = (flat >= 0) & (flat < el)
         key = torch.where(local, flat, torch.full_like(flat, el))  # non-local assignments sort last
         order = torch.argsort(key, stable=True)                    # permuted position -> assignment
-        counts = torch.bincount(key, minlength=el + 1)[:el]
+        # counts by scatter-add (torch.bincount reads the maximum back to the host): no synchronisation, so
+        # the MoE step can be captured in a CUDA graph
+        counts = torch.zeros(el + 1, dtype=torch.int64, device=xb.device).scatter_add_(
+            0, key, torch.ones_like(key))[:el]
         offsets = torch.zeros(el + 1, dtype=torch.int32, device=xb.device)
         offsets[1:] = torch.cumsum(counts, 0).to(torch.int32)
         tok = order // k                                          # token of each permuted row

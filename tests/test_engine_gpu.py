@@ -108,13 +108,15 @@ def test_engine_geometric_synthetic_acceptance():
     assert 1.2 < mean_acc < 3.0, mean_acc   # E[min(Geom(0.3), 6)] ~= 2.06
 
 
-@pytest.mark.parametrize("accept", ["greedy", "geometric"])
-def test_graph_replayed_step_equals_eager_step(accept, monkeypatch):
+@pytest.mark.parametrize("accept,model,mode", [("greedy", "small-fp8", "tree"), ("geometric", "small-fp8", "tree"),
+                                               ("greedy", "small-fp8", "chain"), ("geometric", "small-moe-fp8", "chain"),
+                                               ("greedy", "small-moe-fp8", "tree")])
+def test_graph_replayed_step_equals_eager_step(accept, model, mode, monkeypatch):
     """The CUDA-graph speculative step (static buffers, device-built metadata) must emit exactly the tokens
     of the eager step: same kernels on the same inputs. 16 requests sharing a 128-token prefix (cascade
-    groups)."""
-    cfg = preset("small-fp8")
-    kw = dict(mode="tree", tree_nodes=64, topk=8, depth=6)
+    groups); tree and chain speculation, dense and MoE models (routing on the device inside the graph)."""
+    cfg = preset(model)
+    kw = dict(mode="tree", tree_nodes=64, topk=8, depth=6) if mode == "tree" else dict(mode="chain", num_draft=4)
     if accept == "geometric":
         kw["accept"] = "geometric"
     prompts = _prompts(16, 256, cfg.vocab, seed=4, shared=128)
