@@ -857,7 +857,7 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tenso
 // Row-parallel projection with the scatter epilogue (see ScatterArgs): fp8 (ws defined) or bf16 operands.
 void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tensor w, c10::optional<torch::Tensor> ws,
                   torch::Tensor peer_base, int64_t off_recv, int64_t rows_per, int64_t rank, torch::Tensor status,
-                  bool hws, bool pair) {
+                  bool hws, bool pair, int64_t bn) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && peer_base.is_cuda() && peer_base.scalar_type() == at::kLong);
   const int M = x.size(0), K = x.size(1), N = w.size(0);
   TORCH_CHECK(w.size(1) == K && N % 8 == 0 && x.stride(1) == 1 && w.stride(1) == 1);
@@ -867,7 +867,7 @@ void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tenso
   auto stream = at::cuda::getCurrentCUDAStream();
   const ScatterArgs sc{reinterpret_cast<const uint64_t*>(peer_base.data_ptr<int64_t>()), (uint64_t)off_recv,
                        (int)rows_per, (int)rank};
-  const int b = pick_bn(M, N);
+  const int b = bn > 0 ? (int)bn : pick_bn(M, N);
   if (ws.has_value()) {
     TORCH_CHECK(x.scalar_type() == at::kFloat8_e4m3fn && w.scalar_type() == at::kFloat8_e4m3fn && K % 128 == 0);
     TORCH_CHECK(xs->is_contiguous() && xs->size(0) == K / 128 && xs->size(1) == M);
@@ -875,7 +875,7 @@ void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tenso
     const float* sa = xs->data_ptr<float>();
     const float* sb = ws->data_ptr<float>();
     int* st = status.data_ptr<int>();
-    if (hws && !pair && prefer_promote(b, K)) hws = false;
+    if (hws && !pair && bn <= 0 && prefer_promote(b, K)) hws = false;
     if (hws) {
       if (b == 256 && pair && M > kBM)
         launch_gemm_ptr<256, true, true, true, true>(x, w, nullptr, N, N, sa, sb, st, stream, 0, nullptr, 0, sc);

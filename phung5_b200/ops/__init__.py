@@ -149,15 +149,31 @@ SWIGLU_FUSED = os.environ.get("PHX_SWIGLU_FUSED", "1") != "0"
 GEMM_PAIR = os.environ.get("PHX_GEMM_PAIR", "0") == "1"
 
 
+def _table_choice(kind: str, n: int, k: int, m: int, bn: int, hw_scale, pair, use_table: bool):
+    """The measured per-shape configuration (ops/gemm_table.json) unless the caller chose one."""
+    if not use_table or bn or hw_scale is not None or pair is not None:
+        return bn, hw_scale, pair
+    from . import gemm_table
+    e = gemm_table.lookup(kind, n, k, m)
+    if e is None:
+        return bn, hw_scale, pair
+    hws = e.get("hws")
+    if hws is not None and not FP8_HW_SCALE:
+        hws = False            # arbitrary-scale mode: never hand scales to the hardware path
+    return int(e["bn"]), hws, e.get("pair")
+
+
 def gemm_fp8_block(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
                    out: Optional[torch.Tensor] = None, bn: int = 0, max_ctas: int = 0,
-                   hw_scale: Optional[bool] = None, pair: Optional[bool] = None) -> torch.Tensor:
+                   hw_scale: Optional[bool] = None, pair: Optional[bool] = None, use_table: bool = True) -> torch.Tensor:
     """Block-scaled FP8 linear: xq [M,K] e4m3, xs [K/128, M] fp32, wq [N,K] e4m3, ws [N/128, K/128]
-    fp32 -> bf16 [M, N]. hw_scale (default FP8_HW_SCALE) needs power-of-two scales."""
+    fp32 -> bf16 [M, N]. hw_scale (default FP8_HW_SCALE) needs power-of-two scales. Unless bn / hw_scale / pair
+    are given, the measured per-shape table (ops/gemm_table.py) picks them."""
     m, n = xq.shape[0], wq.shape[0]
     if out is None:
         out = torch.empty(m, n, dtype=torch.bfloat16, device=xq.device)
     if xq.is_cuda:
+        bn, hw_scale, pair = _table_choice("fp8", n, xq.shape[1], m, bn, hw_scale, pair, use_table)
         hws = FP8_HW_SCALE if hw_scale is None else hw_scale
         ext().gemm_fp8_block(xq, xs, wq, ws, out, status_tensor(xq.device), bn, max_ctas, hws,
                              GEMM_PAIR if pair is None else pair)
@@ -167,11 +183,12 @@ def gemm_fp8_block(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: tor
 
 
 def gemm_bf16(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None, bn: int = 0,
-              max_ctas: int = 0) -> torch.Tensor:
+              max_ctas: int = 0, use_table: bool = True) -> torch.Tensor:
     """x [M,K] bf16 @ w [N,K]^T -> bf16 [M,N] (fp32 accumulate)."""
     if out is None:
         out = torch.empty(x.shape[0], w.shape[0], dtype=torch.bfloat16 if x.is_cuda else x.dtype, device=x.device)
     if x.is_cuda:
+        bn, _, _ = _table_choice("bf16", w.shape[0], x.shape[1], x.shape[0], bn, None, None, use_table)
         ext().gemm_bf16(x, w, out, status_tensor(x.device), bn, max_ctas)
     else:
         out.copy_((x.float() @ w.float().t()).to(out.dtype))

@@ -448,11 +448,11 @@ def test_gemm_scatter_epilogue(fp8, m, n, k, hws):
     if fp8:
         xq, xs = quant_act_block(x)
         wq, ws = quant_weight_block(w)
-        ops.ext().gemm_scatter(xq, xs, wq, ws, base, 0, rows_per, rank, ops.status_tensor(DEV), hws, False)
+        ops.ext().gemm_scatter(xq, xs, wq, ws, base, 0, rows_per, rank, ops.status_tensor(DEV), hws, False, 0)
         ref = ops.gemm_fp8_block(xq, xs, wq, ws, hw_scale=hws)
     else:
         xb, wb = x.bfloat16(), w.bfloat16()
-        ops.ext().gemm_scatter(xb, None, wb, None, base, 0, rows_per, rank, ops.status_tensor(DEV), False, False)
+        ops.ext().gemm_scatter(xb, None, wb, None, base, 0, rows_per, rank, ops.status_tensor(DEV), False, False, 0)
         ref = ops.gemm_bf16(xb, wb)
     torch.cuda.synchronize()
     for o in range(world):
