@@ -3,9 +3,9 @@
 
 namespace phx {
 void gemm_fp8_block(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor out,
-                    torch::Tensor status, int64_t bn, int64_t max_ctas, bool hws, bool pair);
+                    torch::Tensor status, int64_t bn, int64_t max_ctas, bool hws, bool pair, int64_t split);
 void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tensor status, int64_t bn,
-               int64_t max_ctas);
+               int64_t max_ctas, int64_t split);
 void add_rmsnorm_quant(torch::Tensor h, c10::optional<torch::Tensor> delta, torch::Tensor w, double eps,
                        c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> qs,
                        c10::optional<torch::Tensor> out);

@@ -28,6 +28,7 @@ enum : int {
   kErrTimeoutPeer = 4,
   kErrBadArgs = 5,
   kErrScaleNotPow2 = 6,   // a block scale handed to the hardware-scaled GEMM is not a positive power of two
+  kErrTimeoutSplit = 7,   // a split-K GEMM part waited too long for the other parts of its tile
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

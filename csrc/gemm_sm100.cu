@@ -72,8 +72,10 @@ struct GemmSmem {
   uint64_t tempty[512 / BN];
   uint64_t done;
   uint64_t up_ready, up_free;   // SWIGLU epilogue: up-half warps -> gate-half warps hand-off of staged rows
+  uint64_t split_bar;           // split-K epilogue: the epilogue warps' barrier (kEpiWarps arrivals a phase)
   uint32_t tmem_base;
   int abort;
+  int split_ok;
 };
 
 // the scatter epilogue stages each warp's 32 output rows in shared memory (8 warps x 32 rows x (BN/2 + 8)
@@ -154,13 +156,67 @@ struct SwigluArgs {
   int F;
 };
 
+// Split-K tail of a plain GEMM whose tile count leaves the last wave of the persistent grid mostly idle
+// (fewer tiles than SMs, or a few tiles past a whole number of waves: Llama-3-70B qkv at TP8 has 160 tiles of
+// 128 x 256 for 148 SMs, the draft rounds' M = 512 GEMMs 20-40 tiles). Tiles [0, dp_tiles) run whole; each
+// later tile is cut into `splits` contiguous K ranges, one work item each. dp_tiles is a multiple of the grid
+// size and the split items number at most the grid size, so every CTA takes at most one split item and takes
+// it in its last round: all parts of a split tile run at the same time (one CTA per SM, grid <= SMs). Each
+// part stores its fp32 partial tile into a workspace slot in epilogue-thread order (coalesced), arrives on
+// the tile's counter, waits (bounded) for the other parts, then sums one 1/splits share of the tile over all
+// parts (L2-resident reads) and stores it as bf16. The last part to leave zeroes the tile's counters for the
+// next launch. splits <= 1: every tile whole (the other epilogues always run that way).
+struct SplitArgs {
+  float* ws;        // [split tiles x splits][BN/8][256] float4 partials
+  int* cnt;         // [2 x split tiles] arrive / depart counters, zero between launches
+  int dp_tiles;
+  int splits;
+};
+
+struct WorkItem {
+  int t, kb0, kb1, part;   // tile, K-step range [kb0, kb1), part index (-1: whole tile)
+};
+
+__device__ __forceinline__ WorkItem work_item(int i, int ksteps, const SplitArgs& sk) {
+  WorkItem w;
+  if (sk.splits <= 1 || i < sk.dp_tiles) {
+    w.t = i;
+    w.kb0 = 0;
+    w.kb1 = ksteps;
+    w.part = -1;
+    return w;
+  }
+  const int j = i - sk.dp_tiles;
+  w.t = sk.dp_tiles + j / sk.splits;
+  w.part = j % sk.splits;
+  w.kb0 = (int)((long long)w.part * ksteps / sk.splits);
+  w.kb1 = (int)((long long)(w.part + 1) * ksteps / sk.splits);
+  return w;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void epi_bar_sync() {   // the kEpiWarps epilogue warps only (named barrier 1)
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
+}
+
+// Workspace of the split-K tail: statically allocated device memory (no allocation at call time, so the
+// split path is also safe inside CUDA-graph capture). kMaxSplitItems parts of up to 128 x 256 fp32.
+constexpr int kMaxSplitItems = 160;
+__device__ __align__(256) float g_split_ws[(size_t)kMaxSplitItems * kBM * 256];
+__device__ __align__(16) int g_split_cnt[2 * kMaxSplitItems];
+
 template <int BN, bool FP8, bool SCATTER, bool HWS, bool PAIR, bool SWIGLU = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       __nv_bfloat16* __restrict__ out, int M, int N, int K, int ldc, const float* __restrict__ sa,
                       const float* __restrict__ sb, int* status, const int* __restrict__ grp_off, int groups,
                       int max_tiles, const ScatterArgs sc, const int* __restrict__ a_rows, int sa_ld,
-                      const SwigluArgs sw) {
+                      const SwigluArgs sw, const SplitArgs sk) {
   static_assert(!HWS || FP8, "hardware scaling is an fp8 mode");
   static_assert(!PAIR || (HWS && BN == 256), "CTA pairs run the hardware-scaled 256-wide tile");
   static_assert(!SWIGLU || (HWS && BN == 256 && !PAIR && !SCATTER), "SwiGLU epilogue: single-CTA hardware-scaled BN=256");
@@ -194,6 +250,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int num_tiles = grp_off ? max_tiles : m_tiles * n_tiles;
   const int ksteps = K / BKE;          // smem stages per tile
   const int kblocks = K / 128;         // scale blocks (fp8)
+  // work items: whole tiles, then the split tiles' K ranges (sk.splits <= 1: one item per tile)
+  const int num_items = sk.splits > 1 ? sk.dp_tiles + (num_tiles - sk.dp_tiles) * sk.splits : num_tiles;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -207,7 +265,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init(&s.done, 1);
     mbar_init(&s.up_ready, 4);   // the four up-half epilogue warps
     mbar_init(&s.up_free, 4);    // the four gate-half epilogue warps
+    mbar_init(&s.split_bar, kEpiWarps);
     s.abort = 0;
+    s.split_ok = 0;
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
@@ -244,7 +304,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ahead; srow are the cursor tile's scale rows for this lane.
     constexpr int LA = 4;
     float fa_r[LA][4], fb_r[LA][BN / 128];
-    int la_t = unit, la_ks = 0;
+    int la_i = unit, la_ks = -1;   // cursor: work item, K step (-1: item not started)
+    WorkItem la_w{0, 0, 0, -1};
     int srow[4] = {0, 0, 0, 0};
     TileInfo la_ti;
     la_ti.valid = false;
@@ -253,9 +314,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int c = 0; c < 4; ++c) fa[c] = 1.f;
 #pragma unroll
       for (int g = 0; g < BN / 128; ++g) fb[g] = 1.f;
-      if (la_t >= num_tiles) return;
-      if (la_ks == 0) {
-        la_ti = tile_info<BN, BMT>(la_t, M, N, m_tiles, n_tiles, grp_off, groups);
+      if (la_i >= num_items) return;
+      if (la_ks < 0) {
+        la_w = work_item(la_i, ksteps, sk);
+        la_ks = la_w.kb0;
+        la_ti = tile_info<BN, BMT>(la_w.t, M, N, m_tiles, n_tiles, grp_off, groups);
         if (la_ti.valid) {
 #pragma unroll
           for (int c = 0; c < 4; ++c) srow[c] = src_row(la_ti.m0 + my_row0 + 32 * c + lane);
@@ -271,7 +334,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           fb[g] = sb[(size_t)(nb < nb_last ? nb : nb_last) * kblocks + la_ks];
         }
       }
-      if (++la_ks == ksteps) la_ks = 0, la_t += units;
+      if (++la_ks == la_w.kb1) la_ks = -1, la_i += units;
     };
     int g4[4] = {0, 0, 0, 0};
     auto ue8m0 = [&](float v) -> uint32_t {
@@ -281,15 +344,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     };
 #pragma unroll
     for (int j = 0; j < LA; ++j) la_load(fa_r[j], fb_r[j]);
-    for (int t = unit; t < num_tiles && !*abort; t += units) {
-      const TileInfo ti = tile_info<BN, BMT>(t, M, N, m_tiles, n_tiles, grp_off, groups);
+    for (int it = unit; it < num_items && !*abort; it += units) {
+      const WorkItem wi = work_item(it, ksteps, sk);
+      const TileInfo ti = tile_info<BN, BMT>(wi.t, M, N, m_tiles, n_tiles, grp_off, groups);
       if (!ti.valid) break;
       if (a_rows) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) g4[i] = src_row(ti.m0 + 4 * lane + i);
       }
       bool ok = true;
-      for (int ks = 0; ks < ksteps; ++ks) {
+      for (int ks = wi.kb0; ks < wi.kb1; ++ks) {
         const uint4 wa = make_uint4(ue8m0(fa_r[0][0]), ue8m0(fa_r[0][1]), ue8m0(fa_r[0][2]), ue8m0(fa_r[0][3]));
         uint32_t wb[BN / 128];
 #pragma unroll
@@ -352,10 +416,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int t = unit; t < num_tiles && !*abort; t += units) {
-        const TileInfo ti = tile_info<BN, BMT>(t, M, N, m_tiles, n_tiles, grp_off, groups);
+      for (int it = unit; it < num_items && !*abort; it += units) {
+        const WorkItem wi = work_item(it, ksteps, sk);
+        const TileInfo ti = tile_info<BN, BMT>(wi.t, M, N, m_tiles, n_tiles, grp_off, groups);
         if (!ti.valid) break;
-        for (int ks = 0; ks < ksteps; ++ks) {
+        for (int ks = wi.kb0; ks < wi.kb1; ++ks) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1, status, kErrTimeoutProducer, abort)) break;
           mbar_arrive_expect_tx(&s.full[stage], (kBM + BN) * 128);
           tma_load_2d(&tmA, &s.full[stage], s.a[stage], ks * BKE, ti.m0);
@@ -378,11 +443,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int tb = 0;
       uint32_t tphase = 0;
-      for (int t = unit; t < num_tiles && !*abort; t += units) {
-        if (grp_off && !tile_info<BN, BMT>(t, M, N, m_tiles, n_tiles, grp_off, groups).valid) break;
-        for (int ks = 0; ks < ksteps; ++ks) {
-          const bool new_acc = PROMOTE || ks == 0;
-          const bool end_acc = PROMOTE || ks == ksteps - 1;
+      for (int it = unit; it < num_items && !*abort; it += units) {
+        const WorkItem wi = work_item(it, ksteps, sk);
+        if (grp_off && !tile_info<BN, BMT>(wi.t, M, N, m_tiles, n_tiles, grp_off, groups).valid) break;
+        for (int ks = wi.kb0; ks < wi.kb1; ++ks) {
+          const bool new_acc = PROMOTE || ks == wi.kb0;
+          const bool end_acc = PROMOTE || ks == wi.kb1 - 1;
           if (new_acc) {
             if (!mbar_wait<PAIR>(&s.tempty[tb], tphase ^ 1, status, kErrTimeoutMma, abort)) goto mma_done;
             tc_fence_after();
@@ -469,9 +535,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       sa_next = sa[(size_t)kb * M + (rr < M ? rr : M - 1)];
       sb_next = c0 < N ? sb[(size_t)(ti.sb_base + (c0 >> 7)) * kblocks + kb] : 0.f;
     };
-    load_scales(t, 0);
-    for (; t < num_tiles && !*abort; t += units) {
-      const TileInfo ti = tile_info<BN, BMT>(t, M, N, m_tiles, n_tiles, grp_off, groups);
+    load_scales(t, 0);   // (software promotion never splits: items are tiles there)
+    uint32_t split_phase = 0;
+    for (; t < num_items && !*abort; t += units) {
+      const WorkItem wi = work_item(t, ksteps, sk);
+      const TileInfo ti = tile_info<BN, BMT>(wi.t, M, N, m_tiles, n_tiles, grp_off, groups);
       if (!ti.valid) break;
       const int row = ti.m0 + my_row0 + sub * 32 + lane;
       const int col0 = ti.n0 + half * CPT;
@@ -510,6 +578,80 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           else mbar_arrive(&s.tempty[tb]);
         }
         if (++tb == NBUF) tb = 0, tphase ^= 1;
+      }
+      if constexpr (!SCATTER && !SWIGLU && !PAIR && !PROMOTE) {
+        if (wi.part >= 0) {
+          // ---- split-K part: publish the fp32 partial, meet the tile's other parts, sum a share ----
+          constexpr int ET = kEpiWarps * 32;            // epilogue threads
+          constexpr int F4 = (CPT / 4) * ET;            // float4s per tile
+          const int et = ew * 32 + lane;
+          const int sti = wi.t - sk.dp_tiles;
+          float4* wsb = reinterpret_cast<float4*>(sk.ws) + (size_t)sti * sk.splits * F4;
+          float4* mine = wsb + (size_t)wi.part * F4;
+#pragma unroll
+          for (int c4 = 0; c4 < CPT / 4; ++c4)
+            __stcg(mine + c4 * ET + et,
+                   make_float4(acc[2 * c4].x, acc[2 * c4].y, acc[2 * c4 + 1].x, acc[2 * c4 + 1].y));
+          __threadfence();
+          auto epi_sync = [&]() -> bool {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.split_bar);
+            const bool ok = mbar_wait(&s.split_bar, split_phase, status, kErrTimeoutSplit, abort);
+            split_phase ^= 1;
+            return __all_sync(0xffffffffu, ok);
+          };
+          if (!epi_sync()) goto epi_done;
+          if (et == 0) {
+            int* arrive = sk.cnt + 2 * sti;
+            __threadfence();
+            atomicAdd(arrive, 1);
+            bool ok = true;
+            const uint64_t t0 = globaltimer();
+            while (ld_acquire_gpu(arrive) < sk.splits) {
+              if (*abort || globaltimer() - t0 > PHX_WAIT_TIMEOUT_NS) {
+                ok = false;
+                break;
+              }
+            }
+            if (!ok) {
+              atomicCAS(status, 0, kErrTimeoutSplit);
+              *abort = 1;
+            }
+            s.split_ok = ok;
+          }
+          if (!epi_sync() || !s.split_ok) goto epi_done;
+          __threadfence();
+          const int lo = (int)((long long)wi.part * F4 / sk.splits);
+          const int hi = (int)((long long)(wi.part + 1) * F4 / sk.splits);
+          for (int f = lo + et; f < hi; f += ET) {
+            float4 v = __ldcg(wsb + f);
+            for (int q = 1; q < sk.splits; ++q) {
+              const float4 u = __ldcg(wsb + (size_t)q * F4 + f);
+              v.x += u.x;
+              v.y += u.y;
+              v.z += u.z;
+              v.w += u.w;
+            }
+            const int e = f % ET, c4 = f / ET, eew = e >> 5;
+            const int r = ti.m0 + ((eew + 2) & 3) * 32 + (e & 31);      // that thread's TMEM lane quarter
+            const int c = ti.n0 + (eew >> 2) * CPT + 4 * c4;             // and column half
+            if (r < M && c < N) {
+              uint2 o;
+              o.x = pack_bf16x2(v.x, v.y);
+              o.y = pack_bf16x2(v.z, v.w);
+              *reinterpret_cast<uint2*>(out + (size_t)r * ldc + c) = o;
+            }
+          }
+          if (!epi_sync()) goto epi_done;   // this CTA's reads of the tile's partials are done
+          if (et == 0) {
+            __threadfence();
+            if (atomicAdd(sk.cnt + 2 * sti + 1, 1) == sk.splits - 1) {   // last part out: reset for the next launch
+              sk.cnt[2 * sti] = 0;
+              sk.cnt[2 * sti + 1] = 0;
+            }
+          }
+          continue;
+        }
       }
       if constexpr (SWIGLU) {
         // up-half warps stage their rows' up values (bf16) in shared memory; gate-half warps combine them with
@@ -638,11 +780,39 @@ int num_sms() {
   return n;
 }
 
+// Parts per split tile of the split-K tail (1: no split). req: 0 = automatic, 1 = off, >= 2 = that many parts
+// (clamped). Automatic: split when the last wave of tiles leaves at least half the SMs idle and the tile has
+// at least 16 K steps (shorter tiles do not repay the partial-tile round trip through L2).
+static int split_parts(int tiles, int ksteps, int P, int req) {
+  const int rem = tiles % P;
+  if (req == 1 || rem == 0) return 1;
+  int parts = req >= 2 ? req : (ksteps >= 16 ? P / rem : 1);
+  parts = std::min(parts, P / rem);                 // every split item in the grid's last round
+  parts = std::min(parts, ksteps / 2);              // at least two K steps per part
+  parts = std::min(parts, kMaxSplitItems / rem);    // workspace
+  return parts >= 2 ? parts : 1;
+}
+
+// This device's copy of the split-K workspace (the device symbols' addresses in the current context).
+static SplitArgs split_workspace(int dev) {
+  static float* ws[64] = {};
+  static int* cnt[64] = {};
+  if (!ws[dev]) {
+    void* a = nullptr;
+    void* c = nullptr;
+    C10_CUDA_CHECK(cudaGetSymbolAddress(&a, g_split_ws));
+    C10_CUDA_CHECK(cudaGetSymbolAddress(&c, g_split_cnt));
+    cnt[dev] = static_cast<int*>(c);
+    ws[dev] = static_cast<float*>(a);
+  }
+  return SplitArgs{ws[dev], cnt[dev], 0, 1};
+}
+
 template <int BN, bool FP8, bool SCATTER = false, bool HWS = false, bool PAIR = false, bool SWIGLU = false>
 void launch_gemm_ptr(const torch::Tensor& a, const torch::Tensor& b, __nv_bfloat16* out_ptr, int ldc, int n_out,
                      const float* sa, const float* sb, int* status, cudaStream_t stream, int max_ctas,
                      const int* grp_off, int groups, ScatterArgs sc, const int* a_rows = nullptr, int m_rows = 0,
-                     SwigluArgs sw = SwigluArgs{nullptr, nullptr, 0}) {
+                     SwigluArgs sw = SwigluArgs{nullptr, nullptr, 0}, int split = 1) {
   static_assert(!PAIR || HWS, "CTA pairs run the hardware-scaled kernel");
   // a_rows: GEMM row r reads activation row a_rows[r] (m_rows GEMM rows; `a` holds the activations and `sa`
   // their scales [K/128, a.size(0)]); A is fetched by TMA gather4 with a one-row box
@@ -703,11 +873,26 @@ void launch_gemm_ptr(const torch::Tensor& a, const torch::Tensor& b, __nv_bfloat
     int pairs = std::min(tiles, max_ctas > 0 ? std::max(1, max_ctas / 2) : max_pairs);
     cfg.gridDim = dim3(2 * pairs);
     C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, out_ptr, M, N, K, ldc, sa, sb, status, grp_off, groups,
-                                      tiles, sc, a_rows, sa_ld, sw));
+                                      tiles, sc, a_rows, sa_ld, sw, SplitArgs{nullptr, nullptr, 0, 1}));
   } else {
-    int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
+    // split-K tail: plain GEMMs with bf16 output and the whole K range in TMEM (bf16, hardware-scaled fp8)
+    SplitArgs sk{nullptr, nullptr, 0, 1};
+    int items = tiles;
+    constexpr bool kCanSplit = !SCATTER && !SWIGLU && (HWS || !FP8);
+    if (kCanSplit && !grp_off && !a_rows && max_ctas <= 0 && split != 1) {
+      const int P = num_sms();
+      const int parts = split_parts(tiles, K / (FP8 ? 128 : 64), P, split);
+      if (parts > 1) {
+        const int rem = tiles % P;
+        sk = split_workspace(dev);
+        sk.dp_tiles = tiles - rem;
+        sk.splits = parts;
+        items = tiles - rem + rem * parts;
+      }
+    }
+    int grid = std::min(items, max_ctas > 0 ? max_ctas : num_sms());
     kern<<<grid, kGemmThreads, smem, stream>>>(ta, tb, out_ptr, M, N, K, ldc, sa, sb, status, grp_off, groups, tiles,
-                                               sc, a_rows, sa_ld, sw);
+                                               sc, a_rows, sa_ld, sw, sk);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
@@ -715,10 +900,10 @@ void launch_gemm_ptr(const torch::Tensor& a, const torch::Tensor& b, __nv_bfloat
 template <int BN, bool FP8, bool HWS = false, bool PAIR = false>
 void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, const float* sa,
                  const float* sb, int* status, cudaStream_t stream, int max_ctas, const int* grp_off = nullptr,
-                 int groups = 0) {
+                 int groups = 0, int split = 1) {
   launch_gemm_ptr<BN, FP8, false, HWS, PAIR>(a, b, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (int)out.stride(0),
                            (int)out.size(1), sa, sb, status, stream, max_ctas, grp_off, groups,
-                           ScatterArgs{nullptr, 0, 1, 0});
+                           ScatterArgs{nullptr, 0, 1, 0}, nullptr, 0, SwigluArgs{nullptr, nullptr, 0}, split);
 }
 
 // Hardware scaling with 256-wide tiles leaves TMEM room for one accumulator only, so the epilogue drain is
@@ -727,18 +912,20 @@ void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& 
 static bool prefer_promote(int bn, int K) { return bn == 256 && K / 128 <= 16; }
 
 static int pick_bn(int M, int N) {
-  // BN=256 halves the A-operand shared-memory traffic per FLOP; use 128 when 256 leaves SMs idle
-  // or N is not a multiple of 256.
-  if (N % 256 != 0) return 128;
-  const long tiles256 = (long)((M + 127) / 128) * (N / 256);
+  // BN=256 halves the A-operand shared-memory traffic per FLOP; use 128 when 256 leaves SMs idle or when
+  // the padded columns of a partial last 256-wide tile exceed an eighth of N (a vocab shard of 16032
+  // columns pads 96: 256 stays, measured 0.61 -> 0.39 ms at 4096 x 16032 x 4096).
+  if (N <= 128 || (N % 256 != 0 && (256 - N % 256) * 8 > N)) return 128;
+  const long tiles256 = (long)((M + 127) / 128) * ((N + 255) / 256);
   if (tiles256 < num_sms() && (long)((M + 127) / 128) * (N / 128) <= 2L * num_sms()) return 128;
   return 256;
 }
 
 // hws: the tensor core applies the (power-of-two) block scales; otherwise the epilogue promotes per K block.
 // pair: run 256 x 256 tiles on CTA pairs (hardware scaling, BN = 256, more than one 128-row block)
+// split: split-K tail parts (0 automatic, 1 off, >= 2 requested; hardware-scaled single-CTA tiles only)
 void gemm_fp8_block(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor out,
-                    torch::Tensor status, int64_t bn, int64_t max_ctas, bool hws, bool pair) {
+                    torch::Tensor status, int64_t bn, int64_t max_ctas, bool hws, bool pair, int64_t split) {
   TORCH_CHECK(xq.is_cuda() && wq.is_cuda() && out.is_cuda());
   TORCH_CHECK(xq.scalar_type() == at::kFloat8_e4m3fn && wq.scalar_type() == at::kFloat8_e4m3fn);
   TORCH_CHECK(out.scalar_type() == at::kBFloat16);
@@ -760,8 +947,8 @@ void gemm_fp8_block(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch:
   if (hws && !pair && bn <= 0 && prefer_promote(b, K)) hws = false;
   if (hws) {
     if (b == 256 && pair && M > kBM) launch_gemm<256, true, true, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
-    else if (b == 256) launch_gemm<256, true, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
-    else launch_gemm<128, true, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
+    else if (b == 256) launch_gemm<256, true, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas, nullptr, 0, (int)split);
+    else launch_gemm<128, true, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas, nullptr, 0, (int)split);
   } else {
     if (b == 256) launch_gemm<256, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
     else launch_gemm<128, true>(xq, wq, out, sa, sb, st, stream, (int)max_ctas);
@@ -837,7 +1024,7 @@ void gemm_bf16_grouped(torch::Tensor x, torch::Tensor w, torch::Tensor offsets, 
 }
 
 void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tensor status, int64_t bn,
-               int64_t max_ctas) {
+               int64_t max_ctas, int64_t split) {
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
               out.scalar_type() == at::kBFloat16);
   const int M = x.size(0), K = x.size(1), N = w.size(0);
@@ -849,9 +1036,11 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tenso
   auto stream = at::cuda::getCurrentCUDAStream();
   const int b = bn > 0 ? (int)bn : pick_bn(M, N);
   if (b == 256)
-    launch_gemm<256, false>(x, w, out, nullptr, nullptr, status.data_ptr<int>(), stream, (int)max_ctas);
+    launch_gemm<256, false>(x, w, out, nullptr, nullptr, status.data_ptr<int>(), stream, (int)max_ctas, nullptr, 0,
+                            (int)split);
   else
-    launch_gemm<128, false>(x, w, out, nullptr, nullptr, status.data_ptr<int>(), stream, (int)max_ctas);
+    launch_gemm<128, false>(x, w, out, nullptr, nullptr, status.data_ptr<int>(), stream, (int)max_ctas, nullptr, 0,
+                            (int)split);
 }
 
 // Row-parallel projection with the scatter epilogue (see ScatterArgs): fp8 (ws defined) or bf16 operands.

@@ -7,9 +7,9 @@
 // IEEE division (the reference's verify top-k divides with div.rn.f32,
 // docker/opt/v5/topkbf_normcfg/topkbf/kopt_topkbf.py:134-141). k = 1 is argmax.
 //
-// Stage 1: grid (rows x splits); a CTA scans its vocab slice with 16-byte loads, every thread keeps an
-// online (max, sum exp) and a sorted register top-k; the CTA reduces (max, sum) and selects its top-k
-// from the per-thread lists in shared memory. Stage 2: one warp per row merges the splits' candidates
+// Stage 1: grid (rows x 16384-column chunks); a CTA holds its chunk in registers (eight 16-byte loads in
+// flight per thread), reduces (max, sum exp), and selects its top-k through a threshold filter (the k-th
+// largest per-thread maximum bounds the chunk's top k from below; see topk_stage1). Stage 2: one warp per row merges the splits' candidates
 // and (max, sum) pairs. The per-split partials are also what a vocab-sharded tensor-parallel merge
 // exchanges between ranks (values, global indices, log-sum-exp), a few hundred bytes per row.
 // The reference's equivalent kernels are Triton (docker/opt/v4/topk20/topk20.py:124-253, kopt_topkbf).
@@ -49,10 +49,11 @@ struct TopK {
   }
 };
 
-__device__ __forceinline__ void ms_combine(float& m, float& s, float m2, float s2) {
+// (m, s) pairs over raw logits: s = sum 2^((x - m) * c2), c2 = log2(e) / T
+__device__ __forceinline__ void ms_combine(float& m, float& s, float m2, float s2, float c2) {
   const float M = fmaxf(m, m2);
   if (M == -INFINITY) return;
-  s = s * expf(m - M) + s2 * expf(m2 - M);
+  s = s * exp2f((m - M) * c2) + s2 * exp2f((m2 - M) * c2);
   m = M;
 }
 
@@ -84,90 +85,186 @@ __device__ __forceinline__ void warp_select(float* vals, int* idxs, int n, float
   }
 }
 
+// The K best entries of a warp's 32 sorted register lists (value desc, index asc): K rounds of a warp-wide
+// argmax over the list heads; the winning lane pops its head.
+template <int K>
+__device__ __forceinline__ void warp_merge_lists(TopK<K>& tk, float* out_v, int* out_i) {
+  const int lane = threadIdx.x & 31;
+  for (int r = 0; r < K; ++r) {
+    float bv = tk.v[0];
+    int bi = tk.i[0], bl = lane;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
+      if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi, bl = ol;
+    }
+    if (lane == 0) out_v[r] = bv, out_i[r] = bi;
+    if (lane == bl) {
+#pragma unroll
+      for (int k = 0; k + 1 < K; ++k) tk.v[k] = tk.v[k + 1], tk.i[k] = tk.i[k + 1];
+      tk.v[K - 1] = -INFINITY;
+      tk.i[K - 1] = 0x7fffffff;
+    }
+  }
+}
+
+constexpr int kTopkVec = 8;                                   // 16-byte vectors per thread
+constexpr int kTopkChunk = kTopkThreads * kTopkVec * 8;        // columns per CTA (16384)
+constexpr int kTopkCap = 1024;                                 // candidate buffer of the threshold filter
+
+// Selection runs on the raw logits: x -> x / T (T > 0, IEEE division) keeps the order of distinct bf16 values
+// (fp32 has 16 more mantissa bits than bf16), so the k largest x are the k largest x / T and only the winners
+// are divided (in stage 2).
+// One CTA per (row, 16384-column chunk); the chunk is read once, 64 values per thread held in registers
+// (eight 16-byte loads in flight per thread). Each thread forms its maximum m_t and s_t = sum 2^((x - m_t) c2),
+// c2 = log2(e) / T; the CTA combines them into the chunk's (max, sum). The threshold tau is the K-th largest of
+// the 256 thread maxima: K distinct elements reach it, so the chunk's top K are all >= tau. Elements >= tau are
+// appended to a shared buffer (typically about K of them), and one warp selects the top K from it by
+// (value desc, index asc). If more than kTopkCap elements tie at or above tau (a constant row, say), every
+// thread builds a register top-K instead and the warps merge those lists: the same result, slower.
 template <int K, bool LSE>
 __global__ void __launch_bounds__(kTopkThreads) topk_stage1(const __nv_bfloat16* __restrict__ logits, int V, int ld,
-                                                            int splits, int chunk, float temp,
-                                                            float* __restrict__ pv, int* __restrict__ pi,
-                                                            float* __restrict__ pm, float* __restrict__ ps) {
-  __shared__ float sv[kTopkThreads * K];
-  __shared__ int si[kTopkThreads * K];
+                                                            int splits, float c2, float* __restrict__ pv,
+                                                            int* __restrict__ pi, float* __restrict__ pm,
+                                                            float* __restrict__ ps) {
+  __shared__ float cv[kTopkCap];
+  __shared__ int ci[kTopkCap];
+  __shared__ float tmax[kTopkThreads];
   __shared__ float wv[(kTopkThreads / 32) * K];
   __shared__ int wi[(kTopkThreads / 32) * K];
   __shared__ float red_m[kTopkThreads / 32], red_s[kTopkThreads / 32];
+  __shared__ float s_tau;
+  __shared__ int s_cnt;
   const int row = blockIdx.x / splits, sp = blockIdx.x % splits;
-  const int v0 = sp * chunk, v1 = min(V, v0 + chunk);
+  const int v0 = sp * kTopkChunk, v1 = min(V, v0 + kTopkChunk);
   const __nv_bfloat16* x = logits + (size_t)row * ld;
-  const bool scaled = temp != 1.0f;
-  TopK<K> tk;
-  tk.init();
-  float m = -INFINITY, s = 0.f;
-  auto take = [&](float val, int idx) {
-    if (scaled) val = __fdiv_rn(val, temp);
-    if (val == -INFINITY) return;
-    if constexpr (LSE) {
-      if (val > m) {
-        s = s * expf(m - val) + 1.f;
-        m = val;
-      } else {
-        s += expf(val - m);
+  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  if (tid == 0) s_cnt = 0;
+
+  // ---- load: vector j of thread t covers columns v0 + (j * 256 + t) * 8 .. + 8 ----
+  uint4 d[kTopkVec];
+  const bool vec_ok = (ld % 8) == 0;
+#pragma unroll
+  for (int j = 0; j < kTopkVec; ++j) {
+    const int c = v0 + (j * kTopkThreads + tid) * 8;
+    if (vec_ok && c + 8 <= v1) {
+      d[j] = __ldcs(reinterpret_cast<const uint4*>(x + c));
+    } else {
+      uint32_t h[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint16_t lo = c + 2 * e < v1 ? __bfloat16_as_ushort(x[c + 2 * e]) : (uint16_t)0xff80u;   // -inf
+        const uint16_t hi = c + 2 * e + 1 < v1 ? __bfloat16_as_ushort(x[c + 2 * e + 1]) : (uint16_t)0xff80u;
+        h[e] = (uint32_t)lo | ((uint32_t)hi << 16);
       }
+      d[j] = make_uint4(h[0], h[1], h[2], h[3]);
     }
-    tk.push(val, idx);
-  };
-  if ((ld % 8) == 0) {
-    // 16-byte vector body over whole 8-element groups (v0 is a multiple of 8), then the < 8 tail
-    const int vend = v0 + ((v1 - v0) / 8) * 8;
-    // argmax (K = 1): four 16-byte loads in flight per thread before any is consumed, the scan is otherwise
-    // latency-bound; K > 1 keeps one (measured faster there: the register top-k list competes for registers)
-    constexpr int U = K == 1 ? 4 : 1, STEP = kTopkThreads * 8;
-    for (int vb = v0 + threadIdx.x * 8; vb < vend; vb += U * STEP) {
-      uint4 w[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (vb + u * STEP < vend) w[u] = __ldcs(reinterpret_cast<const uint4*>(x + vb + u * STEP));
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int v = vb + u * STEP;
-        if (v >= vend) break;
-        const uint32_t ww[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = unpack_bf16x2(ww[e]);
-          take(f.x, v + 2 * e);
-          take(f.y, v + 2 * e + 1);
-        }
-      }
-    }
-    for (int t = vend + threadIdx.x; t < v1; t += kTopkThreads) take(__bfloat162float(x[t]), t);
-  } else {
-    for (int t = v0 + threadIdx.x; t < v1; t += kTopkThreads) take(__bfloat162float(x[t]), t);
   }
-  // (max, sum) block reduction
+  auto val = [&](int j, int e) -> float {   // element e (0..7) of vector j
+    const uint32_t wd = e < 2 ? d[j].x : e < 4 ? d[j].y : e < 6 ? d[j].z : d[j].w;
+    return __uint_as_float((e & 1) ? (wd & 0xffff0000u) : (wd << 16));
+  };
+  auto col = [&](int j, int e) { return v0 + (j * kTopkThreads + tid) * 8 + e; };
+
+  // ---- thread max and sum exp ----
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kTopkVec; ++j)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) m = fmaxf(m, val(j, e));
+  float s = 0.f;
+  if constexpr (LSE) {
+    if (m != -INFINITY) {
+#pragma unroll
+      for (int j = 0; j < kTopkVec; ++j)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s += exp2f((val(j, e) - m) * c2);
+    }
+  }
+  tmax[tid] = m;
   float bm = m, bs = s;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float om = __shfl_xor_sync(0xffffffffu, bm, o), os = __shfl_xor_sync(0xffffffffu, bs, o);
-    ms_combine(bm, bs, om, os);
+    ms_combine(bm, bs, om, os, c2);
   }
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) red_m[w] = bm, red_s[w] = bs;
+  __syncthreads();
+
+  // ---- threshold: the K-th largest thread maximum (counted with multiplicity) ----
+  if (w == 0) {
+    float t[kTopkThreads / 32];
 #pragma unroll
-  for (int k = 0; k < K; ++k) sv[threadIdx.x * K + k] = tk.v[k], si[threadIdx.x * K + k] = tk.i[k];
-  __syncwarp();
-  // two-level selection: every warp reduces its 32 threads' lists to K, then warp 0 selects from 8 x K
-  warp_select<K>(sv + w * 32 * K, si + w * 32 * K, 32 * K, wv + w * K, wi + w * K);
+    for (int q = 0; q < kTopkThreads / 32; ++q) t[q] = tmax[lane + 32 * q];
+    float tau = -INFINITY;
+    for (int r = 0; r < K; ++r) {
+      float lm = t[0];
+      int lq = 0;
+#pragma unroll
+      for (int q = 1; q < kTopkThreads / 32; ++q)
+        if (t[q] > lm) lm = t[q], lq = q;
+      float gm = lm;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+      const unsigned own = __ballot_sync(0xffffffffu, lm == gm);
+      if (lane == __ffs(own) - 1) {   // remove one occurrence
+#pragma unroll
+        for (int q = 0; q < kTopkThreads / 32; ++q)
+          if (q == lq) t[q] = -INFINITY;
+      }
+      tau = gm;
+    }
+    if (lane == 0) s_tau = tau;
+  }
+  __syncthreads();
+
+  // ---- filter: elements >= tau into the candidate buffer ----
+  const float tau = s_tau;
+#pragma unroll
+  for (int j = 0; j < kTopkVec; ++j)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float f = val(j, e);
+      if (f >= tau && f != -INFINITY) {
+        const int slot = atomicAdd(&s_cnt, 1);
+        if (slot < kTopkCap) cv[slot] = f, ci[slot] = col(j, e);
+      }
+    }
+  __syncthreads();
+  const int n = s_cnt;
+  const size_t base = (size_t)blockIdx.x * K;
+  if (n <= kTopkCap) {
+    if (w == 0) {
+      warp_select<K>(cv, ci, n, pv + base, pi + base);
+      if (lane == 0) {
+        float cm = red_m[0], cs = red_s[0];
+        for (int q = 1; q < kTopkThreads / 32; ++q) ms_combine(cm, cs, red_m[q], red_s[q], c2);
+        pm[blockIdx.x] = cm, ps[blockIdx.x] = cs;
+      }
+    }
+    return;
+  }
+  // ---- overflow (heavy ties at the threshold): per-thread register top-K, then two warp-level merges ----
+  TopK<K> tk;
+  tk.init();
+#pragma unroll
+  for (int j = 0; j < kTopkVec; ++j)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float f = val(j, e);
+      if (f != -INFINITY) tk.push(f, col(j, e));
+    }
+  warp_merge_lists<K>(tk, wv + w * K, wi + w * K);
   __syncthreads();
   if (w == 0) {
-    float cm = lane < kTopkThreads / 32 ? red_m[lane] : -INFINITY;
-    float cs = lane < kTopkThreads / 32 ? red_s[lane] : 0.f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float om = __shfl_xor_sync(0xffffffffu, cm, o), os = __shfl_xor_sync(0xffffffffu, cs, o);
-      ms_combine(cm, cs, om, os);
-    }
-    const size_t base = (size_t)blockIdx.x * K;
     warp_select<K>(wv, wi, (kTopkThreads / 32) * K, pv + base, pi + base);
-    if (lane == 0) pm[blockIdx.x] = cm, ps[blockIdx.x] = cs;
+    if (lane == 0) {
+      float cm = red_m[0], cs = red_s[0];
+      for (int q = 1; q < kTopkThreads / 32; ++q) ms_combine(cm, cs, red_m[q], red_s[q], c2);
+      pm[blockIdx.x] = cm, ps[blockIdx.x] = cs;
+    }
   }
 }
 
@@ -175,7 +272,7 @@ template <int K>
 __global__ void topk_stage2(int rows, int splits, int k_out, const float* __restrict__ pv, const int* __restrict__ pi,
                             const float* __restrict__ pm, const float* __restrict__ ps, float* __restrict__ out_lp,
                             int64_t* __restrict__ out_idx, float* __restrict__ out_lse, int vocab_offset,
-                            bool with_lse) {
+                            bool with_lse, float temp, float c2) {
   extern __shared__ uint8_t smem[];
   const int warps = blockDim.x >> 5;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -184,11 +281,12 @@ __global__ void topk_stage2(int rows, int splits, int k_out, const float* __rest
   float* vals = reinterpret_cast<float*>(smem) + (size_t)w * splits * K;
   int* idxs = reinterpret_cast<int*>(reinterpret_cast<float*>(smem) + (size_t)warps * splits * K) + (size_t)w * splits * K;
   float m = -INFINITY, s = 0.f;
-  for (int q = lane; q < splits; q += 32) ms_combine(m, s, pm[(size_t)row * splits + q], ps[(size_t)row * splits + q]);
+  for (int q = lane; q < splits; q += 32)
+    ms_combine(m, s, pm[(size_t)row * splits + q], ps[(size_t)row * splits + q], c2);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
-    ms_combine(m, s, om, os);
+    ms_combine(m, s, om, os, c2);
   }
   for (int q = lane; q < splits * K; q += 32) {
     vals[q] = pv[(size_t)row * splits * K + q];
@@ -198,9 +296,12 @@ __global__ void topk_stage2(int rows, int splits, int k_out, const float* __rest
   __shared__ float ov[32][kTopkMaxK];
   __shared__ int oi[32][kTopkMaxK];
   warp_select<K>(vals, idxs, splits * K, ov[w], oi[w]);
-  const float lse = with_lse ? m + logf(s) : 0.f;
+  const bool scaled = temp != 1.0f;
+  // log-sum-exp of x / T = m / T + ln(sum exp((x - m) / T)); the winners' x / T by IEEE division
+  const float lse = with_lse ? (scaled ? __fdiv_rn(m, temp) : m) + logf(s) : 0.f;
   if (lane < k_out) {
-    out_lp[(size_t)row * k_out + lane] = ov[w][lane] - lse;
+    const float v = ov[w][lane];
+    out_lp[(size_t)row * k_out + lane] = (scaled ? __fdiv_rn(v, temp) : v) - lse;
     out_idx[(size_t)row * k_out + lane] = (int64_t)oi[w][lane] + vocab_offset;
   }
   if (lane == 0 && out_lse) out_lse[row] = lse;
@@ -210,18 +311,16 @@ template <int K>
 static void run_topk(const torch::Tensor& logits, int64_t k, double temperature, torch::Tensor& lp, torch::Tensor& idx,
                      c10::optional<torch::Tensor> lse, int64_t vocab_offset, cudaStream_t stream) {
   const int R = logits.size(0), V = logits.size(1), ld = logits.stride(0);
-  const int target_ctas = 148 * 4;
-  int splits = std::max(1, std::min((V + 4095) / 4096, (target_ctas + R - 1) / R));
-  int chunk = ((V + splits - 1) / splits + 7) / 8 * 8;
-  splits = (V + chunk - 1) / chunk;
+  const int splits = (V + kTopkChunk - 1) / kTopkChunk;
   auto opts = logits.options().dtype(at::kFloat);
   auto pv = torch::empty({R * splits * K}, opts);
   auto pi = torch::empty({R * splits * K}, opts.dtype(at::kInt));
   auto pm = torch::empty({R * splits}, opts);
   auto ps = torch::empty({R * splits}, opts);
   auto stage1 = lse ? topk_stage1<K, true> : topk_stage1<K, false>;
+  const float c2 = (float)(1.4426950408889634 / temperature);   // log2(e) / T
   stage1<<<R * splits, kTopkThreads, 0, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), V, ld, splits, chunk, (float)temperature,
+      reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), V, ld, splits, c2,
       pv.data_ptr<float>(), pi.data_ptr<int>(), pm.data_ptr<float>(), ps.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const int warps = 4;
@@ -229,7 +328,7 @@ static void run_topk(const torch::Tensor& logits, int64_t k, double temperature,
   topk_stage2<K><<<(R + warps - 1) / warps, warps * 32, smem, stream>>>(
       R, splits, (int)k, pv.data_ptr<float>(), pi.data_ptr<int>(), pm.data_ptr<float>(), ps.data_ptr<float>(),
       lp.data_ptr<float>(), idx.data_ptr<int64_t>(), lse ? lse->data_ptr<float>() : nullptr, (int)vocab_offset,
-      lse.has_value());
+      lse.has_value(), (float)temperature, c2);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

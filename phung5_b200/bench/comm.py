@@ -7,6 +7,9 @@ Times, with CUDA events after warm-up and the maximum over ranks:
            shape (M = 4096 rows of H = 8192) and the draft shape (M = 512);
   gather   the fused candidate exchange (512 rows x top-8 (value, index) + lse);
   nccl     torch.distributed all_reduce of the same [M, H] bf16 partial (the unfused baseline's collective).
+--sweep: the fused-kernel sweep instead: AR + residual + RMSNorm + FP8 quant at tokens {1, 16, 128, 1024, 8192}
+and vocab-sharded top-k / top-p sampling at batch {1, 64, 256} x k {1, 8, 50}, each against NCCL + the separate
+kernels.
 NVLink bytes per ar_norm per GPU: (W-1)/W of the partial rows read (bf16) plus (W-1)/W of the fp8 rows and
 scales written; reported against the measured peer-copy bandwidth of 770 GB/s per direction.
 o_proj / down_proj + reduction: the fused path (GEMM epilogue stores rows to their owners, reduction over local
@@ -86,6 +89,58 @@ def ar_norm_sweep(comm, world, iters, H=8192, tokens=(1, 16, 128, 1024, 8192)):
     return rows
 
 
+def sampling_sweep(comm, world, iters, vocab=128256, batches=(1, 64, 256), ks=(1, 8, 50), top_p=0.9):
+    """Fused-kernel sweep (b): vocab-sharded top-k / top-p sampling, vocab 128256 split over the ranks, bf16
+    logits ~N(0, 2^2), temperature 1, top-p 0.9, batch x k. Fused: per-shard candidates (csrc/sample.cu
+    sample_candidates), one in-kernel exchange of the [rows, chunks, KC] candidate lists over NVLink
+    (FusedCommunicator.gather), one draw kernel (spec_accept on a one-node tree: the draw of the step's final
+    coin). Baseline: NCCL all_gather of the logits shards, re-layout to [B, V], then the same two kernels over
+    the full vocab on every rank. Both arms must draw identical tokens. Roofline: the shard read from HBM at
+    the measured copy rate plus the candidate bytes each GPU receives at 770 GB/s (microseconds: these sizes
+    are launch- and latency-bound)."""
+    from .. import ops
+    from .kernels import peaks
+    dev = comm.device
+    vl = vocab // world
+    off = comm.rank * vl
+    hbm = peaks()["hbm_gbs"]
+    rows = []
+    for b in batches:
+        g = torch.Generator(device=dev).manual_seed(17)
+        full = (torch.randn(b, vl * world, device=dev, generator=g) * 2.0).to(torch.bfloat16)
+        shard = full[:, off:off + vl].contiguous()
+        gbuf = torch.empty(world, b, vl, device=dev, dtype=torch.bfloat16)
+        tokens = torch.zeros(b, 1, device=dev, dtype=torch.int64)
+        parent = torch.full((b, 1), -1, device=dev, dtype=torch.int64)
+        temp = torch.ones(b, device=dev)
+        topp = torch.full((b,), top_p, device=dev)
+        seed = torch.arange(b, device=dev, dtype=torch.int64) + 7
+        committed = torch.zeros(b, device=dev, dtype=torch.int64)
+        for k in ks:
+            kc = 16 if k <= 16 else 64
+            topk = torch.full((b,), k, device=dev, dtype=torch.int32)
+            res = {}
+
+            def fused():
+                res["f"] = ops.spec_sample_accept(shard, tokens, parent, temp, topk, topp, seed, committed, 0, kc,
+                                                  vocab_offset=off, gather=comm.gather)[1]
+
+            def nccl():
+                dist.all_gather_into_tensor(gbuf.view(-1), shard.view(-1))
+                lay = gbuf.permute(1, 0, 2).reshape(b, world * vl)
+                res["n"] = ops.spec_sample_accept(lay, tokens, parent, temp, topk, topp, seed, committed, 0, kc)[1]
+            f_ms = _time(fused, iters)
+            n_ms = _time(nccl, iters)
+            same = bool(torch.equal(res["f"], res["n"]))
+            nch = int(ops.ext().sample_chunks(vl))
+            roof = (b * vl * 2 / hbm / 1e6) + (world - 1) * b * nch * kc * 8 / NVLINK_GBS / 1e6
+            rows.append({"op": "sweep_sampling", "batch": b, "k": k, "top_p": top_p, "vocab_shard": vl,
+                         "fused_ms": round(f_ms, 4), "nccl_plus_kernel_ms": round(n_ms, 4),
+                         "speedup": round(n_ms / f_ms, 2), "roofline_ms": round(roof, 5),
+                         "fused_frac_of_roofline": round(roof / f_ms, 3), "same_tokens": same})
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=20)
@@ -97,7 +152,7 @@ def main():
     H = args.hidden
     comm = FusedCommunicator(max_tokens=8192, hidden=H)
     if args.sweep:
-        out = ar_norm_sweep(comm, world, args.iters, H)
+        out = ar_norm_sweep(comm, world, args.iters, H) + sampling_sweep(comm, world, args.iters)
         if rank == 0:
             for o in out:
                 print(json.dumps({"world": world, **o}))

@@ -7,8 +7,8 @@ o, down, the EAGLE head's fc; the bf16 lm_head) and every M bucket (draft rounds
 chunks), each tile configuration the kernel offers is timed with CUDA events after warm-up, flushing L2 before
 every launch, round-robin with the default choice over three passes (best of each), and the fastest is recorded:
   fp8:  BN 128 / 256 x hardware block scaling (tcgen05 kind::mxf8f6f4) or per-K-block promotion x CTA pairs
-        (cta_group::2, BN 256 only)
-  bf16: BN 128 / 256
+        (cta_group::2, BN 256 only) x the split-K tail (hardware-scaled single-CTA tiles)
+  bf16: BN 128 / 256 x the split-K tail
 The reference keeps the same kind of table for its sm90 CUTLASS FP8 GEMM (docker/opt/v5/wq/kopt_wq.py:92-116,
 kopt_wq_table.json: tile, cluster and schedule per (N, K, M)); here the choices are the tcgen05 kernel's.
 Results within 2 % of the default choice keep the default (no churn from timing noise).
@@ -44,9 +44,10 @@ def shapes():
 
 
 def fp8_configs(m):
-    cfgs = [dict(bn=b, hws=h, pair=False) for b in (128, 256) for h in (True, False)]
+    cfgs = [dict(bn=b, hws=h, pair=False, split=1) for b in (128, 256) for h in (True, False)]
+    cfgs += [dict(bn=b, hws=True, pair=False, split=0) for b in (128, 256)]   # automatic split-K tail
     if m > 128:
-        cfgs.append(dict(bn=256, hws=True, pair=True))
+        cfgs.append(dict(bn=256, hws=True, pair=True, split=1))
     return cfgs
 
 
@@ -60,13 +61,15 @@ def measure(kind, n, k, m, iters, rounds=3):
         ws = pow2_scale(torch.rand((n + 127) // 128, k // 128, device=dev) * 4.48)
         out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
         cands = [(c, (lambda c=c: ops.gemm_fp8_block(xq, xs, wq, ws, out=out, bn=c["bn"], hw_scale=c["hws"],
-                                                     pair=c["pair"], use_table=False))) for c in fp8_configs(m)]
+                                                     pair=c["pair"], split=c["split"], use_table=False)))
+                 for c in fp8_configs(m)]
         default = lambda: ops.gemm_fp8_block(xq, xs, wq, ws, out=out, use_table=False)
     else:
         x = torch.randn(m, k, device=dev, dtype=torch.bfloat16)
         w = torch.randn(n, k, device=dev, dtype=torch.bfloat16) * 0.05
         out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
-        cands = [(dict(bn=b), (lambda b=b: ops.gemm_bf16(x, w, out=out, bn=b, use_table=False))) for b in (128, 256)]
+        cands = [(dict(bn=b, split=sp), (lambda b=b, sp=sp: ops.gemm_bf16(x, w, out=out, bn=b, split=sp, use_table=False)))
+                 for b in (128, 256) for sp in (1, 0)]
         default = lambda: ops.gemm_bf16(x, w, out=out, use_table=False)
     best_t = [float("inf")] * len(cands)
     d_ms = float("inf")

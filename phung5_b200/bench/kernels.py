@@ -1,6 +1,9 @@
 """Per-kernel microbenchmarks with roofline fractions.
 
-    python -m phung5_b200.bench.kernels [--kernel NAME ...] [--iters 10]
+    python -m phung5_b200.bench.kernels [--kernel NAME ...] [--iters 10] [--impl reference]
+
+--impl reference times the reference's own Triton kernels (imported unmodified from baseline/_ref) next to
+ours at the same shapes: bf16 top-k of logits / T, verify-row target candidates, GDN target verify.
 
 Each case is timed with CUDA events on the current stream after 3 warm-up launches, flushing L2
 (a 512 MB write) before every timed launch, and reported as achieved TFLOP/s or GB/s and as the fraction
@@ -315,11 +318,124 @@ CASES = {
 }
 
 
+# ------------------------------------------------------------------------------------------------
+# reference arms: the reference's own Triton kernels, unmodified, timed at the same shapes as ours
+# ------------------------------------------------------------------------------------------------
+
+REF_ROOT = os.path.join(ROOT, "baseline", "_ref")
+
+
+def _ref_module(rel: str, name: str):
+    """Import one of the reference's kernel files by path from its unmodified checkout under baseline/_ref
+    (the reference is not pip-installable; its Triton kernels import only torch and triton)."""
+    import importlib.util
+    path = os.path.join(REF_ROOT, rel)
+    if not os.path.exists(path):
+        raise FileNotFoundError(f"reference kernel file missing: {path}")
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def ref_pair_topk(rows, v, k):
+    """top-k of bf16 logits / T per row. Ours: csrc/topk.cu (values are log-probabilities: the kernel also
+    forms each row's logsumexp). Reference: docker/opt/v5/topkbf_normcfg/topkbf/kopt_topkbf.py
+    topk_scaled_bf16 (two Triton stages + torch.topk on the k slots)."""
+    ref = _ref_module("docker/opt/v5/topkbf_normcfg/topkbf/kopt_topkbf.py", "ref_kopt_topkbf")
+    x = torch.randn(rows, v, device="cuda", dtype=torch.bfloat16) * 2
+    t = torch.full((rows, 1), 0.8, device="cuda")
+    ours = lambda: ops.topk_logprobs(x, k, 0.8, with_lse=True)
+    theirs = lambda: ref.topk_scaled_bf16(x, t, k)
+    assert ref.kernel_eligible(x, t.reshape(-1), k) is None, "reference kernel would fall back to torch"
+    lp, idx, _ = ours()
+    rv, ri = theirs()
+    same = bool(torch.equal(idx, ri))
+    return ours, theirs, rows * v * 2, {"same_indices": same}
+
+
+def ref_pair_verify_candidates(rows, v, k):
+    """Verify-row target candidates. Ours: sample_candidates (exact top-64 of x / T per 16384-column chunk,
+    what the device accept kernel merges). Reference: topk_scaled_bf16 with k = 20 (its verify target-probs
+    top-k, kopt_topkbf.py:353-399)."""
+    ref = _ref_module("docker/opt/v5/topkbf_normcfg/topkbf/kopt_topkbf.py", "ref_kopt_topkbf")
+    x = torch.randn(rows, v, device="cuda", dtype=torch.bfloat16) * 2
+    t = torch.full((rows, 1), 0.8, device="cuda")
+    nch = int(ops.ext().sample_chunks(v))
+    cv = torch.empty(rows, nch, 64, device="cuda")
+    ci = torch.empty(rows, nch, 64, device="cuda", dtype=torch.int32)
+    ours = lambda: ops.ext().sample_candidates(x, 64, t.reshape(-1), 1, 0, cv, ci, None, ops.status_tensor(x.device))
+    theirs = lambda: ref.topk_scaled_bf16(x, t, k)
+    return ours, theirs, rows * v * 2, {"ours": "per-chunk top-64 lists", "theirs": f"row top-{k}"}
+
+
+def ref_pair_gdn_verify(reqs, n, hk, hv):
+    """GDN target verify of a draft window of n tokens per request (gates included). Ours: csrc/gdn.cu (fp32
+    state [slots, HV, K, V], per-token recurrence with stash). Reference: docker/opt/kern/braw/kernels.py
+    gdn_b_verify (chunked WY/UT form on tensor cores, bf16 state [slots, HV, V, K], fp32 stash)."""
+    from ..ops import gdn as G
+    ref = _ref_module("docker/opt/kern/braw/kernels.py", "ref_braw")
+    t = reqs * n
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(t, hk, 128, device="cuda", dtype=torch.bfloat16, generator=g)
+    k = torch.randn(t, hk, 128, device="cuda", dtype=torch.bfloat16, generator=g)
+    v = torch.randn(t, hv, 128, device="cuda", dtype=torch.bfloat16, generator=g)
+    a = torch.randn(t, hv, device="cuda", dtype=torch.bfloat16, generator=g)
+    b = torch.randn(t, hv, device="cuda", dtype=torch.bfloat16, generator=g)
+    A_log = torch.rand(hv, device="cuda", generator=g)
+    dt_bias = torch.rand(hv, device="cuda", generator=g)
+    state32 = torch.randn(reqs, hv, 128, 128, device="cuda", generator=g) * 0.01
+    state16 = state32.transpose(-1, -2).contiguous().to(torch.bfloat16)   # [slots, HV, V, K]
+    ts = torch.arange(reqs + 1, device="cuda", dtype=torch.int32) * n
+    slot = torch.arange(reqs, device="cuda", dtype=torch.int32)
+    per_row = ref.stash_floats(hk, hv, 128, 128, n)
+    stash = torch.empty(reqs, n, 1, 1, (per_row + n - 1) // n, device="cuda")
+    scale = 128 ** -0.5
+
+    def ours():
+        gg, beta = G.gdn_gates(a, b, A_log, dt_bias)
+        G.gdn_recurrent(q, k, v, gg, beta, state32, ts, slot, scale, write_state=False, stash=True)
+    theirs = lambda: ref.gdn_b_verify(A_log, dt_bias, q, k, v, a, b, state16, slot, ts, stash, slot, scale=scale)
+    byts = reqs * hv * 128 * 128 * 2 + t * (2 * hk + hv) * 128 * 2 + t * hv * 128 * 2
+    return ours, theirs, byts, {"ours_state": "fp32", "theirs_state": "bf16"}
+
+
+REF_CASES = {
+    "ref_topk8_draft": lambda: ref_pair_topk(512, 128256, 8),
+    "ref_topk16_verify": lambda: ref_pair_topk(4096, 128256, 16),
+    "ref_verify_candidates_k20": lambda: ref_pair_verify_candidates(4096, 128256, 20),
+    "ref_gdn_verify_64x8": lambda: ref_pair_gdn_verify(64, 8, 16, 32),
+}
+
+
+def run_reference(names, iters):
+    """Time each (ours, reference) pair at the same shape: ms of both and reference / ours (> 1: ours faster).
+    The byte count is the minimal HBM traffic of the op (bf16 state for the GDN row)."""
+    pk = peaks()
+    for name in names:
+        ours, theirs, byts, extra = REF_CASES[name]()
+        o_ms = time_it(ours, iters)
+        r_ms = time_it(theirs, iters)
+        ops.check_status()
+        print(json.dumps({"kernel": name, "ours_ms": round(o_ms, 4), "reference_ms": round(r_ms, 4),
+                          "reference_over_ours": round(r_ms / o_ms, 2),
+                          "ours_frac_of_" + pk["src"] + "_hbm": round(byts / o_ms / 1e6 / pk["hbm_gbs"], 3),
+                          "reference_frac_of_" + pk["src"] + "_hbm": round(byts / r_ms / 1e6 / pk["hbm_gbs"], 3),
+                          **extra}))
+        torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", nargs="*", default=list(CASES))
+    ap.add_argument("--kernel", nargs="*", default=None)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"],
+                    help="reference: time the reference's own kernels against ours at the same shapes")
     args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args.kernel or list(REF_CASES), args.iters)
+        return
+    args.kernel = args.kernel or list(CASES)
     pk = peaks()
     for name in args.kernel:
         fn, flops, kind = CASES[name]()

@@ -29,7 +29,8 @@ _STATUS = {}
 
 STATUS_CODES = {1: "timeout in TMA producer", 2: "timeout in MMA issuer", 3: "timeout in epilogue",
                 4: "timeout waiting for a peer rank", 5: "bad arguments",
-                6: "fp8 block scale is not a power of two (hardware-scaled GEMM)"}
+                6: "fp8 block scale is not a power of two (hardware-scaled GEMM)",
+                7: "timeout in a split-K GEMM part waiting for the other parts of its tile"}
 
 
 _LAUNCHES = [0]
@@ -147,49 +148,56 @@ SWIGLU_FUSED = os.environ.get("PHX_SWIGLU_FUSED", "1") != "0"
 # PHX_GEMM_PAIR=1: hardware-scaled 256-wide tiles run as 256 x 256 tiles on CTA pairs (tcgen05 cta_group::2,
 # clusters of two). Off by default: measured no faster than the single-CTA tile under the power cap.
 GEMM_PAIR = os.environ.get("PHX_GEMM_PAIR", "0") == "1"
+# Plain GEMMs whose last wave of tiles leaves most SMs idle split those tiles over K (csrc/gemm_sm100.cu,
+# SplitArgs); PHX_GEMM_SPLIT=0 keeps every tile whole unless a caller asks for a split.
+GEMM_SPLIT = os.environ.get("PHX_GEMM_SPLIT", "1") != "0"
 
 
-def _table_choice(kind: str, n: int, k: int, m: int, bn: int, hw_scale, pair, use_table: bool):
-    """The measured per-shape configuration (ops/gemm_table.json) unless the caller chose one."""
-    if not use_table or bn or hw_scale is not None or pair is not None:
-        return bn, hw_scale, pair
+def _table_choice(kind: str, n: int, k: int, m: int, bn: int, hw_scale, pair, use_table: bool, split=None):
+    """The measured per-shape configuration (ops/gemm_table.json) unless the caller chose one. Returns
+    (bn, hws, pair, split); split 0 = the kernel's automatic split-K tail, 1 = off."""
+    auto = 0 if GEMM_SPLIT else 1
+    if not use_table or bn or hw_scale is not None or pair is not None or split is not None:
+        return bn, hw_scale, pair, (auto if split is None else split)
     from . import gemm_table
     e = gemm_table.lookup(kind, n, k, m)
     if e is None:
-        return bn, hw_scale, pair
+        return bn, hw_scale, pair, auto
     hws = e.get("hws")
     if hws is not None and not FP8_HW_SCALE:
         hws = False            # arbitrary-scale mode: never hand scales to the hardware path
-    return int(e["bn"]), hws, e.get("pair")
+    return int(e["bn"]), hws, e.get("pair"), int(e.get("split", auto))
 
 
 def gemm_fp8_block(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
                    out: Optional[torch.Tensor] = None, bn: int = 0, max_ctas: int = 0,
-                   hw_scale: Optional[bool] = None, pair: Optional[bool] = None, use_table: bool = True) -> torch.Tensor:
+                   hw_scale: Optional[bool] = None, pair: Optional[bool] = None, use_table: bool = True,
+                   split: Optional[int] = None) -> torch.Tensor:
     """Block-scaled FP8 linear: xq [M,K] e4m3, xs [K/128, M] fp32, wq [N,K] e4m3, ws [N/128, K/128]
     fp32 -> bf16 [M, N]. hw_scale (default FP8_HW_SCALE) needs power-of-two scales. Unless bn / hw_scale / pair
-    are given, the measured per-shape table (ops/gemm_table.py) picks them."""
+    / split are given, the measured per-shape table (ops/gemm_table.py) picks them. split: parts of the split-K
+    tail of grids whose last wave is mostly idle (0 automatic, 1 off, >= 2 that many)."""
     m, n = xq.shape[0], wq.shape[0]
     if out is None:
         out = torch.empty(m, n, dtype=torch.bfloat16, device=xq.device)
     if xq.is_cuda:
-        bn, hw_scale, pair = _table_choice("fp8", n, xq.shape[1], m, bn, hw_scale, pair, use_table)
+        bn, hw_scale, pair, split = _table_choice("fp8", n, xq.shape[1], m, bn, hw_scale, pair, use_table, split)
         hws = FP8_HW_SCALE if hw_scale is None else hw_scale
         ext().gemm_fp8_block(xq, xs, wq, ws, out, status_tensor(xq.device), bn, max_ctas, hws,
-                             GEMM_PAIR if pair is None else pair)
+                             GEMM_PAIR if pair is None else pair, split)
     else:
         out.copy_(gemm_fp8_block_ref(xq, xs, wq, ws).to(out.dtype))
     return out
 
 
 def gemm_bf16(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None, bn: int = 0,
-              max_ctas: int = 0, use_table: bool = True) -> torch.Tensor:
-    """x [M,K] bf16 @ w [N,K]^T -> bf16 [M,N] (fp32 accumulate)."""
+              max_ctas: int = 0, use_table: bool = True, split: Optional[int] = None) -> torch.Tensor:
+    """x [M,K] bf16 @ w [N,K]^T -> bf16 [M,N] (fp32 accumulate); split as for gemm_fp8_block."""
     if out is None:
         out = torch.empty(x.shape[0], w.shape[0], dtype=torch.bfloat16 if x.is_cuda else x.dtype, device=x.device)
     if x.is_cuda:
-        bn, _, _ = _table_choice("bf16", w.shape[0], x.shape[1], x.shape[0], bn, None, None, use_table)
-        ext().gemm_bf16(x, w, out, status_tensor(x.device), bn, max_ctas)
+        bn, _, _, split = _table_choice("bf16", w.shape[0], x.shape[1], x.shape[0], bn, None, None, use_table, split)
+        ext().gemm_bf16(x, w, out, status_tensor(x.device), bn, max_ctas, split)
     else:
         out.copy_((x.float() @ w.float().t()).to(out.dtype))
     return out

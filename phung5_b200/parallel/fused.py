@@ -128,8 +128,8 @@ class FusedCommunicator(NcclCommunicator):
         `ar_norm(..., recv=True)`."""
         rows_per = (m + self.size - 1) // self.size
         xq, xs = x if lin.fp8 else (x, None)
-        bn, hws, pair = ops._table_choice("fp8" if lin.fp8 else "bf16", lin.w.shape[0], xq.shape[1], m, 0, None, None,
-                                          True)
+        bn, hws, pair, _ = ops._table_choice("fp8" if lin.fp8 else "bf16", lin.w.shape[0], xq.shape[1], m, 0, None,
+                                             None, True)
         ops.ext().gemm_scatter(xq, xs, lin.w, lin.ws, self.peer_base, self.ws.off["recv"], rows_per, self.rank,
                                ops.status_tensor(self.device), ops.FP8_HW_SCALE if hws is None else hws,
                                ops.GEMM_PAIR if pair is None else pair, bn)
