@@ -113,29 +113,52 @@ __device__ __forceinline__ void warp_merge_lists(TopK<K>& tk, float* out_v, int*
 constexpr int kTopkVec = 8;                                   // 16-byte vectors per thread
 constexpr int kTopkChunk = kTopkThreads * kTopkVec * 8;        // columns per CTA (16384)
 constexpr int kTopkCap = 1024;                                 // candidate buffer of the threshold filter
+constexpr int kTopkCapW = kTopkCap / (kTopkThreads / 32);      // per warp
+
+// 2^x by the MUFU instruction (ex2.approx.ftz: relative error about 2^-22; the log-sum-exp needs no more)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Descending bitonic sort of one value per lane across a warp.
+__device__ __forceinline__ float warp_sort_desc(float v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const float o = __shfl_xor_sync(0xffffffffu, v, j);
+      const bool keep_max = ((lane & j) == 0) == ((lane & k) == 0);
+      v = keep_max ? fmaxf(v, o) : fminf(v, o);
+    }
+  }
+  return v;
+}
 
 // Selection runs on the raw logits: x -> x / T (T > 0, IEEE division) keeps the order of distinct bf16 values
 // (fp32 has 16 more mantissa bits than bf16), so the k largest x are the k largest x / T and only the winners
 // are divided (in stage 2).
 // One CTA per (row, 16384-column chunk); the chunk is read once, 64 values per thread held in registers
 // (eight 16-byte loads in flight per thread). Each thread forms its maximum m_t and s_t = sum 2^((x - m_t) c2),
-// c2 = log2(e) / T; the CTA combines them into the chunk's (max, sum). The threshold tau is the K-th largest of
-// the 256 thread maxima: K distinct elements reach it, so the chunk's top K are all >= tau. Elements >= tau are
-// appended to a shared buffer (typically about K of them), and one warp selects the top K from it by
-// (value desc, index asc). If more than kTopkCap elements tie at or above tau (a constant row, say), every
-// thread builds a register top-K instead and the warps merge those lists: the same result, slower.
+// c2 = log2(e) / T; the CTA combines them into the chunk's (max, sum). Each warp sorts its 32 thread maxima;
+// tau is the largest of the warps' K-th values: K distinct elements reach it, so the chunk's top K are all
+// >= tau. Every warp appends its elements >= tau to its own shared region (ballot order, no atomics; a few
+// dozen on random rows), selects its top K from them, and warp 0 selects from the 8 x K by (value desc,
+// index asc). If a warp has more than kTopkCapW elements at or above tau (a constant row, say), every thread
+// builds a register top-K instead and the warps merge those lists: the same result, slower.
 template <int K, bool LSE>
-__global__ void __launch_bounds__(kTopkThreads) topk_stage1(const __nv_bfloat16* __restrict__ logits, int V, int ld,
+__global__ void __launch_bounds__(kTopkThreads, 3) topk_stage1(const __nv_bfloat16* __restrict__ logits, int V, int ld,
                                                             int splits, float c2, float* __restrict__ pv,
                                                             int* __restrict__ pi, float* __restrict__ pm,
                                                             float* __restrict__ ps) {
   __shared__ float cv[kTopkCap];
   __shared__ int ci[kTopkCap];
-  __shared__ float tmax[kTopkThreads];
   __shared__ float wv[(kTopkThreads / 32) * K];
   __shared__ int wi[(kTopkThreads / 32) * K];
   __shared__ float red_m[kTopkThreads / 32], red_s[kTopkThreads / 32];
-  __shared__ float s_tau;
+  __shared__ float wtau[kTopkThreads / 32];
   __shared__ int s_cnt;
   const int row = blockIdx.x / splits, sp = blockIdx.x % splits;
   const int v0 = sp * kTopkChunk, v1 = min(V, v0 + kTopkChunk);
@@ -168,22 +191,27 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stage1(const __nv_bfloat16*
   };
   auto col = [&](int j, int e) { return v0 + (j * kTopkThreads + tid) * 8 + e; };
 
-  // ---- thread max and sum exp ----
+  // ---- thread max and sum exp (2^(x c2 - m c2): one FFMA and one ex2 per element) ----
+  float vmax[kTopkVec];
   float m = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < kTopkVec; ++j)
+  for (int j = 0; j < kTopkVec; ++j) {
+    float a = val(j, 0);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) m = fmaxf(m, val(j, e));
+    for (int e = 1; e < 8; ++e) a = fmaxf(a, val(j, e));
+    vmax[j] = a;
+    m = fmaxf(m, a);
+  }
   float s = 0.f;
   if constexpr (LSE) {
     if (m != -INFINITY) {
+      const float mc = -m * c2;
 #pragma unroll
       for (int j = 0; j < kTopkVec; ++j)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) s += exp2f((val(j, e) - m) * c2);
+        for (int e = 0; e < 8; ++e) s += ex2_approx(fmaf(val(j, e), c2, mc));
     }
   }
-  tmax[tid] = m;
   float bm = m, bs = s;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -193,51 +221,46 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stage1(const __nv_bfloat16*
   if (lane == 0) red_m[w] = bm, red_s[w] = bs;
   __syncthreads();
 
-  // ---- threshold: the K-th largest thread maximum (counted with multiplicity) ----
-  if (w == 0) {
-    float t[kTopkThreads / 32];
-#pragma unroll
-    for (int q = 0; q < kTopkThreads / 32; ++q) t[q] = tmax[lane + 32 * q];
-    float tau = -INFINITY;
-    for (int r = 0; r < K; ++r) {
-      float lm = t[0];
-      int lq = 0;
-#pragma unroll
-      for (int q = 1; q < kTopkThreads / 32; ++q)
-        if (t[q] > lm) lm = t[q], lq = q;
-      float gm = lm;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
-      const unsigned own = __ballot_sync(0xffffffffu, lm == gm);
-      if (lane == __ffs(own) - 1) {   // remove one occurrence
-#pragma unroll
-        for (int q = 0; q < kTopkThreads / 32; ++q)
-          if (q == lq) t[q] = -INFINITY;
-      }
-      tau = gm;
-    }
-    if (lane == 0) s_tau = tau;
+  // ---- threshold: tau = max over warps of the K-th largest thread maximum of the warp (a warp bitonic sort
+  // of its 32 maxima); the warp reaching tau has K elements >= tau, so the CTA's top K are all >= tau ----
+  {
+    const float srt = warp_sort_desc(m);
+    const float tw = __shfl_sync(0xffffffffu, srt, K - 1);
+    if (lane == 0) wtau[w] = tw;
   }
   __syncthreads();
-
-  // ---- filter: elements >= tau into the candidate buffer ----
-  const float tau = s_tau;
+  float tau = wtau[0];
 #pragma unroll
-  for (int j = 0; j < kTopkVec; ++j)
+  for (int q = 1; q < kTopkThreads / 32; ++q) tau = fmaxf(tau, wtau[q]);
+
+  // ---- filter: every warp appends its elements >= tau to its own region, in (vector, element, lane) order ----
+  float* rv = cv + w * kTopkCapW;
+  int* ri = ci + w * kTopkCapW;
+  int cnt = 0;
+  const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+  for (int j = 0; j < kTopkVec; ++j) {
+    if (!__any_sync(0xffffffffu, vmax[j] >= tau && vmax[j] != -INFINITY)) continue;   // most vectors
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const float f = val(j, e);
-      if (f >= tau && f != -INFINITY) {
-        const int slot = atomicAdd(&s_cnt, 1);
-        if (slot < kTopkCap) cv[slot] = f, ci[slot] = col(j, e);
+      const bool take = f >= tau && f != -INFINITY;
+      const unsigned msk = __ballot_sync(0xffffffffu, take);
+      if (take) {
+        const int slot = cnt + __popc(msk & lt);
+        if (slot < kTopkCapW) rv[slot] = f, ri[slot] = col(j, e);
       }
+      cnt += __popc(msk);
     }
+  }
+  if (lane == 0 && cnt > kTopkCapW) s_cnt = 1;   // overflow flag
+  __syncwarp();
+  if (cnt <= kTopkCapW) warp_select<K>(rv, ri, cnt, wv + w * K, wi + w * K);
   __syncthreads();
-  const int n = s_cnt;
   const size_t base = (size_t)blockIdx.x * K;
-  if (n <= kTopkCap) {
+  if (!s_cnt) {
     if (w == 0) {
-      warp_select<K>(cv, ci, n, pv + base, pi + base);
+      warp_select<K>(wv, wi, (kTopkThreads / 32) * K, pv + base, pi + base);
       if (lane == 0) {
         float cm = red_m[0], cs = red_s[0];
         for (int q = 1; q < kTopkThreads / 32; ++q) ms_combine(cm, cs, red_m[q], red_s[q], c2);
@@ -246,15 +269,18 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stage1(const __nv_bfloat16*
     }
     return;
   }
+  __syncthreads();   // every warp's selection is done before the overflow path rewrites wv / wi
   // ---- overflow (heavy ties at the threshold): per-thread register top-K, then two warp-level merges ----
+  // (re-reads the chunk from global memory, so the register copy is dead by now)
   TopK<K> tk;
   tk.init();
-#pragma unroll
+#pragma unroll 1
   for (int j = 0; j < kTopkVec; ++j)
-#pragma unroll
+#pragma unroll 1
     for (int e = 0; e < 8; ++e) {
-      const float f = val(j, e);
-      if (f != -INFINITY) tk.push(f, col(j, e));
+      const int c = v0 + (j * kTopkThreads + tid) * 8 + e;
+      const float f = c < v1 ? __bfloat162float(x[c]) : -INFINITY;
+      if (f != -INFINITY) tk.push(f, c);
     }
   warp_merge_lists<K>(tk, wv + w * K, wi + w * K);
   __syncthreads();
@@ -265,6 +291,97 @@ __global__ void __launch_bounds__(kTopkThreads) topk_stage1(const __nv_bfloat16*
       for (int q = 1; q < kTopkThreads / 32; ++q) ms_combine(cm, cs, red_m[q], red_s[q], c2);
       pm[blockIdx.x] = cm, ps[blockIdx.x] = cs;
     }
+  }
+}
+
+// K = 1 (argmax, greedy verify): a streaming scan with four 16-byte loads in flight per thread over a slice
+// of about V * R / 592 columns per CTA; per 8-element vector one max (and, with LSE, one rescale check and
+// eight exp2 terms); the thread keeps its first maximum (indices rise along its scan).
+template <bool LSE>
+__global__ void __launch_bounds__(kTopkThreads) argmax_stage1(const __nv_bfloat16* __restrict__ logits, int V, int ld,
+                                                              int splits, int chunk, float c2,
+                                                              float* __restrict__ pv, int* __restrict__ pi,
+                                                              float* __restrict__ pm, float* __restrict__ ps) {
+  __shared__ float wv[kTopkThreads / 32];
+  __shared__ int wi[kTopkThreads / 32];
+  __shared__ float red_m[kTopkThreads / 32], red_s[kTopkThreads / 32];
+  const int row = blockIdx.x / splits, sp = blockIdx.x % splits;
+  const int v0 = sp * chunk, v1 = min(V, v0 + chunk);
+  const __nv_bfloat16* x = logits + (size_t)row * ld;
+  float m = -INFINITY, s = 0.f, bv = -INFINITY;
+  int bi = 0x7fffffff;
+  auto take8 = [&](const float (&f)[8], int idx0) {
+    float gmax = f[0];
+#pragma unroll
+    for (int e = 1; e < 8; ++e) gmax = fmaxf(gmax, f[e]);
+    if (gmax == -INFINITY) return;
+    if constexpr (LSE) {
+      if (gmax > m) {
+        s *= exp2f((m - gmax) * c2);
+        m = gmax;
+      }
+      float acc = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc += exp2f((f[e] - m) * c2);
+      s += acc;
+    }
+    if (gmax > bv) {
+#pragma unroll
+      for (int e = 7; e >= 0; --e)          // the lowest index of the vector's maximum
+        if (f[e] == gmax) bi = idx0 + e;
+      bv = gmax;
+    }
+  };
+  auto take1 = [&](float f, int idx) {
+    float g[8] = {f, -INFINITY, -INFINITY, -INFINITY, -INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    take8(g, idx);
+  };
+  if ((ld % 8) == 0) {
+    const int vend = v0 + ((v1 - v0) / 8) * 8;
+    constexpr int U = 4, STEP = kTopkThreads * 8;
+    for (int vb = v0 + threadIdx.x * 8; vb < vend; vb += U * STEP) {
+      uint4 d[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (vb + u * STEP < vend) d[u] = __ldcs(reinterpret_cast<const uint4*>(x + vb + u * STEP));
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int v = vb + u * STEP;
+        if (v >= vend) break;
+        const uint32_t ww[4] = {d[u].x, d[u].y, d[u].z, d[u].w};
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 t = unpack_bf16x2(ww[e]);
+          f[2 * e] = t.x;
+          f[2 * e + 1] = t.y;
+        }
+        take8(f, v);
+      }
+    }
+    for (int t = vend + threadIdx.x; t < v1; t += kTopkThreads) take1(__bfloat162float(x[t]), t);
+  } else {
+    for (int t = v0 + threadIdx.x; t < v1; t += kTopkThreads) take1(__bfloat162float(x[t]), t);
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
+    ms_combine(m, s, om, os, c2);
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
+  }
+  if (lane == 0) red_m[w] = m, red_s[w] = s, wv[w] = bv, wi[w] = bi;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float cm = red_m[0], cs = red_s[0], cv = wv[0];
+    int cidx = wi[0];
+    for (int q = 1; q < kTopkThreads / 32; ++q) {
+      ms_combine(cm, cs, red_m[q], red_s[q], c2);
+      if (wv[q] > cv || (wv[q] == cv && wi[q] < cidx)) cv = wv[q], cidx = wi[q];
+    }
+    pv[blockIdx.x] = cv, pi[blockIdx.x] = cidx, pm[blockIdx.x] = cm, ps[blockIdx.x] = cs;
   }
 }
 
@@ -311,17 +428,28 @@ template <int K>
 static void run_topk(const torch::Tensor& logits, int64_t k, double temperature, torch::Tensor& lp, torch::Tensor& idx,
                      c10::optional<torch::Tensor> lse, int64_t vocab_offset, cudaStream_t stream) {
   const int R = logits.size(0), V = logits.size(1), ld = logits.stride(0);
-  const int splits = (V + kTopkChunk - 1) / kTopkChunk;
+  int splits = (V + kTopkChunk - 1) / kTopkChunk, chunk = kTopkChunk;
+  if (K == 1) {   // streaming argmax: about four CTAs per SM in total
+    splits = std::max(1, std::min((V + 4095) / 4096, (148 * 4 + R - 1) / R));
+    chunk = ((V + splits - 1) / splits + 7) / 8 * 8;
+    splits = (V + chunk - 1) / chunk;
+  }
   auto opts = logits.options().dtype(at::kFloat);
   auto pv = torch::empty({R * splits * K}, opts);
   auto pi = torch::empty({R * splits * K}, opts.dtype(at::kInt));
   auto pm = torch::empty({R * splits}, opts);
   auto ps = torch::empty({R * splits}, opts);
-  auto stage1 = lse ? topk_stage1<K, true> : topk_stage1<K, false>;
   const float c2 = (float)(1.4426950408889634 / temperature);   // log2(e) / T
-  stage1<<<R * splits, kTopkThreads, 0, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), V, ld, splits, c2,
-      pv.data_ptr<float>(), pi.data_ptr<int>(), pm.data_ptr<float>(), ps.data_ptr<float>());
+  const auto* xp = reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr());
+  if constexpr (K == 1) {
+    auto a1 = lse ? argmax_stage1<true> : argmax_stage1<false>;
+    a1<<<R * splits, kTopkThreads, 0, stream>>>(xp, V, ld, splits, chunk, c2, pv.data_ptr<float>(),
+                                                 pi.data_ptr<int>(), pm.data_ptr<float>(), ps.data_ptr<float>());
+  } else {
+    auto stage1 = lse ? topk_stage1<K, true> : topk_stage1<K, false>;
+    stage1<<<R * splits, kTopkThreads, 0, stream>>>(xp, V, ld, splits, c2, pv.data_ptr<float>(), pi.data_ptr<int>(),
+                                                     pm.data_ptr<float>(), ps.data_ptr<float>());
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const int warps = 4;
   const size_t smem = (size_t)warps * splits * K * 8;
