@@ -113,6 +113,13 @@ def _write_op_timing(rep, comm, rank, world, steps, ms):
             out["kernels"][k] = [max(cur[0], round(v / steps, 4)), n // steps]
         for k, v in r["phases"].items():
             out["phases"][k] = max(out["phases"].get(k, 0.0), round(v / steps, 4))
+    n_ar = sum(n for k, (v, n) in rep["kernels"].items() if k.endswith("tp_ar_norm"))
+    if comm is not None and getattr(comm, "phase", None) is not None:
+        ph = comm.phase_report(n_ar)           # this rank's fused-reduction phases (PHX_TP_PHASES=1)
+        phs = [None] * world
+        import torch.distributed as dist
+        dist.all_gather_object(phs, ph)
+        out["tp_phases_per_rank"] = phs
     ms_all = [ms] if comm is None else [comm.max_float(ms)]
     out["ms_per_step_max"] = round(ms_all[0] / steps, 3)
     if rank == 0:
@@ -226,6 +233,8 @@ def main():
     phys = int(vis.split(",")[local]) if vis else local
     profile = os.environ.get("PHX_PROFILE_TIMED") == "1"   # ncu --profile-from-start off captures only this
     ops.timing_reset()
+    if getattr(comm, "phase", None) is not None:
+        comm.phase_report(1)                   # restart the fused-reduction phase counters
     with ClockSampler(phys) as clk:
         if profile:
             torch.cuda.profiler.start()

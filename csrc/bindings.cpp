@@ -39,7 +39,8 @@ void gemm_bf16_grouped(torch::Tensor x, torch::Tensor w, torch::Tensor offsets, 
                        torch::Tensor status);
 void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M, int64_t H, double eps,
                 torch::Tensor w, bool out_bf16, bool push_h, torch::Tensor status, std::vector<int64_t> offsets,
-                int64_t s_ld, int64_t off_recv, int64_t mc_base);
+                int64_t s_ld, int64_t off_recv, int64_t mc_base,
+                c10::optional<torch::Tensor> phase);
 void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tensor w, c10::optional<torch::Tensor> ws,
                   torch::Tensor peer_base, int64_t off_recv, int64_t rows_per, int64_t rank, torch::Tensor status,
                   bool hws, bool pair, int64_t bn);

@@ -762,7 +762,8 @@ void spec_accept(torch::Tensor cv, torch::Tensor ci, int64_t ranks, int64_t nch,
   const int R = (int)tokens.size(0), N = (int)tokens.size(1);
   const int64_t S = ranks * nch;
   TORCH_CHECK(cv.is_cuda() && ci.is_cuda() && cv.scalar_type() == at::kFloat && ci.scalar_type() == at::kInt);
-  TORCH_CHECK(S * kc <= kMaxCand && kc <= 64 && N <= kMaxNodes && D >= 1, "spec_accept: sizes out of range");
+  // D = 0 with a one-node tree is a plain draw from the row's top-k / top-p distribution (the final coin)
+  TORCH_CHECK(S * kc <= kMaxCand && kc <= 64 && N <= kMaxNodes && D >= 0, "spec_accept: sizes out of range");
   TORCH_CHECK(cv.numel() == ranks * (int64_t)R * N * nch * kc && ci.numel() == cv.numel(),
               "candidates must be [ranks, R * N, chunks, KC]");
   TORCH_CHECK(tokens.scalar_type() == at::kLong && parent.scalar_type() == at::kLong && tokens.is_contiguous() &&

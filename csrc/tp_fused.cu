@@ -29,7 +29,10 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <map>
+#include <mutex>
 #include <type_traits>
+#include <utility>
 
 #include "common.cuh"
 
@@ -49,6 +52,9 @@ struct TpArgs {
   uint64_t off_partial, off_h, off_y, off_q, off_s, off_flags, off_counter;
   int s_ld;                   // row stride (elements) of the scale matrix [H/128, s_ld]
   uint64_t mc_base;           // multicast (NVLS) address of the workspace, 0 = none: see tp_ar_norm_kernel
+  // optional phase timer [4] (ns sums over launches): start-barrier wait and row work summed over CTAs, the
+  // last CTA's end barrier, CTA count
+  unsigned long long* phase_ns;
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -61,10 +67,11 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 // NVLS (NVLink SHARP) multimem accesses through the workspace's multicast address: one load returns the
-// sum of the W ranks' copies (reduced in the switch), one store writes every rank's copy.
+// sum of the W ranks' copies (reduced in the switch with fp32 accumulation, rounded once to bf16, as the
+// peer-load path rounds its fp32 sum), one store writes every rank's copy.
 __device__ __forceinline__ uint4 mm_ld_reduce_bf16x8(const void* mc) {
   uint4 r;
-  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "l"(mc)
                : "memory");
@@ -104,7 +111,8 @@ __device__ __forceinline__ bool wait_flags(const uint32_t* flags, int W, uint32_
 // end barrier: the last CTA of this rank's launch publishes slot [1][rank] to every peer, waits for all
 // peers' slot [1], then stores the epoch for the next launch (all CTAs of this launch have read it).
 __device__ __forceinline__ void end_barrier(uint8_t* mine, uint64_t off_flags, uint64_t off_counter, uint32_t epoch,
-                                            int W, int rank, const uint64_t* peer_base, int* status) {
+                                            int W, int rank, const uint64_t* peer_base, int* status,
+                                            unsigned long long* phase_ns = nullptr) {
   __shared__ int is_last;
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -116,6 +124,7 @@ __device__ __forceinline__ void end_barrier(uint8_t* mine, uint64_t off_flags, u
   }
   __syncthreads();
   if (is_last) {
+    const uint64_t t0 = phase_ns ? globaltimer() : 0;
     uint32_t* my_flags = reinterpret_cast<uint32_t*>(mine + off_flags);
     if (threadIdx.x < W) {
       __threadfence_system();
@@ -125,13 +134,14 @@ __device__ __forceinline__ void end_barrier(uint8_t* mine, uint64_t off_flags, u
     }
     wait_flags(my_flags + W, W, epoch, status);
     if (threadIdx.x == 0) reinterpret_cast<volatile uint32_t*>(mine + off_counter)[1] = epoch;
+    if (phase_ns && threadIdx.x == 0) atomicAdd(&phase_ns[2], (unsigned long long)(globaltimer() - t0));
   }
 }
 
 // WT: the world size as a compile-time constant (2, 4, 8) so the W peer loads of a 16-byte chunk are all
 // issued before the first is consumed; 0 = runtime world size.
 // NV: the reduce-scatter (pull mode) is one multimem.ld_reduce per 16 bytes (the switch sums the W partials in
-// bf16) and the all-gather of the results is one multimem.st per 16/8/4 bytes instead of W peer stores.
+// fp32 and rounds to bf16) and the all-gather of the results is one multimem.st per 16/8/4 bytes instead of W peer stores.
 template <int MAXC, int WT, bool NV>
 __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
   __shared__ float red[32];
@@ -144,11 +154,13 @@ __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(epoch_word) + 1u;
 
   // ---- 1. start barrier ----
+  const uint64_t t_entry = a.phase_ns ? globaltimer() : 0;
   if (blockIdx.x == 0 && threadIdx.x < W) {
     __threadfence_system();
     st_release_sys(reinterpret_cast<uint32_t*>(base(threadIdx.x) + a.off_flags) + a.rank, epoch);
   }
   const bool ok = wait_flags(my_flags, W, epoch, a.status);
+  const uint64_t t_start = a.phase_ns ? globaltimer() : 0;
 
   // ---- 2./3. reduce my rows, normalize, push to every rank ----
   const int H = a.H, nch = H / 8;
@@ -257,19 +269,26 @@ __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
         for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(y[e]));
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        float isc = 0.f;
+        const float sc = valid ? fp8_block_scale(amax, &isc) : 0.f;
+        const uint2 q = make_uint2(pack_fp8x4(y[0] * isc, y[1] * isc, y[2] * isc, y[3] * isc),
+                                   pack_fp8x4(y[4] * isc, y[5] * isc, y[6] * isc, y[7] * isc));
+        // lane pairs hold adjacent chunks (c, c + 1): the even lane stores both as one 16-byte store
+        const uint32_t nx = __shfl_down_sync(0xffffffffu, q.x, 1), ny = __shfl_down_sync(0xffffffffu, q.y, 1);
+        const bool pair = c + 1 < nch && (threadIdx.x & 31) != 31;
         if (valid) {
-          float isc;
-          const float sc = fp8_block_scale(amax, &isc);
-          const uint2 q = make_uint2(pack_fp8x4(y[0] * isc, y[1] * isc, y[2] * isc, y[3] * isc),
-                                     pack_fp8x4(y[4] * isc, y[5] * isc, y[6] * isc, y[7] * isc));
           const size_t qoff = (size_t)row * H + c * 8;
           const size_t soff = ((size_t)(c >> 4) * a.s_ld + row) * 4;
+          const bool even = (c & 1) == 0;
+          const uint4 q2 = make_uint4(q.x, q.y, nx, ny);
           if constexpr (NV) {
-            mm_st8(mc + a.off_q + qoff, q);
+            if (even && pair) mm_st16(mc + a.off_q + qoff, q2);
+            else if (even) mm_st8(mc + a.off_q + qoff, q);
             if ((c & 15) == 0) mm_st4(mc + a.off_s + soff, __float_as_uint(sc));
           } else {
             for (int p = 0; p < W; ++p) {
-              *reinterpret_cast<uint2*>(base(p) + a.off_q + qoff) = q;
+              if (even && pair) *reinterpret_cast<uint4*>(base(p) + a.off_q + qoff) = q2;
+              else if (even) *reinterpret_cast<uint2*>(base(p) + a.off_q + qoff) = q;
               if ((c & 15) == 0) *reinterpret_cast<float*>(base(p) + a.off_s + soff) = sc;
             }
           }
@@ -278,12 +297,38 @@ __global__ void __launch_bounds__(256) tp_ar_norm_kernel(const TpArgs a) {
     }
   }
 
-  end_barrier(mine, a.off_flags, a.off_counter, epoch, W, a.rank, a.peer_base, a.status);
+  if (a.phase_ns && threadIdx.x == 0) {
+    atomicAdd(&a.phase_ns[0], (unsigned long long)(t_start - t_entry));
+    atomicAdd(&a.phase_ns[1], (unsigned long long)(globaltimer() - t_start));
+    atomicAdd(&a.phase_ns[3], 1ull);
+  }
+  end_barrier(mine, a.off_flags, a.off_counter, epoch, W, a.rank, a.peer_base, a.status, a.phase_ns);
+}
+
+// CTAs of `threads` threads of this kernel resident on the current device at once (SMs x CTAs per SM),
+// queried once per kernel and device
+static int resident_ctas(const void* kern, int threads) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find({kern, dev});
+  if (it != cache.end()) return it->second;
+  int per_sm = 0, sms = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, 0) != cudaSuccess || per_sm <= 0) {
+    (void)cudaGetLastError();
+    per_sm = 2;
+  }
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int n = std::max(1, sms * per_sm);
+  cache[{kern, dev}] = n;
+  return n;
 }
 
 void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M, int64_t H, double eps,
                 torch::Tensor w, bool out_bf16, bool push_h, torch::Tensor status, std::vector<int64_t> offsets,
-                int64_t s_ld, int64_t off_recv, int64_t mc_base) {
+                int64_t s_ld, int64_t off_recv, int64_t mc_base, c10::optional<torch::Tensor> phase) {
   TORCH_CHECK(peer_base.is_cuda() && peer_base.scalar_type() == at::kLong && peer_base.numel() == world);
   TORCH_CHECK(H % 128 == 0 && world >= 1 && world <= 32 && offsets.size() == 7);
   if (M == 0) return;
@@ -311,16 +356,27 @@ void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M,
   a.off_counter = offsets[6];
   a.s_ld = (int)s_ld;
   a.mc_base = (uint64_t)mc_base;
+  a.phase_ns = nullptr;
+  if (phase) {
+    TORCH_CHECK(phase->scalar_type() == at::kLong && phase->numel() >= 4 && phase->is_cuda());
+    a.phase_ns = reinterpret_cast<unsigned long long*>(phase->data_ptr<int64_t>());
+  }
   const int rows_per = (int)((M + world - 1) / world);
-  const int grid = std::max(1, std::min(rows_per, 148 * 4));
   const int maxc = (int)((H / 8 + 255) / 256);
+  // one wave: as many CTAs as are resident at once (every CTA of the launch spins at the start barrier, and
+  // a second wave would serialise behind the first), each walking rows; the residency is queried once per
+  // kernel instantiation and device
+  auto go = [&](void (*kern)(const TpArgs)) {
+    const int grid = std::max(1, std::min(rows_per, resident_ctas(reinterpret_cast<const void*>(kern), 256)));
+    kern<<<grid, 256, 0, stream>>>(a);
+  };
   auto launch_nv = [&](auto wt, auto nv) {
     constexpr int WT = decltype(wt)::value;
     constexpr bool NV = decltype(nv)::value;
-    if (maxc <= 1) tp_ar_norm_kernel<1, WT, NV><<<grid, 256, 0, stream>>>(a);
-    else if (maxc <= 2) tp_ar_norm_kernel<2, WT, NV><<<grid, 256, 0, stream>>>(a);
-    else if (maxc <= 4) tp_ar_norm_kernel<4, WT, NV><<<grid, 256, 0, stream>>>(a);
-    else if (maxc <= 8) tp_ar_norm_kernel<8, WT, NV><<<grid, 256, 0, stream>>>(a);
+    if (maxc <= 1) go(tp_ar_norm_kernel<1, WT, NV>);
+    else if (maxc <= 2) go(tp_ar_norm_kernel<2, WT, NV>);
+    else if (maxc <= 4) go(tp_ar_norm_kernel<4, WT, NV>);
+    else if (maxc <= 8) go(tp_ar_norm_kernel<8, WT, NV>);
     else TORCH_CHECK(false, "hidden size too large");
   };
   auto launch = [&](auto wt) {

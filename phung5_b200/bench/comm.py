@@ -47,7 +47,7 @@ def _time(fn, iters):
     return float(t.item())
 
 
-def ar_norm_sweep(comm, world, iters, H=8192, tokens=(1, 16, 128, 1024, 8192)):
+def ar_norm_sweep(comm, world, iters, H=8192, tokens=(1, 16, 128, 512, 1024, 4096, 8192)):
     """Fused-kernel sweep (a): TP all-reduce + residual + RMSNorm + FP8 quant at hidden 8192 over `tokens`, bf16
     partials and residual ~N(0, 1), unit norm weight. Fused: one ar_norm launch (reduce-scatter by peer loads,
     norm + quant of the owned rows, all-gather of the fp8 rows and scales by peer stores). Baseline: NCCL
@@ -152,10 +152,11 @@ def main():
     H = args.hidden
     comm = FusedCommunicator(max_tokens=8192, hidden=H)
     if args.sweep:
-        out = ar_norm_sweep(comm, world, args.iters, H) + sampling_sweep(comm, world, args.iters)
-        if rank == 0:
-            for o in out:
-                print(json.dumps({"world": world, **o}))
+        for sweep in (lambda: ar_norm_sweep(comm, world, args.iters, H), lambda: sampling_sweep(comm, world, args.iters)):
+            rows = sweep()
+            if rank == 0:
+                for o in rows:
+                    print(json.dumps({"world": world, **o}), flush=True)
         comm.close()
         dist.destroy_process_group()
         return
@@ -200,9 +201,10 @@ def main():
         gemm_ms = _time(lambda: lin((xq, xs), out=comm.partial(m)), args.iters)
         out.append({"op": f"{name}_gemm_alone", "M": m, "K": kdim, "ms": round(gemm_ms, 4)})
         for tag, fn in (("then_ar_norm_pull", pull), ("scatter_then_ar_norm_recv", push)):
+            comm.phase_report(1)
             ms = _time(fn, args.iters)
             out.append({"op": f"{name}_{tag}", "M": m, "K": kdim, "ms": round(ms, 4), "roofline_ms": round(roof_ms, 4),
-                        "frac_of_roofline": round(roof_ms / ms, 3)})
+                        "frac_of_roofline": round(roof_ms / ms, 3), **comm.phase_report(args.iters + 3)})
     v = torch.randn(512, 8, device=dev)
     i = torch.randint(0, 1000, (512, 8), device=dev)
     lse = torch.randn(512, 1, device=dev)

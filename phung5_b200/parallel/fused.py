@@ -90,6 +90,10 @@ class FusedCommunicator(NcclCommunicator):
         dist.barrier(group=self.group)
         self.max_tokens = max_tokens
         self.hidden = hidden
+        # PHX_TP_PHASES=1: the fused reduction sums, per launch, its start-barrier wait and row work over CTAs
+        # and its end barrier (device ns; phase_report())
+        self.phase = (torch.zeros(4, dtype=torch.int64, device=dev)
+                      if os.environ.get("PHX_TP_PHASES") == "1" else None)
 
     def reset(self) -> None:
         """Collective recovery after a kernel reported a peer timeout (status 4): every rank calls it between
@@ -141,13 +145,26 @@ class FusedCommunicator(NcclCommunicator):
         push_h); returns the normalized rows on every rank: (q, s) fp8 or y bf16."""
         off = [self.ws.off[k] for k in ("partial", "h", "y", "q", "s", "flags", "counter")]
         ops.ext().tp_ar_norm(self.peer_base, self.rank, self.size, m, self.hidden, eps, w, out_bf16, push_h,
-                             ops.status_tensor(self.device), off, m, self.ws.off["recv"] if recv else -1, self.mc)
+                             ops.status_tensor(self.device), off, m, self.ws.off["recv"] if recv else -1, self.mc,
+                             self.phase)
         if out_bf16:
             return self.ws.view("y", torch.bfloat16, (m, self.hidden))
         q = self.ws.view("q", torch.float8_e4m3fn, (m, self.hidden))
         s = self.ws.view("s", torch.float32, (self.hidden // 128, m))
         return q, s
 
+
+    def phase_report(self, launches: int) -> dict:
+        """Mean device microseconds per fused-reduction launch (PHX_TP_PHASES=1): a CTA's wait at the start
+        barrier (the peers' arrival skew), its row work, and the end barrier; then the counters restart."""
+        if self.phase is None or launches <= 0:
+            return {}
+        p = self.phase.tolist()
+        ctas = max(1, p[3])
+        out = {"start_wait_us": round(p[0] / ctas / 1e3, 2), "row_work_us": round(p[1] / ctas / 1e3, 2),
+               "end_barrier_us": round(p[2] / launches / 1e3, 2), "ctas_per_launch": round(ctas / launches, 1)}
+        self.phase.zero_()
+        return out
 
     def gather(self, parts):
         """All-gather of small tensors (one exchange for all parts): -> [[world, *p.shape] for p in parts]."""

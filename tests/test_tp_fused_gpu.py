@@ -263,7 +263,11 @@ def _nvls_worker(rank, world, port, q):
             torch.cuda.synchronize()
             ops.check_status(dev)
             hg = fused.h(m).cpu().float()
-            errs.append(((hg - h_ref.float()).abs() / h_ref.float().abs().clamp(min=1e-2)).max().item())
+            # in units of the bf16 step of the partial sum's magnitude: the switch adds in fp32 (in its own
+            # order) and rounds once, then the residual is added and rounded; a wrong sum is many steps off
+            mag = (h0.float().abs() + sum(p.float().abs() for p in parts)).clamp(min=1e-3)
+            step = torch.exp2(torch.floor(torch.log2(mag)) - 7)
+            errs.append(((hg - h_ref.float()).abs() / step).max().item())
         hf = fused.h(m).cpu().float()
         y_ref = hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-5) * wn.float()
         deq = qf.float().cpu().view(m, hd // 128, 128) * sf.cpu().t()[..., None]
@@ -304,7 +308,7 @@ def test_fused_tp_nvls_reduction_matches_definition(world):
     if res[0][1] == "skip":
         pytest.skip("no NVLink multicast on this box")
     for rank, _, h_err, y_err, gather_ok in res:
-        # the switch adds the W bf16 partials in bf16: within a few bf16 steps of the fp32-sum definition
-        assert h_err < 3e-2, h_err
+        # within two bf16 steps (of the summed magnitudes) of the fp32-sum definition
+        assert h_err <= 2.0, h_err
         assert y_err <= 1.0 / 15 + 3e-2, y_err
         assert gather_ok
