@@ -710,10 +710,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         ++swg_iter;
       } else if constexpr (SCATTER) {
-        // stage the warp's 32 rows, then store them row-contiguously (2 or 4 rows per warp instruction) into
-        // each row's owner receive slot: NVLink writes of whole 256/128-byte row segments
+        // each lane stages its row's BN/2 bf16 columns in shared memory and hands them to the TMA engine as one
+        // bulk copy into the row's owner receive slot (over NVLink for a peer): the NVLink writes drain
+        // asynchronously while the epilogue moves on to the next tile (lane-issued 16-byte peer stores kept
+        // the epilogue warps waiting on remote-store issue). A lane rewrites its staging row only after its
+        // previous copy has read it.
         constexpr int ROWB = scatter_row_bytes<BN>();
-        uint8_t* st = reinterpret_cast<uint8_t*>(&s) + ((sizeof(Smem) + 127) & ~size_t(127)) + (size_t)ew * 32 * ROWB;
+        uint8_t* my_st = reinterpret_cast<uint8_t*>(&s) + ((sizeof(Smem) + 127) & ~size_t(127)) +
+                         (size_t)ew * 32 * ROWB + (size_t)lane * ROWB;
+        bulk_wait_read0();
 #pragma unroll
         for (int c = 0; c < CPT / 8; ++c) {
           uint4 v;
@@ -721,23 +726,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           v.y = pack_bf16x2(acc[4 * c + 1].x, acc[4 * c + 1].y);
           v.z = pack_bf16x2(acc[4 * c + 2].x, acc[4 * c + 2].y);
           v.w = pack_bf16x2(acc[4 * c + 3].x, acc[4 * c + 3].y);
-          *reinterpret_cast<uint4*>(st + lane * ROWB + c * 16) = v;
+          *reinterpret_cast<uint4*>(my_st + c * 16) = v;
         }
-        __syncwarp();
-        constexpr int CH = CPT / 8;      // 16-byte chunks per staged row
-        constexpr int RPI = 32 / CH;     // rows per warp instruction
-#pragma unroll 4
-        for (int it = 0; it < 32 / RPI; ++it) {
-          const int rl = it * RPI + lane / CH, ch = lane % CH;
-          const int grow = ti.m0 + my_row0 + sub * 32 + rl, gcol = col0 + ch * 8;
-          if (grow < ti.m_end && grow < M && gcol < N) {
-            const int owner = grow / sc.rows_per;
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(sc.peer_base[owner] + sc.off_recv) +
-                                 ((size_t)sc.rank * sc.rows_per + (grow - owner * sc.rows_per)) * ldc + gcol;
-            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(st + rl * ROWB + ch * 16);
-          }
+        fence_proxy_async_smem();
+        if (row < ti.m_end && row < M && col_ok) {
+          const int owner = row / sc.rows_per;
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(sc.peer_base[owner] + sc.off_recv) +
+                               ((size_t)sc.rank * sc.rows_per + (row - owner * sc.rows_per)) * ldc + col0;
+          const int ncols = N - col0 < CPT ? N - col0 : CPT;     // N % 8 == 0: a multiple of 16 bytes
+          bulk_store(dst, my_st, (uint32_t)ncols * 2);
+          bulk_commit();
         }
-        __syncwarp();
       } else if (row < ti.m_end && row < M && col_ok) {
         __nv_bfloat16* dst = out + (size_t)row * ldc + col0;
         const bool full_cols = col0 + CPT <= N;
@@ -754,7 +753,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   epi_done:;
-    if (SCATTER) __threadfence_system();   // peer stores ordered before the reduction's release flags
+    if (SCATTER) {
+      bulk_wait0();              // this lane's bulk copies have landed
+      __threadfence_system();    // peer stores ordered before the reduction's release flags
+    }
   }
 
   tc_fence_before();
