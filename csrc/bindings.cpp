@@ -43,7 +43,7 @@ void tp_ar_norm(torch::Tensor peer_base, int64_t rank, int64_t world, int64_t M,
                 c10::optional<torch::Tensor> phase);
 void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tensor w, c10::optional<torch::Tensor> ws,
                   torch::Tensor peer_base, int64_t off_recv, int64_t rows_per, int64_t rank, torch::Tensor status,
-                  bool hws, bool pair, int64_t bn);
+                  bool hws, bool pair, int64_t bn, bool bulk);
 void gemm_fp8_swiglu(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch::Tensor ws, torch::Tensor q,
                      torch::Tensor qs, torch::Tensor status);
 void moe_combine(torch::Tensor y, torch::Tensor pos, torch::Tensor w, torch::Tensor local, torch::Tensor out);

@@ -142,6 +142,7 @@ struct ScatterArgs {
   const uint64_t* peer_base;
   uint64_t off_recv;
   int rows_per, rank;
+  int bulk;          // 1: each staged row leaves as one TMA bulk copy; 0: row-contiguous 16-byte lane stores
 };
 
 // SwiGLU epilogue of the gate/up projection (hardware-scaled fp8, BN = 256). The weight rows are interleaved
@@ -716,9 +717,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // the epilogue warps waiting on remote-store issue). A lane rewrites its staging row only after its
         // previous copy has read it.
         constexpr int ROWB = scatter_row_bytes<BN>();
-        uint8_t* my_st = reinterpret_cast<uint8_t*>(&s) + ((sizeof(Smem) + 127) & ~size_t(127)) +
-                         (size_t)ew * 32 * ROWB + (size_t)lane * ROWB;
-        bulk_wait_read0();
+        uint8_t* st = reinterpret_cast<uint8_t*>(&s) + ((sizeof(Smem) + 127) & ~size_t(127)) + (size_t)ew * 32 * ROWB;
+        uint8_t* my_st = st + (size_t)lane * ROWB;
+        if (sc.bulk) bulk_wait_read0();
 #pragma unroll
         for (int c = 0; c < CPT / 8; ++c) {
           uint4 v;
@@ -728,14 +729,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           v.w = pack_bf16x2(acc[4 * c + 3].x, acc[4 * c + 3].y);
           *reinterpret_cast<uint4*>(my_st + c * 16) = v;
         }
-        fence_proxy_async_smem();
-        if (row < ti.m_end && row < M && col_ok) {
-          const int owner = row / sc.rows_per;
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(sc.peer_base[owner] + sc.off_recv) +
-                               ((size_t)sc.rank * sc.rows_per + (row - owner * sc.rows_per)) * ldc + col0;
-          const int ncols = N - col0 < CPT ? N - col0 : CPT;     // N % 8 == 0: a multiple of 16 bytes
-          bulk_store(dst, my_st, (uint32_t)ncols * 2);
-          bulk_commit();
+        if (sc.bulk) {
+          fence_proxy_async_smem();
+          if (row < ti.m_end && row < M && col_ok) {
+            const int owner = row / sc.rows_per;
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(sc.peer_base[owner] + sc.off_recv) +
+                                 ((size_t)sc.rank * sc.rows_per + (row - owner * sc.rows_per)) * ldc + col0;
+            const int ncols = N - col0 < CPT ? N - col0 : CPT;     // N % 8 == 0: a multiple of 16 bytes
+            bulk_store(dst, my_st, (uint32_t)ncols * 2);
+            bulk_commit();
+          }
+        } else {
+          // the warp's 32 staged rows stored row-contiguously (2 or 4 rows per warp instruction)
+          __syncwarp();
+          constexpr int CH = CPT / 8;      // 16-byte chunks per staged row
+          constexpr int RPI = 32 / CH;     // rows per warp instruction
+#pragma unroll 4
+          for (int it = 0; it < 32 / RPI; ++it) {
+            const int rl = it * RPI + lane / CH, ch = lane % CH;
+            const int grow = ti.m0 + my_row0 + sub * 32 + rl, gcol = col0 + ch * 8;
+            if (grow < ti.m_end && grow < M && gcol < N) {
+              const int owner = grow / sc.rows_per;
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(sc.peer_base[owner] + sc.off_recv) +
+                                   ((size_t)sc.rank * sc.rows_per + (grow - owner * sc.rows_per)) * ldc + gcol;
+              *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(st + rl * ROWB + ch * 16);
+            }
+          }
+          __syncwarp();
         }
       } else if (row < ti.m_end && row < M && col_ok) {
         __nv_bfloat16* dst = out + (size_t)row * ldc + col0;
@@ -754,7 +774,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   epi_done:;
     if (SCATTER) {
-      bulk_wait0();              // this lane's bulk copies have landed
+      if (sc.bulk) bulk_wait0();   // this lane's bulk copies have landed
       __threadfence_system();    // peer stores ordered before the reduction's release flags
     }
   }
@@ -905,7 +925,7 @@ void launch_gemm(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& 
                  int groups = 0, int split = 1) {
   launch_gemm_ptr<BN, FP8, false, HWS, PAIR>(a, b, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (int)out.stride(0),
                            (int)out.size(1), sa, sb, status, stream, max_ctas, grp_off, groups,
-                           ScatterArgs{nullptr, 0, 1, 0}, nullptr, 0, SwigluArgs{nullptr, nullptr, 0}, split);
+                           ScatterArgs{nullptr, 0, 1, 0, 0}, nullptr, 0, SwigluArgs{nullptr, nullptr, 0}, split);
 }
 
 // Hardware scaling with 256-wide tiles leaves TMEM room for one accumulator only, so the epilogue drain is
@@ -974,7 +994,7 @@ void gemm_fp8_swiglu(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torch
   auto stream = at::cuda::getCurrentCUDAStream();
   launch_gemm_ptr<256, true, false, true, false, true>(
       xq, wq, nullptr, N, N, xs.data_ptr<float>(), ws.data_ptr<float>(), status.data_ptr<int>(), stream, 0, nullptr,
-      0, ScatterArgs{nullptr, 0, 1, 0}, nullptr, 0,
+      0, ScatterArgs{nullptr, 0, 1, 0, 0}, nullptr, 0,
       SwigluArgs{reinterpret_cast<uint8_t*>(q.data_ptr()), qs.data_ptr<float>(), F});
 }
 
@@ -1003,7 +1023,7 @@ void gemm_fp8_grouped(torch::Tensor xq, torch::Tensor xs, torch::Tensor wq, torc
     launch_gemm_ptr<256, true, false, true>(xq, wq, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
                                             (int)out.stride(0), N, xs.data_ptr<float>(), ws.data_ptr<float>(),
                                             status.data_ptr<int>(), stream, 0, offsets.data_ptr<int>(), G,
-                                            ScatterArgs{nullptr, 0, 1, 0}, rows->data_ptr<int>(), M);
+                                            ScatterArgs{nullptr, 0, 1, 0, 0}, rows->data_ptr<int>(), M);
   } else if (hws)
     launch_gemm<256, true, true>(xq, wq, out, xs.data_ptr<float>(), ws.data_ptr<float>(), status.data_ptr<int>(),
                                  stream, 0, offsets.data_ptr<int>(), G);
@@ -1048,7 +1068,7 @@ void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, torch::Tenso
 // Row-parallel projection with the scatter epilogue (see ScatterArgs): fp8 (ws defined) or bf16 operands.
 void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tensor w, c10::optional<torch::Tensor> ws,
                   torch::Tensor peer_base, int64_t off_recv, int64_t rows_per, int64_t rank, torch::Tensor status,
-                  bool hws, bool pair, int64_t bn) {
+                  bool hws, bool pair, int64_t bn, bool bulk) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && peer_base.is_cuda() && peer_base.scalar_type() == at::kLong);
   const int M = x.size(0), K = x.size(1), N = w.size(0);
   TORCH_CHECK(w.size(1) == K && N % 8 == 0 && x.stride(1) == 1 && w.stride(1) == 1);
@@ -1057,7 +1077,7 @@ void gemm_scatter(torch::Tensor x, c10::optional<torch::Tensor> xs, torch::Tenso
   const at::cuda::CUDAGuard guard(x.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   const ScatterArgs sc{reinterpret_cast<const uint64_t*>(peer_base.data_ptr<int64_t>()), (uint64_t)off_recv,
-                       (int)rows_per, (int)rank};
+                       (int)rows_per, (int)rank, bulk ? 1 : 0};
   const int b = bn > 0 ? (int)bn : pick_bn(M, N);
   if (ws.has_value()) {
     TORCH_CHECK(x.scalar_type() == at::kFloat8_e4m3fn && w.scalar_type() == at::kFloat8_e4m3fn && K % 128 == 0);

@@ -7,9 +7,9 @@ Times, with CUDA events after warm-up and the maximum over ranks:
            shape (M = 4096 rows of H = 8192) and the draft shape (M = 512);
   gather   the fused candidate exchange (512 rows x top-8 (value, index) + lse);
   nccl     torch.distributed all_reduce of the same [M, H] bf16 partial (the unfused baseline's collective).
---sweep: the fused-kernel sweep instead: AR + residual + RMSNorm + FP8 quant at tokens {1, 16, 128, 1024, 8192}
-and vocab-sharded top-k / top-p sampling at batch {1, 64, 256} x k {1, 8, 50}, each against NCCL + the separate
-kernels.
+--sweep: the fused-kernel sweep instead: AR + residual + RMSNorm + FP8 quant at tokens {1 ... 8192} and
+vocab-sharded top-k / top-p sampling at batch {1, 64, 256} x k {1, 8, 50}, each against NCCL + the separate
+kernels, timed both as eager launches and as CUDA-graph replays (the engine's step is a graph).
 NVLink bytes per ar_norm per GPU: (W-1)/W of the partial rows read (bf16) plus (W-1)/W of the fp8 rows and
 scales written; reported against the measured peer-copy bandwidth of 770 GB/s per direction.
 o_proj / down_proj + reduction: the fused path (GEMM epilogue stores rows to their owners, reduction over local
@@ -47,6 +47,27 @@ def _time(fn, iters):
     return float(t.item())
 
 
+def _time_graph(fn, iters):
+    """Device time of one call captured in a CUDA graph (replayed `iters` times between events, max over
+    ranks): the engine runs these paths inside its step graph, so host launch cost is not part of it. Returns
+    (ms, graph); the caller drops the graph before the communicator or process group is torn down."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    dist.barrier()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = _time(g.replay, iters)
+    return ms, g
+
+
 def ar_norm_sweep(comm, world, iters, H=8192, tokens=(1, 16, 128, 512, 1024, 4096, 8192)):
     """Fused-kernel sweep (a): TP all-reduce + residual + RMSNorm + FP8 quant at hidden 8192 over `tokens`, bf16
     partials and residual ~N(0, 1), unit norm weight. Fused: one ar_norm launch (reduce-scatter by peer loads,
@@ -76,6 +97,9 @@ def ar_norm_sweep(comm, world, iters, H=8192, tokens=(1, 16, 128, 512, 1024, 409
         p_ms = _time(lambda: comm.ar_norm(m, w, 1e-5), iters)        # peer loads / stores only
         comm.mc = mc
         n_ms = _time(nccl, iters)
+        fg_ms, g1 = _time_graph(lambda: comm.ar_norm(m, w, 1e-5), iters)
+        ng_ms, g2 = _time_graph(nccl, iters)
+        del g1, g2
         nv = (world - 1) / world * m * H * (2 + 1 + 4 / 128)
         # with NVLS the busier direction carries each GPU's partial rows for the other owners (read by the
         # switch) plus its own result rows once (the switch copies them to every rank)
@@ -85,7 +109,9 @@ def ar_norm_sweep(comm, world, iters, H=8192, tokens=(1, 16, 128, 512, 1024, 409
                      "fused_p2p_ms": round(p_ms, 4), "nccl_plus_kernel_ms": round(n_ms, 4),
                      "speedup": round(n_ms / f_ms, 2), "roofline_ms": round(roof, 5),
                      "fused_frac_of_roofline": round(roof / f_ms, 3),
-                     "p2p_frac_of_roofline": round(nv / NVLINK_GBS / 1e6 / p_ms, 3)})
+                     "p2p_frac_of_roofline": round(nv / NVLINK_GBS / 1e6 / p_ms, 3),
+                     "graph_fused_ms": round(fg_ms, 4), "graph_nccl_plus_kernel_ms": round(ng_ms, 4),
+                     "graph_speedup": round(ng_ms / fg_ms, 2)})
     return rows
 
 
@@ -132,12 +158,17 @@ def sampling_sweep(comm, world, iters, vocab=128256, batches=(1, 64, 256), ks=(1
             f_ms = _time(fused, iters)
             n_ms = _time(nccl, iters)
             same = bool(torch.equal(res["f"], res["n"]))
+            fg_ms, g1 = _time_graph(fused, iters)
+            ng_ms, g2 = _time_graph(nccl, iters)
+            del g1, g2
             nch = int(ops.ext().sample_chunks(vl))
             roof = (b * vl * 2 / hbm / 1e6) + (world - 1) * b * nch * kc * 8 / NVLINK_GBS / 1e6
             rows.append({"op": "sweep_sampling", "batch": b, "k": k, "top_p": top_p, "vocab_shard": vl,
                          "fused_ms": round(f_ms, 4), "nccl_plus_kernel_ms": round(n_ms, 4),
                          "speedup": round(n_ms / f_ms, 2), "roofline_ms": round(roof, 5),
-                         "fused_frac_of_roofline": round(roof / f_ms, 3), "same_tokens": same})
+                         "fused_frac_of_roofline": round(roof / f_ms, 3), "same_tokens": same,
+                         "graph_fused_ms": round(fg_ms, 4), "graph_nccl_plus_kernels_ms": round(ng_ms, 4),
+                         "graph_speedup": round(ng_ms / fg_ms, 2)})
     return rows
 
 

@@ -71,6 +71,22 @@ def case_gemm_fp8(m, n, k, bn=0):
     return fn, 2.0 * m * n * k, "fp8"
 
 
+def case_gemm_scatter_local(m, n, k, world=8, bulk=True):
+    """The row-parallel projection's scatter epilogue with W local buffers standing in for the ranks' receive
+    slots: the epilogue's cost without NVLink (compare with the plain GEMM of the same shape)."""
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    xq, xs = ops.act_quant(x)
+    wq = (torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.05).to(FP8_DTYPE)
+    ws = pow2_scale(torch.rand((n + 127) // 128, k // 128, device="cuda") * 4.48)
+    rows_per = (m + world - 1) // world
+    bufs = [torch.empty(world, rows_per, n, device="cuda", dtype=torch.bfloat16) for _ in range(world)]
+    base = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device="cuda")
+    st = ops.status_tensor(x.device)
+    fn = lambda: ops.ext().gemm_scatter(xq, xs, wq, ws, base, 0, rows_per, 1, st, ops.FP8_HW_SCALE, False, 0, bulk)
+    fn.keep = bufs
+    return fn, 2.0 * m * n * k, "fp8"
+
+
 def case_moe_gate_up_gather(tokens, per_expert, n, k, gather=True):
     """One expert's gate/up grouped GEMM with the dispatch inside the A loads (TMA gather4 of token rows), or
     (gather=False) an explicit row gather of the fp8 activations and scales followed by the plain grouped GEMM."""
@@ -293,6 +309,9 @@ CASES = {
     "gemm_fp8_down_tp8_bn128": lambda: case_gemm_fp8(4096, 8192, 3584, bn=128),
     "gemm_fp8_down_tp8": lambda: case_gemm_fp8(4096, 8192, 3584),
     "gemm_bf16_lm_head_tp8": lambda: case_gemm_bf16(4096, 16032, 8192),
+    "gemm_scatter_local_o_tp8": lambda: case_gemm_scatter_local(4096, 8192, 1024),
+    "gemm_scatter_local_o_tp8_lane": lambda: case_gemm_scatter_local(4096, 8192, 1024, bulk=False),
+    "gemm_scatter_local_down_tp8": lambda: case_gemm_scatter_local(4096, 8192, 3584),
     "attn_prefix_tc_tp8": lambda: case_attention("prefix", "tc", hq=8, hkv=1),
     "attn_suffix_tc_tp8": lambda: case_attention("suffix", "tc", hq=8, hkv=1),
     "silu_mul_quant_tp8": lambda: case_silu_quant(4096, 3584),

@@ -151,6 +151,10 @@ GEMM_PAIR = os.environ.get("PHX_GEMM_PAIR", "0") == "1"
 # Plain GEMMs whose last wave of tiles leaves most SMs idle split those tiles over K (csrc/gemm_sm100.cu,
 # SplitArgs); PHX_GEMM_SPLIT=0 keeps every tile whole unless a caller asks for a split.
 GEMM_SPLIT = os.environ.get("PHX_GEMM_SPLIT", "1") != "0"
+# The scatter epilogue (row-parallel projections under tensor parallelism) hands each staged output row to the
+# TMA engine as one bulk copy into its owner's receive slot; PHX_SCATTER_BULK=0 stores the rows with
+# row-contiguous 16-byte lane stores instead.
+SCATTER_BULK = os.environ.get("PHX_SCATTER_BULK", "1") != "0"
 
 
 def _table_choice(kind: str, n: int, k: int, m: int, bn: int, hw_scale, pair, use_table: bool, split=None):

@@ -140,7 +140,7 @@ class FusedCommunicator(NcclCommunicator):
                                              None, True)
         ops.ext().gemm_scatter(xq, xs, lin.w, lin.ws, self.peer_base, self.ws.off["recv"], rows_per, self.rank,
                                ops.status_tensor(self.device), ops.FP8_HW_SCALE if hws is None else hws,
-                               ops.GEMM_PAIR if pair is None else pair, bn)
+                               ops.GEMM_PAIR if pair is None else pair, bn, ops.SCATTER_BULK)
 
     def ar_norm(self, m: int, w: torch.Tensor, eps: float, out_bf16: bool = False, push_h: bool = False,
                 recv: bool = False):

@@ -482,10 +482,11 @@ def test_selftest_cli_passes():
     assert all(v["ok"] for v in res.values()), res
 
 
+@pytest.mark.parametrize("bulk", [True, False])
 @pytest.mark.parametrize("fp8,m,n,k,hws", [(True, 4096, 8192, 1024, True), (True, 300, 1024, 512, True),
                                            (False, 200, 512, 256, False), (True, 77, 256, 128, True),
                                            (True, 300, 1024, 512, False), (True, 4096, 8192, 3584, True)])
-def test_gemm_scatter_epilogue(fp8, m, n, k, hws):
+def test_gemm_scatter_epilogue(fp8, m, n, k, hws, bulk):
     """The row-parallel projection's scatter epilogue: row r lands in buffer owner(r) = r // rows_per at slot
     [rank][r - owner * rows_per]. Four local buffers stand in for the peers' receive regions."""
     world, rank = 4, 1
@@ -497,11 +498,12 @@ def test_gemm_scatter_epilogue(fp8, m, n, k, hws):
     if fp8:
         xq, xs = quant_act_block(x)
         wq, ws = quant_weight_block(w)
-        ops.ext().gemm_scatter(xq, xs, wq, ws, base, 0, rows_per, rank, ops.status_tensor(DEV), hws, False, 0)
+        ops.ext().gemm_scatter(xq, xs, wq, ws, base, 0, rows_per, rank, ops.status_tensor(DEV), hws, False, 0, bulk)
         ref = ops.gemm_fp8_block(xq, xs, wq, ws, hw_scale=hws, split=1)     # the scatter epilogue never splits K
     else:
         xb, wb = x.bfloat16(), w.bfloat16()
-        ops.ext().gemm_scatter(xb, None, wb, None, base, 0, rows_per, rank, ops.status_tensor(DEV), False, False, 0)
+        ops.ext().gemm_scatter(xb, None, wb, None, base, 0, rows_per, rank, ops.status_tensor(DEV), False, False, 0,
+                               bulk)
         ref = ops.gemm_bf16(xb, wb, split=1)
     torch.cuda.synchronize()
     for o in range(world):
