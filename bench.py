@@ -263,10 +263,16 @@ def main():
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
+    step_wall = []
     for _ in range(args.steps):
+        ts = time.perf_counter()
         for o in eng.step():
             e2e_tokens += len(o.new_tokens)
+        step_wall.append(round(1e3 * (time.perf_counter() - ts), 1))
     e2e_s = time.perf_counter() - t0
+    if os.environ.get("PHX_STEP_TIMES") == "1" and rank == 0:   # per-step wall ms of the end-to-end region
+        print(json.dumps({"e2e_step_wall_ms": step_wall, "graph_replays": eng.stats.get("graph_replays"),
+                          "graphs": len(eng._graphs) if eng._graphs is not None else None}), file=sys.stderr)
     e2e_s = comm.max_float(e2e_s) if comm is not None else e2e_s
     h2d = (eng.stats["h2d_bytes"] + UPLOADED_BYTES[0] - h2d0) / args.steps
     d2h = (eng.stats["d2h_bytes"] - d2h0) / args.steps
