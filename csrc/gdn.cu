@@ -6,9 +6,10 @@
 // (the reference's per-token rule, docker/opt/kern/a2/kernels.py:85-96, with g = -exp(A_log) *
 // softplus(a + dt_bias) and beta = sigmoid(b) computed by gdn_gates below).
 //
-// Design: one CTA per (request, value head), 128 threads; thread j owns the state column S[:, j] in
-// registers, so S^T k and S^T q are thread-local dot products and the rank-1 update is thread-local; only
-// the L2 norms of q and k need a block reduction. The state is read once per launch.
+// Design: one CTA per (request, value head), 256 threads; a pair of threads owns the state column S[:, j] in
+// registers (64 rows each), so S^T k and S^T q are pair-local dot products (one shuffle) and the rank-1
+// update is thread-local; the L2 norms of a chunk of tokens' q and k are formed up front (one warp per
+// token), so the token loop has no block barrier. The state is read once per launch.
 //   gdn_verify: runs a request's T verify tokens from its committed state WITHOUT writing the state;
 //               writes outputs and a stash (normalised k, v', g) per token — the reference's
 //               "Track B" verify (docker/opt/kern/braw/kernels.py:69-280) without per-token states.
@@ -30,69 +31,121 @@ namespace phx {
 constexpr int kGdnK = 128;
 constexpr int kGdnV = 128;
 
-__device__ __forceinline__ float block_sum128(float v, float* red) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
-  const float t = red[0] + red[1] + red[2] + red[3];
-  __syncthreads();
-  return t;
-}
-
 // q, k, v: [T, H*, 128] bf16 (rows = tokens of the batch); g, beta: [T, HV] fp32; state: [slots, HV, K, V] fp32
 // (K-major rows: state[slot][h][i][j]). tok_start [R+1]; slot[R] = state slot of request r.
 // GQA: value head h uses q/k head h / (HV / HK).
+// 256 threads: the pair of threads (2j, 2j + 1) owns state column j, each half of its 128 rows in registers
+// (64 floats), and the pair adds its two partial dot products with one shuffle; each dot product keeps four
+// independent accumulators (one chain of 64 dependent FMAs would leave the schedulers waiting on FMA
+// latency). Tokens are taken in chunks of kGdnChunk: the 8 warps first normalise the chunk's q and k rows into
+// shared memory (one warp per token, warp-shuffle norms) with its decays and betas, then every thread runs the
+// chunk's tokens back to back with no block barrier inside the chunk. Column j's update only reads column j.
+constexpr int kGdnChunk = 16;
+constexpr int kGdnHalf = kGdnK / 2;
+constexpr int kGdnRowPad = kGdnK + 8;   // half 1 of a row starts 4 floats past 64: the two halves' float4 reads
+                                        // of one step land in different banks
 template <bool WRITE_STATE, bool STASH>
-__global__ void __launch_bounds__(128) gdn_recurrent_kernel(
+__global__ void __launch_bounds__(256) gdn_recurrent_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
     const float* __restrict__ g, const float* __restrict__ beta, float* __restrict__ state,
     const int* __restrict__ tok_start, const int* __restrict__ slot, int HK, int HV, float scale,
     __nv_bfloat16* __restrict__ out, float* __restrict__ st_k, float* __restrict__ st_v, float* __restrict__ st_g) {
-  __shared__ float sq[kGdnK], sk[kGdnK];
-  __shared__ float red[4];
-  const int r = blockIdx.x, h = blockIdx.y, j = threadIdx.x;
+  __shared__ __align__(16) float sq[kGdnChunk][kGdnRowPad], sk[kGdnChunk][kGdnRowPad];
+  __shared__ float sdec[kGdnChunk], sbeta[kGdnChunk];
+  const int r = blockIdx.x, h = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int j = tid >> 1, half = tid & 1;
   const int hk = h / (HV / HK);
   const int t0 = tok_start[r], t1 = tok_start[r + 1];
   float* S = state + ((size_t)slot[r] * HV + h) * kGdnK * kGdnV;
-  float col[kGdnK];
+  float col[kGdnHalf];
 #pragma unroll
-  for (int i = 0; i < kGdnK; ++i) col[i] = S[(size_t)i * kGdnV + j];
-  for (int t = t0; t < t1; ++t) {
-    const float qi = __bfloat162float(q[((size_t)t * HK + hk) * kGdnK + j]);
-    const float ki = __bfloat162float(k[((size_t)t * HK + hk) * kGdnK + j]);
-    const float qn = rsqrtf(block_sum128(qi * qi, red) + 1e-6f);
-    const float kn = rsqrtf(block_sum128(ki * ki, red) + 1e-6f);
-    sq[j] = qi * qn * scale;
-    sk[j] = ki * kn;
+  for (int i = 0; i < kGdnHalf; ++i) col[i] = S[(size_t)(half * kGdnHalf + i) * kGdnV + j];
+  const int hoff = half * (kGdnHalf + 4);    // this thread's half inside a padded shared row
+  for (int c0 = t0; c0 < t1; c0 += kGdnChunk) {
+    const int n = min(kGdnChunk, t1 - c0);
+    // ---- normalise the chunk's q and k rows (warp w: tokens w, w + 8) ----
+    for (int u = warp; u < n; u += 8) {
+      const int t = c0 + u;
+      float qv[4], kv4[4], sqq = 0.f, skk = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = lane + 32 * e;
+        qv[e] = __bfloat162float(q[((size_t)t * HK + hk) * kGdnK + i]);
+        kv4[e] = __bfloat162float(k[((size_t)t * HK + hk) * kGdnK + i]);
+        sqq += qv[e] * qv[e];
+        skk += kv4[e] * kv4[e];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        sqq += __shfl_xor_sync(0xffffffffu, sqq, o);
+        skk += __shfl_xor_sync(0xffffffffu, skk, o);
+      }
+      const float qn = rsqrtf(sqq + 1e-6f) * scale, kn = rsqrtf(skk + 1e-6f);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = lane + 32 * e;
+        const int pi = i < kGdnHalf ? i : i + 4;
+        sq[u][pi] = qv[e] * qn;
+        sk[u][pi] = kv4[e] * kn;
+        if (STASH) st_k[((size_t)t * HV + h) * kGdnK + i] = kv4[e] * kn;
+      }
+      if (lane == 0) {
+        const float gt = g[(size_t)t * HV + h];
+        sdec[u] = expf(gt);
+        sbeta[u] = beta[(size_t)t * HV + h];
+        if (STASH) st_g[(size_t)t * HV + h] = gt;
+      }
+    }
     __syncthreads();
-    const float gt = g[(size_t)t * HV + h], bt = beta[(size_t)t * HV + h];
-    const float decay = expf(gt);
-    float kv = 0.f;
+    // ---- the chunk's tokens: decay, S^T k, delta-rule update, S^T q ----
+    for (int u = 0; u < n; ++u) {
+      const int t = c0 + u;
+      const float vj = __bfloat162float(v[((size_t)t * HV + h) * kGdnV + j]);
+      const float decay = sdec[u];
+      const float4* k4 = reinterpret_cast<const float4*>(&sk[u][hoff]);
+      const float4* q4 = reinterpret_cast<const float4*>(&sq[u][hoff]);
+      float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < kGdnK; ++i) {
-      col[i] *= decay;
-      kv = fmaf(col[i], sk[i], kv);
-    }
-    const float vj = __bfloat162float(v[((size_t)t * HV + h) * kGdnV + j]);
-    const float vp = (vj - kv) * bt;
-    float o = 0.f;
+      for (int i = 0; i < kGdnHalf / 4; ++i) {
+        const float4 kk = k4[i];
+        col[4 * i] *= decay;
+        col[4 * i + 1] *= decay;
+        col[4 * i + 2] *= decay;
+        col[4 * i + 3] *= decay;
+        a4.x = fmaf(col[4 * i], kk.x, a4.x);
+        a4.y = fmaf(col[4 * i + 1], kk.y, a4.y);
+        a4.z = fmaf(col[4 * i + 2], kk.z, a4.z);
+        a4.w = fmaf(col[4 * i + 3], kk.w, a4.w);
+      }
+      float kv = (a4.x + a4.y) + (a4.z + a4.w);
+      kv += __shfl_xor_sync(0xffffffffu, kv, 1);
+      const float vp = (vj - kv) * sbeta[u];
+      float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < kGdnK; ++i) {
-      col[i] = fmaf(sk[i], vp, col[i]);
-      o = fmaf(col[i], sq[i], o);
+      for (int i = 0; i < kGdnHalf / 4; ++i) {
+        const float4 kk = k4[i], qq = q4[i];
+        col[4 * i] = fmaf(kk.x, vp, col[4 * i]);
+        col[4 * i + 1] = fmaf(kk.y, vp, col[4 * i + 1]);
+        col[4 * i + 2] = fmaf(kk.z, vp, col[4 * i + 2]);
+        col[4 * i + 3] = fmaf(kk.w, vp, col[4 * i + 3]);
+        o4.x = fmaf(col[4 * i], qq.x, o4.x);
+        o4.y = fmaf(col[4 * i + 1], qq.y, o4.y);
+        o4.z = fmaf(col[4 * i + 2], qq.z, o4.z);
+        o4.w = fmaf(col[4 * i + 3], qq.w, o4.w);
+      }
+      float o = (o4.x + o4.y) + (o4.z + o4.w);
+      o += __shfl_xor_sync(0xffffffffu, o, 1);
+      if (half == 0) {
+        out[((size_t)t * HV + h) * kGdnV + j] = __float2bfloat16(o);
+        if (STASH) st_v[((size_t)t * HV + h) * kGdnV + j] = vp;
+      }
     }
-    out[((size_t)t * HV + h) * kGdnV + j] = __float2bfloat16(o);
-    if (STASH) {
-      st_v[((size_t)t * HV + h) * kGdnV + j] = vp;
-      st_k[((size_t)t * HV + h) * kGdnK + j] = sk[j];
-      if (j == 0) st_g[(size_t)t * HV + h] = gt;
-    }
-    __syncthreads();
+    __syncthreads();   // the next chunk rewrites the shared rows
   }
   if (WRITE_STATE) {
 #pragma unroll
-    for (int i = 0; i < kGdnK; ++i) S[(size_t)i * kGdnV + j] = col[i];
+    for (int i = 0; i < kGdnHalf; ++i) S[(size_t)(half * kGdnHalf + i) * kGdnV + j] = col[i];
   }
 }
 
@@ -213,13 +266,13 @@ void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Ten
   float* sg = stash ? st_g->data_ptr<float>() : nullptr;
   auto o = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   if (write_state && stash)
-    gdn_recurrent_kernel<true, true><<<grid, 128, 0, stream>>>(P(q), P(k), P(v), g.data_ptr<float>(), beta.data_ptr<float>(),
+    gdn_recurrent_kernel<true, true><<<grid, 256, 0, stream>>>(P(q), P(k), P(v), g.data_ptr<float>(), beta.data_ptr<float>(),
         state.data_ptr<float>(), tok_start.data_ptr<int>(), slot.data_ptr<int>(), HK, HV, (float)scale, o, sk, sv, sg);
   else if (write_state)
-    gdn_recurrent_kernel<true, false><<<grid, 128, 0, stream>>>(P(q), P(k), P(v), g.data_ptr<float>(), beta.data_ptr<float>(),
+    gdn_recurrent_kernel<true, false><<<grid, 256, 0, stream>>>(P(q), P(k), P(v), g.data_ptr<float>(), beta.data_ptr<float>(),
         state.data_ptr<float>(), tok_start.data_ptr<int>(), slot.data_ptr<int>(), HK, HV, (float)scale, o, sk, sv, sg);
   else
-    gdn_recurrent_kernel<false, true><<<grid, 128, 0, stream>>>(P(q), P(k), P(v), g.data_ptr<float>(), beta.data_ptr<float>(),
+    gdn_recurrent_kernel<false, true><<<grid, 256, 0, stream>>>(P(q), P(k), P(v), g.data_ptr<float>(), beta.data_ptr<float>(),
         state.data_ptr<float>(), tok_start.data_ptr<int>(), slot.data_ptr<int>(), HK, HV, (float)scale, o, sk, sv, sg);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -406,6 +406,35 @@ def test_gdn_kernels_match_definitions():
     assert _rel(y2.float().cpu(), y2c) < 3e-2 and _rel(sg.cpu(), sc) < 3e-2
 
 
+@pytest.mark.parametrize("write_state", [False, True])
+def test_gdn_recurrent_many_requests(write_state):
+    """Many (request, value head) items and token counts from 0 to 37 (chunks of 16, a partial chunk, an empty
+    request): outputs, stash and written states against the plain-torch definition."""
+    from phung5_b200.ops import gdn as G
+    g = torch.Generator().manual_seed(5)
+    R, HK, HV = 40, 4, 8
+    lens = [(i * 7) % 38 for i in range(R)]
+    ts = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+    T = int(ts[-1])
+    q = torch.randn(T, HK, 128, generator=g).bfloat16()
+    k = torch.randn(T, HK, 128, generator=g).bfloat16()
+    v = torch.randn(T, HV, 128, generator=g).bfloat16()
+    gg = -torch.rand(T, HV, generator=g) * 0.5
+    beta = torch.rand(T, HV, generator=g)
+    slot = torch.randperm(R + 3, generator=g)[:R].to(torch.int32)
+    state = torch.randn(R + 3, HV, 128, 128, generator=g) * 0.02
+    st_c = state.clone()
+    out_c, stash_c = G.gdn_recurrent(q.float(), k.float(), v.float(), gg, beta, st_c, ts, slot, 0.088, write_state)
+    st_g = state.to(DEV)
+    out_g, stash_g = G.gdn_recurrent(q.to(DEV), k.to(DEV), v.to(DEV), gg.to(DEV), beta.to(DEV), st_g, ts.to(DEV),
+                                     slot.to(DEV), 0.088, write_state)
+    ops.check_status()
+    assert _rel(out_g.float().cpu(), out_c) < 2e-2
+    assert _rel(stash_g[0].cpu(), stash_c[0]) < 1e-3 and _rel(stash_g[1].cpu(), stash_c[1]) < 2e-2
+    assert torch.equal(stash_g[2].cpu(), stash_c[2])
+    assert _rel(st_g.cpu(), st_c) < (2e-2 if write_state else 1e-7)
+
+
 @pytest.mark.parametrize("t,sizes,n,k", [(300, [120, 0, 333, 47], 512, 1024), (64, [5, 70], 256, 256)])
 def test_gemm_grouped_row_gather_equals_gathered_copy(t, sizes, n, k):
     """The grouped GEMM's A loads gather activation rows by index (TMA gather4, the MoE dispatch fused into
