@@ -146,6 +146,10 @@ def main():
     ap.add_argument("--mode", default="tree", choices=["tree", "chain"])
     ap.add_argument("--num-draft", type=int, default=4)
     ap.add_argument("--comm", default="fused", choices=["nccl", "fused"])
+    ap.add_argument("--accept", default="geometric", choices=["geometric", "greedy", "sample"],
+                    help="geometric: synthetic accept lengths (random weights never agree with their drafter); "
+                         "greedy: target argmax along the tree; sample: seeded top-k 50 / top-p 0.9 / T = 1 target "
+                         "sampling with the device accept walk (a step-cost comparison, not a throughput line)")
     ap.add_argument("--no-cascade", action="store_true")
     ap.add_argument("--layers", type=int, default=0, help="override layer count (smoke runs only; not a bench value)")
     ap.add_argument("--model-path", default=None, help="HF checkpoint directory instead of random-init weights")
@@ -187,7 +191,8 @@ def main():
     if args.layers:
         mc.num_layers = args.layers
     spec = SpecConfig(mode=args.mode, tree_nodes=args.tree_nodes, topk=args.topk, depth=args.depth,
-                      num_draft=args.num_draft, accept="geometric", accept_p=0.3, accept_cap=6, accept_seed=0)
+                      num_draft=args.num_draft, accept="geometric" if args.accept == "geometric" else "exact",
+                      accept_p=0.3, accept_cap=6, accept_seed=0)
     # the shared prefix pages are held once (prefix cache); each request adds its suffix, outputs and
     # speculation scratch
     per_req_pages = (args.suffix + args.out_tokens + 2 * args.tree_nodes + 128) // 64 + 3
@@ -205,7 +210,8 @@ def main():
     g = torch.Generator().manual_seed(1234)
     prefix = torch.randint(0, mc.vocab, (args.prefix,), generator=g).tolist() if args.prefix else []
     prompts = [prefix + torch.randint(0, mc.vocab, (args.suffix,), generator=g).tolist() for _ in range(args.batch)]
-    sp = SamplingParams(temperature=0.0, max_new_tokens=args.out_tokens)
+    sp = (SamplingParams(temperature=1.0, top_k=50, top_p=0.9, seed=7, max_new_tokens=args.out_tokens)
+          if args.accept == "sample" else SamplingParams(temperature=0.0, max_new_tokens=args.out_tokens))
     for p in prompts:
         eng.add_request(p, sp)
     t0 = time.time()
@@ -284,7 +290,9 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp8_block+bf16",
             "data": "synthetic token ids, " + ("checkpoint weights" if args.model_path else "random-init weights")
-                    + ", geometric(p=0.3, cap 6) synthetic acceptance",
+                    + {"geometric": ", geometric(p=0.3, cap 6) synthetic acceptance",
+                       "greedy": ", target-greedy acceptance",
+                       "sample": ", seeded target sampling (T 1, top-k 50, top-p 0.9) with the device accept walk"}[args.accept],
             "config": {"model": mc.name + (f"-{mc.num_layers}L" if args.layers else ""), "global_batch": args.batch,
                        "seq_len": args.prefix + args.suffix, "shared_prefix": args.prefix, "suffix": args.suffix,
                        "out_tokens": args.out_tokens, "spec": args.mode,
