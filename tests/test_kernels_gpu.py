@@ -118,6 +118,44 @@ def test_gemm_split_k_tail(kind, m, n, k, bn, split):
     assert torch.equal(parts[0], parts[1]) and torch.equal(parts[1], parts[2])
 
 
+def test_split_gemm_and_topk_replay_in_cuda_graph():
+    """The split-K tail's static workspace and counters, and the top-k kernels, work inside a captured CUDA graph:
+    two replays on changed inputs equal eager launches bit for bit (the counters are back at zero after every
+    launch)."""
+    g = torch.Generator(device=DEV).manual_seed(11)
+    x = torch.randn(512, 8192, device=DEV, generator=g)
+    w = torch.randn(1280, 8192, device=DEV, generator=g) * 0.05
+    xq, xs = quant_act_block(x)
+    wq, ws = quant_weight_block(w)
+    logits = (torch.randn(512, 128256, device=DEV, generator=g) * 2).bfloat16()
+    out = torch.empty(512, 1280, device=DEV, dtype=torch.bfloat16)
+    res = {}
+
+    def body():
+        ops.gemm_fp8_block(xq, xs, wq, ws, out=out, bn=256, hw_scale=True, split=0)
+        res["topk"] = ops.topk_logprobs(logits, 8)
+        res["argmax"] = ops.topk_logprobs(logits, 1, with_lse=False)
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        body()
+    torch.cuda.current_stream().wait_stream(st)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        body()
+    for _ in range(2):
+        xq.copy_(quant_act_block(torch.randn(512, 8192, device=DEV, generator=g))[0])
+        logits.copy_((torch.randn(512, 128256, device=DEV, generator=g) * 2).bfloat16())
+        graph.replay()
+        torch.cuda.synchronize()
+        got = [out.clone()] + [t.clone() for t in res["topk"]] + [t.clone() for t in res["argmax"]]
+        ref_out = ops.gemm_fp8_block(xq, xs, wq, ws, bn=256, hw_scale=True, split=0)
+        ref = [ref_out] + list(ops.topk_logprobs(logits, 8)) + list(ops.topk_logprobs(logits, 1, with_lse=False))
+        ops.check_status()
+        for a, b in zip(got, ref):
+            assert torch.equal(a, b)
+
+
 def test_gemm_fp8_hw_scale_flags_non_pow2_scales():
     """A weight scale that is not a power of two cannot be a UE8M0 value: the hardware-scaled GEMM records it in
     the status word; the promotion path takes any fp32 scale."""
