@@ -146,6 +146,9 @@ def main():
     ap.add_argument("--mode", default="tree", choices=["tree", "chain"])
     ap.add_argument("--num-draft", type=int, default=4)
     ap.add_argument("--comm", default="fused", choices=["nccl", "fused"])
+    ap.add_argument("--moe-dispatch", default="reduce", choices=["reduce", "a2a"],
+                    help="MoE expert parallelism on the collective path (--comm nccl): all-reduce of every rank's "
+                         "expert outputs, or all-to-all dispatch / combine of each rank's own tokens")
     ap.add_argument("--accept", default="geometric", choices=["geometric", "greedy", "sample"],
                     help="geometric: synthetic accept lengths (random weights never agree with their drafter); "
                          "greedy: target argmax along the tree; sample: seeded top-k 50 / top-p 0.9 / T = 1 target "
@@ -198,7 +201,7 @@ def main():
     per_req_pages = (args.suffix + args.out_tokens + 2 * args.tree_nodes + 128) // 64 + 3
     num_pages = args.prefix // 64 + args.batch * per_req_pages + 64
     ecfg = EngineConfig(model=mc, spec=spec, draft=DraftConfig(kind="eagle"),
-                        parallel=ParallelConfig(tp=world, comm=args.comm),
+                        parallel=ParallelConfig(tp=world, comm=args.comm, moe_dispatch=args.moe_dispatch),
                         cache=CacheConfig(page_size=64, num_pages=num_pages, enable_cascade=not args.no_cascade),
                         max_prefill_tokens=8192, seed=0)
     t0 = time.time()

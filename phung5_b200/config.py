@@ -129,6 +129,9 @@ class ParallelConfig:
     # "nccl" = torch.distributed collectives + separate kernels (the baseline);
     # "fused" = in-kernel NVLink peer / multimem collectives (the product).
     comm: str = "fused"
+    # MoE expert parallelism on the collective path: "reduce" = every rank runs its experts over every token, then
+    # all-reduce; "a2a" = all-to-all dispatch / combine of each rank's own tokens (models/mixtral.py forward_a2a)
+    moe_dispatch: str = "reduce"
 
 
 @dataclass

@@ -166,6 +166,7 @@ class LLMEngine:
                                       self.comm)
         else:
             self.target = LlamaModel(target, self.pool.k, self.pool.v, self.cos_sin, self.comm)
+            self.target.moe_a2a = cfg.parallel.moe_dispatch == "a2a"
         self.drafter = None
         if self.spec_on:
             if self.eagle:

@@ -303,6 +303,10 @@ class LlamaModel:
         self.hq = self.cfg.num_heads // w.tp_size
         self.hkv = self.cfg.num_kv_heads // w.tp_size
         self.scale = 1.0 / math.sqrt(self.cfg.head_dim)
+        # MoE layers under expert parallelism on the collective path: False = every rank runs its experts over
+        # every token and the outputs are all-reduced; True = all-to-all dispatch of each rank's own tokens
+        # (MoEBlock.forward_a2a), outputs all-gathered
+        self.moe_a2a = False
 
     def attention(self, li: int, q: torch.Tensor, fb: ForwardBatch, fp8_out: bool):
         t = q.shape[0]
@@ -340,9 +344,23 @@ class LlamaModel:
         xq, xs, xb = ops.add_rmsnorm_quant(h, o, lw.post_norm, cfg.rms_eps, quant=fp8,
                                            out_bf16=(not fp8) or lw.moe is not None)
         if lw.moe is not None:
+            if self.moe_a2a and self.comm.size > 1:
+                return self._moe_a2a(lw.moe, xb)
             return self.comm.all_reduce(lw.moe((xq, xs) if fp8 else xb, xb))
         act = lw.gu.swiglu((xq, xs) if fp8 else xb)          # fp8: SwiGLU + quant in the GEMM epilogue
         return self.comm.all_reduce(lw.down(act))
+
+    def _moe_a2a(self, moe, xb: torch.Tensor) -> torch.Tensor:
+        """MoE output for every token via all-to-all dispatch: rank r routes rows [r*per, (r+1)*per) (per =
+        ceil(T / W)), then the ranks' results are all-gathered."""
+        W, r = self.comm.size, self.comm.rank
+        t, hd = xb.shape
+        per = (t + W - 1) // W
+        lo, hi = min(t, r * per), min(t, (r + 1) * per)
+        own = moe.forward_a2a(xb[lo:hi].contiguous(), self.comm)
+        buf = torch.zeros(per, hd, dtype=own.dtype, device=xb.device)
+        buf[:hi - lo] = own
+        return self.comm._gather(buf).reshape(W * per, hd)[:t]
 
     def forward_fused(self, fb: ForwardBatch, want_hidden: bool = False):
         """Tensor-parallel forward on a fused communicator (parallel/fused.py): the residual stream lives in

@@ -15,6 +15,10 @@ contributions; the layer's all-reduce (the same collective as tensor-parallel ML
 Rows beyond the local assignment count are never written by the grouped GEMMs; the combine selects
 (not multiplies) them away, so uninitialised rows cannot leak NaN.
 
+`forward_a2a` is the all-to-all alternative (ParallelConfig.moe_dispatch = "a2a", NCCL / gloo collectives):
+each rank routes only its own share of the tokens and sends every (token, expert) row to the expert's rank
+and back, moving the routed rows instead of every token's full output.
+
 The reference serves no MoE model; this follows the Mixtral-8x7B EP8 workload.
 """
 from __future__ import annotations
@@ -24,6 +28,7 @@ from dataclasses import dataclass
 from typing import Dict, Optional
 
 import torch
+import torch.distributed as dist
 
 from .. import ops
 from ..config import ModelConfig
@@ -100,6 +105,58 @@ class MoEBlock:
             out.copy_(res)
             return out
         return res
+
+
+    def _expert_rows(self, xb_rows: torch.Tensor, lexp: torch.Tensor) -> torch.Tensor:
+        """This rank's experts over rows that all belong to them: row i goes through local expert lexp[i];
+        -> [n, H] in the input row order (fp8 experts quantize the bf16 rows here)."""
+        el = self.e_local
+        n = xb_rows.shape[0]
+        order = torch.argsort(lexp, stable=True)
+        counts = torch.zeros(el, dtype=torch.int64, device=xb_rows.device).scatter_add_(0, lexp, torch.ones_like(lexp))
+        offsets = torch.zeros(el + 1, dtype=torch.int32, device=xb_rows.device)
+        offsets[1:] = torch.cumsum(counts, 0).to(torch.int32)
+        xs_rows = xb_rows[order]
+        act = ops.act_quant(xs_rows) if self.fp8 else xs_rows
+        gu = ops.gemm_grouped(act, self.w13, self.w13_s, offsets, 2 * self.ffn)
+        aq, as_, ab = ops.silu_mul_quant(gu, quant=self.fp8, out_bf16=not self.fp8)
+        y = ops.gemm_grouped((aq, as_) if self.fp8 else ab, self.w2, self.w2_s, offsets, self.hidden)
+        out = torch.empty(n, self.hidden, dtype=y.dtype, device=y.device)
+        out[order] = y[:n]
+        return out
+
+    def forward_a2a(self, xb_rows: torch.Tensor, comm) -> torch.Tensor:
+        """Expert parallelism by all-to-all: this rank's own token rows [T_own, H] are routed here, every
+        (token, expert) assignment is sent to the rank that owns the expert (one variable-size all-to-all of the
+        rows and one of their local expert ids), the receiving rank runs its experts over what it received, the
+        outputs return by the reverse all-to-all, and the owner sums them weighted per token. -> [T_own, H].
+        Counts are exchanged on the host (a synchronisation: this path is not captured in a graph). Bytes per rank
+        are the routed rows only, against every token's full output in the reduction path."""
+        W, el, k = comm.size, self.e_local, self.top_k
+        t = xb_rows.shape[0]
+        dev = xb_rows.device
+        ids, w = self.route(xb_rows)                               # [T_own, k]
+        flat = ids.reshape(-1)
+        dest = flat // el                                          # owning rank of each assignment
+        order = torch.argsort(dest, stable=True)                   # assignments grouped by destination rank
+        send = torch.zeros(W, dtype=torch.int64, device=dev).scatter_add_(0, dest, torch.ones_like(dest))
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=comm.group)
+        send_l, recv_l = send.tolist(), recv.tolist()
+        rows = xb_rows[order // k].contiguous()
+        lexp = (flat[order] - dest[order] * el).contiguous()
+        n_recv = sum(recv_l)
+        rows_in = torch.empty(n_recv, self.hidden, dtype=rows.dtype, device=dev)
+        lexp_in = torch.empty(n_recv, dtype=lexp.dtype, device=dev)
+        dist.all_to_all_single(rows_in, rows, recv_l, send_l, group=comm.group)
+        dist.all_to_all_single(lexp_in, lexp, recv_l, send_l, group=comm.group)
+        y = self._expert_rows(rows_in, lexp_in) if n_recv else rows_in.new_zeros(0, self.hidden)
+        y = y.to(rows.dtype).contiguous()
+        back = torch.empty(flat.numel(), self.hidden, dtype=y.dtype, device=dev)
+        dist.all_to_all_single(back, y, send_l, recv_l, group=comm.group)
+        per = torch.empty_like(back)
+        per[order] = back                                          # assignment order again
+        return (per.view(t, k, self.hidden).float() * w[..., None]).sum(1).to(xb_rows.dtype)
 
 
 def _expert_range(cfg: ModelConfig, rank: int, size: int):
