@@ -118,3 +118,31 @@ def test_loader_requantizes_non_pow2_checkpoint_scales():
     n, k = orig.shape
     blk = orig.abs().view(n // 128, 128, k // 128, 128).amax((1, 3)).repeat_interleave(128, 0).repeat_interleave(128, 1)
     assert ((got - orig).abs() / blk).max() <= 1 / 16 + 1e-6
+
+
+def test_gemm_table_lookup_and_switches(monkeypatch, tmp_path):
+    """The per-shape GEMM table: M is bucketed to the nearest measured size at or above it (the largest bucket
+    beyond), entries without a tile choice keep the kernel's heuristic, a caller's explicit choice wins, and
+    PHX_GEMM_SPLIT=0 turns the automatic split-K tail off unless a caller asks for a split."""
+    import json
+
+    from phung5_b200 import ops
+    from phung5_b200.ops import gemm_table as T
+    table = {"m_buckets": [128, 512, 4096],
+             "entries": {"fp8:1280:8192:512": {"bn": 256, "hws": True, "pair": False, "split": 0, "ms": 0.03},
+                         "fp8:1280:8192:4096": {"ms": 0.07, "default_ms": 0.07},
+                         "bf16:16032:8192:4096": {"bn": 256, "split": 1, "ms": 0.8}}}
+    path = tmp_path / "table.json"
+    path.write_text(json.dumps(table))
+    monkeypatch.setattr(T, "PATH", str(path))
+    monkeypatch.setattr(T, "_TABLE", {"loaded": False, "entries": {}, "buckets": []})
+    assert T.lookup("fp8", 1280, 8192, 300)["bn"] == 256          # 300 -> bucket 512
+    assert T.lookup("fp8", 1280, 8192, 2000) is None               # 2000 -> 4096: default kept
+    assert T.lookup("fp8", 1280, 8192, 9000) is None               # beyond the last bucket -> 4096
+    assert T.lookup("bf16", 16032, 8192, 9000)["split"] == 1
+    assert ops._table_choice("fp8", 1280, 8192, 300, 0, None, None, True) == (256, True, False, 0)
+    assert ops._table_choice("fp8", 1280, 8192, 300, 128, None, None, True)[0] == 128     # caller's BN wins
+    assert ops._table_choice("bf16", 16032, 8192, 4096, 0, None, None, True)[3] == 1
+    monkeypatch.setattr(ops, "GEMM_SPLIT", False)
+    assert ops._table_choice("fp8", 1280, 8192, 2000, 0, None, None, True)[3] == 1         # no entry: split off
+    assert ops._table_choice("fp8", 1280, 8192, 2000, 0, None, None, True, split=4)[3] == 4
