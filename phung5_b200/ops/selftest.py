@@ -144,10 +144,75 @@ def _checks() -> List[Tuple[str, Callable[[], Tuple[bool, float]]]]:
         frac = (diff.amax(-1) > 1).float().mean().item()
         return frac < 0.01, frac
 
+    def gemm_split():
+        x = torch.randn(512, 4096, device=dev)
+        w = torch.randn(1280, 4096, device=dev) * 0.05
+        xq, xs = quant_act_block(x)
+        wq, ws = quant_weight_block(w)
+        ref = gemm_fp8_block_ref(xq, xs, wq, ws)
+        e = max(_rel(ops.gemm_fp8_block(xq, xs, wq, ws, bn=256, hw_scale=True, split=s), ref) for s in (0, 5))
+        return e < 5e-3, e
+
+    def argmax():
+        x = (torch.randn(300, 128256, device=dev) * 2).bfloat16()
+        v, idx, _ = ops.topk_logprobs(x, 1, with_lse=False)
+        ok = torch.equal(v[:, 0], x.float().max(-1).values) and torch.equal(x.float().gather(1, idx)[:, 0], v[:, 0])
+        return ok, 0.0 if ok else 1.0
+
+    def rope_kv():
+        hq, hkv, d, ps = 8, 2, 128, 64
+        qkv = torch.randn(37, (hq + 2 * hkv) * d, device=dev).bfloat16()
+        pos = torch.randint(0, 4000, (37,), device=dev, dtype=torch.int32)
+        slots = torch.randperm(10 * ps, device=dev)[:37].to(torch.int64)
+        cs = ops.rope_table(4096, d, 5e5, dev)
+        kc = torch.zeros(10, hkv, ps, d, device=dev, dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        qo = ops.rope_kv_write(qkv, pos, slots, cs, kc, vc, hq, hkv, d)
+        kc2, vc2 = kc.cpu().zero_(), vc.cpu().zero_()
+        qo2 = ops.rope_kv_write(qkv.cpu(), pos.cpu(), slots.cpu(), cs.cpu(), kc2, vc2, hq, hkv, d)
+        e = max(_rel(qo, qo2), _rel(kc, kc2))
+        return e < 1e-2 and torch.equal(vc.cpu(), vc2), e
+
+    def gdn_verify():
+        from . import gdn as G
+        lens = [5, 0, 19, 1]
+        ts = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+        t = int(ts[-1])
+        q = torch.randn(t, 2, 128).bfloat16()
+        k = torch.randn(t, 2, 128).bfloat16()
+        v = torch.randn(t, 4, 128).bfloat16()
+        gg, beta = -torch.rand(t, 4) * 0.5, torch.rand(t, 4)
+        slot = torch.tensor([3, 0, 1, 2], dtype=torch.int32)
+        st = torch.randn(4, 4, 128, 128) * 0.02
+        st_c, st_g = st.clone(), st.to(dev)
+        o_c, _ = G.gdn_recurrent(q.float(), k.float(), v.float(), gg, beta, st_c, ts, slot, 0.088, True)
+        o_g, _ = G.gdn_recurrent(q.to(dev), k.to(dev), v.to(dev), gg.to(dev), beta.to(dev), st_g, ts.to(dev),
+                                 slot.to(dev), 0.088, True)
+        e = max(_rel(o_g, o_c), _rel(st_g, st_c))
+        return e < 2e-2, e
+
+    def sample_candidates():
+        rows, V, kc = 6, 40000, 16
+        x = (torch.randn(rows, V, device=dev) * 2).bfloat16()
+        temp = torch.full((rows,), 0.8, device=dev)
+        nch = int(ops.ext().sample_chunks(V))
+        cv = torch.empty(rows, nch, kc, device=dev)
+        ci = torch.empty(rows, nch, kc, device=dev, dtype=torch.int32)
+        ops.ext().sample_candidates(x, kc, temp, 1, 0, cv, ci, None, ops.status_tensor(x.device))
+        xf = x.float() / 0.8
+        ok = True
+        for c in range(nch):
+            a, b = c * 16384, min(V, (c + 1) * 16384)
+            want = sorted(torch.topk(xf[:, a:b], kc, dim=-1).values.flatten().tolist())
+            got = sorted(cv[:, c].flatten().tolist())
+            ok &= want == got
+        return ok, 0.0 if ok else 1.0
+
     return [("gemm_fp8_block", gemm_fp8), ("gemm_bf16", gemm_bf16), ("gemm_grouped", gemm_grouped),
-            ("add_rmsnorm_quant", norm_quant), ("silu_mul_quant", silu_quant), ("topk_logprobs", topk),
-            ("paged_attention", attention), ("raster", raster), ("gemm_fp8_swiglu", gemm_swiglu),
-            ("moe_combine", moe_combine)]
+            ("gemm_split_k", gemm_split), ("add_rmsnorm_quant", norm_quant), ("silu_mul_quant", silu_quant),
+            ("topk_logprobs", topk), ("argmax", argmax), ("paged_attention", attention), ("raster", raster),
+            ("gemm_fp8_swiglu", gemm_swiglu), ("moe_combine", moe_combine), ("rope_kv_write", rope_kv),
+            ("gdn_recurrent", gdn_verify), ("sample_candidates", sample_candidates)]
 
 
 def run() -> Dict[str, dict]:
