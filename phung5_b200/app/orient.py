@@ -237,19 +237,25 @@ def rotate_source(code: str, steps: Sequence[Tuple[str, str]]) -> Optional[str]:
     if fn is None:
         return None
     three, lo, hi = fn
+    # a name the module does not use yet: a module rotated before (the final's own turn after the per-draft
+    # stage) already holds `return <name>;` inside its block, and `const <name> = (<name>)` would not run
+    var, n = "__oriented", 1
+    while var in code:
+        n += 1
+        var = f"__oriented{n}"
     edits = []
     for r in _own_returns(toks, lo, hi):
         last, semi = _return_end(toks, r, hi)
         if last <= r:
             continue                                   # bare `return;`
         expr = code[toks[r + 1].pos:_token_end(code, toks, last)].rstrip()
-        lines = [f"const __oriented = ({expr});"]
+        lines = [f"const {var} = ({expr});"]
         for axis, angle in steps:
             x, y, z = (int(c) for c in _AXES[axis])
-            lines.append(f"__oriented.rotateOnWorldAxis(new {three}.Vector3({x}, {y}, {z}), {angle});")
-        lines.append(f"__oriented.position.sub(new {three}.Box3().setFromObject(__oriented)"
+            lines.append(f"{var}.rotateOnWorldAxis(new {three}.Vector3({x}, {y}, {z}), {angle});")
+        lines.append(f"{var}.position.sub(new {three}.Box3().setFromObject({var})"
                      f".getCenter(new {three}.Vector3()));")
-        lines.append("return __oriented;")
+        lines.append(f"return {var};")
         end = _token_end(code, toks, semi if semi >= 0 else last)
         edits.append((toks[r].pos, end, "{ " + " ".join(lines) + " }"))
     if not edits:
@@ -309,3 +315,114 @@ async def orient_candidate(code: str, scene: dict, *, renderer, embedder, ref_ve
         return code, scene, res
     res.applied, res.reason = True, "applied"
     return chk.code, chk.scene, res
+
+
+# ------------------------------------------------------------------------------------- the final draft's turns
+
+# Extra turns tried on the bracket's final only (the per-draft probe never flips a model to its back or tilts its
+# underside toward the camera): yaw by pi, tilt the underside (-y) toward the front camera, tilt the top toward it,
+# and the yaw-then-tilt pair.
+FINAL_TURNS: Dict[str, List[Tuple[str, str]]] = {
+    "y180": [("y", "Math.PI")],
+    "xm90": [("x", "-Math.PI / 2")],
+    "xp90": [("x", "Math.PI / 2")],
+    "y180xm90": [("y", "Math.PI"), ("x", "-Math.PI / 2")],
+}
+
+
+@dataclass
+class FinalTurnSettings:
+    enabled: bool = False            # off by default, as in the reference
+    turns: Tuple[str, ...] = ("y180", "xm90", "xp90")
+    min_margin: float = 0.05         # best-view similarity gain a turned copy needs over the final to be tried
+    both_seats: bool = False         # also judge with the seats swapped; the turned copy must win both
+
+
+@dataclass
+class FinalTurnResult:
+    tried: Dict[str, object] = field(default_factory=dict)    # turn -> similarity margin, or why it was skipped
+    picked: Optional[str] = None
+    replaced: bool = False
+    reason: str = ""
+
+
+def best_view_similarity(embed, n_views: int, ref_vec) -> Optional[float]:
+    """Largest cosine similarity between the reference embedding and the candidate's judge views."""
+    if embed is None or ref_vec is None or n_views == 0:
+        return None
+    return float(np.max(np.asarray(embed)[:n_views] @ np.asarray(ref_vec)))
+
+
+def _decisive(verdict, seat: str) -> bool:
+    """A win for `seat` that no tie-break decided (the judge's embedding tie-break settles draws)."""
+    return verdict.winner == seat and "tie-break" not in verdict.decided_by
+
+
+async def turn_final(final, *, renderer, embedder, ref_vec, checker, judge, prompt_url: str, seed: int,
+                     settings: Optional[FinalTurnSettings] = None):
+    """Turned copies of the final draft, each written into its own module by `rotate_source`, re-checked,
+    rendered with the judge's views and embedded like any draft. A copy whose best-view similarity to the
+    reference beats the final's by `min_margin` is a contender; the best contender duels the final (the final in
+    seat A) and replaces it only on a decisive win. -> (candidate to ship, FinalTurnResult). Every failure keeps
+    the final. Reference: pipeline_service/pipeline/orient_final.py (off by default there too)."""
+    from .jscheck import code_digest
+    from .state import Candidate
+    st = settings or FinalTurnSettings()
+    res = FinalTurnResult()
+    if not st.enabled:
+        res.reason = "disabled"
+        return final, res
+    base = best_view_similarity(final.embed, len(final.views), ref_vec)
+    if base is None or embedder is None or judge is None:
+        res.reason = "no_signal"
+        return final, res
+    best = None
+    for name in st.turns:
+        steps = FINAL_TURNS.get(name)
+        if steps is None:
+            res.tried[name] = "unknown_turn"
+            continue
+        try:
+            code = rotate_source(final.code, steps)
+            if code is None:
+                res.tried[name] = "injection_failed"
+                continue
+            chk = await checker.check_async(code)
+            if not chk.ok:
+                res.tried[name] = "checker_rejected"
+                continue
+            views = await renderer.judge_views(chk.scene, gray=True)
+            emb = await embedder.embed(views["white"])
+            sim = best_view_similarity(emb, len(views["white"]), ref_vec)
+        except Exception as e:  # noqa: BLE001 - a failed turn is skipped
+            res.tried[name] = f"failed: {type(e).__name__}"
+            continue
+        if sim is None:
+            res.tried[name] = "no_embedding"
+            continue
+        margin = sim - base
+        res.tried[name] = round(margin, 4)
+        if margin >= st.min_margin and (best is None or margin > best[0]):
+            cand = Candidate(code=chk.code, digest=code_digest(chk.code), coder=final.coder, scene=chk.scene,
+                             views=views["white"], gray_views=views.get("gray", []), embed=emb,
+                             stats={**final.stats, "turn": name})
+            best = (margin, name, cand)
+    if best is None:
+        res.reason = "no_contender"
+        return final, res
+    _, name, cand = best
+    res.picked = name
+    try:
+        v = await judge.duel(prompt_url, final, cand, seed, ref_vec)
+        won = _decisive(v, "B")
+        if won and st.both_seats:
+            v2 = await judge.duel(prompt_url, cand, final, seed, ref_vec)
+            won = _decisive(v2, "A")
+    except Exception as e:  # noqa: BLE001 - a failed duel keeps the final
+        res.reason = f"duel_failed: {type(e).__name__}"
+        return final, res
+    if not won:
+        res.reason = "not_decisive"
+        return final, res
+    res.replaced, res.reason = True, "replaced"
+    return cand, res

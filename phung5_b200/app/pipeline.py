@@ -122,7 +122,32 @@ class Orchestrator:
             rr = pc.round_robin
             if rr == 8 and task.batch_pos >= task.batch_size - pc.round_robin_tail:
                 rr = 4                    # the batch's last prompts keep the cheaper 4-player round robin
-            best = await multigen_first_iter(task, factory, duel, k, rr, pc.shadow, pc.shadow_max_duels)
+            final_turn = None
+            o = self.s.orientation
+            if o.final_enabled and checker is not None and ref_vec is not None:
+                from .orient import FinalTurnSettings, turn_final
+                fts = FinalTurnSettings(enabled=True, turns=tuple(o.final_turns), min_margin=o.final_min_margin,
+                                        both_seats=o.final_both_seats)
+
+                judge, limits = self.judge, self.limits
+
+                class _LimitedJudge:            # the stage's duels take the judge slots like the bracket's
+                    async def duel(self, *a, **kw):
+                        async with limits.judge:
+                            return await judge.duel(*a, **kw)
+
+                async def final_turn(win):
+                    out, fres = await turn_final(win, renderer=self.renderer, embedder=self.embedder,
+                                                 ref_vec=ref_vec, checker=checker, judge=_LimitedJudge(),
+                                                 prompt_url=prompt_url, seed=task.seed, settings=fts)
+                    out.stats["orient_final"] = {"picked": fres.picked, "replaced": fres.replaced,
+                                                 "reason": fres.reason, "tried": fres.tried}
+                    if fres.replaced:
+                        task.judge_log.append({"label": "orient_final", "turn": fres.picked,
+                                               "winner": "turned", "decided_by": "decisive duel"})
+                    return out
+            best = await multigen_first_iter(task, factory, duel, k, rr, pc.shadow, pc.shadow_max_duels,
+                                             final_turn=final_turn)
         else:
             best = None
             for i in range(max(1, k)):

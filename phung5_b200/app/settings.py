@@ -141,6 +141,11 @@ class OrientationConfig(BaseModel):
     enabled: bool = True
     img_size: int = 160
     min_side_margin: float = 0.0
+    # turned copies of the bracket's final (y180 / xm90 / xp90 / y180xm90), kept only after a decisive duel win
+    final_enabled: bool = False
+    final_turns: List[str] = Field(default_factory=lambda: ["y180", "xm90", "xp90"])
+    final_min_margin: float = 0.05
+    final_both_seats: bool = False
 
 
 class EventBusConfig(BaseModel):

@@ -201,7 +201,9 @@ async def round_robin(cands: List[Candidate], duel: DuelFn, bracket_winner: Cand
 
 async def multigen_first_iter(task: PipelineTask, factory: CandidateFactory, duel: DuelFn, k: int,
                               round_robin_size: int = 0, shadow: Sequence[str] = (),
-                              shadow_max_duels: int = 12) -> Optional[Candidate]:
+                              shadow_max_duels: int = 12,
+                              final_turn: Optional[Callable[[Candidate], Awaitable[Candidate]]] = None
+                              ) -> Optional[Candidate]:
     leaves = {i: asyncio.ensure_future(factory.build(i)) for i in range(k)}
     tops = {3: []}
     try:
@@ -219,6 +221,8 @@ async def multigen_first_iter(task: PipelineTask, factory: CandidateFactory, due
     if shadow:
         task.shadow = await shadow_picks(task, shadow, players, duel, bracket_winner, shadow_max_duels)
         task.shadow["shipped"] = winner.stats.get("k")
+    if final_turn is not None:          # turned copies of the final (app/orient.py turn_final)
+        winner = await final_turn(winner)
     return winner
 
 

@@ -45,6 +45,18 @@ def test_rewrite_turns_and_recentres_the_module_output():
         assert np.allclose(hi2 - lo2, want, atol=1e-9), (hi2 - lo2, want)
 
 
+def test_rewrite_of_an_already_rotated_module_composes():
+    """A module the per-draft stage turned can be turned again (the final draft's extra turns): the second
+    block takes a fresh name and the two rotations compose."""
+    once = rotate_source(BOX, [("y", "-Math.PI / 2")])
+    twice = rotate_source(once, [("x", "Math.PI / 2")])
+    assert twice is not None and "__oriented2" in twice
+    lo, hi = _bbox(BOX)
+    lo2, hi2 = _bbox(twice)
+    want = np.abs(steps_matrix([("y", "-Math.PI / 2"), ("x", "Math.PI / 2")])) @ (hi - lo)
+    assert np.allclose(hi2 - lo2, want, atol=1e-9) and np.allclose((lo2 + hi2) / 2, 0, atol=1e-9)
+
+
 @pytest.mark.parametrize("form", [
     "export default (THREE) => { const g = new THREE.Group(); g.add(new THREE.Mesh(new THREE.BoxGeometry(1, 2, 3))); return g; };",
     "function generate(THREE) { const g = new THREE.Group(); g.add(new THREE.Mesh(new THREE.BoxGeometry(1, 2, 3))); return g; }\nexport default generate;",
@@ -142,5 +154,76 @@ def test_probe_turns_a_sideways_model_to_face_front():
         # an already-front model is left alone
         code2, _, res2 = await orient_candidate(code, scene, renderer=ren, embedder=emb, ref_vec=ref_vec, checker=chk)
         assert not res2.applied and res2.reason == "already_front" and code2 == code
+    asyncio.run(go())
+    chk.close()
+
+
+class JudgeRenderer(CpuRenderer):
+    """The judge's views: three front-family angles, white background (gray = white here)."""
+
+    async def judge_views(self, scene, gray=True):
+        views = await self.render(scene, [(0.0, 10.0), (35.0, 10.0), (-35.0, 10.0)], 96)
+        return {"white": views, "gray": views}
+
+
+class StubJudge:
+    def __init__(self, winner, decided_by="S1"):
+        self.winner, self.decided_by, self.calls = winner, decided_by, []
+
+    async def duel(self, prompt_url, a, b, seed, ref_vec=None, early_stop=True):
+        from phung5_b200.app.schemas import JudgeVerdict
+        self.calls.append((a.stats.get("turn"), b.stats.get("turn")))
+        return JudgeVerdict(winner=self.winner, decided_by=self.decided_by, confidence=0.9, detail={})
+
+
+def test_final_turn_replaces_a_back_facing_final_only_on_a_decisive_duel():
+    """The bracket's final shows its back to the camera (the photo shows its marked front): the y180 copy beats it
+    on best-view similarity by far, duels the final from seat B, and is shipped only on a decisive win; a
+    tie-break win, a margin gate above every gain, or a disabled stage keep the final."""
+    try:
+        from phung5_b200 import _C  # noqa: F401 - the rasterizer's CPU restatement lives in the extension
+    except ImportError:
+        pytest.skip("extension not built")
+    from phung5_b200.app.jscheck import code_digest
+    from phung5_b200.app.orient import FinalTurnSettings, turn_final
+    from phung5_b200.app.state import Candidate
+    chk = JSChecker()
+    emb, ren = PixelEmbedder(), JudgeRenderer()
+
+    async def go():
+        photo = chk.check(BOX)                      # the photo's pose: the red mark on the +x side
+        ref_vec = (await emb.embed((await ren.judge_views(photo.scene))["white"][:1]))[0]
+        back = chk.check(rotate_source(BOX, [("y", "Math.PI")]))   # the final: turned by pi
+        assert back.ok, back.summary()
+        views = (await ren.judge_views(back.scene))["white"]
+        final = Candidate(code=back.code, digest=code_digest(back.code), coder="c0", scene=back.scene, views=views,
+                          gray_views=views, embed=await emb.embed(views), stats={"k": 3})
+        st = FinalTurnSettings(enabled=True, turns=("y180", "xm90", "xp90"), min_margin=0.05)
+        judge = StubJudge("B")
+        out, res = await turn_final(final, renderer=ren, embedder=emb, ref_vec=ref_vec, checker=chk, judge=judge,
+                                    prompt_url="p", seed=1, settings=st)
+        assert res.replaced and res.picked == "y180" and out is not final, res
+        assert res.tried["y180"] > 0.05 and judge.calls == [(None, "y180")]   # the final sat in seat A
+        assert out.stats["turn"] == "y180" and out.stats["k"] == 3
+        got = (await emb.embed(out.views[:1]))[0]
+        assert float(got @ ref_vec) > float(np.asarray(final.embed)[0] @ ref_vec)
+        # a win decided by the embedding tie-break is not decisive
+        out2, res2 = await turn_final(final, renderer=ren, embedder=emb, ref_vec=ref_vec, checker=chk,
+                                      judge=StubJudge("B", "S2 consensus -> embed tie-break"), prompt_url="p",
+                                      seed=1, settings=st)
+        assert out2 is final and res2.reason == "not_decisive"
+        # both seats: the copy must also win from seat A
+        out3, res3 = await turn_final(final, renderer=ren, embedder=emb, ref_vec=ref_vec, checker=chk,
+                                      judge=StubJudge("B"), prompt_url="p", seed=1,
+                                      settings=FinalTurnSettings(enabled=True, both_seats=True))
+        assert out3 is final and res3.reason == "not_decisive"
+        # no turned copy clears an unreachable margin; a disabled stage does nothing
+        out4, res4 = await turn_final(final, renderer=ren, embedder=emb, ref_vec=ref_vec, checker=chk,
+                                      judge=StubJudge("B"), prompt_url="p", seed=1,
+                                      settings=FinalTurnSettings(enabled=True, min_margin=5.0))
+        assert out4 is final and res4.reason == "no_contender" and set(res4.tried) == {"y180", "xm90", "xp90"}
+        out5, res5 = await turn_final(final, renderer=ren, embedder=emb, ref_vec=ref_vec, checker=chk,
+                                      judge=StubJudge("B"), prompt_url="p", seed=1, settings=FinalTurnSettings())
+        assert out5 is final and res5.reason == "disabled"
     asyncio.run(go())
     chk.close()
