@@ -17,6 +17,7 @@ from typing import Optional, Tuple
 import torch
 
 from ..weights.quant import FP8_DTYPE, dequant_act_block, gemm_fp8_block_ref, quant_act_block
+from . import check as _check
 
 try:  # the in-tree extension (python setup.py build_ext --inplace)
     from .. import _C  # type: ignore
@@ -187,9 +188,13 @@ def gemm_fp8_block(xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: tor
     if xq.is_cuda:
         bn, hw_scale, pair, split = _table_choice("fp8", n, xq.shape[1], m, bn, hw_scale, pair, use_table, split)
         hws = FP8_HW_SCALE if hw_scale is None else hw_scale
+        if _check.active():
+            _check.gemm_fp8_block(xq, xs, wq, ws, out, hws)
         ext().gemm_fp8_block(xq, xs, wq, ws, out, status_tensor(xq.device), bn, max_ctas, hws,
                              GEMM_PAIR if pair is None else pair, split)
     else:
+        if _check.active():
+            _check.gemm_fp8_block(xq, xs, wq, ws, out, False)
         out.copy_(gemm_fp8_block_ref(xq, xs, wq, ws).to(out.dtype))
     return out
 
@@ -199,6 +204,8 @@ def gemm_bf16(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = No
     """x [M,K] bf16 @ w [N,K]^T -> bf16 [M,N] (fp32 accumulate); split as for gemm_fp8_block."""
     if out is None:
         out = torch.empty(x.shape[0], w.shape[0], dtype=torch.bfloat16 if x.is_cuda else x.dtype, device=x.device)
+    if _check.active():
+        _check.gemm_bf16(x, w, out)
     if x.is_cuda:
         bn, _, _, split = _table_choice("bf16", w.shape[0], x.shape[1], x.shape[0], bn, None, None, use_table, split)
         ext().gemm_bf16(x, w, out, status_tensor(x.device), bn, max_ctas, split)
@@ -219,6 +226,8 @@ def gemm_grouped(x, w: torch.Tensor, ws: Optional[torch.Tensor], offsets: torch.
         x = (x[0][rows.long()], x[1][:, rows.long()].contiguous()) if ws is not None else x[rows.long()]
         xq, rows = (x[0] if isinstance(x, tuple) else x), None
     m = xq.shape[0] if rows is None else rows.shape[0]
+    if _check.active():
+        _check.gemm_grouped(xq.shape[0], w, n, offsets, rows)
     if out is None:
         out = torch.empty(m, n, dtype=torch.bfloat16 if xq.is_cuda else (torch.float32 if ws is not None else xq.dtype),
                           device=xq.device)
@@ -261,10 +270,12 @@ def moe_combine(y: torch.Tensor, pos: torch.Tensor, w: torch.Tensor, local: torc
                 out: torch.Tensor) -> torch.Tensor:
     """out[t] = sum_j local[t, j] * w[t, j] * y[pos[t, j]] (bf16, fp32 accumulate): the MoE combine of the
     expert rows (grouped-GEMM order) back to tokens; `out` may be a strided view (a reduction's buffer)."""
+    if _check.active():
+        _check.moe_combine(y, pos, w, local, out)
     if y.is_cuda:
         ext().moe_combine(y, pos, w, local, out)
         return out
-    g = y[pos.clamp(min=0)].float()
+    g = y[torch.where(local.bool(), pos, torch.zeros_like(pos)).clamp(min=0)].float()   # non-local pos unread
     out.copy_(torch.where(local[..., None], g * w[..., None], torch.zeros(())).sum(1).to(out.dtype))
     return out
 
@@ -276,6 +287,8 @@ def topk_logprobs(logits: torch.Tensor, k: int, temperature: float = 1.0, vocab_
     shard), which a tensor-parallel merge combines. with_lse=False (argmax use) skips the normalisation:
     the values are x / T and lse is 0."""
     r = logits.shape[0]
+    if _check.active():
+        _check.topk_logprobs(logits, k, temperature)
     if logits.is_cuda:
         lp = torch.empty(r, k, dtype=torch.float32, device=logits.device)
         idx = torch.empty(r, k, dtype=torch.int64, device=logits.device)
@@ -319,6 +332,8 @@ def spec_sample_accept(logits: torch.Tensor, tokens: torch.Tensor, parent: torch
     greedy rows and 1 <= top_k <= kc."""
     R, N = tokens.shape
     rows, vl = logits.shape
+    if _check.active():
+        _check.spec_sample_accept(logits, tokens, parent, top_k, temp, depth, kc, vocab_offset)
     nch = int(ext().sample_chunks(vl))
     cv = torch.empty(rows, nch, kc, dtype=torch.float32, device=logits.device)
     ci = torch.empty(rows, nch, kc, dtype=torch.int32, device=logits.device)
@@ -343,6 +358,8 @@ def add_rmsnorm_quant(h: torch.Tensor, delta: Optional[torch.Tensor], w: torch.T
     """In place h <- bf16(h + delta) (if delta), y = rmsnorm(h) * w. Returns (q, qs, y_bf16) with q/qs the
     block-scaled fp8 of y (or None) and y_bf16 (or None)."""
     m, hd = h.shape
+    if _check.active():
+        _check.add_rmsnorm_quant(h, delta, w, quant)
     q = qs = y = None
     if quant:
         q = torch.empty(m, hd, dtype=FP8_DTYPE, device=h.device)
@@ -369,6 +386,8 @@ def silu_mul_quant(gu: torch.Tensor, quant: bool = True, out_bf16: bool = False)
     """gu [M, 2F] = [gate | up] -> a = bf16(silu(gate) * up) as block-scaled fp8 (q, qs) and/or bf16."""
     m, f2 = gu.shape
     f = f2 // 2
+    if _check.active():
+        _check.silu_mul_quant(gu, quant)
     q = qs = y = None
     if quant:
         q = torch.empty(m, f, dtype=FP8_DTYPE, device=gu.device)
@@ -421,6 +440,8 @@ def rope_kv_write(qkv: torch.Tensor, pos: torch.Tensor, slots: Optional[torch.Te
     if q_out is None:
         q_out = torch.empty(m, hq, d, dtype=qkv.dtype, device=qkv.device)
     page_size = k_cache.shape[2] if k_cache is not None else 1
+    if _check.active():
+        _check.rope_kv_write(qkv, pos, slots, cos_sin, k_cache, hq, hkv, d)
     if qkv.is_cuda:
         ext().rope_kv_write(qkv, pos, slots, cos_sin, q_out, k_cache, v_cache, hq, hkv, d, page_size)
         return q_out
@@ -463,6 +484,8 @@ def paged_attention(q, k_cache, v_cache, meta, softmax_scale: float, o_in=None, 
     """Run one attention pass described by `meta` (an AttnMeta from engine/attn_meta.py) and a work list
     (`items`, `tiles` = (tile_item, tile_row0, num_tiles) built with attn_rows(impl) rows per tile); see
     csrc/attention.cu for the semantics. impl: "tc" (tcgen05, default) or "mma" (mma.sync)."""
+    if _check.active() and items is not None:
+        _check.attention(q, k_cache, meta, items, tiles, q.shape[1] // k_cache.shape[1], attn_rows(impl))
     if q.is_cuda:
         ti, tr, nt = tiles
         impl = impl or ATTN_IMPL["impl"]

@@ -4,8 +4,10 @@ The reference's patch kits each carry a `--check` (compile, import probe, GPU bi
 distinct exit codes (e.g. docker/opt/v5/topkbf_normcfg/topkbf/apply_topkbf.py). Here the kernels are part
 of the package, so one command checks them all on the current GPU:
 
-    python -m phung5_b200.ops.selftest [--json out.json]
+    python -m phung5_b200.ops.selftest [--json out.json] [--check-bounds]
 exit 0: all pass; 7: a kernel disagrees with its definition; 8: the extension is missing or no GPU.
+--check-bounds runs every op with the bounds-check debug mode on (ops/check.py: index data validated
+against its buffers, write-conflict and TMA-alignment rules) -- the small-shape bounds-checked run.
 Each check uses the same tolerance as the test suite and reports its error metric.
 """
 from __future__ import annotations
@@ -233,7 +235,11 @@ def run() -> Dict[str, dict]:
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--json")
+    ap.add_argument("--check-bounds", action="store_true")
     args = ap.parse_args(argv)
+    if args.check_bounds:
+        from . import check
+        check.ON[0] = True
     if not torch.cuda.is_available():
         print("selftest: no CUDA device", file=sys.stderr)
         return 8
