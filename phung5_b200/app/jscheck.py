@@ -22,7 +22,7 @@ from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
 from typing import Any, Dict, List, Optional, Set
 
-from . import jsvm
+from . import jsvm, threefix
 
 LIMITS = {"vertices": 250_000, "drawCalls": 200, "depth": 32, "instances": 50_000, "textureBytes": 4 * 1_048_576}
 LITERAL_BUDGET = 50 * 1024
@@ -189,6 +189,26 @@ def _declared_names(prog) -> Set[str]:
     return names
 
 
+def _default_function(body):
+    default = [s for s in body if s[0] == "export_default"]
+    if not default:
+        return None
+    fn = default[0][1]
+    if fn[0] == "ident":
+        target = next((s[2] for s in body if s[0] == "fundecl" and s[1] == fn[1]), None)
+        fn = target if target is not None else fn
+    return fn if fn[0] == "func" else None
+
+
+def three_param(prog) -> Optional[str]:
+    """Name of the default-exported function's first parameter (the THREE namespace), if it has one."""
+    fn = _default_function(prog[1])
+    if fn is None:
+        return None
+    params = fn[2]
+    return params[0][0][1] if params and params[0][0][0] == "id" else None
+
+
 def static_analyze(prog) -> List[Dict[str, str]]:
     fails: List[Dict[str, str]] = []
 
@@ -203,15 +223,11 @@ def static_analyze(prog) -> List[Dict[str, str]]:
         return fails
     if len(exports) > 1:
         fail("MULTIPLE_TOP_LEVEL_EXPORTS", f"found {len(exports)} top-level exports, expected exactly 1")
-    fn = default[0][1]
-    if fn[0] == "ident":
-        target = next((s[2] for s in body if s[0] == "fundecl" and s[1] == fn[1]), None)
-        fn = target if target is not None else fn
-    if fn[0] != "func":
+    fn = _default_function(body)
+    if fn is None:
         fail("DEFAULT_EXPORT_NOT_FUNCTION", "default export must be a function generate(THREE)")
         return fails
-    params = fn[2]
-    three = params[0][0][1] if params and params[0][0][0] == "id" else None
+    three = three_param(prog)
     if three is None:
         fail("MISSING_THREE_PARAM", "generate must take THREE as its first parameter")
     declared = _declared_names(prog)
@@ -394,6 +410,7 @@ class CheckerSettings:
     timeout_s: float = 5.0
     max_steps: int = 20_000_000
     repair: bool = True
+    constant_repair: bool = True     # context-aware repair of unknown THREE constants (app/threefix.py)
     workers: int = 4
     processes: bool = False          # a process pool (true parallelism) instead of threads
     pin_reserve: int = 14            # process pool: leave this many CPUs of the quota to the rest of the host
@@ -430,11 +447,26 @@ class JSChecker:
             self._pool = ThreadPoolExecutor(max_workers=self.s.workers, thread_name_prefix="jscheck")
 
     def check(self, text: str, seed: int = 0) -> CheckResult:
+        """extract -> mechanical repair -> checks; a module whose only failures are unknown THREE constants gets
+        one context-aware constant rewrite, kept only if the rewritten module passes every check."""
         self.counts["checked"] += 1
         code = extract_code(text)
         fixes: List[str] = []
         if self.s.repair:
             code, fixes = mechanical_repair(code)
+        res = self._check_code(code, seed, fixes)
+        if not res.ok and self.s.constant_repair:
+            names = threefix.plan(res.failures)
+            rw = threefix.rewrite(code, names, res.stats.get("three") or "THREE") if names else None
+            if rw is not None:
+                res2 = self._check_code(rw[0], seed, fixes + rw[1])
+                if res2.ok:
+                    res = res2
+        if res.ok:
+            self.counts["passed"] += 1
+        return res
+
+    def _check_code(self, code: str, seed: int, fixes: List[str]) -> CheckResult:
         try:
             prog = jsvm.Parser(code).program()
         except jsvm.JSError as e:
@@ -444,7 +476,7 @@ class JSChecker:
                                repaired=fixes)
         fails = static_analyze(prog)
         if fails:
-            return CheckResult(False, fails, code, repaired=fixes)
+            return CheckResult(False, fails, code, stats={"three": three_param(prog)}, repaired=fixes)
         res = jsvm.run_module(code, jsvm.Limits(steps=self.s.max_steps, seconds=self.s.timeout_s), seed=seed)
         if res.error is not None:
             rule = "EXECUTION_TIMEOUT" if res.error.startswith("TIMEOUT") else "EXECUTION_ERROR"
@@ -459,7 +491,6 @@ class JSChecker:
         except (ValueError, jsvm._Throw) as e:
             return CheckResult(False, [{"stage": "serialize", "rule": "SERIALIZE_ERROR", "detail": str(e)[:200]}],
                                code, stats=stats, repaired=fixes)
-        self.counts["passed"] += 1
         return CheckResult(True, [], code, scene=scene, stats=stats, repaired=fixes)
 
     async def check_async(self, text: str, seed: int = 0) -> CheckResult:

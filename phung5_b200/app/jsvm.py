@@ -2605,7 +2605,11 @@ _GEOM_DEFAULTS = {
 
 
 class Geometry(Host):
-    __slots__ = ("gtype", "params", "xform", "buffer", "id_")
+    """A three.js geometry. Primitives stay parametric (tessellated when the scene is serialised) until a module
+    touches their vertex data (`attributes`, `getAttribute`, `setAttribute`, `index`, `setIndex`); then they are
+    baked once into explicit position / normal / index (and, for planes, uv) buffers, as three.js primitives
+    always are, and the module edits those."""
+    __slots__ = ("gtype", "params", "xform", "buffer", "id_", "baked")
     cls_name = "BufferGeometry"
     bases = ("BufferGeometry",)
 
@@ -2616,6 +2620,7 @@ class Geometry(Host):
         self.xform = _ident4()
         self.buffer: Dict[str, Any] = {}
         self.id_ = _uuid.uuid4().hex
+        self.baked = False
 
     def get_special(self, it, key):
         if key == "type":
@@ -2623,7 +2628,11 @@ class Geometry(Host):
         if key == "parameters":
             return JSObject({k: v for k, v in self.params.items()})
         if key == "attributes":
-            return JSObject(dict(self.buffer))
+            _bake(self)
+            return JSObject({k: v for k, v in self.buffer.items() if k != "__index"})
+        if key == "index":
+            _bake(self)
+            return self.buffer.get("__index", None)
         if key == "uuid":
             return self.id_
         return super().get_special(it, key)
@@ -2632,7 +2641,21 @@ class Geometry(Host):
         return name in (self.gtype, "BufferGeometry")
 
     def apply(self, m):
-        self.xform = _mat_mul(m, self.xform)
+        """Transforms move explicit vertex buffers at once (as three.js's applyMatrix4 does, normals by the
+        inverse transpose); parametric primitives keep the transform until they are tessellated."""
+        pos = self.buffer.get("position")
+        if not (isinstance(pos, BufferAttribute) and pos.item == 3):
+            self.xform = _mat_mul(m, self.xform)
+            return self
+        import torch
+        mt = torch.tensor(m, dtype=torch.float64)
+        v = torch.tensor(pos.array, dtype=torch.float64).view(-1, 3)
+        pos.array = ((v @ mt[:3, :3].t()) + mt[:3, 3]).reshape(-1).tolist()
+        nrm = self.buffer.get("normal")
+        if isinstance(nrm, BufferAttribute) and nrm.item == 3 and nrm is not pos:
+            nm = torch.linalg.inv(mt[:3, :3]).t() if abs(float(torch.det(mt[:3, :3]))) > 1e-30 else mt[:3, :3]
+            n = torch.tensor(nrm.array, dtype=torch.float64).view(-1, 3) @ nm.t()
+            nrm.array = (n / n.norm(dim=1, keepdim=True).clamp(min=1e-30)).reshape(-1).tolist()
         return self
 
     js_methods = {
@@ -2648,9 +2671,10 @@ class Geometry(Host):
         "computeBoundingSphere": lambda s, i, x: UNDEF,
         "clone": lambda s, i, x: _geom_clone(s),
         "dispose": lambda s, i, x: UNDEF,
-        "setAttribute": lambda s, i, x: (s.buffer.__setitem__(_to_str(_arg(x, 0)), _arg(x, 1)), s)[-1],
-        "getAttribute": lambda s, i, x: s.buffer.get(_to_str(_arg(x, 0)), UNDEF),
-        "setIndex": lambda s, i, x: (s.buffer.__setitem__("__index", _arg(x, 0)), s)[-1],
+        "setAttribute": lambda s, i, x: (_bake(s), s.buffer.__setitem__(_to_str(_arg(x, 0)), _arg(x, 1)), s)[-1],
+        "getAttribute": lambda s, i, x: (_bake(s), s.buffer.get(_to_str(_arg(x, 0)), UNDEF))[-1],
+        "deleteAttribute": lambda s, i, x: (_bake(s), s.buffer.pop(_to_str(_arg(x, 0)), None), s)[-1],
+        "setIndex": lambda s, i, x: (_bake(s), s.buffer.__setitem__("__index", _arg(x, 0)), s)[-1],
         "setFromPoints": lambda s, i, x: (s.buffer.__setitem__("position", BufferAttribute(
             [c for p in it_items(_arg(x, 0)) for c in (p.v() + [0.0])[:3]], 3)), s)[-1],
     }
@@ -2659,8 +2683,66 @@ class Geometry(Host):
 def _geom_clone(g: Geometry) -> Geometry:
     n = Geometry(g.gtype, dict(g.params))
     n.xform = [row[:] for row in g.xform]
-    n.buffer = dict(g.buffer)
+    n.buffer = {k: (BufferAttribute(v.array, v.item) if isinstance(v, BufferAttribute) else v)
+                for k, v in g.buffer.items()}
+    n.baked = g.baked
     return n
+
+
+PLANE_MAX_SEGMENTS = 512
+
+
+def _plane_grid(width: float, height: float, gx: int, gy: int):
+    """Vertices, faces and uvs of a width x height plane of gx x gy cells in the xy plane, facing +z: rows of
+    gx + 1 vertices from the top edge (y = height / 2) down, two triangles per cell, counter-clockwise."""
+    import torch
+    xs = torch.arange(gx + 1, dtype=torch.float32) * (width / gx) - width / 2
+    ys = height / 2 - torch.arange(gy + 1, dtype=torch.float32) * (height / gy)
+    v = torch.stack([xs[None, :].expand(gy + 1, -1), ys[:, None].expand(-1, gx + 1),
+                     torch.zeros(gy + 1, gx + 1)], -1).reshape(-1, 3)
+    uv = torch.stack([(torch.arange(gx + 1, dtype=torch.float32) / gx)[None, :].expand(gy + 1, -1),
+                      (1 - torch.arange(gy + 1, dtype=torch.float32) / gy)[:, None].expand(-1, gx + 1)], -1)
+    top = (torch.arange(gy)[:, None] * (gx + 1) + torch.arange(gx)[None, :]).reshape(-1)   # cell's top-left
+    bot = top + gx + 1
+    f = torch.cat([torch.stack([top, bot, top + 1], 1), torch.stack([bot, bot + 1, top + 1], 1)])
+    return v, f, uv.reshape(-1, 2)
+
+
+def _vertex_normals(v, f):
+    import torch
+    n = torch.zeros_like(v)
+    if f.numel():
+        fn = torch.cross(v[f[:, 1]] - v[f[:, 0]], v[f[:, 2]] - v[f[:, 0]], dim=1)    # area-weighted
+        for k in range(3):
+            n.index_add_(0, f[:, k], fn)
+    return n / n.norm(dim=1, keepdim=True).clamp(min=1e-12)
+
+
+def _bake(g: Geometry) -> None:
+    """Turn a parametric primitive into explicit buffers (transform applied), once."""
+    if g.baked or g.gtype == "BufferGeometry":
+        return
+    import torch
+    uv = None
+    if g.gtype == "PlaneGeometry":
+        def seg(k):
+            q = g.params.get(k, 1)
+            return max(1, min(PLANE_MAX_SEGMENTS, int(_to_num(q)) if q not in (UNDEF, None) else 1))
+        def num(k):
+            q = g.params.get(k, 1)
+            return float(_to_num(q)) if q not in (UNDEF, None) else 1.0
+        v, f, uv = _plane_grid(num("width"), num("height"), seg("widthSegments"), seg("heightSegments"))
+        m = torch.tensor(g.xform, dtype=torch.float32)
+        v = (torch.cat([v, torch.ones(v.shape[0], 1)], 1) @ m.t())[:, :3]
+    else:
+        v, f = geometry_mesh(g)
+    g.buffer.setdefault("position", BufferAttribute(v.reshape(-1).tolist(), 3))
+    g.buffer.setdefault("normal", BufferAttribute(_vertex_normals(v, f).reshape(-1).tolist(), 3))
+    if uv is not None:
+        g.buffer.setdefault("uv", BufferAttribute(uv.reshape(-1).tolist(), 2))
+    g.buffer.setdefault("__index", BufferAttribute(f.reshape(-1).tolist(), 1))
+    g.xform = _ident4()
+    g.baked = True
 
 
 def _geom_center(g: Geometry):
@@ -2709,6 +2791,7 @@ class BufferAttribute(Host):
         "getX": lambda s, i, x: s._get(_num_arg(x, 0), 0),
         "getY": lambda s, i, x: s._get(_num_arg(x, 0), 1),
         "getZ": lambda s, i, x: s._get(_num_arg(x, 0), 2),
+        "setUsage": lambda s, i, x: (s.props.__setitem__("usage", _arg(x, 0)), s)[-1],
     }
 
 
@@ -3143,11 +3226,7 @@ def make_three(it: Interp) -> JSObject:
         "cubic", [_arg(x, k).v() for k in range(4)]))
     for t in ("Texture", "CanvasTexture", "DataTexture"):
         three[t] = Native(t, ctor=lambda i, x: Texture(len(it_items(_arg(x, 0))) if x else 0))
-    for name, val in {"DoubleSide": 2.0, "FrontSide": 0.0, "BackSide": 1.0, "RepeatWrapping": 1000.0,
-                      "ClampToEdgeWrapping": 1001.0, "MirroredRepeatWrapping": 1002.0, "NearestFilter": 1003.0,
-                      "LinearFilter": 1006.0, "SRGBColorSpace": "srgb", "LinearSRGBColorSpace": "srgb-linear",
-                      "AdditiveBlending": 2.0, "NormalBlending": 1.0, "FlatShading": 1.0, "SmoothShading": 2.0,
-                      "RGBAFormat": 1023.0, "UnsignedByteType": 1009.0, "FloatType": 1015.0}.items():
+    for name, val in THREE_CONSTANTS.items():
         three[name] = val
     rnd = it.random
     three["MathUtils"] = JSObject({
@@ -3164,6 +3243,24 @@ def make_three(it: Interp) -> JSObject:
         "seededRandom": _nat("seededRandom", lambda i, t, x: rnd()),
         "DEG2RAD": math.pi / 180, "RAD2DEG": 180 / math.pi})
     return JSObject(three)
+
+
+# three.js's public enum values (its constants module): sides, wrapping, filters, texel types and formats,
+# colour spaces, blending modes, buffer usages, shading
+THREE_CONSTANTS = {
+    "FrontSide": 0.0, "BackSide": 1.0, "DoubleSide": 2.0,
+    "RepeatWrapping": 1000.0, "ClampToEdgeWrapping": 1001.0, "MirroredRepeatWrapping": 1002.0,
+    "NearestFilter": 1003.0, "NearestMipmapNearestFilter": 1004.0, "NearestMipmapLinearFilter": 1005.0,
+    "LinearFilter": 1006.0, "LinearMipmapNearestFilter": 1007.0, "LinearMipmapLinearFilter": 1008.0,
+    "UnsignedByteType": 1009.0, "ByteType": 1010.0, "ShortType": 1011.0, "UnsignedShortType": 1012.0,
+    "IntType": 1013.0, "UnsignedIntType": 1014.0, "FloatType": 1015.0, "HalfFloatType": 1016.0,
+    "AlphaFormat": 1021.0, "RGBFormat": 1022.0, "RGBAFormat": 1023.0, "RedFormat": 1028.0, "RGFormat": 1030.0,
+    "NoColorSpace": "", "SRGBColorSpace": "srgb", "LinearSRGBColorSpace": "srgb-linear",
+    "NoBlending": 0.0, "NormalBlending": 1.0, "AdditiveBlending": 2.0, "SubtractiveBlending": 3.0,
+    "MultiplyBlending": 4.0,
+    "StaticDrawUsage": 35044.0, "DynamicDrawUsage": 35048.0, "StreamDrawUsage": 35040.0,
+    "FlatShading": 1.0, "SmoothShading": 2.0,
+}
 
 
 def _smoothstep(x, lo, hi):
@@ -3192,7 +3289,7 @@ def geometry_mesh(g: Geometry):
 
     from ..render import scene as S
     p = g.params
-    t = g.gtype
+    t = "BufferGeometry" if g.baked else g.gtype
 
     def n(key, d=0.0):
         v = p.get(key, d)
