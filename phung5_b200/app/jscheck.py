@@ -20,9 +20,9 @@ import math
 import re
 from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
-from typing import Any, Dict, List, Optional, Set
+from typing import Any, Dict, Iterable, List, Optional, Set
 
-from . import jsvm, threefix
+from . import jsrepair, jsvm, threefix
 
 LIMITS = {"vertices": 250_000, "drawCalls": 200, "depth": 32, "instances": 50_000, "textureBytes": 4 * 1_048_576}
 LITERAL_BUDGET = 50 * 1024
@@ -207,6 +207,77 @@ def three_param(prog) -> Optional[str]:
         return None
     params = fn[2]
     return params[0][0][1] if params and params[0][0][0] == "id" else None
+
+
+def _bound_names(p) -> List[str]:
+    """Names a binding pattern declares: ("id", x), ("objpat", props, rest), ("arrpat", elems, rest)."""
+    if not isinstance(p, tuple) or not p:
+        return []
+    if p[0] == "id":
+        return [p[1]]
+    if p[0] == "objpat":
+        return [n for _, target, _ in p[1] for n in _bound_names(target)] + ([p[2]] if p[2] else [])
+    if p[0] == "arrpat":
+        return [n for target, _ in p[1] for n in _bound_names(target)] + _bound_names(p[2])
+    return []
+
+
+def _scope_clash(stmts, params: Iterable[str] = (), function_top: bool = False) -> Optional[str]:
+    """First name declared twice in one statement list where ES modules (strict code) reject it: a let/const
+    (or, outside a function's top level, function) name declared again by any declaration of the list, or
+    equal to a parameter of the function whose body the list is."""
+    lexical: Set[str] = set()
+    other: Set[str] = set(params)
+    for st in stmts:
+        if not isinstance(st, tuple) or not st:
+            continue
+        if st[0] == "export_decl":
+            st = st[1]
+        if st[0] == "export_named":
+            st = ("fundecl", st[2])
+        if st[0] == "decl":
+            names, var_like = [n for tgt, _ in st[2] for n in _bound_names(tgt)], st[1] == "var"
+        elif st[0] == "fundecl":
+            names, var_like = [st[1]], function_top
+        else:
+            continue
+        for n in names:
+            if n in lexical or (not var_like and n in other):
+                return n
+            (other if var_like else lexical).add(n)
+    return None
+
+
+def redeclared_name(prog) -> Optional[str]:
+    """A name declared twice in one scope (a parse-time error for a JS engine), or None."""
+    def visit(n) -> Optional[str]:
+        if isinstance(n, list):
+            for ch in n:
+                r = visit(ch)
+                if r:
+                    return r
+            return None
+        if not isinstance(n, tuple) or not n:
+            return None
+        tag = n[0]
+        if tag == "func":
+            ps, rest, body = n[2], n[3], n[4]
+            pnames = [x for tgt, _ in ps for x in _bound_names(tgt)] + _bound_names(rest)
+            r = _scope_clash(body[1], pnames, True)
+            if r:
+                return r
+            return visit([d for _, d in ps]) or visit(body[1])
+        if tag == "block":
+            r = _scope_clash(n[1])
+            if r:
+                return r
+        if tag == "switch":
+            r = _scope_clash([st for _, body in n[2] for st in body])
+            if r:
+                return r
+        return visit(list(n[1:]))
+    r = _scope_clash(prog[1])
+    return r or visit(prog[1])
 
 
 def static_analyze(prog) -> List[Dict[str, str]]:
@@ -411,6 +482,8 @@ class CheckerSettings:
     max_steps: int = 20_000_000
     repair: bool = True
     constant_repair: bool = True     # context-aware repair of unknown THREE constants (app/threefix.py)
+    failure_repair: bool = True      # failure-driven mechanical repairs (app/jsrepair.py)
+    repair_rounds: int = 3
     workers: int = 4
     processes: bool = False          # a process pool (true parallelism) instead of threads
     pin_reserve: int = 14            # process pool: leave this many CPUs of the quota to the rest of the host
@@ -462,8 +535,30 @@ class JSChecker:
                 res2 = self._check_code(rw[0], seed, fixes + rw[1])
                 if res2.ok:
                     res = res2
+        if not res.ok and self.s.failure_repair:
+            res = self._repair_rounds(res, seed)
         if res.ok:
             self.counts["passed"] += 1
+        return res
+
+    def _repair_rounds(self, res: CheckResult, seed: int) -> CheckResult:
+        """Apply the failure-driven repairs the failures call for and check again, for a few rounds (a fix can
+        uncover the next failure); the first passing module is kept, else the original result stands."""
+        cur = res
+        for _ in range(self.s.repair_rounds):
+            steps = jsrepair.plan(cur.failures)
+            if not steps:
+                break
+            try:
+                declared = _declared_names(jsvm.Parser(cur.code).program())
+            except (jsvm.JSError, RecursionError):
+                declared = set()
+            rw = jsrepair.apply(cur.code, steps, declared)
+            if rw is None:
+                break
+            cur = self._check_code(rw[0], seed, cur.repaired + rw[1])
+            if cur.ok:
+                return cur
         return res
 
     def _check_code(self, code: str, seed: int, fixes: List[str]) -> CheckResult:
@@ -473,6 +568,11 @@ class JSChecker:
             return CheckResult(False, [{"stage": "parse", "rule": "PARSE_ERROR", "detail": e.msg}], code, repaired=fixes)
         except RecursionError:
             return CheckResult(False, [{"stage": "parse", "rule": "PARSE_ERROR", "detail": "nesting too deep"}], code,
+                               repaired=fixes)
+        dup = redeclared_name(prog)
+        if dup is not None:
+            return CheckResult(False, [{"stage": "parse", "rule": "PARSE_ERROR",
+                                        "detail": f"Identifier '{dup}' has already been declared"}], code,
                                repaired=fixes)
         fails = static_analyze(prog)
         if fails:

@@ -1,0 +1,183 @@
+"""Failure-driven mechanical repairs of coder drafts, on the interpreter's token stream.
+
+A draft that fails the checker for a mechanical reason costs a full LLM repair turn. The reference repairs a
+few such classes deterministically (pipeline_service/modules/js_checker/mech_repair.py, off by default): the
+failure text picks a class, the class rewrites the source, and the same checker runs again; the rewrite is
+kept only if it passes. This module does the same for the failures this checker reports, with rewrites
+planned on `jsvm.tokenize` tokens (so strings, comments and template text are never touched):
+
+- `redeclared`  PARSE_ERROR "Identifier 'x' has already been declared": a later `let/const x = ...` in the same
+                block becomes the assignment `x = ...` and the first declaration of x becomes `let`.
+- `constlet`    EXECUTION_ERROR "assignment to constant variable x": x's `const` declarations become `let`.
+- `paren`       PARSE_ERROR "unexpected token ')'": the first `)` that closes nothing is deleted.
+- `ident`       IDENTIFIER_NOT_ALLOWED `x`: if exactly one declared name equals x up to case and underscores
+                (`roundedPts` / `rounded_pts`), every reference to x is renamed to it.
+- `retry`       EXECUTION_TIMEOUT on the wall-clock deadline only (not the step budget): checked once more, since
+                host load can push a module over the deadline.
+
+Every class refuses (returns None) when its precondition is not met exactly; `plan` picks the classes the
+failures call for, and the checker applies them for at most a few rounds.
+"""
+from __future__ import annotations
+
+import re
+from typing import Dict, Iterable, List, Optional, Set, Tuple
+
+from . import jsvm
+
+CLASSES = ("redeclared", "constlet", "paren", "ident", "retry")
+
+_DUP = re.compile(r"Identifier '([A-Za-z_$][\w$]*)' has already been declared")
+_CONST = re.compile(r"assignment to constant variable ([A-Za-z_$][\w$]*)")
+_IDENT = re.compile(r"`([A-Za-z_$][\w$]*)` is not declared")
+
+
+def plan(fails: Iterable[Dict[str, str]]) -> List[Tuple[str, str]]:
+    """[(class, subject)] for the failures a mechanical class can address; [] when any failure is something
+    no class handles (a partial repair cannot make the module pass)."""
+    out: List[Tuple[str, str]] = []
+    for f in fails:
+        rule, detail = f.get("rule", ""), f.get("detail", "")
+        if rule == "PARSE_ERROR" and _DUP.search(detail):
+            out.append(("redeclared", _DUP.search(detail).group(1)))
+        elif rule == "PARSE_ERROR" and "unexpected token ')'" in detail:
+            out.append(("paren", ")"))
+        elif rule == "EXECUTION_ERROR" and _CONST.search(detail):
+            out.append(("constlet", _CONST.search(detail).group(1)))
+        elif rule == "IDENTIFIER_NOT_ALLOWED" and _IDENT.search(detail):
+            out.append(("ident", _IDENT.search(detail).group(1)))
+        elif rule == "EXECUTION_TIMEOUT" and "execution exceeded" in detail:
+            out.append(("retry", ""))
+        else:
+            return []
+    return out
+
+
+def _edit(code: str, edits: List[Tuple[int, int, str]]) -> str:
+    for a, b, s in sorted(edits, reverse=True):
+        code = code[:a] + s + code[b:]
+    return code
+
+
+def _tokens(code: str) -> Optional[List[jsvm.Tok]]:
+    try:
+        return jsvm.tokenize(code)
+    except jsvm.JSError:
+        return None
+
+
+def _tok_end(t: jsvm.Tok) -> int:
+    return t.pos + len(str(t.val))
+
+
+def _blocks(toks: List[jsvm.Tok]) -> List[int]:
+    """Block id of every token: the index of the `{` that opened the innermost enclosing brace (-1 at top)."""
+    out, stack = [], [-1]
+    for i, t in enumerate(toks):
+        if t.kind == "p" and t.val == "}" and len(stack) > 1:
+            stack.pop()
+        out.append(stack[-1])
+        if t.kind == "p" and t.val == "{":
+            stack.append(i)
+    return out
+
+
+def _is_binding_ref(toks: List[jsvm.Tok], i: int) -> bool:
+    """Token i (an identifier) names a variable, not a property (`a.x`) or an object-literal key (`{x: 1}`)."""
+    if i > 0 and toks[i - 1].kind == "p" and toks[i - 1].val in (".", "?."):
+        return False
+    if i + 1 < len(toks) and toks[i + 1].kind == "p" and toks[i + 1].val == ":" and i > 0 and \
+            toks[i - 1].kind == "p" and toks[i - 1].val in ("{", ","):
+        return False
+    return True
+
+
+def fix_redeclared(code: str, name: str) -> Optional[str]:
+    toks = _tokens(code)
+    if toks is None:
+        return None
+    blk = _blocks(toks)
+    seen: Dict[int, int] = {}
+    edits: List[Tuple[int, int, str]] = []
+    for i in range(len(toks) - 2):
+        t, n, eq = toks[i], toks[i + 1], toks[i + 2]
+        if not (t.kind == "kw" and t.val in ("let", "const") and n.kind == "id" and n.val == name):
+            continue
+        if not (eq.kind == "p" and eq.val == "=") or (i > 0 and toks[i - 1].kind == "p" and toks[i - 1].val == "("):
+            return None                               # destructuring, for-loop heads: not handled
+        b = blk[i]
+        if b not in seen:
+            seen[b] = i
+            if t.val == "const":
+                edits.append((t.pos, _tok_end(t), "let"))
+        else:
+            edits.append((t.pos, n.pos, ""))          # `const x = v` -> `x = v`
+    if not any(e[2] == "" for e in edits):
+        return None
+    return _edit(code, edits)
+
+
+def fix_constlet(code: str, name: str) -> Optional[str]:
+    toks = _tokens(code)
+    if toks is None:
+        return None
+    edits = [(t.pos, _tok_end(t), "let") for i, t in enumerate(toks[:-1])
+             if t.kind == "kw" and t.val == "const" and toks[i + 1].kind == "id" and toks[i + 1].val == name]
+    return _edit(code, edits) if edits else None
+
+
+def fix_paren(code: str) -> Optional[str]:
+    toks = _tokens(code)
+    if toks is None:
+        return None
+    depth = 0
+    for t in toks:
+        if t.kind != "p":
+            continue
+        if t.val == "(":
+            depth += 1
+        elif t.val == ")":
+            if depth == 0:
+                return code[:t.pos] + code[t.pos + 1:]
+            depth -= 1
+    return None
+
+
+def _norm(name: str) -> str:
+    return name.replace("_", "").lower()
+
+
+def fix_ident(code: str, name: str, declared: Set[str]) -> Optional[str]:
+    same = [d for d in declared if d != name and _norm(d) == _norm(name)]
+    if len(same) != 1:
+        return None
+    toks = _tokens(code)
+    if toks is None:
+        return None
+    edits = [(t.pos, _tok_end(t), same[0]) for i, t in enumerate(toks)
+             if t.kind == "id" and t.val == name and _is_binding_ref(toks, i)]
+    return _edit(code, edits) if edits else None
+
+
+def apply(code: str, steps: List[Tuple[str, str]], declared: Set[str]) -> Optional[Tuple[str, List[str]]]:
+    """Apply every planned class -> (code, fixes), or None if one of them refuses."""
+    fixes: List[str] = []
+    for cls, subject in steps:
+        if cls == "retry":
+            fixes.append("retry after a wall-clock timeout")
+            continue
+        if cls == "redeclared":
+            new = fix_redeclared(code, subject)
+        elif cls == "constlet":
+            new = fix_constlet(code, subject)
+        elif cls == "paren":
+            new = fix_paren(code)
+        elif cls == "ident":
+            new = fix_ident(code, subject, declared)
+        else:
+            new = None
+        if new is None:
+            return None
+        code = new
+        fixes.append(f"{cls}: {subject}" if subject else cls)
+    return code, fixes
