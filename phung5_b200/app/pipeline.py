@@ -30,7 +30,7 @@ from .agents import CriticAgent, JudgeAgent, JudgeSettings, PlannerAgent, SceneC
 from .batch_stats import BatchStats
 from .embed import Embedder, EmbedderSettings
 from .jscheck import CheckerSettings, JSChecker, code_digest
-from .kpolicy import BudgetK, TimeGuard
+from .kpolicy import BudgetK, RenderBrake, RoundGuard, detect_cores, start_k
 from .renderer import RendererModule, RendererSettings
 from .session import CALL_LOG, HTTPBackend, ImageResendBackend, InstrumentedBackend, purpose_var
 from .settings import Settings
@@ -69,7 +69,11 @@ class Orchestrator:
         self.limits = StageLimits(asyncio.Semaphore(a.coder.workers), asyncio.Semaphore(a.judge.workers),
                                   asyncio.Semaphore(a.renderer.workers))
         self.k = a.coder.ensemble_size
-        self.budget_k: Optional[BudgetK] = None
+        kp = settings.pipeline.k_policy
+        self.budget_k: Optional[BudgetK] = BudgetK(lo=kp.budget_lo, hi=kp.budget_hi, min_ref=kp.budget_min_ref) \
+            if kp.budget else None
+        self.brake: Optional[RenderBrake] = RenderBrake(a.renderer.workers, kp.render_backlog) \
+            if kp.render_brake else None
 
     async def run_one(self, task: PipelineTask, deadline: Optional[float] = None) -> PipelineTask:
         task.started_at = task.started_at or time.time()
@@ -111,12 +115,11 @@ class Orchestrator:
             orient = OrientSettings(enabled=True, img_size=o.img_size, min_side_margin=o.min_side_margin)
         checker = getattr(self.coders[0], "checker", None) if self.coders else None
         factory = CandidateFactory(task, self.coders, self.renderer, self.embedder, self.limits, prompt_url,
-                                   plan_text, cand_deadline, ref_vec=ref_vec, checker=checker, orient=orient)
+                                   plan_text, cand_deadline, ref_vec=ref_vec, checker=checker, orient=orient,
+                                   brake=self.brake)
         duel = make_duel(task, self.judge, self.limits, prompt_url, ref_vec, on_duel=self.stats.duel,
                          es_max_round=self.s.pipeline.s1_early_stop_max_round) if self.judge is not None else None
         k = self.k
-        if self.budget_k is not None:
-            k = self.budget_k.initial(k)
         if k > 1 and duel is not None:
             pc = self.s.pipeline
             rr = pc.round_robin
@@ -147,7 +150,7 @@ class Orchestrator:
                                                "winner": "turned", "decided_by": "decisive duel"})
                     return out
             best = await multigen_first_iter(task, factory, duel, k, rr, pc.shadow, pc.shadow_max_duels,
-                                             final_turn=final_turn)
+                                             final_turn=final_turn, budget=self.budget_k)
         else:
             best = None
             for i in range(max(1, k)):
@@ -213,7 +216,11 @@ class GenerationPipeline:
         self.stats = BatchStats(CALL_LOG)
         self.checker = self.renderer = self.embedder = None
         self.orch: Optional[Orchestrator] = None
-        self.time_guard = TimeGuard(settings.pipeline.batch_time_budget, settings.pipeline.batch_margin_s)
+        kp = settings.pipeline.k_policy
+        self.guard = RoundGuard(mode=kp.guard, round_batches=kp.round_batches, round_s=kp.round_s,
+                                margin_s=kp.margin_s, overhead_s=kp.overhead_s, steps=tuple(kp.steps),
+                                k_floor=kp.k_floor, idle_reset_s=kp.idle_reset_s)
+        self.k0: Optional[int] = None
         self.current: Dict[str, PipelineTask] = {}
         self.probe_tps: Optional[float] = None
 
@@ -262,6 +269,11 @@ class GenerationPipeline:
         planner = PlannerAgent(planner_be, a.planner.model) if planner_be is not None else None
         self.orch = Orchestrator(coders, judge, critic, planner, self.renderer, self.embedder, self.s, self.stats,
                                  self.http)
+        kp = self.s.pipeline.k_policy
+        cores = detect_cores()[0] if kp.start == "cpu" else None
+        self.k0, src = start_k(kp.start, a.coder.ensemble_size, cores, kp.cpu_per_candidate, kp.k_min)
+        self.orch.k = self.k0
+        self.state.diag["k"], self.state.diag["k_src"] = self.k0, src
 
     # ----------------------------------------------------------------------------------------------- probe
 
@@ -294,6 +306,8 @@ class GenerationPipeline:
         if self.orch is None:
             self.startup()
         self.stats.reset()
+        self.orch.k = self.guard.before_batch(self.k0)
+        self.state.diag["k"] = self.orch.k
         budget = self.s.pipeline.batch_time_budget
         eff = max(1.0, budget - self.s.pipeline.batch_margin_s)
         t_start = time.monotonic()
@@ -337,6 +351,7 @@ class GenerationPipeline:
         finally:
             self.stats.end()
             wall = time.monotonic() - t_start
+            self.guard.after_batch(self.orch.k, wall)
             if self.orch is not None and self.orch.budget_k is not None:
                 self.orch.budget_k.batch_end()
             self.state.stats_header = self.stats.header_parts()

@@ -43,6 +43,41 @@ class PreflightConfig(BaseModel):
     min_download_mbps: Optional[float] = None
 
 
+class KPolicyConfig(BaseModel):
+    """Candidate-count policies (app/kpolicy.py); every one is off unless configured."""
+    start: str = "fixed"               # start-up K: fixed | cpu (cores / cpu_per_candidate cap) | off
+    cpu_per_candidate: float = 0.25
+    k_min: int = 2
+    guard: str = "off"                 # round-budget guard: live | shadow | off
+    round_batches: int = 4
+    round_s: float = 7200.0
+    margin_s: float = 250.0
+    overhead_s: float = 90.0
+    steps: List[float] = Field(default_factory=lambda: [0.85, 0.7, 0.55, 0.4, 0.25])
+    k_floor: int = 2
+    idle_reset_s: float = 900.0
+    budget: bool = False               # per-prompt token budget K (BudgetK)
+    budget_lo: float = 0.5
+    budget_hi: float = 1.5
+    budget_min_ref: int = 8
+    render_brake: bool = False         # hold coder launches while renders are backed up
+    render_backlog: float = 4.0
+
+    @field_validator("start")
+    @classmethod
+    def _start(cls, v):
+        if v not in ("fixed", "cpu", "off"):
+            raise ValueError(f"k_policy.start must be fixed, cpu or off, got {v!r}")
+        return v
+
+    @field_validator("guard")
+    @classmethod
+    def _guard(cls, v):
+        if v not in ("live", "shadow", "off"):
+            raise ValueError(f"k_policy.guard must be live, shadow or off, got {v!r}")
+        return v
+
+
 class PipelineConfig(BaseModel):
     batch_time_budget: float = 1800.0
     batch_margin_s: float = 120.0
@@ -59,6 +94,16 @@ class PipelineConfig(BaseModel):
     salvage: bool = True
     seed_offset: int = 0
     coder_probe: CoderProbeConfig = Field(default_factory=CoderProbeConfig)
+    k_policy: KPolicyConfig = Field(default_factory=KPolicyConfig)
+
+    @field_validator("round_robin", mode="before")
+    @classmethod
+    def _rr(cls, v):
+        if isinstance(v, bool):              # a yes/no switch means the 4-player round robin
+            return 4 if v else 0
+        if v not in (0, 4, 8):
+            raise ValueError(f"pipeline.round_robin must be 0, 4 or 8 (or a bool), got {v!r}")
+        return v
 
 
 class EngineServeConfig(BaseModel):

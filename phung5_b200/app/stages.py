@@ -53,13 +53,36 @@ class CandidateFactory:
     def __init__(self, task: PipelineTask, coders: Sequence[SceneCoderAgent], renderer: RendererModule, embedder,
                  limits: StageLimits, prompt_url: str, plan: Optional[str] = None, deadline: Optional[float] = None,
                  on_event: Optional[Callable[[str, dict], None]] = None, ref_vec=None, checker=None,
-                 orient=None):
+                 orient=None, brake=None):
         self.task, self.coders, self.renderer, self.embedder = task, coders, renderer, embedder
         self.limits, self.prompt_url, self.plan, self.deadline = limits, prompt_url, plan, deadline
         # orientation stage (app/orient.py): needs the prompt's embedding and a checker for the rewritten module
         self.ref_vec, self.checker, self.orient = ref_vec, checker, orient
         self.seen: Dict[str, int] = {}
         self.on_event = on_event or (lambda kind, d: None)
+        self.brake = brake                  # kpolicy.RenderBrake or None
+        self.code_bytes: Dict[int, Optional[int]] = {}    # position -> bytes of its draft (None: no draft)
+        self._arrived = asyncio.Condition()
+
+    async def _note_draft(self, k: int, nbytes: Optional[int]) -> None:
+        async with self._arrived:
+            self.code_bytes[k] = nbytes
+            self._arrived.notify_all()
+
+    async def drafts_of(self, positions: Sequence[int]) -> List[int]:
+        """Wait until every listed position's coder call has returned; their draft sizes in bytes."""
+        async with self._arrived:
+            await self._arrived.wait_for(lambda: all(p in self.code_bytes for p in positions))
+        return [self.code_bytes[p] for p in positions if self.code_bytes[p]]
+
+    async def _render(self, coro):
+        if self.brake is None:
+            return await coro
+        await self.brake.enter_render()
+        try:
+            return await coro
+        finally:
+            await self.brake.leave_render()
 
     def _left(self) -> Optional[float]:
         return None if self.deadline is None else self.deadline - time.monotonic()
@@ -68,15 +91,20 @@ class CandidateFactory:
         coder = self.coders[k % len(self.coders)]
         t = self.task
         try:
+            if self.brake is not None:
+                await self.brake.before_coder()
             async with self.limits.coder:
                 left = self._left()
                 if left is not None and left <= 0:
+                    await self._note_draft(k, None)
                     return None
                 res = await asyncio.wait_for(coder.generate(self.prompt_url, t.seed + k, plan=self.plan), left)
         except (asyncio.TimeoutError, Exception) as e:  # noqa: BLE001 - a failed leaf is a walkover
             t.js_errors.append(f"k{k} {coder.name}: {type(e).__name__}: {str(e)[:160]}")
             self.on_event("coder_error", {"k": k})
+            await self._note_draft(k, None)
             return None
+        await self._note_draft(k, len(res.check.code or "") or None)
         t.n_generated += 1
         if not res.check.ok:
             t.js_errors.append(f"k{k} {coder.name}: {res.check.summary()[:300]}")
@@ -94,14 +122,14 @@ class CandidateFactory:
         if self.orient is not None and self.orient.enabled and self.checker is not None and self.ref_vec is not None:
             from .orient import orient_candidate
             async with self.limits.render:
-                cand.code, cand.scene, ores = await orient_candidate(
+                cand.code, cand.scene, ores = await self._render(orient_candidate(
                     cand.code, cand.scene, renderer=self.renderer, embedder=self.embedder, ref_vec=self.ref_vec,
-                    checker=self.checker, settings=self.orient)
+                    checker=self.checker, settings=self.orient))
             cand.stats["orient"] = ores.reason if not ores.applied else f"{ores.best}:{len(ores.steps)}"
             self.on_event("orient", {"k": k, "applied": ores.applied, "best": ores.best})
         try:
             async with self.limits.render:
-                views = await self.renderer.judge_views(cand.scene, gray=True)
+                views = await self._render(self.renderer.judge_views(cand.scene, gray=True))
         except (asyncio.TimeoutError, Exception) as e:  # noqa: BLE001
             t.js_errors.append(f"k{k} render: {type(e).__name__}: {str(e)[:160]}")
             self.on_event("render_error", {"k": k})
@@ -202,14 +230,39 @@ async def round_robin(cands: List[Candidate], duel: DuelFn, bracket_winner: Cand
 async def multigen_first_iter(task: PipelineTask, factory: CandidateFactory, duel: DuelFn, k: int,
                               round_robin_size: int = 0, shadow: Sequence[str] = (),
                               shadow_max_duels: int = 12,
-                              final_turn: Optional[Callable[[Candidate], Awaitable[Candidate]]] = None
-                              ) -> Optional[Candidate]:
-    leaves = {i: asyncio.ensure_future(factory.build(i)) for i in range(k)}
+                              final_turn: Optional[Callable[[Candidate], Awaitable[Candidate]]] = None,
+                              budget=None) -> Optional[Candidate]:
+    """`budget` (kpolicy.BudgetK): once it has reference prompts, the first K_lo positions start at once, their
+    draft sizes set this prompt's K_i in [K_lo, K_hi], positions K_lo..K_i-1 start then, and positions from K_i
+    on are walkovers of a bracket laid out for K_hi positions (pairing stays by position)."""
+    size = k
+    extra = None
+    if budget is not None and budget.active(k):
+        k_lo = budget.initial(k)
+        size = max(k_lo, int(round(budget.hi * k)))
+        decided = asyncio.Event()
+        k_final = [k]
+
+        async def decide():
+            try:
+                sizes = await factory.drafts_of(list(range(k_lo)))
+                k_final[0] = budget.decide(k, [float(b) for b in sizes]) if sizes else k
+                task.budget_k = k_final[0]
+            finally:
+                decided.set()
+
+        async def gated(i):
+            await decided.wait()
+            return await factory.build(i) if i < k_final[0] else None
+        extra = asyncio.ensure_future(decide())
+        leaves = {i: asyncio.ensure_future(factory.build(i) if i < k_lo else gated(i)) for i in range(size)}
+    else:
+        leaves = {i: asyncio.ensure_future(factory.build(i)) for i in range(k)}
     tops = {3: []}
     try:
-        winner, semis = await resolve_bracket(leaves, duel, k, tops)
+        winner, semis = await resolve_bracket(leaves, duel, size, tops)
     finally:
-        for f in leaves.values():
+        for f in list(leaves.values()) + ([extra] if extra is not None else []):
             if not f.done():
                 f.cancel()
     if winner is None:

@@ -78,6 +78,7 @@ class PipelineTask:
     salvaged: bool = False
     lead_round: int = -1                            # bracket round of the current leader (salvage)
     shadow: Optional[dict] = None                   # shadow picks: what unshipped selection features would pick
+    budget_k: Optional[int] = None                  # drafts the per-prompt token budget gave this prompt
     batch_pos: int = 0
     batch_size: int = 1
 

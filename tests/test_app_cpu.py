@@ -20,7 +20,7 @@ import torch
 from phung5_b200.app import jsvm
 from phung5_b200.app.batch_stats import BatchStats, parse_metrics
 from phung5_b200.app.jscheck import JSChecker, code_digest, mechanical_repair
-from phung5_b200.app.kpolicy import BudgetK, TimeGuard, cpu_k
+from phung5_b200.app.kpolicy import BudgetK, cpu_k
 from phung5_b200.app.session import (BackendError, CallLog, ImageResendBackend, InstrumentedBackend, SessionAgent,
                                      Tool, async_retry)
 from phung5_b200.app.settings import load_settings
@@ -264,9 +264,6 @@ def test_settings_env_rewriters_and_validation():
 
 def test_k_policies():
     assert cpu_k(64, None) == 64 and cpu_k(64, 4.0) == 16 and cpu_k(64, 0.1) == 2
-    tg = TimeGuard(budget_s=1000, margin_s=100)
-    assert tg.next_k(32, 900) == 32                     # inside the dead band
-    assert tg.next_k(32, 1800) == 16 and tg.next_k(32, 300) == 64
     bk = BudgetK(min_ref=4, floor=4)
     assert bk.decide(32, [1000]) == 32                  # no reference yet: fixed K
     for c in (1000, 2000, 4000, 8000):
