@@ -53,6 +53,7 @@ class BurstController:
         self.http = http or httpx.AsyncClient(timeout=httpx.Timeout(600.0, connect=10.0))
         self.delay_s, self.drain_s = delay_s, drain_s
         self.state = "coder"
+        self.parked: List[str] = []             # the coder upstreams the last swap parked
         self.lock = asyncio.Lock()
         self.ledger: Optional[_Ledger] = None
         self.events: List[dict] = []
@@ -135,13 +136,23 @@ class BurstController:
             raise RuntimeError(f"{url} -> {r.status_code} {r.text[:120]}")
         return r
 
+    async def _coder_upstreams(self) -> List[str]:
+        """The configured coder upstreams, else every upstream the proxy has active now."""
+        if self.coders:
+            return self.coders
+        r = await self.http.get(self.proxy + "/park_state")
+        if r.status_code >= 400:
+            raise RuntimeError(f"{self.proxy}/park_state -> {r.status_code}")
+        return list(r.json().get("active", []))
+
     async def to_judge(self) -> bool:
         async with self.lock:
             if self.state != "coder":
                 return False
             woken: List[int] = []
             try:
-                await self._post(self.proxy + "/park", {"upstreams": self.coders})
+                self.parked = await self._coder_upstreams()
+                await self._post(self.proxy + "/park", {"upstreams": self.parked})
                 for i in self.idxs:
                     await self._post(self.lb.urls[i] + "/wake_up")
                     woken.append(i)
@@ -154,7 +165,7 @@ class BurstController:
                 try:
                     for i in woken:
                         await self._post(self.lb.urls[i] + "/sleep")
-                    await self._post(self.proxy + "/unpark", {"upstreams": self.coders})
+                    await self._post(self.proxy + "/unpark", {"upstreams": self.parked})
                 except Exception as e2:  # noqa: BLE001
                     self.state = "broken"
                     self._ev("broken", error=str(e2)[:160])
@@ -179,7 +190,7 @@ class BurstController:
                 await self._drain_judges()
                 for i in self.idxs:
                     await self._post(self.lb.urls[i] + "/sleep")
-                await self._post(self.proxy + "/unpark", {"upstreams": self.coders})
+                await self._post(self.proxy + "/unpark", {"upstreams": self.parked})
                 self.state = "coder"
                 self._ev("to_coder", why=why)
                 return True
@@ -196,8 +207,9 @@ class BurstCoderBackend:
         self.inner, self.ctrl = inner, ctrl
 
     async def chat(self, body: dict) -> dict:
+        from ..serve.router import affinity_key
         await self.ctrl.ensure_coder("coder call")
-        call = self.ctrl.coder_begin(body.get("metadata", {}).get("stem", "?"))
+        call = self.ctrl.coder_begin(str(affinity_key.get() or body.get("metadata", {}).get("stem", "?")))
         try:
             return await self.inner.chat(body)
         finally:

@@ -25,14 +25,15 @@ from typing import Callable, Dict, List, Optional
 
 import httpx
 
-from ..serve.router import LoadBalancedClient
+from ..serve.router import LoadBalancedClient, affinity_key
 from .agents import CriticAgent, JudgeAgent, JudgeSettings, PlannerAgent, SceneCoderAgent, bytes_to_data_url
 from .batch_stats import BatchStats
+from .burst import BurstCoderBackend, BurstController
 from .embed import Embedder, EmbedderSettings
 from .jscheck import CheckerSettings, JSChecker, code_digest
 from .kpolicy import BudgetK, RenderBrake, RoundGuard, detect_cores, start_k
 from .renderer import RendererModule, RendererSettings
-from .session import CALL_LOG, HTTPBackend, ImageResendBackend, InstrumentedBackend, purpose_var
+from .session import CALL_LOG, BackendError, HTTPBackend, ImageResendBackend, InstrumentedBackend, purpose_var
 from .settings import Settings
 from .stages import CandidateFactory, StageLimits, make_duel, multigen_first_iter
 from .state import Candidate, MinerState, PipelineTask
@@ -74,9 +75,11 @@ class Orchestrator:
             if kp.budget else None
         self.brake: Optional[RenderBrake] = RenderBrake(a.renderer.workers, kp.render_backlog) \
             if kp.render_brake else None
+        self.on_task_done: Optional[Callable[[str], None]] = None
 
     async def run_one(self, task: PipelineTask, deadline: Optional[float] = None) -> PipelineTask:
         task.started_at = task.started_at or time.time()
+        affinity_key.set(task.stem)         # the task's LLM calls stick to one replica (prefix cache)
         try:
             await self._run(task, deadline)
         except asyncio.CancelledError:
@@ -88,6 +91,8 @@ class Orchestrator:
             task.fail("no valid candidate")
         task.finished_at = time.time()
         task.done = True
+        if self.on_task_done is not None:
+            self.on_task_done(task.stem)
         return task
 
     async def _run(self, task: PipelineTask, deadline: Optional[float]):
@@ -221,6 +226,7 @@ class GenerationPipeline:
                                 margin_s=kp.margin_s, overhead_s=kp.overhead_s, steps=tuple(kp.steps),
                                 k_floor=kp.k_floor, idle_reset_s=kp.idle_reset_s)
         self.k0: Optional[int] = None
+        self.burst: Optional[BurstController] = None
         self.current: Dict[str, PipelineTask] = {}
         self.probe_tps: Optional[float] = None
 
@@ -234,17 +240,47 @@ class GenerationPipeline:
             raw = HTTPBackend(c.base_url.rstrip("/").removesuffix("/v1"), c.request_timeout_s, api_key=c.key())
         return raw
 
-    def _role_backend(self, role: str):
+    def _role_inner(self, role: str):
+        """The raw backend of a role: one client; several real clients -> a LoadBalancedClient (weighted, per-task
+        affinity, load-aware migration); several with injected backends -> a weighted spread."""
         a = getattr(self.s.actors, role)
         names = [a.client, *a.extra_clients] if a.client else []
         if not names:
             return None
+        weights = a.client_weights or [1] * len(names)
         if len(names) == 1:
-            inner = self._backend(names[0])
-        else:
-            inner = _MultiBackend([self._backend(n) for n in names], a.client_weights or [1] * len(names))
+            return self._backend(names[0])
+        if any(n in self._backends_override for n in names):
+            return _MultiBackend([self._backend(n) for n in names], weights)
+        cs = [self.s.llm_clients[n] for n in names]
+        return LoadBalancedClient([c.base_url.rstrip("/").removesuffix("/v1") for c in cs], weights,
+                                  client=self.http,
+                                  headers=[{"Authorization": f"Bearer {c.key()}"} if c.key() else {} for c in cs],
+                                  error=BackendError)
+
+    def _wrap(self, role: str, inner):
+        if inner is None:
+            return None
         self.stats.roles[role] = role
         return InstrumentedBackend(ImageResendBackend(inner), role)
+
+    def _role_backend(self, role: str):
+        return self._wrap(role, self._role_inner(role))
+
+    def _setup_burst(self, judge_inner) -> Optional[BurstController]:
+        """The burst controller over the judge's load-balanced client, or None (off, or nothing to lend to)."""
+        b = self.s.burst
+        if not b.enabled:
+            return None
+        lb = judge_inner
+        if isinstance(lb, HTTPBackend):
+            lb = LoadBalancedClient([lb.url], headers=[lb.headers], error=BackendError)
+        if not (hasattr(lb, "add_replicas") and hasattr(lb, "set_active")) or not b.proxy_url or not b.judge_replicas:
+            log.warning("burst: needs a load-balanced judge client, burst.proxy_url and burst.judge_replicas; off")
+            return None
+        idxs = lb.add_replicas(b.judge_replicas, active=False)
+        return BurstController(lb, idxs, b.proxy_url, b.coder_upstreams, http=self.http, delay_s=b.delay_s,
+                               drain_s=b.drain_s)
 
     def startup(self) -> None:
         a = self.s.actors
@@ -253,12 +289,17 @@ class GenerationPipeline:
         e = self.s.embedder
         self.embedder = Embedder(EmbedderSettings(enabled=e.enabled, model_dir=e.model_dir, device=e.device,
                                                   batch_size=e.batch_size)) if e.enabled else None
-        coder_be = self._role_backend("coder")
-        if coder_be is None:
+        coder_inner, judge_inner = self._role_inner("coder"), self._role_inner("judge")
+        self.role_inner = {"coder": coder_inner, "judge": judge_inner}
+        if coder_inner is None:
             raise ValueError("actors.coder.client is required")
+        self.burst = self._setup_burst(judge_inner)
+        if self.burst is not None:
+            coder_inner, judge_inner = BurstCoderBackend(coder_inner, self.burst), self.burst.lb
+        coder_be = self._wrap("coder", coder_inner)
         coders = [SceneCoderAgent(coder_be, a.coder.model, self.checker, name="coder", max_repairs=a.coder.max_repairs,
                                   max_tokens=a.coder.max_tokens, temperature=a.coder.temperature, top_p=a.coder.top_p)]
-        judge_be = self._role_backend("judge")
+        judge_be = self._wrap("judge", judge_inner)
         judge = JudgeAgent(judge_be, a.judge.model, JudgeSettings(max_stage=a.judge.max_stage,
                                                                   concurrency=a.judge.workers,
                                                                   max_tokens=min(a.judge.max_tokens, 2048)),
@@ -269,6 +310,8 @@ class GenerationPipeline:
         planner = PlannerAgent(planner_be, a.planner.model) if planner_be is not None else None
         self.orch = Orchestrator(coders, judge, critic, planner, self.renderer, self.embedder, self.s, self.stats,
                                  self.http)
+        if self.burst is not None:
+            self.orch.on_task_done = self.burst.task_done
         kp = self.s.pipeline.k_policy
         cores = detect_cores()[0] if kp.start == "cpu" else None
         self.k0, src = start_k(kp.start, a.coder.ensemble_size, cores, kp.cpu_per_candidate, kp.k_min)
@@ -308,6 +351,8 @@ class GenerationPipeline:
         self.stats.reset()
         self.orch.k = self.guard.before_batch(self.k0)
         self.state.diag["k"] = self.orch.k
+        if self.burst is not None:
+            self.burst.batch_start(len(tasks), [t.stem for t in tasks])
         budget = self.s.pipeline.batch_time_budget
         eff = max(1.0, budget - self.s.pipeline.batch_margin_s)
         t_start = time.monotonic()
@@ -352,6 +397,9 @@ class GenerationPipeline:
             self.stats.end()
             wall = time.monotonic() - t_start
             self.guard.after_batch(self.orch.k, wall)
+            if self.burst is not None:
+                self.burst.batch_end()
+                self.state.diag["burst"] = self.burst.state
             if self.orch is not None and self.orch.budget_k is not None:
                 self.orch.budget_k.batch_end()
             self.state.stats_header = self.stats.header_parts()

@@ -200,10 +200,13 @@ class EventBusConfig(BaseModel):
 
 
 class BurstConfig(BaseModel):
+    """Lend the coder GPUs to sleeping judge replicas in a batch's judge-only tail (app/burst.py)."""
     enabled: bool = False
-    proxy_url: str = ""
-    judge_replicas: List[str] = Field(default_factory=list)
-    tail_fraction: float = 0.2
+    proxy_url: str = ""                                   # the coder engines' router (park / unpark)
+    coder_upstreams: List[str] = Field(default_factory=list)   # engines behind it to park (empty: all active)
+    judge_replicas: List[str] = Field(default_factory=list)    # sleeping judge engines on the coder GPUs
+    delay_s: float = 2.0                                  # quiet period after coding ends before the swap
+    drain_s: float = 60.0
 
 
 class Settings(BaseModel):

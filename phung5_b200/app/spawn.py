@@ -34,6 +34,7 @@ class EngineJob:
     dp: int
     spec: str = "tree"
     extra_args: List[str] = field(default_factory=list)
+    max_num_seqs: int = 64
 
     def replica_gpus(self) -> List[List[str]]:
         return [self.gpu_ids[i * self.tp:(i + 1) * self.tp] for i in range(self.dp)]
@@ -106,7 +107,7 @@ def build_jobs(settings: Settings, all_gpus: Optional[List[str]] = None, base_po
         if tp * dp != len(ids):
             raise ValueError(f"{n}: tp {tp} x dp {dp} != {len(ids)} assigned GPU(s) {ids}")
         port = e.port or urlparse(c.base_url).port or base_port
-        jobs.append(EngineJob(n, e.model, port, ids, tp, dp, e.spec, list(e.extra_args)))
+        jobs.append(EngineJob(n, e.model, port, ids, tp, dp, e.spec, list(e.extra_args), e.max_num_seqs))
     return jobs
 
 
@@ -116,7 +117,7 @@ def build_commands(job: EngineJob, python: str = sys.executable, master_port0: i
     for r, (gids, port) in enumerate(zip(job.replica_gpus(), job.replica_ports())):
         env = {"CUDA_VISIBLE_DEVICES": ",".join(gids)}
         serve = ["-m", "phung5_b200.serve.server", "--model", job.model, "--port", str(port), "--spec", job.spec,
-                 *job.extra_args]
+                 "--max-num-seqs", str(job.max_num_seqs), *job.extra_args]
         if job.tp > 1:
             cmd = [python, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={job.tp}",
                    "--master-addr=127.0.0.1", f"--master-port={master_port0 + job.port % 1000 + r}", *serve]

@@ -58,6 +58,7 @@ class Request:
     t_first: float = 0.0
     t_done: float = 0.0
     gslot: int = -1           # hybrid models: GDN state slot
+    resume_root: Optional[int] = None   # preempted: the pending token to resume with after the recompute
     mm: List[Tuple[int, torch.Tensor]] = field(default_factory=list)   # (prompt position, image features [n, H])
 
 
@@ -190,7 +191,7 @@ class LLMEngine:
         self.running: List[Request] = []
         self._next_rid = 0
         self.stats = {"steps": 0, "spec_steps": 0, "tokens_out": 0, "accepted": 0, "prefill_tokens": 0,
-                      "h2d_bytes": 0, "d2h_bytes": 0, "graph_replays": 0}
+                      "h2d_bytes": 0, "d2h_bytes": 0, "graph_replays": 0, "preempted": 0}
         self.use_cascade = cfg.cache.enable_cascade
         import os as _os
         self._host_timing = _os.environ.get("PHX_HOST_TIMING") == "1"
@@ -318,6 +319,7 @@ class LLMEngine:
             outs += self._prefill()
         live = [r for r in self.running if not r.finished and r.root is not None]
         if live:
+            live = self._make_room(live)
             if self.spec_on:
                 outs += self._spec_step(live)
             else:
@@ -325,6 +327,71 @@ class LLMEngine:
         self.running = [r for r in self.running if not r.finished]
         self.stats["steps"] += 1
         return outs
+
+    # ------------------------------------------------------------------------------------------
+    # admission and preemption: a request is admitted only while fewer than max_running run and the KV pool
+    # can hold its prompt plus every running request's next step; when a step's pages do not fit, the most
+    # recently admitted requests are preempted (pages released, their full pages left in the prefix cache) and
+    # requeued first in line to recompute their committed tokens, resuming with their pending token
+    # ------------------------------------------------------------------------------------------
+    def _step_tokens(self) -> int:
+        """Positions past `committed` a running request's next step writes (verify tree / draft scratch)."""
+        if not self.spec_on:
+            return 1
+        return max(self.N, 1 + (self.D - 1) * self.K) + 1
+
+    def _step_need(self, r: Request) -> int:
+        return max(0, -(-(r.committed + self._step_tokens()) // self.ps) - len(r.pages))
+
+    def _make_room(self, live: List[Request]) -> List[Request]:
+        need = sum(self._step_need(r) for r in live)
+        while need > self.pool.prefix.obtainable() and len(live) > 1:
+            victim = live.pop()
+            need -= self._step_need(victim)
+            self._preempt(victim)
+        return live
+
+    def _preempt(self, r: Request) -> None:
+        if self.hybrid and r.gslot >= 0:
+            self.gdn_pool.release(r.gslot)
+            r.gslot = -1
+        n_full = min(r.committed, len(r.tokens)) // self.ps
+        self.pool.prefix.insert(self._cache_tokens(r), r.pages, n_full)
+        self.pool.prefix.release(r.pages)
+        r.pages = []
+        r.resume_root, r.root = r.root, None
+        r.prompt_len = r.committed            # recompute prompt + accepted output, then continue
+        r.prefilled = r.committed = r.dlen = 0
+        self.running.remove(r)
+        self.waiting.insert(0, r)
+        self.stats["preempted"] += 1
+
+    def _new_pages(self, r: Request, local_keys: Dict[int, int]) -> Tuple[int, int]:
+        """(pages a new request must allocate for its prompt and first step, cached pages it would take out of
+        the evictable set): its leading full pages already in the prefix cache, or being written by a request
+        earlier in this prefill pass, are shared, not allocated."""
+        total = -(-(r.prompt_len + self._step_tokens()) // self.ps)
+        if self.hybrid:
+            return total, 0
+        pc = self.pool.prefix
+        hit = lru_hit = 0
+        for k in pc.chain_keys(self._cache_tokens(r), self.ps, (r.prompt_len - 1) // self.ps):
+            if k in pc.table:
+                lru_hit += k in pc.lru
+            elif k not in local_keys:
+                break
+            hit += 1
+        return total - hit, lru_hit
+
+    def _admissible(self, r: Request, n_new: int, reserve: int, local_keys: Dict[int, int]) -> Tuple[bool, int]:
+        """(admit?, pages it will allocate)."""
+        if len(self.running) + n_new >= self.cfg.max_running:
+            return False, 0
+        if self.hybrid and not self.gdn_pool.free:
+            return False, 0
+        need, lru_hit = self._new_pages(r, local_keys)
+        ok = need + reserve <= self.pool.prefix.obtainable() - lru_hit or (not self.running and n_new == 0)
+        return ok, need
 
     # ------------------------------------------------------------------------------------------
     def _slot(self, r: Request, pos: int) -> int:
@@ -404,8 +471,16 @@ class LLMEngine:
         budget = self.cfg.max_prefill_tokens
         batch: List[Tuple[Request, int, int]] = []  # (req, start, end)
         local_keys: Dict[int, int] = {}
+        reserve = sum(self._step_need(x) for x in self.running if not x.finished)
+        n_new = 0
         while self.waiting and budget > 0:
             r = self.waiting[0]
+            if r.prefilled == 0 and not r.pages:
+                ok, need = self._admissible(r, n_new, reserve, local_keys)
+                if not ok:
+                    break
+                n_new += 1
+                reserve += need
             if self.hybrid and r.gslot < 0:
                 r.gslot = self.gdn_pool.alloc()
             if r.prefilled == 0 and not r.pages and not self.hybrid:
@@ -470,6 +545,16 @@ class LLMEngine:
         done = [(i, r) for i, (r, s, e) in enumerate(batch) if e == r.prompt_len]
         for r, s, e in batch:
             r.committed = e
+        if not self.hybrid:
+            # a finished prompt's full pages join the prefix cache now (later prefill passes share them); its draft
+            # KV is written by this step's catch-up, before any later request can match them
+            for _, r in done:
+                self.pool.prefix.insert(self._cache_tokens(r), r.pages, r.prompt_len // self.ps)
+        resumed = [r for _, r in done if r.resume_root is not None]
+        for r in resumed:                      # recomputed after a preemption: the pending token is known
+            r.root, r.resume_root = r.resume_root, None
+            self.running.append(r)
+        done = [(i, r) for i, r in done if all(r is not x for x in resumed)]
         if done:
             firsts = self._first_token(logits[[i for i, _ in done]], [r for _, r in done])
             for (i, r), t in zip(done, firsts):

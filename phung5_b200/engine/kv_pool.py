@@ -114,6 +114,10 @@ class PrefixCache:
             freed += 1
         return freed
 
+    def obtainable(self) -> int:
+        """Pages an allocation can get now: free ones plus unreferenced cached ones (evicted on demand)."""
+        return self.alloc.available() + len(self.lru)
+
     def alloc_pages(self, n: int) -> List[int]:
         if self.alloc.available() < n:
             self.evict(n - self.alloc.available())

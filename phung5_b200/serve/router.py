@@ -18,7 +18,7 @@ import asyncio
 import contextvars
 import itertools
 import time
-from typing import Dict, List, Optional
+from typing import Callable, Dict, List, Optional
 
 import httpx
 
@@ -148,8 +148,11 @@ class LoadBalancedClient:
     least-loaded active replica."""
 
     def __init__(self, base_urls: List[str], weights: Optional[List[int]] = None, migrate_margin: int = 8,
-                 client: Optional[httpx.AsyncClient] = None):
+                 client: Optional[httpx.AsyncClient] = None, headers: Optional[List[dict]] = None,
+                 error: Optional[Callable[[int, str], Exception]] = None):
         self.urls = [u.rstrip("/") for u in base_urls]
+        self.headers = list(headers or [{} for _ in self.urls])
+        self.error = error            # status, body -> the exception a failed call raises (default: httpx's)
         self.weights = list(weights or [1] * len(self.urls))
         self.active = [True] * len(self.urls)
         self.inflight = [0] * len(self.urls)
@@ -166,6 +169,7 @@ class LoadBalancedClient:
         idx = []
         for u, w in zip(urls, weights or [1] * len(urls)):
             self.urls.append(u.rstrip("/"))
+            self.headers.append({})
             self.weights.append(w)
             self.active.append(active)
             self.inflight.append(0)
@@ -203,7 +207,9 @@ class LoadBalancedClient:
         i = self.pick_index()
         self.inflight[i] += 1
         try:
-            r = await self.http.post(self.urls[i] + "/v1/chat/completions", json=body)
+            r = await self.http.post(self.urls[i] + "/v1/chat/completions", json=body, headers=self.headers[i])
+            if r.status_code >= 400 and self.error is not None:
+                raise self.error(r.status_code, r.text)
             r.raise_for_status()
             return r.json()
         finally:

@@ -348,6 +348,8 @@ def main(argv=None):
     ap.add_argument("--draft-path", default=None, help="EAGLE head checkpoint directory (else a random head)")
     ap.add_argument("--vision", action="store_true", help="serve image inputs with a (seeded random) vision tower")
     ap.add_argument("--num-pages", type=int, default=0)
+    ap.add_argument("--max-num-seqs", type=int, default=256,
+                    help="requests decoded at once; more wait (admission also waits for KV pages)")
     ap.add_argument("--comm", default="fused", choices=["nccl", "fused"],
                     help="tensor-parallel collectives when launched with torchrun over several GPUs")
     args = ap.parse_args(argv)
@@ -378,7 +380,8 @@ def main(argv=None):
         if args.draft_path is not None:
             drafter = load_eagle(args.draft_path, model_cfg, device, rank_, world)
     cfg = EngineConfig(model=model_cfg, spec=spec, draft=DraftConfig(kind="eagle"),
-                       cache=CacheConfig(num_pages=args.num_pages), parallel=ParallelConfig(tp=world, comm=args.comm))
+                       cache=CacheConfig(num_pages=args.num_pages), parallel=ParallelConfig(tp=world, comm=args.comm),
+                       max_running=args.max_num_seqs)
     eng = LLMEngine(cfg, device=device, comm=comm, target=target, drafter=drafter)
     if group is not None and comm.rank != 0:
         tp_worker_loop(eng, group)

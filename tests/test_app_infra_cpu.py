@@ -112,6 +112,7 @@ def test_spawner_allocation_and_commands():
     cmds = build_commands(jobs["coder"], python="py")
     assert len(cmds) == 3 and cmds[0]["env"]["CUDA_VISIBLE_DEVICES"] == "0,1" and cmds[1]["env"]["CUDA_VISIBLE_DEVICES"] == "2,3"
     assert "--nproc-per-node=2" in cmds[0]["cmd"] and cmds[0]["cmd"][cmds[0]["cmd"].index("--port") + 1] == "8101"
+    assert cmds[0]["cmd"][cmds[0]["cmd"].index("--max-num-seqs") + 1] == "64"
     assert cmds[2]["cmd"][:3] == ["py", "-m", "phung5_b200.serve.router"] and cmds[2]["cmd"].count("--upstream") == 2
     assert build_commands(jobs["judge"], python="py")[0]["cmd"][:3] == ["py", "-m", "phung5_b200.serve.server"]
     with pytest.raises(ValueError):
@@ -205,3 +206,97 @@ def test_checker_process_pool():
         assert c.counts == {"checked": 2, "passed": 1}
     finally:
         c.close()
+
+
+def test_pipeline_lends_coder_gpus_to_judge_replicas_in_the_judge_only_tail():
+    """The burst controller wired into the service: a batch's judge-only tail parks the coder engines behind
+    their proxy, wakes the judge replica and routes judge calls to it too; the batch end swaps back."""
+    import asyncio
+    import json as _json
+
+    import httpx
+
+    from phung5_b200.app.pipeline import GenerationPipeline
+    from phung5_b200.app.session import BackendError
+    from phung5_b200.app.state import MinerState, PipelineTask
+    from phung5_b200.serve.router import LoadBalancedClient
+    from test_app_cpu import StubLLM, _png, _settings
+
+    stub = StubLLM()
+    seen = []
+
+    async def handler(req):
+        host, path = req.url.host, req.url.path
+        seen.append((host, path))
+        if path == "/v1/chat/completions":
+            await asyncio.sleep(0.02)
+            return httpx.Response(200, json=await stub.chat(_json.loads(req.content)))
+        if path == "/park_state":
+            return httpx.Response(200, json={"active": ["http://c1"]})
+        return httpx.Response(200, json={"ok": True})
+
+    async def go():
+        http = httpx.AsyncClient(transport=httpx.MockTransport(handler))
+        s = _settings()
+        s.burst.enabled, s.burst.proxy_url, s.burst.judge_replicas, s.burst.delay_s = True, "http://proxy", \
+            ["http://jr1"], 0.01
+        judge = LoadBalancedClient(["http://j0"], client=http, error=BackendError)
+        pipe = GenerationPipeline(s, MinerState(), backends={"coder": stub, "judge": judge}, http=http)
+        pipe.startup()
+        tasks = [PipelineTask(stem=n, image_url=_png(), seed=10 + i) for i, n in enumerate(("chair", "lamp"))]
+        await pipe.run_batch(tasks)
+        await asyncio.sleep(0.05)                 # the batch end's swap back runs in the background
+        pipe.close()
+        return pipe
+    pipe = asyncio.run(go())
+    whats = [e["what"] for e in pipe.burst.events]
+    assert "to_judge" in whats and whats.index("to_judge") < len(whats) - 1 and "to_coder" in whats
+    assert ("proxy", "/park") in seen and ("jr1", "/wake_up") in seen
+    assert ("jr1", "/sleep") in seen and ("proxy", "/unpark") in seen
+    assert ("jr1", "/v1/chat/completions") in seen                 # the lent replica judged
+    assert pipe.burst.state == "coder" and pipe.burst.parked == ["http://c1"]
+    assert all(pipe.state.tasks[n].js_code for n in ("chair", "lamp"))
+
+
+def test_two_judge_clients_share_load_with_per_task_affinity():
+    import asyncio
+    import json as _json
+
+    import httpx
+
+    from phung5_b200.app.pipeline import GenerationPipeline
+    from phung5_b200.app.state import MinerState, PipelineTask
+    from phung5_b200.serve.router import LoadBalancedClient
+    from test_app_cpu import StubLLM, _png, _settings
+
+    stub = StubLLM()
+    hosts = []
+
+    async def handler(req):
+        hosts.append(req.url.host)
+        if req.url.host == "j1" and len([h for h in hosts if h == "j1"]) == 1:
+            # a context-length 400 comes back through the balancer as the session's BackendError: it retries
+            # with a smaller max_tokens
+            return httpx.Response(400, text="This model's maximum context length is 100000 tokens. However, you "
+                                            "requested 100500 tokens (99000 in the messages, 1500 in the "
+                                            "completion).")
+        return httpx.Response(200, json=await stub.chat(_json.loads(req.content)))
+
+    async def go():
+        http = httpx.AsyncClient(transport=httpx.MockTransport(handler))
+        s = _settings()
+        s.llm_clients["judge"].base_url = "http://j0/v1"
+        s.llm_clients["judge2"] = s.llm_clients["judge"].model_copy(update={"base_url": "http://j1/v1"})
+        s.actors.judge.extra_clients = ["judge2"]
+        pipe = GenerationPipeline(s, MinerState(), backends={"coder": stub}, http=http)
+        pipe.startup()
+        tasks = [PipelineTask(stem=n, image_url=_png(), seed=10 + i) for i, n in enumerate(("chair", "lamp"))]
+        await pipe.run_batch(tasks)
+        pipe.close()
+        return pipe
+    pipe = asyncio.run(go())
+    lb = pipe.role_inner["judge"]
+    assert isinstance(lb, LoadBalancedClient)
+    assert sorted(lb.affinity) == ["chair", "lamp"] and sorted(lb.affinity.values()) == [0, 1]
+    assert set(hosts) == {"j0", "j1"}
+    assert all(pipe.state.tasks[n].js_code for n in ("chair", "lamp"))
