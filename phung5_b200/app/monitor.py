@@ -8,7 +8,8 @@ and the coder probe / warm-up finished, and handles an engine going down.
 Here a prober polls `GET /health` and `GET /v1/models` of every enabled client concurrently (bounded by a
 request timeout), mapping the result to STARTING (not answering yet, within the start grace), RUNNING,
 or DOWN (failed after grace, or answering with the wrong model). The watcher drives `MinerState`:
-WARMING_UP -> READY when all RUNNING and `on_ready` (probe, warm-up) completed; a DOWN engine during
+WARMING_UP -> READY when all RUNNING and `on_ready` (probe, warm-up) completed, or -> REPLACE when `on_ready`
+reports an unhealthy coder (probe below its min_tps floor) and replacements remain; a DOWN engine during
 READY/COMPLETE -> REPLACE when replacements remain, else the service keeps serving what it can.
 """
 from __future__ import annotations
@@ -75,13 +76,20 @@ class HealthWatcher:
             self.state.set_llm_status(name, st)
         s = self.state
         if s.status == MinerStatus.WARMING_UP and s.models_ready():
+            healthy = True
             if not self.ready_done and self.on_ready is not None:
                 try:
-                    await self.on_ready()
+                    healthy = await self.on_ready() is not False
                 except Exception:  # noqa: BLE001 - a failed warm-up does not block READY
                     log.exception("warm-up failed")
             self.ready_done = True
-            s.status = MinerStatus.READY
+            if not healthy and s.replacements_remaining > 0:
+                log.warning("coder probe below its floor; requesting replacement")
+                s.status = MinerStatus.REPLACE
+            else:
+                if not healthy:
+                    log.warning("coder probe below its floor but no replacement left; serving anyway")
+                s.status = MinerStatus.READY
         elif s.any_down() and s.status in (MinerStatus.READY, MinerStatus.COMPLETE) and s.replacements_remaining > 0:
             log.warning("engine down (%s); requesting replacement",
                         {n: p.last_error for n, p in self.probers.items() if p.state == ServiceState.DOWN})

@@ -241,8 +241,10 @@ class GenerationPipeline:
         return raw
 
     def _role_inner(self, role: str):
-        """The raw backend of a role: one client; several real clients -> a LoadBalancedClient (weighted, per-task
-        affinity, load-aware migration); several with injected backends -> a weighted spread."""
+        """The raw backend of a role: one client; several real clients of a judging role (replicas of one model)
+        -> a LoadBalancedClient (weighted, per-task affinity for the engines' prefix caches, load-aware
+        migration); the coder's clients (a mix of coder models: every prompt's drafts spread over them) or
+        injected backends -> a weighted per-call spread."""
         a = getattr(self.s.actors, role)
         names = [a.client, *a.extra_clients] if a.client else []
         if not names:
@@ -250,7 +252,7 @@ class GenerationPipeline:
         weights = a.client_weights or [1] * len(names)
         if len(names) == 1:
             return self._backend(names[0])
-        if any(n in self._backends_override for n in names):
+        if role == "coder" or any(n in self._backends_override for n in names):
             return _MultiBackend([self._backend(n) for n in names], weights)
         cs = [self.s.llm_clients[n] for n in names]
         return LoadBalancedClient([c.base_url.rstrip("/").removesuffix("/v1") for c in cs], weights,
@@ -321,7 +323,9 @@ class GenerationPipeline:
     # ----------------------------------------------------------------------------------------------- probe
 
     async def run_coder_probe(self) -> Optional[float]:
-        """Aggregate coder output tokens/s at `concurrency` concurrent text-only requests."""
+        """Aggregate coder output tokens/s at `concurrency` concurrent text-only requests: one untimed burst first
+        (a fresh engine pays its CUDA-graph captures and first-touch allocations on it), then the timed burst.
+        Records probe_tps (and probe_tps_cold, probe_errors) in the diag header; None if every call failed."""
         cfg = self.s.pipeline.coder_probe
         if not cfg.enabled or self.orch is None:
             return None
@@ -330,18 +334,40 @@ class GenerationPipeline:
         body = {"model": model, "max_tokens": cfg.max_tokens, "temperature": 0.7,
                 "messages": [{"role": "user", "content": "Write a three.js function that builds a chair."}]}
         purpose_var.set("coder:probe")
-        t0 = time.monotonic()
+
+        async def burst():
+            t0 = time.monotonic()
+            outs = await asyncio.wait_for(
+                asyncio.gather(*(be.chat({**body, "seed": i}) for i in range(cfg.concurrency)),
+                               return_exceptions=True), cfg.timeout_s)
+            toks = sum(int((o.get("usage") or {}).get("completion_tokens", 0)) for o in outs if isinstance(o, dict))
+            errs = [o for o in outs if not isinstance(o, dict)]
+            return toks, max(time.monotonic() - t0, 1e-3), errs
         try:
-            outs = await asyncio.wait_for(asyncio.gather(*(be.chat({**body, "seed": i}) for i in range(cfg.concurrency))),
-                                          cfg.timeout_s)
+            toks, dt, _ = await burst()
+            self.state.diag["probe_tps_cold"] = round(toks / dt)
+        except Exception as e:  # noqa: BLE001
+            log.warning("coder probe warm-up burst failed (%s); timing the probe anyway", e)
+        try:
+            toks, dt, errs = await burst()
         except (asyncio.TimeoutError, Exception) as e:  # noqa: BLE001
             log.warning("coder probe failed: %s", e)
+            self.state.diag["probe_tps"] = 0
+            return 0.0
+        self.state.diag["probe_errors"] = len(errs)
+        if errs and not toks:
+            self.state.diag["probe_tps"] = "?"
             return None
-        dt = time.monotonic() - t0
-        toks = sum(int((o.get("usage") or {}).get("completion_tokens", 0)) for o in outs)
-        self.probe_tps = toks / dt if dt > 0 else None
-        self.state.diag["probe_tps"] = f"{self.probe_tps:.0f}" if self.probe_tps else "?"
+        self.probe_tps = toks / dt
+        self.state.diag["probe_tps"] = f"{self.probe_tps:.0f}"
+        log.info("coder probe: %d x %d tokens -> %d in %.1f s = %.0f tok/s (errors %d, min_tps %.0f)",
+                 cfg.concurrency, cfg.max_tokens, toks, dt, self.probe_tps, len(errs), cfg.min_tps)
         return self.probe_tps
+
+    def probe_ok(self, tps: Optional[float]) -> bool:
+        """False when the coder probe measured less than pipeline.coder_probe.min_tps (0 = no floor)."""
+        m = self.s.pipeline.coder_probe.min_tps
+        return not (m > 0 and tps is not None and tps < m)
 
     # ----------------------------------------------------------------------------------------------- batch
 

@@ -65,8 +65,10 @@ def build_app(settings: Settings, backends: Optional[Dict[str, object]] = None, 
         probers = {name: EngineProber(name, c.base_url, "") for name, c in settings.enabled_clients().items()}
 
         async def on_ready():
+            """Coder probe before READY; False (a coder slower than min_tps) asks for a replacement."""
             if settings.warmup:
-                await pipeline.run_coder_probe()
+                return pipeline.probe_ok(await pipeline.run_coder_probe())
+            return True
 
         watcher = HealthWatcher(state, probers, on_ready=on_ready)
         app.state.watcher = watcher

@@ -300,3 +300,43 @@ def test_two_judge_clients_share_load_with_per_task_affinity():
     assert sorted(lb.affinity) == ["chair", "lamp"] and sorted(lb.affinity.values()) == [0, 1]
     assert set(hosts) == {"j0", "j1"}
     assert all(pipe.state.tasks[n].js_code for n in ("chair", "lamp"))
+
+
+def test_coder_probe_warm_burst_and_min_tps_replace_gate():
+    import asyncio
+
+    from phung5_b200.app.monitor import HealthWatcher
+    from phung5_b200.app.pipeline import GenerationPipeline
+    from phung5_b200.app.state import MinerState, MinerStatus
+    from test_app_cpu import StubLLM, _settings
+
+    class Slow(StubLLM):
+        def __init__(self):
+            super().__init__()
+            self.n = 0
+
+        async def chat(self, body):
+            self.n += 1
+            await asyncio.sleep(0.05 if self.n <= 4 else 0.01)       # the first burst pays the warm-up
+            return {"choices": [{"message": {"role": "assistant", "content": "x"}, "finish_reason": "stop"}],
+                    "usage": {"prompt_tokens": 5, "completion_tokens": 100}}
+
+    s = _settings()
+    s.pipeline.coder_probe.concurrency, s.pipeline.coder_probe.min_tps = 4, 1e9
+    st = MinerState()
+    pipe = GenerationPipeline(s, st, backends={"coder": Slow(), "judge": StubLLM()})
+    pipe.startup()
+    tps = asyncio.run(pipe.run_coder_probe())
+    assert tps > 0 and int(st.diag["probe_tps"]) > st.diag["probe_tps_cold"] and st.diag["probe_errors"] == 0
+    assert not pipe.probe_ok(tps) and pipe.probe_ok(None)
+    pipe.close()
+
+    async def on_ready():
+        return False
+
+    for remaining, want in ((1, MinerStatus.REPLACE), (0, MinerStatus.READY)):
+        ms = MinerState()
+        ms.replacements_remaining = remaining
+        w = HealthWatcher(ms, {}, on_ready=on_ready)
+        asyncio.run(w.tick())
+        assert ms.status == want
