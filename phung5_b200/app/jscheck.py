@@ -177,7 +177,9 @@ def _declared_names(prog) -> Set[str]:
         tag = n[0]
         if tag in ("id",):
             names.add(n[1])
-        elif tag == "fundecl":
+        elif tag in ("fundecl", "classdecl"):
+            names.add(n[1])
+        elif tag == "class" and n[1]:
             names.add(n[1])
         elif tag == "func":
             if n[1]:
@@ -239,6 +241,8 @@ def _scope_clash(stmts, params: Iterable[str] = (), function_top: bool = False) 
             names, var_like = [n for tgt, _ in st[2] for n in _bound_names(tgt)], st[1] == "var"
         elif st[0] == "fundecl":
             names, var_like = [st[1]], function_top
+        elif st[0] == "classdecl":
+            names, var_like = [st[1]], False
         else:
             continue
         for n in names:

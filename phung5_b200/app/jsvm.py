@@ -44,11 +44,13 @@ class JSBudget(JSError):
 
 
 class _Break(Exception):
-    pass
+    def __init__(self, label=None):
+        self.label = label
 
 
 class _Continue(Exception):
-    pass
+    def __init__(self, label=None):
+        self.label = label
 
 
 class _Return(Exception):
@@ -355,8 +357,12 @@ class Parser:
                 return ("dowhile", body, test)
             if v in ("break", "continue"):
                 self.i += 1
+                label = None
+                if self.cur.kind == "id" and not self.cur.nl:
+                    label = self.cur.val
+                    self.i += 1
                 self.semi()
-                return (v,)
+                return (v, label)
             if v == "throw":
                 self.i += 1
                 e = self.expression()
@@ -389,7 +395,11 @@ class Parser:
             if v == "import":
                 raise JSError("SyntaxError", "import statements are not allowed (THREE is passed to generate)")
             if v == "class":
-                raise JSError("SyntaxError", "class declarations are not supported")
+                node = self.class_def(need_name=True)
+                return ("classdecl", node[1], node)
+        if c.kind == "id" and self.peek().kind == "p" and self.peek().val == ":":
+            self.i += 2
+            return ("labeled", c.val, self.statement())
         e = self.expression()
         self.semi()
         return ("expr", e)
@@ -656,9 +666,8 @@ class Parser:
             if op == "in" and self.no_in:
                 return left
             p = _BINPREC[op]
-            if p < minp or (p == minp and op != "**"):
-                if not (op == "**" and p >= minp):
-                    return left
+            if p < minp:            # binds looser than the operator whose right operand this is
+                return left
             self.i += 1
             right = self.binary(p if op == "**" else p + 1)
             if op in ("&&", "||", "??"):
@@ -746,10 +755,10 @@ class Parser:
             self.i += 1
             parts = [p if isinstance(p, str) else Parser(p[1]).expression_only() for p in c.val]
             return ("tpl", parts)
-        if k == "id":
+        if k == "id" and c.val != "super":
             self.i += 1
             return ("ident", c.val)
-        if k == "kw":
+        if k in ("kw", "id"):
             v = c.val
             if v == "true" or v == "false":
                 self.i += 1
@@ -776,7 +785,20 @@ class Parser:
                 self.i += 1
                 return ("ident", v)
             if v == "class":
-                raise JSError("SyntaxError", "class expressions are not supported")
+                return self.class_def(need_name=False)
+            if v == "super":
+                self.i += 1
+                if self.at("("):
+                    return ("super_call", self.args())
+                if self.eat("."):
+                    name = self.cur
+                    self.i += 1
+                    return ("super_member", ("lit", name.val))
+                if self.eat("["):
+                    k = self.expression()
+                    self.expect("]")
+                    return ("super_member", k)
+                raise JSError("SyntaxError", "'super' must be called or followed by a property")
             if v == "import":
                 raise JSError("SyntaxError", "dynamic import is not allowed")
         if k == "p":
@@ -809,6 +831,57 @@ class Parser:
                 return self.object_lit()
         raise JSError("SyntaxError", f"unexpected token {c.val!r} at {c.pos}")
 
+    def class_def(self, need_name: bool):
+        """class [Name] [extends Expr] { constructor / methods / get / set / static / fields }"""
+        self.expect("class")
+        name = None
+        if self.cur.kind == "id":
+            name = self.cur.val
+            self.i += 1
+        elif need_name:
+            raise JSError("SyntaxError", "class declaration needs a name")
+        parent = None
+        if self.eat("extends", "id"):
+            parent = self.call_member(self.primary())
+        self.expect("{")
+        members = []          # (kind, static, key, value): kind method | get | set | field | ctor
+        while not self.eat("}"):
+            if self.eat(";"):
+                continue
+            static = False
+            if self.at("static", "id") and self.peek().val not in ("(", "=", ";", "}"):
+                self.i += 1
+                static = True
+            kind = "method"
+            if self.cur.val in ("get", "set") and self.cur.kind in ("id", "kw") and \
+                    self.peek().val not in ("(", "=", ";", "}"):
+                kind = self.cur.val
+                self.i += 1
+            if self.cur.kind == "p" and self.cur.val == "#":
+                raise JSError("SyntaxError", "private class members are not supported")
+            if self.eat("["):
+                key = ("computed", self.assign())
+                self.expect("]")
+            else:
+                c = self.cur
+                if c.kind not in ("id", "kw", "str", "num"):
+                    raise JSError("SyntaxError", f"bad class member name {c.val!r} at {c.pos}")
+                self.i += 1
+                key = _prop_key(c.val) if c.kind in ("str", "num") else c.val
+            if self.at("("):
+                ps, rest = self.params()
+                body = self.block()
+                fn = ("func", key if isinstance(key, str) else None, ps, rest, body, False)
+                if key == "constructor" and not static and kind == "method":
+                    members.append(("ctor", False, key, fn))
+                else:
+                    members.append((kind, static, key, fn))
+            else:
+                value = self.assign() if self.eat("=") else None
+                self.semi()
+                members.append(("field", static, key, value))
+        return ("class", name, parent, members)
+
     def object_lit(self):
         self.expect("{")
         props = []
@@ -817,9 +890,12 @@ class Parser:
                 props.append(("spread", self.assign()))
             else:
                 c = self.cur
-                if c.kind in ("id", "kw") and c.val in ("get", "set") and self.peek().kind in ("id", "kw", "str") \
-                        and self.peek().val not in (",", ":", "("):
-                    raise JSError("SyntaxError", "getters/setters are not supported")
+                accessor = None
+                if c.kind in ("id", "kw") and c.val in ("get", "set") and \
+                        self.peek().kind in ("id", "kw", "str", "num") and self.peek().val not in (",", ":", "(", "}"):
+                    accessor = c.val
+                    self.i += 1
+                    c = self.cur
                 if self.eat("["):
                     key = ("computed", self.assign())
                     self.expect("]")
@@ -831,7 +907,11 @@ class Parser:
                     key = _prop_key(c.val)
                 else:
                     raise JSError("SyntaxError", f"bad object key {c.val!r} at {c.pos}")
-                if self.eat(":"):
+                if accessor is not None:
+                    ps, rest = self.params()
+                    body = self.block()
+                    props.append((accessor, key, ("func", None, ps, rest, body, False)))
+                elif self.eat(":"):
                     props.append(("kv", key, self.assign()))
                 elif self.at("("):
                     ps, rest = self.params()
@@ -899,12 +979,13 @@ def _to_pattern(node):
 
 
 class JSObject:
-    """A plain JS object: ordered own properties."""
-    __slots__ = ("props",)
+    """A plain JS object: ordered own properties and an optional prototype (another JSObject)."""
+    __slots__ = ("props", "proto")
     cls_name = "Object"
 
-    def __init__(self, props: Optional[dict] = None):
+    def __init__(self, props: Optional[dict] = None, proto: Optional["JSObject"] = None):
         self.props = {} if props is None else props
+        self.proto = proto
 
     def js_get(self, key: str):
         return self.props.get(key, UNDEF)
@@ -928,11 +1009,30 @@ class JSArray:
 
 
 class JSFunction:
-    __slots__ = ("name", "params", "rest", "body", "env", "arrow", "this", "props")
+    __slots__ = ("name", "params", "rest", "body", "env", "arrow", "this", "props", "home")
 
     def __init__(self, name, params, rest, body, env, arrow, this=UNDEF):
         self.name, self.params, self.rest, self.body = name, params, rest, body
         self.env, self.arrow, self.this = env, arrow, this
+        self.props = {}
+        self.home = None          # class methods: the object they were defined on (for `super.x`)
+
+
+class Accessor:
+    """A getter / setter pair stored as a property value (object literals and classes)."""
+    __slots__ = ("get", "set")
+
+    def __init__(self, get=None, set=None):
+        self.get, self.set = get, set
+
+
+class JSClass:
+    """A class: constructor, prototype object (methods and accessors), parent (a class, a host constructor
+    such as THREE.Group, or None), instance field initialisers, and static members in `props`."""
+    __slots__ = ("name", "ctor", "proto", "parent", "fields", "props", "env")
+
+    def __init__(self, name, ctor, proto, parent, fields, env):
+        self.name, self.ctor, self.proto, self.parent, self.fields, self.env = name, ctor, proto, parent, fields, env
         self.props = {}
 
 
@@ -986,6 +1086,12 @@ class Env:
 
 
 _TDZ = object()
+_MISSING = object()
+
+
+def _mine(ex, labels) -> bool:
+    """A break / continue belongs to this loop: unlabeled, or naming one of the loop's labels."""
+    return ex.label is None or ex.label in labels
 
 
 def _error_obj(kind, msg):
@@ -1024,6 +1130,8 @@ def _to_str(v) -> str:
         return ",".join("" if x is None or x is UNDEF else _to_str(x) for x in v.items)
     if isinstance(v, (JSFunction, Native)):
         return f"function {getattr(v, 'name', '') or ''}() {{ [code] }}"
+    if isinstance(v, JSClass):
+        return f"class {v.name} {{ }}"
     if isinstance(v, Host):
         return v.to_string()
     if isinstance(v, JSObject):
@@ -1079,7 +1187,7 @@ def _typeof(v) -> str:
         return "number"
     if isinstance(v, str):
         return "string"
-    if isinstance(v, (JSFunction, Native)):
+    if isinstance(v, (JSFunction, Native, JSClass)):
         return "function"
     return "object"
 
@@ -1187,6 +1295,8 @@ class Interp:
                 for target, _ in st[2]:
                     for nm in _pattern_names(target):
                         env.vars[nm] = _TDZ
+            elif tag == "classdecl":
+                env.vars[st[1]] = _TDZ
 
     def make_func(self, node, env, this=UNDEF):
         _, name, ps, rest, body, arrow = node
@@ -1197,7 +1307,7 @@ class Interp:
         for st in body:
             self.exec(st, env)
 
-    def exec(self, st, env):
+    def exec(self, st, env, labels=()):
         self.tick()
         tag = st[0]
         if tag == "expr":
@@ -1223,9 +1333,9 @@ class Interp:
         elif tag == "block":
             self.exec_block(st[1], Env(env))
         elif tag == "for":
-            self.exec_for(st, env)
+            self.exec_for(st, env, labels)
         elif tag == "forof":
-            self.exec_forof(st, env)
+            self.exec_forof(st, env, labels)
         elif tag == "forin":
             _, kind, target, it, body = st
             obj = self.eval(it, env)
@@ -1239,34 +1349,57 @@ class Interp:
                     self.bind(target, k, loop, kind)
                 try:
                     self.exec_body(body, loop)
-                except _Break:
-                    break
-                except _Continue:
-                    continue
+                except _Break as b:
+                    if _mine(b, labels):
+                        break
+                    raise
+                except _Continue as c:
+                    if _mine(c, labels):
+                        continue
+                    raise
         elif tag == "while":
             while _truthy(self.eval(st[1], env)):
                 self.tick()
                 try:
                     self.exec_body(st[2], Env(env))
-                except _Break:
-                    break
-                except _Continue:
-                    continue
+                except _Break as b:
+                    if _mine(b, labels):
+                        break
+                    raise
+                except _Continue as c:
+                    if _mine(c, labels):
+                        continue
+                    raise
         elif tag == "dowhile":
             while True:
                 self.tick()
                 try:
                     self.exec_body(st[1], Env(env))
-                except _Break:
-                    break
-                except _Continue:
-                    pass
+                except _Break as b:
+                    if _mine(b, labels):
+                        break
+                    raise
+                except _Continue as c:
+                    if not _mine(c, labels):
+                        raise
                 if not _truthy(self.eval(st[2], env)):
                     break
         elif tag == "break":
-            raise _Break()
+            raise _Break(st[1] if len(st) > 1 else None)
         elif tag == "continue":
-            raise _Continue()
+            raise _Continue(st[1] if len(st) > 1 else None)
+        elif tag == "labeled":
+            inner = st[2]
+            if inner[0] in ("for", "forof", "forin", "while", "dowhile"):
+                self.exec(inner, env, labels + (st[1],))
+            else:
+                try:
+                    self.exec(inner, env)
+                except _Break as b:
+                    if b.label != st[1]:
+                        raise
+        elif tag == "classdecl":
+            env.declare(st[1], self.make_class(st[2], env))
         elif tag == "fundecl":
             pass   # hoisted
         elif tag == "empty":
@@ -1296,7 +1429,7 @@ class Interp:
         else:
             self.exec(st, env)
 
-    def exec_for(self, st, env):
+    def exec_for(self, st, env, labels=()):
         _, init, test, update, body = st
         loop_env = Env(env)
         per_iter = init is not None and init[0] == "decl" and init[1] in ("let", "const")
@@ -1315,16 +1448,19 @@ class Interp:
                 it_env.consts = set(loop_env.consts)
             try:
                 self.exec_body(body, Env(it_env))
-            except _Break:
-                break
-            except _Continue:
-                pass
+            except _Break as b:
+                if _mine(b, labels):
+                    break
+                raise
+            except _Continue as c:
+                if not _mine(c, labels):
+                    raise
             if per_iter:
                 loop_env.vars.update({k: it_env.vars[k] for k in loop_env.vars})
             if update is not None:
                 self.eval(update, loop_env)
 
-    def exec_forof(self, st, env):
+    def exec_forof(self, st, env, labels=()):
         _, kind, target, it, body = st
         seq = self.iterate(self.eval(it, env))
         for v in seq:
@@ -1336,10 +1472,14 @@ class Interp:
                 self.bind(target, v, loop, kind)
             try:
                 self.exec_body(body, loop)
-            except _Break:
-                break
-            except _Continue:
-                continue
+            except _Break as b:
+                if _mine(b, labels):
+                    break
+                raise
+            except _Continue as c:
+                if _mine(c, labels):
+                    continue
+                raise
 
     def exec_try(self, st, env):
         _, body, param, handler, fin = st
@@ -1376,8 +1516,9 @@ class Interp:
                         self.exec(s, senv)
                 if matched:
                     break
-        except _Break:
-            pass
+        except _Break as b:
+            if b.label is not None:
+                raise
 
     def iterate(self, v) -> list:
         if isinstance(v, JSArray):
@@ -1440,13 +1581,17 @@ class Interp:
             put(target[2], JSArray(items[len(target[1]):]))
 
     # calls
-    def call(self, f, this, args):
+    def call(self, f, this, args, super_fn=None):
         self.tick()
         if isinstance(f, JSFunction):
             env = Env(f.env)
             if not f.arrow:
                 env.declare("this", this if this is not UNDEF else f.this)
                 env.declare("arguments", JSArray(list(args)))
+                if f.home is not None:
+                    env.declare("%home", f.home)
+                if super_fn is not None:
+                    env.declare("%super", _nat("super", lambda i, t, x, _e=env: super_fn(x, _e)))
             for i, (pat, default) in enumerate(f.params):
                 v = args[i] if i < len(args) else UNDEF
                 if v is UNDEF and default is not None:
@@ -1463,18 +1608,135 @@ class Interp:
             if f.fn is None:
                 raise _Throw(_error_obj("TypeError", f"class constructor {f.name} cannot be invoked without 'new'"))
             return f.fn(self, this, list(args))
+        if isinstance(f, JSClass):
+            raise _Throw(_error_obj("TypeError", f"class constructor {f.name} cannot be invoked without 'new'"))
         raise _Throw(_error_obj("TypeError", f"{_to_str(f)[:40]} is not a function"))
 
-    def construct(self, f, args):
+    def construct(self, f, args, new_target=None):
         self.tick()
+        if isinstance(f, JSClass):
+            return self.construct_class(f, list(args), new_target or f)
         if isinstance(f, Native) and f.ctor is not None:
-            return f.ctor(self, list(args))
+            obj = f.ctor(self, list(args))
+            if new_target is not None and isinstance(obj, JSObject):
+                obj.proto = new_target.proto
+            return obj
         if isinstance(f, JSFunction) and not f.arrow:
-            obj = JSObject()
-            env_this = obj
-            r = self.call(f, env_this, args)
+            obj = JSObject(proto=new_target.proto if new_target is not None else self.fn_prototype(f))
+            r = self.call(f, obj, args)
             return r if isinstance(r, (JSObject, JSArray, Host)) else obj
         raise _Throw(_error_obj("TypeError", f"{getattr(f, 'name', _typeof(f))} is not a constructor"))
+
+    @staticmethod
+    def fn_prototype(f: JSFunction) -> JSObject:
+        p = f.props.get("prototype")
+        if not isinstance(p, JSObject):
+            p = JSObject()
+            f.props["prototype"] = p
+        return p
+
+    def make_class(self, node, env) -> JSClass:
+        _, name, parent_e, members = node
+        parent = None
+        if parent_e is not None:
+            parent = self.eval(parent_e, env)
+            if parent is not None and not isinstance(parent, (JSClass, Native, JSFunction)):
+                raise _Throw(_error_obj("TypeError", "class extends value is not a constructor"))
+        cenv = Env(env)
+        proto = JSObject(proto=parent.proto if isinstance(parent, JSClass) else
+                         (self.fn_prototype(parent) if isinstance(parent, JSFunction) else None))
+        cls = JSClass(name or "", None, proto, parent, [], cenv)
+        if name:
+            cenv.declare(name, cls, const=True)
+        for kind, static, key, value in members:
+            k = _to_str(self.eval(key[1], cenv)) if isinstance(key, tuple) else key
+            target = cls.props if static else proto.props
+            if kind == "ctor":
+                cls.ctor = self.make_func(value, cenv)
+                cls.ctor.home = proto
+            elif kind == "field":
+                if static:
+                    fenv = Env(cenv)
+                    fenv.declare("this", cls)
+                    cls.props[k] = UNDEF if value is None else self.eval(value, fenv)
+                else:
+                    cls.fields.append((k, value))
+            else:
+                fn = self.make_func(value, cenv)
+                fn.home = cls if static else proto
+                if kind == "method":
+                    target[k] = fn
+                else:
+                    acc = target.get(k)
+                    if not isinstance(acc, Accessor):
+                        acc = Accessor()
+                        target[k] = acc
+                    if kind == "get":
+                        acc.get = fn
+                    else:
+                        acc.set = fn
+        return cls
+
+    def init_fields(self, cls: JSClass, obj) -> None:
+        for k, value in cls.fields:
+            fenv = Env(cls.env)
+            fenv.declare("this", obj)
+            fenv.declare("%home", cls.proto)
+            self.put(obj, k, UNDEF if value is None else self.eval(value, fenv))
+
+    def construct_class(self, cls: JSClass, args, nt: JSClass):
+        parent = cls.parent
+        if parent is None:
+            obj = JSObject(proto=nt.proto)
+            self.init_fields(cls, obj)
+            if cls.ctor is not None:
+                r = self.call(cls.ctor, obj, args)
+                if isinstance(r, (JSObject, JSArray)):
+                    return r
+            return obj
+        made = []
+
+        def do_super(sargs, fenv):
+            if made:
+                raise _Throw(_error_obj("ReferenceError", "super constructor may only be called once"))
+            o = self.construct(parent, sargs, new_target=nt)
+            made.append(o)
+            if fenv is not None:
+                fenv.vars["this"] = o
+            self.init_fields(cls, o)
+            return UNDEF
+        if cls.ctor is None:
+            do_super(list(args), None)
+            return made[0]
+        r = self.call(cls.ctor, _TDZ, args, super_fn=do_super)
+        if isinstance(r, (JSObject, JSArray)):
+            return r
+        if not made:
+            raise _Throw(_error_obj("ReferenceError", "derived class constructor must call super()"))
+        return made[0]
+
+    def proto_get(self, proto, key: str, receiver):
+        """Property `key` found on a prototype chain starting at `proto` (accessors called on `receiver`)."""
+        depth = 0
+        while proto is not None and depth < 64:
+            v = proto.props.get(key, _MISSING)
+            if v is not _MISSING:
+                if isinstance(v, Accessor):
+                    return UNDEF if v.get is None else self.call(v.get, receiver, [])
+                return v
+            proto = proto.proto
+            depth += 1
+        return _MISSING
+
+    def proto_setter(self, proto, key: str):
+        depth = 0
+        while proto is not None and depth < 64:
+            v = proto.props.get(key, _MISSING)
+            if v is not _MISSING:
+                return v if isinstance(v, Accessor) else None
+            proto = proto.proto
+            depth += 1
+        return None
 
     # property access
     def get(self, obj, key):
@@ -1484,13 +1746,40 @@ class Interp:
                 return obj.items[idx] if idx < len(obj.items) else UNDEF
             return _array_method(self, obj, _to_str(key))
         if isinstance(obj, Host):
-            return obj.js_get(self, _to_str(key))
+            k = _to_str(key)
+            if obj.proto is not None and k not in obj.props:       # a class built on a host object
+                w = self.proto_get(obj.proto, k, obj)
+                if w is not _MISSING:
+                    return w
+            return obj.js_get(self, k)
         if isinstance(obj, JSObject):
             k = _to_str(key)
-            v = obj.props.get(k, UNDEF)
-            if v is UNDEF and k in _OBJECT_PROTO:
-                return _OBJECT_PROTO[k](self, obj)
+            v = obj.props.get(k, _MISSING)
+            if v is _MISSING:
+                if obj.proto is not None:
+                    v = self.proto_get(obj.proto, k, obj)
+                if v is _MISSING:
+                    return _OBJECT_PROTO[k](self, obj) if k in _OBJECT_PROTO else UNDEF
+            if isinstance(v, Accessor):
+                return UNDEF if v.get is None else self.call(v.get, obj, [])
             return v
+        if isinstance(obj, JSClass):
+            k = _to_str(key)
+            c = obj
+            while isinstance(c, JSClass):
+                if k in c.props:
+                    v = c.props[k]
+                    return self.call(v.get, obj, []) if isinstance(v, Accessor) and v.get else v
+                c = c.parent
+            if isinstance(c, (Native, JSFunction)) and k in c.props:
+                return c.props[k]
+            if k == "name":
+                return obj.name
+            if k == "prototype":
+                return obj.proto
+            if k in ("call", "apply", "bind"):
+                return _function_method(self, obj, k)
+            return UNDEF
         if isinstance(obj, str):
             idx = _index(key)
             if idx is not None:
@@ -1502,6 +1791,8 @@ class Interp:
             k = _to_str(key)
             if k in obj.props:
                 return obj.props[k]
+            if k == "prototype" and isinstance(obj, JSFunction) and not obj.arrow:
+                return self.fn_prototype(obj)
             if k == "name":
                 return obj.name or ""
             if k in ("call", "apply", "bind"):
@@ -1530,12 +1821,27 @@ class Interp:
                 return
             raise _Throw(_error_obj("TypeError", f"cannot set property {_to_str(key)} of an array"))
         if isinstance(obj, Host):
-            obj.js_set(self, _to_str(key), value)
+            k = _to_str(key)
+            if obj.proto is not None and k not in obj.props:
+                acc = self.proto_setter(obj.proto, k)
+                if acc is not None:
+                    if acc.set is not None:
+                        self.call(acc.set, obj, [value])
+                    return
+            obj.js_set(self, k, value)
             return
         if isinstance(obj, JSObject):
-            obj.props[_to_str(key)] = value
+            k = _to_str(key)
+            cur = obj.props.get(k, _MISSING)
+            if cur is _MISSING and obj.proto is not None:
+                cur = self.proto_setter(obj.proto, k) or _MISSING
+            if isinstance(cur, Accessor):
+                if cur.set is not None:
+                    self.call(cur.set, obj, [value])
+                return
+            obj.props[k] = value
             return
-        if isinstance(obj, (JSFunction, Native)):
+        if isinstance(obj, (JSFunction, Native, JSClass)):
             obj.props[_to_str(key)] = value
             return
         if obj is None or obj is UNDEF:
@@ -1560,6 +1866,10 @@ class Interp:
             return self.get(obj, self.member_key(e, env))
         if tag == "call":
             callee = e[1]
+            if callee[0] == "super_member":
+                this = self.eval(("this",), env)
+                f = self.super_get(self.member_super_key(callee, env), env, this)
+                return self.call(f, this, self.eval_args(e[2], env))
             if callee[0] == "member":
                 this = self.eval(callee[1], env)
                 if callee[3] and (this is None or this is UNDEF):
@@ -1642,6 +1952,18 @@ class Interp:
                         obj.props[k] = self.get(src, k)
                 elif p[0] == "shorthand_default":
                     raise JSError("SyntaxError", "invalid shorthand property initializer")
+                elif p[0] in ("get", "set"):
+                    key = p[1]
+                    k = _to_str(self.eval(key[1], env)) if isinstance(key, tuple) else key
+                    acc = obj.props.get(k)
+                    if not isinstance(acc, Accessor):
+                        acc = Accessor()
+                        obj.props[k] = acc
+                    fn = self.make_func(p[2], env)
+                    if p[0] == "get":
+                        acc.get = fn
+                    else:
+                        acc.set = fn
                 else:
                     key = p[1]
                     k = _to_str(self.eval(key[1], env)) if isinstance(key, tuple) else key
@@ -1652,6 +1974,16 @@ class Interp:
             return obj
         if tag == "func":
             return self.make_func(e, env)
+        if tag == "class":
+            return self.make_class(e, env)
+        if tag == "super_call":
+            sup = env.lookup("%super")
+            if sup is None:
+                raise JSError("SyntaxError", "'super' call outside a derived constructor")
+            return self.call(sup.vars["%super"], UNDEF, self.eval_args(e[1], env))
+        if tag == "super_member":
+            this = self.eval(("this",), env)
+            return self.super_get(self.member_super_key(e, env), env, this)
         if tag == "new":
             return self.construct(self.eval(e[1], env), self.eval_args(e[2], env))
         if tag == "tpl":
@@ -1666,10 +1998,32 @@ class Interp:
             return v
         if tag == "this":
             ev = env.lookup("this")
-            return ev.vars["this"] if ev is not None else UNDEF
+            if ev is None:
+                return UNDEF
+            v = ev.vars["this"]
+            if v is _TDZ:
+                raise _Throw(_error_obj("ReferenceError", "must call super constructor before accessing 'this'"))
+            return v
         if tag == "spread":
             raise JSError("SyntaxError", "unexpected spread")
         raise JSError("SyntaxError", f"unsupported expression {tag}")
+
+    def member_super_key(self, node, env):
+        k = node[1]
+        return _to_str(k[1] if k[0] == "lit" else self.eval(k, env))
+
+    def super_get(self, key: str, env, this):
+        h = env.lookup("%home")
+        if h is None:
+            raise JSError("SyntaxError", "'super' outside a method")
+        home = h.vars["%home"]
+        if isinstance(home, JSClass):                         # static method: the parent class's statics
+            return self.get(home.parent, key) if home.parent is not None else UNDEF
+        v = self.proto_get(home.proto, key, this) if home.proto is not None else _MISSING
+        if v is _MISSING:
+            # a host parent (e.g. THREE.Group): its own methods, not the subclass's overrides
+            return this.js_get(self, key) if isinstance(this, Host) else UNDEF
+        return v
 
     def eval_args(self, args, env):
         out = []
@@ -1774,6 +2128,15 @@ class Interp:
         if op == ">>>":
             return float((_to_int32(a) & 0xFFFFFFFF) >> (_to_int32(b) & 31))
         if op == "instanceof":
+            if isinstance(b, (JSClass, JSFunction)):
+                target = b.proto if isinstance(b, JSClass) else self.fn_prototype(b)
+                p = a.proto if isinstance(a, JSObject) else None
+                depth = 0
+                while p is not None and depth < 64:
+                    if p is target:
+                        return True
+                    p, depth = p.proto, depth + 1
+                return False
             if isinstance(b, Native) and isinstance(a, Host):
                 return a.is_instance(b.name)
             if isinstance(b, Native) and b.name == "Array":

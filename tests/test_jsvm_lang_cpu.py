@@ -1,0 +1,72 @@
+"""The module interpreter's JavaScript semantics: operator precedence, classes (extends, super, accessors, fields,
+statics, subclassing a three.js object), object-literal accessors, function prototypes and labeled loops."""
+import pytest
+
+from phung5_b200.app import jsvm
+
+
+def _ev(expr, pre=""):
+    src = ("export default function generate(THREE) { const g = new THREE.Group(); " + pre +
+           " g.userData.v = " + expr + "; return g; }")
+    r = jsvm.run_module(src, jsvm.Limits(steps=500_000, seconds=5))
+    assert r.error is None, r.error
+    return r.root.props["userData"].props["v"]
+
+
+@pytest.mark.parametrize("expr,want", [
+    ("2 + 1 * 100", 102), ("2 * 3 + 4 * 5", 26), ("1 + 2 * 3 + 4", 11), ("1 - 2 * 3 - 4", -9), ("10 - 2 - 3", 5),
+    ("8 / 2 / 2", 2), ("7 % 4 * 2", 6), ("2 ** 3 * 2", 16), ("2 ** 3 ** 2", 512), ("1 + 2 * 3 ** 2 / 3 - 1", 6),
+    ("(true ? 10 : 0) + 1 * 100", 110), ("1 << 2 + 1", 8), ("1 | 2 & 3 ^ 4", 7), ("3 > 2 > 1", False),
+    ("1 + 2 < 4 && 5 > 3 || false", True), ("null ?? 5 + 1", 6), ("-2 * 3 + 1", -5), ('typeof 1 + "x"', "numberx"),
+    ("0.5 * Math.PI * 2 - Math.PI", 0.0),
+])
+def test_operator_precedence(expr, want):
+    assert _ev(expr) == want
+
+
+def test_classes_extends_super_accessors_fields_and_statics():
+    pre = """
+      class A { constructor(x) { this.x = x; } f() { return this.x; } static make(x) { return new this(x); } }
+      class B extends A {
+        n = 2;
+        static k = 7;
+        constructor(x) { super(x + 1); this.y = this.n * 10; }
+        f() { return super.f() * 100 + this.y; }
+        get double() { return this.x * 2; }
+        set double(v) { this.x = v / 2; }
+      }
+      const b = new B(1);
+      b.double = 18;
+    """
+    assert _ev("b.f() + B.k", pre) == 927          # x 9 after the setter: 900 + 20 + 7
+    assert _ev("[b instanceof B, b instanceof A, B.make(4) instanceof B, b.double]", pre).items == [True, True,
+                                                                                                    True, 18.0]
+
+
+def test_subclass_of_a_three_object_keeps_host_methods_and_overrides():
+    pre = """
+      class Tree extends THREE.Group {
+        constructor(h) { super(); this.add(new THREE.Mesh(new THREE.CylinderGeometry(0.1, 0.1, h, 8),
+                                                           new THREE.MeshStandardMaterial())); }
+        add(o) { super.add(o); this.userData.n = (this.userData.n || 0) + 1; return this; }
+        trunk() { return this.children[0]; }
+      }
+      const t = new Tree(2);
+      t.add(new THREE.Mesh(new THREE.SphereGeometry(0.3), new THREE.MeshStandardMaterial()));
+      g.add(t);
+    """
+    assert _ev("[t instanceof THREE.Group, t instanceof Tree, t.children.length, t.userData.n, !!t.trunk()]",
+               pre).items == [True, True, 2.0, 2.0, True]
+
+
+def test_object_accessors_prototypes_labels_and_errors():
+    assert _ev("o.v", "const o = { _v: 1, get v() { return this._v * 2; }, set v(x) { this._v = x; } }; o.v = 3;") == 6
+    assert _ev("q.get() + (q instanceof P ? 10 : 0)",
+               "function P(x) { this.x = x; } P.prototype.get = function () { return this.x + 1; }; const q = new P(4);") == 15
+    assert _ev("n", "let n = 0; outer: for (let i = 0; i < 5; i++) { for (let j = 0; j < 5; j++) "
+                    "{ if (j == 3) continue outer; if (i == 4) break outer; n++; } }") == 12
+    r = jsvm.run_module("export default function generate(THREE) { class A {} class B extends A "
+                        "{ constructor() { this.x = 1; super(); } } new B(); }", jsvm.Limits(steps=10_000, seconds=2))
+    assert "before accessing 'this'" in r.error
+    r = jsvm.run_module("export default function generate(THREE) { class A {} A(); }", jsvm.Limits(steps=10_000, seconds=2))
+    assert "without 'new'" in r.error
