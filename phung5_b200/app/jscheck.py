@@ -22,43 +22,20 @@ from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
 from typing import Any, Dict, Iterable, List, Optional, Set
 
-from . import jsrepair, jsvm, threefix
+from . import jsrepair, jsvm, threefix, threespec
 
 LIMITS = {"vertices": 250_000, "drawCalls": 200, "depth": 32, "instances": 50_000, "textureBytes": 4 * 1_048_576}
 LITERAL_BUDGET = 50 * 1024
 ROOT_TYPES = {"Group", "Mesh", "LineSegments", "Points", "Object3D", "InstancedMesh", "Line"}
 
-ALLOWED_ROOTS = {"Math", "Number", "String", "Array", "Object", "Boolean", "Error", "Infinity", "NaN", "undefined",
-                 "parseInt", "parseFloat", "isFinite", "isNaN", "console", "Float32Array", "Float64Array",
-                 "Uint8Array", "Uint8ClampedArray", "Uint16Array", "Uint32Array", "Int8Array", "Int16Array",
-                 "Int32Array", "arguments", "this"}
-FORBIDDEN_IDENTIFIERS = {"eval", "Function", "setTimeout", "setInterval", "setImmediate", "queueMicrotask", "fetch",
-                         "XMLHttpRequest", "WebSocket", "document", "window", "navigator", "localStorage",
-                         "sessionStorage", "indexedDB", "OffscreenCanvas", "HTMLCanvasElement", "crypto", "Date",
-                         "performance", "Proxy", "Reflect", "WeakRef", "FinalizationRegistry", "SharedArrayBuffer",
-                         "Atomics", "Worker", "process", "module", "global", "globalThis", "require", "importScripts",
-                         "self", "Buffer"}
-FORBIDDEN_PROPERTIES = {"constructor", "__proto__", "prototype", "__defineGetter__", "__defineSetter__",
-                        "__lookupGetter__", "__lookupSetter__", "caller", "callee"}
-# THREE members the interpreter implements (everything else is UNKNOWN or, if a real three.js name that is
-# excluded on purpose, FORBIDDEN)
-THREE_DISALLOWED_KNOWN = {"AmbientLight", "DirectionalLight", "PointLight", "SpotLight", "HemisphereLight",
-                          "RectAreaLight", "PerspectiveCamera", "OrthographicCamera", "WebGLRenderer",
-                          "TextureLoader", "ObjectLoader", "FileLoader", "ImageLoader", "GLTFLoader", "Fog",
-                          "FogExp2", "ShaderMaterial", "RawShaderMaterial", "VideoTexture", "CubeTexture",
-                          "AnimationMixer", "Clock", "Raycaster", "Audio", "AudioListener", "SkinnedMesh",
-                          "Skeleton", "Bone", "LOD", "Sprite", "SpriteMaterial", "CanvasTexture", "Texture",
-                          "MeshDepthMaterial", "MeshDistanceMaterial", "ShadowMaterial", "Scene"}
-THREE_BLOCKED_SUBMEMBERS = {"MathUtils": {"generateUUID"}}
-
-
-def three_allowed() -> Set[str]:
-    it = jsvm.Interp()
-    names = set(jsvm.make_three(it).props.keys())
-    return names - THREE_DISALLOWED_KNOWN
-
-
-THREE_ALLOWED = three_allowed()
+# the output specification's tables (app/threespec.py); `arguments` is a function's implicit binding
+ALLOWED_ROOTS = set(threespec.ALLOWED_ROOT_IDENTIFIERS) | {"arguments"}
+FORBIDDEN_IDENTIFIERS = set(threespec.FORBIDDEN_IDENTIFIERS)
+FORBIDDEN_PROPERTIES = set(threespec.FORBIDDEN_PROPERTY_NAMES)
+COMPUTED_ACCESS_GATED = set(threespec.COMPUTED_ACCESS_GATED)
+THREE_DISALLOWED_KNOWN = set(threespec.THREE_DISALLOWED_KNOWN)
+THREE_BLOCKED_SUBMEMBERS = {k: set(v) for k, v in threespec.THREE_BLOCKED_SUBMEMBERS.items()}
+THREE_ALLOWED = set(threespec.THREE_ALLOWED)
 
 
 @dataclass
@@ -328,6 +305,9 @@ def static_analyze(prog) -> List[Dict[str, str]]:
             obj, key, computed = n[1], n[2], n[4]
             if key[0] == "lit" and isinstance(key[1], str) and key[1] in FORBIDDEN_PROPERTIES:
                 fail("FORBIDDEN_PROPERTY_ACCESS", f"`.{key[1]}` is not allowed")
+            if obj[0] == "ident" and computed and obj[1] != three and obj[1] in COMPUTED_ACCESS_GATED \
+                    and obj[1] not in declared:
+                fail("COMPUTED_PROPERTY_ACCESS", f"`{obj[1]}[...]` is not allowed")
             if obj[0] == "ident" and obj[1] == three:
                 if computed or key[0] != "lit":
                     fail("COMPUTED_PROPERTY_ACCESS", f"`{three}[...]` is not allowed")
@@ -335,8 +315,8 @@ def static_analyze(prog) -> List[Dict[str, str]]:
                     nm = str(key[1])
                     if nm not in THREE_ALLOWED:
                         if nm in THREE_DISALLOWED_KNOWN:
-                            fail("FORBIDDEN_THREE_API", f"THREE.{nm} is excluded (lights, cameras, loaders and "
-                                                        f"renderers belong to the renderer)")
+                            fail("FORBIDDEN_THREE_API", f"THREE.{nm} is a real three.js API that the output "
+                                                        f"specification excludes")
                         else:
                             fail("UNKNOWN_THREE_API", f"THREE.{nm} is not a supported three.js member")
                 _walk(key, visit)

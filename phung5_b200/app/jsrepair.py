@@ -12,6 +12,8 @@ planned on `jsvm.tokenize` tokens (so strings, comments and template text are ne
 - `paren`       PARSE_ERROR "unexpected token ')'": the first `)` that closes nothing is deleted.
 - `ident`       IDENTIFIER_NOT_ALLOWED `x`: if exactly one declared name equals x up to case and underscores
                 (`roundedPts` / `rounded_pts`), every reference to x is renamed to it.
+- `console`     IDENTIFIER_NOT_ALLOWED `console` (not a global the specification allows): every `console.x(...);`
+                statement is removed; a use of console anywhere but a statement of its own is not rewritten.
 - `retry`       EXECUTION_TIMEOUT on the wall-clock deadline only (not the step budget): checked once more, since
                 host load can push a module over the deadline.
 
@@ -25,7 +27,7 @@ from typing import Dict, Iterable, List, Optional, Set, Tuple
 
 from . import jsvm
 
-CLASSES = ("redeclared", "constlet", "paren", "ident", "retry")
+CLASSES = ("redeclared", "constlet", "paren", "ident", "console", "retry")
 
 _DUP = re.compile(r"Identifier '([A-Za-z_$][\w$]*)' has already been declared")
 _CONST = re.compile(r"assignment to constant variable ([A-Za-z_$][\w$]*)")
@@ -45,7 +47,8 @@ def plan(fails: Iterable[Dict[str, str]]) -> List[Tuple[str, str]]:
         elif rule == "EXECUTION_ERROR" and _CONST.search(detail):
             out.append(("constlet", _CONST.search(detail).group(1)))
         elif rule == "IDENTIFIER_NOT_ALLOWED" and _IDENT.search(detail):
-            out.append(("ident", _IDENT.search(detail).group(1)))
+            name = _IDENT.search(detail).group(1)
+            out.append(("console", name) if name == "console" else ("ident", name))
         elif rule == "EXECUTION_TIMEOUT" and "execution exceeded" in detail:
             out.append(("retry", ""))
         else:
@@ -143,6 +146,44 @@ def fix_paren(code: str) -> Optional[str]:
     return None
 
 
+def fix_console(code: str) -> Optional[str]:
+    toks = _tokens(code)
+    if toks is None:
+        return None
+    edits: List[Tuple[int, int, str]] = []
+    i = 0
+    while i < len(toks):
+        t = toks[i]
+        if t.kind == "id" and t.val == "console":
+            prev = toks[i - 1] if i > 0 else None
+            ok_start = prev is None or (prev.kind == "p" and prev.val in (";", "{", "}"))
+            if not (ok_start and i + 3 < len(toks) and toks[i + 1].val == "." and toks[i + 2].kind in ("id", "kw")
+                    and toks[i + 3].kind == "p" and toks[i + 3].val == "("):
+                return None
+            depth, j = 0, i + 3
+            while j < len(toks):
+                if toks[j].kind == "p" and toks[j].val == "(":
+                    depth += 1
+                elif toks[j].kind == "p" and toks[j].val == ")":
+                    depth -= 1
+                    if depth == 0:
+                        break
+                j += 1
+            if j >= len(toks):
+                return None
+            end = _tok_end(toks[j])
+            if j + 1 < len(toks) and toks[j + 1].kind == "p" and toks[j + 1].val == ";":
+                j += 1
+                end = _tok_end(toks[j])
+            elif j + 1 < len(toks) and not toks[j + 1].nl and not (toks[j + 1].kind == "p" and toks[j + 1].val == "}"):
+                return None                                   # something follows on the same line
+            edits.append((t.pos, end, ""))
+            i = j + 1
+            continue
+        i += 1
+    return _edit(code, edits) if edits else None
+
+
 def _norm(name: str) -> str:
     return name.replace("_", "").lower()
 
@@ -174,6 +215,8 @@ def apply(code: str, steps: List[Tuple[str, str]], declared: Set[str]) -> Option
             new = fix_paren(code)
         elif cls == "ident":
             new = fix_ident(code, subject, declared)
+        elif cls == "console":
+            new = fix_console(code)
         else:
             new = None
         if new is None:

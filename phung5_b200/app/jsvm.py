@@ -19,6 +19,7 @@ tables list, so no Python internals (`__class__`, builtins) are reachable from a
 """
 from __future__ import annotations
 
+import json
 import math
 import re
 import struct
@@ -2458,6 +2459,105 @@ def _install_globals(it: Interp):
     for cls in ("Float32Array", "Uint16Array", "Uint32Array", "Int32Array", "Uint8Array", "Float64Array", "Int16Array",
                 "Uint8ClampedArray", "Int8Array"):
         g.declare(cls, _typed_array_ctor(it, cls))
+    for kind in ("TypeError", "RangeError"):
+        g.declare(kind, Native(kind, fn=lambda i, t, x, _k=kind: _error_obj(_k, _to_str(_arg(x, 0, ""))),
+                               ctor=lambda i, x, _k=kind: _error_obj(_k, _to_str(_arg(x, 0, "")))))
+    for nm in ("BigInt", "ArrayBuffer", "DataView", "BigInt64Array", "BigUint64Array"):
+        def unsupported(i, *a, _n=nm):
+            raise _Throw(_error_obj("TypeError", f"{_n} is not supported by the module checker"))
+        g.declare(nm, Native(nm, fn=lambda i, t, x, _u=unsupported: _u(i), ctor=lambda i, x, _u=unsupported: _u(i)))
+    num = g.vars["Number"].props
+    num.update({
+        "parseInt": _nat("parseInt", lambda i, t, x: _parse_int(_to_str(_arg(x, 0)), _arg(x, 1))),
+        "isNaN": _nat("isNaN", lambda i, t, x: isinstance(_arg(x, 0), float) and x[0] != x[0]),
+        "isSafeInteger": _nat("isSafeInteger", lambda i, t, x: isinstance(_arg(x, 0), float) and math.isfinite(x[0])
+                              and x[0] == int(x[0]) and abs(x[0]) <= 2.0 ** 53 - 1),
+        "MIN_VALUE": 5e-324, "MIN_SAFE_INTEGER": -(2.0 ** 53 - 1)})
+    g.declare("JSON", JSObject({
+        "parse": _nat("parse", lambda i, t, x: _json_parse(_to_str(_arg(x, 0)))),
+        "stringify": _nat("stringify", lambda i, t, x: _json_stringify(it, _arg(x, 0), _arg(x, 2)))}))
+    g.declare("Map", Native("Map", ctor=lambda i, x: JSMap(it, _arg(x, 0))))
+    g.declare("Set", Native("Set", ctor=lambda i, x: JSSet(it, _arg(x, 0))))
+    counter = [0]
+
+    def symbol(i, t, x):
+        counter[0] += 1
+        return f"@@symbol({_to_str(_arg(x, 0, ''))})#{counter[0]}"
+    g.declare("Symbol", Native("Symbol", fn=symbol, props={"iterator": "@@iterator"}))
+
+
+def _json_parse(text: str):
+    try:
+        v = json.loads(text)
+    except (ValueError, RecursionError) as e:
+        raise _Throw(_error_obj("SyntaxError", f"JSON.parse: {str(e)[:80]}"))
+
+    def conv(o):
+        if isinstance(o, dict):
+            return JSObject({str(k): conv(w) for k, w in o.items()})
+        if isinstance(o, list):
+            return JSArray([conv(w) for w in o])
+        if isinstance(o, bool) or o is None or isinstance(o, str):
+            return o
+        return float(o)
+    return conv(v)
+
+
+def _json_stringify(it, v, indent):
+    seen = set()
+
+    def conv(o):
+        if o is None or isinstance(o, (bool, str)):
+            return o
+        if isinstance(o, (int, float)):
+            f = float(o)
+            return None if not math.isfinite(f) else (int(f) if f == int(f) and abs(f) < 2 ** 53 else f)
+        if isinstance(o, (JSFunction, Native, JSClass)) or o is UNDEF:
+            return _SKIP
+        if id(o) in seen:
+            raise _Throw(_error_obj("TypeError", "converting circular structure to JSON"))
+        seen.add(id(o))
+        try:
+            if isinstance(o, JSArray):
+                return [None if (c := conv(w)) is _SKIP else c for w in o.items]
+            if isinstance(o, Vec):
+                return {c: conv(w) for c, w in zip(o.comps, o.v())}
+            out = {}
+            for k in _own_keys(o):
+                c = conv(it.get(o, k))
+                if c is not _SKIP:
+                    out[k] = c
+            return out
+        finally:
+            seen.discard(id(o))
+    r = conv(v)
+    if r is _SKIP:
+        return UNDEF
+    ind = None
+    if isinstance(indent, float) and indent > 0:
+        ind = min(10, int(indent))
+    elif isinstance(indent, str) and indent:
+        ind = indent[:10]
+    return json.dumps(r, indent=ind, separators=None if ind else (",", ":"), ensure_ascii=False)
+
+
+_SKIP = object()
+
+
+def _mkey(v):
+    """SameValueZero key of a Map / Set entry."""
+    if isinstance(v, bool):
+        return ("b", v)
+    if isinstance(v, (int, float)):
+        f = float(v)
+        return ("nan",) if f != f else ("n", f + 0.0)
+    if isinstance(v, str):
+        return ("s", v)
+    if v is None:
+        return ("null",)
+    if v is UNDEF:
+        return ("undef",)
+    return ("o", id(v))
 
 
 def _typed_array_ctor(it, cls):
@@ -2631,11 +2731,76 @@ def _vec_methods():
         "applyMatrix4": lambda s, i, x: s.setv(_mat4_point(_arg(x, 0).m, s.v())),
         "rotateAround": lambda s, i, x: s.setv(_rot2(s.v(), _arg(x, 0).v(), _num_arg(x, 1))),
         "angle": lambda s, i, x: math.atan2(s.v()[1], s.v()[0]) % (2 * math.pi),
+        "setX": lambda s, i, x: _set_comp(s, 0, _num_arg(x, 0)),
+        "setY": lambda s, i, x: _set_comp(s, 1, _num_arg(x, 0)),
+        "setZ": lambda s, i, x: _set_comp(s, 2, _num_arg(x, 0)),
+        "setW": lambda s, i, x: _set_comp(s, 3, _num_arg(x, 0)),
+        "setComponent": lambda s, i, x: _set_comp(s, int(_num_arg(x, 0)), _num_arg(x, 1)),
+        "getComponent": lambda s, i, x: s.v()[int(_num_arg(x, 0))] if 0 <= int(_num_arg(x, 0)) < len(s.comps) else UNDEF,
+        "addScaledVector": lambda s, i, x: s.setv([a + b * _num_arg(x, 1) for a, b in zip(s.v(), other(x, s))]),
+        "distanceToSquared": lambda s, i, x: sum((a - b) ** 2 for a, b in zip(s.v(), other(x, s))),
+        "manhattanLength": lambda s, i, x: sum(abs(a) for a in s.v()),
+        "min": lambda s, i, x: s.setv([min(a, b) for a, b in zip(s.v(), other(x, s))]),
+        "max": lambda s, i, x: s.setv([max(a, b) for a, b in zip(s.v(), other(x, s))]),
+        "clamp": lambda s, i, x: s.setv([max(lo, min(hi, a)) for a, lo, hi in zip(s.v(), _arg(x, 0).v(), _arg(x, 1).v())]),
+        "clampScalar": lambda s, i, x: s.setv([max(_num_arg(x, 0), min(_num_arg(x, 1), a)) for a in s.v()]),
+        "floor": lambda s, i, x: s.setv([float(math.floor(a)) for a in s.v()]),
+        "ceil": lambda s, i, x: s.setv([float(math.ceil(a)) for a in s.v()]),
+        "round": lambda s, i, x: s.setv([float(math.floor(a + 0.5)) for a in s.v()]),
+        "applyQuaternion": lambda s, i, x: s.setv(_mat3_apply(_arg(x, 0).r, s.v())),
+        "applyMatrix3": lambda s, i, x: s.setv(_mat3_apply(_arg(x, 0).m, s.v()[:3])),
+        "transformDirection": lambda s, i, x: s.setv(_unit(_mat3_apply([r[:3] for r in _arg(x, 0).m[:3]], s.v()))),
+        "angleTo": lambda s, i, x: _angle_to(s.v(), other(x, s)),
+        "projectOnVector": lambda s, i, x: s.setv(_project(s.v(), other(x, s))),
+        "projectOnPlane": lambda s, i, x: s.setv([a - b for a, b in zip(s.v(), _project(s.v(), other(x, s)))]),
+        "reflect": lambda s, i, x: s.setv([a - 2 * sum(p * q for p, q in zip(s.v(), other(x, s))) * b
+                                          for a, b in zip(s.v(), other(x, s))]),
+        "setFromSpherical": lambda s, i, x: s.setv(_from_spherical(*_arg(x, 0).rpt())),
+        "setFromSphericalCoords": lambda s, i, x: s.setv(_from_spherical(_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2))),
+        "setFromCylindrical": lambda s, i, x: s.setv(_from_cylindrical(*_arg(x, 0).rty())),
+        "setFromCylindricalCoords": lambda s, i, x: s.setv(_from_cylindrical(_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2))),
+        "setFromMatrixPosition": lambda s, i, x: s.setv([_arg(x, 0).m[r][3] for r in range(3)]),
     }
 
 
 def it_items(v):
     return v.items if isinstance(v, JSArray) else []
+
+
+def _set_comp(s, k, val):
+    if 0 <= k < len(s.comps):
+        s.props[s.comps[k]] = float(val)
+    return s
+
+
+def _unit(v):
+    n = math.sqrt(sum(a * a for a in v)) or 1.0
+    return [a / n for a in v]
+
+
+def _angle_to(a, b):
+    den = math.sqrt(sum(x * x for x in a) * sum(y * y for y in b))
+    if den == 0:
+        return math.pi / 2
+    return math.acos(max(-1.0, min(1.0, sum(x * y for x, y in zip(a, b)) / den)))
+
+
+def _project(v, onto):
+    den = sum(x * x for x in onto)
+    if den == 0:
+        return [0.0] * len(v)
+    k = sum(x * y for x, y in zip(v, onto)) / den
+    return [k * x for x in onto]
+
+
+def _from_spherical(r, phi, theta):
+    """three.js spherical coordinates: polar angle phi from +y, azimuth theta around y from +z."""
+    sp = math.sin(phi) * r
+    return [sp * math.sin(theta), math.cos(phi) * r, sp * math.cos(theta)]
+
+
+def _from_cylindrical(r, theta, y):
+    return [r * math.sin(theta), y, r * math.cos(theta)]
 
 
 Vec.js_methods = _vec_methods()
@@ -3439,16 +3604,49 @@ class _HolesProxy(Host):
 
 
 class Curve(Host):
-    """CatmullRomCurve3 / LineCurve3 / QuadraticBezierCurve3 / CubicBezierCurve3: getPoint(t) in [0, 1]."""
-    __slots__ = ("kind_", "ctrl", "closed")
+    """getPoint(t), t in [0, 1], of the curve classes: 3D CatmullRomCurve3 / LineCurve3 / QuadraticBezierCurve3 /
+    CubicBezierCurve3; 2D EllipseCurve / ArcCurve / LineCurve / SplineCurve / QuadraticBezierCurve /
+    CubicBezierCurve (same formulas on two components); "custom" = THREE.Curve subclassed by the module (its own
+    getPoint is called); "path" = CurvePath (its curves in sequence, equal shares of t); "poly" = points sampled
+    from a custom curve (piecewise linear)."""
+    __slots__ = ("kind_", "ctrl", "closed", "dim", "interp", "params")
     cls_name = "Curve"
 
-    def __init__(self, kind, ctrl, closed=False):
+    def __init__(self, kind, ctrl, closed=False, dim=3, interp=None, params=None):
         super().__init__({})
-        self.kind_, self.ctrl, self.closed = kind, ctrl, closed
+        self.kind_, self.ctrl, self.closed, self.dim, self.interp = kind, ctrl, closed, dim, interp
+        self.params = params or {}
+        if kind == "path":
+            self.props["curves"] = JSArray(list(ctrl))
+
+    def vec(self, p):
+        return Vec(("x", "y", "z")[:self.dim], list(p)[:self.dim], "Vector3" if self.dim == 3 else "Vector2")
 
     def point(self, t):
         c = self.ctrl
+        if self.kind_ == "custom":
+            f = self.interp.get(self, "getPoint") if self.interp is not None else UNDEF
+            if not isinstance(f, (JSFunction, Native)) or isinstance(f, Native) and f.name == "getPoint":
+                raise _Throw(_error_obj("TypeError", "THREE.Curve subclass must implement getPoint(t)"))
+            r = self.interp.call(f, self, [float(t), self.vec([0.0] * self.dim)])
+            if not isinstance(r, Vec):
+                raise _Throw(_error_obj("TypeError", "getPoint must return a vector"))
+            return r.v()
+        if self.kind_ == "path":
+            curves = [k for k in it_items(self.props.get("curves")) if isinstance(k, Curve)]
+            if not curves:
+                return [0.0] * self.dim
+            f = min(max(t, 0.0), 1.0) * len(curves)
+            k = min(int(f), len(curves) - 1)
+            return curves[k].point(f - k)
+        if self.kind_ == "poly":
+            n = len(c) - 1
+            f = min(max(t, 0.0), 1.0) * n
+            k = min(int(f), max(n - 1, 0))
+            w = f - k
+            return [a + (b - a) * w for a, b in zip(c[k], c[min(k + 1, n)])]
+        if self.kind_ == "ellipse":
+            return _ellipse_point(self.params, t)
         if self.kind_ == "line":
             return [a + (b - a) * t for a, b in zip(c[0], c[1])]
         if self.kind_ == "quad":
@@ -3472,11 +3670,47 @@ class Curve(Host):
         return [0.5 * (2 * b + (-a + d) * w + (2 * a - 5 * b + 4 * d - e) * w * w + (-a + 3 * b - 3 * d + e) * w ** 3)
                 for a, b, d, e in zip(p0, p1, p2, p3)]
 
+    def points(self, n):
+        n = max(1, min(int(n), 4096))
+        return JSArray([self.vec(self.point(k / n)) for k in range(n + 1)])
+
     js_methods = {
-        "getPoint": lambda s, i, x: Vec(("x", "y", "z"), s.point(_num_arg(x, 0)), "Vector3"),
-        "getPoints": lambda s, i, x: JSArray([Vec(("x", "y", "z"), s.point(k / max(1, int(_num_arg(x, 0, 50.0)))), "Vector3")
-                                              for k in range(int(_num_arg(x, 0, 50.0)) + 1)]),
+        "getPoint": lambda s, i, x: s.vec(s.point(_num_arg(x, 0))),
+        "getPointAt": lambda s, i, x: s.vec(s.point(_num_arg(x, 0))),
+        "getPoints": lambda s, i, x: s.points(_num_arg(x, 0, 5.0 if s.kind_ in ("line", "line2") else 50.0)),
+        "getSpacedPoints": lambda s, i, x: s.points(_num_arg(x, 0, 5.0)),
+        "getLength": lambda s, i, x: _curve_length(s),
+        "add": lambda s, i, x: (s.props["curves"].items.append(_arg(x, 0)), UNDEF)[-1] if s.kind_ == "path" else UNDEF,
     }
+
+
+def _ellipse_point(p, t):
+    """A point of an ellipse arc (centre, radii, start / end angle, direction, rotation about the centre)."""
+    cx, cy, rx, ry = p["aX"], p["aY"], p["xRadius"], p["yRadius"]
+    a0, a1, cw, rot = p["aStartAngle"], p["aEndAngle"], p["aClockwise"], p["aRotation"]
+    two_pi = 2 * math.pi
+    delta = a1 - a0
+    same = abs(delta) < 1e-12
+    while delta < 0:
+        delta += two_pi
+    while delta > two_pi:
+        delta -= two_pi
+    if delta < 1e-12:
+        delta = 0.0 if same else two_pi
+    if cw and not same:
+        delta = -two_pi if delta == two_pi else delta - two_pi
+    ang = a0 + t * delta
+    x, y = cx + rx * math.cos(ang), cy + ry * math.sin(ang)
+    if rot:
+        c, s_ = math.cos(rot), math.sin(rot)
+        dx, dy = x - cx, y - cy
+        x, y = dx * c - dy * s_ + cx, dx * s_ + dy * c + cy
+    return [x, y]
+
+
+def _curve_length(c: "Curve", n: int = 200) -> float:
+    pts = [c.point(k / n) for k in range(n + 1)]
+    return sum(math.sqrt(sum((a - b) ** 2 for a, b in zip(p, q))) for p, q in zip(pts, pts[1:]))
 
 
 def _ctor(cls_name, build):
@@ -3492,6 +3726,11 @@ def _geom_ctor(gtype):
         for k, nm in enumerate(names):
             v = _arg(x, k)
             params[nm] = defaults[k] if v is UNDEF else (_to_num(v) if isinstance(v, (int, float, bool)) and not isinstance(v, bool) else v)
+        path = params.get("path")
+        if gtype == "TubeGeometry" and isinstance(path, Curve) and path.kind_ in ("custom", "path"):
+            n = max(1, min(int(_to_num(params.get("tubularSegments") or 64)), 256))
+            pts = [list(path.point(k / n)) + [0.0] * (3 - path.dim) for k in range(n + 1)]
+            params["path"] = Curve("poly", pts)
         return Geometry(gtype, params)
     return Native(gtype, ctor=build)
 
@@ -3536,8 +3775,39 @@ class Box3(Host):
     def empty(self):
         return any(a > b for a, b in zip(self.props["min"].v(), self.props["max"].v()))
 
+    def expand(self, p):
+        lo, hi = self.props["min"], self.props["max"]
+        lo.setv([min(a, b) for a, b in zip(lo.v(), p)])
+        hi.setv([max(a, b) for a, b in zip(hi.v(), p)])
+        return self
+
+    def set_pts(self, pts):
+        self.props["min"].setv([math.inf] * 3)
+        self.props["max"].setv([-math.inf] * 3)
+        for q in pts:
+            self.expand(q.v()[:3])
+        return self
+
+    def copy_from(self, o):
+        self.props["min"].setv(o.props["min"].v())
+        self.props["max"].setv(o.props["max"].v())
+        return self
+
     js_methods = {
         "setFromObject": lambda s, i, x: s.set_from(_arg(x, 0)),
+        "setFromPoints": lambda s, i, x: s.set_pts(it_items(_arg(x, 0))),
+        "set": lambda s, i, x: (s.props["min"].setv(_arg(x, 0).v()), s.props["max"].setv(_arg(x, 1).v()), s)[-1],
+        "expandByPoint": lambda s, i, x: s.expand(_arg(x, 0).v()),
+        "expandByScalar": lambda s, i, x: (s.props["min"].setv([a - _num_arg(x, 0) for a in s.props["min"].v()]),
+                                           s.props["max"].setv([a + _num_arg(x, 0) for a in s.props["max"].v()]), s)[-1],
+        "expandByObject": lambda s, i, x: s.expand(Box3().set_from(_arg(x, 0)).props["min"].v()).expand(
+            Box3().set_from(_arg(x, 0)).props["max"].v()) if not Box3().set_from(_arg(x, 0)).empty() else s,
+        "union": lambda s, i, x: s.expand(_arg(x, 0).props["min"].v()).expand(_arg(x, 0).props["max"].v()),
+        "containsPoint": lambda s, i, x: all(a <= p <= b for a, p, b in zip(s.props["min"].v(), _arg(x, 0).v(),
+                                                                             s.props["max"].v())),
+        "makeEmpty": lambda s, i, x: s.set_pts([]),
+        "clone": lambda s, i, x: Box3().copy_from(s),
+        "copy": lambda s, i, x: s.copy_from(_arg(x, 0)),
         "isEmpty": lambda s, i, x: s.empty(),
         "getCenter": lambda s, i, x: _arg(x, 0).setv([0.0] * 3 if s.empty() else
                                                      [(a + b) / 2 for a, b in zip(s.props["min"].v(), s.props["max"].v())]),
@@ -3561,7 +3831,7 @@ def make_three(it: Interp) -> JSObject:
     for m in mats:
         three[m] = Native(m, ctor=lambda i, x, _m=m: Material(_m, _arg(x, 0) if x else None))
     for cls in ("Float32BufferAttribute", "BufferAttribute", "Uint16BufferAttribute", "Uint32BufferAttribute",
-                "Int32BufferAttribute"):
+                "Int32BufferAttribute", "Uint8BufferAttribute", "Int8BufferAttribute", "Int16BufferAttribute"):
         three[cls] = Native(cls, ctor=lambda i, x: BufferAttribute(i.iterate(_arg(x, 0)) if isinstance(_arg(x, 0), JSArray)
                                                                    else [], _num_arg(x, 1, 3.0)))
     three["Group"] = Native("Group", ctor=lambda i, x: Object3D("Group"))
@@ -3589,6 +3859,7 @@ def make_three(it: Interp) -> JSObject:
         "cubic", [_arg(x, k).v() for k in range(4)]))
     for t in ("Texture", "CanvasTexture", "DataTexture"):
         three[t] = Native(t, ctor=lambda i, x: Texture(len(it_items(_arg(x, 0))) if x else 0))
+    _install_spec_members(it, three)
     for name, val in THREE_CONSTANTS.items():
         three[name] = val
     rnd = it.random
@@ -3622,7 +3893,7 @@ THREE_CONSTANTS = {
     "NoBlending": 0.0, "NormalBlending": 1.0, "AdditiveBlending": 2.0, "SubtractiveBlending": 3.0,
     "MultiplyBlending": 4.0,
     "StaticDrawUsage": 35044.0, "DynamicDrawUsage": 35048.0, "StreamDrawUsage": 35040.0,
-    "FlatShading": 1.0, "SmoothShading": 2.0,
+    "FlatShading": 1.0, "SmoothShading": 2.0, "LuminanceFormat": 1024.0,
 }
 
 
@@ -3949,3 +4220,543 @@ def to_scene_json(root: Object3D, max_depth: int = 64) -> dict:
     obj = node(root, 0)
     return {"metadata": {"version": 4.6, "type": "Object", "generator": "phung5_b200.app.jsvm"},
             "geometries": list(geoms.values()), "materials": list(mats.values()), "object": obj}
+
+
+# ------------------------------------------------------------------------------------------------------------
+# the rest of the specification's THREE members: math helpers, 2D / custom curves and paths, polyhedra, edge and
+# wireframe geometries, more attribute types and interleaved buffers
+# ------------------------------------------------------------------------------------------------------------
+
+def _v3(vals=(0.0, 0.0, 0.0)):
+    return Vec(("x", "y", "z"), list(vals), "Vector3")
+
+
+def _v2(vals=(0.0, 0.0)):
+    return Vec(("x", "y"), list(vals), "Vector2")
+
+
+def _vec_or(x, k, dim=3):
+    v = _arg(x, k)
+    return v.v()[:dim] if isinstance(v, Vec) else [0.0] * dim
+
+
+def _target(x, k, dim=3):
+    t = _arg(x, k)
+    return t if isinstance(t, Vec) else (_v3() if dim == 3 else _v2())
+
+
+class _Shape3(Host):
+    """A math object whose state is a few vector / number properties (Sphere, Plane, Ray, Line3, Triangle, Box2,
+    Spherical, Cylindrical); `fields` lists them for clone / copy."""
+    __slots__ = ("kind",)
+    fields: Tuple[str, ...] = ()
+
+    def __init__(self, kind, props):
+        super().__init__(dict(props, **{"is" + kind: True}))
+        self.kind = kind
+
+    @property
+    def cls_name(self):
+        return self.kind
+
+    def is_instance(self, name):
+        return name == self.kind
+
+    def clone_(self):
+        return type(self)(**{f: (self.props[f].v() if isinstance(self.props[f], Vec) else self.props[f])
+                             for f in self.fields})
+
+    def copy_(self, o):
+        for f in self.fields:
+            if isinstance(self.props[f], Vec):
+                self.props[f].setv(o.props[f].v())
+            else:
+                self.props[f] = o.props[f]
+        return self
+
+
+class Sphere(_Shape3):
+    fields = ("center", "radius")
+
+    def __init__(self, center=(0.0, 0.0, 0.0), radius=-1.0):
+        super().__init__("Sphere", {"center": _v3(center), "radius": float(radius)})
+
+    def from_points(self, pts):
+        vs = [p.v() for p in pts if isinstance(p, Vec)]
+        if not vs:
+            return self
+        c = [(min(a) + max(a)) / 2 for a in zip(*vs)]
+        self.props["center"].setv(c)
+        self.props["radius"] = max(math.dist(c, v) for v in vs)
+        return self
+
+    js_methods = {
+        "set": lambda s, i, x: (s.props["center"].setv(_vec_or(x, 0)), s.props.__setitem__("radius", _num_arg(x, 1)), s)[-1],
+        "setFromPoints": lambda s, i, x: s.from_points(it_items(_arg(x, 0))),
+        "clone": lambda s, i, x: s.clone_(),
+        "copy": lambda s, i, x: s.copy_(_arg(x, 0)),
+        "isEmpty": lambda s, i, x: _to_num(s.props["radius"]) < 0,
+        "containsPoint": lambda s, i, x: math.dist(_vec_or(x, 0), s.props["center"].v()) <= _to_num(s.props["radius"]),
+        "distanceToPoint": lambda s, i, x: math.dist(_vec_or(x, 0), s.props["center"].v()) - _to_num(s.props["radius"]),
+        "translate": lambda s, i, x: (s.props["center"].setv([a + b for a, b in zip(s.props["center"].v(), _vec_or(x, 0))]), s)[-1],
+    }
+
+
+class Plane(_Shape3):
+    fields = ("normal", "constant")
+
+    def __init__(self, normal=(1.0, 0.0, 0.0), constant=0.0):
+        super().__init__("Plane", {"normal": _v3(normal), "constant": float(constant)})
+
+    def dist(self, p):
+        return sum(a * b for a, b in zip(self.props["normal"].v(), p)) + _to_num(self.props["constant"])
+
+    def from_coplanar(self, a, b, c):
+        n = _unit(_cross([q - p for p, q in zip(b, c)], [q - p for p, q in zip(b, a)]))
+        self.props["normal"].setv(n)
+        self.props["constant"] = -sum(x * y for x, y in zip(a, n))
+        return self
+
+    js_methods = {
+        "set": lambda s, i, x: (s.props["normal"].setv(_vec_or(x, 0)), s.props.__setitem__("constant", _num_arg(x, 1)), s)[-1],
+        "setComponents": lambda s, i, x: (s.props["normal"].setv([_num_arg(x, k) for k in range(3)]),
+                                          s.props.__setitem__("constant", _num_arg(x, 3)), s)[-1],
+        "setFromNormalAndCoplanarPoint": lambda s, i, x: (s.props["normal"].setv(_vec_or(x, 0)), s.props.__setitem__(
+            "constant", -sum(a * b for a, b in zip(_vec_or(x, 1), _vec_or(x, 0)))), s)[-1],
+        "setFromCoplanarPoints": lambda s, i, x: s.from_coplanar(_vec_or(x, 0), _vec_or(x, 1), _vec_or(x, 2)),
+        "normalize": lambda s, i, x: (lambda n: (s.props["normal"].setv([a / n for a in s.props["normal"].v()]),
+                                                 s.props.__setitem__("constant", _to_num(s.props["constant"]) / n), s)[-1])(
+            math.sqrt(sum(a * a for a in s.props["normal"].v())) or 1.0),
+        "negate": lambda s, i, x: (s.props["normal"].setv([-a for a in s.props["normal"].v()]),
+                                   s.props.__setitem__("constant", -_to_num(s.props["constant"])), s)[-1],
+        "distanceToPoint": lambda s, i, x: s.dist(_vec_or(x, 0)),
+        "projectPoint": lambda s, i, x: _target(x, 1).setv([p - s.dist(_vec_or(x, 0)) * n for p, n in zip(
+            _vec_or(x, 0), s.props["normal"].v())]),
+        "clone": lambda s, i, x: s.clone_(),
+        "copy": lambda s, i, x: s.copy_(_arg(x, 0)),
+    }
+
+
+class Ray(_Shape3):
+    fields = ("origin", "direction")
+
+    def __init__(self, origin=(0.0, 0.0, 0.0), direction=(0.0, 0.0, -1.0)):
+        super().__init__("Ray", {"origin": _v3(origin), "direction": _v3(direction)})
+
+    js_methods = {
+        "set": lambda s, i, x: (s.props["origin"].setv(_vec_or(x, 0)), s.props["direction"].setv(_vec_or(x, 1)), s)[-1],
+        "at": lambda s, i, x: _target(x, 1).setv([o + d * _num_arg(x, 0) for o, d in zip(
+            s.props["origin"].v(), s.props["direction"].v())]),
+        "clone": lambda s, i, x: s.clone_(),
+        "copy": lambda s, i, x: s.copy_(_arg(x, 0)),
+    }
+
+
+class Line3(_Shape3):
+    fields = ("start", "end")
+
+    def __init__(self, start=(0.0, 0.0, 0.0), end=(0.0, 0.0, 0.0)):
+        super().__init__("Line3", {"start": _v3(start), "end": _v3(end)})
+
+    def ab(self):
+        return self.props["start"].v(), self.props["end"].v()
+
+    js_methods = {
+        "set": lambda s, i, x: (s.props["start"].setv(_vec_or(x, 0)), s.props["end"].setv(_vec_or(x, 1)), s)[-1],
+        "getCenter": lambda s, i, x: _target(x, 0).setv([(a + b) / 2 for a, b in zip(*s.ab())]),
+        "delta": lambda s, i, x: _target(x, 0).setv([b - a for a, b in zip(*s.ab())]),
+        "distance": lambda s, i, x: math.dist(*s.ab()),
+        "distanceSq": lambda s, i, x: math.dist(*s.ab()) ** 2,
+        "at": lambda s, i, x: _target(x, 1).setv([a + (b - a) * _num_arg(x, 0) for a, b in zip(*s.ab())]),
+        "clone": lambda s, i, x: s.clone_(),
+        "copy": lambda s, i, x: s.copy_(_arg(x, 0)),
+    }
+
+
+class Triangle(_Shape3):
+    fields = ("a", "b", "c")
+
+    def __init__(self, a=(0.0, 0.0, 0.0), b=(0.0, 0.0, 0.0), c=(0.0, 0.0, 0.0)):
+        super().__init__("Triangle", {"a": _v3(a), "b": _v3(b), "c": _v3(c)})
+
+    def abc(self):
+        return self.props["a"].v(), self.props["b"].v(), self.props["c"].v()
+
+    def normal_(self):
+        a, b, c = self.abc()
+        return _cross([q - p for p, q in zip(b, c)], [q - p for p, q in zip(b, a)])
+
+    js_methods = {
+        "set": lambda s, i, x: (s.props["a"].setv(_vec_or(x, 0)), s.props["b"].setv(_vec_or(x, 1)),
+                                s.props["c"].setv(_vec_or(x, 2)), s)[-1],
+        "getNormal": lambda s, i, x: _target(x, 0).setv(_unit(s.normal_())),
+        "getArea": lambda s, i, x: 0.5 * math.sqrt(sum(a * a for a in s.normal_())),
+        "getMidpoint": lambda s, i, x: _target(x, 0).setv([sum(t) / 3 for t in zip(*s.abc())]),
+        "clone": lambda s, i, x: s.clone_(),
+        "copy": lambda s, i, x: s.copy_(_arg(x, 0)),
+    }
+
+
+class Box2(_Shape3):
+    fields = ("min", "max")
+
+    def __init__(self, min=(math.inf, math.inf), max=(-math.inf, -math.inf)):
+        super().__init__("Box2", {"min": _v2(min), "max": _v2(max)})
+
+    def expand(self, p):
+        lo, hi = self.props["min"], self.props["max"]
+        lo.setv([_mn(a, b) for a, b in zip(lo.v(), p)])
+        hi.setv([_mx(a, b) for a, b in zip(hi.v(), p)])
+        return self
+
+    def empty(self):
+        return any(a > b for a, b in zip(self.props["min"].v(), self.props["max"].v()))
+
+    js_methods = {
+        "set": lambda s, i, x: (s.props["min"].setv(_vec_or(x, 0, 2)), s.props["max"].setv(_vec_or(x, 1, 2)), s)[-1],
+        "setFromPoints": lambda s, i, x: (s.props["min"].setv([math.inf] * 2), s.props["max"].setv([-math.inf] * 2),
+                                          [s.expand(p.v()[:2]) for p in it_items(_arg(x, 0))], s)[-1],
+        "expandByPoint": lambda s, i, x: s.expand(_vec_or(x, 0, 2)),
+        "makeEmpty": lambda s, i, x: (s.props["min"].setv([math.inf] * 2), s.props["max"].setv([-math.inf] * 2), s)[-1],
+        "isEmpty": lambda s, i, x: s.empty(),
+        "getSize": lambda s, i, x: _target(x, 0, 2).setv([0.0, 0.0] if s.empty() else
+                                                         [b - a for a, b in zip(s.props["min"].v(), s.props["max"].v())]),
+        "getCenter": lambda s, i, x: _target(x, 0, 2).setv([0.0, 0.0] if s.empty() else
+                                                           [(a + b) / 2 for a, b in zip(s.props["min"].v(), s.props["max"].v())]),
+        "containsPoint": lambda s, i, x: all(a <= p <= b for a, p, b in zip(s.props["min"].v(), _vec_or(x, 0, 2),
+                                                                             s.props["max"].v())),
+        "clone": lambda s, i, x: s.clone_(),
+        "copy": lambda s, i, x: s.copy_(_arg(x, 0)),
+    }
+
+
+def _mn(a, b):
+    return a if a < b else b
+
+
+def _mx(a, b):
+    return a if a > b else b
+
+
+class Spherical(_Shape3):
+    fields = ("radius", "phi", "theta")
+
+    def __init__(self, radius=1.0, phi=0.0, theta=0.0):
+        super().__init__("Spherical", {"radius": float(radius), "phi": float(phi), "theta": float(theta)})
+
+    def rpt(self):
+        return _to_num(self.props["radius"]), _to_num(self.props["phi"]), _to_num(self.props["theta"])
+
+    def from_xyz(self, x, y, z):
+        r = math.sqrt(x * x + y * y + z * z)
+        self.props["radius"] = r
+        self.props["theta"] = math.atan2(x, z) if r else 0.0
+        self.props["phi"] = math.acos(max(-1.0, min(1.0, y / r))) if r else 0.0
+        return self
+
+    js_methods = {
+        "set": lambda s, i, x: (s.props.update(radius=_num_arg(x, 0), phi=_num_arg(x, 1), theta=_num_arg(x, 2)), s)[-1],
+        "setFromVector3": lambda s, i, x: s.from_xyz(*_vec_or(x, 0)),
+        "setFromCartesianCoords": lambda s, i, x: s.from_xyz(_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2)),
+        "makeSafe": lambda s, i, x: (s.props.__setitem__("phi", max(1e-6, min(math.pi - 1e-6, _to_num(s.props["phi"])))), s)[-1],
+        "clone": lambda s, i, x: s.clone_(),
+        "copy": lambda s, i, x: s.copy_(_arg(x, 0)),
+    }
+
+
+class Cylindrical(_Shape3):
+    fields = ("radius", "theta", "y")
+
+    def __init__(self, radius=1.0, theta=0.0, y=0.0):
+        super().__init__("Cylindrical", {"radius": float(radius), "theta": float(theta), "y": float(y)})
+
+    def rty(self):
+        return _to_num(self.props["radius"]), _to_num(self.props["theta"]), _to_num(self.props["y"])
+
+    def from_xyz(self, x, y, z):
+        self.props.update(radius=math.sqrt(x * x + z * z), theta=math.atan2(x, z), y=float(y))
+        return self
+
+    js_methods = {
+        "set": lambda s, i, x: (s.props.update(radius=_num_arg(x, 0), theta=_num_arg(x, 1), y=_num_arg(x, 2)), s)[-1],
+        "setFromVector3": lambda s, i, x: s.from_xyz(*_vec_or(x, 0)),
+        "setFromCartesianCoords": lambda s, i, x: s.from_xyz(_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2)),
+        "clone": lambda s, i, x: s.clone_(),
+        "copy": lambda s, i, x: s.copy_(_arg(x, 0)),
+    }
+
+
+class Matrix3(Host):
+    __slots__ = ("m",)
+    cls_name = "Matrix3"
+
+    def __init__(self, m=None):
+        super().__init__({"isMatrix3": True})
+        self.m = m or [[1.0, 0.0, 0.0], [0.0, 1.0, 0.0], [0.0, 0.0, 1.0]]
+
+    def get_special(self, it, key):
+        if key == "elements":
+            return JSArray([self.m[r][c] for c in range(3) for r in range(3)])
+        return super().get_special(it, key)
+
+    def put(self, m):
+        self.m = [list(map(float, row)) for row in m]
+        return self
+
+    def det(self):
+        m = self.m
+        return (m[0][0] * (m[1][1] * m[2][2] - m[1][2] * m[2][1]) - m[0][1] * (m[1][0] * m[2][2] - m[1][2] * m[2][0]) +
+                m[0][2] * (m[1][0] * m[2][1] - m[1][1] * m[2][0]))
+
+    def inv(self):
+        d = self.det()
+        if d == 0:
+            return self.put([[0.0] * 3 for _ in range(3)])
+        m = self.m
+        cof = [[(m[(r + 1) % 3][(c + 1) % 3] * m[(r + 2) % 3][(c + 2) % 3] -
+                 m[(r + 1) % 3][(c + 2) % 3] * m[(r + 2) % 3][(c + 1) % 3]) for c in range(3)] for r in range(3)]
+        return self.put([[cof[c][r] / d for c in range(3)] for r in range(3)])
+
+    js_methods = {
+        "set": lambda s, i, x: s.put([[_num_arg(x, 3 * r + c) for c in range(3)] for r in range(3)]),
+        "identity": lambda s, i, x: s.put([[1.0 if r == c else 0.0 for c in range(3)] for r in range(3)]),
+        "copy": lambda s, i, x: s.put(_arg(x, 0).m),
+        "clone": lambda s, i, x: Matrix3([row[:] for row in s.m]),
+        "multiply": lambda s, i, x: s.put(_mat_mul(s.m, _arg(x, 0).m)),
+        "premultiply": lambda s, i, x: s.put(_mat_mul(_arg(x, 0).m, s.m)),
+        "multiplyMatrices": lambda s, i, x: s.put(_mat_mul(_arg(x, 0).m, _arg(x, 1).m)),
+        "multiplyScalar": lambda s, i, x: s.put([[a * _num_arg(x, 0) for a in row] for row in s.m]),
+        "determinant": lambda s, i, x: s.det(),
+        "invert": lambda s, i, x: s.inv(),
+        "transpose": lambda s, i, x: s.put([list(col) for col in zip(*s.m)]),
+        "setFromMatrix4": lambda s, i, x: s.put([row[:3] for row in _arg(x, 0).m[:3]]),
+        "makeRotation": lambda s, i, x: s.put([[math.cos(_num_arg(x, 0)), -math.sin(_num_arg(x, 0)), 0.0],
+                                               [math.sin(_num_arg(x, 0)), math.cos(_num_arg(x, 0)), 0.0],
+                                               [0.0, 0.0, 1.0]]),
+        "makeScale": lambda s, i, x: s.put([[_num_arg(x, 0), 0.0, 0.0], [0.0, _num_arg(x, 1), 0.0], [0.0, 0.0, 1.0]]),
+        "makeTranslation": lambda s, i, x: s.put([[1.0, 0.0, _num_arg(x, 0)], [0.0, 1.0, _num_arg(x, 1)],
+                                                  [0.0, 0.0, 1.0]]),
+        "toArray": lambda s, i, x: JSArray([s.m[r][c] for c in range(3) for r in range(3)]),
+        "fromArray": lambda s, i, x: s.put([[_to_num(it_items(_arg(x, 0))[3 * c + r]) for c in range(3)]
+                                            for r in range(3)]),
+    }
+
+
+class InterleavedBuffer(Host):
+    __slots__ = ("array", "stride")
+    cls_name = "InterleavedBuffer"
+
+    def __init__(self, array, stride):
+        super().__init__({"isInterleavedBuffer": True, "stride": float(stride)})
+        self.array, self.stride = [float(_to_num(a)) for a in array], max(1, int(stride))
+
+    def get_special(self, it, key):
+        if key == "count":
+            return float(len(self.array) // self.stride)
+        if key == "array":
+            return JSArray(list(self.array))
+        return super().get_special(it, key)
+
+
+def _interleaved_attr(x):
+    """An attribute view of an interleaved buffer, copied out into a plain attribute (edits do not write back)."""
+    ib, item, off = _arg(x, 0), max(1, int(_num_arg(x, 1, 3.0))), int(_num_arg(x, 2, 0.0))
+    if not isinstance(ib, InterleavedBuffer):
+        raise _Throw(_error_obj("TypeError", "InterleavedBufferAttribute needs an InterleavedBuffer"))
+    n = len(ib.array) // ib.stride
+    return BufferAttribute([ib.array[r * ib.stride + off + k] for r in range(n) for k in range(item)
+                            if r * ib.stride + off + k < len(ib.array)], item)
+
+
+def _baked(gtype, verts, faces=None, params=None):
+    g = Geometry(gtype, params or {})
+    g.buffer["position"] = BufferAttribute([float(c) for v in verts for c in v], 3)
+    if faces is not None:
+        g.buffer["__index"] = BufferAttribute([float(i) for f in faces for i in f], 1)
+    g.baked = True
+    return g
+
+
+def _polyhedron(x):
+    """PolyhedronGeometry(vertices, indices, radius, detail): every face split into (detail + 1)^2 triangles,
+    every vertex pushed out to the sphere of the radius."""
+    vs = [float(_to_num(a)) for a in it_items(_arg(x, 0))]
+    ids = [int(_to_num(a)) for a in it_items(_arg(x, 1))]
+    radius, detail = _num_arg(x, 2, 1.0), max(0, min(int(_num_arg(x, 3, 0.0)), 6))
+    pts = [vs[k:k + 3] for k in range(0, len(vs) - 2, 3)]
+    verts, faces = [], []
+    for f in range(0, len(ids) - 2, 3):
+        try:
+            a, b, c = (pts[ids[f + j]] for j in range(3))
+        except IndexError:
+            raise _Throw(_error_obj("RangeError", "PolyhedronGeometry index out of range"))
+        n = detail + 1
+        grid = {}
+        for r in range(n + 1):
+            for k in range(n + 1 - r):
+                w_b, w_c = r / n, k / n
+                p = [a[j] + (b[j] - a[j]) * w_b + (c[j] - a[j]) * w_c for j in range(3)]
+                grid[(r, k)] = len(verts)
+                verts.append([q * radius for q in _unit(p)])
+        for r in range(n):
+            for k in range(n - r):
+                faces.append((grid[(r, k)], grid[(r + 1, k)], grid[(r, k + 1)]))
+                if k + 1 <= n - r - 1:
+                    faces.append((grid[(r + 1, k)], grid[(r + 1, k + 1)], grid[(r, k + 1)]))
+    return _baked("PolyhedronGeometry", verts, faces, {"radius": radius, "detail": float(detail)})
+
+
+def _edge_segments(geom, threshold_deg=None):
+    """Line segments of a geometry's triangle edges: every edge (wireframe), or only edges whose two faces bend by
+    more than `threshold_deg` plus open edges (EdgesGeometry). Vertices are merged by position first."""
+    if not isinstance(geom, Geometry):
+        raise _Throw(_error_obj("TypeError", "expected a geometry"))
+    v, f = geometry_mesh(geom)
+    key = {}
+    remap = []
+    for p in v.tolist():
+        k = tuple(round(c, 5) for c in p)
+        remap.append(key.setdefault(k, len(key)))
+    pos = list(key.keys())
+    edges = {}
+    for tri in f.tolist():
+        a, b, c = (remap[t] for t in tri)
+        n = _cross([q - p for p, q in zip(pos[a], pos[b])], [q - p for p, q in zip(pos[a], pos[c])])
+        if sum(t * t for t in n) == 0:
+            continue
+        n = _unit(n)
+        for e in ((a, b), (b, c), (c, a)):
+            edges.setdefault(tuple(sorted(e)), []).append(n)
+    out = []
+    cos_t = None if threshold_deg is None else math.cos(math.radians(threshold_deg))
+    for (a, b), ns in edges.items():
+        if cos_t is None or len(ns) == 1 or sum(p * q for p, q in zip(ns[0], ns[1])) <= cos_t:
+            out += [pos[a], pos[b]]
+    return out
+
+
+def _install_spec_members(it: "Interp", three: Dict[str, Any]) -> None:
+    three["Vector4"] = _vec_ctor("Vector4", ("x", "y", "z", "w"))
+    three["Matrix3"] = Native("Matrix3", ctor=lambda i, x: Matrix3())
+    three["Box2"] = Native("Box2", ctor=lambda i, x: Box2(_vec_or(x, 0, 2) if x else (math.inf,) * 2,
+                                                          _vec_or(x, 1, 2) if len(x) > 1 else (-math.inf,) * 2))
+    three["Sphere"] = Native("Sphere", ctor=lambda i, x: Sphere(_vec_or(x, 0), _num_arg(x, 1, -1.0)))
+    three["Plane"] = Native("Plane", ctor=lambda i, x: Plane(_vec_or(x, 0) if x else (1.0, 0.0, 0.0), _num_arg(x, 1)))
+    three["Ray"] = Native("Ray", ctor=lambda i, x: Ray(_vec_or(x, 0), _vec_or(x, 1) if len(x) > 1 else (0.0, 0.0, -1.0)))
+    three["Line3"] = Native("Line3", ctor=lambda i, x: Line3(_vec_or(x, 0), _vec_or(x, 1)))
+    three["Triangle"] = Native("Triangle", ctor=lambda i, x: Triangle(_vec_or(x, 0), _vec_or(x, 1), _vec_or(x, 2)))
+    three["Spherical"] = Native("Spherical", ctor=lambda i, x: Spherical(_num_arg(x, 0, 1.0), _num_arg(x, 1), _num_arg(x, 2)))
+    three["Cylindrical"] = Native("Cylindrical", ctor=lambda i, x: Cylindrical(_num_arg(x, 0, 1.0), _num_arg(x, 1),
+                                                                               _num_arg(x, 2)))
+    three["Curve"] = Native("Curve", ctor=lambda i, x: Curve("custom", [], interp=it))
+    three["CurvePath"] = Native("CurvePath", ctor=lambda i, x: Curve("path", [], interp=it))
+
+    def ellipse(x, arc=False):
+        if arc:                     # ArcCurve(aX, aY, aRadius, aStartAngle, aEndAngle, aClockwise)
+            names = ("aX", "aY", "xRadius", "aStartAngle", "aEndAngle", "aClockwise")
+            d = {n: _arg(x, k) for k, n in enumerate(names)}
+            d["yRadius"] = d["xRadius"]
+            d["aRotation"] = 0.0
+        else:
+            names = ("aX", "aY", "xRadius", "yRadius", "aStartAngle", "aEndAngle", "aClockwise", "aRotation")
+            d = {n: _arg(x, k) for k, n in enumerate(names)}
+        defaults = {"aX": 0.0, "aY": 0.0, "xRadius": 1.0, "yRadius": 1.0, "aStartAngle": 0.0,
+                    "aEndAngle": 2 * math.pi, "aClockwise": False, "aRotation": 0.0}
+        p = {k: (defaults[k] if v is UNDEF else (_truthy(v) if k == "aClockwise" else _to_num(v))) for k, v in d.items()}
+        return Curve("ellipse", [], dim=2, params=p)
+    three["EllipseCurve"] = Native("EllipseCurve", ctor=lambda i, x: ellipse(x))
+    three["ArcCurve"] = Native("ArcCurve", ctor=lambda i, x: ellipse(x, arc=True))
+    three["LineCurve"] = Native("LineCurve", ctor=lambda i, x: Curve("line", [_vec_or(x, 0, 2), _vec_or(x, 1, 2)], dim=2))
+    three["QuadraticBezierCurve"] = Native("QuadraticBezierCurve", ctor=lambda i, x: Curve(
+        "quad", [_vec_or(x, k, 2) for k in range(3)], dim=2))
+    three["CubicBezierCurve"] = Native("CubicBezierCurve", ctor=lambda i, x: Curve(
+        "cubic", [_vec_or(x, k, 2) for k in range(4)], dim=2))
+    three["SplineCurve"] = Native("SplineCurve", ctor=lambda i, x: Curve(
+        "catmull", [p.v()[:2] for p in it_items(_arg(x, 0)) if isinstance(p, Vec)] or [[0.0, 0.0]], dim=2))
+    three["PolyhedronGeometry"] = Native("PolyhedronGeometry", ctor=lambda i, x: _polyhedron(x))
+    three["EdgesGeometry"] = Native("EdgesGeometry", ctor=lambda i, x: _baked(
+        "EdgesGeometry", _edge_segments(_arg(x, 0), _num_arg(x, 1, 1.0))))
+    three["WireframeGeometry"] = Native("WireframeGeometry", ctor=lambda i, x: _baked(
+        "WireframeGeometry", _edge_segments(_arg(x, 0))))
+    three["InterleavedBuffer"] = Native("InterleavedBuffer", ctor=lambda i, x: InterleavedBuffer(
+        i.iterate(_arg(x, 0)) if isinstance(_arg(x, 0), JSArray) else [], _num_arg(x, 1, 3.0)))
+    three["InterleavedBufferAttribute"] = Native("InterleavedBufferAttribute", ctor=lambda i, x: _interleaved_attr(x))
+
+
+class JSMap(Host):
+    __slots__ = ("d",)
+    cls_name = "Map"
+
+    def __init__(self, it, src=UNDEF):
+        super().__init__({})
+        self.d: Dict[Any, Tuple[Any, Any]] = {}
+        if src is not UNDEF and src is not None:
+            for e in it.iterate(src):
+                self.d[_mkey(it.get(e, 0.0))] = (it.get(e, 0.0), it.get(e, 1.0))
+
+    def get_special(self, it, key):
+        if key == "size":
+            return float(len(self.d))
+        return super().get_special(it, key)
+
+    def iterable(self):
+        return [JSArray([k, v]) for k, v in self.d.values()]
+
+    def own_keys(self):
+        return []
+
+    def _each(self, it, f):
+        for k, v in list(self.d.values()):
+            it.call(f, UNDEF, [v, k, self])
+        return UNDEF
+
+    js_methods = {
+        "get": lambda s, i, x: s.d.get(_mkey(_arg(x, 0)), (None, UNDEF))[1],
+        "set": lambda s, i, x: (s.d.__setitem__(_mkey(_arg(x, 0)), (_arg(x, 0), _arg(x, 1))), s)[-1],
+        "has": lambda s, i, x: _mkey(_arg(x, 0)) in s.d,
+        "delete": lambda s, i, x: s.d.pop(_mkey(_arg(x, 0)), None) is not None,
+        "clear": lambda s, i, x: (s.d.clear(), UNDEF)[-1],
+        "forEach": lambda s, i, x: s._each(i, _arg(x, 0)),
+        "keys": lambda s, i, x: JSArray([k for k, _ in s.d.values()]),
+        "values": lambda s, i, x: JSArray([v for _, v in s.d.values()]),
+        "entries": lambda s, i, x: JSArray(s.iterable()),
+    }
+
+
+class JSSet(Host):
+    __slots__ = ("d",)
+    cls_name = "Set"
+
+    def __init__(self, it, src=UNDEF):
+        super().__init__({})
+        self.d: Dict[Any, Any] = {}
+        if src is not UNDEF and src is not None:
+            for v in it.iterate(src):
+                self.d[_mkey(v)] = v
+
+    def get_special(self, it, key):
+        if key == "size":
+            return float(len(self.d))
+        return super().get_special(it, key)
+
+    def iterable(self):
+        return list(self.d.values())
+
+    def own_keys(self):
+        return []
+
+    def _each(self, it, f):
+        for v in list(self.d.values()):
+            it.call(f, UNDEF, [v, v, self])
+        return UNDEF
+
+    js_methods = {
+        "add": lambda s, i, x: (s.d.__setitem__(_mkey(_arg(x, 0)), _arg(x, 0)), s)[-1],
+        "has": lambda s, i, x: _mkey(_arg(x, 0)) in s.d,
+        "delete": lambda s, i, x: s.d.pop(_mkey(_arg(x, 0)), _SKIP) is not _SKIP,
+        "clear": lambda s, i, x: (s.d.clear(), UNDEF)[-1],
+        "forEach": lambda s, i, x: s._each(i, _arg(x, 0)),
+        "keys": lambda s, i, x: JSArray(s.iterable()),
+        "values": lambda s, i, x: JSArray(s.iterable()),
+        "entries": lambda s, i, x: JSArray([JSArray([v, v]) for v in s.iterable()]),
+    }

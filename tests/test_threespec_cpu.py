@@ -1,0 +1,122 @@
+"""The checker follows the output specification's name tables (app/threespec.py), and the interpreter implements
+every THREE member the specification allows."""
+import numpy as np
+import pytest
+
+from phung5_b200.app import jsvm, threespec
+from phung5_b200.app.jscheck import JSChecker
+
+TAIL = " g.add(new THREE.Mesh(new THREE.BoxGeometry(1, 1, 1), new THREE.MeshStandardMaterial())); return g; }"
+
+
+def _check(body, **kw):
+    return JSChecker(_inline=True).check("export default function generate(THREE) { const g = new THREE.Group(); "
+                                         + body + TAIL)
+
+
+def _rules(body):
+    return {f["rule"] for f in _check(body).failures}
+
+
+def test_every_allowed_member_is_implemented():
+    three = jsvm.make_three(jsvm.Interp())
+    assert sorted(n for n in threespec.THREE_ALLOWED if n not in three.props) == []
+
+
+@pytest.mark.parametrize("body,rule", [
+    ("const m = new THREE.MeshPhongMaterial();", "FORBIDDEN_THREE_API"),
+    ("const m = new THREE.MeshLambertMaterial();", "FORBIDDEN_THREE_API"),
+    ("const t = new THREE.CanvasTexture();", "FORBIDDEN_THREE_API"),
+    ("const l = new THREE.LineLoop();", "UNKNOWN_THREE_API"),
+    ("const r = THREE.MathUtils.seededRandom();", "FORBIDDEN_THREE_API"),
+    ("const k = 'sin'; const v = Math[k](1);", "COMPUTED_PROPERTY_ACCESS"),
+    ("const o = {}; const p = o.__proto__;", "FORBIDDEN_PROPERTY_ACCESS"),
+    ("const d = Date.now();", "FORBIDDEN_IDENTIFIER"),
+])
+def test_specification_rejections(body, rule):
+    assert rule in _rules(body)
+
+
+def test_console_is_not_a_global_and_its_statements_are_repaired_away():
+    off = JSChecker(_inline=True)
+    off.s.failure_repair = False
+    src = "export default function generate(THREE) { const g = new THREE.Group(); console.log('x', 1);" + TAIL
+    assert "IDENTIFIER_NOT_ALLOWED" in {f["rule"] for f in off.check(src).failures}
+    res = JSChecker(_inline=True).check(src)
+    assert res.ok and "console: console" in res.repaired and "console" not in res.code
+
+
+def test_spec_globals_json_map_set_and_prototype_access():
+    res = _check("""
+      const o = JSON.parse(JSON.stringify({a: [1, 2], b: {c: 'x'}}));
+      const m = new Map([['k', 2]]); m.set('j', 3);
+      const s = new Set([1, 2, 2, 3]);
+      let sum = 0; for (const [k, v] of m) sum += v; for (const v of s) sum += v;
+      function F() {} F.prototype.w = 5;
+      g.userData.v = [o.a[1], o.b.c, m.size, s.size, sum, new F().w, Number.parseInt('12'), JSON.stringify([1, 'a'])];
+    """)
+    assert res.ok, res.summary()
+
+
+def _run(body):
+    r = jsvm.run_module("export default function generate(THREE) { const g = new THREE.Group(); " + body + TAIL,
+                        jsvm.Limits(steps=2_000_000, seconds=10))
+    assert r.error is None, r.error
+    return r.root.props["userData"].props
+
+
+def _arr(v):
+    return [float(x) for x in v.items]
+
+
+def test_edges_wireframe_and_polyhedron_geometries():
+    ud = _run("""
+      const box = new THREE.BoxGeometry(1, 1, 1);
+      g.userData.edges = new THREE.EdgesGeometry(box).attributes.position.count;
+      g.userData.wire = new THREE.WireframeGeometry(box).attributes.position.count;
+      const tet = new THREE.PolyhedronGeometry([1, 1, 1, -1, -1, 1, -1, 1, -1, 1, -1, -1], [2, 1, 0, 0, 3, 2, 1, 3, 0, 2, 3, 1], 2, 1);
+      const p = tet.attributes.position;
+      g.userData.tet = [p.count, Math.hypot(p.getX(0), p.getY(0), p.getZ(0))];
+      g.add(new THREE.LineSegments(new THREE.EdgesGeometry(box), new THREE.LineBasicMaterial()));
+    """)
+    assert ud["edges"] == 24            # a cube's 12 edges, two points each; the diagonals are flat
+    assert ud["wire"] == 36             # 18 distinct triangle edges
+    assert _arr(ud["tet"])[0] == 24 and _arr(ud["tet"])[1] == pytest.approx(2.0)
+
+
+def test_math_helpers_and_curves():
+    ud = _run("""
+      const sp = new THREE.Spherical().setFromVector3(new THREE.Vector3(1, 2, 3));
+      const back = new THREE.Vector3().setFromSpherical(sp);
+      g.userData.sph = [back.x, back.y, back.z];
+      const cyl = new THREE.Vector3().setFromCylindricalCoords(2, Math.PI / 2, 5);
+      g.userData.cyl = [cyl.x, cyl.y, cyl.z];
+      const pl = new THREE.Plane().setFromNormalAndCoplanarPoint(new THREE.Vector3(0, 1, 0), new THREE.Vector3(0, 2, 0));
+      g.userData.pl = [pl.distanceToPoint(new THREE.Vector3(5, 7, 1))];
+      const tri = new THREE.Triangle(new THREE.Vector3(0, 0, 0), new THREE.Vector3(2, 0, 0), new THREE.Vector3(0, 2, 0));
+      g.userData.tri = [tri.getArea()];
+      const m3 = new THREE.Matrix3().set(2, 0, 0, 0, 3, 0, 0, 0, 4).invert();
+      g.userData.m3 = [m3.determinant()];
+      const arc = new THREE.EllipseCurve(0, 0, 2, 1, 0, Math.PI, false, 0).getPoints(4);
+      g.userData.arc = [arc.length, arc[2].x, arc[2].y, arc[4].x];
+      const path = new THREE.CurvePath();
+      path.add(new THREE.LineCurve(new THREE.Vector2(0, 0), new THREE.Vector2(1, 0)));
+      path.add(new THREE.LineCurve(new THREE.Vector2(1, 0), new THREE.Vector2(1, 1)));
+      const mid = path.getPoint(0.75);
+      g.userData.path = [mid.x, mid.y];
+      class Helix extends THREE.Curve {
+        getPoint(t, target = new THREE.Vector3()) { return target.set(Math.cos(6 * t), t, Math.sin(6 * t)); }
+      }
+      const tube = new THREE.TubeGeometry(new Helix(), 32, 0.05, 6, false);
+      g.add(new THREE.Mesh(tube, new THREE.MeshStandardMaterial()));
+      const q = new THREE.Quaternion().setFromAxisAngle(new THREE.Vector3(0, 0, 1), Math.PI / 2);
+      const v = new THREE.Vector3(1, 0, 0).applyQuaternion(q).addScaledVector(new THREE.Vector3(0, 0, 1), 2);
+      g.userData.q = [v.x, v.y, v.z];
+    """)
+    np.testing.assert_allclose(_arr(ud["sph"]), [1, 2, 3], atol=1e-9)
+    np.testing.assert_allclose(_arr(ud["cyl"]), [2, 5, 0], atol=1e-9)
+    assert _arr(ud["pl"]) == [5.0] and _arr(ud["tri"]) == [2.0]
+    assert _arr(ud["m3"])[0] == pytest.approx(1 / 24)
+    np.testing.assert_allclose(_arr(ud["arc"]), [5, 0, 1, -2], atol=1e-9)
+    np.testing.assert_allclose(_arr(ud["path"]), [1, 0.5], atol=1e-9)
+    np.testing.assert_allclose(_arr(ud["q"]), [0, 1, 2], atol=1e-9)
