@@ -25,6 +25,9 @@ from typing import Any, Dict, Iterable, List, Optional, Set
 from . import jsrepair, jsvm, threefix, threespec
 
 LIMITS = {"vertices": 250_000, "drawCalls": 200, "depth": 32, "instances": 50_000, "textureBytes": 4 * 1_048_576}
+MAX_FILE_BYTES = 1_048_576          # source size (UTF-8)
+BOUND = 0.5                         # the model must fit inside [-0.5, 0.5] on every axis
+BOUND_TOL = 1e-6                    # float32 vertex storage vs the validator's doubles
 LITERAL_BUDGET = 50 * 1024
 ROOT_TYPES = {"Group", "Mesh", "LineSegments", "Points", "Object3D", "InstancedMesh", "Line"}
 
@@ -449,11 +452,21 @@ def post_validate(root) -> tuple:
     if bad_numbers:
         fail("NON_FINITE_VALUE", "a transform or vertex is NaN or infinite")
     for key, rule in (("vertices", "VERTEX_LIMIT_EXCEEDED"), ("drawCalls", "DRAW_CALL_LIMIT_EXCEEDED"),
-                      ("instances", "INSTANCE_LIMIT_EXCEEDED"), ("textureBytes", "TEXTURE_BYTES_EXCEEDED")):
+                      ("instances", "INSTANCE_LIMIT_EXCEEDED"), ("textureBytes", "TEXTURE_DATA_EXCEEDED")):
         if stats[key] > LIMITS[key]:
             fail(rule, f"{stats[key]} {key} (limit {LIMITS[key]})")
     if stats["meshes"] == 0 and not fails:
         fail("EMPTY_SCENE", "the returned object contains no meshes")
+    elif not fails:
+        bb = jsvm.world_bbox(root)
+        if bb is None:
+            fail("EMPTY_SCENE", "the returned object's bounding box is empty")
+        else:
+            lo, hi = [float(v) for v in bb[0]], [float(v) for v in bb[1]]
+            stats["bbox"] = {"min": lo, "max": hi}
+            if any(v < -BOUND - BOUND_TOL for v in lo) or any(v > BOUND + BOUND_TOL for v in hi):
+                fail("BOUNDING_BOX_OUT_OF_RANGE", "box [" + ", ".join(f"{v:.3f}" for v in lo) + "] to [" +
+                     ", ".join(f"{v:.3f}" for v in hi) + "] (must fit in [-0.5, 0.5] on every axis)")
     return fails, stats
 
 
@@ -546,6 +559,10 @@ class JSChecker:
         return res
 
     def _check_code(self, code: str, seed: int, fixes: List[str]) -> CheckResult:
+        size = len(code.encode("utf-8"))
+        if size > MAX_FILE_BYTES:
+            return CheckResult(False, [{"stage": "parse", "rule": "FILE_SIZE_EXCEEDED",
+                                        "detail": f"{size} bytes (limit {MAX_FILE_BYTES})"}], code, repaired=fixes)
         try:
             prog = jsvm.Parser(code).program()
         except jsvm.JSError as e:
@@ -563,7 +580,8 @@ class JSChecker:
             return CheckResult(False, fails, code, stats={"three": three_param(prog)}, repaired=fixes)
         res = jsvm.run_module(code, jsvm.Limits(steps=self.s.max_steps, seconds=self.s.timeout_s), seed=seed)
         if res.error is not None:
-            rule = "EXECUTION_TIMEOUT" if res.error.startswith("TIMEOUT") else "EXECUTION_ERROR"
+            rule = ("HEAP_EXCEEDED" if res.error.startswith("HEAP") else
+                    "TIMEOUT_EXCEEDED" if res.error.startswith("TIMEOUT") else "EXECUTION_THREW")
             return CheckResult(False, [{"stage": "execution", "rule": rule, "detail": res.error}], code,
                                stats={"steps": res.steps, "exec_s": res.seconds}, repaired=fixes)
         fails, stats = post_validate(res.root)

@@ -8,13 +8,13 @@ planned on `jsvm.tokenize` tokens (so strings, comments and template text are ne
 
 - `redeclared`  PARSE_ERROR "Identifier 'x' has already been declared": a later `let/const x = ...` in the same
                 block becomes the assignment `x = ...` and the first declaration of x becomes `let`.
-- `constlet`    EXECUTION_ERROR "assignment to constant variable x": x's `const` declarations become `let`.
+- `constlet`    EXECUTION_THREW "assignment to constant variable x": x's `const` declarations become `let`.
 - `paren`       PARSE_ERROR "unexpected token ')'": the first `)` that closes nothing is deleted.
 - `ident`       IDENTIFIER_NOT_ALLOWED `x`: if exactly one declared name equals x up to case and underscores
                 (`roundedPts` / `rounded_pts`), every reference to x is renamed to it.
 - `console`     IDENTIFIER_NOT_ALLOWED `console` (not a global the specification allows): every `console.x(...);`
                 statement is removed; a use of console anywhere but a statement of its own is not rewritten.
-- `retry`       EXECUTION_TIMEOUT on the wall-clock deadline only (not the step budget): checked once more, since
+- `retry`       TIMEOUT_EXCEEDED on the wall-clock deadline only (not the step budget): checked once more, since
                 host load can push a module over the deadline.
 
 Every class refuses (returns None) when its precondition is not met exactly; `plan` picks the classes the
@@ -44,12 +44,12 @@ def plan(fails: Iterable[Dict[str, str]]) -> List[Tuple[str, str]]:
             out.append(("redeclared", _DUP.search(detail).group(1)))
         elif rule == "PARSE_ERROR" and "unexpected token ')'" in detail:
             out.append(("paren", ")"))
-        elif rule == "EXECUTION_ERROR" and _CONST.search(detail):
+        elif rule == "EXECUTION_THREW" and _CONST.search(detail):
             out.append(("constlet", _CONST.search(detail).group(1)))
         elif rule == "IDENTIFIER_NOT_ALLOWED" and _IDENT.search(detail):
             name = _IDENT.search(detail).group(1)
             out.append(("console", name) if name == "console" else ("ident", name))
-        elif rule == "EXECUTION_TIMEOUT" and "execution exceeded" in detail:
+        elif rule == "TIMEOUT_EXCEEDED" and "execution exceeded" in detail:
             out.append(("retry", ""))
         else:
             return []

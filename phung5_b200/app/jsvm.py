@@ -4144,7 +4144,8 @@ def run_module(source: str, limits: Optional[Limits] = None, seed: int = 0) -> M
         root = it.call(gen, UNDEF, [make_three(it)])
         return ModuleResult(root=root, steps=it.steps, seconds=time.monotonic() - t0)
     except JSBudget as e:
-        return ModuleResult(error=f"TIMEOUT: {e.msg}", steps=it.steps, seconds=time.monotonic() - t0)
+        kind = "TIMEOUT" if ("budget" in e.msg or "exceeded" in e.msg) else "HEAP"   # time / steps, or memory
+        return ModuleResult(error=f"{kind}: {e.msg}", steps=it.steps, seconds=time.monotonic() - t0)
     except JSError as e:
         return ModuleResult(error=f"{e.kind}: {e.msg}", steps=it.steps, seconds=time.monotonic() - t0)
     except _Throw as e:

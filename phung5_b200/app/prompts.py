@@ -14,9 +14,10 @@ _ALLOWED = ", ".join(sorted(n for n in THREE_ALLOWED if n[0].isupper() and not n
 CODER_SYSTEM = f"""You write a single JavaScript ES module that builds a 3D model of the object in the user's image
 with three.js. Contract:
 - `export default function generate(THREE) {{ ... return root; }}` is the only export; `THREE` is passed in,
-  never imported. `root` is a THREE.Group (or Mesh) centred near the origin, +Y up, the object's front facing +Z.
+  never imported. `root` is a THREE.Group (or Mesh) centred near the origin, +Y up, the object's front facing +Z,
+  and the whole model fits inside the cube [-0.5, 0.5] on every axis (scale it to fit).
 - Use only these THREE members: {_ALLOWED}, plus MathUtils and the side/colour-space constants.
-- No lights, cameras, renderers, loaders, textures from URLs, timers, randomness from the environment, classes,
+- No lights, cameras, renderers, loaders, textures from URLs, timers, console, randomness from the environment,
   async code or imports. Math.random is deterministic.
 - Budget: at most {LIMITS['vertices']} vertices, {LIMITS['drawCalls']} meshes, nesting depth {LIMITS['depth']}.
 - Model the silhouette first (proportions, part count, placement), then colour and materials, then details.

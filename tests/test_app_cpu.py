@@ -119,7 +119,7 @@ def test_jsvm_budgets_and_isolation():
     r = jsvm.run_module("export default function generate(THREE) { for(;;){} }", jsvm.Limits(steps=10_000))
     assert r.error.startswith("TIMEOUT")
     r = jsvm.run_module("export default function generate(THREE) { const a = []; a.length = 1e12; }")
-    assert r.error.startswith("TIMEOUT") or "RangeError" in r.error
+    assert r.error.startswith(("TIMEOUT", "HEAP")) or "RangeError" in r.error
     r = jsvm.run_module("export default function generate(THREE) { return THREE.Mesh.__class__ }")
     assert r.error is None and r.root is jsvm.UNDEF      # host internals are not reachable
     r = jsvm.run_module("export default function generate(THREE) { function f(){ return f() } return f() }")
@@ -137,10 +137,10 @@ def test_jsvm_budgets_and_isolation():
 GOOD = """export default function generate(THREE) {
   const g = new THREE.Group();
   const m = new THREE.MeshStandardMaterial({ color: 0xaa3311 });
-  const seat = new THREE.Mesh(new THREE.BoxGeometry(1, 0.1, 1), m); seat.position.y = 0.5; g.add(seat);
+  const seat = new THREE.Mesh(new THREE.BoxGeometry(1, 0.1, 1), m); seat.position.y = 0.3; g.add(seat);
   for (const [x, z] of [[-0.4, -0.4], [0.4, -0.4], [-0.4, 0.4], [0.4, 0.4]]) {
-    const leg = new THREE.Mesh(new THREE.CylinderGeometry(0.05, 0.05, 0.5, 8), m);
-    leg.position.set(x, 0.25, z); g.add(leg);
+    const leg = new THREE.Mesh(new THREE.CylinderGeometry(0.05, 0.05, 0.3, 8), m);
+    leg.position.set(x, 0.15, z); g.add(leg);
   }
   return g;
 }"""
@@ -164,7 +164,7 @@ def test_checker_rules_limits_and_repair():
     assert "COMPUTED_PROPERTY_ACCESS" in rules("export default function generate(THREE) { return new THREE['Group']() }")
     assert "FORBIDDEN_PROPERTY_ACCESS" in rules("export default function generate(THREE) { const g = new THREE.Group(); g.constructor; return g }")
     assert "LITERAL_BUDGET_EXCEEDED" in rules("export default function generate(THREE) { const s = '" + "a" * 60000 + "'; return new THREE.Group() }")
-    assert "EXECUTION_ERROR" in rules("export default function generate(THREE) { return undefinedThing.x }".replace(
+    assert "EXECUTION_THREW" in rules("export default function generate(THREE) { return undefinedThing.x }".replace(
         "undefinedThing", "(null)"))
     assert "EMPTY_SCENE" in rules("export default function generate(THREE) { return new THREE.Group() }")
     assert "PARSE_ERROR" in rules("export default function generate(THREE) { return (( }")
@@ -339,6 +339,7 @@ CODE_T = """export default function generate(THREE) {
   const m = new THREE.MeshStandardMaterial({ color: 0x%06x });
   const body = new THREE.Mesh(new THREE.BoxGeometry(%s, %s, 0.5), m);
   g.add(body);
+  g.scale.setScalar(1 / Math.max(%s, 1));        // fit the unit cube
   return g;
 }"""
 
@@ -375,7 +376,7 @@ class StubLLM:
             if seed % 5 == 0 and "failed validation" not in text:
                 return reply("```js\nexport default function generate(THREE) { return new THREE.Group() }\n```")
             w = 0.4 + (seed % 7) * 0.2
-            return reply("```js\n" + CODE_T % (0x10 * (seed % 13) + 0x204060, w, 1.0) + "\n```", ctok=120)
+            return reply("```js\n" + CODE_T % (0x10 * (seed % 13) + 0x204060, w, 1.0, w) + "\n```", ctok=120)
         if "review a 3D model" in system:
             self.calls["critic"] += 1
             return reply(json.dumps({"issues": [{"kind": "wrong_size", "description": "too small", "severity": 8}],

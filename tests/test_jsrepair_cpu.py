@@ -73,11 +73,11 @@ def test_no_repair_when_a_failure_has_no_class_or_the_fix_is_ambiguous():
     assert jsrepair.fix_redeclared("const {a} = o; const a = 2;", "a") is None
     # off: the failure stands
     res = _checker(failure_repair=False).check(_module("const w = 1; w = 2;"))
-    assert not res.ok and res.failures[0]["rule"] == "EXECUTION_ERROR"
+    assert not res.ok and res.failures[0]["rule"] == "EXECUTION_THREW"
 
 
 def test_only_the_wall_clock_timeout_is_retried():
-    assert jsrepair.plan([{"rule": "EXECUTION_TIMEOUT", "detail": "TIMEOUT: execution exceeded 5.0s"}]) == \
+    assert jsrepair.plan([{"rule": "TIMEOUT_EXCEEDED", "detail": "TIMEOUT: execution exceeded 5.0s"}]) == \
         [("retry", "")]
-    assert jsrepair.plan([{"rule": "EXECUTION_TIMEOUT",
+    assert jsrepair.plan([{"rule": "TIMEOUT_EXCEEDED",
                            "detail": "TIMEOUT: step budget of 20000000 exceeded"}]) == []

@@ -16,12 +16,12 @@ from phung5_b200.app.orient import (OrientSettings, decide, orient_candidate, pr
 
 BOX = """export default function generate(THREE) {
   const g = new THREE.Group();
-  const body = new THREE.Mesh(new THREE.BoxGeometry(2, 1, 0.5), new THREE.MeshStandardMaterial({ color: 0xdddddd }));
+  const body = new THREE.Mesh(new THREE.BoxGeometry(0.6, 0.3, 0.15), new THREE.MeshStandardMaterial({ color: 0xdddddd }));
   g.add(body);
-  const mark = new THREE.Mesh(new THREE.BoxGeometry(0.2, 0.8, 0.4), new THREE.MeshStandardMaterial({ color: 0xff0000 }));
-  mark.position.set(1.1, 0, 0);          // on the +x side: seen by the right-hand camera
+  const mark = new THREE.Mesh(new THREE.BoxGeometry(0.06, 0.24, 0.12), new THREE.MeshStandardMaterial({ color: 0xff0000 }));
+  mark.position.set(0.33, 0, 0);         // on the +x side: seen by the right-hand camera
   g.add(mark);
-  g.position.set(5, 0, 0);
+  g.position.set(0.05, 0, 0);
   return g;
 }
 """

@@ -13,7 +13,7 @@ MODULE = """export default function generate(THREE) {
   tex.minFilter = THREE.LinearMipMapLinear;
   tex.colorSpace = THREE.sRGBEncoding;
   const geo = new THREE.BufferGeometry();
-  const pos = new THREE.Float32BufferAttribute([0, 0, 0, 1, 0, 0, 0, 1, 0], 3);
+  const pos = new THREE.Float32BufferAttribute([-0.5, -0.5, 0, 0.5, -0.5, 0, 0, 0.5, 0], 3);
   pos.setUsage(THREE.DynamicDraw);
   geo.setAttribute("position", pos);
   const mat = new THREE.MeshStandardMaterial({ color: 0x884422, map: tex, side: THREE.BothSides,
