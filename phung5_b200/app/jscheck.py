@@ -264,6 +264,36 @@ def redeclared_name(prog) -> Optional[str]:
     return r or visit(prog[1])
 
 
+def _ctor_params(cls_node):
+    for kind, _static, _key, fn in cls_node[3]:
+        if kind == "ctor":
+            return fn[2]
+    return []
+
+
+def _function_params(prog) -> Dict[str, list]:
+    """name -> parameter list of the module's named functions and classes (declarations, and const / let / var
+    bindings of function or class expressions); scopes are not distinguished."""
+    out: Dict[str, list] = {}
+
+    def visit(n):
+        tag = n[0]
+        if tag == "fundecl":
+            out[n[1]] = n[2][2]
+        elif tag == "classdecl":
+            out[n[1]] = _ctor_params(n[2])
+        elif tag == "decl":
+            for target, init in n[2]:
+                if target[0] == "id" and isinstance(init, tuple) and init:
+                    if init[0] == "func":
+                        out[target[1]] = init[2]
+                    elif init[0] == "class":
+                        out[target[1]] = _ctor_params(init)
+        return True
+    _walk(prog, visit)
+    return out
+
+
 def static_analyze(prog) -> List[Dict[str, str]]:
     fails: List[Dict[str, str]] = []
 
@@ -288,17 +318,112 @@ def static_analyze(prog) -> List[Dict[str, str]]:
     declared = _declared_names(prog)
     literal_bytes = [0]
     seen_forbidden: Set[str] = set()
+    # THREE flows only into member access, destructuring of allowed members, and helpers whose parameter is
+    # named THREE (or destructures allowed members); `THREE` as a parameter name of such a helper counts too
+    three_names = {n for n in (three, "THREE") if n is not None and (n == three or n in declared)}
+    funcs = _function_params(prog)
+
+    def is_three(e) -> bool:
+        return isinstance(e, tuple) and len(e) == 2 and e[0] == "ident" and e[1] in three_names
+
+    def member_rule(nm: str, how: str = "") -> None:
+        if nm not in THREE_ALLOWED:
+            if nm in THREE_DISALLOWED_KNOWN:
+                fail("FORBIDDEN_THREE_API", f"THREE.{nm}{how} is a real three.js API that the output "
+                                            f"specification excludes")
+            else:
+                fail("UNKNOWN_THREE_API", f"THREE.{nm}{how} is not a supported three.js member")
+
+    def receive_three(p, param: bool) -> None:
+        """A binding that receives THREE itself: a parameter named THREE, or object destructuring of allowed
+        members (nested destructuring of MathUtils may not take its blocked members)."""
+        if p[0] == "id":
+            if not (param and p[1] == "THREE"):
+                fail("THREE_ALIAS_FORBIDDEN", f"passing THREE to a parameter named `{p[1]}` (name it THREE)" if param
+                     else f"aliasing THREE as `{p[1]}`")
+            return
+        if p[0] != "objpat":
+            fail("THREE_ALIAS_FORBIDDEN", "THREE may only be destructured as an object of allowed members")
+            return
+        if p[2]:
+            fail("THREE_ALIAS_FORBIDDEN", f"rest-destructure of THREE (...{p[2]})")
+        for key, target, default in p[1]:
+            if isinstance(key, tuple):
+                fail("COMPUTED_PROPERTY_ACCESS", "computed destructure of THREE")
+                continue
+            member_rule(str(key), " (destructured)")
+            inner = target
+            if key in THREE_BLOCKED_SUBMEMBERS and inner[0] == "objpat":
+                if inner[2]:
+                    fail("FORBIDDEN_THREE_API", f"THREE.{key}.{{...}} rest-destructure")
+                for sub, _, _ in inner[1]:
+                    if isinstance(sub, str) and sub in THREE_BLOCKED_SUBMEMBERS[key]:
+                        fail("FORBIDDEN_THREE_API", f"THREE.{key}.{sub} (destructured) is not allowed")
+            if default is not None:
+                _walk(default, visit)
+
+    def three_args(callee, args, is_new: bool) -> None:
+        ks = [k for k, a in enumerate(args) if is_three(a)]
+        if not ks:
+            return
+        if is_new and callee[0] == "member" and is_three(callee[1]):
+            fail("THREE_ALIAS_FORBIDDEN", "THREE passed to a three.js constructor")
+            return
+        params = None
+        if callee[0] == "ident":
+            params = funcs.get(callee[1])
+        elif callee[0] == "func":
+            params = callee[2]
+        elif callee[0] == "class":
+            params = _ctor_params(callee)
+        if params is None:
+            fail("THREE_ALIAS_FORBIDDEN", "THREE passed to a function the checker cannot resolve")
+            return
+        for k in ks:
+            if k >= len(params):
+                fail("THREE_ALIAS_FORBIDDEN", "THREE passed to a rest or missing parameter")
+            else:
+                receive_three(params[k][0], True)
 
     def visit(n):
         tag = n[0]
+        if tag in ("call", "new"):
+            three_args(n[1], n[2], tag == "new")
+            _walk(n[1], visit)
+            for a in n[2]:
+                if not is_three(a):
+                    _walk(a, visit)
+            return False
+        if tag == "decl":
+            for target, init in n[2]:
+                if is_three(init):
+                    receive_three(target, False)
+                else:
+                    _walk(target, visit)
+                    if init is not None:
+                        _walk(init, visit)
+            return False
+        if tag == "assign" and n[1] == "=" and is_three(n[3]):
+            fail("THREE_ALIAS_FORBIDDEN", "assigning THREE to a variable or member")
+            _walk(n[2], visit)
+            return False
+        if tag == "assign_pat" and is_three(n[2]):
+            receive_three(n[1], False)
+            return False
+        if tag == "spread" and is_three(n[1]):
+            fail("THREE_ALIAS_FORBIDDEN", "spread of THREE")
+            return False
         if tag == "ident":
             nm = n[1]
             if nm in FORBIDDEN_IDENTIFIERS:
                 if nm not in seen_forbidden:
                     fail("FORBIDDEN_IDENTIFIER", f"`{nm}` is not allowed")
                     seen_forbidden.add(nm)
-            elif nm == three:
-                fail("THREE_ALIAS_FORBIDDEN", f"`{three}` may only be used as `{three}.Member`")
+            elif nm in three_names:
+                fail("THREE_ALIAS_FORBIDDEN", f"`{nm}` used in a position the checker cannot follow "
+                                              f"(only THREE.Member, destructuring, or a helper's THREE parameter)")
+            elif nm == "THREE" and nm not in declared:
+                fail("THREE_AT_TOP_LEVEL", "THREE referenced outside generate")
             elif nm not in declared and nm not in ALLOWED_ROOTS:
                 if nm not in seen_forbidden:
                     fail("IDENTIFIER_NOT_ALLOWED", f"`{nm}` is not declared and not an allowed global")
@@ -311,20 +436,20 @@ def static_analyze(prog) -> List[Dict[str, str]]:
             if obj[0] == "ident" and computed and obj[1] != three and obj[1] in COMPUTED_ACCESS_GATED \
                     and obj[1] not in declared:
                 fail("COMPUTED_PROPERTY_ACCESS", f"`{obj[1]}[...]` is not allowed")
-            if obj[0] == "ident" and obj[1] == three:
+            if obj[0] == "ident" and obj[1] == "Math" and not computed and key == ("lit", "random") \
+                    and "Math" not in declared:
+                fail("FORBIDDEN_IDENTIFIER", "Math.random is not allowed (write a seeded generator)")
+            if obj[0] == "ident" and obj[1] in three_names:
                 if computed or key[0] != "lit":
-                    fail("COMPUTED_PROPERTY_ACCESS", f"`{three}[...]` is not allowed")
+                    fail("COMPUTED_PROPERTY_ACCESS", f"`{obj[1]}[...]` is not allowed")
                 else:
-                    nm = str(key[1])
-                    if nm not in THREE_ALLOWED:
-                        if nm in THREE_DISALLOWED_KNOWN:
-                            fail("FORBIDDEN_THREE_API", f"THREE.{nm} is a real three.js API that the output "
-                                                        f"specification excludes")
-                        else:
-                            fail("UNKNOWN_THREE_API", f"THREE.{nm} is not a supported three.js member")
+                    member_rule(str(key[1]))
                 _walk(key, visit)
                 return False
-            if obj[0] == "member" and obj[1][0] == "ident" and obj[1][1] == three and key[0] == "lit":
+            if obj[0] == "ident" and obj[1] == "THREE" and "THREE" not in declared:
+                fail("THREE_AT_TOP_LEVEL", "THREE referenced outside generate")
+                return False
+            if obj[0] == "member" and obj[1][0] == "ident" and obj[1][1] in three_names and key[0] == "lit":
                 ns = obj[2][1] if obj[2][0] == "lit" else None
                 if ns in THREE_BLOCKED_SUBMEMBERS and key[1] in THREE_BLOCKED_SUBMEMBERS[ns]:
                     fail("FORBIDDEN_THREE_API", f"THREE.{ns}.{key[1]} is not allowed")

@@ -14,6 +14,8 @@ planned on `jsvm.tokenize` tokens (so strings, comments and template text are ne
                 (`roundedPts` / `rounded_pts`), every reference to x is renamed to it.
 - `console`     IDENTIFIER_NOT_ALLOWED `console` (not a global the specification allows): every `console.x(...);`
                 statement is removed; a use of console anywhere but a statement of its own is not rewritten.
+- `random`      FORBIDDEN_IDENTIFIER Math.random: every `Math.random` becomes a seeded generator defined at the top of
+                the module (a 32-bit linear congruential generator), so the module is valid and deterministic.
 - `retry`       TIMEOUT_EXCEEDED on the wall-clock deadline only (not the step budget): checked once more, since
                 host load can push a module over the deadline.
 
@@ -27,7 +29,10 @@ from typing import Dict, Iterable, List, Optional, Set, Tuple
 
 from . import jsvm
 
-CLASSES = ("redeclared", "constlet", "paren", "ident", "console", "retry")
+CLASSES = ("redeclared", "constlet", "paren", "ident", "console", "random", "retry")
+
+SEEDED_RANDOM = ("const __phxRandom = (() => { let s = 0x2545F491; "
+                 "return () => { s = (s * 1664525 + 1013904223) >>> 0; return s / 4294967296; }; })();\n")
 
 _DUP = re.compile(r"Identifier '([A-Za-z_$][\w$]*)' has already been declared")
 _CONST = re.compile(r"assignment to constant variable ([A-Za-z_$][\w$]*)")
@@ -49,6 +54,8 @@ def plan(fails: Iterable[Dict[str, str]]) -> List[Tuple[str, str]]:
         elif rule == "IDENTIFIER_NOT_ALLOWED" and _IDENT.search(detail):
             name = _IDENT.search(detail).group(1)
             out.append(("console", name) if name == "console" else ("ident", name))
+        elif rule == "FORBIDDEN_IDENTIFIER" and detail.startswith("Math.random"):
+            out.append(("random", ""))
         elif rule == "TIMEOUT_EXCEEDED" and "execution exceeded" in detail:
             out.append(("retry", ""))
         else:
@@ -184,6 +191,18 @@ def fix_console(code: str) -> Optional[str]:
     return _edit(code, edits) if edits else None
 
 
+def fix_random(code: str) -> Optional[str]:
+    toks = _tokens(code)
+    if toks is None:
+        return None
+    edits = [(t.pos, _tok_end(toks[i + 2]), "__phxRandom") for i, t in enumerate(toks[:-2])
+             if t.kind == "id" and t.val == "Math" and toks[i + 1].kind == "p" and toks[i + 1].val == "."
+             and toks[i + 2].val == "random" and (i == 0 or toks[i - 1].val not in (".", "?."))]
+    if not edits:
+        return None
+    return SEEDED_RANDOM + _edit(code, edits)
+
+
 def _norm(name: str) -> str:
     return name.replace("_", "").lower()
 
@@ -217,6 +236,8 @@ def apply(code: str, steps: List[Tuple[str, str]], declared: Set[str]) -> Option
             new = fix_ident(code, subject, declared)
         elif cls == "console":
             new = fix_console(code)
+        elif cls == "random":
+            new = fix_random(code)
         else:
             new = None
         if new is None:

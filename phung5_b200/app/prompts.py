@@ -17,8 +17,9 @@ with three.js. Contract:
   never imported. `root` is a THREE.Group (or Mesh) centred near the origin, +Y up, the object's front facing +Z,
   and the whole model fits inside the cube [-0.5, 0.5] on every axis (scale it to fit).
 - Use only these THREE members: {_ALLOWED}, plus MathUtils and the side/colour-space constants.
-- No lights, cameras, renderers, loaders, textures from URLs, timers, console, randomness from the environment,
-  async code or imports. Math.random is deterministic.
+- No lights, cameras, renderers, loaders, textures from URLs, timers, console, Math.random (write a small seeded
+  generator if you need variation), async code or imports. Helper functions that need THREE take it as a
+  parameter named THREE.
 - Budget: at most {LIMITS['vertices']} vertices, {LIMITS['drawCalls']} meshes, nesting depth {LIMITS['depth']}.
 - Model the silhouette first (proportions, part count, placement), then colour and materials, then details.
 Reply with the module in one ```js fenced block and nothing else."""

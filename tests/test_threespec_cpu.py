@@ -120,3 +120,36 @@ def test_math_helpers_and_curves():
     np.testing.assert_allclose(_arr(ud["arc"]), [5, 0, 1, -2], atol=1e-9)
     np.testing.assert_allclose(_arr(ud["path"]), [1, 0.5], atol=1e-9)
     np.testing.assert_allclose(_arr(ud["q"]), [0, 1, 2], atol=1e-9)
+
+
+@pytest.mark.parametrize("pre,body,ok,rule", [
+    ("function leg(THREE, h) { return new THREE.Mesh(new THREE.BoxGeometry(0.1, h, 0.1), "
+     "new THREE.MeshStandardMaterial()); }\n", "g.add(leg(THREE, 0.5));", True, None),
+    ("function leg(T, h) { return new T.Mesh(); }\n", "g.add(leg(THREE, 0.5));", False, "THREE_ALIAS_FORBIDDEN"),
+    ("", "const { Mesh, BoxGeometry } = THREE; g.add(new Mesh(new BoxGeometry(0.2, 0.2, 0.2)));", True, None),
+    ("", "const make = ({ Mesh, SphereGeometry }) => new Mesh(new SphereGeometry(0.1)); g.add(make(THREE));", True, None),
+    ("", "const { ShaderMaterial } = THREE;", False, "FORBIDDEN_THREE_API"),
+    ("", "const { MathUtils: { seededRandom } } = THREE;", False, "FORBIDDEN_THREE_API"),
+    ("", "const T = THREE;", False, "THREE_ALIAS_FORBIDDEN"),
+    ("", "const o = { ...THREE };", False, "THREE_ALIAS_FORBIDDEN"),
+    ("", "g.userData.t = [THREE];", False, "THREE_ALIAS_FORBIDDEN"),
+    ("", "const m = new THREE.Mesh(THREE);", False, "THREE_ALIAS_FORBIDDEN"),
+    ("", "const x = Math.random();", False, "FORBIDDEN_IDENTIFIER"),
+])
+def test_three_flow_and_math_random(pre, body, ok, rule):
+    c = JSChecker(_inline=True)
+    c.s.failure_repair = False
+    res = c.check(pre + "export default function generate(THREE) { const g = new THREE.Group(); " + body + TAIL)
+    assert res.ok == ok, res.summary()
+    if rule:
+        assert rule in {f["rule"] for f in res.failures}
+
+
+def test_math_random_is_repaired_with_a_seeded_generator():
+    src = ("export default function generate(THREE) { const g = new THREE.Group(); "
+           "for (let i = 0; i < 3; i++) { const m = new THREE.Mesh(new THREE.BoxGeometry(0.1, 0.1, 0.1), "
+           "new THREE.MeshStandardMaterial()); m.position.x = Math.random() * 0.5 - 0.25; g.add(m); }" + TAIL)
+    a, b = JSChecker(_inline=True).check(src), JSChecker(_inline=True).check(src)
+    assert a.ok and "random" in a.repaired and "Math.random" not in a.code
+    mats = [[c["matrix"] for c in r.scene["object"]["children"]] for r in (a, b)]
+    assert mats[0] == mats[1] and len({m[12] for m in mats[0]}) > 1      # deterministic, and the draws differ
