@@ -2158,6 +2158,10 @@ class Interp:
         raise JSError("SyntaxError", f"unsupported operator {op}")
 
 
+def _is_index_key(k: str) -> bool:
+    return k.isdigit() and (k == "0" or k[0] != "0") and int(k) < 4294967295
+
+
 def _is_objlike(v):
     return isinstance(v, (JSObject, JSArray)) and not isinstance(v, Host) or isinstance(v, JSArray)
 
@@ -2187,7 +2191,12 @@ def _own_keys(v) -> List[str]:
     if isinstance(v, Host):
         return v.own_keys()
     if isinstance(v, JSObject):
-        return list(v.props.keys())
+        keys = list(v.props.keys())
+        idx = [k for k in keys if _is_index_key(k)]
+        if not idx:
+            return keys
+        # integer-like keys first, ascending, then the others in insertion order
+        return sorted(idx, key=int) + [k for k in keys if not _is_index_key(k)]
     if isinstance(v, str):
         return [str(i) for i in range(len(v))]
     return []
@@ -2319,23 +2328,113 @@ def _string_method(it, s: str, name: str):
         "toLowerCase": lambda i, t, x: s.lower(),
         "trim": lambda i, t, x: s.strip(),
         "slice": lambda i, t, x: s[_slice_idx(x, 0, len(s), 0):_slice_idx(x, 1, len(s), len(s))],
-        "substring": lambda i, t, x: s[max(0, int(_num_arg(x, 0))):(len(s) if len(x) < 2 else max(0, int(_num_arg(x, 1))))],
+        "substring": lambda i, t, x: _substring(s, x),
+        "substr": lambda i, t, x: _substr(s, x),
+        "at": lambda i, t, x: (lambda k: s[k] if 0 <= k < len(s) else UNDEF)(
+            int(_num_arg(x, 0)) + (len(s) if _num_arg(x, 0) < 0 else 0)),
+        "lastIndexOf": lambda i, t, x: float(s.rfind(_to_str(_arg(x, 0)))),
+        "trimStart": lambda i, t, x: s.lstrip(),
+        "trimEnd": lambda i, t, x: s.rstrip(),
+        "concat": lambda i, t, x: s + "".join(_to_str(v) for v in x),
+        "localeCompare": lambda i, t, x: float((s > _to_str(_arg(x, 0))) - (s < _to_str(_arg(x, 0)))),
         "charAt": lambda i, t, x: s[int(_num_arg(x, 0))] if 0 <= int(_num_arg(x, 0)) < len(s) else "",
         "charCodeAt": lambda i, t, x: float(ord(s[int(_num_arg(x, 0))])) if 0 <= int(_num_arg(x, 0)) < len(s) else math.nan,
-        "indexOf": lambda i, t, x: float(s.find(_to_str(_arg(x, 0)))),
+        "indexOf": lambda i, t, x: float(s.find(_to_str(_arg(x, 0)), max(0, int(_num_arg(x, 1))))),
         "includes": lambda i, t, x: _to_str(_arg(x, 0)) in s,
         "startsWith": lambda i, t, x: s.startswith(_to_str(_arg(x, 0))),
         "endsWith": lambda i, t, x: s.endswith(_to_str(_arg(x, 0))),
-        "split": lambda i, t, x: JSArray(list(s) if _to_str(_arg(x, 0, "")) == "" else s.split(_to_str(x[0]))),
+        "split": lambda i, t, x: _split(s, x),
         "repeat": lambda i, t, x: _repeat(it, s, int(_num_arg(x, 0))),
-        "padStart": lambda i, t, x: s.rjust(int(_num_arg(x, 0)), (_to_str(_arg(x, 1, " ")) or " ")[0]),
-        "padEnd": lambda i, t, x: s.ljust(int(_num_arg(x, 0)), (_to_str(_arg(x, 1, " ")) or " ")[0]),
+        "padStart": lambda i, t, x: _pad(it, s, x, True),
+        "padEnd": lambda i, t, x: _pad(it, s, x, False),
         "replace": lambda i, t, x: s.replace(_to_str(_arg(x, 0)), _to_str(_arg(x, 1)), 1),
         "replaceAll": lambda i, t, x: s.replace(_to_str(_arg(x, 0)), _to_str(_arg(x, 1))),
         "toString": lambda i, t, x: s,
     }
     f = m.get(name)
     return _nat(name, f) if f is not None else UNDEF
+
+
+def _substring(s, x):
+    n = len(s)
+
+    def clamp(v):
+        v = _to_num(v)
+        return 0 if v != v else int(max(0, min(n, v)))
+    a = clamp(_arg(x, 0, 0.0))
+    b = n if len(x) < 2 or x[1] is UNDEF else clamp(x[1])
+    return s[min(a, b):max(a, b)]
+
+
+def _substr(s, x):
+    n = len(s)
+    a = int(_num_arg(x, 0))
+    a = max(0, n + a) if a < 0 else min(a, n)
+    ln = n - a if len(x) < 2 or x[1] is UNDEF else max(0, int(_num_arg(x, 1)))
+    return s[a:a + ln]
+
+
+def _split(s, x):
+    sep = _arg(x, 0)
+    lim = _arg(x, 1)
+    if sep is UNDEF:
+        parts = [s]
+    elif _to_str(sep) == "":
+        parts = list(s)
+    else:
+        parts = s.split(_to_str(sep))
+    if lim is not UNDEF:
+        parts = parts[:max(0, int(_to_num(lim)))]
+    return JSArray(parts)
+
+
+def _pad(it, s, x, start):
+    n = int(_num_arg(x, 0))
+    fill = _to_str(_arg(x, 1, " "))
+    if n <= len(s) or fill == "":
+        return s
+    if n > it.lim.string_len:
+        raise JSBudget("RangeError", "string too large")
+    k = n - len(s)
+    pad = (fill * (k // len(fill) + 1))[:k]
+    return pad + s if start else s + pad
+
+
+def _to_fixed(v: float, digits: int) -> str:
+    """Number.prototype.toFixed: the exact binary value rounded half away from zero (JS picks the larger n on a
+    tie, applied to the magnitude)."""
+    from decimal import ROUND_HALF_UP, Decimal
+    if v != v:
+        return "NaN"
+    if abs(v) >= 1e21 or math.isinf(v):
+        return _num_to_str(v)
+    d = max(0, min(100, digits))
+    q = Decimal(v if v != 0 else 0.0).quantize(Decimal(1).scaleb(-d), rounding=ROUND_HALF_UP)
+    return f"{q:f}"             # a negative value that rounds to zero keeps its sign, as in JS ("-0.00")
+
+
+def _radix_str(v: float, radix: int) -> str:
+    if radix == 10 or v != v or math.isinf(v):
+        return _num_to_str(v)
+    digits = "0123456789abcdefghijklmnopqrstuvwxyz"
+    neg, v = v < 0, abs(v)
+    ip, fp = int(v), v - int(v)
+    out = ""
+    while True:
+        out = digits[ip % radix] + out
+        ip //= radix
+        if ip == 0:
+            break
+    if fp:
+        out += "."
+        for _ in range(52):
+            fp *= radix
+            dgt = int(fp)
+            out += digits[dgt]
+            fp -= dgt
+            if not fp:
+                break
+    return ("-" if neg else "") + out
 
 
 def _repeat(it, s, n):
@@ -2346,9 +2445,9 @@ def _repeat(it, s, n):
 
 def _number_method(it, v: float, name: str):
     if name == "toFixed":
-        return _nat(name, lambda i, t, x: f"{v:.{int(_num_arg(x, 0))}f}")
+        return _nat(name, lambda i, t, x: _to_fixed(v, int(_num_arg(x, 0))))
     if name == "toString":
-        return _nat(name, lambda i, t, x: _num_to_str(v))
+        return _nat(name, lambda i, t, x: _radix_str(v, max(2, min(36, int(_num_arg(x, 0, 10.0))))))
     if name == "toPrecision":
         return _nat(name, lambda i, t, x: f"{v:.{int(_num_arg(x, 0))}g}")
     return UNDEF
@@ -2416,7 +2515,9 @@ def _install_globals(it: Interp):
         "EPSILON": 2.0 ** -52, "MAX_SAFE_INTEGER": 2.0 ** 53 - 1, "MAX_VALUE": 1.7976931348623157e308,
         "POSITIVE_INFINITY": math.inf, "NEGATIVE_INFINITY": -math.inf, "NaN": math.nan,
         "parseFloat": _nat("parseFloat", lambda i, t, x: _parse_float(_to_str(_arg(x, 0))))}))
-    g.declare("String", Native("String", fn=lambda i, t, x: _to_str(_arg(x, 0, ""))))
+    g.declare("String", Native("String", fn=lambda i, t, x: _to_str(_arg(x, 0, "")), props={
+        "fromCharCode": _nat("fromCharCode", lambda i, t, x: "".join(chr(int(_to_num(c)) & 0xFFFF) for c in x)),
+        "fromCodePoint": _nat("fromCodePoint", lambda i, t, x: "".join(chr(int(_to_num(c))) for c in x))}))
     g.declare("Boolean", Native("Boolean", fn=lambda i, t, x: _truthy(_arg(x, 0, False))))
 
     def array_ctor(i, x):

@@ -70,3 +70,19 @@ def test_object_accessors_prototypes_labels_and_errors():
     assert "before accessing 'this'" in r.error
     r = jsvm.run_module("export default function generate(THREE) { class A {} A(); }", jsvm.Limits(steps=10_000, seconds=2))
     assert "without 'new'" in r.error
+
+
+@pytest.mark.parametrize("expr,want", [
+    ("-5 % 3", -2), ("5 % -3", 2), ("(0 - 1) % 4", -1), ("1 + '2'", "12"), ("'3' * '4'", 12),
+    ("String(0.1 + 0.2)", "0.30000000000000004"), ("String(1e21)", "1e+21"), ("String(2e-7)", "2e-7"),
+    ("(2.5).toFixed(0)", "3"), ("(-2.5).toFixed(0)", "-3"), ("(1.005).toFixed(2)", "1.00"), ("(-0.0001).toFixed(2)", "-0.00"),
+    ("(255).toString(16)", "ff"), ("(25).toString(2)", "11001"), ("(0.5).toString(2)", "0.1"),
+    ("'10' < '9'", True), ("null == undefined", True), ("typeof null", "object"), ("~~-3.7", -3), ("-1 >>> 0", 4294967295),
+    ("1 << 31", -2147483648), ("Math.round(-2.5)", -2), ("[10, 9, 1].sort().join()", "1,10,9"),
+    ("Object.keys({b: 1, 2: 1, a: 1, 1: 1}).join(',')", "1,2,b,a"), ("parseInt('0x1f')", 31), ("Number(' 12 ')", 12),
+    ("'a,b,c'.split(',', 2).join('|')", "a|b"), ("String.fromCharCode(65, 66)", "AB"), ("'abc'.at(-1)", "c"),
+    ("'abc'.substring(2, 0)", "ab"), ("'abcdef'.substr(1, 2)", "bc"), ("'7'.padStart(4, 'ab')", "aba7"),
+    ("'b' + 'a' + + 'a' + 'a'", "baNaNa"), ("[null, undefined, 1].join('-')", "--1"), ("(function () { return arguments.length; })(1, 2, 3)", 3),
+])
+def test_js_semantics(expr, want):
+    assert _ev(expr) == want
