@@ -4033,15 +4033,18 @@ def geometry_mesh(g: Geometry):
     if t == "BoxGeometry":
         v, f = S._box(n("width", 1), n("height", 1), n("depth", 1))
     elif t in ("SphereGeometry",):
-        v, f = S._sphere(n("radius", 1), min(int(n("widthSegments", 32)), 64), min(int(n("heightSegments", 16)), 48))
+        v, f = S._sphere(n("radius", 1), min(int(n("widthSegments", 32)), 64), min(int(n("heightSegments", 16)), 48),
+                         n("phiStart", 0.0), n("phiLength", 2 * math.pi), n("thetaStart", 0.0), n("thetaLength", math.pi))
     elif t in ("IcosahedronGeometry", "OctahedronGeometry", "TetrahedronGeometry", "DodecahedronGeometry"):
-        seg = {"IcosahedronGeometry": 6, "OctahedronGeometry": 4, "TetrahedronGeometry": 3, "DodecahedronGeometry": 8}[t]
-        seg = seg * (1 + int(n("detail", 0)))
-        v, f = S._sphere(n("radius", 1), max(seg, 3), max(seg // 2, 2))
+        v, f = _platonic(t, n("radius", 1), int(n("detail", 0)))
     elif t == "CylinderGeometry":
-        v, f = S._cylinder(n("radiusTop", 1), n("radiusBottom", 1), n("height", 1), min(int(n("radialSegments", 32)), 64))
+        v, f = S._cylinder(n("radiusTop", 1), n("radiusBottom", 1), n("height", 1), min(int(n("radialSegments", 32)), 64),
+                           min(int(n("heightSegments", 1)), 32), _truthy(p.get("openEnded", False)),
+                           n("thetaStart", 0.0), n("thetaLength", 2 * math.pi))
     elif t == "ConeGeometry":
-        v, f = S._cone(n("radius", 1), n("height", 1), min(int(n("radialSegments", 32)), 64))
+        v, f = S._cone(n("radius", 1), n("height", 1), min(int(n("radialSegments", 32)), 64),
+                       min(int(n("heightSegments", 1)), 32), _truthy(p.get("openEnded", False)),
+                       n("thetaStart", 0.0), n("thetaLength", 2 * math.pi))
     elif t == "PlaneGeometry":
         v, f = S._plane(n("width", 1), n("height", 1))
     elif t == "CircleGeometry":
@@ -4051,7 +4054,7 @@ def geometry_mesh(g: Geometry):
                     n("thetaStart", 0), n("thetaLength", 2 * math.pi))
     elif t == "TorusGeometry":
         v, f = S._torus(n("radius", 1), n("tube", 0.4), min(int(n("radialSegments", 12)), 32),
-                        min(int(n("tubularSegments", 48)), 96))
+                        min(int(n("tubularSegments", 48)), 96), n("arc", 2 * math.pi))
     elif t == "CapsuleGeometry":
         r, L = n("radius", 1), n("length", 1)
         prof = [(r * math.sin(math.pi / 2 * k / 6), L / 2 + r * math.cos(math.pi / 2 * k / 6)) for k in range(7)]
@@ -4059,7 +4062,8 @@ def geometry_mesh(g: Geometry):
         v, f = S._lathe([(0.0, L / 2 + r)] + prof + [(0.0, -L / 2 - r)], min(int(n("radialSegments", 8)) * 2, 48))
     elif t == "LatheGeometry":
         pts = [q.v()[:2] for q in it_items(p.get("points"))] or [[0, 0], [1, 0]]
-        v, f = S._lathe([(a, b) for a, b in pts], min(max(int(n("segments", 12)), 3), 96))
+        v, f = S._lathe([(a, b) for a, b in pts], min(max(int(n("segments", 12)), 3), 96), n("phiStart", 0.0),
+                        n("phiLength", 2 * math.pi))
     elif t == "TorusKnotGeometry":
         v, f = _knot(n("radius", 1), n("tube", 0.4), min(int(n("tubularSegments", 64)), 128),
                      min(int(n("radialSegments", 8)), 16), n("p", 2), n("q", 3))
@@ -4677,6 +4681,52 @@ def _baked(gtype, verts, faces=None, params=None):
         g.buffer["__index"] = BufferAttribute([float(i) for f in faces for i in f], 1)
     g.baked = True
     return g
+
+
+_PHI = (1 + math.sqrt(5)) / 2
+_PLATONIC_VERTS = {
+    "TetrahedronGeometry": [(1, 1, 1), (-1, -1, 1), (-1, 1, -1), (1, -1, -1)],
+    "OctahedronGeometry": [(1, 0, 0), (-1, 0, 0), (0, 1, 0), (0, -1, 0), (0, 0, 1), (0, 0, -1)],
+    "IcosahedronGeometry": [(sx, sy * _PHI, 0) for sx in (-1, 1) for sy in (-1, 1)] +
+                           [(0, sx, sy * _PHI) for sx in (-1, 1) for sy in (-1, 1)] +
+                           [(sy * _PHI, 0, sx) for sx in (-1, 1) for sy in (-1, 1)],
+    "DodecahedronGeometry": [(a, b, c) for a in (-1, 1) for b in (-1, 1) for c in (-1, 1)] +
+                            [(0, a / _PHI, b * _PHI) for a in (-1, 1) for b in (-1, 1)] +
+                            [(a / _PHI, b * _PHI, 0) for a in (-1, 1) for b in (-1, 1)] +
+                            [(a * _PHI, 0, b / _PHI) for a in (-1, 1) for b in (-1, 1)],
+}
+
+
+def _subdivided_sphere_mesh(pts, tris, radius, detail):
+    """Split every triangle into (detail + 1)^2 and push every vertex out to the sphere of the radius."""
+    n = detail + 1
+    verts, faces = [], []
+    for a, b, c in tris:
+        a, b, c = pts[a], pts[b], pts[c]
+        grid = {}
+        for r in range(n + 1):
+            for k in range(n + 1 - r):
+                q = [a[j] + (b[j] - a[j]) * r / n + (c[j] - a[j]) * k / n for j in range(3)]
+                grid[(r, k)] = len(verts)
+                verts.append([x * radius for x in _unit(q)])
+        for r in range(n):
+            for k in range(n - r):
+                faces.append((grid[(r, k)], grid[(r + 1, k)], grid[(r, k + 1)]))
+                if k + 1 <= n - r - 1:
+                    faces.append((grid[(r + 1, k)], grid[(r + 1, k + 1)], grid[(r, k + 1)]))
+    return verts, faces
+
+
+def _platonic(gtype, radius, detail):
+    """A Platonic solid inscribed in the sphere of the radius (its faces triangulated from the convex hull of
+    its vertices), optionally subdivided toward the sphere."""
+    import torch
+    from scipy.spatial import ConvexHull
+    pts = [list(map(float, q)) for q in _PLATONIC_VERTS[gtype]]
+    hull = ConvexHull(pts)
+    verts, faces = _subdivided_sphere_mesh(pts, [tuple(int(i) for i in t) for t in hull.simplices],
+                                           radius, max(0, min(int(detail), 5)))
+    return torch.tensor(verts, dtype=torch.float32), torch.tensor(faces, dtype=torch.long).view(-1, 3)
 
 
 def _polyhedron(x):

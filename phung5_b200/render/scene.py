@@ -27,34 +27,77 @@ def _box(w=1, h=1, d=1, **_):
     return v, torch.tensor(f)
 
 
-def _lathe(profile: List[Tuple[float, float]], seg: int):
-    """Surface of revolution around y: profile [(radius, y)]."""
-    verts, faces = [], []
+def _grid_faces(rows: int, cols: int, offset: int = 0):
+    """Two triangles per cell of a (rows + 1) x (cols + 1) vertex grid stored row by row."""
+    faces = []
+    w = cols + 1
+    for r in range(rows):
+        for c in range(cols):
+            a, b = offset + r * w + c, offset + r * w + c + 1
+            d, e = a + w, b + w
+            faces += [(a, d, b), (b, d, e)]
+    return faces
+
+
+def _lathe(profile: List[Tuple[float, float]], seg: int, phiStart: float = 0.0, phiLength: float = 2 * math.pi):
+    """Surface of revolution around y of a profile [(radius, y)], over azimuths phiStart .. phiStart + phiLength
+    (x = r sin(phi), z = r cos(phi), as three.js's LatheGeometry)."""
+    seg = max(1, int(seg))
+    verts = []
     for (r, y) in profile:
-        for i in range(seg):
-            a = 2 * math.pi * i / seg
+        for i in range(seg + 1):
+            a = phiStart + phiLength * i / seg
             verts.append((r * math.sin(a), y, r * math.cos(a)))
-    for j in range(len(profile) - 1):
-        for i in range(seg):
-            a, b = j * seg + i, j * seg + (i + 1) % seg
-            c, d = a + seg, b + seg
-            faces += [(a, b, d), (a, d, c)]
-    return torch.tensor(verts, dtype=torch.float32), torch.tensor(faces)
+    faces = _grid_faces(len(profile) - 1, seg)
+    return torch.tensor(verts, dtype=torch.float32), torch.tensor(faces, dtype=torch.long).view(-1, 3)
 
 
-def _sphere(radius=1, widthSegments=24, heightSegments=12, **_):
-    prof = [(radius * math.sin(math.pi * k / heightSegments), radius * math.cos(math.pi * k / heightSegments))
-            for k in range(heightSegments + 1)]
-    return _lathe(prof, max(3, int(widthSegments)))
+def _sphere(radius=1, widthSegments=24, heightSegments=12, phiStart=0.0, phiLength=2 * math.pi, thetaStart=0.0,
+            thetaLength=math.pi, **_):
+    """A sphere patch: polar angle theta from +y over thetaStart .. +thetaLength, azimuth phi over phiStart ..
+    +phiLength (three.js's SphereGeometry: x = -r cos(phi) sin(theta), y = r cos(theta), z = r sin(phi) sin(theta))."""
+    W, H = max(3, int(widthSegments)), max(2, int(heightSegments))
+    verts = []
+    for iy in range(H + 1):
+        th = thetaStart + thetaLength * iy / H
+        for ix in range(W + 1):
+            ph = phiStart + phiLength * ix / W
+            verts.append((-radius * math.cos(ph) * math.sin(th), radius * math.cos(th),
+                          radius * math.sin(ph) * math.sin(th)))
+    return torch.tensor(verts, dtype=torch.float32), torch.tensor(_grid_faces(H, W), dtype=torch.long).view(-1, 3)
 
 
-def _cylinder(radiusTop=1, radiusBottom=1, height=1, radialSegments=24, **_):
+def _cylinder(radiusTop=1, radiusBottom=1, height=1, radialSegments=24, heightSegments=1, openEnded=False,
+              thetaStart=0.0, thetaLength=2 * math.pi, **_):
+    """A (truncated) cone's side over thetaStart .. +thetaLength (x = r sin(theta), z = r cos(theta)), radius
+    interpolated from the top (+height/2) to the bottom, plus the two caps unless openEnded."""
+    R, Hs = max(3, int(radialSegments)), max(1, int(heightSegments))
     h = height / 2
-    return _lathe([(0.0, h), (radiusTop, h), (radiusBottom, -h), (0.0, -h)], max(3, int(radialSegments)))
+    verts = []
+    for iy in range(Hs + 1):
+        v = iy / Hs
+        r = radiusTop + (radiusBottom - radiusTop) * v
+        y = h - height * v
+        for ix in range(R + 1):
+            t = thetaStart + thetaLength * ix / R
+            verts.append((r * math.sin(t), y, r * math.cos(t)))
+    faces = _grid_faces(Hs, R)
+    if not openEnded:
+        for r, y in ((radiusTop, h), (radiusBottom, -h)):
+            if r <= 0:
+                continue
+            c = len(verts)
+            verts.append((0.0, y, 0.0))
+            for ix in range(R + 1):
+                t = thetaStart + thetaLength * ix / R
+                verts.append((r * math.sin(t), y, r * math.cos(t)))
+            faces += [(c, c + 1 + ix, c + 2 + ix) for ix in range(R)]
+    return torch.tensor(verts, dtype=torch.float32), torch.tensor(faces, dtype=torch.long).view(-1, 3)
 
 
-def _cone(radius=1, height=1, radialSegments=24, **_):
-    return _cylinder(0.0, radius, height, radialSegments)
+def _cone(radius=1, height=1, radialSegments=24, heightSegments=1, openEnded=False, thetaStart=0.0,
+          thetaLength=2 * math.pi, **_):
+    return _cylinder(0.0, radius, height, radialSegments, heightSegments, openEnded, thetaStart, thetaLength)
 
 
 def _plane(width=1, height=1, **_):
@@ -62,20 +105,17 @@ def _plane(width=1, height=1, **_):
     return torch.tensor([[-x, -y, 0], [x, -y, 0], [x, y, 0], [-x, y, 0]], dtype=torch.float32), torch.tensor([(0, 1, 2), (0, 2, 3)])
 
 
-def _torus(radius=1, tube=0.4, radialSegments=12, tubularSegments=32, **_):
-    verts, faces = [], []
-    R, T = int(radialSegments), int(tubularSegments)
-    for j in range(R):
-        for i in range(T):
-            u, v = 2 * math.pi * i / T, 2 * math.pi * j / R
+def _torus(radius=1, tube=0.4, radialSegments=12, tubularSegments=32, arc=2 * math.pi, **_):
+    """A torus in the xy plane around z, swept over 0 .. arc (three.js's TorusGeometry)."""
+    R, T = max(2, int(radialSegments)), max(3, int(tubularSegments))
+    verts = []
+    for j in range(R + 1):
+        v = 2 * math.pi * j / R
+        for i in range(T + 1):
+            u = arc * i / T
             verts.append(((radius + tube * math.cos(v)) * math.cos(u), (radius + tube * math.cos(v)) * math.sin(u),
                           tube * math.sin(v)))
-    for j in range(R):
-        for i in range(T):
-            a, b = j * T + i, j * T + (i + 1) % T
-            c, d = ((j + 1) % R) * T + i, ((j + 1) % R) * T + (i + 1) % T
-            faces += [(a, b, d), (a, d, c)]
-    return torch.tensor(verts, dtype=torch.float32), torch.tensor(faces)
+    return torch.tensor(verts, dtype=torch.float32), torch.tensor(_grid_faces(R, T), dtype=torch.long).view(-1, 3)
 
 
 _PRIMS = {"BoxGeometry": _box, "SphereGeometry": _sphere, "CylinderGeometry": _cylinder, "ConeGeometry": _cone,

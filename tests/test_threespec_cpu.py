@@ -153,3 +153,20 @@ def test_math_random_is_repaired_with_a_seeded_generator():
     assert a.ok and "random" in a.repaired and "Math.random" not in a.code
     mats = [[c["matrix"] for c in r.scene["object"]["children"]] for r in (a, b)]
     assert mats[0] == mats[1] and len({m[12] for m in mats[0]}) > 1      # deterministic, and the draws differ
+
+
+@pytest.mark.parametrize("gtype,params,lo,hi", [
+    ("SphereGeometry", {"radius": 1.0, "thetaLength": np.pi / 2}, [-1, 0, -1], [1, 1, 1]),          # dome
+    ("SphereGeometry", {"radius": 1.0, "phiLength": np.pi}, [-1, -1, 0], [1, 1, 1]),                # half, z >= 0
+    ("CylinderGeometry", {"radiusTop": 1.0, "radiusBottom": 1.0, "height": 1.0, "thetaLength": np.pi,
+                          "openEnded": True}, [0, -0.5, -1], [1, 0.5, 1]),
+    ("ConeGeometry", {"radius": 0.5, "height": 2.0, "thetaStart": np.pi / 2, "thetaLength": np.pi},
+     [-0.5, -1, -0.5], [0.5, 1, 0]),
+    ("TorusGeometry", {"radius": 1.0, "tube": 0.2, "arc": np.pi}, [-1.2, 0, -0.2], [1.2, 1.2, 0.2]),
+    ("IcosahedronGeometry", {"radius": 1.0, "detail": 0.0}, [-0.851] * 3, [0.851] * 3),
+])
+def test_partial_primitives_follow_their_angle_parameters(gtype, params, lo, hi):
+    v, f = jsvm.geometry_mesh(jsvm.Geometry(gtype, params))
+    np.testing.assert_allclose(v.min(0).values.numpy(), lo, atol=2e-3)
+    np.testing.assert_allclose(v.max(0).values.numpy(), hi, atol=2e-3)
+    assert f.shape[0] > 0 and int(f.max()) < v.shape[0]
