@@ -3680,7 +3680,37 @@ class Shape(Host):
             self.pts.append([cx + r * math.cos(a), cy + r * math.sin(a)])
         return self
 
+    def _ellipse(self, x, absolute):
+        """absellipse / ellipse(aX, aY, xRadius, yRadius, aStartAngle, aEndAngle, aClockwise, aRotation)."""
+        names = ("aX", "aY", "xRadius", "yRadius", "aStartAngle", "aEndAngle", "aClockwise", "aRotation")
+        defaults = (0.0, 0.0, 1.0, 1.0, 0.0, 2 * math.pi, False, 0.0)
+        p = {}
+        for k, (nm, d) in enumerate(zip(names, defaults)):
+            v = _arg(x, k)
+            p[nm] = d if v is UNDEF else (_truthy(v) if nm == "aClockwise" else _to_num(v))
+        if not absolute and self.pts:
+            p["aX"] += self.pts[-1][0]
+            p["aY"] += self.pts[-1][1]
+        for k in range(33):
+            self.pts.append(_ellipse_point(p, k / 32))
+        return self
+
+    def _spline(self, x):
+        pts = ([self.pts[-1]] if self.pts else []) + [q.v()[:2] for q in it_items(_arg(x, 0)) if isinstance(q, Vec)]
+        if len(pts) >= 2:
+            c = Curve("catmull", pts, dim=2)
+            n = 8 * (len(pts) - 1)
+            self.pts += [c.point(k / n) for k in range(1, n + 1)]
+        return self
+
     js_methods = {
+        "absellipse": lambda s, i, x: s._ellipse(x, True),
+        "ellipse": lambda s, i, x: s._ellipse(x, False),
+        "splineThru": lambda s, i, x: s._spline(x),
+        "getSpacedPoints": lambda s, i, x: JSArray([Vec(("x", "y"), p, "Vector2") for p in s.pts]),
+        "extractPoints": lambda s, i, x: JSObject({
+            "shape": JSArray([Vec(("x", "y"), p, "Vector2") for p in s.pts]),
+            "holes": JSArray([JSArray([Vec(("x", "y"), p, "Vector2") for p in h.pts]) for h in s.holes_])}),
         "moveTo": lambda s, i, x: (s.pts.append([_num_arg(x, 0), _num_arg(x, 1)]), s)[-1],
         "lineTo": lambda s, i, x: (s.pts.append([_num_arg(x, 0), _num_arg(x, 1)]), s)[-1],
         "quadraticCurveTo": lambda s, i, x: s._quad(x),
@@ -3699,6 +3729,17 @@ class _HolesProxy(Host):
     def __init__(self, shape):
         super().__init__({})
         self.shape = shape
+
+    def get_special(self, it, key):
+        if key == "length":
+            return float(len(self.shape.holes_))
+        k = _index(key)
+        if k is not None:
+            return self.shape.holes_[k] if k < len(self.shape.holes_) else UNDEF
+        return super().get_special(it, key)
+
+    def iterable(self):
+        return list(self.shape.holes_)
 
     js_methods = {"push": lambda s, i, x: (s.shape.holes_.extend(v for v in x if isinstance(v, Shape)),
                                            float(len(s.shape.holes_)))[-1]}
@@ -4073,23 +4114,34 @@ def geometry_mesh(g: Geometry):
             raise _Throw(_error_obj("TypeError", "TubeGeometry needs a Curve path"))
         v, f = _tube(path, min(int(n("tubularSegments", 64)), 256), n("radius", 1), min(int(n("radialSegments", 8)), 24))
     elif t in ("ExtrudeGeometry", "ShapeGeometry"):
+        from . import extrude as X
         shapes = p.get("shapes")
         shapes = it_items(shapes) if isinstance(shapes, JSArray) else [shapes]
-        depth = 0.0
         opts = p.get("options")
+        o = opts.props if isinstance(opts, JSObject) else {}
+
+        def opt(key, d):
+            v = o.get(key, UNDEF)
+            return d if v is UNDEF or v is None else v
         if t == "ExtrudeGeometry":
-            depth = _to_num(opts.props.get("depth", opts.props.get("amount", 1.0))) if isinstance(opts, JSObject) else 1.0
+            depth = _to_num(opt("depth", opt("amount", 1.0)))
+            bevel = _truthy(opt("bevelEnabled", True))
+            thick = _to_num(opt("bevelThickness", 0.2))
+            size = _to_num(opt("bevelSize", thick - 0.1))
+            kw = dict(depth=depth, bevel=bevel, thickness=thick, size=size, offset=_to_num(opt("bevelOffset", 0.0)),
+                      segments=int(_to_num(opt("bevelSegments", 3))))
+        else:
+            kw = dict(depth=0.0, bevel=False)
         vs, fs, off = [], [], 0
         for sh in shapes:
             if isinstance(sh, Shape) and len(sh.pts) >= 3:
-                vv, ff = _extrude(sh.pts, depth)
-                vs.append(vv)
-                fs.append(ff + off)
-                off += vv.shape[0]
-        if not vs:
-            v, f = torch.zeros(0, 3), torch.zeros(0, 3, dtype=torch.long)
-        else:
-            v, f = torch.cat(vs), torch.cat(fs)
+                vv, ff = X.extrude(sh.pts, [h.pts for h in sh.holes_ if len(h.pts) >= 3], **kw)
+                if vv:
+                    vs += vv
+                    fs += [(a + off, b + off, c + off) for a, b, c in ff]
+                    off += len(vv)
+        v = torch.tensor(vs, dtype=torch.float32).view(-1, 3)
+        f = torch.tensor(fs, dtype=torch.long).view(-1, 3)
     elif t == "BufferGeometry":
         pos = g.buffer.get("position")
         if not isinstance(pos, BufferAttribute) or pos.item < 2:
@@ -4168,57 +4220,6 @@ def _tube(curve: Curve, tseg, radius, rseg):
             a, b = k * rseg + j, k * rseg + (j + 1) % rseg
             faces += [(a, b, b + rseg), (a, b + rseg, a + rseg)]
     return torch.tensor(verts, dtype=torch.float32), torch.tensor(faces)
-
-
-def _extrude(pts, depth):
-    """Ear-clipped cap(s) plus side walls of a simple polygon in the xy plane, extruded along +z."""
-    import torch
-    poly = [tuple(p) for p in pts]
-    if len(poly) > 1 and poly[0] == poly[-1]:
-        poly = poly[:-1]
-    area = sum(poly[i][0] * poly[(i + 1) % len(poly)][1] - poly[(i + 1) % len(poly)][0] * poly[i][1]
-               for i in range(len(poly)))
-    if area < 0:
-        poly = poly[::-1]
-    tri = _ear_clip(poly)
-    n = len(poly)
-    verts = [(x, y, 0.0) for x, y in poly] + [(x, y, depth) for x, y in poly]
-    faces = [(c, b, a) for a, b, c in tri] + [(a + n, b + n, c + n) for a, b, c in tri]
-    if depth != 0.0:
-        for i in range(n):
-            j = (i + 1) % n
-            faces += [(i, j, j + n), (i, j + n, i + n)]
-    return torch.tensor(verts, dtype=torch.float32), torch.tensor(faces, dtype=torch.long)
-
-
-def _ear_clip(poly):
-    idx = list(range(len(poly)))
-    out = []
-
-    def inside(p, a, b, c):
-        def s(p1, p2, p3):
-            return (p1[0] - p3[0]) * (p2[1] - p3[1]) - (p2[0] - p3[0]) * (p1[1] - p3[1])
-        d1, d2, d3 = s(p, a, b), s(p, b, c), s(p, c, a)
-        return not ((d1 < 0 or d2 < 0 or d3 < 0) and (d1 > 0 or d2 > 0 or d3 > 0))
-
-    guard = 0
-    while len(idx) > 3 and guard < 10000:
-        guard += 1
-        for k in range(len(idx)):
-            i0, i1, i2 = idx[k - 1], idx[k], idx[(k + 1) % len(idx)]
-            a, b, c = poly[i0], poly[i1], poly[i2]
-            if (b[0] - a[0]) * (c[1] - a[1]) - (b[1] - a[1]) * (c[0] - a[0]) <= 0:
-                continue
-            if any(inside(poly[j], a, b, c) for j in idx if j not in (i0, i1, i2)):
-                continue
-            out.append((i0, i1, i2))
-            idx.pop(k)
-            break
-        else:
-            break
-    if len(idx) == 3:
-        out.append(tuple(idx))
-    return out
 
 
 @dataclass

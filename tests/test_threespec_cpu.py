@@ -170,3 +170,34 @@ def test_partial_primitives_follow_their_angle_parameters(gtype, params, lo, hi)
     np.testing.assert_allclose(v.min(0).values.numpy(), lo, atol=2e-3)
     np.testing.assert_allclose(v.max(0).values.numpy(), hi, atol=2e-3)
     assert f.shape[0] > 0 and int(f.max()) < v.shape[0]
+
+
+def _cap_area(v, f):
+    import torch
+    tri = v[f]
+    n = torch.cross(tri[:, 1] - tri[:, 0], tri[:, 2] - tri[:, 0], dim=1)
+    top = tri[:, :, 2].min(1).values > float(v[:, 2].max()) - 1e-6
+    return float(n[top].norm(dim=1).sum() / 2)
+
+
+def test_extrude_holes_and_default_bevel():
+    r = jsvm.run_module("""export default function generate(THREE) {
+      const g = new THREE.Group();
+      const s = new THREE.Shape(); s.moveTo(-1, -1); s.lineTo(1, -1); s.lineTo(1, 1); s.lineTo(-1, 1); s.lineTo(-1, -1);
+      const h = new THREE.Path(); h.absellipse(0, 0, 0.5, 0.5, 0, Math.PI * 2, false, 0); s.holes.push(h);
+      g.userData.n = s.holes.length;
+      g.add(new THREE.Mesh(new THREE.ExtrudeGeometry(s)));                                   // three.js's defaults
+      g.add(new THREE.Mesh(new THREE.ExtrudeGeometry(s, { depth: 0.5, bevelEnabled: false })));
+      g.add(new THREE.Mesh(new THREE.ShapeGeometry(s)));
+      return g; }""", jsvm.Limits(steps=2_000_000, seconds=10))
+    assert r.error is None, r.error
+    meshes = r.root.props["children"].items
+    bev, flat_ext, flat = (jsvm.geometry_mesh(m.props["geometry"]) for m in meshes)
+    # the default bevel: 0.1 wider in x / y, 0.2 thicker on both sides of the unit depth
+    np.testing.assert_allclose(bev[0].min(0).values.numpy(), [-1.1, -1.1, -0.2], atol=1e-5)
+    np.testing.assert_allclose(bev[0].max(0).values.numpy(), [1.1, 1.1, 1.2], atol=1e-5)
+    np.testing.assert_allclose(flat_ext[0].max(0).values.numpy(), [1, 1, 0.5], atol=1e-6)
+    hole = np.pi * 0.25
+    for v, f in (bev, flat_ext, flat):
+        assert _cap_area(v, f) == pytest.approx(4 - hole, rel=0.01)      # the hole is cut out of both caps
+    assert float(r.root.props["userData"].props["n"]) == 1
