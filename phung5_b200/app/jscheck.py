@@ -479,9 +479,9 @@ def static_analyze(prog) -> List[Dict[str, str]]:
 # --------------------------------------------------------------------------------------------- post-validation
 
 
-def declared_vertices(g) -> int:
+def declared_vertices(g, n_triangles: int = 0) -> int:
     """Vertex count three.js would build for a primitive's parameters (the preview mesh caps segments, the
-    limit must not)."""
+    limit must not). Non-indexed three.js geometries (polyhedra, extrusions) count three vertices per triangle."""
     p = g.params
 
     def n(k, d):
@@ -498,7 +498,17 @@ def declared_vertices(g) -> int:
         return (n("widthSegments", 32) + 1) * (n("heightSegments", 16) + 1)
     if t in ("CylinderGeometry", "ConeGeometry"):
         r = n("radialSegments", 32)
-        return (r + 1) * (n("heightSegments", 1) + 1) + 2 * (2 * r + 1)
+        caps = 0
+        if not jsvm._truthy(p.get("openEnded", False)):
+            radii = ((jsvm._to_num(p.get("radiusTop", 1.0)), jsvm._to_num(p.get("radiusBottom", 1.0)))
+                     if t == "CylinderGeometry" else (0.0, 1.0))
+            caps = sum(1 for x in radii if x > 0)
+        return (r + 1) * (n("heightSegments", 1) + 1) + caps * (2 * r + 1)
+    faces = {"TetrahedronGeometry": 4, "OctahedronGeometry": 8, "IcosahedronGeometry": 20, "DodecahedronGeometry": 36}
+    if t in faces:
+        return 3 * faces[t] * (n("detail", 0) + 1) ** 2
+    if t in ("ExtrudeGeometry", "PolyhedronGeometry"):
+        return 3 * n_triangles
     if t == "PlaneGeometry":
         return (n("widthSegments", 1) + 1) * (n("heightSegments", 1) + 1)
     if t == "TorusGeometry":
@@ -551,8 +561,8 @@ def post_validate(root) -> tuple:
         g = o.props.get("geometry")
         if isinstance(g, jsvm.Geometry) and o.otype in ("Mesh", "InstancedMesh", "LineSegments", "Points", "Line"):
             try:
-                v, _ = jsvm.geometry_mesh(g)
-                nv = max(int(v.shape[0]), declared_vertices(g))
+                v, tris = jsvm.geometry_mesh(g)
+                nv = max(int(v.shape[0]), declared_vertices(g, int(tris.shape[0])))
                 if v.numel() and not bool(v.isfinite().all()):
                     bad_numbers = True
             except jsvm._Throw as e:

@@ -201,3 +201,17 @@ def test_extrude_holes_and_default_bevel():
     for v, f in (bev, flat_ext, flat):
         assert _cap_area(v, f) == pytest.approx(4 - hole, rel=0.01)      # the hole is cut out of both caps
     assert float(r.root.props["userData"].props["n"]) == 1
+
+
+def test_vertex_counts_follow_three_js():
+    from phung5_b200.app.jscheck import declared_vertices
+    G = jsvm.Geometry
+    assert declared_vertices(G("ConeGeometry", {"radius": 1.0})) == 33 * 2 + 65          # one cap
+    assert declared_vertices(G("CylinderGeometry", {"openEnded": True})) == 33 * 2       # no caps
+    assert declared_vertices(G("CylinderGeometry", {})) == 33 * 2 + 2 * 65
+    assert declared_vertices(G("IcosahedronGeometry", {"detail": 2.0})) == 60 * 9        # non-indexed
+    c = JSChecker(_inline=True)
+    src = ("export default function generate(THREE) { const g = new THREE.Group(); g.add(new THREE.Mesh("
+           "new THREE.IcosahedronGeometry(0.5, %d), new THREE.MeshStandardMaterial())); return g; }")
+    assert c.check(src % 60).ok                                    # 223,260 vertices
+    assert "VERTEX_LIMIT_EXCEEDED" in {f["rule"] for f in c.check(src % 70).failures}   # 302,460
