@@ -52,6 +52,7 @@ class Request:
     dlen: int = 0             # positions with draft KV written
     out: List[int] = field(default_factory=list)
     finished: bool = False
+    finish_reason: Optional[str] = None
     steps: int = 0
     accepted: List[int] = field(default_factory=list)
     t_arrive: float = 0.0
@@ -67,6 +68,7 @@ class StepOutput:
     rid: int
     new_tokens: List[int]
     finished: bool
+    finish_reason: Optional[str] = None     # "stop" (a stop token), "length" (max tokens or context), "abort"
 
 
 class _VocabOps:
@@ -444,12 +446,40 @@ class LLMEngine:
     def _emit(self, r: Request, new: List[int]) -> StepOutput:
         room = r.params.max_new_tokens - len(r.out)
         new = new[:room]
+        stop = r.params.stop_token_ids
+        hit = False
+        if stop:
+            for k, t in enumerate(new):
+                if t in stop:                  # the stop token ends the output and is not part of it
+                    new, hit = new[:k], True
+                    break
         r.out += new
         self.stats["tokens_out"] += len(new)
-        done = len(r.out) >= r.params.max_new_tokens or r.committed + self.N + 2 * self.ps >= self.max_context
+        done = hit or len(r.out) >= r.params.max_new_tokens or r.committed + self.N + 2 * self.ps >= self.max_context
         if done:
+            r.finish_reason = "stop" if hit else "length"
             self._finish(r)
-        return StepOutput(r.rid, new, done)
+        return StepOutput(r.rid, new, done, r.finish_reason)
+
+    def abort(self, rid: int) -> bool:
+        """End a request now (client gone, stop string seen): its pages are released (full ones kept in the
+        prefix cache). False if it is unknown or already finished."""
+        r = self.reqs.get(rid)
+        if r is None or r.finished:
+            return False
+        if any(x is r for x in self.waiting):
+            self.waiting = [x for x in self.waiting if x is not r]
+            if self.hybrid and r.gslot >= 0:
+                self.gdn_pool.release(r.gslot)
+                r.gslot = -1
+            self.pool.prefix.release(r.pages)
+            r.pages = []
+            r.finished = True
+            r.t_done = time.perf_counter()
+        else:
+            self._finish(r)
+        r.finish_reason = "abort"
+        return True
 
     def _first_token(self, logits: torch.Tensor, reqs: List[Request]) -> List[int]:
         full = self.vocab.full(logits)

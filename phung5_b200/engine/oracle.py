@@ -33,6 +33,7 @@ class SamplingParams:
     top_p: float = 1.0
     seed: int = 42
     max_new_tokens: int = 64
+    stop_token_ids: tuple = ()      # generation ends at the first of these (not emitted); e.g. the EOS id
 
 
 def _probs(logits: torch.Tensor, sp: SamplingParams) -> torch.Tensor:

@@ -7,7 +7,9 @@ per-request streams. Endpoints mirror what the reference's clients use of SGLang
 
   GET  /health                      200 while serving, 503 while asleep or after an engine error
   GET  /v1/models
-  POST /v1/completions              prompt: str | [int]; max_tokens, temperature, top_p, top_k, seed, stream
+  POST /v1/completions              prompt: str | [int]; max_tokens, temperature, top_p, top_k, seed, stream, stop
+                                    (strings), stop_token_ids, ignore_eos (generation ends at the tokenizer's EOS
+                                    otherwise); finish_reason "stop" / "length"; a caller that goes away aborts
   POST /v1/chat/completions         messages (chat template of the tokenizer); same sampling fields; with a vision
                                     tower, `image_url` content parts (data URLs) -- sent once with a `uuid`, later
                                     by `uuid` alone; an unknown uuid answers 400 so the client resends in full
@@ -47,6 +49,7 @@ class _Pending:
     loop: asyncio.AbstractEventLoop
     rid: int = -1
     mm: Optional[list] = None          # image inputs: [(position, features [n, H])]
+    cancelled: bool = False            # the caller went away before the engine took the request
 
 
 class AsyncEngine:
@@ -88,16 +91,24 @@ class AsyncEngine:
                         subs.append(self._submit.get_nowait())
                     except queue.Empty:
                         break
+                subs = [p for p in subs if not p.cancelled]
+                # aborts name engine request ids, so every rank drops the same request
+                ops = [(op, (a.rid,) if op == "abort" else a, fut, loop) for op, a, fut, loop in ops
+                       if not (op == "abort" and a.rid < 0)]
                 if self.group is not None:
-                    _broadcast_cmds({"ops": [o[0] for o in ops],
+                    _broadcast_cmds({"ops": [(o[0], o[1]) for o in ops],
                                      "reqs": [(p.prompt, p.params, _mm_to_host(p.mm)) for p in subs],
                                      "steps": self.steps, "stop": False}, self.group)
-                for op, fut, loop in ops:
+                for op, args, fut, loop in ops:
                     try:
-                        getattr(eng, op)()
-                        loop.call_soon_threadsafe(fut.set_result, True)
+                        getattr(eng, op)(*args)
+                        if op == "abort":
+                            self._streams.pop(args[0], None)
+                        if fut is not None:
+                            loop.call_soon_threadsafe(fut.set_result, True)
                     except Exception as e:  # pragma: no cover - surfaced to the caller
-                        loop.call_soon_threadsafe(fut.set_exception, e)
+                        if fut is not None:
+                            loop.call_soon_threadsafe(fut.set_exception, e)
                 for p in subs:
                     p.rid = eng.add_request(p.prompt, p.params, mm=p.mm)
                     self._streams[p.rid] = p
@@ -114,34 +125,53 @@ class AsyncEngine:
                     p = self._streams.get(o.rid)
                     if p is None:
                         continue
-                    p.loop.call_soon_threadsafe(p.out.put_nowait, o)
+                    if p.cancelled or not _deliver(p, o):
+                        # the caller is gone (its abort may still be queued): drop the request now; every
+                        # tensor-parallel rank learns of it through the abort op that the caller queued
+                        del self._streams[o.rid]
+                        if self.group is None and not o.finished:
+                            eng.abort(o.rid)
+                        continue
                     if o.finished:
                         del self._streams[o.rid]
             except Exception:  # keep serving health; report the error
                 self.error = traceback.format_exc()
                 for p in list(self._streams.values()):
-                    p.loop.call_soon_threadsafe(p.out.put_nowait, None)
+                    _deliver(p, None)
                 self._streams.clear()
                 time.sleep(0.1)
 
     # -- asyncio side ---------------------------------------------------------------------------
     async def generate(self, prompt: List[int], params: SamplingParams, mm: Optional[list] = None) -> AsyncIterator:
+        """Stream a request's StepOutputs; a caller that stops early (client gone, stop string) aborts it."""
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
-        self._submit.put(_Pending(prompt, params, q, loop, mm=mm))
+        p = _Pending(prompt, params, q, loop, mm=mm)
+        self._submit.put(p)
         self._wake.set()
-        while True:
-            o = await q.get()
-            if o is None:
-                raise RuntimeError(self.error or "engine error")
-            yield o
-            if o.finished:
-                return
+        done = False
+        try:
+            while True:
+                o = await q.get()
+                if o is None:
+                    raise RuntimeError(self.error or "engine error")
+                done = o.finished
+                yield o
+                if o.finished:
+                    return
+        finally:
+            if not done:
+                self.abort(p)
+
+    def abort(self, p: _Pending) -> None:
+        p.cancelled = True
+        self._control.put(("abort", p, None, None))
+        self._wake.set()
 
     async def control(self, op: str):
         loop = asyncio.get_running_loop()
         fut = loop.create_future()
-        self._control.put((op, fut, loop))
+        self._control.put((op, (), fut, loop))
         self._wake.set()
         return await fut
 
@@ -154,6 +184,16 @@ class AsyncEngine:
         self._thread.join(timeout=5)
         if self.group is not None:
             _broadcast_cmds({"ops": [], "reqs": [], "steps": self.steps, "stop": True}, self.group)
+
+
+def _deliver(p: _Pending, item) -> bool:
+    """Hand a step's output to the caller's event loop; False if that loop is gone."""
+    try:
+        p.loop.call_soon_threadsafe(p.out.put_nowait, item)
+        return True
+    except RuntimeError:            # the loop was closed
+        p.cancelled = True
+        return False
 
 
 def _mm_to_host(mm):
@@ -177,8 +217,8 @@ def tp_worker_loop(engine, group) -> None:
             return
         if cmds["steps"] != steps:
             raise RuntimeError(f"TP ranks diverged: rank 0 took {cmds['steps']} steps, this rank {steps}")
-        for op in cmds["ops"]:
-            getattr(engine, op)()
+        for op, args in cmds["ops"]:
+            getattr(engine, op)(*args)
         for prompt, params, mm in cmds["reqs"]:
             engine.add_request(prompt, params, mm=mm)
         if engine.has_work():
@@ -186,12 +226,31 @@ def tp_worker_loop(engine, group) -> None:
             steps += 1
 
 
-def _sampling(body: dict, default_max: int = 256) -> SamplingParams:
+def _sampling(body: dict, default_max: int = 256, eos_id: Optional[int] = None) -> SamplingParams:
+    """Request fields -> SamplingParams; generation stops at the tokenizer's EOS (unless `ignore_eos`) and at any
+    of `stop_token_ids`."""
+    stop = [int(t) for t in (body.get("stop_token_ids") or [])]
+    if eos_id is not None and not body.get("ignore_eos"):
+        stop.append(int(eos_id))
     return SamplingParams(temperature=float(body.get("temperature", 0.0) or 0.0),
                           top_k=int(body.get("top_k", 0) or 0), top_p=float(body.get("top_p", 1.0) or 1.0),
                           seed=int(body.get("seed", 42) if body.get("seed") is not None else 42),
                           max_new_tokens=int(body.get("max_tokens", body.get("max_completion_tokens", default_max))
-                                             or default_max))
+                                             or default_max),
+                          stop_token_ids=tuple(stop))
+
+
+def _stop_strings(body: dict) -> List[str]:
+    s = body.get("stop")
+    if not s:
+        return []
+    return [s] if isinstance(s, str) else [x for x in s if isinstance(x, str) and x]
+
+
+def _cut_at_stop(text: str, stops: List[str]) -> Optional[int]:
+    """Index where the earliest stop string starts in `text`, or None."""
+    hits = [i for i in (text.find(x) for x in stops) if i >= 0]
+    return min(hits) if hits else None
 
 
 class UnknownImage(Exception):
@@ -281,37 +340,60 @@ def build_app(aeng: AsyncEngine, tokenizer, model_name: str = "phung5_b200", vis
         return await _control("wake_up")
 
     async def _complete(ids: List[int], body: dict, chat: bool, mm: Optional[list] = None):
-        sp = _sampling(body)
+        sp = _sampling(body, eos_id=getattr(tokenizer, "eos_id", None))
+        stops = _stop_strings(body)
         rid = f"{'chatcmpl' if chat else 'cmpl'}-{uuid.uuid4().hex[:16]}"
         created = int(time.time())
+
+        async def pieces():
+            """(text delta, token ids, finish reason or None); a stop string ends the text before it and the
+            request (leaving the generator aborts it in the engine)."""
+            toks: List[int] = []
+            sent = 0
+            gen = aeng.generate(ids, sp, mm)
+            try:
+                async for o in gen:
+                    toks += o.new_tokens
+                    text = tokenizer.decode(toks)
+                    cut = _cut_at_stop(text, stops) if stops else None
+                    if cut is not None:
+                        yield text[sent:cut], o.new_tokens, "stop"
+                        return
+                    # hold back a tail that could still grow into a stop string
+                    hold = max((len(x) - 1 for x in stops), default=0)
+                    upto = len(text) if o.finished else max(sent, len(text) - hold)
+                    yield text[sent:upto], o.new_tokens, (o.finish_reason or "length") if o.finished else None
+                    sent = upto
+                    if o.finished:
+                        return
+            finally:
+                await gen.aclose()
+
         if body.get("stream"):
             async def events():
-                n = 0
-                async for o in aeng.generate(ids, sp, mm):
-                    n += len(o.new_tokens)
-                    text = tokenizer.decode(o.new_tokens)
+                async for text, new, fin in pieces():
                     if chat:
                         chunk = {"id": rid, "object": "chat.completion.chunk", "created": created, "model": model_name,
-                                 "choices": [{"index": 0, "delta": {"content": text},
-                                              "finish_reason": "length" if o.finished else None}]}
+                                 "choices": [{"index": 0, "delta": {"content": text}, "finish_reason": fin}]}
                     else:
                         chunk = {"id": rid, "object": "text_completion", "created": created, "model": model_name,
-                                 "choices": [{"index": 0, "text": text, "token_ids": o.new_tokens,
-                                              "finish_reason": "length" if o.finished else None}]}
+                                 "choices": [{"index": 0, "text": text, "token_ids": new, "finish_reason": fin}]}
                     yield f"data: {json.dumps(chunk)}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(events(), media_type="text/event-stream")
-        toks: List[int] = []
-        async for o in aeng.generate(ids, sp, mm):
-            toks += o.new_tokens
-        text = tokenizer.decode(toks)
+        parts, toks, fin = [], [], "length"
+        async for text, new, f in pieces():
+            parts.append(text)
+            toks += new
+            fin = f or fin
+        text = "".join(parts)
         usage = {"prompt_tokens": len(ids), "completion_tokens": len(toks), "total_tokens": len(ids) + len(toks)}
         if chat:
             return {"id": rid, "object": "chat.completion", "created": created, "model": model_name,
                     "choices": [{"index": 0, "message": {"role": "assistant", "content": text},
-                                 "finish_reason": "length"}], "usage": usage}
+                                 "finish_reason": fin}], "usage": usage}
         return {"id": rid, "object": "text_completion", "created": created, "model": model_name,
-                "choices": [{"index": 0, "text": text, "token_ids": toks, "finish_reason": "length"}], "usage": usage}
+                "choices": [{"index": 0, "text": text, "token_ids": toks, "finish_reason": fin}], "usage": usage}
 
     @app.post("/v1/completions")
     async def completions(req: Request):

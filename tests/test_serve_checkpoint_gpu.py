@@ -62,7 +62,7 @@ def test_server_serves_a_safetensors_checkpoint(tmp_path):
             assert time.time() - t0 < 240, "server did not come up"
             time.sleep(1)
         r = httpx.post(f"http://127.0.0.1:{port}/v1/completions",
-                       json={"prompt": prompt, "max_tokens": 16, "temperature": 0}, timeout=120)
+                       json={"prompt": prompt, "max_tokens": 16, "temperature": 0, "ignore_eos": True}, timeout=120)
         assert r.status_code == 200, r.text
         assert r.json()["choices"][0]["token_ids"] == want
     finally:

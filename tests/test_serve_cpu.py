@@ -41,7 +41,7 @@ def served():
 def test_completion_token_ids_match_greedy(served):
     c, ref, _ = served
     prompt = list(range(10, 50))
-    r = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 12, "temperature": 0})
+    r = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 12, "temperature": 0, "ignore_eos": True})
     assert r.status_code == 200
     out = r.json()["choices"][0]["token_ids"]
     assert out == greedy_generate(ref, prompt, 12)
@@ -50,7 +50,7 @@ def test_completion_token_ids_match_greedy(served):
 
 def test_stream_equals_non_stream(served):
     c, _, _ = served
-    body = {"prompt": list(range(60, 90)), "max_tokens": 10, "temperature": 0}
+    body = {"prompt": list(range(60, 90)), "max_tokens": 10, "temperature": 0, "ignore_eos": True}
     full = c.post("/v1/completions", json=body).json()["choices"][0]["token_ids"]
     toks = []
     with c.stream("POST", "/v1/completions", json={**body, "stream": True}) as r:
@@ -118,3 +118,63 @@ def test_load_balanced_client_affinity_and_migration():
     affinity_key.reset(tok)
     lb.set_active([j], False)
     assert lb.pick_index() == i
+
+
+def test_stop_tokens_stop_strings_and_finish_reasons(served):
+    c, ref, aeng = served
+    prompt = list(range(10, 50))
+    want = greedy_generate(ref, prompt, 12)
+    stop_tok = want[5]
+    k = want.index(stop_tok)
+    r = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 12, "temperature": 0, "ignore_eos": True,
+                                        "stop_token_ids": [stop_tok]}).json()["choices"][0]
+    assert r["token_ids"] == want[:k] and r["finish_reason"] == "stop"
+    r = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 12, "temperature": 0,
+                                        "ignore_eos": True}).json()["choices"][0]
+    assert r["finish_reason"] == "length"
+    text = ByteTokenizer().decode(want)
+    stop = text[3:5] if len(text) >= 5 else None
+    if stop:
+        r = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 12, "temperature": 0,
+                                            "ignore_eos": True, "stop": [stop]}).json()["choices"][0]
+        assert r["finish_reason"] == "stop" and r["text"] == text[:text.find(stop)]
+
+
+def test_engine_abort_releases_the_request():
+    eng, _ = _engine()
+    free0 = eng.pool.alloc.available() + len(eng.pool.prefix.lru)
+    rid = eng.add_request(list(range(5, 60)), __import__("phung5_b200.engine.oracle", fromlist=["x"]).SamplingParams(
+        max_new_tokens=50))
+    eng.step()
+    eng.step()
+    assert eng.reqs[rid].pages
+    assert eng.abort(rid) and eng.reqs[rid].finish_reason == "abort" and not eng.abort(rid)
+    assert not eng.has_work()
+    assert eng.pool.alloc.available() + len(eng.pool.prefix.lru) == free0
+    queued = eng.add_request(list(range(5, 20)), None)
+    assert eng.abort(queued) and not eng.waiting
+
+
+def test_client_going_away_aborts_its_request(served):
+    """A caller that stops reading the stream (the HTTP handler's generator is closed when its client goes
+    away) aborts the engine request."""
+    import asyncio
+    import time as _t
+
+    from phung5_b200.engine.oracle import SamplingParams
+    _, _, aeng = served
+    n0 = len(aeng.engine.reqs)
+
+    async def go():
+        gen = aeng.generate(list(range(20, 60)), SamplingParams(max_new_tokens=400))
+        await gen.__anext__()
+        await gen.aclose()
+    asyncio.run(go())
+    t0 = _t.time()
+    while _t.time() - t0 < 10:
+        reqs = list(aeng.engine.reqs.values())[n0:]
+        if reqs and reqs[-1].finished:
+            break
+        _t.sleep(0.02)
+    r = list(aeng.engine.reqs.values())[n0:][-1]
+    assert r.finished and r.finish_reason == "abort" and len(r.out) < 400
