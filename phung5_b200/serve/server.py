@@ -226,12 +226,12 @@ def tp_worker_loop(engine, group) -> None:
             steps += 1
 
 
-def _sampling(body: dict, default_max: int = 256, eos_id: Optional[int] = None) -> SamplingParams:
-    """Request fields -> SamplingParams; generation stops at the tokenizer's EOS (unless `ignore_eos`) and at any
-    of `stop_token_ids`."""
+def _sampling(body: dict, default_max: int = 256, eos_ids=()) -> SamplingParams:
+    """Request fields -> SamplingParams; generation stops at the tokenizer's end-of-sequence / end-of-turn ids
+    (unless `ignore_eos`) and at any of `stop_token_ids`."""
     stop = [int(t) for t in (body.get("stop_token_ids") or [])]
-    if eos_id is not None and not body.get("ignore_eos"):
-        stop.append(int(eos_id))
+    if not body.get("ignore_eos"):
+        stop += [int(t) for t in eos_ids if t is not None]
     return SamplingParams(temperature=float(body.get("temperature", 0.0) or 0.0),
                           top_k=int(body.get("top_k", 0) or 0), top_p=float(body.get("top_p", 1.0) or 1.0),
                           seed=int(body.get("seed", 42) if body.get("seed") is not None else 42),
@@ -340,7 +340,7 @@ def build_app(aeng: AsyncEngine, tokenizer, model_name: str = "phung5_b200", vis
         return await _control("wake_up")
 
     async def _complete(ids: List[int], body: dict, chat: bool, mm: Optional[list] = None):
-        sp = _sampling(body, eos_id=getattr(tokenizer, "eos_id", None))
+        sp = _sampling(body, eos_ids=getattr(tokenizer, "stop_ids", None) or [getattr(tokenizer, "eos_id", None)])
         stops = _stop_strings(body)
         rid = f"{'chatcmpl' if chat else 'cmpl'}-{uuid.uuid4().hex[:16]}"
         created = int(time.time())
@@ -475,9 +475,10 @@ def main(argv=None):
         from ..models.vision import VisionConfig, VisionEncoder
         vision = VisionEncoder(VisionConfig(out_hidden=model_cfg.hidden), device=device,
                                dtype=torch.bfloat16 if str(device).startswith("cuda") else torch.float32)
-    uvicorn.run(build_app(aeng, __import__("phung5_b200.serve.tokenizer", fromlist=["load_tokenizer"]).load_tokenizer(
-        args.tokenizer), model_cfg.name if args.model_path else args.model, vision=vision), host=args.host,
-        port=args.port, log_level="warning")
+    from .tokenizer import has_tokenizer, load_tokenizer
+    tok_path = args.tokenizer or (args.model_path if has_tokenizer(args.model_path) else None)
+    uvicorn.run(build_app(aeng, load_tokenizer(tok_path), model_cfg.name if args.model_path else args.model,
+                          vision=vision), host=args.host, port=args.port, log_level="warning")
     aeng.shutdown()
 
 

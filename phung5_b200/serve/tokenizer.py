@@ -12,6 +12,7 @@ from typing import List, Optional, Sequence
 class ByteTokenizer:
     bos_id = 256
     eos_id = 257
+    stop_ids = [257]
     vocab_size = 258
 
     def encode(self, text: str, add_bos: bool = False) -> List[int]:
@@ -36,6 +37,7 @@ class HFTokenizer:
         from transformers import AutoTokenizer
         self.tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
         self.eos_id = self.tok.eos_token_id
+        self.stop_ids = sorted(set(([self.eos_id] if self.eos_id is not None else []) + _generation_eos(path)))
         self.vocab_size = len(self.tok)
 
     def encode(self, text: str, add_bos: bool = False) -> List[int]:
@@ -46,6 +48,25 @@ class HFTokenizer:
 
     def apply_chat_template(self, messages: List[dict]) -> str:
         return self.tok.apply_chat_template(messages, tokenize=False, add_generation_prompt=True)
+
+
+def _generation_eos(path: str) -> List[int]:
+    """End-of-turn ids a chat checkpoint lists in generation_config.json (an int or a list)."""
+    import json
+    import os
+    f = os.path.join(path, "generation_config.json")
+    try:
+        with open(f) as fh:
+            v = json.load(fh).get("eos_token_id")
+    except (OSError, ValueError):
+        return []
+    return [int(x) for x in (v if isinstance(v, list) else [v]) if isinstance(x, int)]
+
+
+def has_tokenizer(path: Optional[str]) -> bool:
+    import os
+    return bool(path) and any(os.path.exists(os.path.join(path, f))
+                              for f in ("tokenizer.json", "tokenizer.model", "tokenizer_config.json"))
 
 
 def load_tokenizer(path: Optional[str] = None):
