@@ -2861,6 +2861,12 @@ def _vec_methods():
         "setFromCylindrical": lambda s, i, x: s.setv(_from_cylindrical(*_arg(x, 0).rty())),
         "setFromCylindricalCoords": lambda s, i, x: s.setv(_from_cylindrical(_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2))),
         "setFromMatrixPosition": lambda s, i, x: s.setv([_arg(x, 0).m[r][3] for r in range(3)]),
+        "setFromQuaternion": lambda s, i, x: s.setv(_mat3_to_euler(_arg(x, 0).cur())),
+        "setFromRotationMatrix": lambda s, i, x: s.setv(_mat3_to_euler(_rot_part(_arg(x, 0).m))),
+        "setFromVector3": lambda s, i, x: s.setv(_arg(x, 0).v()[:3]),
+        "setFromMatrixScale": lambda s, i, x: s.setv([math.sqrt(sum(_arg(x, 0).m[r][c] ** 2 for r in range(3)))
+                                                      for c in range(3)]),
+        "setFromMatrixColumn": lambda s, i, x: s.setv([_arg(x, 0).m[r][int(_num_arg(x, 1))] for r in range(3)]),
     }
 
 
@@ -2972,6 +2978,55 @@ def _compose(pos, rot, scl):
             [0.0, 0.0, 0.0, 1.0]]
 
 
+def _m3to4(r):
+    return [list(r[0]) + [0.0], list(r[1]) + [0.0], list(r[2]) + [0.0], [0.0, 0.0, 0.0, 1.0]]
+
+
+def _det4(m):
+    import numpy as np
+    return float(np.linalg.det(np.asarray(m, dtype=np.float64)))
+
+
+def _inv4(m):
+    import numpy as np
+    a = np.asarray(m, dtype=np.float64)
+    if abs(np.linalg.det(a)) < 1e-300:
+        return [[0.0] * 4 for _ in range(4)]
+    return np.linalg.inv(a).tolist()
+
+
+def _decompose(m, pos, quat, scl):
+    sx, sy, sz = (math.sqrt(sum(m[r][c] ** 2 for r in range(3))) for c in range(3))
+    if _det4(m) < 0:
+        sx = -sx
+    if isinstance(pos, Vec):
+        pos.setv([m[0][3], m[1][3], m[2][3]])
+    if isinstance(scl, Vec):
+        scl.setv([sx, sy, sz])
+    if isinstance(quat, Quaternion):
+        ss = (sx or 1.0, sy or 1.0, sz or 1.0)
+        quat.put([[m[r][c] / ss[c] for c in range(3)] for r in range(3)])
+    return None
+
+
+def _look4(m, eye, target, up):
+    """Rotation part of three.js's Matrix4.lookAt: the z axis points from target to eye."""
+    z = [a - b for a, b in zip(eye, target)]
+    if sum(v * v for v in z) == 0:
+        z = [0.0, 0.0, 1.0]
+    z = _unit(z)
+    x = _cross(up, z)
+    if sum(v * v for v in x) == 0:
+        z = _unit([z[0] + 1e-4, z[1], z[2]])
+        x = _cross(up, z)
+    x = _unit(x)
+    y = _cross(z, x)
+    out = [row[:] for row in m]
+    for r in range(3):
+        out[r][0], out[r][1], out[r][2] = x[r], y[r], z[r]
+    return out
+
+
 def _ident4():
     return [[1.0 if r == c else 0.0 for c in range(4)] for r in range(4)]
 
@@ -3010,6 +3065,19 @@ class Matrix4(Host):
         "makeRotationY": lambda s, i, x: s._rot("y", _num_arg(x, 0)),
         "makeRotationZ": lambda s, i, x: s._rot("z", _num_arg(x, 0)),
         "makeRotationFromEuler": lambda s, i, x: (setattr(s, "m", _compose([0, 0, 0], _arg(x, 0).v(), [1, 1, 1])), s)[-1],
+        "makeRotationFromQuaternion": lambda s, i, x: (setattr(s, "m", _m3to4(_arg(x, 0).cur())), s)[-1],
+        "makeRotationAxis": lambda s, i, x: (setattr(s, "m", _m3to4(_axis_mat(_arg(x, 0).v(), _num_arg(x, 1)))), s)[-1],
+        "invert": lambda s, i, x: (setattr(s, "m", _inv4(s.m)), s)[-1],
+        "transpose": lambda s, i, x: (setattr(s, "m", [list(c) for c in zip(*s.m)]), s)[-1],
+        "determinant": lambda s, i, x: _det4(s.m),
+        "decompose": lambda s, i, x: _decompose(s.m, _arg(x, 0), _arg(x, 1), _arg(x, 2)) or s,
+        "lookAt": lambda s, i, x: (setattr(s, "m", _look4(s.m, _arg(x, 0).v(), _arg(x, 1).v(), _arg(x, 2).v())), s)[-1],
+        "extractRotation": lambda s, i, x: (setattr(s, "m", _m3to4(_rot_part(_arg(x, 0).m))), s)[-1],
+        "scale": lambda s, i, x: (setattr(s, "m", [[s.m[r][c] * (_arg(x, 0).v()[c] if c < 3 else 1.0) for c in range(4)]
+                                                   for r in range(4)]), s)[-1],
+        "getMaxScaleOnAxis": lambda s, i, x: max(math.sqrt(sum(s.m[r][c] ** 2 for r in range(3))) for c in range(3)),
+        "makeBasis": lambda s, i, x: (setattr(s, "m", [[_arg(x, 0).v()[r], _arg(x, 1).v()[r], _arg(x, 2).v()[r], 0.0]
+                                                       for r in range(3)] + [[0.0, 0.0, 0.0, 1.0]]), s)[-1],
         "compose": lambda s, i, x: (setattr(s, "m", _compose(_arg(x, 0).v(), _quat_or_euler(_arg(x, 1)), _arg(x, 2).v())), s)[-1],
         "multiply": lambda s, i, x: (setattr(s, "m", _mat_mul(s.m, _arg(x, 0).m)), s)[-1],
         "premultiply": lambda s, i, x: (setattr(s, "m", _mat_mul(_arg(x, 0).m, s.m)), s)[-1],
@@ -3024,28 +3092,128 @@ def _set_pos(m, p):
 
 
 class Quaternion(Host):
-    """Held as a rotation matrix; enough for setFromEuler / setFromAxisAngle / Matrix4.compose."""
-    __slots__ = ("r",)
+    """A rotation, held as a 3x3 matrix. An object's `quaternion` is a live view of its rotation: reads come from
+    the object's Euler angles and every change is written back to them."""
+    __slots__ = ("r", "owner")
     cls_name = "Quaternion"
 
-    def __init__(self):
+    def __init__(self, r=None, owner=None):
         super().__init__({"isQuaternion": True})
-        self.r = _euler_mat([0, 0, 0])
+        self.r = r or _euler_mat([0, 0, 0])
+        self.owner = owner
+
+    def cur(self):
+        if self.owner is not None:
+            self.r = _euler_mat(self.owner.props["rotation"].v())
+        return self.r
+
+    def put(self, r):
+        self.r = [list(map(float, row)) for row in r]
+        if self.owner is not None:
+            self.owner.props["rotation"].setv(_mat3_to_euler(self.r))
+        return self
+
+    def get_special(self, it, key):
+        if key in ("x", "y", "z", "w"):
+            return _m2q(self.cur())["xyzw".index(key)]
+        return super().get_special(it, key)
+
+    def set_special(self, it, key, value):
+        if key in ("x", "y", "z", "w"):
+            q = list(_m2q(self.cur()))
+            q["xyzw".index(key)] = _to_num(value)
+            self.put(_q2m(q))
+            return True
+        return False
 
     js_methods = {
-        "setFromEuler": lambda s, i, x: (setattr(s, "r", _euler_mat(_arg(x, 0).v())), s)[-1],
-        "setFromAxisAngle": lambda s, i, x: (setattr(s, "r", _axis_mat(_arg(x, 0).v(), _num_arg(x, 1))), s)[-1],
-        "identity": lambda s, i, x: (setattr(s, "r", _euler_mat([0, 0, 0])), s)[-1],
-        "multiply": lambda s, i, x: (setattr(s, "r", _mat_mul(s.r, _arg(x, 0).r)), s)[-1],
-        "clone": lambda s, i, x: _quat_copy(s),
-        "copy": lambda s, i, x: (setattr(s, "r", [row[:] for row in _arg(x, 0).r]), s)[-1],
+        "set": lambda s, i, x: s.put(_q2m([_num_arg(x, k) for k in range(4)])),
+        "setFromEuler": lambda s, i, x: s.put(_euler_mat(_arg(x, 0).v())),
+        "setFromAxisAngle": lambda s, i, x: s.put(_axis_mat(_arg(x, 0).v(), _num_arg(x, 1))),
+        "setFromUnitVectors": lambda s, i, x: s.put(_between(_arg(x, 0).v(), _arg(x, 1).v())),
+        "setFromRotationMatrix": lambda s, i, x: s.put(_rot_part(_arg(x, 0).m)),
+        "identity": lambda s, i, x: s.put(_euler_mat([0, 0, 0])),
+        "multiply": lambda s, i, x: s.put(_mat_mul(s.cur(), _arg(x, 0).cur())),
+        "premultiply": lambda s, i, x: s.put(_mat_mul(_arg(x, 0).cur(), s.cur())),
+        "multiplyQuaternions": lambda s, i, x: s.put(_mat_mul(_arg(x, 0).cur(), _arg(x, 1).cur())),
+        "slerp": lambda s, i, x: s.put(_q2m(_slerp(_m2q(s.cur()), _m2q(_arg(x, 0).cur()), _num_arg(x, 1)))),
+        "slerpQuaternions": lambda s, i, x: s.put(_q2m(_slerp(_m2q(_arg(x, 0).cur()), _m2q(_arg(x, 1).cur()),
+                                                              _num_arg(x, 2)))),
+        "invert": lambda s, i, x: s.put([list(c) for c in zip(*s.cur())]),
+        "conjugate": lambda s, i, x: s.put([list(c) for c in zip(*s.cur())]),
+        "normalize": lambda s, i, x: s,
+        "angleTo": lambda s, i, x: 2 * math.acos(min(1.0, abs(sum(a * b for a, b in zip(_m2q(s.cur()),
+                                                                                        _m2q(_arg(x, 0).cur())))))),
+        "dot": lambda s, i, x: sum(a * b for a, b in zip(_m2q(s.cur()), _m2q(_arg(x, 0).cur()))),
+        "toArray": lambda s, i, x: JSArray(list(_m2q(s.cur()))),
+        "clone": lambda s, i, x: Quaternion([row[:] for row in s.cur()]),
+        "copy": lambda s, i, x: s.put([row[:] for row in _arg(x, 0).cur()]),
     }
 
 
+def _m2q(m):
+    """Unit quaternion (x, y, z, w) of a rotation matrix (the largest-diagonal branch is taken for stability)."""
+    t = m[0][0] + m[1][1] + m[2][2]
+    if t > 0:
+        s = 0.5 / math.sqrt(t + 1.0)
+        q = ((m[2][1] - m[1][2]) * s, (m[0][2] - m[2][0]) * s, (m[1][0] - m[0][1]) * s, 0.25 / s)
+    elif m[0][0] > m[1][1] and m[0][0] > m[2][2]:
+        s = 2.0 * math.sqrt(max(1e-30, 1.0 + m[0][0] - m[1][1] - m[2][2]))
+        q = (0.25 * s, (m[0][1] + m[1][0]) / s, (m[0][2] + m[2][0]) / s, (m[2][1] - m[1][2]) / s)
+    elif m[1][1] > m[2][2]:
+        s = 2.0 * math.sqrt(max(1e-30, 1.0 + m[1][1] - m[0][0] - m[2][2]))
+        q = ((m[0][1] + m[1][0]) / s, 0.25 * s, (m[1][2] + m[2][1]) / s, (m[0][2] - m[2][0]) / s)
+    else:
+        s = 2.0 * math.sqrt(max(1e-30, 1.0 + m[2][2] - m[0][0] - m[1][1]))
+        q = ((m[0][2] + m[2][0]) / s, (m[1][2] + m[2][1]) / s, 0.25 * s, (m[1][0] - m[0][1]) / s)
+    return q
+
+
+def _q2m(q):
+    x, y, z, w = q
+    n = math.sqrt(x * x + y * y + z * z + w * w) or 1.0
+    x, y, z, w = x / n, y / n, z / n, w / n
+    return [[1 - 2 * (y * y + z * z), 2 * (x * y - z * w), 2 * (x * z + y * w)],
+            [2 * (x * y + z * w), 1 - 2 * (x * x + z * z), 2 * (y * z - x * w)],
+            [2 * (x * z - y * w), 2 * (y * z + x * w), 1 - 2 * (x * x + y * y)]]
+
+
+def _slerp(a, b, t):
+    d = sum(p * q for p, q in zip(a, b))
+    if d < 0:
+        b, d = [-v for v in b], -d
+    if d > 0.9995:
+        return [p + (q - p) * t for p, q in zip(a, b)]
+    th = math.acos(d)
+    sa, sb = math.sin((1 - t) * th) / math.sin(th), math.sin(t * th) / math.sin(th)
+    return [p * sa + q * sb for p, q in zip(a, b)]
+
+
+def _between(a, b):
+    """Rotation matrix taking the unit vector a onto the unit vector b."""
+    a, b = _unit(a), _unit(b)
+    c = sum(p * q for p, q in zip(a, b))
+    if c < -0.999999:                               # opposite: half a turn about any perpendicular axis
+        axis = _cross([1.0, 0.0, 0.0], a)
+        if sum(v * v for v in axis) < 1e-12:
+            axis = _cross([0.0, 1.0, 0.0], a)
+        return _axis_mat(_unit(axis), math.pi)
+    v = _cross(a, b)
+    k = 1.0 / (1.0 + c)
+    vx = [[0.0, -v[2], v[1]], [v[2], 0.0, -v[0]], [-v[1], v[0], 0.0]]
+    vx2 = _mat_mul(vx, vx)
+    return [[(1.0 if r == q else 0.0) + vx[r][q] + k * vx2[r][q] for q in range(3)] for r in range(3)]
+
+
+def _rot_part(m4):
+    """The rotation of a 4x4 transform (its upper 3x3 with the column scales divided out)."""
+    cols = [[m4[r][c] for r in range(3)] for c in range(3)]
+    cols = [_unit(c) for c in cols]
+    return [[cols[c][r] for c in range(3)] for r in range(3)]
+
+
 def _quat_copy(q):
-    n = Quaternion()
-    n.r = [row[:] for row in q.r]
-    return n
+    return Quaternion([row[:] for row in q.cur()])
 
 
 def _axis_mat(axis, ang):
@@ -3055,7 +3223,7 @@ def _axis_mat(axis, ang):
 
 def _quat_or_euler(q):
     if isinstance(q, Quaternion):
-        return _mat3_to_euler(q.r)
+        return _mat3_to_euler(q.cur())
     if isinstance(q, Vec):
         return q.v()
     return [0.0, 0.0, 0.0]
@@ -3296,17 +3464,48 @@ class Geometry(Host):
         "applyMatrix4": lambda s, i, x: s.apply(_arg(x, 0).m),
         "center": lambda s, i, x: _geom_center(s),
         "computeVertexNormals": lambda s, i, x: UNDEF,
-        "computeBoundingBox": lambda s, i, x: UNDEF,
-        "computeBoundingSphere": lambda s, i, x: UNDEF,
         "clone": lambda s, i, x: _geom_clone(s),
         "dispose": lambda s, i, x: UNDEF,
         "setAttribute": lambda s, i, x: (_bake(s), s.buffer.__setitem__(_to_str(_arg(x, 0)), _arg(x, 1)), s)[-1],
         "getAttribute": lambda s, i, x: (_bake(s), s.buffer.get(_to_str(_arg(x, 0)), UNDEF))[-1],
         "deleteAttribute": lambda s, i, x: (_bake(s), s.buffer.pop(_to_str(_arg(x, 0)), None), s)[-1],
         "setIndex": lambda s, i, x: (_bake(s), s.buffer.__setitem__("__index", _arg(x, 0)), s)[-1],
+        "addGroup": lambda s, i, x: (s.props.setdefault("groups", JSArray()).items.append(JSObject(
+            {"start": _num_arg(x, 0), "count": _num_arg(x, 1), "materialIndex": _num_arg(x, 2)})), UNDEF)[-1],
+        "clearGroups": lambda s, i, x: (s.props.__setitem__("groups", JSArray()), UNDEF)[-1],
+        "setDrawRange": lambda s, i, x: (s.props.__setitem__("drawRange", JSObject(
+            {"start": _num_arg(x, 0), "count": _num_arg(x, 1, math.inf)})), UNDEF)[-1],
+        "toNonIndexed": lambda s, i, x: _non_indexed(s),
+        "computeBoundingBox": lambda s, i, x: (s.props.__setitem__("boundingBox", _geom_box(s)), UNDEF)[-1],
+        "computeBoundingSphere": lambda s, i, x: (s.props.__setitem__("boundingSphere", _geom_sphere(s)), UNDEF)[-1],
         "setFromPoints": lambda s, i, x: (s.buffer.__setitem__("position", BufferAttribute(
             [c for p in it_items(_arg(x, 0)) for c in (p.v() + [0.0])[:3]], 3)), s)[-1],
     }
+
+
+def _non_indexed(g: Geometry) -> Geometry:
+    """A copy with three vertices per triangle (positions only), as three.js's toNonIndexed."""
+    v, f = geometry_mesh(g)
+    return _baked(g.gtype if g.gtype != "BufferGeometry" else "BufferGeometry", v[f.reshape(-1)].tolist())
+
+
+def _geom_box(g: Geometry):
+    v, _ = geometry_mesh(g)
+    b = Box3()
+    if v.shape[0]:
+        b.props["min"].setv(v.min(0).values.tolist())
+        b.props["max"].setv(v.max(0).values.tolist())
+    return b
+
+
+def _geom_sphere(g: Geometry):
+    v, _ = geometry_mesh(g)
+    sp = Sphere()
+    if v.shape[0]:
+        c = ((v.min(0).values + v.max(0).values) / 2)
+        sp.props["center"].setv(c.tolist())
+        sp.props["radius"] = float((v - c).norm(dim=1).max())
+    return sp
 
 
 def _geom_clone(g: Geometry) -> Geometry:
@@ -3479,7 +3678,7 @@ class Texture(Host):
 
 
 class Object3D(Host):
-    __slots__ = ("otype", "id_")
+    __slots__ = ("otype", "id_", "quat_")
     cls_name = "Object3D"
 
     def __init__(self, otype="Object3D", geometry=None, material=None):
@@ -3502,9 +3701,11 @@ class Object3D(Host):
         if key == "uuid":
             return self.id_
         if key == "quaternion":
-            q = Quaternion()
-            q.r = _euler_mat(self.props["rotation"].v())
-            return q
+            if getattr(self, "quat_", None) is None:
+                self.quat_ = Quaternion(owner=self)
+            return self.quat_
+        if key == "matrixWorld":
+            return Matrix4(_world4(self))
         if key == "up":
             return Vec(("x", "y", "z"), [0, 1, 0], "Vector3")
         return super().get_special(it, key)
@@ -3582,11 +3783,70 @@ class Object3D(Host):
         "setColorAt": lambda s, i, x: UNDEF,
         "getMatrixAt": lambda s, i, x: (setattr(_arg(x, 1), "m", [row[:] for row in s.props.get("__inst", {}).get(int(_num_arg(x, 0)), _ident4())]), UNDEF)[-1],
         "applyMatrix4": lambda s, i, x: _apply_obj_matrix(s, _arg(x, 0).m),
+        "applyQuaternion": lambda s, i, x: (s.props["rotation"].setv(_mat3_to_euler(_mat_mul(
+            _arg(x, 0).cur(), _euler_mat(s.props["rotation"].v())))), s)[-1],
+        "setRotationFromEuler": lambda s, i, x: (s.props["rotation"].setv(_arg(x, 0).v()), UNDEF)[-1],
+        "setRotationFromQuaternion": lambda s, i, x: (s.props["rotation"].setv(_mat3_to_euler(_arg(x, 0).cur())), UNDEF)[-1],
+        "setRotationFromMatrix": lambda s, i, x: (s.props["rotation"].setv(_mat3_to_euler(_rot_part(_arg(x, 0).m))), UNDEF)[-1],
+        "setRotationFromAxisAngle": lambda s, i, x: (s.props["rotation"].setv(_mat3_to_euler(_axis_mat(
+            _arg(x, 0).v(), _num_arg(x, 1)))), UNDEF)[-1],
+        "getWorldPosition": lambda s, i, x: _target_vec(x).setv([_world4(s)[r][3] for r in range(3)]),
+        "getWorldScale": lambda s, i, x: _target_vec(x).setv([math.sqrt(sum(_world4(s)[r][c] ** 2 for r in range(3)))
+                                                              for c in range(3)]),
+        "getWorldQuaternion": lambda s, i, x: (_arg(x, 0) if isinstance(_arg(x, 0), Quaternion) else Quaternion()).put(
+            _rot_part(_world4(s))),
+        "getWorldDirection": lambda s, i, x: _target_vec(x).setv(_unit([_world4(s)[r][2] for r in range(3)])),
+        "localToWorld": lambda s, i, x: _arg(x, 0).setv(_mat4_point(_world4(s), _arg(x, 0).v())),
+        "worldToLocal": lambda s, i, x: _arg(x, 0).setv(_mat4_point(_inv4(_world4(s)), _arg(x, 0).v())),
+        "attach": lambda s, i, x: _attach(s, _arg(x, 0)),
+        "removeFromParent": lambda s, i, x: _remove_from_parent(s),
+        "getObjectById": lambda s, i, x: UNDEF,
+        "computeBoundingSphere": lambda s, i, x: UNDEF,
+        "computeBoundingBox": lambda s, i, x: UNDEF,
     }
 
 
 def _add3(a, b):
     return [p + q for p, q in zip(a, b)]
+
+
+def _target_vec(x):
+    t = _arg(x, 0)
+    return t if isinstance(t, Vec) else Vec(("x", "y", "z"), [0.0, 0.0, 0.0], "Vector3")
+
+
+def _world4(o: "Object3D"):
+    m = o.local()
+    p = o.props.get("parent")
+    depth = 0
+    while isinstance(p, Object3D) and depth < 64:
+        m = _mat_mul(p.local(), m)
+        p = p.props.get("parent")
+        depth += 1
+    return m
+
+
+def _remove_from_parent(o: "Object3D"):
+    p = o.props.get("parent")
+    if isinstance(p, Object3D):
+        kids = p.children()
+        kids[:] = [c for c in kids if c is not o]
+    o.props["parent"] = None
+    return o
+
+
+def _attach(new_parent: "Object3D", o):
+    """Reparent `o` under `new_parent` keeping its world transform."""
+    if not isinstance(o, Object3D):
+        return new_parent
+    local = _mat_mul(_inv4(_world4(new_parent)), _world4(o))
+    _remove_from_parent(o)
+    new_parent.add([o])
+    sx, sy, sz = (math.sqrt(sum(local[r][c] ** 2 for r in range(3))) or 1.0 for c in range(3))
+    o.props["position"].setv([local[0][3], local[1][3], local[2][3]])
+    o.props["scale"].setv([sx, sy, sz])
+    o.props["rotation"].setv(_mat3_to_euler([[local[r][c] / (sx, sy, sz)[c] for c in range(3)] for r in range(3)]))
+    return new_parent
 
 
 def _apply_obj_matrix(o: Object3D, m):
@@ -4017,6 +4277,19 @@ def make_three(it: Interp) -> JSObject:
         "randFloatSpread": _nat("randFloatSpread", lambda i, t, x: _num_arg(x, 0) * (0.5 - rnd())),
         "randInt": _nat("randInt", lambda i, t, x: float(math.floor(_num_arg(x, 0) + rnd() * (_num_arg(x, 1) - _num_arg(x, 0) + 1)))),
         "seededRandom": _nat("seededRandom", lambda i, t, x: rnd()),
+        "euclideanModulo": _nat("euclideanModulo", lambda i, t, x: (_num_arg(x, 0) % _num_arg(x, 1)) if _num_arg(x, 1) else math.nan),
+        "inverseLerp": _nat("inverseLerp", lambda i, t, x: ((_num_arg(x, 2) - _num_arg(x, 0)) / (_num_arg(x, 1) - _num_arg(x, 0)))
+                            if _num_arg(x, 0) != _num_arg(x, 1) else 0.0),
+        "damp": _nat("damp", lambda i, t, x: _num_arg(x, 0) + (_num_arg(x, 1) - _num_arg(x, 0)) *
+                     (1 - math.exp(-_num_arg(x, 2) * _num_arg(x, 3)))),
+        "pingpong": _nat("pingpong", lambda i, t, x: _num_arg(x, 1, 1.0) - abs(
+            (_num_arg(x, 0) % (2 * _num_arg(x, 1, 1.0))) - _num_arg(x, 1, 1.0))),
+        "smootherstep": _nat("smootherstep", lambda i, t, x: (lambda u: u * u * u * (u * (u * 6 - 15) + 10))(
+            min(1.0, max(0.0, (_num_arg(x, 0) - _num_arg(x, 1)) / ((_num_arg(x, 2) - _num_arg(x, 1)) or 1.0))))),
+        "isPowerOfTwo": _nat("isPowerOfTwo", lambda i, t, x: (lambda v: v > 0 and v == int(v) and (int(v) & (int(v) - 1)) == 0)(
+            _num_arg(x, 0))),
+        "ceilPowerOfTwo": _nat("ceilPowerOfTwo", lambda i, t, x: float(2 ** math.ceil(math.log2(max(_num_arg(x, 0), 1e-300))))),
+        "floorPowerOfTwo": _nat("floorPowerOfTwo", lambda i, t, x: float(2 ** math.floor(math.log2(max(_num_arg(x, 0), 1e-300))))),
         "DEG2RAD": math.pi / 180, "RAD2DEG": 180 / math.pi})
     return JSObject(three)
 

@@ -86,3 +86,32 @@ def test_object_accessors_prototypes_labels_and_errors():
 ])
 def test_js_semantics(expr, want):
     assert _ev(expr) == want
+
+
+def test_object_quaternion_is_a_live_view_and_world_transforms():
+    # the usual beam-between-two-points idiom: orient a cylinder with quaternion.setFromUnitVectors
+    pre = """
+      const a = new THREE.Vector3(0, 0, 0), b = new THREE.Vector3(0.3, 0.3, 0);
+      const dir = b.clone().sub(a);
+      const beam = new THREE.Mesh(new THREE.CylinderGeometry(0.02, 0.02, dir.length(), 8), new THREE.MeshStandardMaterial());
+      beam.position.copy(a).add(b).multiplyScalar(0.5);
+      beam.quaternion.setFromUnitVectors(new THREE.Vector3(0, 1, 0), dir.clone().normalize());
+      const up = new THREE.Vector3(0, 1, 0).applyQuaternion(beam.quaternion);
+      const parent = new THREE.Group(); parent.position.set(1, 0, 0); parent.add(beam);
+      const w = beam.getWorldPosition(new THREE.Vector3());
+      const child = new THREE.Mesh(new THREE.BoxGeometry(0.1, 0.1, 0.1), new THREE.MeshStandardMaterial());
+      child.position.set(0.5, 0, 0); parent.add(child);
+      g.attach(child);
+      const q = new THREE.Quaternion().setFromAxisAngle(new THREE.Vector3(0, 0, 1), Math.PI / 2);
+      const h = new THREE.Quaternion().slerp(q, 0.5);
+      const m = new THREE.Matrix4().makeRotationZ(0.3).setPosition(1, 2, 3);
+      const p = new THREE.Vector3(), qq = new THREE.Quaternion(), sc = new THREE.Vector3();
+      m.clone().invert().invert().decompose(p, qq, sc);
+    """
+    got = _ev("[up.x, up.y, beam.rotation.z, w.x, child.position.x, child.parent === g, "
+              "new THREE.Euler().setFromQuaternion(h).z, p.z, sc.x]", pre).items
+    r2 = 1 / 2 ** 0.5
+    assert got[0] == pytest.approx(r2) and got[1] == pytest.approx(r2)       # the rotation really changed
+    assert got[2] == pytest.approx(-3.14159265 / 4)
+    assert got[3] == pytest.approx(1.15) and got[4] == pytest.approx(1.5) and got[5] is True
+    assert got[6] == pytest.approx(3.14159265 / 4) and got[7] == pytest.approx(3.0) and got[8] == pytest.approx(1.0)
