@@ -2828,7 +2828,7 @@ def _vec_methods():
         "toArray": lambda s, i, x: JSArray(s.v()),
         "fromArray": lambda s, i, x: s.setv([_to_num(v) for v in it_items(_arg(x, 0))][int(_num_arg(x, 1)):]),
         "applyAxisAngle": lambda s, i, x: s.setv(_rot_axis(s.v(), other(x, s), _num_arg(x, 1))),
-        "applyEuler": lambda s, i, x: s.setv(_mat3_apply(_euler_mat(_arg(x, 0).v()), s.v())),
+        "applyEuler": lambda s, i, x: s.setv(_mat3_apply(_rot_mat(_arg(x, 0)), s.v())),
         "applyMatrix4": lambda s, i, x: s.setv(_mat4_point(_arg(x, 0).m, s.v())),
         "rotateAround": lambda s, i, x: s.setv(_rot2(s.v(), _arg(x, 0).v(), _num_arg(x, 1))),
         "angle": lambda s, i, x: math.atan2(s.v()[1], s.v()[0]) % (2 * math.pi),
@@ -2861,8 +2861,8 @@ def _vec_methods():
         "setFromCylindrical": lambda s, i, x: s.setv(_from_cylindrical(*_arg(x, 0).rty())),
         "setFromCylindricalCoords": lambda s, i, x: s.setv(_from_cylindrical(_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2))),
         "setFromMatrixPosition": lambda s, i, x: s.setv([_arg(x, 0).m[r][3] for r in range(3)]),
-        "setFromQuaternion": lambda s, i, x: s.setv(_mat3_to_euler(_arg(x, 0).cur())),
-        "setFromRotationMatrix": lambda s, i, x: s.setv(_mat3_to_euler(_rot_part(_arg(x, 0).m))),
+        "setFromQuaternion": lambda s, i, x: _set_rot(s, _arg(x, 0).cur()),
+        "setFromRotationMatrix": lambda s, i, x: _set_rot(s, _rot_part(_arg(x, 0).m)),
         "setFromVector3": lambda s, i, x: s.setv(_arg(x, 0).v()[:3]),
         "setFromMatrixScale": lambda s, i, x: s.setv([math.sqrt(sum(_arg(x, 0).m[r][c] ** 2 for r in range(3)))
                                                       for c in range(3)]),
@@ -2932,30 +2932,84 @@ def _rot_axis(v, axis, ang):
     return [v[j] * cs + kxv[j] * sn + k[j] * kdv * (1 - cs) for j in range(3)]
 
 
-def _euler_mat(e):
-    """Rotation matrix of an XYZ Euler (three.js default order): R = Rx * Ry * Rz."""
-    x, y, z = e[:3]
-    a, b = math.cos(x), math.sin(x)
-    c, d = math.cos(y), math.sin(y)
-    ee, f = math.cos(z), math.sin(z)
-    return [[c * ee, -c * f, d],
-            [a * f + b * ee * d, a * ee - b * f * d, -b * c],
-            [b * f - a * ee * d, b * ee + a * f * d, a * c]]
+def _axis_rot(axis, a):
+    c, s = math.cos(a), math.sin(a)
+    if axis == "X":
+        return [[1.0, 0.0, 0.0], [0.0, c, -s], [0.0, s, c]]
+    if axis == "Y":
+        return [[c, 0.0, s], [0.0, 1.0, 0.0], [-s, 0.0, c]]
+    return [[c, -s, 0.0], [s, c, 0.0], [0.0, 0.0, 1.0]]
+
+
+def _euler_mat(e, order="XYZ"):
+    """Rotation matrix of Euler angles (x, y, z) applied in `order` (three.js: for "XYZ", R = Rx * Ry * Rz)."""
+    if order not in _ORDERS:
+        order = "XYZ"
+    ang = {"X": e[0], "Y": e[1], "Z": e[2]}
+    m = [[1.0, 0.0, 0.0], [0.0, 1.0, 0.0], [0.0, 0.0, 1.0]]
+    for ax in order:
+        m = _mat_mul(m, _axis_rot(ax, ang[ax]))
+    return m
+
+
+_ORDERS = ("XYZ", "YXZ", "ZXY", "ZYX", "YZX", "XZY")
+
+
+def _order(e) -> str:
+    o = e.props.get("order", "XYZ") if isinstance(e, Vec) else "XYZ"
+    return o if o in _ORDERS else "XYZ"
+
+
+def _rot_mat(e):
+    """Rotation matrix of an Euler vector in its own order (a plain vector: XYZ)."""
+    return _euler_mat(e.v() if isinstance(e, Vec) else list(e), _order(e))
+
+
+def _set_rot(e, m):
+    """Write a rotation matrix into an Euler vector, in the vector's order; returns the vector."""
+    e.setv(_mat3_to_euler(m, _order(e)))
+    return e
 
 
 def _mat3_apply(m, v):
     return [sum(m[r][k] * v[k] for k in range(3)) for r in range(3)]
 
 
-def _mat3_to_euler(m):
-    y = math.asin(max(-1.0, min(1.0, m[0][2])))
-    if abs(m[0][2]) < 0.9999999:
-        x = math.atan2(-m[1][2], m[2][2])
-        z = math.atan2(-m[0][1], m[0][0])
-    else:
-        x = math.atan2(m[2][1], m[1][1])
-        z = 0.0
-    return [x, y, z]
+def _mat3_to_euler(m, order="XYZ"):
+    """Euler angles (x, y, z) in `order` of a rotation matrix (the inverse of _euler_mat; at gimbal lock the
+    first-applied free angle takes the whole rotation)."""
+    def cl(v):
+        return max(-1.0, min(1.0, v))
+    lim = 0.9999999
+    if order == "YXZ":
+        x = math.asin(-cl(m[1][2]))
+        if abs(m[1][2]) < lim:
+            return [x, math.atan2(m[0][2], m[2][2]), math.atan2(m[1][0], m[1][1])]
+        return [x, math.atan2(-m[2][0], m[0][0]), 0.0]
+    if order == "ZXY":
+        x = math.asin(cl(m[2][1]))
+        if abs(m[2][1]) < lim:
+            return [x, math.atan2(-m[2][0], m[2][2]), math.atan2(-m[0][1], m[1][1])]
+        return [x, 0.0, math.atan2(m[1][0], m[0][0])]
+    if order == "ZYX":
+        y = math.asin(-cl(m[2][0]))
+        if abs(m[2][0]) < lim:
+            return [math.atan2(m[2][1], m[2][2]), y, math.atan2(m[1][0], m[0][0])]
+        return [0.0, y, math.atan2(-m[0][1], m[1][1])]
+    if order == "YZX":
+        z = math.asin(cl(m[1][0]))
+        if abs(m[1][0]) < lim:
+            return [math.atan2(-m[1][2], m[1][1]), math.atan2(-m[2][0], m[0][0]), z]
+        return [0.0, math.atan2(m[0][2], m[2][2]), z]
+    if order == "XZY":
+        z = math.asin(-cl(m[0][1]))
+        if abs(m[0][1]) < lim:
+            return [math.atan2(m[2][1], m[1][1]), math.atan2(m[0][2], m[0][0]), z]
+        return [math.atan2(-m[1][2], m[2][2]), 0.0, z]
+    y = math.asin(cl(m[0][2]))
+    if abs(m[0][2]) < lim:
+        return [math.atan2(-m[1][2], m[2][2]), y, math.atan2(-m[0][1], m[0][0])]
+    return [math.atan2(m[2][1], m[1][1]), y, 0.0]
 
 
 def _mat_mul(a, b):
@@ -2970,8 +3024,8 @@ def _mat4_point(m, v):
     return [(m[r][0] * v[0] + m[r][1] * v[1] + m[r][2] * v[2] + m[r][3]) / w for r in range(3)]
 
 
-def _compose(pos, rot, scl):
-    r = _euler_mat(rot)
+def _compose(pos, rot, scl, order="XYZ"):
+    r = _euler_mat(rot, order)
     return [[r[0][0] * scl[0], r[0][1] * scl[1], r[0][2] * scl[2], pos[0]],
             [r[1][0] * scl[0], r[1][1] * scl[1], r[1][2] * scl[2], pos[1]],
             [r[2][0] * scl[0], r[2][1] * scl[1], r[2][2] * scl[2], pos[2]],
@@ -3064,7 +3118,7 @@ class Matrix4(Host):
         "makeRotationX": lambda s, i, x: s._rot("x", _num_arg(x, 0)),
         "makeRotationY": lambda s, i, x: s._rot("y", _num_arg(x, 0)),
         "makeRotationZ": lambda s, i, x: s._rot("z", _num_arg(x, 0)),
-        "makeRotationFromEuler": lambda s, i, x: (setattr(s, "m", _compose([0, 0, 0], _arg(x, 0).v(), [1, 1, 1])), s)[-1],
+        "makeRotationFromEuler": lambda s, i, x: (setattr(s, "m", _m3to4(_rot_mat(_arg(x, 0)))), s)[-1],
         "makeRotationFromQuaternion": lambda s, i, x: (setattr(s, "m", _m3to4(_arg(x, 0).cur())), s)[-1],
         "makeRotationAxis": lambda s, i, x: (setattr(s, "m", _m3to4(_axis_mat(_arg(x, 0).v(), _num_arg(x, 1)))), s)[-1],
         "invert": lambda s, i, x: (setattr(s, "m", _inv4(s.m)), s)[-1],
@@ -3104,13 +3158,13 @@ class Quaternion(Host):
 
     def cur(self):
         if self.owner is not None:
-            self.r = _euler_mat(self.owner.props["rotation"].v())
+            self.r = _rot_mat(self.owner.props["rotation"])
         return self.r
 
     def put(self, r):
         self.r = [list(map(float, row)) for row in r]
         if self.owner is not None:
-            self.owner.props["rotation"].setv(_mat3_to_euler(self.r))
+            _set_rot(self.owner.props["rotation"], (self.r))
         return self
 
     def get_special(self, it, key):
@@ -3128,7 +3182,7 @@ class Quaternion(Host):
 
     js_methods = {
         "set": lambda s, i, x: s.put(_q2m([_num_arg(x, k) for k in range(4)])),
-        "setFromEuler": lambda s, i, x: s.put(_euler_mat(_arg(x, 0).v())),
+        "setFromEuler": lambda s, i, x: s.put(_rot_mat(_arg(x, 0))),
         "setFromAxisAngle": lambda s, i, x: s.put(_axis_mat(_arg(x, 0).v(), _num_arg(x, 1))),
         "setFromUnitVectors": lambda s, i, x: s.put(_between(_arg(x, 0).v(), _arg(x, 1).v())),
         "setFromRotationMatrix": lambda s, i, x: s.put(_rot_part(_arg(x, 0).m)),
@@ -3719,7 +3773,8 @@ class Object3D(Host):
         return False
 
     def local(self):
-        return _compose(self.props["position"].v(), self.props["rotation"].v(), self.props["scale"].v())
+        return _compose(self.props["position"].v(), self.props["rotation"].v(), self.props["scale"].v(),
+                        _order(self.props["rotation"]))
 
     def children(self) -> list:
         return self.props["children"].items
@@ -3738,9 +3793,9 @@ class Object3D(Host):
         return self
 
     def rotate_local(self, axis, ang):
-        r = _euler_mat(self.props["rotation"].v())
+        r = _rot_mat(self.props["rotation"])
         a = {"x": [1, 0, 0], "y": [0, 1, 0], "z": [0, 0, 1]}[axis]
-        self.props["rotation"].setv(_mat3_to_euler(_mat_mul(r, _axis_mat(a, ang))))
+        _set_rot(self.props["rotation"], (_mat_mul(r, _axis_mat(a, ang))))
         return self
 
     def look_at(self, target):
@@ -3754,7 +3809,7 @@ class Object3D(Host):
         x = [c / xn for c in x]
         y = _cross(z, x)
         m = [[x[0], y[0], z[0]], [x[1], y[1], z[1]], [x[2], y[2], z[2]]]
-        self.props["rotation"].setv(_mat3_to_euler(m))
+        _set_rot(self.props["rotation"], (m))
         return self
 
     js_methods = {
@@ -3766,13 +3821,13 @@ class Object3D(Host):
         "rotateZ": lambda s, i, x: s.rotate_local("z", _num_arg(x, 0)),
         # world axis: the rotation composes on the left (the object turns about a world-space axis through its
         # own origin; its position is unchanged)
-        "rotateOnWorldAxis": lambda s, i, x: (s.props["rotation"].setv(_mat3_to_euler(_mat_mul(
-            _axis_mat(_arg(x, 0).v(), _num_arg(x, 1)), _euler_mat(s.props["rotation"].v())))), s)[-1],
-        "rotateOnAxis": lambda s, i, x: (s.props["rotation"].setv(_mat3_to_euler(_mat_mul(_euler_mat(s.props["rotation"].v()),
+        "rotateOnWorldAxis": lambda s, i, x: (_set_rot(s.props["rotation"], (_mat_mul(
+            _axis_mat(_arg(x, 0).v(), _num_arg(x, 1)), _rot_mat(s.props["rotation"])))), s)[-1],
+        "rotateOnAxis": lambda s, i, x: (_set_rot(s.props["rotation"], (_mat_mul(_rot_mat(s.props["rotation"]),
                                                                                          _axis_mat(_arg(x, 0).v(), _num_arg(x, 1))))), s)[-1],
-        "translateX": lambda s, i, x: (s.props["position"].setv(_add3(s.props["position"].v(), _mat3_apply(_euler_mat(s.props["rotation"].v()), [_num_arg(x, 0), 0, 0]))), s)[-1],
-        "translateY": lambda s, i, x: (s.props["position"].setv(_add3(s.props["position"].v(), _mat3_apply(_euler_mat(s.props["rotation"].v()), [0, _num_arg(x, 0), 0]))), s)[-1],
-        "translateZ": lambda s, i, x: (s.props["position"].setv(_add3(s.props["position"].v(), _mat3_apply(_euler_mat(s.props["rotation"].v()), [0, 0, _num_arg(x, 0)]))), s)[-1],
+        "translateX": lambda s, i, x: (s.props["position"].setv(_add3(s.props["position"].v(), _mat3_apply(_rot_mat(s.props["rotation"]), [_num_arg(x, 0), 0, 0]))), s)[-1],
+        "translateY": lambda s, i, x: (s.props["position"].setv(_add3(s.props["position"].v(), _mat3_apply(_rot_mat(s.props["rotation"]), [0, _num_arg(x, 0), 0]))), s)[-1],
+        "translateZ": lambda s, i, x: (s.props["position"].setv(_add3(s.props["position"].v(), _mat3_apply(_rot_mat(s.props["rotation"]), [0, 0, _num_arg(x, 0)]))), s)[-1],
         "lookAt": lambda s, i, x: s.look_at(_arg(x, 0).v() if isinstance(_arg(x, 0), Vec) else [_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2)]),
         "updateMatrix": lambda s, i, x: (setattr(s.props["matrix"], "m", s.local()), UNDEF)[-1],
         "updateMatrixWorld": lambda s, i, x: UNDEF,
@@ -3783,12 +3838,13 @@ class Object3D(Host):
         "setColorAt": lambda s, i, x: UNDEF,
         "getMatrixAt": lambda s, i, x: (setattr(_arg(x, 1), "m", [row[:] for row in s.props.get("__inst", {}).get(int(_num_arg(x, 0)), _ident4())]), UNDEF)[-1],
         "applyMatrix4": lambda s, i, x: _apply_obj_matrix(s, _arg(x, 0).m),
-        "applyQuaternion": lambda s, i, x: (s.props["rotation"].setv(_mat3_to_euler(_mat_mul(
-            _arg(x, 0).cur(), _euler_mat(s.props["rotation"].v())))), s)[-1],
-        "setRotationFromEuler": lambda s, i, x: (s.props["rotation"].setv(_arg(x, 0).v()), UNDEF)[-1],
-        "setRotationFromQuaternion": lambda s, i, x: (s.props["rotation"].setv(_mat3_to_euler(_arg(x, 0).cur())), UNDEF)[-1],
-        "setRotationFromMatrix": lambda s, i, x: (s.props["rotation"].setv(_mat3_to_euler(_rot_part(_arg(x, 0).m))), UNDEF)[-1],
-        "setRotationFromAxisAngle": lambda s, i, x: (s.props["rotation"].setv(_mat3_to_euler(_axis_mat(
+        "applyQuaternion": lambda s, i, x: (_set_rot(s.props["rotation"], (_mat_mul(
+            _arg(x, 0).cur(), _rot_mat(s.props["rotation"])))), s)[-1],
+        "setRotationFromEuler": lambda s, i, x: (s.props["rotation"].setv(_arg(x, 0).v()), s.props["rotation"].props.__setitem__(
+            "order", _order(_arg(x, 0))), UNDEF)[-1],
+        "setRotationFromQuaternion": lambda s, i, x: (_set_rot(s.props["rotation"], (_arg(x, 0).cur())), UNDEF)[-1],
+        "setRotationFromMatrix": lambda s, i, x: (_set_rot(s.props["rotation"], (_rot_part(_arg(x, 0).m))), UNDEF)[-1],
+        "setRotationFromAxisAngle": lambda s, i, x: (_set_rot(s.props["rotation"], (_axis_mat(
             _arg(x, 0).v(), _num_arg(x, 1)))), UNDEF)[-1],
         "getWorldPosition": lambda s, i, x: _target_vec(x).setv([_world4(s)[r][3] for r in range(3)]),
         "getWorldScale": lambda s, i, x: _target_vec(x).setv([math.sqrt(sum(_world4(s)[r][c] ** 2 for r in range(3)))
@@ -3845,7 +3901,7 @@ def _attach(new_parent: "Object3D", o):
     sx, sy, sz = (math.sqrt(sum(local[r][c] ** 2 for r in range(3))) or 1.0 for c in range(3))
     o.props["position"].setv([local[0][3], local[1][3], local[2][3]])
     o.props["scale"].setv([sx, sy, sz])
-    o.props["rotation"].setv(_mat3_to_euler([[local[r][c] / (sx, sy, sz)[c] for c in range(3)] for r in range(3)]))
+    _set_rot(o.props["rotation"], ([[local[r][c] / (sx, sy, sz)[c] for c in range(3)] for r in range(3)]))
     return new_parent
 
 
@@ -3856,7 +3912,7 @@ def _apply_obj_matrix(o: Object3D, m):
     rot = [[full[r][c] / (sc[c] or 1.0) for c in range(3)] for r in range(3)]
     o.props["position"].setv(pos)
     o.props["scale"].setv(sc)
-    o.props["rotation"].setv(_mat3_to_euler(rot))
+    _set_rot(o.props["rotation"], (rot))
     return o
 
 

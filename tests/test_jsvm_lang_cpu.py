@@ -115,3 +115,29 @@ def test_object_quaternion_is_a_live_view_and_world_transforms():
     assert got[2] == pytest.approx(-3.14159265 / 4)
     assert got[3] == pytest.approx(1.15) and got[4] == pytest.approx(1.5) and got[5] is True
     assert got[6] == pytest.approx(3.14159265 / 4) and got[7] == pytest.approx(3.0) and got[8] == pytest.approx(1.0)
+
+
+def test_euler_order_is_honoured():
+    pre = """
+      const a = new THREE.Object3D(); a.rotation.order = 'YXZ'; a.rotation.set(0.3, 0.5, 0.2); a.updateMatrix();
+      const b = new THREE.Object3D(); b.rotation.set(0.3, 0.5, 0.2); b.updateMatrix();
+      const v1 = new THREE.Vector3(1, 2, 3).applyMatrix4(a.matrix), v2 = new THREE.Vector3(1, 2, 3).applyMatrix4(b.matrix);
+      const q = new THREE.Quaternion().setFromEuler(a.rotation);
+      const c = new THREE.Object3D(); c.rotation.order = 'YXZ'; c.quaternion.copy(q);
+    """
+    got = _ev("[v1.x, v2.x, c.rotation.x, c.rotation.y, c.rotation.z]", pre).items
+    import math
+
+    def rot(order, e, v):
+        def R(ax, t):
+            c_, s_ = math.cos(t), math.sin(t)
+            return {"X": [[1, 0, 0], [0, c_, -s_], [0, s_, c_]], "Y": [[c_, 0, s_], [0, 1, 0], [-s_, 0, c_]],
+                    "Z": [[c_, -s_, 0], [s_, c_, 0], [0, 0, 1]]}[ax]
+        m = [[1, 0, 0], [0, 1, 0], [0, 0, 1]]
+        for ax in order:
+            r = R(ax, e["XYZ".index(ax)])
+            m = [[sum(m[i][k] * r[k][j] for k in range(3)) for j in range(3)] for i in range(3)]
+        return [sum(m[i][k] * v[k] for k in range(3)) for i in range(3)]
+    assert got[0] == pytest.approx(rot("YXZ", (0.3, 0.5, 0.2), (1, 2, 3))[0])
+    assert got[1] == pytest.approx(rot("XYZ", (0.3, 0.5, 0.2), (1, 2, 3))[0]) and got[0] != pytest.approx(got[1])
+    assert got[2:] == pytest.approx([0.3, 0.5, 0.2])          # written back in the object's own order
