@@ -4600,18 +4600,66 @@ def _col_major(m):
     return [m[r][c] for c in range(4) for r in range(4)]
 
 
+def _tri_groups(g: "Geometry", n_tris: int) -> Dict[int, List[int]]:
+    """Material index -> triangle indices: explicit groups (addGroup, in index units), else three.js's groups of
+    a box (one per face: +x, -x, +y, -y, +z, -z) or a cylinder / cone (side, top cap, bottom cap), else one
+    group 0."""
+    out: Dict[int, List[int]] = {}
+    groups = g.props.get("groups")
+    if isinstance(groups, JSArray) and groups.items:
+        for gr in groups.items:
+            st, cnt = int(_to_num(gr.js_get("start"))), _to_num(gr.js_get("count"))
+            cnt = n_tris * 3 - st if not math.isfinite(cnt) else int(cnt)
+            mi = int(_to_num(gr.js_get("materialIndex")))
+            out.setdefault(mi, []).extend(range(max(0, st // 3), min(n_tris, (st + cnt) // 3)))
+        return out
+    if not g.baked and g.gtype == "BoxGeometry" and n_tris == 12:
+        for pair, mi in enumerate((5, 4, 3, 2, 0, 1)):        # our face order: -z, +z, -y, +y, +x, -x
+            out[mi] = [2 * pair, 2 * pair + 1]
+        return out
+    if not g.baked and g.gtype in ("CylinderGeometry", "ConeGeometry"):
+        R = max(3, min(int(_to_num(g.params.get("radialSegments", 32))), 64))
+        Hs = max(1, min(int(_to_num(g.params.get("heightSegments", 1))), 32))
+        side = 2 * R * Hs
+        out[0] = list(range(min(side, n_tris)))
+        caps = list(range(side, n_tris))
+        rt = _to_num(g.params.get("radiusTop", 1.0)) if g.gtype == "CylinderGeometry" else 0.0
+        k = 1
+        while caps:
+            out[k] = caps[:R]
+            caps = caps[R:]
+            k += 1
+        if rt <= 0 and 1 in out and 2 not in out:             # a cone's only cap is the bottom (group 2)
+            out[2] = out.pop(1)
+        return out
+    return {0: list(range(n_tris))}
+
+
 def to_scene_json(root: Object3D, max_depth: int = 64) -> dict:
     """Object3D tree -> the scene JSON of render/scene.py (geometries baked to BufferGeometry where needed)."""
     geoms: Dict[int, dict] = {}
     mats: Dict[int, dict] = {}
 
-    def geom_ref(g: Geometry) -> str:
-        key = id(g)
+    meshes: Dict[int, tuple] = {}
+
+    def mesh_of(g: Geometry):
+        if id(g) not in meshes:
+            meshes[id(g)] = geometry_mesh(g)
+        return meshes[id(g)]
+
+    def geom_ref(g: Geometry, group: Optional[int] = None, tris=None) -> str:
+        key = (id(g), group)
         if key not in geoms:
-            v, f = geometry_mesh(g)
+            v, f = mesh_of(g)
+            if tris is not None:
+                f = f[tris]
+            attrs = {"position": {"itemSize": 3, "type": "Float32Array", "array": v.reshape(-1).tolist()}}
+            col = g.buffer.get("color")
+            if isinstance(col, BufferAttribute) and col.item >= 3 and len(col.array) // col.item == v.shape[0]:
+                attrs["color"] = {"itemSize": 3, "type": "Float32Array",
+                                  "array": [c for k in range(v.shape[0]) for c in col.array[k * col.item:k * col.item + 3]]}
             geoms[key] = {"uuid": g.id_ + f"-{len(geoms)}", "type": "BufferGeometry",
-                          "data": {"attributes": {"position": {"itemSize": 3, "type": "Float32Array",
-                                                               "array": v.reshape(-1).tolist()}},
+                          "data": {"attributes": attrs,
                                    "index": {"type": "Uint32Array", "array": f.reshape(-1).tolist()}}}
         return geoms[key]["uuid"]
 
@@ -4626,6 +4674,8 @@ def to_scene_json(root: Object3D, max_depth: int = 64) -> dict:
             mats[key] = {"uuid": f"m{len(mats)}", "type": m.mtype,
                          "color": col.hex() if isinstance(col, Color) else 0xCCCCCC,
                          "opacity": _to_num(m.props.get("opacity", 1.0))}
+            if _truthy(m.props.get("vertexColors", False)):
+                mats[key]["vertexColors"] = True
             if m.mtype in ("MeshStandardMaterial", "MeshPhysicalMaterial"):
                 mats[key]["roughness"] = _to_num(m.props.get("roughness", 1.0))
                 mats[key]["metalness"] = _to_num(m.props.get("metalness", 0.0))
@@ -4647,6 +4697,16 @@ def to_scene_json(root: Object3D, max_depth: int = 64) -> dict:
                 for k in range(count):
                     d["children"].append({"uuid": f"{o.id_}-{k}", "type": "Mesh", "geometry": gid, "material": mid,
                                           "matrix": _col_major(inst.get(k, _ident4())), "children": []})
+            elif isinstance(o.props.get("material"), JSArray):
+                # one material per geometry group: a sub-mesh per group (three.js draws each group with its
+                # material; a geometry without groups takes the first material here)
+                mlist = o.props["material"].items
+                for grp, tris in _tri_groups(g, mesh_of(g)[1].shape[0]).items():
+                    m = mlist[grp] if 0 <= grp < len(mlist) else None
+                    if isinstance(m, Material) and tris:
+                        d["children"].append({"uuid": f"{o.id_}-g{grp}", "type": "Mesh",
+                                              "geometry": geom_ref(g, grp, tris), "material": mat_ref(m),
+                                              "matrix": _col_major(_ident4()), "children": []})
             else:
                 d["geometry"], d["material"] = gid, mid
         for c in o.children():

@@ -156,9 +156,17 @@ def scene_triangles(scene: dict, with_materials: bool = False):
             v, f = cache[gid]
             vh = torch.cat([v, torch.ones(v.shape[0], 1)], 1) @ world.t()
             tris.append(vh[:, :3][f])
-            c = mats.get(node.get("material"), {}).get("color", 0xCCCCCC)
+            md = mats.get(node.get("material"), {})
+            c = md.get("color", 0xCCCCCC)
             rgb = torch.tensor([(c >> 16) & 255, (c >> 8) & 255, c & 255], dtype=torch.float32) / 255.0
-            cols.append((rgb ** 2.2).expand(f.shape[0], 3))     # sRGB material colour -> linear
+            lin = rgb ** 2.2                                    # sRGB material colour -> linear
+            vcol = geoms[gid]["data"]["attributes"].get("color") if "data" in geoms[gid] else None
+            if md.get("vertexColors") and vcol is not None:
+                # vertex colours are linear; a triangle takes the mean of its corners, times the material colour
+                per_v = torch.tensor(vcol["array"], dtype=torch.float32).view(-1, 3)
+                cols.append(per_v[f].mean(1).clamp(0, 1) * lin)
+            else:
+                cols.append(lin.expand(f.shape[0], 3))
             md = mats.get(node.get("material"), {})
             pbr.append(torch.tensor([float(md.get("roughness", 1.0)), float(md.get("metalness", 0.0))]).expand(
                 f.shape[0], 2))

@@ -215,3 +215,32 @@ def test_vertex_counts_follow_three_js():
            "new THREE.IcosahedronGeometry(0.5, %d), new THREE.MeshStandardMaterial())); return g; }")
     assert c.check(src % 60).ok                                    # 223,260 vertices
     assert "VERTEX_LIMIT_EXCEEDED" in {f["rule"] for f in c.check(src % 70).failures}   # 302,460
+
+
+def test_material_arrays_follow_geometry_groups_and_vertex_colours_render():
+    import torch
+
+    from phung5_b200.render import scene as S
+    src = """export default function generate(THREE) { const g = new THREE.Group();
+      const cols = [0xff0000, 0x00ff00, 0x0000ff, 0xffff00, 0xff00ff, 0x00ffff];
+      g.add(new THREE.Mesh(new THREE.BoxGeometry(0.5, 0.5, 0.5), cols.map(c => new THREE.MeshStandardMaterial({color: c}))));
+      const q = new THREE.BufferGeometry();
+      q.setAttribute('position', new THREE.Float32BufferAttribute([0, 0, 0.3, 0.2, 0, 0.3, 0, 0.2, 0.3,
+                                                                   0, 0, 0.4, 0.2, 0, 0.4, 0, 0.2, 0.4], 3));
+      q.setAttribute('color', new THREE.Float32BufferAttribute([0, 1, 0, 0, 1, 0, 0, 1, 0, 0, 0, 1, 0, 0, 1, 0, 0, 1], 3));
+      q.addGroup(0, 3, 1); q.addGroup(3, 3, 0);
+      g.add(new THREE.Mesh(q, [new THREE.MeshBasicMaterial({vertexColors: true}), new THREE.MeshBasicMaterial({color: 0xff0000})]));
+      return g; }"""
+    res = JSChecker(_inline=True).check(src)
+    assert res.ok, res.summary()
+    t, col = S.scene_triangles(res.scene)
+    n = torch.linalg.cross(t[:, 1] - t[:, 0], t[:, 2] - t[:, 0])
+    c = t.mean(1)
+    px = (n[:, 0].abs() > 1e-6) & (c[:, 0] > 0.2)
+    ny = (n[:, 1].abs() > 1e-6) & (c[:, 1] < -0.2)
+    assert torch.allclose(col[px], torch.tensor([1.0, 0.0, 0.0]))         # group 0: +x
+    assert torch.allclose(col[ny], torch.tensor([1.0, 1.0, 0.0]))         # group 3: -y
+    z3 = (c[:, 2] - 0.3).abs() < 1e-6
+    z4 = (c[:, 2] - 0.4).abs() < 1e-6
+    assert torch.allclose(col[z3], torch.tensor([1.0, 0.0, 0.0]))         # group -> material 1 (plain red)
+    assert torch.allclose(col[z4], torch.tensor([0.0, 0.0, 1.0]))         # material 0: its vertex colours
