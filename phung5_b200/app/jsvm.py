@@ -2218,6 +2218,16 @@ def _num_arg(args, i, default=0.0):
     return default if v is UNDEF else _to_num(v)
 
 
+def _flat(items, depth: float) -> list:
+    out = []
+    for v in items:
+        if isinstance(v, JSArray) and depth >= 1:
+            out.extend(_flat(v.items, depth - 1))
+        else:
+            out.append(v)
+    return out
+
+
 def _array_method(it: Interp, arr: JSArray, name: str):
     a = arr.items
     if name == "length":
@@ -2249,7 +2259,7 @@ def _array_method(it: Interp, arr: JSArray, name: str):
         "reduce": lambda i, t, x: _reduce(it, arr, x),
         "sort": lambda i, t, x: (_sort(it, a, x), arr)[-1],
         "splice": lambda i, t, x: _splice(a, x),
-        "flat": lambda i, t, x: JSArray([w for v in a for w in (v.items if isinstance(v, JSArray) else [v])]),
+        "flat": lambda i, t, x: JSArray(_flat(list(a), _num_arg(x, 0, 1.0))),
         "flatMap": lambda i, t, x: JSArray([w for k, v in enumerate(list(a))
                                             for r in [cb(x[0], v, float(k), arr)]
                                             for w in (r.items if isinstance(r, JSArray) else [r])]),
