@@ -3730,15 +3730,47 @@ def _mat_clone(m: Material):
 
 
 class Texture(Host):
-    __slots__ = ("nbytes",)
+    """A texture: its data size (the texture-data limit) and the mean texel colour (the renders tint a mapped
+    surface by it; texel values are read as 8-bit or float channels of an RGBA / RGB / RG / R layout)."""
+    __slots__ = ("nbytes", "mean")
     cls_name = "Texture"
 
-    def __init__(self, nbytes=0):
+    def __init__(self, nbytes=0, mean=None):
         super().__init__({"isTexture": True, "repeat": Vec(("x", "y"), [1, 1], "Vector2"),
-                          "offset": Vec(("x", "y"), [0, 0], "Vector2")})
+                          "offset": Vec(("x", "y"), [0, 0], "Vector2"), "colorSpace": ""})
         self.nbytes = nbytes
+        self.mean = mean                     # raw mean texel RGB in [0, 1], or None
 
-    js_methods = {"clone": lambda s, i, x: Texture(s.nbytes), "dispose": lambda s, i, x: UNDEF}
+    def linear_mean(self):
+        if self.mean is None:
+            return None
+        if self.props.get("colorSpace") == "srgb":
+            return [c ** 2.2 for c in self.mean]
+        return list(self.mean)
+
+    js_methods = {"clone": lambda s, i, x: Texture(s.nbytes, s.mean), "dispose": lambda s, i, x: UNDEF}
+
+
+def _data_texture(x):
+    """DataTexture(data, width, height, format, type): size and mean texel colour of the data."""
+    data = it_items(_arg(x, 0)) if x else []
+    fmt = _num_arg(x, 3, 1023.0)
+    ch = {1023.0: 4, 1022.0: 3, 1030.0: 2, 1028.0: 1, 1024.0: 1}.get(fmt, 4)
+    typ = _num_arg(x, 4, 1009.0)
+    scale = 255.0 if typ in (1009.0, 1010.0) else 1.0
+    mean = None
+    n = len(data) // ch
+    if n:
+        step = max(1, n // 4096)                  # a sample of the texels is enough for the mean
+        acc = [0.0, 0.0, 0.0]
+        cnt = 0
+        for k in range(0, n, step):
+            px = [_to_num(data[k * ch + c]) / scale for c in range(ch)]
+            rgb = px[:3] if ch >= 3 else [px[0]] * 3
+            acc = [a + max(0.0, min(1.0, v)) for a, v in zip(acc, rgb)]
+            cnt += 1
+        mean = [a / cnt for a in acc]
+    return Texture(len(data), mean)
 
 
 class Object3D(Host):
@@ -4325,8 +4357,9 @@ def make_three(it: Interp) -> JSObject:
         "quad", [_arg(x, k).v() for k in range(3)]))
     three["CubicBezierCurve3"] = Native("CubicBezierCurve3", ctor=lambda i, x: Curve(
         "cubic", [_arg(x, k).v() for k in range(4)]))
-    for t in ("Texture", "CanvasTexture", "DataTexture"):
+    for t in ("Texture", "CanvasTexture"):
         three[t] = Native(t, ctor=lambda i, x: Texture(len(it_items(_arg(x, 0))) if x else 0))
+    three["DataTexture"] = Native("DataTexture", ctor=lambda i, x: _data_texture(x))
     _install_spec_members(it, three)
     for name, val in THREE_CONSTANTS.items():
         three[name] = val
@@ -4686,6 +4719,9 @@ def to_scene_json(root: Object3D, max_depth: int = 64) -> dict:
                          "opacity": _to_num(m.props.get("opacity", 1.0))}
             if _truthy(m.props.get("vertexColors", False)):
                 mats[key]["vertexColors"] = True
+            tex = m.props.get("map")
+            if isinstance(tex, Texture) and tex.linear_mean() is not None:
+                mats[key]["mapMean"] = tex.linear_mean()
             if m.mtype in ("MeshStandardMaterial", "MeshPhysicalMaterial"):
                 mats[key]["roughness"] = _to_num(m.props.get("roughness", 1.0))
                 mats[key]["metalness"] = _to_num(m.props.get("metalness", 0.0))

@@ -160,6 +160,8 @@ def scene_triangles(scene: dict, with_materials: bool = False):
             c = md.get("color", 0xCCCCCC)
             rgb = torch.tensor([(c >> 16) & 255, (c >> 8) & 255, c & 255], dtype=torch.float32) / 255.0
             lin = rgb ** 2.2                                    # sRGB material colour -> linear
+            if md.get("mapMean") is not None:                  # a texture map tints by its mean texel colour
+                lin = lin * torch.tensor(md["mapMean"], dtype=torch.float32)
             vcol = geoms[gid]["data"]["attributes"].get("color") if "data" in geoms[gid] else None
             if md.get("vertexColors") and vcol is not None:
                 # vertex colours are linear; a triangle takes the mean of its corners, times the material colour

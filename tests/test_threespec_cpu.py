@@ -244,3 +244,17 @@ def test_material_arrays_follow_geometry_groups_and_vertex_colours_render():
     z4 = (c[:, 2] - 0.4).abs() < 1e-6
     assert torch.allclose(col[z3], torch.tensor([1.0, 0.0, 0.0]))         # group -> material 1 (plain red)
     assert torch.allclose(col[z4], torch.tensor([0.0, 0.0, 1.0]))         # material 0: its vertex colours
+
+
+def test_data_texture_tints_the_render_by_its_mean_colour():
+    from phung5_b200.render import scene as S
+    src = """export default function generate(THREE) { const g = new THREE.Group();
+      const n = 4; const data = new Uint8Array(n * n * 4);
+      for (let i = 0; i < n * n; i++) { data[4 * i] = i % 2 ? 255 : 0; data[4 * i + 1] = 128; data[4 * i + 3] = 255; }
+      const t = new THREE.DataTexture(data, n, n, THREE.RGBAFormat);          // NoColorSpace: texels are linear
+      g.add(new THREE.Mesh(new THREE.BoxGeometry(0.5, 0.5, 0.5), new THREE.MeshStandardMaterial({map: t, color: 0xffffff})));
+      return g; }"""
+    res = JSChecker(_inline=True).check(src)
+    assert res.ok, res.summary()
+    _, col = S.scene_triangles(res.scene)
+    np.testing.assert_allclose(col[0].numpy(), [0.5, 128 / 255, 0.0], atol=1e-4)
