@@ -286,7 +286,7 @@ class GenerationPipeline:
 
     def startup(self) -> None:
         a = self.s.actors
-        self.checker = JSChecker(CheckerSettings(workers=a.checker.workers))
+        self.checker = JSChecker(CheckerSettings(workers=a.checker.workers, processes=a.checker.processes))
         self.renderer = RendererModule(RendererSettings(slots=a.renderer.workers))
         e = self.s.embedder
         self.embedder = Embedder(EmbedderSettings(enabled=e.enabled, model_dir=e.model_dir, device=e.device,

@@ -163,6 +163,7 @@ class JudgeConfig(ActorConfig):
 
 class WorkerPoolConfig(ActorConfig):
     workers: int = 4
+    processes: bool = False          # checker: a process pool (the interpreter is CPU-bound Python) instead of threads
 
 
 class ActorsConfig(BaseModel):
