@@ -20,7 +20,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, mode, q):
+def _worker(rank, world, port, mode, q, num_pages=200, n_req=2, new_tokens=16):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -35,14 +35,14 @@ def _worker(rank, world, port, mode, q):
         comm = NcclCommunicator()
         spec = SpecConfig(mode=mode, num_draft=3, tree_nodes=10, topk=3, depth=3)
         ecfg = EngineConfig(model=tcfg, spec=spec, draft=DraftConfig(kind="model"),
-                            cache=CacheConfig(page_size=16, num_pages=200))
+                            cache=CacheConfig(page_size=16, num_pages=num_pages))
         eng = LLMEngine(ecfg, device="cpu", target=pack_weights(tcfg, tw, "cpu", rank, world, dtype=torch.float32),
                         drafter=pack_weights(dcfg, dw, "cpu", rank, world, dtype=torch.float32), comm=comm,
                         dtype=torch.float32, max_context=1024)
         g = torch.Generator().manual_seed(3)
-        prompts = [torch.randint(0, 4096, (40,), generator=g).tolist() for _ in range(2)]
-        outs = eng.generate(prompts, SamplingParams(max_new_tokens=16))
-        q.put((rank, outs, prompts))
+        prompts = [torch.randint(0, 4096, (40,), generator=g).tolist() for _ in range(n_req)]
+        outs = eng.generate(prompts, SamplingParams(max_new_tokens=new_tokens))
+        q.put((rank, outs, prompts, eng.stats["preempted"]))
     finally:
         dist.destroy_process_group()
 
@@ -227,3 +227,25 @@ def test_tp2_eagle_head_fused_path_matches_nccl_path():
     ref = RefModel(preset("tiny"), random_weights(preset("tiny"), seed=0, std=0.05))
     for p, o in zip(prompts, fused_out):
         assert o == greedy_generate(ref, p, 12)
+
+
+def test_tp2_preemption_stays_in_step_across_ranks():
+    """A KV pool too small for every request: both ranks admit, preempt and resume the same requests (the
+    scheduler is replicated), and the output still equals the oracle's."""
+    from phung5_b200.engine.oracle import greedy_generate
+    from phung5_b200.models.reference import RefModel
+    from phung5_b200.weights.init import random_weights
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, "chain", q, 16, 4, 40)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert all(p.exitcode == 0 for p in procs)
+    assert res[0][1] == res[1][1] and res[0][3] == res[1][3] > 0
+    ref = RefModel(preset("tiny"), random_weights(preset("tiny"), seed=0, std=0.05))
+    for p, o in zip(res[0][2], res[0][1]):
+        assert o == greedy_generate(ref, p, 40)
