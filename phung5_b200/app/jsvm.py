@@ -2799,7 +2799,22 @@ class Vec(Host):
 
 def _vec_methods():
     def new_like(s, vals):
-        return Vec(s.comps, vals, s.kind)
+        n = Vec(s.comps, vals, s.kind)
+        if s.kind == "Euler":
+            n.props["order"] = _order(s)
+        return n
+
+    def copy_from(s, x):
+        s.setv(other(x, s))
+        if s.kind == "Euler" and isinstance(_arg(x, 0), Vec) and _arg(x, 0).kind == "Euler":
+            s.props["order"] = _order(_arg(x, 0))
+        return s
+
+    def set_all(s, x):
+        s.setv([_num_arg(x, k) for k in range(len(s.comps))])
+        if s.kind == "Euler" and isinstance(_arg(x, 3), str) and _arg(x, 3) in _ORDERS:
+            s.props["order"] = _arg(x, 3)               # Euler.set(x, y, z, order)
+        return s
 
     def other(x, s):
         o = _arg(x, 0)
@@ -2811,9 +2826,9 @@ def _vec_methods():
         return math.sqrt(sum(c * c for c in s.v()))
 
     return {
-        "set": lambda s, i, x: s.setv([_num_arg(x, k) for k in range(len(s.comps))]),
+        "set": lambda s, i, x: set_all(s, x),
         "setScalar": lambda s, i, x: s.setv([_num_arg(x, 0)] * len(s.comps)),
-        "copy": lambda s, i, x: s.setv(other(x, s)),
+        "copy": lambda s, i, x: copy_from(s, x),
         "clone": lambda s, i, x: new_like(s, s.v()),
         "add": lambda s, i, x: s.setv([a + b for a, b in zip(s.v(), other(x, s))]),
         "sub": lambda s, i, x: s.setv([a - b for a, b in zip(s.v(), other(x, s))]),
@@ -3874,7 +3889,9 @@ class Object3D(Host):
         "updateMatrix": lambda s, i, x: (setattr(s.props["matrix"], "m", s.local()), UNDEF)[-1],
         "updateMatrixWorld": lambda s, i, x: UNDEF,
         "traverse": lambda s, i, x: (_traverse(i, s, _arg(x, 0)), UNDEF)[-1],
-        "clone": lambda s, i, x: _obj_clone(s),
+        "clone": lambda s, i, x: _obj_clone(i, s),
+        "copy": lambda s, i, x: _copy_obj(i, s, _arg(x, 0), _arg(x, 1) is UNDEF or _truthy(_arg(x, 1)))
+        if isinstance(_arg(x, 0), Object3D) else s,
         "getObjectByName": lambda s, i, x: _find_name(s, _to_str(_arg(x, 0))),
         "setMatrixAt": lambda s, i, x: (s.props.setdefault("__inst", {}).__setitem__(int(_num_arg(x, 0)), [row[:] for row in _arg(x, 1).m]), UNDEF)[-1],
         "setColorAt": lambda s, i, x: UNDEF,
@@ -3974,18 +3991,42 @@ def _find_name(o, name):
     return UNDEF
 
 
-def _obj_clone(o: Object3D) -> Object3D:
-    n = Object3D(o.otype, o.props.get("geometry"), o.props.get("material"))
+def _copy_obj(it, n: Object3D, o: Object3D, recursive: bool = True) -> Object3D:
+    """Object3D.copy: n takes o's transform (rotation order included), name, flags, a deep copy of userData and
+    (recursive) clones of o's children; geometry and material are shared, as three.js shares them."""
     for k, v in o.props.items():
         if k in ("children", "parent", "matrix"):
             continue
-        if isinstance(v, Vec):
+        if k in ("position", "rotation", "scale"):
             n.props[k].setv(v.v())
-        elif k not in ("position", "rotation", "scale"):
+            if k == "rotation":
+                n.props[k].props["order"] = _order(v)
+        elif k == "userData":
+            n.props[k] = _user_data_copy(it, v)
+        elif k == "__inst":
+            n.props[k] = {i: [row[:] for row in m] for i, m in v.items()}
+        else:
             n.props[k] = v
-    for c in o.children():
-        n.add([_obj_clone(c)])
+    if recursive:
+        for c in o.children():
+            n.add([_obj_clone(it, c)])
     return n
+
+
+def _user_data_copy(it, v):
+    """three.js copies userData through JSON; data JSON cannot hold (a cycle, e.g. a stored object) is copied
+    shallowly instead of throwing."""
+    if not isinstance(v, JSObject):
+        return v
+    try:
+        text = _json_stringify(it, v, None)
+        return _json_parse(text) if isinstance(text, str) else JSObject()
+    except _Throw:
+        return JSObject(dict(v.props))
+
+
+def _obj_clone(it, o: Object3D) -> Object3D:
+    return _copy_obj(it, Object3D(o.otype, o.props.get("geometry"), o.props.get("material")), o)
 
 
 class Shape(Host):
@@ -4317,7 +4358,12 @@ class Box3(Host):
 
 
 def _vec_ctor(name, comps):
-    return Native(name, ctor=lambda it, x: Vec(comps, [_num_arg(x, k) for k in range(len(comps))], name))
+    def make(it, x):
+        v = Vec(comps, [_num_arg(x, k) for k in range(len(comps))], name)
+        if name == "Euler" and isinstance(_arg(x, 3), str) and _arg(x, 3) in _ORDERS:
+            v.props["order"] = _arg(x, 3)               # new Euler(x, y, z, order)
+        return v
+    return Native(name, ctor=make)
 
 
 def make_three(it: Interp) -> JSObject:

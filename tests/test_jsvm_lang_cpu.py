@@ -141,3 +141,22 @@ def test_euler_order_is_honoured():
     assert got[0] == pytest.approx(rot("YXZ", (0.3, 0.5, 0.2), (1, 2, 3))[0])
     assert got[1] == pytest.approx(rot("XYZ", (0.3, 0.5, 0.2), (1, 2, 3))[0]) and got[0] != pytest.approx(got[1])
     assert got[2:] == pytest.approx([0.3, 0.5, 0.2])          # written back in the object's own order
+
+
+def test_euler_order_travels_with_constructor_set_copy_and_object_clone():
+    pre = """
+      const e = new THREE.Euler(0.1, 0.2, 0.3, 'ZYX');
+      const f = new THREE.Euler().copy(e), h = e.clone(), k = new THREE.Euler().set(1, 2, 3, 'YZX');
+      const m = new THREE.Mesh(new THREE.BoxGeometry(0.2, 0.2, 0.2), new THREE.MeshBasicMaterial());
+      m.rotation.order = 'ZXY'; m.rotation.set(0.3, 0.5, 0.7); m.position.set(0.1, 0.2, 0);
+      m.userData.tag = {a: 1}; m.add(new THREE.Object3D());
+      const c = m.clone(); c.position.x = 0.3;
+      const d = new THREE.Mesh(); d.copy(m, false);
+    """
+    got = _ev("[e.order, f.order, h.order, k.order, c.rotation.order, c.quaternion.w - m.quaternion.w, m.position.x, "
+              "c.geometry === m.geometry, c.userData.tag === m.userData.tag, c.userData.tag.a, c.children.length, "
+              "d.rotation.order, d.position.y, d.children.length, d.material === m.material]", pre).items
+    assert got[:5] == ["ZYX", "ZYX", "ZYX", "YZX", "ZXY"]
+    assert got[5] == pytest.approx(0.0) and got[6] == pytest.approx(0.1)      # the clone owns its transform
+    assert got[7] is True and got[8] is False and got[9] == 1 and got[10] == 1  # shared geometry, copied userData
+    assert got[11:] == ["ZXY", pytest.approx(0.2), 0, True]                     # copy(source, recursive = false)
