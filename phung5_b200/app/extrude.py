@@ -179,8 +179,9 @@ def extrude(outer, holes=(), depth: float = 1.0, bevel: bool = True, thickness: 
     poly = bridge_holes(cap_rings[0], cap_rings[1:]) if len(cap_rings) > 1 else cap_rings[0]
     tris = ear_clip(poly)
     lookup: Dict[Pt, int] = {}
-    for zc, back in ((layers[0][0], False), (layers[-1][0], True)):
-        base = len(verts)
+    # two caps facing out of the solid; a flat shape (one layer) is a single face toward +z with no side walls
+    caps = ((layers[0][0], False), (layers[-1][0], True)) if len(layers) > 1 else ((layers[0][0], True),)
+    for zc, back in caps:
         lookup = {}
         idx = []
         for p in poly:
@@ -190,8 +191,8 @@ def extrude(outer, holes=(), depth: float = 1.0, bevel: bool = True, thickness: 
             idx.append(lookup[p])
         for a, b, c in tris:
             faces.append((idx[a], idx[b], idx[c]) if back else (idx[c], idx[b], idx[a]))
-        if len(layers) == 1:
-            break
+    if len(layers) == 1:
+        return verts, faces
     # side walls between consecutive layers, for the outline and every hole
     for r in range(len(rings)):
         n = len(rings[r])

@@ -29,7 +29,13 @@ MAX_FILE_BYTES = 1_048_576          # source size (UTF-8)
 BOUND = 0.5                         # the model must fit inside [-0.5, 0.5] on every axis
 BOUND_TOL = 1e-6                    # float32 vertex storage vs the validator's doubles
 LITERAL_BUDGET = 50 * 1024
-ROOT_TYPES = {"Group", "Mesh", "LineSegments", "Points", "Object3D", "InstancedMesh", "Line"}
+ROOT_TYPES = {"Group", "Mesh", "LineSegments", "Points"}      # the returned object's type (a bare one is wrapped)
+DRAW_TYPES = {"Mesh", "InstancedMesh", "Line", "LineSegments", "LineLoop", "Points"}   # isMesh / isLine / isPoints
+# material slots whose DataTexture counts toward the texture-data limit
+MAP_PROPS = ("map", "normalMap", "roughnessMap", "metalnessMap", "aoMap", "emissiveMap", "displacementMap", "bumpMap",
+             "alphaMap", "envMap", "lightMap", "specularIntensityMap", "specularColorMap", "sheenRoughnessMap",
+             "sheenColorMap", "transmissionMap", "thicknessMap", "clearcoatMap", "clearcoatNormalMap",
+             "clearcoatRoughnessMap", "iridescenceMap", "iridescenceThicknessMap", "anisotropyMap")
 
 # the output specification's tables (app/threespec.py); `arguments` is a function's implicit binding
 ALLOWED_ROOTS = set(threespec.ALLOWED_ROOT_IDENTIFIERS) | {"arguments"}
@@ -540,9 +546,11 @@ def post_validate(root) -> tuple:
         fail("INVALID_RETURN_TYPE", f"generate must return an Object3D, got {jsvm._typeof(root)}")
         return fails, {}
     if root.otype not in ROOT_TYPES:
-        fail("INVALID_ROOT_TYPE", f"root type {root.otype} is not one of {sorted(ROOT_TYPES)}")
+        fail("INVALID_RETURN_TYPE", f"returned {root.otype}, expected Group/Mesh/LineSegments/Points")
+        return fails, {}
     stats = {"vertices": 0, "drawCalls": 0, "depth": 0, "instances": 0, "textureBytes": 0, "meshes": 0}
     seen = set()
+    seen_tex = set()
     stack = [(root, 0)]
     bad_numbers = False
     while stack:
@@ -559,7 +567,9 @@ def post_validate(root) -> tuple:
             if any(not math.isfinite(x) for x in o.props[k].v()):
                 bad_numbers = True
         g = o.props.get("geometry")
-        if isinstance(g, jsvm.Geometry) and o.otype in ("Mesh", "InstancedMesh", "LineSegments", "Points", "Line"):
+        if o.otype in DRAW_TYPES and not isinstance(g, jsvm.Geometry):
+            stats["drawCalls"] += 1
+        if isinstance(g, jsvm.Geometry) and o.otype in DRAW_TYPES:
             try:
                 v, tris = jsvm.geometry_mesh(g)
                 nv = max(int(v.shape[0]), declared_vertices(g, int(tris.shape[0])))
@@ -568,19 +578,18 @@ def post_validate(root) -> tuple:
             except jsvm._Throw as e:
                 fail("GEOMETRY_ERROR", jsvm._to_str(e.value.props.get("message", "")) if isinstance(e.value, jsvm.JSObject) else "bad geometry")
                 nv = 0
-            if o.otype == "InstancedMesh":
-                cnt = int(jsvm._to_num(o.props.get("count", 0)))
-                stats["instances"] += cnt
-                stats["vertices"] += nv * cnt
-            else:
-                stats["vertices"] += nv
+            if o.otype == "InstancedMesh":                 # one draw of the geometry, `count` instances
+                stats["instances"] += int(jsvm._to_num(o.props.get("count", 0)))
+            stats["vertices"] += nv
             stats["drawCalls"] += 1
             stats["meshes"] += 1
             m = o.props.get("material")
             for mm in (m.items if isinstance(m, jsvm.JSArray) else [m]):
                 if isinstance(mm, jsvm.Material):
-                    for val in mm.props.values():
-                        if isinstance(val, jsvm.Texture):
+                    for key in MAP_PROPS:
+                        val = mm.props.get(key)
+                        if isinstance(val, jsvm.Texture) and val.props.get("isDataTexture") and id(val) not in seen_tex:
+                            seen_tex.add(id(val))
                             stats["textureBytes"] += val.nbytes
         for c in o.children():
             stack.append((c, d + 1))

@@ -1009,6 +1009,21 @@ class JSArray:
         self.items = [] if items is None else items
 
 
+class TypedArray(JSArray):
+    """Float32Array, Uint16Array, ...: a fixed-length array whose elements are stored converted to its element
+    type (float32 rounding, modular integers, clamped bytes). A BufferAttribute holds the module's own typed
+    array, so writes through either are seen by both, as in three.js."""
+    __slots__ = ("kind",)
+
+    def __init__(self, kind: str, items: Optional[list] = None, coerced: bool = False):
+        super().__init__([] if items is None else (items if coerced else _typed_values(kind, items)))
+        self.kind = kind
+
+    @property
+    def cls_name(self):
+        return self.kind
+
+
 class JSFunction:
     __slots__ = ("name", "params", "rest", "body", "env", "arrow", "this", "props", "home")
 
@@ -1745,6 +1760,8 @@ class Interp:
             idx = _index(key)
             if idx is not None:
                 return obj.items[idx] if idx < len(obj.items) else UNDEF
+            if isinstance(obj, TypedArray):
+                return _typed_method(self, obj, _to_str(key))
             return _array_method(self, obj, _to_str(key))
         if isinstance(obj, Host):
             k = _to_str(key)
@@ -1804,6 +1821,11 @@ class Interp:
         return UNDEF
 
     def put(self, obj, key, value):
+        if isinstance(obj, TypedArray):
+            idx = _index(key)
+            if idx is not None and idx < len(obj.items):
+                obj.items[idx] = _typed_value(obj.kind, value)
+            return                                      # out-of-range indices and length are ignored
         if isinstance(obj, JSArray):
             idx = _index(key)
             if idx is not None:
@@ -2506,7 +2528,7 @@ def _install_globals(it: Interp):
                   "trunc": lambda v: float(math.trunc(v)) if math.isfinite(v) else v,
                   "sign": lambda v: v if v != v else float((v > 0) - (v < 0)),
                   "pow": lambda a, b: a ** b, "hypot": lambda *v: math.hypot(*v),
-                  "fround": lambda v: struct.unpack("f", struct.pack("f", v))[0]}.items():
+                  "fround": _fround}.items():
         math_props[nm] = _nat(nm, mfn(safe(f)))
     math_props["min"] = _nat("min", lambda i, t, x: min([_to_num(v) for v in x], default=math.inf))
     math_props["max"] = _nat("max", lambda i, t, x: max([_to_num(v) for v in x], default=-math.inf))
@@ -2553,7 +2575,8 @@ def _install_globals(it: Interp):
         return JSArray(items)
 
     g.declare("Array", Native("Array", fn=lambda i, t, x: array_ctor(i, x), ctor=array_ctor, props={
-        "isArray": _nat("isArray", lambda i, t, x: isinstance(_arg(x, 0), JSArray)),
+        "isArray": _nat("isArray", lambda i, t, x: isinstance(_arg(x, 0), JSArray) and
+                        not isinstance(_arg(x, 0), TypedArray)),
         "from": _nat("from", array_from),
         "of": _nat("of", lambda i, t, x: JSArray(list(x)))}))
     g.declare("Object", Native("Object", fn=lambda i, t, x: JSObject(), ctor=lambda i, x: JSObject(), props={
@@ -2671,16 +2694,131 @@ def _mkey(v):
     return ("o", id(v))
 
 
+TYPED_BYTES = {"Float32Array": 4, "Float64Array": 8, "Int8Array": 1, "Uint8Array": 1, "Uint8ClampedArray": 1,
+               "Int16Array": 2, "Uint16Array": 2, "Int32Array": 4, "Uint32Array": 4}
+_TYPED_INT = {"Int8Array": (8, True), "Uint8Array": (8, False), "Int16Array": (16, True), "Uint16Array": (16, False),
+              "Int32Array": (32, True), "Uint32Array": (32, False)}
+
+
+def _fround(v: float) -> float:
+    try:
+        return struct.unpack("f", struct.pack("f", v))[0]
+    except OverflowError:
+        return math.copysign(math.inf, v)
+
+
+def _typed_value(kind: str, v) -> float:
+    """One element stored into a typed array of `kind` (ECMAScript's ToInt8 ... ToUint32, ToUint8Clamp, and float32
+    rounding)."""
+    x = _to_num(v)
+    if kind == "Float64Array":
+        return x
+    if kind == "Float32Array":
+        return _fround(x)
+    if kind == "Uint8ClampedArray":
+        return 0.0 if x != x else float(round(min(255.0, max(0.0, x))))      # ties to even
+    if not math.isfinite(x):
+        return 0.0
+    bits, signed = _TYPED_INT[kind]
+    n = int(x) % (1 << bits)
+    return float(n - (1 << bits) if signed and n >= 1 << (bits - 1) else n)
+
+
+def _typed_values(kind: str, vals) -> list:
+    """_typed_value over a sequence, vectorised for the large buffers geometry code builds."""
+    import numpy as np
+    a = np.asarray([_to_num(v) if not isinstance(v, float) else v for v in vals], dtype=np.float64)
+    if kind == "Float64Array":
+        return a.tolist()
+    if kind == "Float32Array":
+        with np.errstate(over="ignore"):
+            return a.astype(np.float32).astype(np.float64).tolist()
+    if kind == "Uint8ClampedArray":
+        return np.round(np.clip(np.nan_to_num(a, nan=0.0), 0.0, 255.0)).tolist()
+    bits, signed = _TYPED_INT[kind]
+    a = np.trunc(np.where(np.isfinite(a), a, 0.0))
+    m = float(1 << bits)
+    a = np.mod(a, m)
+    if signed:
+        a = np.where(a >= m / 2, a - m, a)
+    return (a + 0.0).tolist()
+
+
+def _typed_from(it, kind: str, src, fn=UNDEF) -> TypedArray:
+    if isinstance(src, (int, float)) and not isinstance(src, bool):
+        n = int(src) if src == src else 0
+        if n < 0 or n > it.lim.array_len:
+            raise JSBudget("RangeError", "invalid typed array length")
+        return TypedArray(kind, [0.0] * n, coerced=True)
+    if src is UNDEF or src is None:
+        return TypedArray(kind, [], coerced=True)
+    if isinstance(src, (JSArray, JSMap, JSSet, str)):
+        vals = list(it.iterate(src))
+    else:                                               # an array-like object: {length: n, 0: ..., 1: ...}
+        n = _to_num(it.get(src, "length"))
+        n = int(n) if n == n and n > 0 else 0
+        if n > it.lim.array_len:
+            raise JSBudget("RangeError", "invalid typed array length")
+        vals = [it.get(src, float(k)) for k in range(n)]
+    if fn is not UNDEF:
+        vals = [it.call(fn, UNDEF, [v, float(k)]) for k, v in enumerate(vals)]
+    return TypedArray(kind, vals)
+
+
 def _typed_array_ctor(it, cls):
-    def ctor(i, x):
-        src = _arg(x, 0, 0.0)
-        if isinstance(src, float):
-            n = int(src)
-            if n < 0 or n > it.lim.array_len:
-                raise JSBudget("RangeError", "invalid typed array length")
-            return JSArray([0.0] * n)
-        return JSArray([_to_num(v) for v in it.iterate(src)])
-    return Native(cls, ctor=ctor, props={"from": _nat("from", lambda i, t, x: ctor(i, [x[0]]))})
+    return Native(cls, ctor=lambda i, x: _typed_from(it, cls, _arg(x, 0, 0.0)),
+                  props={"from": _nat("from", lambda i, t, x: _typed_from(it, cls, _arg(x, 0), _arg(x, 1))),
+                         "of": _nat("of", lambda i, t, x: TypedArray(cls, list(x))),
+                         "BYTES_PER_ELEMENT": float(TYPED_BYTES[cls])})
+
+
+_TYPED_SAME_KIND = ("map", "filter", "slice")
+_TYPED_ABSENT = ("push", "pop", "shift", "unshift", "splice", "concat", "flat", "flatMap")
+
+
+def _typed_method(it, arr: TypedArray, name: str):
+    """Typed-array members: set / subarray / BYTES_PER_ELEMENT / byteLength, map / filter / slice returning the
+    same kind, fill converting its value, sort numeric by default; no push / pop / splice / concat (fixed length).
+    subarray returns a copy of the range (three.js modules read it; a write through it does not reach the
+    parent array)."""
+    a = arr.items
+    if name == "BYTES_PER_ELEMENT":
+        return float(TYPED_BYTES[arr.kind])
+    if name == "byteLength":
+        return float(len(a) * TYPED_BYTES[arr.kind])
+    if name in _TYPED_ABSENT:
+        return UNDEF
+    if name == "set":
+        def set_(i, t, x):
+            src, off = _arg(x, 0), int(_num_arg(x, 1, 0.0))
+            vals = list(it.iterate(src)) if isinstance(src, JSArray) else []
+            if off < 0 or off + len(vals) > len(a):
+                raise _Throw(_error_obj("RangeError", "offset is out of bounds"))
+            a[off:off + len(vals)] = [_typed_value(arr.kind, v) for v in vals]
+            return UNDEF
+        return _nat("set", set_)
+    if name == "subarray":
+        return _nat("subarray", lambda i, t, x: TypedArray(
+            arr.kind, a[_slice_idx(x, 0, len(a), 0):_slice_idx(x, 1, len(a), len(a))], coerced=True))
+    if name == "fill":
+        def fill(i, t, x):
+            _fill(a, [_typed_value(arr.kind, _arg(x, 0))] + list(x[1:]))
+            return arr
+        return _nat("fill", fill)
+    if name == "sort":
+        def sort(i, t, x):
+            if _arg(x, 0) is UNDEF:
+                a.sort(key=lambda v: (v != v, v))       # numeric, NaN last
+            else:
+                _sort(it, a, x)
+            return arr
+        return _nat("sort", sort)
+    m = _array_method(it, arr, name)
+    if name in _TYPED_SAME_KIND and isinstance(m, Native):
+        inner = m.fn
+        return _nat(name, lambda i, t, x: (lambda r: TypedArray(arr.kind, r.items) if isinstance(r, JSArray) else r)(
+            inner(i, t, x)))
+    return m
 
 
 def _assign(it, x):
@@ -3225,9 +3363,25 @@ class Quaternion(Host):
                                                                                         _m2q(_arg(x, 0).cur())))))),
         "dot": lambda s, i, x: sum(a * b for a, b in zip(_m2q(s.cur()), _m2q(_arg(x, 0).cur()))),
         "toArray": lambda s, i, x: JSArray(list(_m2q(s.cur()))),
+        "fromArray": lambda s, i, x: s.put(_q2m([_to_num(i.get(_arg(x, 0), float(int(_num_arg(x, 1, 0.0)) + k)))
+                                                 for k in range(4)])),
+        "length": lambda s, i, x: 1.0,                  # held as a rotation: always a unit quaternion
+        "lengthSq": lambda s, i, x: 1.0,
+        "equals": lambda s, i, x: isinstance(_arg(x, 0), Quaternion) and all(
+            abs(a - b) < 1e-12 for a, b in zip(_m2q(s.cur()), _m2q(_arg(x, 0).cur()))),
+        "rotateTowards": lambda s, i, x: _rotate_towards(s, _arg(x, 0), _num_arg(x, 1)),
         "clone": lambda s, i, x: Quaternion([row[:] for row in s.cur()]),
         "copy": lambda s, i, x: s.put([row[:] for row in _arg(x, 0).cur()]),
     }
+
+
+def _rotate_towards(q: "Quaternion", target, step: float):
+    """Turn q toward target by at most `step` radians (slerp by step / angle)."""
+    a, b = _m2q(q.cur()), _m2q(target.cur())
+    angle = 2 * math.acos(min(1.0, abs(sum(p * r for p, r in zip(a, b)))))
+    if angle == 0:
+        return q
+    return q.put(_q2m(_slerp(a, b, min(1.0, step / angle))))
 
 
 def _m2q(m):
@@ -3319,8 +3473,20 @@ _NAMED_COLORS = {"white": 0xFFFFFF, "black": 0x000000, "red": 0xFF0000, "green":
                  "dimgray": 0x696969, "wheat": 0xF5DEB3, "crimson": 0xDC143C, "indigo": 0x4B0082, "violet": 0xEE82EE}
 
 
+def _srgb_to_linear(c: float) -> float:
+    """The sRGB transfer function's inverse (IEC 61966-2-1)."""
+    return c * 0.0773993808 if c < 0.04045 else (c * 0.9478672986 + 0.0521327014) ** 2.4
+
+
+def _linear_to_srgb(c: float) -> float:
+    return c * 12.92 if c < 0.0031308 else 1.055 * (c ** 0.41666) - 0.055
+
+
 class Color(Host):
-    """sRGB components in [0, 1] (three.js keeps linear internally; the scene JSON stores the sRGB hex)."""
+    """r, g, b in three.js's working colour space, linear sRGB: hex values, CSS strings and the sRGB colour-space
+    arguments are converted on the way in, getHex / getStyle / the scene JSON's hex convert back, and
+    setRGB / setHSL / setScalar / arithmetic work on the linear components (as three.js's colour management
+    does)."""
     __slots__ = ()
     cls_name = "Color"
 
@@ -3330,6 +3496,12 @@ class Color(Host):
     def rgb(self):
         return [_to_num(self.props[c]) for c in "rgb"]
 
+    def srgb(self):
+        return [_linear_to_srgb(c) for c in self.rgb()]
+
+    def set_srgb(self, r, g, b):
+        return self.set_rgb(_srgb_to_linear(r), _srgb_to_linear(g), _srgb_to_linear(b))
+
     def set_any(self, x):
         a = _arg(x, 0)
         if len(x) >= 3:
@@ -3338,7 +3510,7 @@ class Color(Host):
             return self.set_rgb(*a.rgb())
         if isinstance(a, (int, float)) and not isinstance(a, bool):
             h = int(a) & 0xFFFFFF
-            return self.set_rgb(((h >> 16) & 255) / 255, ((h >> 8) & 255) / 255, (h & 255) / 255)
+            return self.set_srgb(((h >> 16) & 255) / 255, ((h >> 8) & 255) / 255, (h & 255) / 255)
         if isinstance(a, str):
             s = a.strip().lower()
             if s.startswith("#"):
@@ -3350,12 +3522,12 @@ class Color(Host):
                 except ValueError:
                     return self
                 return self.set_any([float(h)])
-            m = re.match(r"rgb\(\s*(\d+)\s*,\s*(\d+)\s*,\s*(\d+)\s*\)", s)
+            m = re.match(r"rgba?\(\s*(\d+)\s*,\s*(\d+)\s*,\s*(\d+)\s*(,\s*[\d.]+\s*)?\)", s)
             if m:
-                return self.set_rgb(*(int(g) / 255 for g in m.groups()))
-            m = re.match(r"hsl\(\s*([\d.]+)\s*,\s*([\d.]+)%\s*,\s*([\d.]+)%\s*\)", s)
+                return self.set_srgb(*(min(255, int(g)) / 255 for g in m.groups()[:3]))
+            m = re.match(r"hsla?\(\s*([\d.]+)\s*,\s*([\d.]+)%\s*,\s*([\d.]+)%\s*(,\s*[\d.]+\s*)?\)", s)
             if m:
-                return self.set_hsl(float(m.group(1)) / 360, float(m.group(2)) / 100, float(m.group(3)) / 100)
+                return self.set_hsl(float(m.group(1)) / 360, float(m.group(2)) / 100, float(m.group(3)) / 100, True)
             if s in _NAMED_COLORS:
                 return self.set_any([float(_NAMED_COLORS[s])])
         return self
@@ -3364,12 +3536,13 @@ class Color(Host):
         self.props.update({"r": float(r), "g": float(g), "b": float(b)})
         return self
 
-    def set_hsl(self, h, s, l):
+    def set_hsl(self, h, s, l, srgb=False):
         h = h % 1.0
         s = min(max(s, 0.0), 1.0)
         l = min(max(l, 0.0), 1.0)
+        put = self.set_srgb if srgb else self.set_rgb
         if s == 0:
-            return self.set_rgb(l, l, l)
+            return put(l, l, l)
         p = l * (1 + s) if l <= 0.5 else l + s - l * s
         q = 2 * l - p
 
@@ -3382,10 +3555,10 @@ class Color(Host):
             if t < 2 / 3:
                 return q + (p - q) * 6 * (2 / 3 - t)
             return q
-        return self.set_rgb(hue(h + 1 / 3), hue(h), hue(h - 1 / 3))
+        return put(hue(h + 1 / 3), hue(h), hue(h - 1 / 3))
 
-    def get_hsl(self):
-        r, g, b = self.rgb()
+    def get_hsl(self, srgb=False):
+        r, g, b = self.srgb() if srgb else self.rgb()
         mx, mn = max(r, g, b), min(r, g, b)
         l = (mx + mn) / 2
         if mx == mn:
@@ -3401,7 +3574,8 @@ class Color(Host):
         return h / 6, s, l
 
     def hex(self) -> int:
-        r, g, b = (max(0, min(255, int(round(c * 255)))) for c in self.rgb())
+        """The sRGB hex value (getHex)."""
+        r, g, b = (int(math.floor(max(0.0, min(255.0, c * 255)) + 0.5)) for c in self.srgb())
         return (r << 16) | (g << 8) | b
 
     def set_special(self, it, key, value):
@@ -3413,14 +3587,22 @@ class Color(Host):
     js_methods = {
         "set": lambda s, i, x: s.set_any(x),
         "setHex": lambda s, i, x: s.set_any([float(int(_num_arg(x, 0)))]),
-        "setRGB": lambda s, i, x: s.set_rgb(_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2)),
-        "setHSL": lambda s, i, x: s.set_hsl(_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2)),
+        "setRGB": lambda s, i, x: (s.set_srgb if _arg(x, 3) == "srgb" else s.set_rgb)(
+            _num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2)),
+        "setHSL": lambda s, i, x: s.set_hsl(_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2), _arg(x, 3) == "srgb"),
+        "getRGB": lambda s, i, x: (lambda t, c: (t.props.update({"r": c[0], "g": c[1], "b": c[2]}), t)[-1])(
+            _arg(x, 0) if isinstance(_arg(x, 0), (JSObject, Color)) else JSObject(),
+            s.srgb() if _arg(x, 1) == "srgb" else s.rgb()),
+        "convertSRGBToLinear": lambda s, i, x: s.set_srgb(*s.rgb()),
+        "convertLinearToSRGB": lambda s, i, x: s.set_rgb(*s.srgb()),
+        "copySRGBToLinear": lambda s, i, x: s.set_srgb(*_arg(x, 0).rgb()),
+        "copyLinearToSRGB": lambda s, i, x: s.set_rgb(*_arg(x, 0).srgb()),
         "setStyle": lambda s, i, x: s.set_any(x[:1]),
         "setScalar": lambda s, i, x: s.set_rgb(*[_num_arg(x, 0)] * 3),
         "getHex": lambda s, i, x: float(s.hex()),
         "getHexString": lambda s, i, x: f"{s.hex():06x}",
-        "getStyle": lambda s, i, x: f"rgb({','.join(str(int(round(c * 255))) for c in s.rgb())})",
-        "getHSL": lambda s, i, x: _hsl_out(s, _arg(x, 0)),
+        "getStyle": lambda s, i, x: f"rgb({','.join(str(int(math.floor(c * 255 + 0.5))) for c in s.srgb())})",
+        "getHSL": lambda s, i, x: _hsl_out(s, _arg(x, 0), _arg(x, 1) == "srgb"),
         "offsetHSL": lambda s, i, x: (lambda h: s.set_hsl(h[0] + _num_arg(x, 0), h[1] + _num_arg(x, 1),
                                                          h[2] + _num_arg(x, 2)))(s.get_hsl()),
         "clone": lambda s, i, x: Color(*s.rgb()),
@@ -3432,14 +3614,12 @@ class Color(Host):
         "lerp": lambda s, i, x: s.set_rgb(*[a + (b - a) * _num_arg(x, 1) for a, b in zip(s.rgb(), _arg(x, 0).rgb())]),
         "lerpColors": lambda s, i, x: s.set_rgb(*[a + (b - a) * _num_arg(x, 2)
                                                   for a, b in zip(_arg(x, 0).rgb(), _arg(x, 1).rgb())]),
-        "convertSRGBToLinear": lambda s, i, x: s,
-        "convertLinearToSRGB": lambda s, i, x: s,
         "equals": lambda s, i, x: s.rgb() == _arg(x, 0).rgb(),
     }
 
 
-def _hsl_out(c, target):
-    h, s, l = c.get_hsl()
+def _hsl_out(c, target, srgb=False):
+    h, s, l = c.get_hsl(srgb)
     o = target if isinstance(target, JSObject) else JSObject()
     o.props.update({"h": h, "s": s, "l": l})
     return o
@@ -3542,13 +3722,13 @@ class Geometry(Host):
         "rotateZ": lambda s, i, x: s.apply(_compose([0, 0, 0], [0, 0, _num_arg(x, 0)], [1, 1, 1])),
         "applyMatrix4": lambda s, i, x: s.apply(_arg(x, 0).m),
         "center": lambda s, i, x: _geom_center(s),
-        "computeVertexNormals": lambda s, i, x: UNDEF,
+        "computeVertexNormals": lambda s, i, x: _compute_normals(s),
         "clone": lambda s, i, x: _geom_clone(s),
         "dispose": lambda s, i, x: UNDEF,
         "setAttribute": lambda s, i, x: (_bake(s), s.buffer.__setitem__(_to_str(_arg(x, 0)), _arg(x, 1)), s)[-1],
         "getAttribute": lambda s, i, x: (_bake(s), s.buffer.get(_to_str(_arg(x, 0)), UNDEF))[-1],
         "deleteAttribute": lambda s, i, x: (_bake(s), s.buffer.pop(_to_str(_arg(x, 0)), None), s)[-1],
-        "setIndex": lambda s, i, x: (_bake(s), s.buffer.__setitem__("__index", _arg(x, 0)), s)[-1],
+        "setIndex": lambda s, i, x: (_bake(s), s.buffer.__setitem__("__index", _index_attr(i, _arg(x, 0))), s)[-1],
         "addGroup": lambda s, i, x: (s.props.setdefault("groups", JSArray()).items.append(JSObject(
             {"start": _num_arg(x, 0), "count": _num_arg(x, 1), "materialIndex": _num_arg(x, 2)})), UNDEF)[-1],
         "clearGroups": lambda s, i, x: (s.props.__setitem__("groups", JSArray()), UNDEF)[-1],
@@ -3560,6 +3740,34 @@ class Geometry(Host):
         "setFromPoints": lambda s, i, x: (s.buffer.__setitem__("position", BufferAttribute(
             [c for p in it_items(_arg(x, 0)) for c in (p.v() + [0.0])[:3]], 3)), s)[-1],
     }
+
+
+def _index_attr(it, idx):
+    """setIndex's argument as three.js stores it: an array becomes a Uint16 (or, above 65535, Uint32) attribute."""
+    if isinstance(idx, JSArray) and not isinstance(idx, TypedArray):
+        vals = [_to_num(v) for v in it.iterate(idx)]
+        return BufferAttribute(vals, 1, "Uint32Array" if any(v > 65535 for v in vals) else "Uint16Array")
+    if isinstance(idx, TypedArray):
+        return BufferAttribute(idx, 1)
+    return idx if isinstance(idx, BufferAttribute) else None
+
+
+def _compute_normals(g: Geometry):
+    """computeVertexNormals: area-weighted sums of the face normals around each vertex of the position buffer
+    (indexed geometry shares them across faces; non-indexed geometry gets flat normals), written into the existing
+    normal attribute when it has the right size."""
+    _bake(g)
+    pos = g.buffer.get("position")
+    if not (isinstance(pos, BufferAttribute) and pos.item == 3):
+        return UNDEF
+    v, f = geometry_mesh(g)
+    vals = _vertex_normals(v, f).reshape(-1).tolist()
+    nrm = g.buffer.get("normal")
+    if isinstance(nrm, BufferAttribute) and nrm.item == 3 and len(nrm.array) == len(vals) and nrm is not pos:
+        nrm.array = vals
+    else:
+        g.buffer["normal"] = BufferAttribute(vals, 3)
+    return UNDEF
 
 
 def _non_indexed(g: Geometry) -> Geometry:
@@ -3590,7 +3798,7 @@ def _geom_sphere(g: Geometry):
 def _geom_clone(g: Geometry) -> Geometry:
     n = Geometry(g.gtype, dict(g.params))
     n.xform = [row[:] for row in g.xform]
-    n.buffer = {k: (BufferAttribute(v.array, v.item) if isinstance(v, BufferAttribute) else v)
+    n.buffer = {k: (BufferAttribute(list(v.array), v.item, v.data.kind) if isinstance(v, BufferAttribute) else v)
                 for k, v in g.buffer.items()}
     n.baked = g.baked
     return n
@@ -3625,6 +3833,10 @@ def _vertex_normals(v, f):
     return n / n.norm(dim=1, keepdim=True).clamp(min=1e-12)
 
 
+_NON_INDEXED = {"ExtrudeGeometry", "PolyhedronGeometry", "TetrahedronGeometry", "OctahedronGeometry",
+                "IcosahedronGeometry", "DodecahedronGeometry"}
+
+
 def _bake(g: Geometry) -> None:
     """Turn a parametric primitive into explicit buffers (transform applied), once."""
     if g.baked or g.gtype == "BufferGeometry":
@@ -3643,11 +3855,21 @@ def _bake(g: Geometry) -> None:
         v = (torch.cat([v, torch.ones(v.shape[0], 1)], 1) @ m.t())[:, :3]
     else:
         v, f = geometry_mesh(g)
+    nrm = _vertex_normals(v, f)
+    indexed = g.gtype not in _NON_INDEXED
+    if not indexed and f.numel():
+        # three.js builds these without an index: three vertices of their own per triangle; the polyhedra with
+        # detail > 0 keep smooth (shared) normals, the rest are flat
+        smooth = g.gtype != "ExtrudeGeometry" and int(_to_num(g.params.get("detail", 0) or 0)) > 0
+        flat = f.reshape(-1)
+        nrm = nrm[flat] if smooth else _vertex_normals(v[flat], torch.arange(flat.numel()).view(-1, 3))
+        v = v[flat]
     g.buffer.setdefault("position", BufferAttribute(v.reshape(-1).tolist(), 3))
-    g.buffer.setdefault("normal", BufferAttribute(_vertex_normals(v, f).reshape(-1).tolist(), 3))
+    g.buffer.setdefault("normal", BufferAttribute(nrm.reshape(-1).tolist(), 3))
     if uv is not None:
         g.buffer.setdefault("uv", BufferAttribute(uv.reshape(-1).tolist(), 2))
-    g.buffer.setdefault("__index", BufferAttribute(f.reshape(-1).tolist(), 1))
+    if indexed:
+        g.buffer.setdefault("__index", BufferAttribute(f.reshape(-1).tolist(), 1, "Uint32Array"))
     g.xform = _ident4()
     g.baked = True
 
@@ -3661,13 +3883,23 @@ def _geom_center(g: Geometry):
 
 
 class BufferAttribute(Host):
-    __slots__ = ("array", "item")
+    """A vertex attribute over a typed array. The array is the module's own (`new BufferAttribute(arr, 3)` keeps
+    `arr`, and `attribute.array` returns it), so element writes through either reach the geometry."""
+    __slots__ = ("data", "item")
     cls_name = "BufferAttribute"
 
-    def __init__(self, array, item_size):
+    def __init__(self, array, item_size, kind: str = "Float32Array"):
         super().__init__({"isBufferAttribute": True})
-        self.array = [float(_to_num(a)) for a in array]
-        self.item = int(item_size)
+        self.data = array if isinstance(array, TypedArray) else TypedArray(kind, list(array))
+        self.item = max(1, int(item_size))
+
+    @property
+    def array(self) -> list:
+        return self.data.items
+
+    @array.setter
+    def array(self, vals) -> None:
+        self.data.items = _typed_values(self.data.kind, vals)
 
     def get_special(self, it, key):
         if key == "count":
@@ -3675,13 +3907,13 @@ class BufferAttribute(Host):
         if key == "itemSize":
             return float(self.item)
         if key == "array":
-            return JSArray(list(self.array))
+            return self.data
         return super().get_special(it, key)
 
     def _set(self, i, k, v):
         j = int(i) * self.item + k
         if 0 <= j < len(self.array):
-            self.array[j] = float(v)
+            self.array[j] = _typed_value(self.data.kind, v)
         return self
 
     def _get(self, i, k):
@@ -3714,13 +3946,18 @@ class Material(Host):
             for k, v in params.props.items():
                 self.js_set(None, k, v)
 
+    def chain(self):
+        return _MAT_CHAIN.get(self.mtype, (self.mtype,))
+
     def get_special(self, it, key):
         if key == "type":
             return self.mtype
+        if key.startswith("is") and key[2:] in self.chain() and key not in self.props:
+            return True                                 # isMeshStandardMaterial, isLineBasicMaterial ...
         return super().get_special(it, key)
 
     def is_instance(self, name):
-        return name in (self.mtype, "Material")
+        return name == "Material" or name in self.chain()
 
     def set_special(self, it, key, value):
         if key in ("color", "emissive", "specular", "sheenColor", "attenuationColor"):
@@ -3745,47 +3982,83 @@ def _mat_clone(m: Material):
 
 
 class Texture(Host):
-    """A texture: its data size (the texture-data limit) and the mean texel colour (the renders tint a mapped
-    surface by it; texel values are read as 8-bit or float channels of an RGBA / RGB / RG / R layout)."""
-    __slots__ = ("nbytes", "mean")
+    """A texture over the module's data array (DataTexture keeps the array it is given, so texels written after
+    construction count): its data size in bytes (a typed array's byteLength, as the texture-data limit counts
+    it; 0 for a plain array, which has none) and the mean texel colour (the renders tint a mapped surface by it;
+    texel values are read as 8-bit or float channels of an RGBA / RGB / RG / R layout)."""
+    __slots__ = ("src", "ch", "scale", "size")
     cls_name = "Texture"
 
-    def __init__(self, nbytes=0, mean=None):
+    def __init__(self, src=None, ch: int = 4, scale: float = 255.0, size=(0.0, 0.0), data_texture: bool = False):
         super().__init__({"isTexture": True, "repeat": Vec(("x", "y"), [1, 1], "Vector2"),
-                          "offset": Vec(("x", "y"), [0, 0], "Vector2"), "colorSpace": ""})
-        self.nbytes = nbytes
-        self.mean = mean                     # raw mean texel RGB in [0, 1], or None
+                          "offset": Vec(("x", "y"), [0, 0], "Vector2"), "colorSpace": "", "needsUpdate": False})
+        if data_texture:
+            self.props["isDataTexture"] = True
+        self.src, self.ch, self.scale, self.size = src, ch, scale, size
 
-    def linear_mean(self):
-        if self.mean is None:
+    def get_special(self, it, key):
+        if key == "image":
+            return JSObject({"data": self.src if self.src is not None else None,
+                             "width": self.size[0], "height": self.size[1]})
+        return super().get_special(it, key)
+
+    @property
+    def nbytes(self) -> int:
+        return len(self.src.items) * TYPED_BYTES[self.src.kind] if isinstance(self.src, TypedArray) else 0
+
+    @property
+    def mean(self):
+        """Raw mean texel RGB in [0, 1] of the data as it is now, or None."""
+        data = self.src.items if isinstance(self.src, JSArray) else []
+        ch = self.ch
+        n = len(data) // ch
+        if not n:
             return None
-        if self.props.get("colorSpace") == "srgb":
-            return [c ** 2.2 for c in self.mean]
-        return list(self.mean)
-
-    js_methods = {"clone": lambda s, i, x: Texture(s.nbytes, s.mean), "dispose": lambda s, i, x: UNDEF}
-
-
-def _data_texture(x):
-    """DataTexture(data, width, height, format, type): size and mean texel colour of the data."""
-    data = it_items(_arg(x, 0)) if x else []
-    fmt = _num_arg(x, 3, 1023.0)
-    ch = {1023.0: 4, 1022.0: 3, 1030.0: 2, 1028.0: 1, 1024.0: 1}.get(fmt, 4)
-    typ = _num_arg(x, 4, 1009.0)
-    scale = 255.0 if typ in (1009.0, 1010.0) else 1.0
-    mean = None
-    n = len(data) // ch
-    if n:
         step = max(1, n // 4096)                  # a sample of the texels is enough for the mean
         acc = [0.0, 0.0, 0.0]
         cnt = 0
         for k in range(0, n, step):
-            px = [_to_num(data[k * ch + c]) / scale for c in range(ch)]
+            px = [_to_num(data[k * ch + c]) / self.scale for c in range(ch)]
             rgb = px[:3] if ch >= 3 else [px[0]] * 3
-            acc = [a + max(0.0, min(1.0, v)) for a, v in zip(acc, rgb)]
+            acc = [a + (max(0.0, min(1.0, v)) if v == v else 0.0) for a, v in zip(acc, rgb)]
             cnt += 1
-        mean = [a / cnt for a in acc]
-    return Texture(len(data), mean)
+        return [a / cnt for a in acc]
+
+    def linear_mean(self):
+        mean = self.mean
+        if mean is None:
+            return None
+        if self.props.get("colorSpace") == "srgb":
+            return [c ** 2.2 for c in mean]
+        return list(mean)
+
+    js_methods = {"clone": lambda s, i, x: _texture_clone(s), "dispose": lambda s, i, x: UNDEF}
+
+
+def _texture_clone(t: Texture) -> Texture:
+    """clone shares the image data, as three.js's does; settings are copied."""
+    n = Texture(t.src, t.ch, t.scale, t.size, data_texture=bool(t.props.get("isDataTexture")))
+    for k, v in t.props.items():
+        n.props[k] = Vec(v.comps, v.v(), v.kind) if isinstance(v, Vec) else v
+    return n
+
+
+def _data_texture(x):
+    """DataTexture(data, width, height, format, type)."""
+    data = _arg(x, 0) if x else None
+    fmt = _num_arg(x, 3, 1023.0)
+    ch = {1023.0: 4, 1022.0: 3, 1030.0: 2, 1028.0: 1, 1024.0: 1}.get(fmt, 4)
+    typ = _num_arg(x, 4, 1009.0)
+    scale = 255.0 if typ in (1009.0, 1010.0) else 1.0
+    return Texture(data if isinstance(data, JSArray) else None, ch, scale, (_num_arg(x, 1, 1.0), _num_arg(x, 2, 1.0)),
+                   data_texture=True)
+
+
+# three.js class chains below Object3D: an object answers is<Class> and instanceof for each
+_OBJ_CHAIN = {"InstancedMesh": ("InstancedMesh", "Mesh"), "LineSegments": ("LineSegments", "Line"),
+              "LineLoop": ("LineLoop", "Line")}
+_MAT_CHAIN = {"MeshPhysicalMaterial": ("MeshPhysicalMaterial", "MeshStandardMaterial"),
+              "LineDashedMaterial": ("LineDashedMaterial", "LineBasicMaterial")}
 
 
 class Object3D(Host):
@@ -3806,11 +4079,16 @@ class Object3D(Host):
         if material is not None:
             self.props["material"] = material
 
+    def chain(self):
+        return _OBJ_CHAIN.get(self.otype, (self.otype,))
+
     def get_special(self, it, key):
         if key == "type":
             return self.otype
         if key == "uuid":
             return self.id_
+        if key.startswith("is") and key[2:] in self.chain() and key not in self.props:
+            return True                                 # isMesh, isInstancedMesh, isLine, isLineSegments, isGroup ...
         if key == "quaternion":
             if getattr(self, "quat_", None) is None:
                 self.quat_ = Quaternion(owner=self)
@@ -3822,16 +4100,24 @@ class Object3D(Host):
         return super().get_special(it, key)
 
     def is_instance(self, name):
-        return name in (self.otype, "Object3D") or (self.otype == "InstancedMesh" and name == "Mesh")
+        return name == "Object3D" or name in self.chain()
 
     def set_special(self, it, key, value):
         if key in ("position", "rotation", "scale"):
             raise _Throw(_error_obj("TypeError", f"cannot assign to read only property '{key}' of object"))
         return False
 
-    def local(self):
+    def composed(self):
         return _compose(self.props["position"].v(), self.props["rotation"].v(), self.props["scale"].v(),
                         _order(self.props["rotation"]))
+
+    def local(self):
+        """The local matrix three.js renders with: composed from position / rotation / scale, or, once the module
+        sets matrixAutoUpdate = false, the `matrix` it holds (kept by updateMatrix or written directly)."""
+        m = self.props.get("matrix")
+        if self.props.get("matrixAutoUpdate", True) is False and isinstance(m, Matrix4):
+            return [row[:] for row in m.m]
+        return self.composed()
 
     def children(self) -> list:
         return self.props["children"].items
@@ -3886,7 +4172,7 @@ class Object3D(Host):
         "translateY": lambda s, i, x: (s.props["position"].setv(_add3(s.props["position"].v(), _mat3_apply(_rot_mat(s.props["rotation"]), [0, _num_arg(x, 0), 0]))), s)[-1],
         "translateZ": lambda s, i, x: (s.props["position"].setv(_add3(s.props["position"].v(), _mat3_apply(_rot_mat(s.props["rotation"]), [0, 0, _num_arg(x, 0)]))), s)[-1],
         "lookAt": lambda s, i, x: s.look_at(_arg(x, 0).v() if isinstance(_arg(x, 0), Vec) else [_num_arg(x, 0), _num_arg(x, 1), _num_arg(x, 2)]),
-        "updateMatrix": lambda s, i, x: (setattr(s.props["matrix"], "m", s.local()), UNDEF)[-1],
+        "updateMatrix": lambda s, i, x: (setattr(s.props["matrix"], "m", s.composed()), UNDEF)[-1],
         "updateMatrixWorld": lambda s, i, x: UNDEF,
         "traverse": lambda s, i, x: (_traverse(i, s, _arg(x, 0)), UNDEF)[-1],
         "clone": lambda s, i, x: _obj_clone(i, s),
@@ -4116,7 +4402,8 @@ class Shape(Host):
         "bezierCurveTo": lambda s, i, x: s._bez(x),
         "absarc": lambda s, i, x: s._arc(x, True),
         "arc": lambda s, i, x: s._arc(x, False),
-        "closePath": lambda s, i, x: s,
+        "closePath": lambda s, i, x: (s.pts.append(list(s.pts[0])) if len(s.pts) > 1 and s.pts[-1] != s.pts[0]
+                                      else None, s)[-1],
         "getPoints": lambda s, i, x: JSArray([Vec(("x", "y"), p, "Vector2") for p in s.pts]),
         "setFromPoints": lambda s, i, x: (setattr(s, "pts", [list(p.v()[:2]) for p in it_items(_arg(x, 0))]), s)[-1],
     }
@@ -4276,27 +4563,48 @@ def _geom_ctor(gtype):
     return Native(gtype, ctor=build)
 
 
-def world_bbox(root: "Object3D"):
-    """World-space (min, max) corners of every mesh under `root` (its own transform included), or None."""
+def world_bbox(root: "Object3D", precise: bool = False):
+    """World-space (min, max) of every object with a geometry under `root` (its own transform included), or None,
+    by three.js's Box3.setFromObject: each geometry's bounding box (all of its positions) has its eight corners
+    moved by the object's world matrix (so a rotated object contributes the box around its rotated box, not around
+    its vertices); an InstancedMesh contributes its instances' boxes. `precise` uses every vertex instead
+    (setFromObject(object, true); instanced meshes stay boxes). Invisible objects count, as in three.js."""
     import numpy as np
-    sc = to_scene_json(root)
-    geoms = {g["uuid"]: g for g in sc["geometries"]}
     lo, hi = np.full(3, np.inf), np.full(3, -np.inf)
+    corners = np.array([[x, y, z, 1.0] for x in (0, 1) for y in (0, 1) for z in (0, 1)])
 
-    def walk(nd, parent):
-        m = np.asarray(nd.get("matrix"), dtype=np.float64).reshape(4, 4).T
-        w = parent @ m
-        g = geoms.get(nd.get("geometry"))
-        if g is not None and not nd.get("visible", True) is False:
-            v = np.asarray(g["data"]["attributes"]["position"]["array"], dtype=np.float64).reshape(-1, 3)
+    def box_points(bmin, bmax, m):
+        pts = np.where(corners[:, :3] > 0, bmax, bmin)
+        return pts @ m[:3, :3].T + m[:3, 3]
+
+    def walk(o, parent, depth):
+        w = parent @ np.asarray(o.local(), dtype=np.float64)
+        g = o.props.get("geometry")
+        if isinstance(g, Geometry):
+            v = geometry_mesh(g)[0].double().numpy()
             if len(v):
-                p = v @ w[:3, :3].T + w[:3, 3]
-                lo[:] = np.minimum(lo, p.min(0))
-                hi[:] = np.maximum(hi, p.max(0))
-        for c in nd.get("children", []):
-            walk(c, w)
-    walk(sc["object"], np.eye(4))
-    return None if not np.isfinite(lo).all() else (lo.tolist(), hi.tolist())
+                if o.otype == "InstancedMesh":
+                    gmin, gmax = v.min(0), v.max(0)
+                    inst = o.props.get("__inst", {})
+                    n = max(0, int(_to_num(o.props.get("count", 0))))
+                    mats = [np.asarray(inst.get(k, _ident4()), dtype=np.float64) for k in range(min(n, 1 << 16))]
+                    if mats:
+                        ip = np.concatenate([box_points(gmin, gmax, mk) for mk in mats])
+                        p = box_points(ip.min(0), ip.max(0), w)
+                    else:
+                        p = np.zeros((0, 3))
+                elif precise:
+                    p = v @ w[:3, :3].T + w[:3, 3]
+                else:
+                    p = box_points(v.min(0), v.max(0), w)
+                if len(p):
+                    lo[:] = np.minimum(lo, p.min(0))
+                    hi[:] = np.maximum(hi, p.max(0))
+        if depth < 64:
+            for c in o.children():
+                walk(c, w, depth + 1)
+    walk(root, np.eye(4), 0)
+    return None if not (np.isfinite(lo).all() and np.isfinite(hi).all()) else (lo.tolist(), hi.tolist())
 
 
 class Box3(Host):
@@ -4307,8 +4615,8 @@ class Box3(Host):
         super().__init__({"min": Vec(("x", "y", "z"), [math.inf] * 3, "Vector3"),
                           "max": Vec(("x", "y", "z"), [-math.inf] * 3, "Vector3"), "isBox3": True})
 
-    def set_from(self, o):
-        bb = world_bbox(o) if isinstance(o, Object3D) else None
+    def set_from(self, o, precise=False):
+        bb = world_bbox(o, precise) if isinstance(o, Object3D) else None
         self.props["min"].setv(bb[0] if bb else [math.inf] * 3)
         self.props["max"].setv(bb[1] if bb else [-math.inf] * 3)
         return self
@@ -4335,14 +4643,14 @@ class Box3(Host):
         return self
 
     js_methods = {
-        "setFromObject": lambda s, i, x: s.set_from(_arg(x, 0)),
+        "setFromObject": lambda s, i, x: s.set_from(_arg(x, 0), _truthy(_arg(x, 1, False))),
         "setFromPoints": lambda s, i, x: s.set_pts(it_items(_arg(x, 0))),
         "set": lambda s, i, x: (s.props["min"].setv(_arg(x, 0).v()), s.props["max"].setv(_arg(x, 1).v()), s)[-1],
         "expandByPoint": lambda s, i, x: s.expand(_arg(x, 0).v()),
         "expandByScalar": lambda s, i, x: (s.props["min"].setv([a - _num_arg(x, 0) for a in s.props["min"].v()]),
                                            s.props["max"].setv([a + _num_arg(x, 0) for a in s.props["max"].v()]), s)[-1],
-        "expandByObject": lambda s, i, x: s.expand(Box3().set_from(_arg(x, 0)).props["min"].v()).expand(
-            Box3().set_from(_arg(x, 0)).props["max"].v()) if not Box3().set_from(_arg(x, 0)).empty() else s,
+        "expandByObject": lambda s, i, x: (lambda b: s if b.empty() else s.expand(b.props["min"].v()).expand(
+            b.props["max"].v()))(Box3().set_from(_arg(x, 0), _truthy(_arg(x, 1, False)))),
         "union": lambda s, i, x: s.expand(_arg(x, 0).props["min"].v()).expand(_arg(x, 0).props["max"].v()),
         "containsPoint": lambda s, i, x: all(a <= p <= b for a, p, b in zip(s.props["min"].v(), _arg(x, 0).v(),
                                                                              s.props["max"].v())),
@@ -4355,6 +4663,18 @@ class Box3(Host):
         "getSize": lambda s, i, x: _arg(x, 0).setv([0.0] * 3 if s.empty() else
                                                    [b - a for a, b in zip(s.props["min"].v(), s.props["max"].v())]),
     }
+
+
+def _buffer_attribute(it, x, kind):
+    """new BufferAttribute(typedArray, itemSize) keeps the module's typed array and rejects a plain array, as
+    three.js does; new Float32BufferAttribute(arrayOrLength, itemSize) (and the other typed kinds) copies into a
+    fresh typed array of its kind."""
+    src, item = _arg(x, 0), _num_arg(x, 1, 3.0)
+    if kind is None:
+        if not isinstance(src, TypedArray):
+            raise _Throw(_error_obj("TypeError", "THREE.BufferAttribute: array should be a Typed Array."))
+        return BufferAttribute(src, item)
+    return BufferAttribute(_typed_from(it, kind, src), item)
 
 
 def _vec_ctor(name, comps):
@@ -4376,10 +4696,10 @@ def make_three(it: Interp) -> JSObject:
     three["BufferGeometry"] = Native("BufferGeometry", ctor=lambda i, x: Geometry())
     for m in mats:
         three[m] = Native(m, ctor=lambda i, x, _m=m: Material(_m, _arg(x, 0) if x else None))
-    for cls in ("Float32BufferAttribute", "BufferAttribute", "Uint16BufferAttribute", "Uint32BufferAttribute",
-                "Int32BufferAttribute", "Uint8BufferAttribute", "Int8BufferAttribute", "Int16BufferAttribute"):
-        three[cls] = Native(cls, ctor=lambda i, x: BufferAttribute(i.iterate(_arg(x, 0)) if isinstance(_arg(x, 0), JSArray)
-                                                                   else [], _num_arg(x, 1, 3.0)))
+    three["BufferAttribute"] = Native("BufferAttribute", ctor=lambda i, x: _buffer_attribute(i, x, None))
+    for cls in ("Float32BufferAttribute", "Uint16BufferAttribute", "Uint32BufferAttribute", "Int32BufferAttribute",
+                "Uint8BufferAttribute", "Int8BufferAttribute", "Int16BufferAttribute"):
+        three[cls] = Native(cls, ctor=lambda i, x, _k=cls.replace("BufferAttribute", "Array"): _buffer_attribute(i, x, _k))
     three["Group"] = Native("Group", ctor=lambda i, x: Object3D("Group"))
     three["Box3"] = Native("Box3", ctor=lambda i, x: Box3())
     three["Object3D"] = Native("Object3D", ctor=lambda i, x: Object3D("Object3D"))
@@ -4404,7 +4724,7 @@ def make_three(it: Interp) -> JSObject:
     three["CubicBezierCurve3"] = Native("CubicBezierCurve3", ctor=lambda i, x: Curve(
         "cubic", [_arg(x, k).v() for k in range(4)]))
     for t in ("Texture", "CanvasTexture"):
-        three[t] = Native(t, ctor=lambda i, x: Texture(len(it_items(_arg(x, 0))) if x else 0))
+        three[t] = Native(t, ctor=lambda i, x: Texture())
     three["DataTexture"] = Native("DataTexture", ctor=lambda i, x: _data_texture(x))
     _install_spec_members(it, three)
     for name, val in THREE_CONSTANTS.items():
@@ -5160,7 +5480,7 @@ def _baked(gtype, verts, faces=None, params=None):
     g = Geometry(gtype, params or {})
     g.buffer["position"] = BufferAttribute([float(c) for v in verts for c in v], 3)
     if faces is not None:
-        g.buffer["__index"] = BufferAttribute([float(i) for f in faces for i in f], 1)
+        g.buffer["__index"] = BufferAttribute([float(i) for f in faces for i in f], 1, "Uint32Array")
     g.baked = True
     return g
 

@@ -3,6 +3,7 @@ statics, subclassing a three.js object), object-literal accessors, function prot
 import pytest
 
 from phung5_b200.app import jsvm
+from phung5_b200.app.jsvm import UNDEF
 
 
 def _ev(expr, pre=""):
@@ -160,3 +161,66 @@ def test_euler_order_travels_with_constructor_set_copy_and_object_clone():
     assert got[5] == pytest.approx(0.0) and got[6] == pytest.approx(0.1)      # the clone owns its transform
     assert got[7] is True and got[8] is False and got[9] == 1 and got[10] == 1  # shared geometry, copied userData
     assert got[11:] == ["ZXY", pytest.approx(0.2), 0, True]                     # copy(source, recursive = false)
+
+
+def test_class_flags_typed_arrays_and_shared_attribute_arrays():
+    pre = """
+      const m = new THREE.Mesh(new THREE.BoxGeometry(0.1, 0.1, 0.1), new THREE.MeshPhysicalMaterial());
+      const im = new THREE.InstancedMesh(new THREE.BoxGeometry(0.1, 0.1, 0.1), new THREE.MeshBasicMaterial(), 2);
+      const ls = new THREE.LineSegments(new THREE.BufferGeometry(), new THREE.LineDashedMaterial());
+      const u = new Uint8Array([300, -1, 7.9]); const c = new Uint8ClampedArray([300, -5, 2.5]);
+      const f = new Float32Array(4); f.set([1, 2], 1); f[9] = 5;
+      const pos = new Float32Array([0, 0, 0, 1, 0, 0, 0, 1, 0]);
+      const bg = new THREE.BufferGeometry(); bg.setAttribute('position', new THREE.BufferAttribute(pos, 3));
+      pos[4] = 2;                                           // written after the attribute was made
+      bg.attributes.position.array[6] = 3;                   // written through the attribute's own array
+      bg.setIndex([0, 1, 2]); bg.computeVertexNormals();
+      let threw = false; try { new THREE.BufferAttribute([0, 0, 0], 3); } catch (e) { threw = true; }
+    """
+    got = _ev("[m.isMesh, im.isMesh, im.isInstancedMesh, ls.isLine, ls instanceof THREE.Line, m.isGroup, "
+              "m.material.isMeshStandardMaterial, ls.material.isLineBasicMaterial, u[0], u[1], u[2], c[0], c[1], c[2], "
+              "f.length, f[1], f[9], Array.isArray(f), typeof f.push, new Float32Array([10, 9, 1]).sort().join(','), "
+              "bg.attributes.position.getY(1), bg.attributes.position.getX(2), bg.index.count, "
+              "bg.getAttribute('normal').getZ(0), threw, Math.fround(0.1) === 0.1]", pre).items
+    assert got[:8] == [True, True, True, True, True, UNDEF, True, True]
+    assert got[8:14] == [44, 255, 7, 255, 0, 2]            # modular bytes; clamped bytes round half to even
+    assert got[14:20] == [4, 1, UNDEF, False, "undefined", "1,9,10"]
+    assert got[20:] == [2, 3, 3, -1, True, False]          # (1, 2, 0) x (3, 1, 0) points to -z
+
+
+def test_colors_live_in_linear_srgb_like_three_js():
+    pre = """
+      const a = new THREE.Color(0xff8000); const h = {}; a.getHSL(h); const hs = {}; a.getHSL(hs, THREE.SRGBColorSpace);
+      const b = new THREE.Color(0.5, 0.5, 0.5); const d = new THREE.Color('#808080');
+      const e = new THREE.Color().setRGB(0.5, 0.5, 0.5, THREE.SRGBColorSpace);
+      const half = new THREE.Color(0xffffff).multiplyScalar(0.5);
+    """
+    got = _ev("[a.getHex(), a.r, a.g, h.h, hs.h, b.getHexString(), d.r, e.getHexString(), half.getHexString(), "
+              "d.getStyle()]", pre).items
+    assert got[0] == 0xFF8000 and got[1] == 1.0 and got[2] == pytest.approx(0.2158605, abs=1e-6)
+    assert got[3] == pytest.approx(0.2158605 / 6, abs=1e-6) and got[4] == pytest.approx((128 / 255) / 6, abs=1e-6)
+    assert got[5] == "bcbcbc" and got[6] == pytest.approx(0.2158605, abs=1e-6) and got[7] == "808080"
+    assert got[8] == "bcbcbc" and got[9] == "rgb(128,128,128)"
+
+
+def test_bounding_boxes_follow_set_from_object():
+    pre = """
+      const m = new THREE.Mesh(new THREE.SphereGeometry(0.5, 32, 16), new THREE.MeshBasicMaterial());
+      m.rotation.y = Math.PI / 4; g.add(m);
+      const loose = new THREE.Box3().setFromObject(g), tight = new THREE.Box3().setFromObject(g, true);
+      const hidden = new THREE.Mesh(new THREE.BoxGeometry(4, 0.1, 0.1), new THREE.MeshBasicMaterial());
+      hidden.visible = false; const g2 = new THREE.Group(); g2.add(hidden);
+      const hb = new THREE.Box3().setFromObject(g2);
+      const im = new THREE.InstancedMesh(new THREE.BoxGeometry(0.1, 0.1, 0.1), new THREE.MeshBasicMaterial(), 2);
+      im.setMatrixAt(1, new THREE.Matrix4().makeTranslation(1, 0, 0));
+      const ib = new THREE.Box3().setFromObject(im);
+      const fixed = new THREE.Object3D(); fixed.matrixAutoUpdate = false; fixed.position.set(5, 0, 0);
+      fixed.add(new THREE.Mesh(new THREE.BoxGeometry(1, 1, 1), new THREE.MeshBasicMaterial()));
+      const fb = new THREE.Box3().setFromObject(fixed);
+    """
+    got = _ev("[loose.max.x, tight.max.x, hb.max.x, ib.min.x, ib.max.x, fb.max.x]", pre).items
+    assert got[0] == pytest.approx(0.5 * 2 ** 0.5, abs=1e-6)        # the box around the rotated box
+    assert got[1] == pytest.approx(0.5, abs=1e-3)                    # every vertex
+    assert got[2] == pytest.approx(2.0)                               # invisible objects count
+    assert got[3:5] == [pytest.approx(-0.05), pytest.approx(1.05)]    # instances: identity until set
+    assert got[5] == pytest.approx(0.5)                               # matrixAutoUpdate = false keeps its matrix

@@ -258,3 +258,31 @@ def test_data_texture_tints_the_render_by_its_mean_colour():
     assert res.ok, res.summary()
     _, col = S.scene_triangles(res.scene)
     np.testing.assert_allclose(col[0].numpy(), [0.5, 128 / 255, 0.0], atol=1e-4)
+
+
+def test_post_validation_counts_like_the_reference_validator():
+    # an InstancedMesh draws its geometry once: vertices are counted once, instances separately
+    res = _check("const im = new THREE.InstancedMesh(new THREE.SphereGeometry(0.01, 64, 32), "
+                 "new THREE.MeshStandardMaterial(), 400); g.add(im);")
+    assert res.ok, res.summary()
+    # DataTextures count by byteLength, once each, from the map slots only
+    tex = ("const data = new Float32Array(512 * 512 * 4); const t = new THREE.DataTexture(data, 512, 512, "
+           "THREE.RGBAFormat, THREE.FloatType); ")
+    res = _check(tex + "g.add(new THREE.Mesh(new THREE.BoxGeometry(0.1, 0.1, 0.1), new THREE.MeshStandardMaterial({map: t})));")
+    assert "TEXTURE_DATA_EXCEEDED" not in {f["rule"] for f in res.failures}
+    assert res.stats["textureBytes"] == 512 * 512 * 16
+    res = _check(tex + "const t2 = new THREE.DataTexture(new Float32Array(4), 1, 1); "
+                       "const mat = new THREE.MeshStandardMaterial({map: t, roughnessMap: t2}); "
+                       "g.add(new THREE.Mesh(new THREE.BoxGeometry(0.1, 0.1, 0.1), mat)); "
+                       "g.add(new THREE.Mesh(new THREE.BoxGeometry(0.1, 0.1, 0.1), mat)); "
+                       "g.add(new THREE.Mesh(new THREE.BoxGeometry(0.1, 0.1, 0.1), new THREE.MeshStandardMaterial({map: t})));")
+    assert res.stats["textureBytes"] == 512 * 512 * 16 + 16
+    res = _check(tex + "const t2 = new THREE.DataTexture(new Float32Array(512 * 512 * 4), 512, 512); "
+                       "g.add(new THREE.Mesh(new THREE.BoxGeometry(0.1, 0.1, 0.1), "
+                       "new THREE.MeshStandardMaterial({map: t, emissiveMap: t2})));")
+    assert "TEXTURE_DATA_EXCEEDED" in {f["rule"] for f in res.failures}
+    # only a Group, Mesh, LineSegments or Points may be returned
+    res = JSChecker(_inline=True).check("export default function generate(THREE) { const o = new THREE.Object3D(); "
+                                        "o.add(new THREE.Mesh(new THREE.BoxGeometry(0.1, 0.1, 0.1), "
+                                        "new THREE.MeshBasicMaterial())); return o; }")
+    assert [f["rule"] for f in res.failures] == ["INVALID_RETURN_TYPE"]
