@@ -595,10 +595,12 @@ def post_validate(root) -> tuple:
             stack.append((c, d + 1))
     if bad_numbers:
         fail("NON_FINITE_VALUE", "a transform or vertex is NaN or infinite")
-    for key, rule in (("vertices", "VERTEX_LIMIT_EXCEEDED"), ("drawCalls", "DRAW_CALL_LIMIT_EXCEEDED"),
-                      ("instances", "INSTANCE_LIMIT_EXCEEDED"), ("textureBytes", "TEXTURE_DATA_EXCEEDED")):
+    for key, rule, unit in (("vertices", "VERTEX_LIMIT_EXCEEDED", "vertices"),
+                            ("drawCalls", "DRAW_CALL_LIMIT_EXCEEDED", "draw calls"),
+                            ("instances", "INSTANCE_LIMIT_EXCEEDED", "instances"),
+                            ("textureBytes", "TEXTURE_DATA_EXCEEDED", "bytes")):
         if stats[key] > LIMITS[key]:
-            fail(rule, f"{stats[key]} {key} (limit {LIMITS[key]})")
+            fail(rule, f"{stats[key]} {unit} (limit {LIMITS[key]})")
     if stats["meshes"] == 0 and not fails:
         fail("EMPTY_SCENE", "the returned object contains no meshes")
     elif not fails:

@@ -11,11 +11,16 @@ planned on `jsvm.tokenize` tokens (so strings, comments and template text are ne
 - `constlet`    EXECUTION_THREW "assignment to constant variable x": x's `const` declarations become `let`.
 - `paren`       PARSE_ERROR "unexpected token ')'": the first `)` that closes nothing is deleted.
 - `ident`       IDENTIFIER_NOT_ALLOWED `x`: if exactly one declared name equals x up to case and underscores
-                (`roundedPts` / `rounded_pts`), every reference to x is renamed to it.
+                (`roundedPts` / `rounded_pts`), every reference to x is renamed to it; if none does and x is only
+                read as a value (never called, constructed, indexed or dereferenced), `let x = 0;` is declared at the
+                top of generate().
 - `console`     IDENTIFIER_NOT_ALLOWED `console` (not a global the specification allows): every `console.x(...);`
                 statement is removed; a use of console anywhere but a statement of its own is not rewritten.
 - `random`      FORBIDDEN_IDENTIFIER Math.random: every `Math.random` becomes a seeded generator defined at the top of
                 the module (a 32-bit linear congruential generator), so the module is valid and deterministic.
+- `texture`     TEXTURE_DATA_EXCEEDED "<b> bytes (limit <l>)" with b <= 4 l: every `new THREE.DataTexture(` goes
+                through a helper that box-filters an RGBA Uint8Array texture of at least 256 x 256 texels (even sizes)
+                down to half its width and height (a quarter of the bytes); other textures pass through unchanged.
 - `retry`       TIMEOUT_EXCEEDED on the wall-clock deadline only (not the step budget): checked once more, since
                 host load can push a module over the deadline.
 
@@ -29,11 +34,53 @@ from typing import Dict, Iterable, List, Optional, Set, Tuple
 
 from . import jsvm
 
-CLASSES = ("redeclared", "constlet", "paren", "ident", "console", "random", "retry")
+CLASSES = ("redeclared", "constlet", "paren", "ident", "console", "random", "texture", "retry")
 
 SEEDED_RANDOM = ("const __phxRandom = (() => { let s = 0x2545F491; "
                  "return () => { s = (s * 1664525 + 1013904223) >>> 0; return s / 4294967296; }; })();\n")
 
+HALF_TEXTURE = (
+    "const __phxDataTexture = (THREE, data, w, h, ...rest) => {\n"
+    "  if (data instanceof Uint8Array && w >= 256 && h >= 256 && w % 2 === 0 && h % 2 === 0 && data.length === w * h * 4) {\n"
+    "    const w2 = w / 2, h2 = h / 2, out = new Uint8Array(w2 * h2 * 4);\n"
+    "    for (let y = 0; y < h2; y++) {\n"
+    "      for (let x = 0; x < w2; x++) {\n"
+    "        const i = (2 * y * w + 2 * x) * 4, o = (y * w2 + x) * 4;\n"
+    "        for (let c = 0; c < 4; c++) {\n"
+    "          out[o + c] = (data[i + c] + data[i + 4 + c] + data[i + 4 * w + c] + data[i + 4 * w + 4 + c] + 2) >> 2;\n"
+    "        }\n"
+    "      }\n"
+    "    }\n"
+    "    return new THREE.DataTexture(out, w2, h2, ...rest);\n"
+    "  }\n"
+    "  return new THREE.DataTexture(data, w, h, ...rest);\n"
+    "};\n")
+
+def _half_texture_native(it):
+    """What HALF_TEXTURE computes, for the interpreter: the same test, the same rounded 2 x 2 box mean per
+    channel, the same constructor calls."""
+    import numpy as np
+
+    def call(i, this, x):
+        three, data, w, h = (x + [jsvm.UNDEF] * 4)[:4]
+        rest = list(x[4:])
+        ctor = it.get(three, "DataTexture")
+        wn = w if isinstance(w, float) else None
+        hn = h if isinstance(h, float) else None
+        if isinstance(data, jsvm.TypedArray) and data.kind == "Uint8Array" and wn is not None and hn is not None \
+                and wn >= 256 and hn >= 256 and wn % 2 == 0 and hn % 2 == 0 and len(data.items) == wn * hn * 4:
+            W, H = int(wn), int(hn)
+            a = np.asarray(data.items, dtype=np.int64).reshape(H // 2, 2, W // 2, 2, 4)
+            out = (a.sum(axis=(1, 3)) + 2) >> 2
+            arr = jsvm.TypedArray("Uint8Array", out.reshape(-1).astype(np.float64).tolist(), coerced=True)
+            return it.construct(ctor, [arr, float(W // 2), float(H // 2)] + rest)
+        return it.construct(ctor, [data, w, h] + rest)
+    return jsvm.Native("__phxDataTexture", fn=call)
+
+
+jsvm.register_intrinsic("__phxDataTexture", HALF_TEXTURE, _half_texture_native)
+
+_TEX = re.compile(r"^(\d+) bytes \(limit (\d+)\)")
 _DUP = re.compile(r"Identifier '([A-Za-z_$][\w$]*)' has already been declared")
 _CONST = re.compile(r"assignment to constant variable ([A-Za-z_$][\w$]*)")
 _IDENT = re.compile(r"`([A-Za-z_$][\w$]*)` is not declared")
@@ -56,6 +103,9 @@ def plan(fails: Iterable[Dict[str, str]]) -> List[Tuple[str, str]]:
             out.append(("console", name) if name == "console" else ("ident", name))
         elif rule == "FORBIDDEN_IDENTIFIER" and detail.startswith("Math.random"):
             out.append(("random", ""))
+        elif rule == "TEXTURE_DATA_EXCEEDED" and _TEX.match(detail) and \
+                int(_TEX.match(detail).group(1)) <= 4 * int(_TEX.match(detail).group(2)):
+            out.append(("texture", ""))
         elif rule == "TIMEOUT_EXCEEDED" and "execution exceeded" in detail:
             out.append(("retry", ""))
         else:
@@ -203,12 +253,70 @@ def fix_random(code: str) -> Optional[str]:
     return SEEDED_RANDOM + _edit(code, edits)
 
 
+def fix_texture(code: str) -> Optional[str]:
+    toks = _tokens(code)
+    if toks is None:
+        return None
+    edits: List[Tuple[int, int, str]] = []
+    for i in range(len(toks) - 4):
+        a, b, c, d, e = toks[i:i + 5]
+        if a.kind == "kw" and a.val == "new" and b.val == "THREE" and c.val == "." and d.val == "DataTexture" \
+                and e.kind == "p" and e.val == "(":
+            empty = i + 5 < len(toks) and toks[i + 5].kind == "p" and toks[i + 5].val == ")"
+            edits.append((a.pos, _tok_end(e), "__phxDataTexture(THREE" + ("" if empty else ", ")))
+    if not edits:
+        return None
+    return HALF_TEXTURE + _edit(code, edits)
+
+
+def _generate_body(toks: List[jsvm.Tok]) -> Optional[int]:
+    """Source offset just after the `{` that opens generate()'s body."""
+    for i in range(len(toks) - 2):
+        if toks[i].kind == "kw" and toks[i].val == "function" and toks[i + 1].val == "generate" and \
+                toks[i + 2].val == "(":
+            depth, j = 0, i + 2
+            while j < len(toks):
+                if toks[j].kind == "p" and toks[j].val == "(":
+                    depth += 1
+                elif toks[j].kind == "p" and toks[j].val == ")":
+                    depth -= 1
+                    if depth == 0:
+                        break
+                j += 1
+            if j + 1 < len(toks) and toks[j + 1].kind == "p" and toks[j + 1].val == "{":
+                return _tok_end(toks[j + 1])
+    return None
+
+
+def _stub_ident(code: str, name: str) -> Optional[str]:
+    """`let name = 0;` at the top of generate() when name is only read as a plain value."""
+    toks = _tokens(code)
+    if toks is None:
+        return None
+    uses = [i for i, t in enumerate(toks) if t.kind == "id" and t.val == name and _is_binding_ref(toks, i)]
+    if not uses:
+        return None
+    for i in uses:
+        nxt = toks[i + 1] if i + 1 < len(toks) else None
+        prev = toks[i - 1] if i > 0 else None
+        if nxt is not None and nxt.kind == "p" and nxt.val in ("(", ".", "[", "?.", "`"):
+            return None
+        if prev is not None and prev.kind == "kw" and prev.val == "new":
+            return None
+    at = _generate_body(toks)
+    if at is None:
+        return None
+    return code[:at] + f" let {name} = 0;" + code[at:]
+
+
 def _norm(name: str) -> str:
     return name.replace("_", "").lower()
 
 
 def fix_ident(code: str, name: str, declared: Set[str]) -> Optional[str]:
     same = [d for d in declared if d != name and _norm(d) == _norm(name)]
+    if not same and name not in declared:
+        return _stub_ident(code, name)
     if len(same) != 1:
         return None
     toks = _tokens(code)
@@ -238,6 +346,8 @@ def apply(code: str, steps: List[Tuple[str, str]], declared: Set[str]) -> Option
             new = fix_console(code)
         elif cls == "random":
             new = fix_random(code)
+        elif cls == "texture":
+            new = fix_texture(code)
         else:
             new = None
         if new is None:

@@ -1293,6 +1293,10 @@ class Interp:
         env = self.globals
         self.hoist(prog[1], env)
         for st in prog[1]:
+            name = _intrinsic_name(st)
+            if name is not None:
+                env.declare(name, _INTRINSICS[name][1](self), const=True)
+                continue
             self.exec(st, env)
 
     def hoist(self, body, env):
@@ -2162,8 +2166,10 @@ class Interp:
                 return False
             if isinstance(b, Native) and isinstance(a, Host):
                 return a.is_instance(b.name)
+            if isinstance(b, Native) and b.name in TYPED_BYTES:
+                return isinstance(a, TypedArray) and a.kind == b.name
             if isinstance(b, Native) and b.name == "Array":
-                return isinstance(a, JSArray)
+                return isinstance(a, JSArray) and not isinstance(a, TypedArray)
             if isinstance(b, Native) and b.name == "Object":
                 return isinstance(a, (JSObject, JSArray, Host))
             return False
@@ -4967,6 +4973,30 @@ class ModuleResult:
     steps: int = 0
     seconds: float = 0.0
     texture_bytes: int = 0
+
+
+# Module-level `const NAME = ...` declarations that the interpreter runs natively when the statement's syntax tree
+# equals a registered source exactly: the helpers that mechanical repairs insert, whose per-texel loops a JS engine
+# runs in milliseconds and this tree-walker in tens of seconds. The native must compute what the source computes.
+_INTRINSICS: Dict[str, Tuple[str, Callable]] = {}
+_INTRINSIC_AST: Dict[str, Any] = {}
+
+
+def register_intrinsic(name: str, source: str, native: Callable) -> None:
+    """source: one `const name = ...;` statement; native(interp) -> the value bound to name."""
+    _INTRINSICS[name] = (source, native)
+    _INTRINSIC_AST.pop(name, None)
+
+
+def _intrinsic_name(st) -> Optional[str]:
+    if not (st[0] == "decl" and st[1] == "const" and len(st[2]) == 1 and st[2][0][0][0] == "id"):
+        return None
+    name = st[2][0][0][1]
+    if name not in _INTRINSICS:
+        return None
+    if name not in _INTRINSIC_AST:
+        _INTRINSIC_AST[name] = Parser(_INTRINSICS[name][0]).program()[1][0]
+    return name if _INTRINSIC_AST[name] == st else None
 
 
 def run_module(source: str, limits: Optional[Limits] = None, seed: int = 0) -> ModuleResult:

@@ -81,3 +81,50 @@ def test_only_the_wall_clock_timeout_is_retried():
         [("retry", "")]
     assert jsrepair.plan([{"rule": "TIMEOUT_EXCEEDED",
                            "detail": "TIMEOUT: step budget of 20000000 exceeded"}]) == []
+
+
+def test_undeclared_value_gets_a_stub_only_when_it_is_a_plain_value():
+    res = _checker().check(_module("const q = widthh * 2;"))
+    assert res.ok and res.repaired == ["ident: widthh"] and "let widthh = 0;" in res.code
+    for use in ("const q = widthh(2);", "const q = widthh.x;", "const q = new widthh();", "const q = widthh[0];"):
+        res = _checker().check(_module(use))
+        assert not res.ok and not res.repaired, use
+
+
+TEXTURES = """export default function generate(THREE) { const g = new THREE.Group();
+  for (let k = 0; k < 5; k++) {
+    const n = 512; const data = new Uint8Array(n * n * 4);
+    for (let i = 0; i < 64; i++) data[i] = 4 * i;
+    const t = new THREE.DataTexture(data, n, n, THREE.RGBAFormat); t.needsUpdate = true;
+    g.add(new THREE.Mesh(new THREE.BoxGeometry(0.1, 0.1, 0.1), new THREE.MeshStandardMaterial({map: t})));
+  }
+  return g; }"""
+
+
+def test_texture_class_halves_large_rgba_textures():
+    off = _checker(failure_repair=False).check(TEXTURES)
+    assert [f["rule"] for f in off.failures] == ["TEXTURE_DATA_EXCEEDED"]
+    assert off.failures[0]["detail"] == "5242880 bytes (limit 4194304)"
+    res = _checker().check(TEXTURES)
+    assert res.ok and res.repaired == ["texture"] and res.stats["textureBytes"] == 5 * 256 * 256 * 4
+    # beyond four times the limit a halving cannot fit: no rewrite
+    assert jsrepair.plan([{"rule": "TEXTURE_DATA_EXCEEDED", "detail": "16777217 bytes (limit 4194304)"}]) == []
+
+
+def test_texture_helper_runs_natively_with_the_same_result():
+    body = """export default function generate(THREE) { const g = new THREE.Group();
+      const n = 256; const data = new Uint8Array(n * n * 4);
+      for (let i = 0; i < data.length; i += 97) data[i] = (i * 7) % 256;
+      const t = __phxDataTexture(THREE, data, n, n, THREE.RGBAFormat);
+      const s = __phxDataTexture(THREE, new Uint8Array(16), 2, 2);
+      g.userData.v = [t.image.width, t.image.height, s.image.width, Array.from(t.image.data)];
+      return g; }"""
+    fast = jsvm.run_module(jsrepair.HALF_TEXTURE + body, jsvm.Limits(seconds=60))
+    slow_src = (jsrepair.HALF_TEXTURE + body).replace("__phxDataTexture", "__phxDataTextureInterpreted")
+    slow = jsvm.run_module(slow_src, jsvm.Limits(seconds=120))
+    assert fast.error is None and slow.error is None, (fast.error, slow.error)
+    assert fast.steps < slow.steps // 10                       # the native ran
+    a = fast.root.props["userData"].props["v"].items
+    b = slow.root.props["userData"].props["v"].items
+    assert a[:3] == b[:3] == [128, 128, 2]
+    assert a[3].items == b[3].items and len(a[3].items) == 128 * 128 * 4
