@@ -535,6 +535,46 @@ def declared_vertices(g, n_triangles: int = 0) -> int:
     return 0
 
 
+def async_use(code: str) -> Optional[str]:
+    """The specification's ASYNC_NOT_ALLOWED detail for the first async function, async arrow or method, `for await`
+    or `await` in the module, or None. (The interpreter does not run async code, so this is decided on tokens,
+    before parsing.)"""
+    try:
+        toks = jsvm.tokenize(code)
+    except jsvm.JSError:
+        return None
+
+    def line(t):
+        return code.count("\n", 0, t.pos) + 1
+
+    def val(i):
+        return toks[i].val if 0 <= i < len(toks) else None
+    for i, t in enumerate(toks):
+        if t.val == "async" and t.kind in ("kw", "id") and val(i - 1) != ".":
+            nxt = val(i + 1)
+            is_async = nxt == "function" or (toks[i + 1].kind == "id" and val(i + 2) in ("=>", "(")) if nxt else False
+            if nxt == "(":                                  # async (a, b) => ...
+                depth, j = 0, i + 1
+                while j < len(toks):
+                    if toks[j].val == "(" and toks[j].kind == "p":
+                        depth += 1
+                    elif toks[j].val == ")" and toks[j].kind == "p":
+                        depth -= 1
+                        if depth == 0:
+                            break
+                    j += 1
+                is_async = val(j + 1) == "=>"
+            if is_async:
+                if val(i - 1) == "default" and val(i - 2) == "export":
+                    return "default export is an async function"
+                return f"async function at line {line(t)}"
+        if t.val == "for" and t.kind == "kw" and val(i + 1) == "await":
+            return f"for await loop at line {line(t)}"
+        if t.val == "await" and t.kind in ("kw", "id") and val(i - 1) != ".":
+            return f"top-level await at line {line(t)}"
+    return None
+
+
 def post_validate(root) -> tuple:
     """Walk the returned tree once with cycle detection. -> (failures, stats)."""
     fails: List[Dict[str, str]] = []
@@ -711,6 +751,10 @@ class JSChecker:
         if size > MAX_FILE_BYTES:
             return CheckResult(False, [{"stage": "parse", "rule": "FILE_SIZE_EXCEEDED",
                                         "detail": f"{size} bytes (limit {MAX_FILE_BYTES})"}], code, repaired=fixes)
+        asy = async_use(code)
+        if asy is not None:
+            return CheckResult(False, [{"stage": "static_analysis", "rule": "ASYNC_NOT_ALLOWED", "detail": asy}], code,
+                               repaired=fixes)
         try:
             prog = jsvm.Parser(code).program()
         except jsvm.JSError as e:

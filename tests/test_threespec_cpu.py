@@ -32,6 +32,8 @@ def test_every_allowed_member_is_implemented():
     ("const k = 'sin'; const v = Math[k](1);", "COMPUTED_PROPERTY_ACCESS"),
     ("const o = {}; const p = o.__proto__;", "FORBIDDEN_PROPERTY_ACCESS"),
     ("const d = Date.now();", "FORBIDDEN_IDENTIFIER"),
+    ("const f = async () => 1;", "ASYNC_NOT_ALLOWED"),
+    ("class A { async m() {} }", "ASYNC_NOT_ALLOWED"),
 ])
 def test_specification_rejections(body, rule):
     assert rule in _rules(body)
