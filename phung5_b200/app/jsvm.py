@@ -4508,11 +4508,51 @@ class Curve(Host):
         n = max(1, min(int(n), 4096))
         return JSArray([self.vec(self.point(k / n)) for k in range(n + 1)])
 
+    def arc_table(self, n=200):
+        """Cumulative chord lengths at t = k / n (three.js's arcLengthDivisions = 200)."""
+        pts = [self.point(k / n) for k in range(n + 1)]
+        acc = [0.0]
+        for a, b in zip(pts, pts[1:]):
+            acc.append(acc[-1] + math.sqrt(sum((p - q) ** 2 for p, q in zip(a, b))))
+        return acc
+
+    def u_to_t(self, u, acc=None):
+        """three.js's getUtoTmapping: the t at which the arc length is u of the whole."""
+        acc = acc or self.arc_table()
+        n = len(acc) - 1
+        total = acc[-1]
+        if total <= 0:
+            return u
+        target = min(max(u, 0.0), 1.0) * total
+        lo, hi = 0, n
+        while lo < hi:                                  # first sample whose length reaches the target
+            mid = (lo + hi) // 2
+            if acc[mid] < target:
+                lo = mid + 1
+            else:
+                hi = mid
+        if acc[lo] == target or lo == 0:
+            return lo / n
+        seg = acc[lo] - acc[lo - 1]
+        return (lo - 1 + ((target - acc[lo - 1]) / seg if seg > 0 else 0.0)) / n
+
+    def tangent(self, t):
+        """three.js's Curve.getTangent: the normalised difference of the points 1e-4 either side (clamped)."""
+        a, b = self.point(max(0.0, t - 1e-4)), self.point(min(1.0, t + 1e-4))
+        d = [q - p for p, q in zip(a, b)]
+        n = math.sqrt(sum(c * c for c in d)) or 1.0
+        return self.vec([c / n for c in d])
+
     js_methods = {
         "getPoint": lambda s, i, x: s.vec(s.point(_num_arg(x, 0))),
-        "getPointAt": lambda s, i, x: s.vec(s.point(_num_arg(x, 0))),
-        "getPoints": lambda s, i, x: s.points(_num_arg(x, 0, 5.0 if s.kind_ in ("line", "line2") else 50.0)),
-        "getSpacedPoints": lambda s, i, x: s.points(_num_arg(x, 0, 5.0)),
+        "getPointAt": lambda s, i, x: s.vec(s.point(s.u_to_t(_num_arg(x, 0)))),
+        "getPoints": lambda s, i, x: s.points(_num_arg(x, 0, 12.0 if s.kind_ == "path" else 5.0)),
+        "getSpacedPoints": lambda s, i, x: (lambda n, tab: JSArray([s.vec(s.point(s.u_to_t(k / n, tab)))
+                                                                    for k in range(n + 1)]))(
+            max(1, min(int(_num_arg(x, 0, 5.0)), 4096)), s.arc_table()),
+        "getTangent": lambda s, i, x: s.tangent(_num_arg(x, 0)),
+        "getTangentAt": lambda s, i, x: s.tangent(s.u_to_t(_num_arg(x, 0))),
+        "getUtoTmapping": lambda s, i, x: s.u_to_t(_num_arg(x, 0)),
         "getLength": lambda s, i, x: _curve_length(s),
         "add": lambda s, i, x: (s.props["curves"].items.append(_arg(x, 0)), UNDEF)[-1] if s.kind_ == "path" else UNDEF,
     }
@@ -4941,7 +4981,8 @@ def _knot(R, r, tseg, rseg, p, q):
 
 def _tube(curve: Curve, tseg, radius, rseg):
     import torch
-    pts = [curve.point(k / tseg) for k in range(tseg + 1)]
+    tab = curve.arc_table()
+    pts = [curve.point(curve.u_to_t(k / tseg, tab)) for k in range(tseg + 1)]     # equal arc lengths, as three.js
     verts, faces = [], []
     prev_n = None
     for k, pt in enumerate(pts):

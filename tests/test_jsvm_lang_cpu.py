@@ -224,3 +224,16 @@ def test_bounding_boxes_follow_set_from_object():
     assert got[2] == pytest.approx(2.0)                               # invisible objects count
     assert got[3:5] == [pytest.approx(-0.05), pytest.approx(1.05)]    # instances: identity until set
     assert got[5] == pytest.approx(0.5)                               # matrixAutoUpdate = false keeps its matrix
+
+
+def test_curves_space_points_by_arc_length_and_give_tangents():
+    pre = """
+      const c = new THREE.LineCurve3(new THREE.Vector3(0, 0, 0), new THREE.Vector3(2, 0, 0));
+      const q = new THREE.QuadraticBezierCurve3(new THREE.Vector3(0, 0, 0), new THREE.Vector3(1, 2, 0), new THREE.Vector3(3, 0, 0));
+      const sp = q.getSpacedPoints(4).map(p => p.x);
+    """
+    got = _ev("[c.getTangent(0.5).x, c.getLength(), c.getPoints().length, q.getPoints().length, q.getTangentAt(0).y > 0, "
+              "q.getPointAt(0.5).x, q.getPoint(0.5).x, sp.length]", pre).items
+    assert got[:5] == [pytest.approx(1.0), pytest.approx(2.0), 6, 6, True]       # getPoints(divisions = 5)
+    # the arc-length midpoint of this asymmetric arc differs from its parameter midpoint
+    assert got[6] == pytest.approx(1.25) and abs(got[5] - got[6]) > 0.01 and got[7] == 5
