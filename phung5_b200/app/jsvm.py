@@ -4322,53 +4322,88 @@ def _obj_clone(it, o: Object3D) -> Object3D:
 
 
 class Shape(Host):
-    """Shape / Path / CurvePath: polyline outline from moveTo/lineTo/curves (sampled)."""
-    __slots__ = ("pts", "holes_")
+    """Shape / Path: a list of segments (points from moveTo / lineTo, quadratic and cubic Beziers, arcs and
+    ellipses, splines, closePath) sampled as three.js's CurvePath.getPoints(divisions) samples them: each curve at
+    `divisions` steps (ellipses and arcs at twice that, splines at that times their point count), a point equal to
+    the one before it skipped. getPoints() and the shape geometries use 12 (ExtrudeGeometry's and ShapeGeometry's
+    curveSegments when given)."""
+    __slots__ = ("segs", "holes_")
     cls_name = "Shape"
 
     def __init__(self, pts=None):
         super().__init__({})
-        self.pts: List[List[float]] = [list(p.v()[:2]) for p in pts] if pts else []
+        self.segs: List[Tuple[str, Any]] = [("pt", list(p.v()[:2])) for p in pts] if pts else []
         self.holes_: List["Shape"] = []
 
     def get_special(self, it, key):
         if key == "holes":
             return _HolesProxy(self)
+        if key == "currentPoint":
+            return Vec(("x", "y"), self.current(), "Vector2")
         return super().get_special(it, key)
 
+    @property
+    def pts(self) -> List[List[float]]:
+        return self.sample(12)
+
+    def current(self) -> List[float]:
+        out = self.sample(1)
+        return out[-1] if out else [0.0, 0.0]
+
+    def sample(self, n: int) -> List[List[float]]:
+        n = max(1, min(int(n), 256))
+        out: List[List[float]] = []
+
+        def push(p):
+            p = [float(p[0]), float(p[1])]
+            if not out or out[-1] != p:
+                out.append(p)
+        for kind, d in self.segs:
+            sx, sy = out[-1] if out else (0.0, 0.0)
+            if kind == "pt":
+                push(d)
+            elif kind == "quad":
+                cx, cy, ex, ey = d
+                for k in range(0 if not out else 1, n + 1):
+                    t = k / n
+                    push([(1 - t) ** 2 * sx + 2 * (1 - t) * t * cx + t * t * ex,
+                          (1 - t) ** 2 * sy + 2 * (1 - t) * t * cy + t * t * ey])
+            elif kind == "bez":
+                c1x, c1y, c2x, c2y, ex, ey = d
+                for k in range(0 if not out else 1, n + 1):
+                    t = k / n
+                    u = 1 - t
+                    push([u ** 3 * sx + 3 * u * u * t * c1x + 3 * u * t * t * c2x + t ** 3 * ex,
+                          u ** 3 * sy + 3 * u * u * t * c1y + 3 * u * t * t * c2y + t ** 3 * ey])
+            elif kind == "ell":
+                for k in range(2 * n + 1):
+                    push(_ellipse_point(d, k / (2 * n)))
+            elif kind == "spline":
+                pts = ([[sx, sy]] if out else []) + d
+                if len(pts) >= 2:
+                    c = Curve("catmull", pts, dim=2)
+                    m = n * len(pts)
+                    for k in range(0 if not out else 1, m + 1):
+                        push(c.point(k / m))
+            elif kind == "close" and len(out) > 1 and out[-1] != out[0]:
+                out.append(list(out[0]))
+        return out
+
     def _quad(self, x):
-        cx, cy, ex, ey = (_num_arg(x, k) for k in range(4))
-        sx, sy = self.pts[-1] if self.pts else (0.0, 0.0)
-        for k in range(1, 9):
-            t = k / 8
-            self.pts.append([(1 - t) ** 2 * sx + 2 * (1 - t) * t * cx + t * t * ex,
-                             (1 - t) ** 2 * sy + 2 * (1 - t) * t * cy + t * t * ey])
+        self.segs.append(("quad", tuple(_num_arg(x, k) for k in range(4))))
         return self
 
     def _bez(self, x):
-        c1x, c1y, c2x, c2y, ex, ey = (_num_arg(x, k) for k in range(6))
-        sx, sy = self.pts[-1] if self.pts else (0.0, 0.0)
-        for k in range(1, 13):
-            t = k / 12
-            u = 1 - t
-            self.pts.append([u ** 3 * sx + 3 * u * u * t * c1x + 3 * u * t * t * c2x + t ** 3 * ex,
-                             u ** 3 * sy + 3 * u * u * t * c1y + 3 * u * t * t * c2y + t ** 3 * ey])
+        self.segs.append(("bez", tuple(_num_arg(x, k) for k in range(6))))
         return self
 
     def _arc(self, x, absolute):
         cx, cy, r, a0, a1 = (_num_arg(x, k) for k in range(5))
-        cw = _truthy(_arg(x, 5, False))
-        if not absolute and self.pts:
-            cx += self.pts[-1][0]
-            cy += self.pts[-1][1]
-        span = a1 - a0
-        if cw and span > 0:
-            span -= 2 * math.pi
-        elif not cw and span < 0:
-            span += 2 * math.pi
-        for k in range(17):
-            a = a0 + span * k / 16
-            self.pts.append([cx + r * math.cos(a), cy + r * math.sin(a)])
+        if not absolute:
+            px, py = self.current()
+            cx, cy = cx + px, cy + py
+        self.segs.append(("ell", {"aX": cx, "aY": cy, "xRadius": r, "yRadius": r, "aStartAngle": a0,
+                                  "aEndAngle": a1, "aClockwise": _truthy(_arg(x, 5, False)), "aRotation": 0.0}))
         return self
 
     def _ellipse(self, x, absolute):
@@ -4379,39 +4414,40 @@ class Shape(Host):
         for k, (nm, d) in enumerate(zip(names, defaults)):
             v = _arg(x, k)
             p[nm] = d if v is UNDEF else (_truthy(v) if nm == "aClockwise" else _to_num(v))
-        if not absolute and self.pts:
-            p["aX"] += self.pts[-1][0]
-            p["aY"] += self.pts[-1][1]
-        for k in range(33):
-            self.pts.append(_ellipse_point(p, k / 32))
+        if not absolute:
+            px, py = self.current()
+            p["aX"] += px
+            p["aY"] += py
+        self.segs.append(("ell", p))
         return self
 
     def _spline(self, x):
-        pts = ([self.pts[-1]] if self.pts else []) + [q.v()[:2] for q in it_items(_arg(x, 0)) if isinstance(q, Vec)]
-        if len(pts) >= 2:
-            c = Curve("catmull", pts, dim=2)
-            n = 8 * (len(pts) - 1)
-            self.pts += [c.point(k / n) for k in range(1, n + 1)]
+        self.segs.append(("spline", [q.v()[:2] for q in it_items(_arg(x, 0)) if isinstance(q, Vec)]))
         return self
+
+    def _vecs(self, x, key_index=0):
+        n = _arg(x, key_index)
+        return JSArray([Vec(("x", "y"), p, "Vector2") for p in self.sample(12 if n is UNDEF else _to_num(n))])
 
     js_methods = {
         "absellipse": lambda s, i, x: s._ellipse(x, True),
         "ellipse": lambda s, i, x: s._ellipse(x, False),
         "splineThru": lambda s, i, x: s._spline(x),
-        "getSpacedPoints": lambda s, i, x: JSArray([Vec(("x", "y"), p, "Vector2") for p in s.pts]),
-        "extractPoints": lambda s, i, x: JSObject({
-            "shape": JSArray([Vec(("x", "y"), p, "Vector2") for p in s.pts]),
-            "holes": JSArray([JSArray([Vec(("x", "y"), p, "Vector2") for p in h.pts]) for h in s.holes_])}),
-        "moveTo": lambda s, i, x: (s.pts.append([_num_arg(x, 0), _num_arg(x, 1)]), s)[-1],
-        "lineTo": lambda s, i, x: (s.pts.append([_num_arg(x, 0), _num_arg(x, 1)]), s)[-1],
+        "getSpacedPoints": lambda s, i, x: s._vecs(x),
+        "extractPoints": lambda s, i, x: (lambda n: JSObject({
+            "shape": JSArray([Vec(("x", "y"), p, "Vector2") for p in s.sample(n)]),
+            "holes": JSArray([JSArray([Vec(("x", "y"), p, "Vector2") for p in h.sample(n)]) for h in s.holes_])}))(
+            12 if _arg(x, 0) is UNDEF else _to_num(_arg(x, 0))),
+        "moveTo": lambda s, i, x: (s.segs.append(("pt", [_num_arg(x, 0), _num_arg(x, 1)])), s)[-1],
+        "lineTo": lambda s, i, x: (s.segs.append(("pt", [_num_arg(x, 0), _num_arg(x, 1)])), s)[-1],
         "quadraticCurveTo": lambda s, i, x: s._quad(x),
         "bezierCurveTo": lambda s, i, x: s._bez(x),
         "absarc": lambda s, i, x: s._arc(x, True),
         "arc": lambda s, i, x: s._arc(x, False),
-        "closePath": lambda s, i, x: (s.pts.append(list(s.pts[0])) if len(s.pts) > 1 and s.pts[-1] != s.pts[0]
-                                      else None, s)[-1],
-        "getPoints": lambda s, i, x: JSArray([Vec(("x", "y"), p, "Vector2") for p in s.pts]),
-        "setFromPoints": lambda s, i, x: (setattr(s, "pts", [list(p.v()[:2]) for p in it_items(_arg(x, 0))]), s)[-1],
+        "closePath": lambda s, i, x: (s.segs.append(("close", None)), s)[-1],
+        "getPoints": lambda s, i, x: s._vecs(x),
+        "setFromPoints": lambda s, i, x: (setattr(s, "segs", [("pt", list(p.v()[:2])) for p in it_items(_arg(x, 0))]),
+                                          s)[-1],
     }
 
 
@@ -4907,6 +4943,7 @@ def geometry_mesh(g: Geometry):
         def opt(key, d):
             v = o.get(key, UNDEF)
             return d if v is UNDEF or v is None else v
+        segs = int(_to_num(opt("curveSegments", 12))) if t == "ExtrudeGeometry" else int(n("curveSegments", 12))
         if t == "ExtrudeGeometry":
             depth = _to_num(opt("depth", opt("amount", 1.0)))
             bevel = _truthy(opt("bevelEnabled", True))
@@ -4918,8 +4955,9 @@ def geometry_mesh(g: Geometry):
             kw = dict(depth=0.0, bevel=False)
         vs, fs, off = [], [], 0
         for sh in shapes:
-            if isinstance(sh, Shape) and len(sh.pts) >= 3:
-                vv, ff = X.extrude(sh.pts, [h.pts for h in sh.holes_ if len(h.pts) >= 3], **kw)
+            if isinstance(sh, Shape) and len(sh.sample(segs)) >= 3:
+                holes = [h.sample(segs) for h in sh.holes_]
+                vv, ff = X.extrude(sh.sample(segs), [h for h in holes if len(h) >= 3], **kw)
                 if vv:
                     vs += vv
                     fs += [(a + off, b + off, c + off) for a, b, c in ff]

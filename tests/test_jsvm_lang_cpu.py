@@ -237,3 +237,21 @@ def test_curves_space_points_by_arc_length_and_give_tangents():
     assert got[:5] == [pytest.approx(1.0), pytest.approx(2.0), 6, 6, True]       # getPoints(divisions = 5)
     # the arc-length midpoint of this asymmetric arc differs from its parameter midpoint
     assert got[6] == pytest.approx(1.25) and abs(got[5] - got[6]) > 0.01 and got[7] == 5
+
+
+def test_shapes_sample_their_curves_by_divisions():
+    pre = """
+      const c = new THREE.Shape(); c.absarc(0, 0, 0.3, 0, Math.PI * 2, false);
+      const q = new THREE.Shape(); q.moveTo(0, 0); q.quadraticCurveTo(1, 1, 2, 0); q.closePath();
+      const e = new THREE.ExtrudeGeometry(c, {depth: 0.1, bevelEnabled: false, curveSegments: 6});
+      const f = new THREE.ShapeGeometry(c, 4);
+      const s = new THREE.Shape(); s.moveTo(0, 0); s.lineTo(1, 0); s.lineTo(1, 1); s.closePath();
+    """
+    got = _ev("[c.getPoints().length, c.getPoints(6).length, q.getPoints().length, q.getPoints(3).length, "
+              "e.attributes.position.count, f.attributes.position.count, s.getPoints().length, "
+              "s.currentPoint.x, c.extractPoints(2).shape.length]", pre).items
+    # a full circle: 2 x divisions + 1 points with the last equal to the first; a quadratic: divisions + 1, closed
+    assert got[:4] == [25, 13, 14, 5]
+    # extrude: 12 outline points, caps of 12 + sides of 2 rings x 12, non-indexed: 3 per triangle
+    assert got[4] == 3 * (2 * 10 + 2 * 12) and got[5] == 8          # flat shape: one vertex per outline point
+    assert got[6:] == [4, 0, 5]
