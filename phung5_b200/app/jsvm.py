@@ -4186,7 +4186,9 @@ class Object3D(Host):
         if isinstance(_arg(x, 0), Object3D) else s,
         "getObjectByName": lambda s, i, x: _find_name(s, _to_str(_arg(x, 0))),
         "setMatrixAt": lambda s, i, x: (s.props.setdefault("__inst", {}).__setitem__(int(_num_arg(x, 0)), [row[:] for row in _arg(x, 1).m]), UNDEF)[-1],
-        "setColorAt": lambda s, i, x: UNDEF,
+        "setColorAt": lambda s, i, x: _set_color_at(s, int(_num_arg(x, 0)), _arg(x, 1)),
+        "getColorAt": lambda s, i, x: (_arg(x, 1).set_rgb(*s.props.get("__icol", {}).get(int(_num_arg(x, 0)), (1.0, 1.0, 1.0)))
+                                       if isinstance(_arg(x, 1), Color) else None, UNDEF)[-1],
         "getMatrixAt": lambda s, i, x: (setattr(_arg(x, 1), "m", [row[:] for row in s.props.get("__inst", {}).get(int(_num_arg(x, 0)), _ident4())]), UNDEF)[-1],
         "applyMatrix4": lambda s, i, x: _apply_obj_matrix(s, _arg(x, 0).m),
         "applyQuaternion": lambda s, i, x: (_set_rot(s.props["rotation"], (_mat_mul(
@@ -4211,6 +4213,16 @@ class Object3D(Host):
         "computeBoundingSphere": lambda s, i, x: UNDEF,
         "computeBoundingBox": lambda s, i, x: UNDEF,
     }
+
+
+def _set_color_at(o: "Object3D", k: int, c):
+    """InstancedMesh.setColorAt: the instance's colour (linear), which multiplies the material colour; the first
+    call creates `instanceColor`, as three.js does, so `instanceColor.needsUpdate = true` works after it."""
+    if isinstance(c, Color) and 0 <= k < max(0, int(_to_num(o.props.get("count", 0)))):
+        o.props.setdefault("__icol", {})[k] = tuple(c.rgb())
+        if not isinstance(o.props.get("instanceColor"), JSObject):
+            o.props["instanceColor"] = JSObject({"needsUpdate": False, "isInstancedBufferAttribute": True})
+    return UNDEF
 
 
 def _add3(a, b):
@@ -5156,7 +5168,7 @@ def _tri_groups(g: "Geometry", n_tris: int) -> Dict[int, List[int]]:
 def to_scene_json(root: Object3D, max_depth: int = 64) -> dict:
     """Object3D tree -> the scene JSON of render/scene.py (geometries baked to BufferGeometry where needed)."""
     geoms: Dict[int, dict] = {}
-    mats: Dict[int, dict] = {}
+    mats: Dict[Any, dict] = {}
 
     meshes: Dict[int, tuple] = {}
 
@@ -5202,6 +5214,17 @@ def to_scene_json(root: Object3D, max_depth: int = 64) -> dict:
                 mats[key]["metalness"] = _to_num(m.props.get("metalness", 0.0))
         return mats[key]["uuid"]
 
+    def tinted(mid: str, rgb) -> str:
+        """A copy of material `mid` whose colour is multiplied by an instance colour (linear)."""
+        key = (mid, tuple(round(c, 6) for c in rgb))
+        if key not in mats:
+            base = next(v for v in mats.values() if v["uuid"] == mid)
+            c = Color()
+            c.set_any([float(base.get("color", 0xFFFFFF))])
+            c.set_rgb(*[a * b for a, b in zip(c.rgb(), rgb)])
+            mats[key] = dict(base, uuid=f"{mid}-{len(mats)}", color=c.hex())
+        return mats[key]["uuid"]
+
     def node(o: Object3D, depth: int) -> dict:
         if depth > max_depth:
             raise ValueError("scene depth limit exceeded")
@@ -5215,8 +5238,10 @@ def to_scene_json(root: Object3D, max_depth: int = 64) -> dict:
             if o.otype == "InstancedMesh":
                 count = int(_to_num(o.props.get("count", 0)))
                 inst = o.props.get("__inst", {})
+                icol = o.props.get("__icol", {})
                 for k in range(count):
-                    d["children"].append({"uuid": f"{o.id_}-{k}", "type": "Mesh", "geometry": gid, "material": mid,
+                    mk = mid if k not in icol else tinted(mid, icol[k])
+                    d["children"].append({"uuid": f"{o.id_}-{k}", "type": "Mesh", "geometry": gid, "material": mk,
                                           "matrix": _col_major(inst.get(k, _ident4())), "children": []})
             elif isinstance(o.props.get("material"), JSArray):
                 # one material per geometry group: a sub-mesh per group (three.js draws each group with its

@@ -288,3 +288,19 @@ def test_post_validation_counts_like_the_reference_validator():
                                         "o.add(new THREE.Mesh(new THREE.BoxGeometry(0.1, 0.1, 0.1), "
                                         "new THREE.MeshBasicMaterial())); return o; }")
     assert [f["rule"] for f in res.failures] == ["INVALID_RETURN_TYPE"]
+
+
+def test_instance_colours_multiply_the_material_colour():
+    src = """export default function generate(THREE) { const g = new THREE.Group();
+      const im = new THREE.InstancedMesh(new THREE.BoxGeometry(0.1, 0.1, 0.1), new THREE.MeshStandardMaterial({color: 0xffffff}), 3);
+      const d = new THREE.Object3D();
+      for (let i = 0; i < 3; i++) { d.position.set(0.2 * i - 0.2, 0, 0); d.updateMatrix(); im.setMatrixAt(i, d.matrix); }
+      im.setColorAt(0, new THREE.Color(0xff0000)); im.setColorAt(2, new THREE.Color(0x00ff00));
+      im.instanceMatrix.needsUpdate = true; im.instanceColor.needsUpdate = true;
+      const c = new THREE.Color(); im.getColorAt(2, c); g.userData.c = c.getHex();
+      g.add(im); return g; }"""
+    res = JSChecker(_inline=True).check(src)
+    assert res.ok, res.summary()
+    mats = {m["uuid"]: m for m in res.scene["materials"]}
+    kids = res.scene["object"]["children"][0]["children"]
+    assert [mats[k["material"]]["color"] for k in kids] == [0xFF0000, 0xFFFFFF, 0x00FF00]
